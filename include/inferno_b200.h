@@ -1,0 +1,201 @@
+/*
+ * inferno_b200.h -- C ABI of libinferno_b200.so, the sm_100a decode engine
+ * for Inferno.jl's Qwen3.5 hybrid models.
+ *
+ * Every entry is extern "C" with plain pointers and sizes.  Functions return
+ * an int status (0 = OK, negative = error) unless noted; the message of the
+ * last error on the calling thread is inferno_last_error().  Citations give
+ * the reference interface (Inferno.jl source tree) each entry replaces.
+ *
+ * Three tiers:
+ *   1. compatibility: the exact symbols of src/kernels/quant_kernels.c, so the
+ *      library can be dropped in at QuantizedKernels.LIBQUANT_PATH;
+ *   2. device kernels: dequantize / GEMV on device pointers;
+ *   3. engine: the model lives on the GPU; the host calls per layer
+ *      (`layer(x, pos, rope, cache)`) or per token / per decode loop.
+ */
+#ifndef INFERNO_B200_H
+#define INFERNO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define INFERNO_B200_VERSION 1
+
+/* status codes */
+#define INFERNO_OK 0
+#define INFERNO_EINVAL (-1)  /* bad argument                               */
+#define INFERNO_ECUDA (-2)   /* CUDA runtime / launch error                 */
+#define INFERNO_ENOMEM (-3)  /* device allocation failed                    */
+#define INFERNO_ESTATE (-4)  /* call not valid in the engine's state        */
+#define INFERNO_EDEVICE (-5) /* a kernel reported an error (timeout, ...)   */
+#define INFERNO_ENCCL (-6)   /* NCCL error                                  */
+
+/* ggml type ids accepted (GGUF spec; src/GGUF.jl:25-60) */
+#define INFERNO_F32 0
+#define INFERNO_Q8_0 8
+#define INFERNO_Q4_K 12
+#define INFERNO_Q5_K 13
+#define INFERNO_Q6_K 14
+#define INFERNO_IQ2_XXS 16
+
+/* thread-local message of the last failing call on this thread */
+const char* inferno_last_error(void);
+int inferno_version(void);
+/* device-side error word (1 = a bounded wait timed out); clear != 0 resets it */
+int inferno_device_error(int device, int clear);
+
+/* ======================= 1. compatibility tier ===========================
+ * Same names and signatures as src/kernels/quant_kernels.c:602-697, bound by
+ * the ccalls at src/QuantizedKernels.jl:88-90, 106-108, 125-127, 141-143.
+ * Host pointers in, host results out (each call copies x in and y out; a
+ * weight array is uploaded on first sight and cached by host pointer, size
+ * and a content signature).  Numerics: fp32 activations (the reference
+ * quantizes x to Q8_K); q8_buf is accepted and ignored.  void returns as in
+ * the reference; failures are printed to stderr and kept in
+ * inferno_last_error(). */
+void q4_k_gemv(const uint8_t* weight, const float* x, float* out, void* q8_buf, int inner_dim, int outer_dim);
+void q5_k_gemv(const uint8_t* weight, const float* x, float* out, void* q8_buf, int inner_dim, int outer_dim);
+void q6_k_gemv(const uint8_t* weight, const float* x, float* out, void* q8_buf, int inner_dim, int outer_dim);
+void q8_0_gemv(const uint8_t* weight, const float* x, float* out, int inner_dim, int outer_dim);
+/* frees the cached device copies of compatibility-tier weights */
+int inferno_compat_release(void);
+
+/* ======================= 2. device kernel tier ============================
+ * All pointers are device pointers; `stream` is a cudaStream_t (NULL = legacy
+ * default stream).  Weight buffers hold GGUF blocks in native row-major layout
+ * (src/QuantsCPU.jl:37-115): row r at byte r*(inner/QK)*block_bytes; they must
+ * be 16-byte aligned and readable up to the next 16-byte boundary (true of
+ * every cudaMalloc allocation). */
+
+/* Bit-exact dequantization to fp32: replaces Dequant.dequantize_{q4_k,q5_k,
+ * q6_k,q8_0,iq2_xxs} (src/Dequant.jl:12-54, 304-441, 558-601). */
+int inferno_dequantize(int ggml_type, const void* src, int64_t n_elements, float* dst, void* stream);
+
+/* y[b*outer + r] = sum_i W[r,i] * x[b*inner + i] for b < batch: replaces
+ * ModelCPU.mul! on quantized weights (src/ModelCPU.jl:284-444). */
+int inferno_gemv(int ggml_type, const void* W, const float* x, float* y, int inner, int outer, int batch,
+                 void* stream);
+
+/* GEMV with a fused prologue / epilogue:
+ *   prologue 0 = none, 1 = RMSNorm(x; norm_w, eps) (src/ModelCPU.jl:110-122)
+ *   epilogue 0 = store, 1 = y += W x (residual, src/ModelCPU.jl:880-889),
+ *            3 = first-max argmax into argmax[b] as a packed 64-bit key
+ *                (ordered-float << 32 | 0xffffffff - row); y may be NULL.
+ *                argmax[] must be zeroed first (src/ModelCPU.jl:1123-1127).
+ * force_rows_per_warp: 0 = planner's choice, else 1, 2 or 4 (tuning). */
+int inferno_gemv_ex(int ggml_type, const void* W, const float* x, float* y, int inner, int outer, int batch,
+                    int prologue, const float* norm_w, float eps, int epilogue, unsigned long long* argmax,
+                    int force_rows_per_warp, void* stream);
+
+/* h = silu(Wg x') * (Wu x') with x' = RMSNorm(x; norm_w) if norm_w != NULL:
+ * the fused gate/up half of mlp_forward (src/ModelCPU.jl:447-473). */
+int inferno_gemv_swiglu(int ggml_type, const void* Wg, const void* Wu, const float* x, float* h, int inner,
+                        int rows, int batch, const float* norm_w, float eps, void* stream);
+
+/* ======================= 3. engine tier ==================================== */
+
+/* Model hyper-parameters, filled by the host from GGUF metadata
+ * (LoaderCPU.get_config, src/LoaderCPU.jl:393-418; ssm dims per
+ * src/LoaderCPU.jl:498-516 with nk taken from ssm.group_count). */
+typedef struct InfernoConfig {
+  int32_t struct_size;           /* sizeof(InfernoConfig) */
+  int32_t device;                /* CUDA device ordinal */
+  int32_t hidden_size;
+  int32_t intermediate_size;     /* dense FFN (0 for MoE models) */
+  int32_t num_layers;
+  int32_t vocab_size;
+  int32_t n_heads;               /* full-attention query heads */
+  int32_t n_kv_heads;
+  int32_t head_dim;
+  int32_t ssm_nv;                /* Gated DeltaNet value heads (time_step_rank) */
+  int32_t ssm_nk;                /* Gated DeltaNet q/k heads (group_count) */
+  int32_t ssm_dk;                /* state_size */
+  int32_t ssm_dv;                /* inner_size / nv */
+  int32_t ssm_conv_kernel;
+  int32_t max_ctx;               /* KV-cache capacity in positions */
+  int32_t n_experts;             /* 0 = dense FFN */
+  int32_t n_experts_used;
+  int32_t expert_ffn;
+  int32_t shared_expert_ffn;
+  int32_t max_batch;             /* sequences per step (1 for batch-1 decode) */
+  float rms_eps;
+  float rope_theta;
+  float partial_rotary_factor;
+  int32_t use_graphs;            /* capture the decode step in a CUDA graph */
+  int32_t use_pdl;               /* programmatic dependent launch between kernels */
+  int32_t tp_rank, tp_size;      /* tensor parallel (tp_size 1 = off) */
+  const void* nccl_unique_id;    /* 128-byte ncclUniqueId when tp_size > 1 */
+} InfernoConfig;
+
+typedef struct InfernoEngine InfernoEngine;
+
+int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out);
+
+/* Raw GGUF tensor bytes in native layout (the keep_quantized branch of
+ * LoaderCPU.extract_tensor_cpu, src/LoaderCPU.jl:131-155), by GGUF name;
+ * ne[] in GGUF order (ne[0] fastest), unused dims = 1. */
+int inferno_engine_upload_tensor(InfernoEngine* eng, const char* name, int ggml_type, const int64_t ne[4],
+                                 const void* host_bytes, size_t nbytes);
+
+/* Binds uploaded tensors to layers (a layer is Gated DeltaNet iff
+ * blk.i.ssm_a exists, src/LoaderCPU.jl:431), allocates state and builds the
+ * RoPE table (src/ModelCPU.jl:134-153). */
+int inferno_engine_finalize(InfernoEngine* eng);
+
+/* One decoder layer in place on x[hidden] (host pointer), at position pos:
+ * replaces DecoderLayerCPU(x, pos, rope, cache) (src/ModelCPU.jl:870-891). */
+int inferno_layer_forward(InfernoEngine* eng, int layer, float* x_host, int pos);
+
+/* Runs tokens tok[0..n) (0-based ids) at positions pos0.. and returns the
+ * logits of the last one (vocab floats, may be NULL) and its first-max argmax
+ * (may be NULL): replaces forward_cpu! + argmax (src/ModelCPU.jl:945-989,
+ * 1123-1127). */
+int inferno_forward_tokens(InfernoEngine* eng, const int32_t* tok, int n, int pos0, float* logits_out,
+                           int32_t* argmax_out);
+
+/* Greedy decode on the device: feeds `tok` at `pos`, then each argmax at the
+ * next position, n_steps times; out_tokens[i] = token produced at step i.
+ * The generation loop of test/benchmark_e2e.jl:43-59 / Engine.generate
+ * (src/Engine.jl:327-344) with temperature 0. */
+int inferno_decode_greedy(InfernoEngine* eng, int32_t tok, int pos, int n_steps, int32_t* out_tokens);
+
+/* Zero GDN conv + recurrent state and the KV cache (src/ModelCPU.jl:525-529). */
+int inferno_reset_states(InfernoEngine* eng);
+
+/* Hidden state after `layer` for the last token run (debug / parity). */
+int inferno_dump_hidden(InfernoEngine* eng, int layer, float* out_host);
+
+/* Serialise / restore the recurrent state + KV cache (host buffer). */
+int64_t inferno_state_size(InfernoEngine* eng);
+int inferno_state_export(InfernoEngine* eng, void* host_buf, int64_t nbytes);
+int inferno_state_import(InfernoEngine* eng, const void* host_buf, int64_t nbytes);
+
+/* Checkpoint / resume on the device: copy the recurrent state + KV cache to
+ * an engine-owned device snapshot, and back (stream-ordered, no host copy). */
+int inferno_state_save_device(InfernoEngine* eng);
+int inferno_state_restore_device(InfernoEngine* eng);
+
+/* Kernels launched per decode token by this engine (for launch accounting). */
+int inferno_kernels_per_token(InfernoEngine* eng);
+
+/* Profiling pass: runs n_tokens greedy steps eagerly (no graph, no PDL) with
+ * CUDA events between kernels and accumulates device time per kernel class:
+ * [0] embedding, [1] layer GEMVs, [2] GDN step, [3] attention, [4] lm_head
+ * GEMV + argmax, [5] finalize.  Arrays hold 6 entries. */
+int inferno_profile_tokens(InfernoEngine* eng, int32_t tok, int pos, int n_tokens, float* ms_by_class,
+                           int32_t* launches_by_class);
+
+/* Device time of the last inferno_decode_greedy call in ms (CUDA events). */
+float inferno_last_decode_ms(InfernoEngine* eng);
+
+int inferno_engine_destroy(InfernoEngine* eng);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* INFERNO_B200_H */

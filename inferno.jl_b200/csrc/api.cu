@@ -1,0 +1,272 @@
+// C ABI: error channel, device-pointer tier and the QuantizedKernels.jl
+// compatibility tier (same symbols and signatures as the reference's
+// src/kernels/quant_kernels.c, so the .so can stand in for
+// libquant_kernels.so at QuantizedKernels.LIBQUANT_PATH).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+#include "internal.h"
+#include "gemv.cuh"
+#include "../../include/inferno_b200.h"
+
+namespace inf {
+
+namespace {
+thread_local std::string g_last_error;
+std::mutex g_mu;
+int g_sms[64] = {};
+int* g_err_word[64] = {};
+}  // namespace
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+const char* last_error() { return g_last_error.c_str(); }
+
+int num_sms(int device) {
+  if (device < 0 || device >= 64) return 148;
+  if (!g_sms[device]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device);
+    g_sms[device] = v > 0 ? v : 148;
+  }
+  return g_sms[device];
+}
+
+int* device_error_word(int device) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (device < 0 || device >= 64) return nullptr;
+  if (!g_err_word[device]) {
+    int* p = nullptr;
+    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+    cudaMemset(p, 0, sizeof(int));
+    g_err_word[device] = p;
+  }
+  return g_err_word[device];
+}
+
+// ---------------------------------------------------------------------------
+// compatibility tier state: device copies of host weight arrays, keyed by the
+// host pointer and size (Julia keeps its weight arrays alive and immutable),
+// plus staging for x / y.  One mutex: the reference's C kernels are also not
+// meant to be called concurrently on one scratch pool.
+// ---------------------------------------------------------------------------
+struct CompatState {
+  bool init = false;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  struct W { void* dev; size_t bytes; uint64_t sig; };
+  std::unordered_map<const void*, W> weights;
+  float* dx = nullptr; size_t dx_cap = 0;
+  float* dy = nullptr; size_t dy_cap = 0;
+};
+CompatState g_compat;
+std::mutex g_compat_mu;
+
+static uint64_t sig_of(const uint8_t* p, size_t n) {
+  // cheap content signature: size + first/last 64 bytes (FNV-1a)
+  uint64_t h = 1469598103934665603ull ^ n;
+  size_t k = n < 64 ? n : 64;
+  for (size_t i = 0; i < k; ++i) h = (h ^ p[i]) * 1099511628211ull;
+  for (size_t i = n - k; i < n; ++i) h = (h ^ p[i]) * 1099511628211ull;
+  return h;
+}
+
+static int compat_init() {
+  if (g_compat.init) return 0;
+  int dev = 0;
+  const char* e = getenv("INFERNO_B200_DEVICE");
+  if (e) dev = atoi(e);
+  INF_CUDA_TRY(cudaSetDevice(dev));
+  INF_CUDA_TRY(cudaStreamCreateWithFlags(&g_compat.stream, cudaStreamNonBlocking));
+  g_compat.device = dev;
+  g_compat.init = true;
+  return 0;
+}
+
+static int compat_weight(const uint8_t* host, size_t bytes, const void** dev) {
+  uint64_t s = sig_of(host, bytes);
+  auto it = g_compat.weights.find(host);
+  if (it != g_compat.weights.end() && it->second.bytes == bytes && it->second.sig == s) {
+    *dev = it->second.dev;
+    return 0;
+  }
+  if (it != g_compat.weights.end()) {
+    cudaFree(it->second.dev);
+    g_compat.weights.erase(it);
+  }
+  void* d = nullptr;
+  INF_CUDA_TRY(cudaMalloc(&d, (bytes + 15) / 16 * 16));
+  INF_CUDA_TRY(cudaMemcpyAsync(d, host, bytes, cudaMemcpyHostToDevice, g_compat.stream));
+  g_compat.weights[host] = {d, bytes, s};
+  *dev = d;
+  return 0;
+}
+
+static int grow(float** p, size_t* cap, size_t n) {
+  if (*cap >= n) return 0;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  INF_CUDA_TRY(cudaMalloc(p, n * sizeof(float)));
+  *cap = n;
+  return 0;
+}
+
+static int compat_gemv(int type, const uint8_t* W, const float* x, float* out, int inner, int outer) {
+  std::lock_guard<std::mutex> lk(g_compat_mu);
+  int rc;
+  if ((rc = compat_init())) return rc;
+  INF_CUDA_TRY(cudaSetDevice(g_compat.device));
+  if (inner <= 0 || outer <= 0) return set_error(-1, "compat gemv: bad dims %d x %d", outer, inner);
+  const size_t bytes = (size_t)outer * (inner / qk_of(type)) * bb_of(type);
+  const void* dW;
+  if ((rc = compat_weight(W, bytes, &dW))) return rc;
+  if ((rc = grow(&g_compat.dx, &g_compat.dx_cap, inner))) return rc;
+  if ((rc = grow(&g_compat.dy, &g_compat.dy_cap, outer))) return rc;
+  INF_CUDA_TRY(cudaMemcpyAsync(g_compat.dx, x, (size_t)inner * 4, cudaMemcpyHostToDevice, g_compat.stream));
+  GemvCall c;
+  c.type = type;
+  c.inner = inner;
+  c.mats[0] = {dW, g_compat.dy, outer};
+  c.nmats = 1;
+  c.x = g_compat.dx;
+  if ((rc = launch_gemv(c, g_compat.stream, false))) return rc;
+  INF_CUDA_TRY(cudaMemcpyAsync(out, g_compat.dy, (size_t)outer * 4, cudaMemcpyDeviceToHost, g_compat.stream));
+  INF_CUDA_TRY(cudaStreamSynchronize(g_compat.stream));
+  return 0;
+}
+
+}  // namespace inf
+
+using namespace inf;
+
+extern "C" {
+
+const char* inferno_last_error(void) { return inf::last_error(); }
+int inferno_version(void) { return INFERNO_B200_VERSION; }
+
+int inferno_device_error(int device, int clear) {
+  int* w = device_error_word(device);
+  if (!w) return set_error(INFERNO_ECUDA, "no device error word");
+  int v = 0;
+  if (cudaMemcpy(&v, w, sizeof v, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return set_error(INFERNO_ECUDA, "reading device error word failed");
+  if (clear) cudaMemset(w, 0, sizeof(int));
+  return v;
+}
+
+int inferno_dequantize(int ggml_type, const void* src, int64_t n, float* dst, void* stream) {
+  if (!src || !dst || n < 0) return set_error(INFERNO_EINVAL, "dequantize: null pointer or negative size");
+  if (!type_supported(ggml_type)) return set_error(INFERNO_EINVAL, "dequantize: unsupported ggml type %d", ggml_type);
+  if (n % (ggml_type == T_Q8_0 || ggml_type == T_F32 ? 32 : 256))
+    return set_error(INFERNO_EINVAL, "dequantize: %lld elements not a whole number of blocks", (long long)n);
+  int rc = launch_dequant(ggml_type, src, n, dst, (cudaStream_t)stream);
+  return rc ? set_error(INFERNO_ECUDA, "dequantize launch failed") : 0;
+}
+
+int inferno_gemv(int ggml_type, const void* W, const float* x, float* y, int inner, int outer, int batch,
+                 void* stream) {
+  if (!W || !x || !y) return set_error(INFERNO_EINVAL, "gemv: null pointer");
+  if (outer < 0 || batch < 1) return set_error(INFERNO_EINVAL, "gemv: bad outer/batch");
+  GemvCall c;
+  c.type = ggml_type;
+  c.inner = inner;
+  c.mats[0] = {W, y, outer};
+  c.nmats = 1;
+  c.nb = batch;
+  c.x = x;
+  c.x_stride = inner;
+  c.y_stride = outer;
+  return launch_gemv(c, (cudaStream_t)stream, false);
+}
+
+int inferno_gemv_ex(int ggml_type, const void* W, const float* x, float* y, int inner, int outer, int batch,
+                    int prologue, const float* norm_w, float eps, int epilogue, unsigned long long* argmax,
+                    int force_rows_per_warp, void* stream) {
+  if (!W || !x) return set_error(INFERNO_EINVAL, "gemv_ex: null pointer");
+  GemvCall c;
+  c.type = ggml_type;
+  c.inner = inner;
+  c.mats[0] = {W, y, outer};
+  c.nmats = 1;
+  c.nb = batch;
+  c.x = x;
+  c.x_stride = inner;
+  c.y_stride = outer;
+  c.pro = prologue;
+  c.pro_w = norm_w;
+  c.eps = eps;
+  c.epi = epilogue;
+  c.argmax = argmax;
+  c.force_r = force_rows_per_warp;
+  if (prologue == PRO_RMSNORM && !norm_w) return set_error(INFERNO_EINVAL, "gemv_ex: RMSNorm needs a weight");
+  if (epilogue == EPI_ARGMAX && !argmax) return set_error(INFERNO_EINVAL, "gemv_ex: argmax output missing");
+  if (epilogue == EPI_SWIGLU) return set_error(INFERNO_EINVAL, "gemv_ex: use inferno_gemv_swiglu");
+  return launch_gemv(c, (cudaStream_t)stream, false);
+}
+
+int inferno_gemv_swiglu(int ggml_type, const void* Wg, const void* Wu, const float* x, float* h, int inner,
+                        int rows, int batch, const float* norm_w, float eps, void* stream) {
+  GemvCall c;
+  c.type = ggml_type;
+  c.inner = inner;
+  c.mats[0] = {Wg, h, rows};
+  c.mats[1] = {Wu, nullptr, rows};
+  c.nmats = 2;
+  c.nb = batch;
+  c.x = x;
+  c.x_stride = inner;
+  c.y_stride = rows;
+  c.pro = norm_w ? PRO_RMSNORM : PRO_NONE;
+  c.pro_w = norm_w;
+  c.eps = eps;
+  c.epi = EPI_SWIGLU;
+  return launch_gemv(c, (cudaStream_t)stream, false);
+}
+
+// ---- compatibility tier (void returns, as in the reference) -----------------
+// Numerics note: the reference quantizes x to Q8_K and does integer dots
+// (quant_kernels.c:166-306); these run the engine's fp32-activation kernel.
+// The q8 scratch argument is accepted and ignored.
+static void compat_report(int rc, const char* fn) {
+  if (rc) fprintf(stderr, "[inferno_b200] %s failed: %s\n", fn, inf::last_error());
+}
+void q4_k_gemv(const uint8_t* weight, const float* x, float* out, void* q8_buf, int inner_dim, int outer_dim) {
+  (void)q8_buf;
+  compat_report(compat_gemv(T_Q4_K, weight, x, out, inner_dim, outer_dim), "q4_k_gemv");
+}
+void q5_k_gemv(const uint8_t* weight, const float* x, float* out, void* q8_buf, int inner_dim, int outer_dim) {
+  (void)q8_buf;
+  compat_report(compat_gemv(T_Q5_K, weight, x, out, inner_dim, outer_dim), "q5_k_gemv");
+}
+void q6_k_gemv(const uint8_t* weight, const float* x, float* out, void* q8_buf, int inner_dim, int outer_dim) {
+  (void)q8_buf;
+  compat_report(compat_gemv(T_Q6_K, weight, x, out, inner_dim, outer_dim), "q6_k_gemv");
+}
+void q8_0_gemv(const uint8_t* weight, const float* x, float* out, int inner_dim, int outer_dim) {
+  compat_report(compat_gemv(T_Q8_0, weight, x, out, inner_dim, outer_dim), "q8_0_gemv");
+}
+
+int inferno_compat_release(void) {
+  std::lock_guard<std::mutex> lk(g_compat_mu);
+  if (!g_compat.init) return 0;
+  cudaSetDevice(g_compat.device);
+  for (auto& kv : g_compat.weights) cudaFree(kv.second.dev);
+  g_compat.weights.clear();
+  if (g_compat.dx) cudaFree(g_compat.dx);
+  if (g_compat.dy) cudaFree(g_compat.dy);
+  g_compat.dx = g_compat.dy = nullptr;
+  g_compat.dx_cap = g_compat.dy_cap = 0;
+  return 0;
+}
+
+}  // extern "C"

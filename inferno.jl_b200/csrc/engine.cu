@@ -1,0 +1,760 @@
+// The decode engine: owns the model on one GPU and runs Inferno.jl's
+// per-token loop (src/ModelCPU.jl:945-989 forward_cpu!, :870-891 decoder
+// layer, :1014-1046 lm_head, :1123-1127 greedy argmax) as a chain of fused
+// sm_100a kernels, captured once into CUDA graphs with programmatic dependent
+// launch between kernels.
+//
+// Per token (batch 1):
+//   embed row (Q6_K dequant of token_embd row `tok`)
+//   per GDN layer:  [in_proj|attn_gate] GEMV (RMSNorm prologue)
+//                   GDN step (conv, norms, gates, delta rule)
+//                   ssm_out GEMV (head-norm x SiLU(z) prologue, residual add)
+//                   ffn gate/up GEMV (RMSNorm prologue, SwiGLU epilogue)
+//                   ffn_down GEMV (residual add)
+//   per attn layer: [wq|wk|wv] GEMV (RMSNorm prologue)
+//                   split-K attention (norms, RoPE, KV append, gate)
+//                   wo GEMV (residual add), FFN as above
+//   lm_head GEMV (final RMSNorm prologue, first-max argmax epilogue)
+//   finalize (next token, position, output slot)
+// All control state (token, position, step) lives in device memory so the
+// same graph replays for prompt tokens and for greedy decode.
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+#include "internal.h"
+#include "gemv.cuh"
+#include "params.h"
+#include "../../include/inferno_b200.h"
+
+namespace inf {
+
+struct Ctl {                 // device-resident step control
+  int tok;                   // token embedded by the next step
+  int pos;                   // its position
+  int step;                  // steps run in the current call
+  int n_prompt;              // prompt tokens of the current call
+  int last;                  // argmax of the last step
+  int pad[3];
+  unsigned long long argkey; // packed first-max of the running lm_head
+};
+
+__global__ void finalize_kernel(Ctl* c, const int* prompt, int* out, int max_out) {
+  pdl_trigger();
+  pdl_wait();
+  const unsigned long long key = c->argkey;
+  const int am = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull));
+  c->last = am;
+  const int s = c->step;
+  c->tok = (s + 1 < c->n_prompt) ? prompt[s + 1] : am;
+  const int o = s - (c->n_prompt - 1);
+  if (o >= 0 && o < max_out) out[o] = am;
+  c->pos = c->pos + 1;
+  c->step = s + 1;
+  c->argkey = 0ull;
+}
+
+struct DevTensor {
+  int type = -1;
+  int64_t ne[4] = {1, 1, 1, 1};
+  void* d = nullptr;
+  size_t bytes = 0;
+  int64_t rows() const { return ne[1] * ne[2] * ne[3]; }
+};
+
+struct LayerBind {
+  bool ssm = false;
+  DevTensor *attn_norm = nullptr, *post_norm = nullptr;
+  DevTensor *in_proj = nullptr, *gate = nullptr, *ssm_out = nullptr, *conv1d = nullptr, *alpha = nullptr,
+            *beta = nullptr, *ssm_a = nullptr, *dt_bias = nullptr, *ssm_norm = nullptr;
+  DevTensor *wq = nullptr, *wk = nullptr, *wv = nullptr, *wo = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+  DevTensor *ffn_gate = nullptr, *ffn_up = nullptr, *ffn_down = nullptr;
+  float* ring = nullptr;
+  float* S = nullptr;
+  int* step = nullptr;
+  int* done = nullptr;
+  float* kc = nullptr;
+  float* vc = nullptr;
+};
+
+}  // namespace inf
+
+struct InfernoEngine {
+  InfernoConfig cfg{};
+  int dev = 0;
+  cudaStream_t st = nullptr;
+  std::map<std::string, inf::DevTensor> tensors;
+  std::vector<inf::LayerBind> layers;
+  inf::DevTensor *embd = nullptr, *out_norm = nullptr, *lm_head = nullptr;
+  bool finalized = false;
+  int C = 0, di = 0, rd = 0, split_len = 64, nsplit = 1;
+  // activations
+  float *x = nullptr, *qkv = nullptr, *z = nullptr, *y = nullptr, *qg = nullptr, *k = nullptr, *v = nullptr,
+        *o = nullptr, *h = nullptr, *logits = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr, *part_o = nullptr, *part_ml = nullptr, *hidden = nullptr;
+  int* att_counters = nullptr;
+  inf::Ctl* ctl = nullptr;
+  int *prompt = nullptr, *out_tokens = nullptr;
+  int max_out = 0;
+  int* err = nullptr;
+  // state arena (for reset / export)
+  std::vector<std::pair<void*, size_t>> state_bufs;
+  std::vector<void*> allocs;
+  cudaGraphExec_t g1 = nullptr, g1_logits = nullptr, g8 = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float last_ms = 0.f;
+  bool dump = false;
+  int launches = 0;              // kernels enqueued by the last enqueue_token
+  void* snapshot = nullptr;      // device copy of the state arena
+  size_t state_bytes = 0;
+  // profiling: events between the kernels of one eager token
+  bool profiling = false;
+  std::vector<cudaEvent_t> prof_ev;
+  std::vector<int> prof_kind;     // kernel class per interval
+};
+
+namespace inf {
+
+namespace {
+
+template <class T>
+int dalloc(InfernoEngine* e, T** p, size_t count, bool state = false) {
+  void* d = nullptr;
+  size_t bytes = (count * sizeof(T) + 255) / 256 * 256;
+  cudaError_t r = cudaMalloc(&d, bytes);
+  if (r != cudaSuccess)
+    return set_error(INFERNO_ENOMEM, "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(r));
+  cudaMemset(d, 0, bytes);
+  e->allocs.push_back(d);
+  if (state) e->state_bufs.push_back({d, bytes});
+  *p = (T*)d;
+  return 0;
+}
+
+DevTensor* find(InfernoEngine* e, const std::string& n) {
+  auto it = e->tensors.find(n);
+  return it == e->tensors.end() ? nullptr : &it->second;
+}
+
+int require(InfernoEngine* e, const std::string& n, DevTensor** out, int type = -2) {
+  DevTensor* t = find(e, n);
+  if (!t) return set_error(INFERNO_EINVAL, "missing tensor %s", n.c_str());
+  if (type != -2 && t->type != type) return set_error(INFERNO_EINVAL, "tensor %s: type %d, expected %d", n.c_str(), t->type, type);
+  *out = t;
+  return 0;
+}
+
+// kernel classes reported by the profiling pass
+enum KClass { K_EMBED = 0, K_GEMV = 1, K_GDN = 2, K_ATTN = 3, K_LMHEAD = 4, K_FINAL = 5, K_NCLASS = 6 };
+
+void mark(InfernoEngine* e, int kind) {
+  ++e->launches;
+  if (!e->profiling) return;
+  cudaEvent_t ev;
+  cudaEventCreate(&ev);
+  cudaEventRecord(ev, e->st);
+  e->prof_ev.push_back(ev);
+  e->prof_kind.push_back(kind);
+}
+
+int gemv(InfernoEngine* e, int type, int inner, std::initializer_list<GemvMat> mats, const float* x, int pro,
+         const float* pro_w, const float* pro_z, int group, int epi, unsigned long long* argmax, bool pdl) {
+  GemvCall c;
+  c.type = type;
+  c.inner = inner;
+  for (auto& m : mats) c.mats[c.nmats++] = m;
+  c.x = x;
+  c.x_stride = inner;
+  c.pro = pro;
+  c.pro_w = pro_w;
+  c.pro_z = pro_z;
+  c.pro_group = group;
+  c.eps = e->cfg.rms_eps;
+  c.epi = epi;
+  c.argmax = argmax;
+  c.err = e->err;
+  int rc = launch_gemv(c, e->st, pdl);
+  if (!rc) mark(e, epi == EPI_ARGMAX ? K_LMHEAD : K_GEMV);
+  return rc;
+}
+
+GemvMat M(DevTensor* t, float* y) { return GemvMat{t->d, y, (int)t->rows()}; }
+
+int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
+  LayerBind& L = e->layers[li];
+  const InfernoConfig& c = e->cfg;
+  const int H = c.hidden_size;
+  int rc;
+  if (L.ssm) {
+    // [in_proj | attn_gate] on RMSNorm(x)
+    if (L.in_proj->type == L.gate->type) {
+      if ((rc = gemv(e, L.in_proj->type, H, {M(L.in_proj, e->qkv), M(L.gate, e->z)}, e->x, PRO_RMSNORM,
+                     (const float*)L.attn_norm->d, nullptr, 0, EPI_STORE, nullptr, pdl)))
+        return rc;
+    } else {
+      if ((rc = gemv(e, L.in_proj->type, H, {M(L.in_proj, e->qkv)}, e->x, PRO_RMSNORM, (const float*)L.attn_norm->d,
+                     nullptr, 0, EPI_STORE, nullptr, pdl)))
+        return rc;
+      if ((rc = gemv(e, L.gate->type, H, {M(L.gate, e->z)}, e->x, PRO_RMSNORM, (const float*)L.attn_norm->d,
+                     nullptr, 0, EPI_STORE, nullptr, pdl)))
+        return rc;
+    }
+    GdnParams g{};
+    g.x = e->x;
+    g.in_norm = (const float*)L.attn_norm->d;
+    g.eps = c.rms_eps;
+    g.H = H;
+    g.nv = c.ssm_nv;
+    g.nk = c.ssm_nk;
+    g.dv = c.ssm_dv;
+    g.K = c.ssm_conv_kernel;
+    g.C = e->C;
+    g.qkv = e->qkv;
+    g.conv_w = (const float*)L.conv1d->d;
+    g.ring = L.ring;
+    g.w_alpha = (const float*)L.alpha->d;
+    g.w_beta = (const float*)L.beta->d;
+    g.ssm_a = (const float*)L.ssm_a->d;
+    g.dt_bias = (const float*)L.dt_bias->d;
+    g.S = L.S;
+    g.y = e->y;
+    g.step = L.step;
+    g.done = L.done;
+    if ((rc = launch_gdn_step(g, e->st, pdl))) return rc;
+    mark(e, K_GDN);
+    if ((rc = gemv(e, L.ssm_out->type, e->di, {M(L.ssm_out, e->x)}, e->y, PRO_HEADNORM_GATE,
+                   (const float*)L.ssm_norm->d, e->z, c.ssm_dv, EPI_ADD, nullptr, pdl)))
+      return rc;
+  } else {
+    const int qrows = (int)L.wq->rows();
+    (void)qrows;
+    if (L.wq->type == L.wk->type && L.wk->type == L.wv->type) {
+      if ((rc = gemv(e, L.wq->type, H, {M(L.wq, e->qg), M(L.wk, e->k), M(L.wv, e->v)}, e->x, PRO_RMSNORM,
+                     (const float*)L.attn_norm->d, nullptr, 0, EPI_STORE, nullptr, pdl)))
+        return rc;
+    } else {
+      if ((rc = gemv(e, L.wq->type, H, {M(L.wq, e->qg), M(L.wk, e->k)}, e->x, PRO_RMSNORM,
+                     (const float*)L.attn_norm->d, nullptr, 0, EPI_STORE, nullptr, pdl)))
+        return rc;
+      if ((rc = gemv(e, L.wv->type, H, {M(L.wv, e->v)}, e->x, PRO_RMSNORM, (const float*)L.attn_norm->d, nullptr,
+                     0, EPI_STORE, nullptr, pdl)))
+        return rc;
+    }
+    AttnParams a{};
+    a.qg = e->qg;
+    a.k = e->k;
+    a.v = e->v;
+    a.q_norm = (const float*)L.q_norm->d;
+    a.k_norm = (const float*)L.k_norm->d;
+    a.eps = c.rms_eps;
+    a.rope_cos = e->rope_cos;
+    a.rope_sin = e->rope_sin;
+    a.rd = e->rd;
+    a.kc = L.kc;
+    a.vc = L.vc;
+    a.nh = c.n_heads;
+    a.nkv = c.n_kv_heads;
+    a.ctx = c.max_ctx;
+    a.split_len = e->split_len;
+    a.nsplit = e->nsplit;
+    a.pos = &e->ctl->pos;
+    a.part_o = e->part_o;
+    a.part_ml = e->part_ml;
+    a.counters = e->att_counters;
+    a.out = e->o;
+    a.err = e->err;
+    if ((rc = launch_attn_decode(a, e->st, pdl))) return rc;
+    mark(e, K_ATTN);
+    if ((rc = gemv(e, L.wo->type, c.n_heads * c.head_dim, {M(L.wo, e->x)}, e->o, PRO_NONE, nullptr, nullptr, 0,
+                   EPI_ADD, nullptr, pdl)))
+      return rc;
+  }
+  // FFN: SwiGLU(gate, up) on RMSNorm(x), then down with residual add
+  if (L.ffn_gate->type == L.ffn_up->type) {
+    if ((rc = gemv(e, L.ffn_gate->type, H, {M(L.ffn_gate, e->h), M(L.ffn_up, nullptr)}, e->x, PRO_RMSNORM,
+                   (const float*)L.post_norm->d, nullptr, 0, EPI_SWIGLU, nullptr, pdl)))
+      return rc;
+  } else {
+    return set_error(INFERNO_EINVAL, "layer %d: ffn_gate and ffn_up must share a type", li);
+  }
+  if ((rc = gemv(e, L.ffn_down->type, c.intermediate_size, {M(L.ffn_down, e->x)}, e->h, PRO_NONE, nullptr, nullptr,
+                 0, EPI_ADD, nullptr, pdl)))
+    return rc;
+  if (e->dump)
+    INF_CUDA_TRY(cudaMemcpyAsync(e->hidden + (size_t)li * H, e->x, (size_t)H * 4, cudaMemcpyDeviceToDevice, e->st));
+  return 0;
+}
+
+int launch_finalize(InfernoEngine* e, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(32);
+  cfg.stream = e->st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t r = cudaLaunchKernelEx(&cfg, finalize_kernel, e->ctl, (const int*)e->prompt, e->out_tokens, e->max_out);
+  if (r != cudaSuccess) return set_error(INFERNO_ECUDA, "finalize launch: %s", cudaGetErrorString(r));
+  mark(e, K_FINAL);
+  return 0;
+}
+
+int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
+  const InfernoConfig& c = e->cfg;
+  int rc;
+  e->launches = 0;
+  if (e->profiling) mark(e, -1), --e->launches;
+  if ((rc = launch_embed_row(e->embd->type, e->embd->d, (long long)e->embd->bytes / e->embd->rows(), c.hidden_size,
+                             &e->ctl->tok, e->x, c.vocab_size, e->st, pdl)))
+    return set_error(INFERNO_ECUDA, "embedding launch failed (%d)", rc);
+  mark(e, K_EMBED);
+  for (int i = 0; i < c.num_layers; ++i)
+    if ((rc = enqueue_layer(e, i, pdl))) return rc;
+  if ((rc = gemv(e, e->lm_head->type, c.hidden_size, {M(e->lm_head, write_logits ? e->logits : nullptr)}, e->x,
+                 PRO_RMSNORM, (const float*)e->out_norm->d, nullptr, 0, EPI_ARGMAX, &e->ctl->argkey, pdl)))
+    return rc;
+  return launch_finalize(e, pdl);
+}
+
+int capture(InfernoEngine* e, int ntok, bool logits, cudaGraphExec_t* out) {
+  cudaGraph_t g = nullptr;
+  INF_CUDA_TRY(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+  int rc = 0;
+  for (int t = 0; t < ntok && !rc; ++t) rc = enqueue_token(e, logits && t == ntok - 1, e->cfg.use_pdl != 0);
+  cudaError_t r = cudaStreamEndCapture(e->st, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (r != cudaSuccess) return set_error(INFERNO_ECUDA, "graph capture failed: %s", cudaGetErrorString(r));
+  r = cudaGraphInstantiate(out, g, 0);
+  cudaGraphDestroy(g);
+  if (r != cudaSuccess) return set_error(INFERNO_ECUDA, "graph instantiate failed: %s", cudaGetErrorString(r));
+  return 0;
+}
+
+int check_device_error(InfernoEngine* e) {
+  int v = 0;
+  INF_CUDA_TRY(cudaMemcpy(&v, e->err, sizeof v, cudaMemcpyDeviceToHost));
+  if (v) {
+    cudaMemset(e->err, 0, sizeof(int));
+    return set_error(INFERNO_EDEVICE, "a kernel reported device error %d (1 = bounded wait timed out, 2 = bad "
+                                      "argument such as a position beyond max_ctx)", v);
+  }
+  return 0;
+}
+
+// run `n` steps: graph replays (8-token graph for bulk) or eager launches
+int run_steps(InfernoEngine* e, int n, bool logits_last) {
+  int rc;
+  if (e->cfg.use_graphs && !e->dump) {
+    int left = n;
+    while (left >= 8 + (logits_last ? 1 : 0)) {
+      INF_CUDA_TRY(cudaGraphLaunch(e->g8, e->st));
+      left -= 8;
+    }
+    while (left > 0) {
+      INF_CUDA_TRY(cudaGraphLaunch((left == 1 && logits_last) ? e->g1_logits : e->g1, e->st));
+      --left;
+    }
+  } else {
+    for (int t = 0; t < n; ++t)
+      if ((rc = enqueue_token(e, logits_last && t == n - 1, e->cfg.use_pdl != 0))) return rc;
+  }
+  return 0;
+}
+
+void build_rope(int ctx, int rd, float theta, std::vector<float>& cs, std::vector<float>& sn) {
+  // src/ModelCPU.jl:134-153: inv_freq in Float64 rounded to Float32, angle in
+  // Float32, cos/sin of that Float32 angle (correctly rounded here).
+  const int half = rd / 2;
+  cs.assign((size_t)ctx * half, 0.f);
+  sn.assign((size_t)ctx * half, 0.f);
+  for (int i = 0; i < half; ++i) {
+    float inv = (float)(1.0 / std::pow((double)theta, (2.0 * i) / (double)rd));
+    for (int p = 0; p < ctx; ++p) {
+      float f = inv * (float)p;
+      cs[(size_t)p * half + i] = (float)std::cos((double)f);
+      sn[(size_t)p * half + i] = (float)std::sin((double)f);
+    }
+  }
+}
+
+}  // namespace
+}  // namespace inf
+
+using namespace inf;
+
+extern "C" {
+
+int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
+  if (!cfg || !out) return set_error(INFERNO_EINVAL, "engine_create: null argument");
+  if (cfg->struct_size != (int)sizeof(InfernoConfig))
+    return set_error(INFERNO_EINVAL, "engine_create: struct_size %d != %d (header mismatch)", cfg->struct_size,
+                     (int)sizeof(InfernoConfig));
+  const InfernoConfig& c = *cfg;
+  if (c.hidden_size <= 0 || c.hidden_size % 256 || c.num_layers <= 0 || c.vocab_size <= 0)
+    return set_error(INFERNO_EINVAL, "engine_create: hidden_size must be a positive multiple of 256");
+  if (c.head_dim != 256) return set_error(INFERNO_EINVAL, "engine_create: head_dim %d unsupported (256)", c.head_dim);
+  if (c.ssm_dk != 128) return set_error(INFERNO_EINVAL, "engine_create: ssm state size %d unsupported (128)", c.ssm_dk);
+  if (c.ssm_nk <= 0 || c.ssm_nv % c.ssm_nk) return set_error(INFERNO_EINVAL, "engine_create: nv %% nk != 0");
+  if (c.max_ctx <= 0) return set_error(INFERNO_EINVAL, "engine_create: max_ctx must be positive");
+  if (c.max_batch > 1) return set_error(INFERNO_EINVAL, "engine_create: max_batch > 1 is not supported yet");
+  if (c.tp_size > 1) return set_error(INFERNO_EINVAL, "engine_create: tensor parallel needs the TP build");
+  auto* e = new InfernoEngine();
+  e->cfg = c;
+  e->dev = c.device;
+  if (cudaSetDevice(e->dev) != cudaSuccess) {
+    delete e;
+    return set_error(INFERNO_ECUDA, "cudaSetDevice(%d) failed", c.device);
+  }
+  if (cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking) != cudaSuccess) {
+    delete e;
+    return set_error(INFERNO_ECUDA, "stream creation failed");
+  }
+  cudaEventCreate(&e->ev0);
+  cudaEventCreate(&e->ev1);
+  const char* d = getenv("INFERNO_B200_DUMP");
+  e->dump = d && atoi(d) != 0;
+  *out = e;
+  return 0;
+}
+
+int inferno_engine_upload_tensor(InfernoEngine* e, const char* name, int ggml_type, const int64_t ne[4],
+                                 const void* host, size_t nbytes) {
+  if (!e || !name || !ne || !host) return set_error(INFERNO_EINVAL, "upload: null argument");
+  if (e->finalized) return set_error(INFERNO_ESTATE, "upload after finalize");
+  if (!type_supported(ggml_type)) return set_error(INFERNO_EINVAL, "upload %s: unsupported ggml type %d", name, ggml_type);
+  int64_t n = ne[0] * ne[1] * ne[2] * ne[3];
+  if (ne[0] <= 0 || n <= 0 || ne[0] % qk_of(ggml_type))
+    return set_error(INFERNO_EINVAL, "upload %s: bad dims", name);
+  size_t want = (size_t)(n / qk_of(ggml_type)) * bb_of(ggml_type);
+  if (want != nbytes)
+    return set_error(INFERNO_EINVAL, "upload %s: %zu bytes given, %zu expected for its type and dims", name, nbytes,
+                     want);
+  INF_CUDA_TRY(cudaSetDevice(e->dev));
+  DevTensor t;
+  t.type = ggml_type;
+  for (int i = 0; i < 4; ++i) t.ne[i] = ne[i];
+  t.bytes = nbytes;
+  if (cudaMalloc(&t.d, (nbytes + 255) / 256 * 256) != cudaSuccess)
+    return set_error(INFERNO_ENOMEM, "upload %s: cudaMalloc(%zu) failed", name, nbytes);
+  INF_CUDA_TRY(cudaMemcpy(t.d, host, nbytes, cudaMemcpyHostToDevice));
+  auto it = e->tensors.find(name);
+  if (it != e->tensors.end()) cudaFree(it->second.d);
+  e->tensors[name] = t;
+  return 0;
+}
+
+int inferno_engine_finalize(InfernoEngine* e) {
+  if (!e) return set_error(INFERNO_EINVAL, "finalize: null engine");
+  if (e->finalized) return 0;
+  INF_CUDA_TRY(cudaSetDevice(e->dev));
+  InfernoConfig& c = e->cfg;
+  int rc;
+  if ((rc = require(e, "token_embd.weight", &e->embd))) return rc;
+  if ((rc = require(e, "output_norm.weight", &e->out_norm, T_F32))) return rc;
+  e->lm_head = find(e, "output.weight");
+  if (!e->lm_head) e->lm_head = e->embd;   // tied (src/LoaderCPU.jl:358-371)
+  if (e->embd->ne[0] != c.hidden_size || e->embd->rows() != c.vocab_size)
+    return set_error(INFERNO_EINVAL, "token_embd dims do not match hidden/vocab");
+  e->di = c.ssm_nv * c.ssm_dv;
+  e->C = 2 * c.ssm_nk * c.ssm_dk + e->di;
+  e->layers.resize(c.num_layers);
+  bool any_attn = false;
+  for (int i = 0; i < c.num_layers; ++i) {
+    const std::string p = "blk." + std::to_string(i) + ".";
+    LayerBind& L = e->layers[i];
+    if ((rc = require(e, p + "attn_norm.weight", &L.attn_norm, T_F32)) ||
+        (rc = require(e, p + "post_attention_norm.weight", &L.post_norm, T_F32)))
+      return rc;
+    L.ssm = find(e, p + "ssm_a") != nullptr;   // src/LoaderCPU.jl:431
+    if (L.ssm) {
+      if ((rc = require(e, p + "attn_qkv.weight", &L.in_proj)) || (rc = require(e, p + "attn_gate.weight", &L.gate)) ||
+          (rc = require(e, p + "ssm_out.weight", &L.ssm_out)) ||
+          (rc = require(e, p + "ssm_conv1d.weight", &L.conv1d, T_F32)) ||
+          (rc = require(e, p + "ssm_alpha.weight", &L.alpha, T_F32)) ||
+          (rc = require(e, p + "ssm_beta.weight", &L.beta, T_F32)) || (rc = require(e, p + "ssm_a", &L.ssm_a, T_F32)) ||
+          (rc = require(e, p + "ssm_dt.bias", &L.dt_bias, T_F32)) ||
+          (rc = require(e, p + "ssm_norm.weight", &L.ssm_norm, T_F32)))
+        return rc;
+      if (L.in_proj->rows() != e->C || L.gate->rows() != e->di || L.ssm_out->ne[0] != e->di ||
+          L.conv1d->ne[0] != c.ssm_conv_kernel || L.conv1d->ne[1] != e->C || L.alpha->rows() != c.ssm_nv ||
+          L.ssm_norm->ne[0] != c.ssm_dv)
+        return set_error(INFERNO_EINVAL, "layer %d: GDN tensor dims do not match the config", i);
+      if ((rc = dalloc(e, &L.ring, (size_t)c.ssm_conv_kernel * e->C, true)) ||
+          (rc = dalloc(e, &L.S, (size_t)c.ssm_nv * c.ssm_dv * c.ssm_dk, true)) || (rc = dalloc(e, &L.step, 4, true)) ||
+          (rc = dalloc(e, &L.done, 4)))
+        return rc;
+    } else {
+      any_attn = true;
+      if ((rc = require(e, p + "attn_q.weight", &L.wq)) || (rc = require(e, p + "attn_k.weight", &L.wk)) ||
+          (rc = require(e, p + "attn_v.weight", &L.wv)) || (rc = require(e, p + "attn_output.weight", &L.wo)) ||
+          (rc = require(e, p + "attn_q_norm.weight", &L.q_norm, T_F32)) ||
+          (rc = require(e, p + "attn_k_norm.weight", &L.k_norm, T_F32)))
+        return rc;
+      if (L.wq->rows() != 2LL * c.n_heads * c.head_dim || L.wk->rows() != (int64_t)c.n_kv_heads * c.head_dim ||
+          L.wo->ne[0] != (int64_t)c.n_heads * c.head_dim)
+        return set_error(INFERNO_EINVAL, "layer %d: attention tensor dims do not match the config", i);
+      size_t kv = (size_t)c.max_ctx * c.n_kv_heads * c.head_dim;
+      if ((rc = dalloc(e, &L.kc, kv, true)) || (rc = dalloc(e, &L.vc, kv, true))) return rc;
+    }
+    if (c.n_experts) return set_error(INFERNO_EINVAL, "MoE layers need the MoE build");
+    if ((rc = require(e, p + "ffn_gate.weight", &L.ffn_gate)) || (rc = require(e, p + "ffn_up.weight", &L.ffn_up)) ||
+        (rc = require(e, p + "ffn_down.weight", &L.ffn_down)))
+      return rc;
+    if (L.ffn_gate->rows() != c.intermediate_size || L.ffn_down->ne[0] != c.intermediate_size)
+      return set_error(INFERNO_EINVAL, "layer %d: FFN dims do not match the config", i);
+  }
+  const int H = c.hidden_size;
+  if ((rc = dalloc(e, &e->x, H)) || (rc = dalloc(e, &e->qkv, e->C)) || (rc = dalloc(e, &e->z, e->di)) ||
+      (rc = dalloc(e, &e->y, e->di)) || (rc = dalloc(e, &e->qg, (size_t)2 * c.n_heads * c.head_dim)) ||
+      (rc = dalloc(e, &e->k, (size_t)c.n_kv_heads * c.head_dim)) ||
+      (rc = dalloc(e, &e->v, (size_t)c.n_kv_heads * c.head_dim)) ||
+      (rc = dalloc(e, &e->o, (size_t)c.n_heads * c.head_dim)) || (rc = dalloc(e, &e->h, c.intermediate_size)) ||
+      (rc = dalloc(e, &e->logits, c.vocab_size)) || (rc = dalloc(e, &e->hidden, (size_t)c.num_layers * H)) ||
+      (rc = dalloc(e, &e->ctl, 1)) || (rc = dalloc(e, &e->prompt, c.max_ctx + 8)) ||
+      (rc = dalloc(e, &e->out_tokens, c.max_ctx + 8)) || (rc = dalloc(e, &e->err, 1)))
+    return rc;
+  e->max_out = c.max_ctx + 8;
+  // attention splits: at least 64 positions, at most 128 splits
+  e->split_len = 64;
+  while ((c.max_ctx + e->split_len - 1) / e->split_len > 128 && e->split_len < 256) e->split_len *= 2;
+  e->nsplit = (c.max_ctx + e->split_len - 1) / e->split_len;
+  e->rd = (int)std::lround(c.head_dim * (double)c.partial_rotary_factor);   // src/LoaderCPU.jl:375
+  if (any_attn) {
+    if ((rc = dalloc(e, &e->part_o, (size_t)c.n_heads * e->nsplit * c.head_dim)) ||
+        (rc = dalloc(e, &e->part_ml, (size_t)c.n_heads * e->nsplit * 2)) ||
+        (rc = dalloc(e, &e->att_counters, c.n_kv_heads)))
+      return rc;
+    std::vector<float> cs, sn;
+    build_rope(c.max_ctx, e->rd, c.rope_theta, cs, sn);
+    if ((rc = dalloc(e, &e->rope_cos, cs.size() + 1)) || (rc = dalloc(e, &e->rope_sin, sn.size() + 1))) return rc;
+    INF_CUDA_TRY(cudaMemcpy(e->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    INF_CUDA_TRY(cudaMemcpy(e->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  }
+  INF_CUDA_TRY(cudaDeviceSynchronize());
+  e->finalized = true;
+  if (c.use_graphs && !e->dump) {
+    if ((rc = capture(e, 1, false, &e->g1)) || (rc = capture(e, 1, true, &e->g1_logits)) ||
+        (rc = capture(e, 8, false, &e->g8))) {
+      e->finalized = false;
+      return rc;
+    }
+  }
+  return 0;
+}
+
+static int ready(InfernoEngine* e) {
+  if (!e) return set_error(INFERNO_EINVAL, "null engine");
+  if (!e->finalized) return set_error(INFERNO_ESTATE, "engine not finalized");
+  INF_CUDA_TRY(cudaSetDevice(e->dev));
+  return 0;
+}
+
+static int set_ctl(InfernoEngine* e, int tok, int pos, int n_prompt) {
+  Ctl h{};
+  h.tok = tok;
+  h.pos = pos;
+  h.step = 0;
+  h.n_prompt = n_prompt;
+  h.argkey = 0;
+  INF_CUDA_TRY(cudaMemcpyAsync(e->ctl, &h, sizeof h, cudaMemcpyHostToDevice, e->st));
+  return 0;
+}
+
+int inferno_layer_forward(InfernoEngine* e, int layer, float* x_host, int pos) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  if (layer < 0 || layer >= e->cfg.num_layers || !x_host) return set_error(INFERNO_EINVAL, "layer_forward: bad layer");
+  if (pos < 0 || pos >= e->cfg.max_ctx) return set_error(INFERNO_EINVAL, "layer_forward: pos %d outside [0, %d)", pos, e->cfg.max_ctx);
+  const int H = e->cfg.hidden_size;
+  if ((rc = set_ctl(e, 0, pos, 1))) return rc;
+  INF_CUDA_TRY(cudaMemcpyAsync(e->x, x_host, (size_t)H * 4, cudaMemcpyHostToDevice, e->st));
+  if ((rc = enqueue_layer(e, layer, false))) return rc;
+  INF_CUDA_TRY(cudaMemcpyAsync(x_host, e->x, (size_t)H * 4, cudaMemcpyDeviceToHost, e->st));
+  INF_CUDA_TRY(cudaStreamSynchronize(e->st));
+  return check_device_error(e);
+}
+
+int inferno_forward_tokens(InfernoEngine* e, const int32_t* tok, int n, int pos0, float* logits_out,
+                           int32_t* argmax_out) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  if (!tok || n <= 0) return set_error(INFERNO_EINVAL, "forward_tokens: no tokens");
+  if (pos0 < 0 || pos0 + n > e->cfg.max_ctx)
+    return set_error(INFERNO_EINVAL, "forward_tokens: positions [%d, %d) exceed max_ctx %d", pos0, pos0 + n, e->cfg.max_ctx);
+  for (int i = 0; i < n; ++i)
+    if (tok[i] < 0 || tok[i] >= e->cfg.vocab_size) return set_error(INFERNO_EINVAL, "forward_tokens: token %d out of range", tok[i]);
+  INF_CUDA_TRY(cudaMemcpyAsync(e->prompt, tok, (size_t)n * 4, cudaMemcpyHostToDevice, e->st));
+  if ((rc = set_ctl(e, tok[0], pos0, n))) return rc;
+  if ((rc = run_steps(e, n, logits_out != nullptr))) return rc;
+  Ctl h{};
+  INF_CUDA_TRY(cudaMemcpyAsync(&h, e->ctl, sizeof h, cudaMemcpyDeviceToHost, e->st));
+  if (logits_out)
+    INF_CUDA_TRY(cudaMemcpyAsync(logits_out, e->logits, (size_t)e->cfg.vocab_size * 4, cudaMemcpyDeviceToHost, e->st));
+  INF_CUDA_TRY(cudaStreamSynchronize(e->st));
+  if ((rc = check_device_error(e))) return rc;
+  if (argmax_out) *argmax_out = h.last;
+  return 0;
+}
+
+int inferno_decode_greedy(InfernoEngine* e, int32_t tok, int pos, int n_steps, int32_t* out_tokens) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  if (n_steps <= 0 || !out_tokens) return set_error(INFERNO_EINVAL, "decode_greedy: bad n_steps/out");
+  if (pos < 0 || pos + n_steps > e->cfg.max_ctx)
+    return set_error(INFERNO_EINVAL, "decode_greedy: positions [%d, %d) exceed max_ctx %d", pos, pos + n_steps,
+                     e->cfg.max_ctx);
+  if (tok < 0 || tok >= e->cfg.vocab_size) return set_error(INFERNO_EINVAL, "decode_greedy: token out of range");
+  if (n_steps > e->max_out) return set_error(INFERNO_EINVAL, "decode_greedy: n_steps too large");
+  if ((rc = set_ctl(e, tok, pos, 1))) return rc;
+  INF_CUDA_TRY(cudaEventRecord(e->ev0, e->st));
+  if ((rc = run_steps(e, n_steps, false))) return rc;
+  INF_CUDA_TRY(cudaEventRecord(e->ev1, e->st));
+  INF_CUDA_TRY(cudaMemcpyAsync(out_tokens, e->out_tokens, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, e->st));
+  INF_CUDA_TRY(cudaStreamSynchronize(e->st));
+  cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1);
+  return check_device_error(e);
+}
+
+float inferno_last_decode_ms(InfernoEngine* e) { return e ? e->last_ms : -1.f; }
+
+int inferno_reset_states(InfernoEngine* e) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  for (auto& b : e->state_bufs) INF_CUDA_TRY(cudaMemsetAsync(b.first, 0, b.second, e->st));
+  INF_CUDA_TRY(cudaStreamSynchronize(e->st));
+  return 0;
+}
+
+int inferno_dump_hidden(InfernoEngine* e, int layer, float* out) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  if (!e->dump) return set_error(INFERNO_ESTATE, "dump_hidden needs INFERNO_B200_DUMP=1 at engine creation");
+  if (layer < 0 || layer >= e->cfg.num_layers || !out) return set_error(INFERNO_EINVAL, "dump_hidden: bad layer");
+  INF_CUDA_TRY(cudaMemcpy(out, e->hidden + (size_t)layer * e->cfg.hidden_size, (size_t)e->cfg.hidden_size * 4,
+                          cudaMemcpyDeviceToHost));
+  return 0;
+}
+
+int64_t inferno_state_size(InfernoEngine* e) {
+  if (ready(e)) return INFERNO_ESTATE;
+  int64_t s = 0;
+  for (auto& b : e->state_bufs) s += (int64_t)b.second;
+  return s;
+}
+
+int inferno_state_export(InfernoEngine* e, void* host, int64_t nbytes) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  if (nbytes < inferno_state_size(e) || !host) return set_error(INFERNO_EINVAL, "state_export: buffer too small");
+  char* p = (char*)host;
+  for (auto& b : e->state_bufs) {
+    INF_CUDA_TRY(cudaMemcpyAsync(p, b.first, b.second, cudaMemcpyDeviceToHost, e->st));
+    p += b.second;
+  }
+  INF_CUDA_TRY(cudaStreamSynchronize(e->st));
+  return 0;
+}
+
+int inferno_state_import(InfernoEngine* e, const void* host, int64_t nbytes) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  if (nbytes != inferno_state_size(e) || !host) return set_error(INFERNO_EINVAL, "state_import: size mismatch");
+  const char* p = (const char*)host;
+  for (auto& b : e->state_bufs) {
+    INF_CUDA_TRY(cudaMemcpyAsync(b.first, p, b.second, cudaMemcpyHostToDevice, e->st));
+    p += b.second;
+  }
+  INF_CUDA_TRY(cudaStreamSynchronize(e->st));
+  return 0;
+}
+
+int inferno_state_save_device(InfernoEngine* e) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  size_t tot = 0;
+  for (auto& b : e->state_bufs) tot += b.second;
+  if (!e->snapshot) {
+    if (cudaMalloc(&e->snapshot, tot) != cudaSuccess) return set_error(INFERNO_ENOMEM, "snapshot alloc (%zu B)", tot);
+    e->state_bytes = tot;
+  }
+  char* p = (char*)e->snapshot;
+  for (auto& b : e->state_bufs) {
+    INF_CUDA_TRY(cudaMemcpyAsync(p, b.first, b.second, cudaMemcpyDeviceToDevice, e->st));
+    p += b.second;
+  }
+  return 0;
+}
+
+int inferno_state_restore_device(InfernoEngine* e) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  if (!e->snapshot) return set_error(INFERNO_ESTATE, "no device snapshot saved");
+  const char* p = (const char*)e->snapshot;
+  for (auto& b : e->state_bufs) {
+    INF_CUDA_TRY(cudaMemcpyAsync(b.first, p, b.second, cudaMemcpyDeviceToDevice, e->st));
+    p += b.second;
+  }
+  return 0;
+}
+
+int inferno_kernels_per_token(InfernoEngine* e) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  return e->launches;
+}
+
+int inferno_profile_tokens(InfernoEngine* e, int32_t tok, int pos, int n_tokens, float* ms_by_class,
+                           int32_t* launches_by_class) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  if (n_tokens <= 0 || pos < 0 || pos + n_tokens > e->cfg.max_ctx || !ms_by_class || !launches_by_class)
+    return set_error(INFERNO_EINVAL, "profile_tokens: bad arguments");
+  for (int k = 0; k < K_NCLASS; ++k) { ms_by_class[k] = 0.f; launches_by_class[k] = 0; }
+  if ((rc = set_ctl(e, tok, pos, 1))) return rc;
+  for (int t = 0; t < n_tokens; ++t) {
+    e->profiling = true;
+    rc = enqueue_token(e, false, false);
+    e->profiling = false;
+    if (!rc) {
+      cudaError_t r = cudaStreamSynchronize(e->st);
+      if (r != cudaSuccess) rc = set_error(INFERNO_ECUDA, "profile sync: %s", cudaGetErrorString(r));
+    }
+    for (size_t i = 1; i < e->prof_ev.size() && !rc; ++i) {
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, e->prof_ev[i - 1], e->prof_ev[i]);
+      int k = e->prof_kind[i];
+      if (k >= 0 && k < K_NCLASS) { ms_by_class[k] += ms; launches_by_class[k] += 1; }
+    }
+    for (auto ev : e->prof_ev) cudaEventDestroy(ev);
+    e->prof_ev.clear();
+    e->prof_kind.clear();
+    if (rc) return rc;
+  }
+  return check_device_error(e);
+}
+
+int inferno_engine_destroy(InfernoEngine* e) {
+  if (!e) return 0;
+  cudaSetDevice(e->dev);
+  cudaStreamSynchronize(e->st);
+  if (e->g1) cudaGraphExecDestroy(e->g1);
+  if (e->g1_logits) cudaGraphExecDestroy(e->g1_logits);
+  if (e->g8) cudaGraphExecDestroy(e->g8);
+  if (e->snapshot) cudaFree(e->snapshot);
+  for (auto& kv : e->tensors) cudaFree(kv.second.d);
+  for (void* p : e->allocs) cudaFree(p);
+  if (e->ev0) cudaEventDestroy(e->ev0);
+  if (e->ev1) cudaEventDestroy(e->ev1);
+  cudaStreamDestroy(e->st);
+  delete e;
+  return 0;
+}
+
+}  // extern "C"

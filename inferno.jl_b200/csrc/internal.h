@@ -1,0 +1,58 @@
+// Host-side internal declarations shared by the engine's translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string>
+
+namespace inf {
+
+// ---- error channel (thread-local last error, int status codes) ------------
+int set_error(int code, const char* fmt, ...);
+const char* last_error();
+
+#define INF_CUDA_TRY(expr)                                                            \
+  do {                                                                                \
+    cudaError_t e_ = (expr);                                                          \
+    if (e_ != cudaSuccess)                                                            \
+      return ::inf::set_error(-2, "%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), \
+                              __FILE__, __LINE__);                                    \
+  } while (0)
+
+int num_sms(int device);
+
+// ---- kernel launchers (return 0 or a negative status) ---------------------
+struct GemvMat {
+  const void* W;   // device, 16-byte aligned
+  float* y;        // device output rows
+  int rows;
+};
+
+struct GemvCall {
+  int type = 0;
+  int inner = 0;
+  GemvMat mats[4];
+  int nmats = 0;
+  int nb = 1;
+  const float* x = nullptr;
+  long long x_stride = 0;     // elements between batch columns of x
+  long long y_stride = 0;     // elements between batch columns of y
+  int pro = 0;
+  const float* pro_w = nullptr;
+  const float* pro_z = nullptr;
+  float eps = 1e-6f;
+  int pro_group = 0;
+  int epi = 0;
+  unsigned long long* argmax = nullptr;
+  int* err = nullptr;
+  int force_r = 0;            // 0 = planner's choice
+};
+
+int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl);
+int launch_dequant(int type, const void* src, long long n, float* dst, cudaStream_t st);
+int launch_embed_row(int type, const void* W, long long row_bytes, int inner, const int* row_ptr, float* dst,
+                     int vocab, cudaStream_t st, bool pdl);
+
+// device error word of the library (per device)
+int* device_error_word(int device);
+
+}  // namespace inf

@@ -1,0 +1,50 @@
+// Parameter blocks of the decode-step kernels (shared by the kernels and the
+// engine that launches them).
+#pragma once
+#include <cuda_runtime.h>
+
+namespace inf {
+
+struct GdnParams {
+  const float* x;          // residual stream (pre-norm) [H]
+  const float* in_norm;    // [H]
+  float eps;
+  int H, nv, nk, dv, K, C;
+  const float* qkv;        // in_proj output [C]
+  const float* conv_w;     // [C][K] (GGUF ssm_conv1d data, w[c,k] at k + K*c)
+  float* ring;             // [K][C]
+  const float* w_alpha;    // [nv][H]
+  const float* w_beta;     // [nv][H]
+  const float* ssm_a;      // [nv]
+  const float* dt_bias;    // [nv]
+  float* S;                // [nv][dv][dk]
+  float* y;                // [nv*dv] pre-norm output
+  int* step;               // per-layer step counter
+  int* done;               // per-layer CTA completion counter
+};
+
+struct AttnParams {
+  const float* qg;       // [nh][2*hd]: per head q then gate (src/ModelCPU.jl:766-772)
+  const float* k;        // [nkv*hd] new key (pre-norm)
+  const float* v;        // [nkv*hd]
+  const float* q_norm;   // [hd]
+  const float* k_norm;   // [hd]
+  float eps;
+  const float* rope_cos; // [ctx][rd/2]
+  const float* rope_sin;
+  int rd;
+  float* kc;             // [ctx][nkv][hd]
+  float* vc;
+  int nh, nkv, ctx, split_len, nsplit;
+  const int* pos;        // device scalar
+  float* part_o;         // [nh][nsplit][hd]
+  float* part_ml;        // [nh][nsplit][2]
+  int* counters;         // [nkv]
+  float* out;            // [nh*hd] gated attention output
+  int* err;
+};
+
+int launch_gdn_step(const GdnParams& p, cudaStream_t st, bool pdl);
+int launch_attn_decode(const AttnParams& p, cudaStream_t st, bool pdl);
+
+}  // namespace inf

@@ -1,0 +1,120 @@
+"""GPU parity of the decode engine against the CPU oracle on seeded models:
+per-layer hidden states (rel 2e-3), logits, greedy token identity, state
+export/import and reset.  All calls go through the C ABI."""
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from inferno_b200 import synth as S
+from inferno_b200.model import Model
+
+pytestmark = pytest.mark.gpu
+
+LAYER_RTOL = 2e-3      # per-layer hidden state, max|d| / max|ref| (north_star)
+LOGIT_RTOL = 2e-3
+
+
+def rel(a, b):
+    return float(np.abs(a - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    spec = S.CONFIGS["tiny"]
+    T = S.make_model(spec, seed=11)
+    return spec, T, O.OracleModel(spec, T)
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_tiny_generate_matches_oracle(tiny, graphs):
+    spec, T, orc = tiny
+    prompt = S.tokens(11, 12, spec.vocab)
+    m = Model(spec, T, use_graphs=graphs)
+    got = m.generate(prompt, 24)
+    want = orc.generate(prompt, 24)
+    m.close()
+    assert got == want
+
+
+def test_tiny_logits_and_layers(tiny):
+    spec, T, orc = tiny
+    prompt = S.tokens(12, 9, spec.vocab)
+    m = Model(spec, T)
+    orc.reset()
+    m.reset()
+    am_o, lg_o = orc.forward(prompt, 0)
+    am_g, lg_g = m.forward(prompt, 0)
+    assert rel(lg_g, lg_o) < LOGIT_RTOL
+    assert am_g == am_o
+    # layer-by-layer on the same input, continuing at the next position
+    x = orc.embed(int(am_o))
+    for i in range(spec.layers):
+        xo = orc.layer(i, x, len(prompt))
+        xg = m.layer(i, x, len(prompt))
+        assert rel(xg, xo) < LAYER_RTOL, (i, rel(xg, xo))
+        x = xo
+    m.close()
+
+
+def test_tiny_dump_hidden(tiny, monkeypatch):
+    spec, T, orc = tiny
+    monkeypatch.setenv("INFERNO_B200_DUMP", "1")
+    m = Model(spec, T)
+    prompt = S.tokens(13, 7, spec.vocab)
+    orc.reset()
+    orc.forward(prompt, 0, want_logits=False)
+    m.forward(prompt, 0, want_logits=False)
+    for i in range(spec.layers):
+        assert rel(m.hidden(i), orc.hidden(i)) < LAYER_RTOL, i
+    m.close()
+
+
+def test_state_export_import_and_reset(tiny):
+    spec, T, _ = tiny
+    m = Model(spec, T)
+    prompt = S.tokens(14, 10, spec.vocab)
+    m.reset()
+    tok, _ = m.forward(prompt, 0, want_logits=False)
+    snap = m.state_export()
+    a = m.decode_greedy(tok, len(prompt), 6)
+    m.state_import(snap)
+    b = m.decode_greedy(tok, len(prompt), 6)
+    assert np.array_equal(a, b)
+    m.reset()
+    t2, _ = m.forward(prompt, 0, want_logits=False)
+    assert t2 == tok
+    m.close()
+
+
+def test_errors_are_reported(tiny):
+    from inferno_b200._lib import InfernoError
+    spec, T, _ = tiny
+    m = Model(spec, T)
+    with pytest.raises(InfernoError):
+        m.forward([spec.vocab + 5], 0)            # token out of range
+    with pytest.raises(InfernoError):
+        m.decode_greedy(1, spec.ctx - 2, 8)       # beyond max_ctx
+    with pytest.raises(InfernoError):
+        m.layer(spec.layers, np.zeros(spec.hidden, np.float32), 0)
+    m.close()
+    bad = dict(T)
+    del bad["blk.0.ssm_a"]
+    with pytest.raises(InfernoError):
+        Model(spec, bad)                            # layer 0 becomes attention without its tensors
+
+
+@pytest.mark.skipif(os.environ.get("INFERNO_SKIP_08B") == "1", reason="config-1 test disabled")
+def test_config1_greedy_identity():
+    """Config 1 (0.8B-shaped hybrid): 32-token prompt, 64 greedy tokens
+    identical to the oracle's (north_star asks >= 64)."""
+    spec = S.CONFIGS["qwen35-0.8b"]
+    T = S.make_model(spec, seed=0)
+    prompt = S.tokens(0, 32, spec.vocab)
+    m = Model(spec, T, max_ctx=512)
+    got = m.generate(prompt, 64)
+    m.close()
+    orc = O.OracleModel(spec, T)
+    want = orc.generate(prompt, 64)
+    assert got == want
