@@ -98,6 +98,17 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def max_over_ranks(v: float, device: str = "cuda") -> float:
+    """Max of a per-rank scalar over all ranks (device times: slowest rank)."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return float(v)
+    t = torch.tensor([float(v)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 def build_model(spec_name="qwen35-0.8b"):
     from inferno_b200 import synth as S
     spec = S.CONFIGS[spec_name]
@@ -216,11 +227,7 @@ def run_ours(args):
     wall = time.perf_counter() - wall0
     clk = clocks.stop()
     assert np.array_equal(out, ref_tokens), "decode is not deterministic across steps"
-    ms_step = t_dev / args.steps
-    if ws > 1:
-        t = torch.tensor([ms_step], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms_step = float(t.item())
+    ms_step = max_over_ranks(t_dev / args.steps)
     value = ws * NDEC / (ms_step / 1000.0)
 
     # ---- e2e through the public API (host prompt in, host tokens out) ----
@@ -230,11 +237,7 @@ def run_ours(args):
     for _ in range(e2e_steps):
         toks = m.generate(prompt, NDEC + 1)      # prefill + 128 decode tokens
     torch.cuda.synchronize()
-    e2e_s = (time.perf_counter() - w0) / e2e_steps
-    if ws > 1:
-        t = torch.tensor([e2e_s], device="cuda")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_s = float(t.item())
+    e2e_s = max_over_ranks((time.perf_counter() - w0) / e2e_steps)
     e2e = {"value": ws * NDEC / e2e_s, "unit": UNIT, "h2d_bytes_per_step": PROMPT * 4 + 32,
            "d2h_bytes_per_step": (NDEC + 1) * 4 + 32,
            "note": "wall time of Model.generate (reset, prompt H2D, 32-token prefill, 128 greedy tokens, "

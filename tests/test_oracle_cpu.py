@@ -1,0 +1,160 @@
+"""CPU tests of the oracle (test infrastructure): pinned against the
+reference's known-answer tests, against gguf-py golden vectors, and against an
+independent numpy restatement of the forward pass."""
+import math
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle as O
+from inferno_b200 import synth as S
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "dequant_golden.npz"
+REF_QUANTSDATA = Path("/root/reference/src/QuantsData.jl")
+
+
+# ---- tests/unit/core_components.jl:114-122 (IQ2_XXS known answers) --------
+def test_iq2xxs_known_answers():
+    data = np.zeros(66, np.uint8)
+    data[1] = 0x3C                     # d = 1.0
+    y = O.dequant(S.IQ2_XXS, data, 256)
+    assert np.all(y == 0)
+    data[2] = 0x01                     # grid[1] = 0x08...082b
+    y = O.dequant(S.IQ2_XXS, data, 256)
+    assert y[0] == np.float32(4.375)   # (43 - 8) * 0.125
+    assert np.all(y[1:8] == 0)
+
+
+def test_iq2xxs_grid_matches_reference_source():
+    if not REF_QUANTSDATA.exists():
+        pytest.skip("reference tree not present")
+    import importlib.util
+    spec = importlib.util.spec_from_file_location(
+        "gen", Path(__file__).resolve().parent.parent / "inferno.jl_b200" / "csrc" / "gen_iq2xxs_grid.py")
+    gen = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gen)
+    ref = np.array(gen.extract(REF_QUANTSDATA.read_text()), dtype=np.uint64)
+    assert np.array_equal(ref, S.IQ2XXS_GRID)
+
+
+def test_ksigns_table():
+    # src/QuantsData.jl:7-16 first row
+    assert list(S.KSIGNS[:16]) == [0, 129, 130, 3, 132, 5, 6, 135, 136, 9, 10, 139, 12, 141, 142, 15]
+
+
+# ---- golden vectors (gguf-py 0.19.0, ggml semantics) ------------------------
+@pytest.mark.parametrize("name,t", [("Q8_0", S.Q8_0), ("Q4_K", S.Q4_K), ("Q5_K", S.Q5_K), ("Q6_K", S.Q6_K)])
+def test_dequant_bitexact_vs_golden(name, t):
+    g = np.load(GOLDEN)
+    q, want = g[f"{name}_bytes"], g[f"{name}_ggml"]
+    got = O.dequant(t, q, want.size)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_iq2xxs_inferno_semantics_vs_golden():
+    g = np.load(GOLDEN)
+    q, inf, ggml = g["IQ2_XXS_bytes"], g["IQ2_XXS_inferno"], g["IQ2_XXS_ggml"]
+    got = O.dequant(S.IQ2_XXS, q, inf.size)
+    assert np.array_equal(got.view(np.uint32), inf.view(np.uint32))
+    # Inferno = ggml - 8*db*sign (src/Dequant.jl:46 vs ggml)
+    nb = q.size // 66
+    d = q.reshape(nb, 66)[:, :2].copy().view(np.float16).astype(np.float32).reshape(nb)
+    a2 = q.reshape(nb, 66)[:, 2:].copy().view("<u4").reshape(nb, 8, 2)[..., 1]
+    db = (d[:, None] * (0.5 + (a2 >> 28).astype(np.float32))) * 0.25
+    sign = np.sign(ggml.reshape(nb, 8, 32))
+    off = 8 * db[..., None] * sign
+    np.testing.assert_allclose(inf.reshape(nb, 8, 32), ggml.reshape(nb, 8, 32) - off, atol=1e-6)
+
+
+def test_packers_round_trip():
+    rng = np.random.default_rng(1)
+    w = (rng.standard_normal((8, 1024)) * 0.02).astype(np.float32)
+    for t, tol in ((S.Q8_0, 0.01), (S.Q6_K, 0.03), (S.Q5_K, 0.05), (S.Q4_K, 0.1)):
+        d = O.dequant(t, S.quantize(w, t).reshape(-1), w.size).reshape(w.shape)
+        assert np.abs(d - w).max() / np.abs(w).max() < tol, S.TYPE_NAME[t]
+
+
+# ---- tests/flash_attention_verification.jl:55-101 ---------------------------
+@pytest.mark.parametrize("seq", [32, 64, 128, 256, 512, 1024, 2048])
+def test_flash_vs_standard_attention(seq):
+    rng = np.random.default_rng(42)
+    hd, nkv = 256, 2
+    q = rng.random(hd, dtype=np.float32)
+    ck = rng.random((seq, nkv, hd), dtype=np.float32)
+    cv = rng.random((seq, nkv, hd), dtype=np.float32)
+    scale = np.float32(1.0 / math.sqrt(hd))
+    a = O.flash_attention(q, ck, cv, 0, seq, scale, hd, nkv)
+    b = O.flash_attention(q, ck, cv, 0, seq, scale, hd, nkv, standard=True)
+    assert np.abs(a - b).max() < 1e-4
+
+
+def test_gemv_matches_dequant_matmul():
+    rng = np.random.default_rng(3)
+    w = (rng.standard_normal((37, 512)) * 0.02).astype(np.float32)
+    for t in (S.Q4_K, S.Q6_K, S.Q8_0, S.IQ2_XXS):
+        q = S.quantize(w, t)
+        x = rng.standard_normal((2, 512)).astype(np.float32)
+        y = O.gemv(t, q, x, 512, 37)
+        ref = x.astype(np.float64) @ O.dequant(t, q.reshape(-1), w.size).reshape(w.shape).T.astype(np.float64)
+        assert np.abs(y - ref).max() / np.abs(ref).max() < 1e-5
+
+
+def test_gdn_recurrence_vs_numpy():
+    rng = np.random.default_rng(4)
+    T, H, dk, dv = 5, 2, 16, 8
+    q = rng.standard_normal((T, H, dk)).astype(np.float32)
+    k = rng.standard_normal((T, H, dk)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=-1, keepdims=True)
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = rng.standard_normal((T, H, dv)).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.standard_normal((T, H))))).astype(np.float32)
+    g = (-np.log1p(np.exp(rng.standard_normal((T, H))))).astype(np.float32)
+    S0 = np.zeros((H, dv, dk), np.float32)
+    y = O.gdn_recurrence(q, k, v, beta, g, S0)
+    Sr = np.zeros((H, dv, dk))
+    for t in range(T):
+        for h in range(H):
+            Sr[h] *= np.exp(g[t, h])
+            d = beta[t, h] * (v[t, h] - Sr[h] @ k[t, h])
+            Sr[h] += np.outer(d, k[t, h])
+            np.testing.assert_allclose(y[t, h], Sr[h] @ q[t, h], rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(S0, Sr, rtol=1e-4, atol=1e-5)
+
+
+# ---- the full forward against the numpy restatement -------------------------
+@pytest.fixture(scope="module")
+def tiny_pair():
+    from numpy_ref import NumpyModel
+    spec = S.CONFIGS["tiny"]
+    T = S.make_model(spec, seed=5)
+    return spec, T, O.OracleModel(spec, T), NumpyModel(spec, T)
+
+
+def test_oracle_forward_vs_numpy(tiny_pair):
+    spec, T, orc, ref = tiny_pair
+    prompt = S.tokens(5, 6, spec.vocab)
+    orc.reset()
+    ref.reset()
+    a, la = orc.forward(prompt, 0)
+    b, lb = ref.forward(prompt, 0)
+    assert np.abs(la - lb).max() / np.abs(lb).max() < 1e-4
+    assert a == b
+    for step in range(3):
+        a, la = orc.forward([a], len(prompt) + step)
+        b, lb = ref.forward([b], len(prompt) + step)
+        assert a == b
+        assert np.abs(la - lb).max() / np.abs(lb).max() < 1e-4
+
+
+def test_oracle_greedy_first_max():
+    """Julia argmax returns the first maximum (tests/unit/test_engine.jl:45-79);
+    the oracle's argmax scan uses a strict '>' so ties keep the lower index."""
+    spec = S.CONFIGS["tiny"]
+    T = S.make_model(spec, seed=6)
+    e = T["token_embd.weight"]
+    row = e.data.reshape(spec.vocab, -1)[0]
+    T["token_embd.weight"] = S.Tensor(e.ggml_type, e.ne, np.tile(row, spec.vocab))
+    m = O.OracleModel(spec, T)
+    tok, lg = m.forward([7], 0)
+    assert np.all(lg == lg[0]) and tok == 0
