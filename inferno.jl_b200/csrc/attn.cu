@@ -6,14 +6,17 @@
 // (:245-258), flash_attention_cpu! (src/FlashAttention.jl:16-74, blocked GQA
 // head map kv = h / (nq/nkv)) and the gate (:846-851).
 //
-// Grid (n_kv heads, n_split).  A CTA owns one KV head and one split of
-// `split_len` positions and serves all nq/nkv query heads of that KV head, so
-// each K/V row is read from HBM once per token.  Softmax is exact per split
-// (max, sum of exp) and the last CTA of a KV head (atomic ticket) merges the
-// splits: o = sum_s e^{m_s-M} o_s / sum_s e^{m_s-M} l_s, then o *= sigmoid(g).
-// The new K/V row at `pos` is normalised/rotated in the CTA whose split holds
-// `pos`, used from shared memory and written to the cache by that CTA; no
-// other CTA reads position `pos` in the same launch.
+// Grid (n_heads, n_split), 256 threads (one per head dim).  A CTA owns one
+// query head and one split of `split_len` positions, processed in chunks of
+// 32 keys: 8 threads per key compute the q.k partial dots, the chunk's
+// softmax statistics are folded into a running (max, sum, o) online softmax,
+// and each thread accumulates one output dim from the V rows.  The last CTA
+// of a head (atomic ticket) merges the splits,
+//   o = sum_s e^{m_s-M} o_s / sum_s e^{m_s-M} l_s,  then  o *= sigmoid(g).
+// The first chunk's K/V rows (all positions < pos) are loaded before
+// griddepcontrol.wait; the new row at `pos` is normalised / rotated from the
+// q/k/v GEMV output, used from shared memory and written to the cache by one
+// CTA per KV head.
 //
 // Cache layout: [ctx][n_kv][head_dim] fp32 (the reference's (hd, nkv, seq)
 // column-major array, element (d, h, p) at d + hd*(h + nkv*p)).
@@ -26,167 +29,171 @@ namespace inf {
 
 constexpr int ATT_HD = 256;          // head_dim (one thread per dim)
 constexpr int ATT_THREADS = 256;
-constexpr int ATT_MAX_GQA = 8;
-constexpr int ATT_MAX_SPLIT = 256;   // positions per split (scores in smem)
+constexpr int ATT_CHUNK = 32;        // keys per pass (8 threads per key)
 
-
-
-// RMSNorm over 256 dims (one value per thread) + half-split RoPE on the
-// first rd dims, in place in smem row `x` (src/ModelCPU.jl:187-231).
-__device__ __forceinline__ void norm_rope(float* x, const float* w, float eps, const float* c, const float* s,
-                                          int rd, float* red) {
-  const int d = threadIdx.x;
-  float v = x[d];
-  float ss = warp_sum(v * v);
-  if ((d & 31) == 0) red[d >> 5] = ss;
-  __syncthreads();
-  float tot = 0.f;
+__device__ __forceinline__ void load_chunk(const AttnParams& p, int kvh, int j0, int jend, int pos, float4 (&kreg)[8],
+                                           float (&vreg)[ATT_CHUNK]) {
+  const int t = threadIdx.x, kk = t >> 3, part = t & 7;
+  const int j = j0 + kk;
+  if (j < jend && j != pos) {
+    const float4* kr = (const float4*)(p.kc + ((long long)j * p.nkv + kvh) * ATT_HD + part * 32);
 #pragma unroll
-  for (int i = 0; i < ATT_THREADS / 32; ++i) tot += red[i];
-  const float inv = 1.0f / sqrtf(tot / (float)ATT_HD + eps);
-  v = v * inv * w[d];
-  __syncthreads();
-  x[d] = v;
-  __syncthreads();
-  const int half = rd / 2;
-  if (d < half) {
-    float x1 = x[d], x2 = x[d + half];
-    x[d] = x1 * c[d] - x2 * s[d];
-    x[d + half] = x1 * s[d] + x2 * c[d];
+    for (int i = 0; i < 8; ++i) kreg[i] = kr[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) kreg[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < ATT_CHUNK; ++q) {
+    const int jj = j0 + q;
+    vreg[q] = (jj < jend && jj != pos) ? p.vc[((long long)jj * p.nkv + kvh) * ATT_HD + t] : 0.f;
+  }
 }
 
 __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_constant__ AttnParams p) {
-  __shared__ __align__(16) float qs[ATT_MAX_GQA][ATT_HD];
-  __shared__ __align__(16) float knew[ATT_HD], vnew[ATT_HD];
-  __shared__ float sc[ATT_MAX_GQA][ATT_MAX_SPLIT];
-  __shared__ float red[ATT_THREADS / 32];
-  __shared__ float ml[ATT_MAX_GQA][2];
+  __shared__ __align__(16) float qs[ATT_HD], knew[ATT_HD], vnew[ATT_HD];
+  __shared__ float sc[ATT_CHUNK];
+  __shared__ float red[2][ATT_THREADS / 32];
   __shared__ int ticket;
-  pdl_trigger();
-  pdl_wait();
-  const int kvh = blockIdx.x, s = blockIdx.y, d = threadIdx.x;
-  const int warp = d >> 5, lane = d & 31;
-  const int gqa = p.nh / p.nkv;
-  const int pos = *p.pos;
+  const int h = blockIdx.x, s = blockIdx.y, d = threadIdx.x;
+  const int kvh = h / (p.nh / p.nkv);
+  const int lane = d & 31, warp = d >> 5;
+
+  // ---------------- pre-wait: position and the first K/V chunk ----------------
+  const int pos = *p.pos;     // written by the previous step's finalize
   if (pos < 0 || pos >= p.ctx) {
-    if (d == 0 && s == 0 && kvh == 0) atomicExch(p.err, DERR_BAD_ARG);
+    pdl_wait();
+    pdl_trigger();
+    if (d == 0 && s == 0 && h == 0) atomicExch(p.err, DERR_BAD_ARG);
     return;
   }
   const int L = pos + 1;
   const int nact = (L + p.split_len - 1) / p.split_len;
-  if (s >= nact) return;
   const int j0 = s * p.split_len, j1 = min(j0 + p.split_len, L);
-  const int nj = j1 - j0;
-  const int half = p.rd / 2;
-  const float* cs = p.rope_cos + (long long)pos * half;
-  const float* sn = p.rope_sin + (long long)pos * half;
-  const float scale = 1.0f / sqrtf((float)ATT_HD);
+  float4 kreg[8];
+  float vreg[ATT_CHUNK];
+  if (s < nact) load_chunk(p, kvh, j0, min(j0 + ATT_CHUNK, j1), pos, kreg, vreg);
+  pdl_wait();
+  pdl_trigger();
+  if (s >= nact) return;
 
-  // query heads of this KV head (blocked GQA, src/ModelCPU.jl:790-795)
-  for (int i = 0; i < gqa; ++i) {
-    const int qh = kvh * gqa + i;
-    qs[i][d] = p.qg[(long long)qh * 2 * ATT_HD + d];
-    __syncthreads();
-    norm_rope(qs[i], p.q_norm, p.eps, cs, sn, p.rd, red);
-  }
+  // ---------------- q (and the new k) : RMSNorm + RoPE ----------------
   const bool has_new = (pos >= j0 && pos < j1);
-  if (has_new) {
-    knew[d] = p.k[kvh * ATT_HD + d];
-    vnew[d] = p.v[kvh * ATT_HD + d];
-    __syncthreads();
-    norm_rope(knew, p.k_norm, p.eps, cs, sn, p.rd, red);
-    long long off = ((long long)pos * p.nkv + kvh) * ATT_HD + d;
+  const float qv = p.qg[(long long)h * 2 * ATT_HD + d];
+  const float kv = has_new ? p.k[kvh * ATT_HD + d] : 0.f;
+  if (has_new) vnew[d] = p.v[kvh * ATT_HD + d];
+  float a = warp_sum(qv * qv), b = warp_sum(kv * kv);
+  if (lane == 0) { red[0][warp] = a; red[1][warp] = b; }
+  __syncthreads();
+  a = 0.f;
+  b = 0.f;
+#pragma unroll
+  for (int i = 0; i < ATT_THREADS / 32; ++i) { a += red[0][i]; b += red[1][i]; }
+  const float iq = 1.0f / sqrtf(a / (float)ATT_HD + p.eps);
+  const float ik = 1.0f / sqrtf(b / (float)ATT_HD + p.eps);
+  qs[d] = qv * iq * p.q_norm[d];
+  if (has_new) knew[d] = kv * ik * p.k_norm[d];
+  __syncthreads();
+  const int half = p.rd / 2;
+  if (d < half) {
+    const float c = p.rope_cos[(long long)pos * half + d], sn = p.rope_sin[(long long)pos * half + d];
+    float x1 = qs[d], x2 = qs[d + half];
+    qs[d] = x1 * c - x2 * sn;
+    qs[d + half] = x1 * sn + x2 * c;
+    if (has_new) {
+      x1 = knew[d];
+      x2 = knew[d + half];
+      knew[d] = x1 * c - x2 * sn;
+      knew[d + half] = x1 * sn + x2 * c;
+    }
+  }
+  __syncthreads();
+  if (has_new && (h % (p.nh / p.nkv)) == 0) {
+    const long long off = ((long long)pos * p.nkv + kvh) * ATT_HD + d;
     p.kc[off] = knew[d];
     p.vc[off] = vnew[d];
   }
 
-  // scores: one warp per key, 8 dims per lane
-#pragma unroll 4
-  for (int jj = warp; jj < nj; jj += ATT_THREADS / 32) {
-    const int j = j0 + jj;
-    const float* kr = (j == pos) ? knew : p.kc + ((long long)j * p.nkv + kvh) * ATT_HD;
-    const float4 k0 = *(const float4*)(kr + lane * 8), k1 = *(const float4*)(kr + lane * 8 + 4);
-    for (int i = 0; i < gqa; ++i) {
-      const float4 q0 = *(const float4*)(&qs[i][lane * 8]), q1 = *(const float4*)(&qs[i][lane * 8 + 4]);
-      float a = q0.x * k0.x + q0.y * k0.y + q0.z * k0.z + q0.w * k0.w + q1.x * k1.x + q1.y * k1.y +
-                q1.z * k1.z + q1.w * k1.w;
-      a = warp_sum(a);
-      if (lane == 0) sc[i][jj] = a * scale;
+  // ---------------- online softmax over 32-key chunks ----------------
+  const float scale = 1.0f / sqrtf((float)ATT_HD);
+  const int kk = d >> 3, part = d & 7;
+  float4 q8[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) q8[i] = *(const float4*)&qs[part * 32 + 4 * i];
+  float m = -INFINITY, l = 0.f, o = 0.f;
+  for (int c0 = j0; c0 < j1; c0 += ATT_CHUNK) {
+    const int cend = min(c0 + ATT_CHUNK, j1);
+    if (c0 != j0) load_chunk(p, kvh, c0, cend, pos, kreg, vreg);
+    // the new row at pos comes from shared memory
+    if (c0 + kk == pos) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) kreg[i] = *(const float4*)&knew[part * 32 + 4 * i];
     }
-  }
-  __syncthreads();
-  // per-head softmax statistics of this split (warp i owns head i)
-  for (int i = warp; i < gqa; i += ATT_THREADS / 32) {
-    float m = -INFINITY;
-    for (int jj = lane; jj < nj; jj += 32) m = fmaxf(m, sc[i][jj]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int jj = lane; jj < nj; jj += 32) {
-      float e = expf(sc[i][jj] - m);
-      sc[i][jj] = e;
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      dot += q8[i].x * kreg[i].x + q8[i].y * kreg[i].y + q8[i].z * kreg[i].z + q8[i].w * kreg[i].w;
+    dot += __shfl_xor_sync(0xffffffffu, dot, 4);
+    dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+    dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+    __syncthreads();   // previous chunk's sc[] consumed
+    if (part == 0) sc[kk] = (c0 + kk < cend) ? dot * scale : -INFINITY;
+    __syncthreads();
+    float cm = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < ATT_CHUNK; ++q) cm = fmaxf(cm, sc[q]);
+    const float mn = fmaxf(m, cm);
+    const float corr = expf(m - mn);        // 0 on the first chunk (m = -inf)
+    l *= corr;
+    o *= corr;
+#pragma unroll
+    for (int q = 0; q < ATT_CHUNK; ++q) {
+      const float e = expf(sc[q] - mn);
       l += e;
+      const float vv = (c0 + q == pos) ? vnew[d] : vreg[q];
+      o = fmaf(e, vv, o);
     }
-    l = warp_sum(l);
-    if (lane == 0) { ml[i][0] = m; ml[i][1] = l; }
+    m = mn;
   }
-  __syncthreads();
-  // o[i][d] = sum_j p[i][j] v[j][d]
-  float o[ATT_MAX_GQA];
-#pragma unroll
-  for (int i = 0; i < ATT_MAX_GQA; ++i) o[i] = 0.f;
-#pragma unroll 8
-  for (int jj = 0; jj < nj; ++jj) {
-    const int j = j0 + jj;
-    const float vv = (j == pos) ? vnew[d] : p.vc[((long long)j * p.nkv + kvh) * ATT_HD + d];
-#pragma unroll
-    for (int i = 0; i < ATT_MAX_GQA; ++i)
-      if (i < gqa) o[i] = fmaf(sc[i][jj], vv, o[i]);
-  }
-#pragma unroll
-  for (int i = 0; i < ATT_MAX_GQA; ++i) {
-    if (i >= gqa) break;
-    const int qh = kvh * gqa + i;
-    p.part_o[((long long)qh * p.nsplit + s) * ATT_HD + d] = o[i];
-    if (d == 0) {
-      p.part_ml[((long long)qh * p.nsplit + s) * 2 + 0] = ml[i][0];
-      p.part_ml[((long long)qh * p.nsplit + s) * 2 + 1] = ml[i][1];
-    }
+  p.part_o[((long long)h * p.nsplit + s) * ATT_HD + d] = o;
+  if (d == 0) {
+    p.part_ml[((long long)h * p.nsplit + s) * 2 + 0] = m;
+    p.part_ml[((long long)h * p.nsplit + s) * 2 + 1] = l;
   }
 
-  // ---- last CTA of this KV head merges the splits ----
+  // ---------------- last CTA of this head merges the splits ----------------
   __threadfence();
   __syncthreads();
-  if (d == 0) ticket = atomicAdd(&p.counters[kvh], 1);
+  if (d == 0) ticket = atomicAdd(&p.counters[h], 1);
   __syncthreads();
   if (ticket != nact - 1) return;
   __threadfence();
-  if (d == 0) p.counters[kvh] = 0;
-  for (int i = 0; i < gqa; ++i) {
-    const int qh = kvh * gqa + i;
-    const float* mlp = p.part_ml + (long long)qh * p.nsplit * 2;
-    float M = -INFINITY;
-    for (int t = 0; t < nact; ++t) M = fmaxf(M, __ldcg(mlp + 2 * t));
-    float num = 0.f, den = 0.f;
-    for (int t = 0; t < nact; ++t) {
-      const float w = expf(__ldcg(mlp + 2 * t) - M);
-      num = fmaf(w, __ldcg(p.part_o + ((long long)qh * p.nsplit + t) * ATT_HD + d), num);
-      den = fmaf(w, __ldcg(mlp + 2 * t + 1), den);
-    }
-    const float g = p.qg[(long long)qh * 2 * ATT_HD + ATT_HD + d];
-    const float gate = 1.0f / (1.0f + expf(-g));
-    p.out[(long long)qh * ATT_HD + d] = (num / den) * gate;
+  if (d == 0) p.counters[h] = 0;
+  const float* mlp = p.part_ml + (long long)h * p.nsplit * 2;
+  float M = -INFINITY;
+  for (int t = 0; t < nact; ++t) M = fmaxf(M, __ldcg(mlp + 2 * t));
+  float num = 0.f, den = 0.f;
+  for (int t = 0; t < nact; ++t) {
+    const float w = expf(__ldcg(mlp + 2 * t) - M);
+    num = fmaf(w, __ldcg(p.part_o + ((long long)h * p.nsplit + t) * ATT_HD + d), num);
+    den = fmaf(w, __ldcg(mlp + 2 * t + 1), den);
   }
+  const float g = p.qg[(long long)h * 2 * ATT_HD + ATT_HD + d];
+  p.out[(long long)h * ATT_HD + d] = (num / den) * (1.0f / (1.0f + expf(-g)));
 }
 
 int launch_attn_decode(const AttnParams& p, cudaStream_t st, bool pdl) {
-  if (p.nh % p.nkv || p.nh / p.nkv > ATT_MAX_GQA || p.split_len > ATT_MAX_SPLIT || p.split_len < 1 ||
-      p.rd > ATT_HD || p.rd % 2)
+  if (p.nh % p.nkv || p.split_len % ATT_CHUNK || p.split_len < ATT_CHUNK || p.rd > ATT_HD || p.rd % 2)
     return set_error(INFERNO_EINVAL, "attention: unsupported shape (nh=%d nkv=%d split=%d rd=%d)", p.nh, p.nkv,
                      p.split_len, p.rd);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared);
+    attr = true;
+  }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.nkv, p.nsplit);
+  cfg.gridDim = dim3(p.nh, p.nsplit);
   cfg.blockDim = dim3(ATT_THREADS);
   cfg.stream = st;
   cudaLaunchAttribute at[1];

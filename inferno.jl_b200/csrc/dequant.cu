@@ -119,8 +119,8 @@ int launch_dequant(int type, const void* src, long long n, float* dst, cudaStrea
 template <int TYPE>
 __global__ void embed_row_kernel(const uint8_t* __restrict__ W, long long row_bytes, int inner,
                                  const int* __restrict__ row_ptr, float* __restrict__ dst, int vocab) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   int row = *row_ptr;
   if (row < 0 || row >= vocab) row = 0;
   long long runs = inner / 32;

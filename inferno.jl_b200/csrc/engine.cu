@@ -42,8 +42,8 @@ struct Ctl {                 // device-resident step control
 };
 
 __global__ void finalize_kernel(Ctl* c, const int* prompt, int* out, int max_out) {
-  pdl_trigger();
   pdl_wait();
+  pdl_trigger();
   const unsigned long long key = c->argkey;
   const int am = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull));
   c->last = am;
@@ -521,15 +521,15 @@ int inferno_engine_finalize(InfernoEngine* e) {
       (rc = dalloc(e, &e->out_tokens, c.max_ctx + 8)) || (rc = dalloc(e, &e->err, 1)))
     return rc;
   e->max_out = c.max_ctx + 8;
-  // attention splits: at least 64 positions, at most 128 splits
-  e->split_len = 64;
-  while ((c.max_ctx + e->split_len - 1) / e->split_len > 128 && e->split_len < 256) e->split_len *= 2;
+  // attention splits: multiples of 32 positions, at most 128 splits
+  e->split_len = 32;
+  while ((c.max_ctx + e->split_len - 1) / e->split_len > 128) e->split_len += 32;
   e->nsplit = (c.max_ctx + e->split_len - 1) / e->split_len;
   e->rd = (int)std::lround(c.head_dim * (double)c.partial_rotary_factor);   // src/LoaderCPU.jl:375
   if (any_attn) {
     if ((rc = dalloc(e, &e->part_o, (size_t)c.n_heads * e->nsplit * c.head_dim)) ||
         (rc = dalloc(e, &e->part_ml, (size_t)c.n_heads * e->nsplit * 2)) ||
-        (rc = dalloc(e, &e->att_counters, c.n_kv_heads)))
+        (rc = dalloc(e, &e->att_counters, c.n_heads)))
       return rc;
     std::vector<float> cs, sn;
     build_rope(c.max_ctx, e->rd, c.rope_theta, cs, sn);

@@ -17,6 +17,13 @@
 // GDN_ROWS rows of the head's state.  State layout [nv][dv][dk] row-major.
 // The conv ring holds the last K inputs: input of step t lives in slot t % K;
 // the step counter is per layer and advanced by the last CTA to finish.
+//
+// Latency structure: everything that does not depend on the preceding
+// kernel (state rows, ring slots, conv / alpha / beta / norm weights) is
+// loaded before griddepcontrol.wait; after it only x and the in_proj output
+// are read, followed by two block reductions.  Every engine kernel triggers
+// its dependents only after its own wait, so data written two or more
+// launches earlier is complete when this pre-wait code runs.
 #include "internal.h"
 #include "common.cuh"
 #include "params.h"
@@ -27,113 +34,161 @@ namespace inf {
 constexpr int GDN_THREADS = 128;
 constexpr int GDN_ROWS = 16;
 constexpr int GDN_DK = 128;
+constexpr int GDN_MAXK = 4;          // conv taps held in registers
+constexpr int GDN_MAX_H = 8192;      // hidden size (smem for the alpha/beta weights)
 
-
-
-__device__ __forceinline__ float block_sum128(float v, float* red) {
-  v = warp_sum(v);
+template <int NV>
+__device__ __forceinline__ void block_sum_n(float (&v)[NV], float (*red)[4]) {
+#pragma unroll
+  for (int i = 0; i < NV; ++i) v[i] = warp_sum(v[i]);
+  if ((threadIdx.x & 31) == 0)
+#pragma unroll
+    for (int i = 0; i < NV; ++i) red[i][threadIdx.x >> 5] = v[i];
   __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  return red[0] + red[1] + red[2] + red[3];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) v[i] = (red[i][0] + red[i][1]) + (red[i][2] + red[i][3]);
 }
 
 __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(const __grid_constant__ GdnParams p) {
-  __shared__ float qn[GDN_DK], kn[GDN_DK], vrow[GDN_ROWS];
-  __shared__ float red[4];
+  extern __shared__ __align__(16) float gsm[];     // [3][H]: w_alpha row, w_beta row, in_norm
+  __shared__ __align__(16) float qn[GDN_DK], kn[GDN_DK];
+  __shared__ float vrow[GDN_ROWS];
+  __shared__ float red[3][4];
   __shared__ float gate_s[2];
-  pdl_trigger();
-  pdl_wait();
   const int h = blockIdx.x, r0 = blockIdx.y * GDN_ROWS, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
   const int g = h % p.nk;
-  const int t = *p.step;
-  const int K = p.K, C = p.C;
+  const int K = p.K, C = p.C, H = p.H;
+
+  // ---------------- pre-wait: state and constants ----------------
+  const int t = *p.step;            // written by this layer's previous step
   const int cur = t % K;
-
-  // ---- RMSNorm(x) folded into the alpha/beta dots ----
-  float ss = 0.f;
-  for (int i = tid; i < p.H; i += GDN_THREADS) ss += p.x[i] * p.x[i];
-  ss = block_sum128(ss, red);
-  const float scale = 1.0f / sqrtf(ss / (float)p.H + p.eps);
-  float da = 0.f, dbv = 0.f;
-  const float* wa = p.w_alpha + (long long)h * p.H;
-  const float* wb = p.w_beta + (long long)h * p.H;
-  for (int i = tid; i < p.H; i += GDN_THREADS) {
-    float xn = p.x[i] * scale * p.in_norm[i];
-    da = fmaf(wa[i], xn, da);
-    dbv = fmaf(wb[i], xn, dbv);
+  float* wa_s = gsm;
+  float* wb_s = gsm + H;
+  float* wn_s = gsm + 2 * H;
+  for (int i = tid * 4; i < H; i += GDN_THREADS * 4) {
+    *(float4*)&wa_s[i] = *(const float4*)&p.w_alpha[(long long)h * H + i];
+    *(float4*)&wb_s[i] = *(const float4*)&p.w_beta[(long long)h * H + i];
+    *(float4*)&wn_s[i] = *(const float4*)&p.in_norm[i];
   }
-  float alpha = block_sum128(da, red);
-  float beta_raw = block_sum128(dbv, red);
-
-  // ---- conv1d + SiLU for this head's q, k (group g) and v rows ----
-  auto conv = [&](int c, bool write) -> float {
-    float nv = p.qkv[c];
-    float v = 0.f;
-    for (int k = 0; k < K - 1; ++k) {
+  // conv taps and past inputs for this thread's channels
+  const int cq = g * GDN_DK + tid, ck = p.nk * GDN_DK + g * GDN_DK + tid;
+  const int cv = 2 * p.nk * GDN_DK + h * p.dv + r0 + tid;     // valid for tid < GDN_ROWS
+  float wq[GDN_MAXK], wk[GDN_MAXK], wv[GDN_MAXK], hq[GDN_MAXK], hk[GDN_MAXK], hv[GDN_MAXK];
+#pragma unroll
+  for (int k = 0; k < GDN_MAXK; ++k) {
+    wq[k] = wk[k] = wv[k] = hq[k] = hk[k] = hv[k] = 0.f;
+    if (k < K) {
       int slot = (t - (K - 1) + k) % K;
       if (slot < 0) slot += K;
-      v += p.ring[(long long)slot * C + c] * p.conv_w[(long long)c * K + k];
+      wq[k] = p.conv_w[(long long)cq * K + k];
+      wk[k] = p.conv_w[(long long)ck * K + k];
+      if (k < K - 1) {
+        hq[k] = p.ring[(long long)slot * C + cq];
+        hk[k] = p.ring[(long long)slot * C + ck];
+      }
+      if (tid < GDN_ROWS) {
+        wv[k] = p.conv_w[(long long)cv * K + k];
+        if (k < K - 1) hv[k] = p.ring[(long long)slot * C + cv];
+      }
     }
-    v += nv * p.conv_w[(long long)c * K + K - 1];
-    if (write) p.ring[(long long)cur * C + c] = nv;
-    return v / (1.0f + expf(-v));
-  };
-  const bool qk_owner = (h == g) && blockIdx.y == 0;   // first head of group g
-  float qv = 0.f, kv = 0.f;
-  if (tid < GDN_DK) {
-    qv = conv(g * GDN_DK + tid, qk_owner);
-    kv = conv(p.nk * GDN_DK + g * GDN_DK + tid, qk_owner);
   }
-  if (tid < GDN_ROWS) vrow[tid] = conv(2 * p.nk * GDN_DK + h * p.dv + r0 + tid, true);
+  // this warp's state rows (4 fp32 per lane per row)
+  constexpr int RPW = GDN_ROWS / (GDN_THREADS / 32);
+  float4 srow[RPW];
+#pragma unroll
+  for (int j = 0; j < RPW; ++j)
+    srow[j] = *((const float4*)(p.S + ((long long)h * p.dv + r0 + warp + 4 * j) * GDN_DK) + lane);
+  const float a_h = p.ssm_a[h], dt_h = p.dt_bias[h];
 
-  // ---- L2 norms (src/ModelCPU.jl:597-616) ----
-  float qs = block_sum128(qv * qv, red);
-  float ks = block_sum128(kv * kv, red);
-  const float eps6 = 1.0e-6f;
-  const float qscale = 1.0f / sqrtf((float)GDN_DK);
-  const float qnv = 1.0f / (sqrtf(qs) + eps6) * qscale;
-  const float knv = 1.0f / (sqrtf(ks) + eps6);
-  if (tid < GDN_DK) {
-    qn[tid] = qv * qnv;
-    kn[tid] = kv * knv;
+  pdl_wait();
+  pdl_trigger();
+
+  // ---------------- alpha / beta of RMSNorm(x) ----------------
+  // alpha = sum_i Wa[i] * (x[i]*scale*w[i]) = scale * sum_i Wa[i]*w[i]*x[i]
+  __syncthreads();   // smem weights visible
+  float acc3[3] = {0.f, 0.f, 0.f};
+  for (int i = tid; i < H; i += GDN_THREADS) {
+    const float xv = p.x[i];
+    const float xw = xv * wn_s[i];
+    acc3[0] = fmaf(xv, xv, acc3[0]);
+    acc3[1] = fmaf(wa_s[i], xw, acc3[1]);
+    acc3[2] = fmaf(wb_s[i], xw, acc3[2]);
   }
-  // ---- gates in Float64 (src/ModelCPU.jl:618-636) ----
+  // conv1d + SiLU on this thread's channels (newest input last, :555-564)
+  const float nq = p.qkv[cq], nk_ = p.qkv[ck];
+  const float nv_ = tid < GDN_ROWS ? p.qkv[cv] : 0.f;
+  float vq = 0.f, vk = 0.f, vvv = 0.f;
+#pragma unroll
+  for (int k = 0; k < GDN_MAXK; ++k) {
+    if (k < K - 1) {
+      vq += hq[k] * wq[k];
+      vk += hk[k] * wk[k];
+      vvv += hv[k] * wv[k];
+    } else if (k == K - 1) {
+      vq += nq * wq[k];
+      vk += nk_ * wk[k];
+      vvv += nv_ * wv[k];
+    }
+  }
+  const float qv = vq / (1.0f + expf(-vq));
+  const float kv = vk / (1.0f + expf(-vk));
+  if (tid < GDN_ROWS) vrow[tid] = vvv / (1.0f + expf(-vvv));
+  // ring update (owners only; no CTA reads slot `cur` in this step)
+  if (h == g && blockIdx.y == 0) {
+    p.ring[(long long)cur * C + cq] = nq;
+    p.ring[(long long)cur * C + ck] = nk_;
+  }
+  if (tid < GDN_ROWS) p.ring[(long long)cur * C + cv] = nv_;
+
+  block_sum_n<3>(acc3, red);
+  const float scale = 1.0f / sqrtf(acc3[0] / (float)H + p.eps);
+  const float alpha = acc3[1] * scale, beta_raw = acc3[2] * scale;
+  // gates in Float64 (src/ModelCPU.jl:618-636), one thread, overlapped with
+  // the L2-norm reduction below
   if (tid == 0) {
-    double a = (double)alpha + (double)p.dt_bias[h];
+    double a = (double)alpha + (double)dt_h;
     a = fmin(20.0, fmax(-20.0, a));
-    double sp = log(1.0 + exp(a));
-    float decay = (float)((double)p.ssm_a[h] * sp);
+    const double sp = log(1.0 + exp(a));
+    const float decay = (float)((double)a_h * sp);
     gate_s[0] = expf(decay);
-    double bv = fmin(20.0, fmax(-20.0, (double)beta_raw));
+    const double bv = fmin(20.0, fmax(-20.0, (double)beta_raw));
     gate_s[1] = (float)(1.0 / (1.0 + exp(-bv)));
   }
+  // ---------------- L2 norms (src/ModelCPU.jl:597-616) ----------------
+  float qk2[2] = {qv * qv, kv * kv};
+  __syncthreads();   // red[] reuse
+  block_sum_n<2>(qk2, red);
+  const float qscale = 1.0f / sqrtf((float)GDN_DK);
+  const float qnv = 1.0f / (sqrtf(qk2[0]) + 1.0e-6f) * qscale;
+  const float knv = 1.0f / (sqrtf(qk2[1]) + 1.0e-6f);
+  qn[tid] = qv * qnv;
+  kn[tid] = kv * knv;
   __syncthreads();
   const float dec = gate_s[0], bg = gate_s[1];
 
-  // ---- delta rule, one warp per state row, 4 fp32 per lane ----
-  const int warp = tid >> 5, lane = tid & 31;
+  // ---------------- delta rule ----------------
   const float4 k4 = *(const float4*)&kn[lane * 4];
   const float4 q4 = *(const float4*)&qn[lane * 4];
-  for (int rr = warp; rr < GDN_ROWS; rr += GDN_THREADS / 32) {
-    const int i = r0 + rr;
-    float4* Srow = (float4*)(p.S + ((long long)h * p.dv + i) * GDN_DK) + lane;
-    float4 s = *Srow;
+#pragma unroll
+  for (int j = 0; j < RPW; ++j) {
+    const int rr = warp + 4 * j, i = r0 + rr;
+    float4 s = srow[j];
     s.x *= dec; s.y *= dec; s.z *= dec; s.w *= dec;
-    float sk = warp_sum(s.x * k4.x + s.y * k4.y + s.z * k4.z + s.w * k4.w);
-    float d = bg * (vrow[rr] - sk);
+    const float sk = warp_sum(s.x * k4.x + s.y * k4.y + s.z * k4.z + s.w * k4.w);
+    const float d = bg * (vrow[rr] - sk);
     s.x += d * k4.x; s.y += d * k4.y; s.z += d * k4.z; s.w += d * k4.w;
-    float yv = warp_sum(s.x * q4.x + s.y * q4.y + s.z * q4.z + s.w * q4.w);
-    *Srow = s;
+    const float yv = warp_sum(s.x * q4.x + s.y * q4.y + s.z * q4.z + s.w * q4.w);
+    *((float4*)(p.S + ((long long)h * p.dv + i) * GDN_DK) + lane) = s;
     if (lane == 0) p.y[h * p.dv + i] = yv;
   }
 
-  // ---- advance the layer's step counter once all CTAs have read it ----
+  // ---------------- advance the layer's step counter ----------------
   __syncthreads();
   if (tid == 0) {
     __threadfence();
-    int total = gridDim.x * gridDim.y;
-    int prev = atomicAdd(p.done, 1);
+    const int total = gridDim.x * gridDim.y;
+    const int prev = atomicAdd(p.done, 1);
     if (prev == total - 1) {
       *p.done = 0;
       *p.step = t + 1;
@@ -143,11 +198,19 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(const __grid_cons
 }
 
 int launch_gdn_step(const GdnParams& p, cudaStream_t st, bool pdl) {
-  if (p.dv % GDN_ROWS || p.K < 1 || p.K > 8)
-    return set_error(INFERNO_EINVAL, "gdn: unsupported dims (dv=%d, K=%d)", p.dv, p.K);
+  if (p.dv % GDN_ROWS || p.K < 1 || p.K > GDN_MAXK || p.H % 4 || p.H > GDN_MAX_H)
+    return set_error(INFERNO_EINVAL, "gdn: unsupported dims (dv=%d, K=%d, H=%d)", p.dv, p.K, p.H);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(gdn_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 3 * GDN_MAX_H * 4);
+    cudaFuncSetAttribute(gdn_step_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared);
+    attr = true;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.nv, p.dv / GDN_ROWS);
   cfg.blockDim = dim3(GDN_THREADS);
+  cfg.dynamicSmemBytes = (size_t)3 * p.H * 4;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -33,8 +33,9 @@ namespace inf {
 enum Pro : int { PRO_NONE = 0, PRO_RMSNORM = 1, PRO_HEADNORM_GATE = 2 };
 enum Epi : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
 
-constexpr int GEMV_NW = 16;                   // consumer warps
-constexpr int GEMV_THREADS = (GEMV_NW + 1) * 32;
+// Consumer warps per CTA (template NW): 8 for the per-layer matrices (two
+// CTAs fit on an SM, so the next kernel can be resident under programmatic
+// dependent launch), 16 for large matrices (lm_head).
 constexpr int GEMV_CHUNK = 1024;              // elements per chunk (32 lanes x 32)
 constexpr int GEMV_MAX_SEG = 4;
 constexpr int GEMV_MAX_STAGES = 8;
@@ -51,6 +52,7 @@ struct GemvParams {
   int nseg, ntiles;
   int inner, row_bytes, nkc;
   int TR, slot, stages;
+  int nkg;                        // K groups: warps splitting a tile's chunks
   int contig;                     // 1: a tile's rows are copied as one range (nkc == 1)
   int stage_bytes;
   int part1_off;                  // contig + SwiGLU: stage offset of the up-rows range
@@ -89,6 +91,11 @@ __device__ __forceinline__ float2 upk2(f2_t v) {
 __device__ __forceinline__ f2_t ffma2(f2_t a, f2_t b, f2_t c) {
   f2_t d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f2_t fadd2(f2_t a, f2_t b) {
+  f2_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 __device__ __forceinline__ f2_t fsub2(f2_t a, f2_t b) {
@@ -355,22 +362,6 @@ __device__ __forceinline__ bool reduce_writer(int lane) {
   else return lane == 0;
 }
 
-// ---------------------------------------------------------------------------
-// prologue: build the transformed input vector(s) in shared memory
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ float block_sum_consumers(float v, float* red, int tid) {
-  v = warp_sum(v);
-  int w = tid >> 5;
-  __syncwarp();
-  if ((tid & 31) == 0) red[w] = v;
-  named_bar_sync(1, GEMV_NW * 32);
-  float t = 0.f;
-#pragma unroll
-  for (int i = 0; i < GEMV_NW; ++i) t += red[i];
-  named_bar_sync(1, GEMV_NW * 32);
-  return t;
-}
-
 // Shared-memory activation layout ("fragment-interleaved"): element e of
 // chunk kc, held by lane L in fragment slot q (e == Frag::xpos(L, q)), lives at
 // float index  kc*1024 + (q/4)*128 + L*4 + q%4  so that for every float4 k a
@@ -394,61 +385,51 @@ __device__ __forceinline__ int xperm(int i) {
   return (kc << 10) + (q >> 2) * 128 + lane * 4 + (q & 3);
 }
 
-// Prologue: the transformed input vector(s) in the permuted layout, plus (Q4_K,
-// Q5_K) the per-lane sums of the lo / hi 16-element runs of every chunk.
-template <int TYPE, bool SUMS>
-__device__ void gemv_prologue(const GemvParams& p, float* xs, float* xsum, float* red, int tid) {
+// Prologue: the input vector(s) in the permuted layout, in one pass and one
+// barrier.  For RMSNorm the stored value is x*w (norm weight) and the 1/rms
+// factor, a scalar per batch column, is applied to each row's dot product in
+// the epilogue: scale * sum_i W[r,i] x[i] w[i] == sum_i W[r,i] (x[i]*scale*w[i])
+// (rmsnorm_cpu!, src/ModelCPU.jl:110-122, reassociated).  red[b*NW + warp]
+// receives the per-warp partial sums of x^2.
+template <int TYPE, int NW>
+__device__ void gemv_prologue(const GemvParams& p, float* xs, float* red, int tid) {
   const int n = p.inner;
   const int npad = p.nkc * GEMV_CHUNK;
+  const int lane = tid & 31, w = tid >> 5;
   for (int b = 0; b < p.nb; ++b) {
     const float* x = p.x + (long long)b * p.x_stride;
     float* o = xs + (long long)b * npad;
     if (p.pro == PRO_RMSNORM) {
-      // rmsnorm_cpu! (src/ModelCPU.jl:110-122): out = x * scale * w
       float ss = 0.f;
-      for (int i = tid; i < n; i += GEMV_NW * 32) ss += x[i] * x[i];
-      ss = block_sum_consumers(ss, red, tid);
-      float scale = 1.0f / sqrtf(ss / (float)n + p.eps);
-      for (int i = tid; i < n; i += GEMV_NW * 32) o[xperm<TYPE>(i)] = x[i] * scale * p.pro_w[i];
+      for (int i = tid; i < n; i += NW * 32) {
+        const float v = x[i];
+        ss = fmaf(v, v, ss);
+        o[xperm<TYPE>(i)] = v * p.pro_w[i];
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) red[b * NW + w] = ss;
     } else if (p.pro == PRO_HEADNORM_GATE) {
       // per-head rmsnorm of the GDN output, then * z * sigmoid(z)
       // (src/ModelCPU.jl:682-692)
       const int G = p.pro_group;
       const float* z = p.pro_z + (long long)b * p.x_stride;
-      int lane = tid & 31, w = tid >> 5;
-      for (int h = w; h < n / G; h += GEMV_NW) {
+      for (int h = w; h < n / G; h += NW) {
         const float* y = x + h * G;
         float ss = 0.f;
         for (int i = lane; i < G; i += 32) ss += y[i] * y[i];
         ss = warp_sum(ss);
-        float scale = 1.0f / sqrtf(ss / (float)G + p.eps);
+        const float scale = 1.0f / sqrtf(ss / (float)G + p.eps);
         for (int i = lane; i < G; i += 32) {
-          float v = y[i] * scale * p.pro_w[i];
-          float zz = z[h * G + i];
+          const float v = y[i] * scale * p.pro_w[i];
+          const float zz = z[h * G + i];
           o[xperm<TYPE>(h * G + i)] = v * zz * (1.0f / (1.0f + expf(-zz)));
         }
       }
     } else {
-      for (int i = tid; i < n; i += GEMV_NW * 32) o[xperm<TYPE>(i)] = x[i];
+      for (int i = tid; i < n; i += NW * 32) o[xperm<TYPE>(i)] = x[i];
     }
   }
-  named_bar_sync(1, GEMV_NW * 32);
-  if (SUMS) {
-    // xsum[b][kc][lane] = (sum of slots 0..15, sum of slots 16..31)
-    for (int k = tid; k < p.nb * p.nkc * 32; k += GEMV_NW * 32) {
-      const int lane = k & 31, bk = k >> 5;
-      const float* v = xs + (long long)bk * GEMV_CHUNK + lane * 4;
-      float lo = 0.f, hi = 0.f;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 a = *(const float4*)(v + q * 128), c = *(const float4*)(v + (q + 4) * 128);
-        lo += (a.x + a.y) + (a.z + a.w);
-        hi += (c.x + c.y) + (c.z + c.w);
-      }
-      ((float2*)xsum)[k] = make_float2(lo, hi);
-    }
-    named_bar_sync(1, GEMV_NW * 32);
-  }
+  named_bar_sync(1, NW * 32);
 }
 
 // ---------------------------------------------------------------------------
@@ -459,156 +440,136 @@ __device__ __forceinline__ void tile_locate(const GemvParams& p, int tile, int& 
 #pragma unroll
   for (int s = 1; s < GEMV_MAX_SEG; ++s)
     if (s < p.nseg && tile >= p.seg[s].tile0) seg = s;
-  int half = (p.epi == EPI_SWIGLU) ? p.TR / 2 : p.TR;
+  const int half = (p.epi == EPI_SWIGLU) ? p.TR / 2 : p.TR;
   row0 = (tile - p.seg[seg].tile0) * half;
 }
 
-template <int TYPE, int NB, int R>
-__global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
+template <int TYPE, int NB, int R, int NW>
+__global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr bool SUMS = Frag<TYPE>::kNeedSums;
-  // layout: [full bars][empty bars][red 32 floats][grid 2KB][xs][xsum][stages]
+  // layout: [full bars][empty bars][red NB*NW][kpart][grid 2KB][xs][stages]
   uint64_t* full = (uint64_t*)smem;
   uint64_t* empty = full + GEMV_MAX_STAGES;
-  float* red = (float*)(empty + GEMV_MAX_STAGES);
-  uint2* grid = (uint2*)(red + 32);
+  float* red = (float*)(empty + GEMV_MAX_STAGES);   // [NB][NW] partial sums of x^2
+  float* kpart = red + 128;                         // [NB][8][64] K-group partial row sums
+  uint2* grid = (uint2*)(kpart + NB * 8 * 64);
   float* xs = (float*)(grid + 256);
-  float* xsum = xs + NB * p.nkc * GEMV_CHUNK;
-  uint8_t* stage0 = (uint8_t*)(((uintptr_t)(xsum + (SUMS ? NB * p.nkc * 64 : 0)) + 127) & ~(uintptr_t)127);
+  uint8_t* stage0 = (uint8_t*)(((uintptr_t)(xs + NB * p.nkc * GEMV_CHUNK) + 127) & ~(uintptr_t)127);
   const int stage_bytes = p.stage_bytes;
 
   if (tid == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], GEMV_NW);
+      mbar_init(&empty[s], NW);
     }
     fence_mbar_init();
   }
   __syncthreads();
 
   const int G = gridDim.x;
-  const int my_tiles = (p.ntiles - (int)blockIdx.x + G - 1) / G;
-  const int n_items = my_tiles * p.nkc;
+  const int n_items = (p.ntiles - (int)blockIdx.x + G - 1) / G;   // one item = one tile, all of K
   const bool paired = (p.epi == EPI_SWIGLU);
-  const int half_tr = p.TR / 2;
+  const int TR = p.TR, half_tr = TR / 2;
 
-  if (warp == GEMV_NW) {
-    // ---------------- producer warp ----------------
+  if (warp == NW) {
+    // ---------------- producer warp: one bulk copy per row range ----------------
+    bool waited = false;
     for (int it = 0; it < n_items; ++it) {
       const int s = it % p.stages;
       if (it >= p.stages) {
         if (!mbar_wait(&empty[s], ((it / p.stages) - 1) & 1, p.err)) break;
       }
-      const int tile = blockIdx.x + (it / p.nkc) * G, kc = it % p.nkc;
       int sg, row0;
-      tile_locate(p, tile, sg, row0);
-      const int ce = min(GEMV_CHUNK, p.inner - kc * GEMV_CHUNK);
-      const int cbytes = ce / qk_of(TYPE) * bb_of(TYPE);
-      const long long coff = (long long)kc * (GEMV_CHUNK / qk_of(TYPE)) * bb_of(TYPE);
+      tile_locate(p, blockIdx.x + it * G, sg, row0);
       uint8_t* st = stage0 + (long long)s * stage_bytes;
-      if (p.contig) {
-        // one bulk copy per contiguous row range (two for paired gate/up)
-        if (lane < (paired ? 2 : 1)) {
-          const int sgr = paired ? lane : sg;
-          const int nrows = min(paired ? half_tr : p.TR, p.seg[sgr].rows - row0);
-          uint32_t bytes = 0;
-          uintptr_t a0 = 0;
-          if (nrows > 0) {
-            uintptr_t src = (uintptr_t)(p.seg[sgr].W + (long long)row0 * p.row_bytes);
-            a0 = src & ~(uintptr_t)15;
-            uintptr_t a1 = (src + (long long)nrows * p.row_bytes + 15) & ~(uintptr_t)15;
-            bytes = (uint32_t)(a1 - a0);
-          }
-          uint32_t other = __shfl_down_sync(paired ? 3u : 1u, bytes, 1, paired ? 2 : 1);
-          if (lane == 0) mbar_arrive_expect_tx(&full[s], bytes + (paired ? other : 0u));
-          __syncwarp(paired ? 3u : 1u);
-          if (bytes) tma_load_1d(st + (lane ? p.part1_off : 0), (const void*)a0, bytes, &full[s]);
-        }
-      } else {
-        // per-lane row copies of the chunk's row segments
+      if (lane < (paired ? 2 : 1)) {
+        const int sgr = paired ? lane : sg;
+        const int nrows = min(paired ? half_tr : TR, p.seg[sgr].rows - row0);
         uint32_t bytes = 0;
-        for (int r = lane; r < p.TR; r += 32) {
-          const int sgr = paired ? (r < half_tr ? 0 : 1) : sg;
-          const int rr = row0 + (paired ? r % half_tr : r);
-          if (rr < p.seg[sgr].rows) {
-            uintptr_t src = (uintptr_t)(p.seg[sgr].W + (long long)rr * p.row_bytes + coff);
-            uintptr_t a0 = src & ~(uintptr_t)15, a1 = (src + cbytes + 15) & ~(uintptr_t)15;
-            bytes += (uint32_t)(a1 - a0);
-          }
+        uintptr_t a0 = 0;
+        if (nrows > 0) {
+          const uintptr_t src = (uintptr_t)(p.seg[sgr].W + (long long)row0 * p.row_bytes);
+          a0 = src & ~(uintptr_t)15;
+          const uintptr_t a1 = (src + (long long)nrows * p.row_bytes + 15) & ~(uintptr_t)15;
+          bytes = (uint32_t)(a1 - a0);
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
-        if (lane == 0) mbar_arrive_expect_tx(&full[s], bytes);
-        __syncwarp();
-        for (int r = lane; r < p.TR; r += 32) {
-          const int sgr = paired ? (r < half_tr ? 0 : 1) : sg;
-          const int rr = row0 + (paired ? r % half_tr : r);
-          if (rr < p.seg[sgr].rows) {
-            uintptr_t src = (uintptr_t)(p.seg[sgr].W + (long long)rr * p.row_bytes + coff);
-            uintptr_t a0 = src & ~(uintptr_t)15, a1 = (src + cbytes + 15) & ~(uintptr_t)15;
-            tma_load_1d(st + r * p.slot, (const void*)a0, (uint32_t)(a1 - a0), &full[s]);
-          }
-        }
+        const uint32_t other = __shfl_down_sync(paired ? 3u : 1u, bytes, 1, paired ? 2 : 1);
+        if (lane == 0) mbar_arrive_expect_tx(&full[s], bytes + (paired ? other : 0u));
+        __syncwarp(paired ? 3u : 1u);
+        if (bytes) tma_load_1d(st + (lane ? p.part1_off : 0), (const void*)a0, bytes, &full[s]);
       }
-      if (it == 0) pdl_trigger();
+      // weights stream before the wait; dependents launch only after it
+      if ((it == p.stages - 1 || it == n_items - 1) && !waited) {
+        pdl_wait();
+        pdl_trigger();
+        waited = true;
+      }
     }
-    if (n_items == 0) pdl_trigger();
-    pdl_wait();
+    if (!waited) {
+      pdl_wait();
+      pdl_trigger();
+    }
     return;
   }
 
   // ---------------- consumer warps ----------------
   pdl_wait();
   if (TYPE == T_IQ2_XXS) {
-    for (int i = tid; i < 256; i += GEMV_NW * 32) {
-      uint64_t g = c_iq2xxs_grid_init[i];
+    for (int i = tid; i < 256; i += NW * 32) {
+      const uint64_t g = c_iq2xxs_grid_init[i];
       grid[i] = make_uint2((uint32_t)g, (uint32_t)(g >> 32));
     }
   }
-  gemv_prologue<TYPE, SUMS>(p, xs, xsum, red, tid);
+  gemv_prologue<TYPE, NW>(p, xs, red, tid);
+  // per-column factor applied to the row dots (1/rms for RMSNorm, else 1)
+  float colscale[NB];
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    colscale[b] = 1.0f;
+    if (p.pro == PRO_RMSNORM && b < p.nb) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < NW; ++i) ss += red[b * NW + i];
+      colscale[b] = 1.0f / sqrtf(ss / (float)p.inner + p.eps);
+    }
+  }
 
-  float acc[NB][R];
-#pragma unroll
-  for (int b = 0; b < NB; ++b)
-#pragma unroll
-    for (int r = 0; r < R; ++r) acc[b][r] = 0.f;
+  // warp -> (row group wr, K group wk); the tile's rows are wr*R + r
+  const int nwr = NW / p.nkg;
+  const int wr = warp % nwr, wk = warp / nwr;
   float best_v[NB];
   int best_i[NB];
 #pragma unroll
   for (int b = 0; b < NB; ++b) { best_v[b] = -INFINITY; best_i[b] = 0x7fffffff; }
-
   const int x0 = Frag<TYPE>::xpos(lane, 0);
-  const bool lane_in_chunk_blk = true;
-  (void)lane_in_chunk_blk;
+  const int blk_mask = ~(qk_of(TYPE) == 256 ? 255 : 31);
+
   for (int it = 0; it < n_items; ++it) {
     const int s = it % p.stages;
     if (!mbar_wait(&full[s], (it / p.stages) & 1, p.err)) return;
-    const int tile = blockIdx.x + (it / p.nkc) * G, kc = it % p.nkc;
     int sg, row0;
-    tile_locate(p, tile, sg, row0);
-    const int ce = min(GEMV_CHUNK, p.inner - kc * GEMV_CHUNK);
-    const long long coff = (long long)kc * (GEMV_CHUNK / qk_of(TYPE)) * bb_of(TYPE);
-    const bool active = (x0 & ~(qk_of(TYPE) == 256 ? 255 : 31)) < ce;
+    tile_locate(p, blockIdx.x + it * G, sg, row0);
     const uint8_t* st = stage0 + (long long)s * stage_bytes;
-    // shared-memory address of this warp's first row and the row stride
+    // shared-memory address of each of this warp's rows
     const uint8_t* rp[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      const int slot = paired ? ((r < R / 2) ? warp * (R / 2) + r : half_tr + warp * (R / 2) + (r - R / 2))
-                              : warp * R + r;
       const int sgr = paired ? (r < R / 2 ? 0 : 1) : sg;
-      const int rrel = paired ? slot % half_tr : slot;
-      const uint8_t* Wb = p.seg[sgr].W;
-      if (p.contig) {
-        const uint32_t mis = (uint32_t)((uintptr_t)(Wb + (long long)row0 * p.row_bytes) & 15);
-        rp[r] = st + ((paired && sgr) ? p.part1_off : 0) + mis + rrel * p.row_bytes;
-      } else {
-        const uint32_t mis = (uint32_t)((uintptr_t)(Wb + (long long)(row0 + rrel) * p.row_bytes + coff) & 15);
-        rp[r] = st + slot * p.slot + mis;
-      }
+      const int rrel = paired ? wr * (R / 2) + (r % (R >= 2 ? R / 2 : 1)) : wr * R + r;
+      const uint32_t mis = (uint32_t)((uintptr_t)(p.seg[sgr].W + (long long)row0 * p.row_bytes) & 15);
+      rp[r] = st + ((paired && sgr) ? p.part1_off : 0) + mis + (long long)rrel * p.row_bytes;
     }
-    if (active) {
+    float acc[NB][R];
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int r = 0; r < R; ++r) acc[b][r] = 0.f;
+    for (int kc = wk; kc < p.nkc; kc += p.nkg) {
+      const int ce = min(GEMV_CHUNK, p.inner - kc * GEMV_CHUNK);
+      if ((x0 & blk_mask) >= ce) continue;
+      const long long coff = (long long)kc * (GEMV_CHUNK / qk_of(TYPE)) * bb_of(TYPE);
 #pragma unroll
       for (int b = 0; b < NB; ++b) {
         if (b >= p.nb) break;
@@ -622,15 +583,21 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
         }
         float xs_lo = 0.f, xs_hi = 0.f;
         if (SUMS) {
-          const float2 sv = ((const float2*)xsum)[((long long)b * p.nkc + kc) * 32 + lane];
-          xs_lo = sv.x;
-          xs_hi = sv.y;
+          // lo run = slots 0..15, hi run = slots 16..31 of the fragment
+          f2_t a0 = xv[0], a1 = xv[8];
+#pragma unroll
+          for (int k = 1; k < 8; ++k) {
+            a0 = fadd2(a0, xv[k]);
+            a1 = fadd2(a1, xv[8 + k]);
+          }
+          xs_lo = hsum2(a0);
+          xs_hi = hsum2(a1);
         }
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           float v;
-          if constexpr (TYPE == T_IQ2_XXS) v = Frag<T_IQ2_XXS>::dot_grid(rp[r], lane, xv, grid);
-          else v = Frag<TYPE>::dot(rp[r], lane, xv, xs_lo, xs_hi);
+          if constexpr (TYPE == T_IQ2_XXS) v = Frag<T_IQ2_XXS>::dot_grid(rp[r] + coff, lane, xv, grid);
+          else v = Frag<TYPE>::dot(rp[r] + coff, lane, xv, xs_lo, xs_hi);
           acc[b][r] += v;
         }
       }
@@ -638,43 +605,52 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
 
-    if (kc == p.nkc - 1) {
-      // ---- epilogue for this tile ----
-      const int myrow = reduce_row_of<R>(lane);
-      const bool writer = reduce_writer<R>(lane);
+    // ---- reduce the tile's rows: lanes, then K groups through smem ----
+    const int myrow = reduce_row_of<R>(lane);
+    const bool writer = reduce_writer<R>(lane);
+    float tot[NB];
 #pragma unroll
-      for (int b = 0; b < NB; ++b) {
-        if (b >= p.nb) break;
-        const float tot = reduce_rows<R>(acc[b], lane);
-        if (paired) {
-          // rows r < R/2 are gate rows, r >= R/2 the matching up rows
-          const float other = __shfl_xor_sync(0xffffffffu, tot, (R == 4) ? 16 : 16);
-          const int row = row0 + warp * (R / 2) + (R >= 2 ? myrow % (R >= 2 ? R / 2 : 1) : 0);
-          if (writer && myrow < R / 2 && row < p.seg[0].rows) {
-            const float g = tot, u = other;
-            const float sg_ = g / (1.0f + expf(-g));      // mlp_forward (src/ModelCPU.jl:455-468)
-            p.seg[0].y[(long long)b * p.y_stride + row] = sg_ * u;
-          }
-        } else {
-          const int row = row0 + warp * R + myrow;
-          const bool valid = row < p.seg[sg].rows;
+    for (int b = 0; b < NB; ++b) tot[b] = (b < p.nb) ? reduce_rows<R>(acc[b], lane) : 0.f;
+    if (p.nkg > 1) {
+      if (wk > 0 && writer)
+#pragma unroll
+        for (int b = 0; b < NB; ++b) kpart[(b * 8 + wk) * 64 + wr * R + myrow] = tot[b];
+      named_bar_sync(2, NW * 32);
+      if (wk == 0 && writer)
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+          for (int g = 1; g < p.nkg; ++g) tot[b] += kpart[(b * 8 + g) * 64 + wr * R + myrow];
+      named_bar_sync(2, NW * 32);   // kpart reused by the next tile
+    }
+    if (wk != 0) continue;
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+      if (b >= p.nb) break;
+      const float t = tot[b] * colscale[b];
+      if (paired) {
+        // rows r < R/2 are gate rows, r >= R/2 the matching up rows
+        const float other = __shfl_xor_sync(0xffffffffu, t, 16);
+        const int row = row0 + wr * (R / 2) + (R >= 2 ? myrow % (R >= 2 ? R / 2 : 1) : 0);
+        if (writer && myrow < R / 2 && row < p.seg[0].rows) {
+          const float sg_ = t / (1.0f + expf(-t));      // mlp_forward (src/ModelCPU.jl:455-468)
+          p.seg[0].y[(long long)b * p.y_stride + row] = sg_ * other;
+        }
+      } else {
+        const int row = row0 + wr * R + myrow;
+        if (writer && row < p.seg[sg].rows) {
           if (p.epi == EPI_ARGMAX) {
-            if (writer && valid) {
-              if (tot > best_v[b] || (tot == best_v[b] && row < best_i[b])) { best_v[b] = tot; best_i[b] = row; }
-              if (p.seg[sg].y) p.seg[sg].y[(long long)b * p.y_stride + row] = tot;
-            }
-          } else if (writer && valid) {
+            if (t > best_v[b] || (t == best_v[b] && row < best_i[b])) { best_v[b] = t; best_i[b] = row; }
+            if (p.seg[sg].y) p.seg[sg].y[(long long)b * p.y_stride + row] = t;
+          } else {
             float* y = p.seg[sg].y + (long long)b * p.y_stride + row;
-            if (p.epi == EPI_ADD) *y += tot;
-            else *y = tot;
+            if (p.epi == EPI_ADD) *y += t;
+            else *y = t;
           }
         }
-#pragma unroll
-        for (int r = 0; r < R; ++r) acc[b][r] = 0.f;
       }
     }
   }
-  if (p.epi == EPI_ARGMAX) {
+  if (p.epi == EPI_ARGMAX && wk == 0) {
 #pragma unroll
     for (int b = 0; b < NB; ++b) {
       if (b >= p.nb) break;
@@ -683,13 +659,13 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) gemv_kernel(const __grid_cons
       int i = best_i[b];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, v, o);
-        int oi = __shfl_xor_sync(0xffffffffu, i, o);
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, i, o);
         if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
       }
       if (lane == 0 && i != 0x7fffffff) {
-        unsigned long long key = ((unsigned long long)float_ordered(v) << 32) |
-                                 (unsigned long long)(0xffffffffu - (uint32_t)i);
+        const unsigned long long key = ((unsigned long long)float_ordered(v) << 32) |
+                                       (unsigned long long)(0xffffffffu - (uint32_t)i);
         atomicMax(&p.argmax[b], key);
       }
     }
