@@ -65,6 +65,24 @@ void q8_0_gemv(const uint8_t* weight, const float* x, float* out, int inner_dim,
 /* frees the cached device copies of compatibility-tier weights */
 int inferno_compat_release(void);
 
+/* Allocation-free host-pointer GEMV: out[r] = sum_i W[r,i] * x[i], same
+ * kernel and numerics as q*_gemv above, but it never calls cudaMalloc (or
+ * any allocating routine).  It is for callers that cannot let a library
+ * allocate device memory -- a host runtime that owns the device allocator or
+ * enforces a hard memory budget, or a sandboxed plugin without allocation
+ * rights.  This entry has no counterpart in the reference.
+ * Weight, x and y are staged in one static device array of
+ * INFERNO_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps
+ * until exit; weight + x + y (each rounded up to 256 B, plus 256 B) must fit,
+ * else INFERNO_EINVAL.  The array is shared by all calls and keeps the last
+ * call's contents; calls are synchronous and serialised by a mutex, but
+ * overlapping GPU work on the array from elsewhere would race.  The first
+ * call on a device looks up the array's address; make it before any stream
+ * capture.  Returns 0 or a negative status. */
+#define INFERNO_NOALLOC_SCRATCH_BYTES (32u << 20)
+int inferno_gemv_host_noalloc(int ggml_type, const uint8_t* weight, const float* x, float* out, int inner_dim,
+                              int outer_dim);
+
 /* ======================= 2. device kernel tier ============================
  * All pointers are device pointers; `stream` is a cudaStream_t (NULL = legacy
  * default stream).  Weight buffers hold GGUF blocks in native row-major layout
