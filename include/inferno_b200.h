@@ -208,6 +208,13 @@ int inferno_kernels_per_token(InfernoEngine* eng);
 int inferno_profile_tokens(InfernoEngine* eng, int32_t tok, int pos, int n_tokens, float* ms_by_class,
                            int32_t* launches_by_class);
 
+/* Debug: with INFERNO_B200_TRACE set at engine creation, each GEMV of a
+ * token records %globaltimer stamps (32 slots per GEMV, in launch order:
+ * CTA 0 at [0..15], last CTA at [16..31]; 0 entry, 1 first weight copy
+ * issued, 2 griddepcontrol.wait returned, 3 prologue done, 4 first tile
+ * arrived, 5 first tile consumed, 6 all tiles done).  Copies n stamps out. */
+int inferno_debug_trace(InfernoEngine* eng, unsigned long long* out, int n);
+
 /* Device time of the last inferno_decode_greedy call in ms (CUDA events). */
 float inferno_last_decode_ms(InfernoEngine* eng);
 

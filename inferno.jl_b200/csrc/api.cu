@@ -208,6 +208,8 @@ int inferno_gemv_ex(int ggml_type, const void* W, const float* x, float* y, int 
   c.epi = epilogue;
   c.argmax = argmax;
   c.force_r = force_rows_per_warp;
+  // debug: INFERNO_GEMV_TRACE=<device address of 32 u64> records phase times
+  if (const char* tr = getenv("INFERNO_GEMV_TRACE")) c.trace = (unsigned long long*)strtoull(tr, nullptr, 0);
   if (prologue == PRO_RMSNORM && !norm_w) return set_error(INFERNO_EINVAL, "gemv_ex: RMSNorm needs a weight");
   if (epilogue == EPI_ARGMAX && !argmax) return set_error(INFERNO_EINVAL, "gemv_ex: argmax output missing");
   if (epilogue == EPI_SWIGLU) return set_error(INFERNO_EINVAL, "gemv_ex: use inferno_gemv_swiglu");

@@ -106,6 +106,9 @@ struct InfernoEngine {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   float last_ms = 0.f;
   bool dump = false;
+  unsigned ablate = 0;           // debug: kernel classes left out (INFERNO_B200_ABLATE)
+  unsigned long long* trace = nullptr;   // debug: per-GEMV phase stamps (INFERNO_B200_TRACE)
+  int trace_idx = 0;
   int launches = 0;              // kernels enqueued by the last enqueue_token
   void* snapshot = nullptr;      // device copy of the state arena
   size_t state_bytes = 0;
@@ -175,6 +178,7 @@ int gemv(InfernoEngine* e, int type, int inner, std::initializer_list<GemvMat> m
   c.epi = epi;
   c.argmax = argmax;
   c.err = e->err;
+  if (e->trace && e->trace_idx < 256) c.trace = e->trace + 32 * (e->trace_idx++);
   int rc = launch_gemv(c, e->st, pdl);
   if (!rc) mark(e, epi == EPI_ARGMAX ? K_LMHEAD : K_GEMV);
   return rc;
@@ -187,9 +191,11 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
   const InfernoConfig& c = e->cfg;
   const int H = c.hidden_size;
   int rc;
+  const unsigned ab = e->ablate;   // timing experiments only: results are wrong when set
   if (L.ssm) {
     // [in_proj | attn_gate] on RMSNorm(x)
-    if (L.in_proj->type == L.gate->type) {
+    if (ab & 1) {
+    } else if (L.in_proj->type == L.gate->type) {
       if ((rc = gemv(e, L.in_proj->type, H, {M(L.in_proj, e->qkv), M(L.gate, e->z)}, e->x, PRO_RMSNORM,
                      (const float*)L.attn_norm->d, nullptr, 0, EPI_STORE, nullptr, pdl)))
         return rc;
@@ -222,15 +228,16 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     g.y = e->y;
     g.step = L.step;
     g.done = L.done;
-    if ((rc = launch_gdn_step(g, e->st, pdl))) return rc;
+    if (!(ab & 2) && (rc = launch_gdn_step(g, e->st, pdl))) return rc;
     mark(e, K_GDN);
-    if ((rc = gemv(e, L.ssm_out->type, e->di, {M(L.ssm_out, e->x)}, e->y, PRO_HEADNORM_GATE,
+    if (!(ab & 8) && (rc = gemv(e, L.ssm_out->type, e->di, {M(L.ssm_out, e->x)}, e->y, (ab & 128) ? PRO_NONE : PRO_HEADNORM_GATE,
                    (const float*)L.ssm_norm->d, e->z, c.ssm_dv, EPI_ADD, nullptr, pdl)))
       return rc;
   } else {
     const int qrows = (int)L.wq->rows();
     (void)qrows;
-    if (L.wq->type == L.wk->type && L.wk->type == L.wv->type) {
+    if (ab & 1) {
+    } else if (L.wq->type == L.wk->type && L.wk->type == L.wv->type) {
       if ((rc = gemv(e, L.wq->type, H, {M(L.wq, e->qg), M(L.wk, e->k), M(L.wv, e->v)}, e->x, PRO_RMSNORM,
                      (const float*)L.attn_norm->d, nullptr, 0, EPI_STORE, nullptr, pdl)))
         return rc;
@@ -265,21 +272,21 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     a.counters = e->att_counters;
     a.out = e->o;
     a.err = e->err;
-    if ((rc = launch_attn_decode(a, e->st, pdl))) return rc;
+    if (!(ab & 4) && (rc = launch_attn_decode(a, e->st, pdl))) return rc;
     mark(e, K_ATTN);
-    if ((rc = gemv(e, L.wo->type, c.n_heads * c.head_dim, {M(L.wo, e->x)}, e->o, PRO_NONE, nullptr, nullptr, 0,
+    if (!(ab & 8) && (rc = gemv(e, L.wo->type, c.n_heads * c.head_dim, {M(L.wo, e->x)}, e->o, PRO_NONE, nullptr, nullptr, 0,
                    EPI_ADD, nullptr, pdl)))
       return rc;
   }
   // FFN: SwiGLU(gate, up) on RMSNorm(x), then down with residual add
   if (L.ffn_gate->type == L.ffn_up->type) {
-    if ((rc = gemv(e, L.ffn_gate->type, H, {M(L.ffn_gate, e->h), M(L.ffn_up, nullptr)}, e->x, PRO_RMSNORM,
+    if (!(ab & 16) && (rc = gemv(e, L.ffn_gate->type, H, {M(L.ffn_gate, e->h), M(L.ffn_up, nullptr)}, e->x, PRO_RMSNORM,
                    (const float*)L.post_norm->d, nullptr, 0, EPI_SWIGLU, nullptr, pdl)))
       return rc;
   } else {
     return set_error(INFERNO_EINVAL, "layer %d: ffn_gate and ffn_up must share a type", li);
   }
-  if ((rc = gemv(e, L.ffn_down->type, c.intermediate_size, {M(L.ffn_down, e->x)}, e->h, PRO_NONE, nullptr, nullptr,
+  if (!(ab & 32) && (rc = gemv(e, L.ffn_down->type, c.intermediate_size, {M(L.ffn_down, e->x)}, e->h, PRO_NONE, nullptr, nullptr,
                  0, EPI_ADD, nullptr, pdl)))
     return rc;
   if (e->dump)
@@ -307,6 +314,7 @@ int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
   const InfernoConfig& c = e->cfg;
   int rc;
   e->launches = 0;
+  e->trace_idx = 0;
   if (e->profiling) mark(e, -1), --e->launches;
   if ((rc = launch_embed_row(e->embd->type, e->embd->d, (long long)e->embd->bytes / e->embd->rows(), c.hidden_size,
                              &e->ctl->tok, e->x, c.vocab_size, e->st, pdl)))
@@ -314,7 +322,7 @@ int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
   mark(e, K_EMBED);
   for (int i = 0; i < c.num_layers; ++i)
     if ((rc = enqueue_layer(e, i, pdl))) return rc;
-  if ((rc = gemv(e, e->lm_head->type, c.hidden_size, {M(e->lm_head, write_logits ? e->logits : nullptr)}, e->x,
+  if (!(e->ablate & 64) && (rc = gemv(e, e->lm_head->type, c.hidden_size, {M(e->lm_head, write_logits ? e->logits : nullptr)}, e->x,
                  PRO_RMSNORM, (const float*)e->out_norm->d, nullptr, 0, EPI_ARGMAX, &e->ctl->argkey, pdl)))
     return rc;
   return launch_finalize(e, pdl);
@@ -420,6 +428,11 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
   cudaEventCreate(&e->ev1);
   const char* d = getenv("INFERNO_B200_DUMP");
   e->dump = d && atoi(d) != 0;
+  if (const char* ab = getenv("INFERNO_B200_ABLATE")) e->ablate = (unsigned)strtoul(ab, nullptr, 0);
+  if (getenv("INFERNO_B200_TRACE")) {
+    if (cudaMalloc(&e->trace, 32 * 256 * 8) != cudaSuccess) e->trace = nullptr;
+    else cudaMemset(e->trace, 0, 32 * 256 * 8);
+  }
   *out = e;
   return 0;
 }
@@ -740,6 +753,15 @@ int inferno_profile_tokens(InfernoEngine* e, int32_t tok, int pos, int n_tokens,
   return check_device_error(e);
 }
 
+int inferno_debug_trace(InfernoEngine* e, unsigned long long* out, int n) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  if (!e->trace) return set_error(INFERNO_ESTATE, "engine created without INFERNO_B200_TRACE");
+  if (n > 32 * 256) n = 32 * 256;
+  INF_CUDA_TRY(cudaMemcpy(out, e->trace, (size_t)n * 8, cudaMemcpyDeviceToHost));
+  return 0;
+}
+
 int inferno_engine_destroy(InfernoEngine* e) {
   if (!e) return 0;
   cudaSetDevice(e->dev);
@@ -748,6 +770,7 @@ int inferno_engine_destroy(InfernoEngine* e) {
   if (e->g1_logits) cudaGraphExecDestroy(e->g1_logits);
   if (e->g8) cudaGraphExecDestroy(e->g8);
   if (e->snapshot) cudaFree(e->snapshot);
+  if (e->trace) cudaFree(e->trace);
   for (auto& kv : e->tensors) cudaFree(kv.second.d);
   for (void* p : e->allocs) cudaFree(p);
   if (e->ev0) cudaEventDestroy(e->ev0);

@@ -75,7 +75,8 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
     if (((uintptr_t)c.mats[i].W & 15) != 0) return set_error(-1, "gemv: weight pointer not 16-byte aligned");
     if (c.mats[i].rows < 0) return set_error(-1, "gemv: negative rows");
   }
-  if (c.pro == PRO_HEADNORM_GATE && (c.pro_group <= 0 || c.inner % c.pro_group))
+  if (c.pro == PRO_HEADNORM_GATE &&
+      (c.pro_group <= 0 || c.pro_group % 32 || c.pro_group > 256 || c.inner % c.pro_group))
     return set_error(-1, "gemv: bad head group %d", c.pro_group);
   int dev = 0;
   cudaGetDevice(&dev);
@@ -105,10 +106,15 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
   // bytes the slowest CTA streams, with small penalties for fewer rows per
   // warp (activation reuse) and for K groups (cross-warp reduction).
   int best_r = 0, best_g = 1;
+  static const int env_force_r = getenv("INFERNO_GEMV_FORCE_R") ? atoi(getenv("INFERNO_GEMV_FORCE_R")) : 0;
+  // single-column calls use 4 rows per warp: one GEMV instantiation per type
+  // keeps the engine's instruction working set small (the per-layer kernels
+  // are latency-bound and cold code costs microseconds per launch)
+  const int force_r = c.force_r ? c.force_r : (env_force_r ? env_force_r : (c.nb == 1 ? 4 : 0));
   double best_cost = 1e300;
   for (int R : {4, 2, 1}) {
     if (paired && R < 2) continue;
-    if (c.force_r && R != c.force_r) continue;
+    if (force_r && R != force_r) continue;
     if (c.nb > 1 && R != (paired ? 2 : 1)) continue;
     for (int g : {1, 2, 4, 8}) {
       if (g > nkc) continue;
@@ -153,6 +159,7 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
   p.pro_group = c.pro_group;
   p.epi = c.epi;
   p.err = c.err ? c.err : device_error_word(dev);
+  p.trace = c.trace;
   if (ntiles == 0) return 0;
   const size_t stage_bytes = stage_of(TR);
   int stages = (int)std::min<size_t>(GEMV_MAX_STAGES, std::max<size_t>(2, ring_budget / stage_bytes));

@@ -67,7 +67,20 @@ struct GemvParams {
   int epi;
   unsigned long long* argmax;     // [nb] packed (ordered value, ~index)
   int* err;
+  unsigned long long* trace;      // debug: phase timestamps of CTA 0 / last CTA (null = off)
 };
+
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// debug phase stamps (INFERNO_GEMV_TRACE): CTA 0 -> slots 0..15, last CTA -> 16..31
+#define GEMV_TRACE(slot)                                                            \
+  do {                                                                              \
+    if (p.trace && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1))                \
+      p.trace[(blockIdx.x == 0 ? 0 : 16) + (slot)] = gtimer();                      \
+  } while (0)
 
 __device__ __constant__ uint64_t c_iq2xxs_grid_init[256] = {
 #include "iq2xxs_grid.inc"
@@ -410,19 +423,31 @@ __device__ void gemv_prologue(const GemvParams& p, float* xs, float* red, int ti
       if (lane == 0) red[b * NW + w] = ss;
     } else if (p.pro == PRO_HEADNORM_GATE) {
       // per-head rmsnorm of the GDN output, then * z * sigmoid(z)
-      // (src/ModelCPU.jl:682-692)
+      // (src/ModelCPU.jl:682-692); warp per head, loads first, compact code
       const int G = p.pro_group;
       const float* z = p.pro_z + (long long)b * p.x_stride;
-      for (int h = w; h < n / G; h += NW) {
-        const float* y = x + h * G;
+      const int per = G >> 5;                 // elements per lane (G <= 256)
+#pragma unroll 1
+      for (int hh = w; hh < n / G; hh += NW) {
+        float yv[8], zv[8], wv[8];
         float ss = 0.f;
-        for (int i = lane; i < G; i += 32) ss += y[i] * y[i];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const bool ok = q < per;
+          const int i = hh * G + q * 32 + lane;
+          yv[q] = ok ? x[i] : 0.f;
+          zv[q] = ok ? z[i] : 0.f;
+          wv[q] = ok ? p.pro_w[q * 32 + lane] : 0.f;
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) ss = fmaf(yv[q], yv[q], ss);
         ss = warp_sum(ss);
         const float scale = 1.0f / sqrtf(ss / (float)G + p.eps);
-        for (int i = lane; i < G; i += 32) {
-          const float v = y[i] * scale * p.pro_w[i];
-          const float zz = z[h * G + i];
-          o[xperm<TYPE>(h * G + i)] = v * zz * (1.0f / (1.0f + expf(-zz)));
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (q >= per) break;
+          const float v = yv[q] * scale * wv[q];
+          o[xperm<TYPE>(hh * G + q * 32 + lane)] = v * zv[q] * (1.0f / (1.0f + expf(-zv[q])));
         }
       }
     } else {
@@ -448,6 +473,7 @@ template <int TYPE, int NB, int R, int NW>
 __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) GEMV_TRACE(0);
   constexpr bool SUMS = Frag<TYPE>::kNeedSums;
   // layout: [full bars][empty bars][red NB*NW][kpart][grid 2KB][xs][stages]
   uint64_t* full = (uint64_t*)smem;
@@ -499,6 +525,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
         if (lane == 0) mbar_arrive_expect_tx(&full[s], bytes + (paired ? other : 0u));
         __syncwarp(paired ? 3u : 1u);
         if (bytes) tma_load_1d(st + (lane ? p.part1_off : 0), (const void*)a0, bytes, &full[s]);
+        if (lane == 0 && it == 0) GEMV_TRACE(1);
       }
       // weights stream before the wait; dependents launch only after it
       if ((it == p.stages - 1 || it == n_items - 1) && !waited) {
@@ -516,6 +543,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
 
   // ---------------- consumer warps ----------------
   pdl_wait();
+  if (tid == 0) GEMV_TRACE(2);
   if (TYPE == T_IQ2_XXS) {
     for (int i = tid; i < 256; i += NW * 32) {
       const uint64_t g = c_iq2xxs_grid_init[i];
@@ -523,6 +551,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
     }
   }
   gemv_prologue<TYPE, NW>(p, xs, red, tid);
+  if (tid == 0) GEMV_TRACE(3);
   // per-column factor applied to the row dots (1/rms for RMSNorm, else 1)
   float colscale[NB];
 #pragma unroll
@@ -549,6 +578,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
   for (int it = 0; it < n_items; ++it) {
     const int s = it % p.stages;
     if (!mbar_wait(&full[s], (it / p.stages) & 1, p.err)) return;
+    if (tid == 0 && it == 0) GEMV_TRACE(4);
     int sg, row0;
     tile_locate(p, blockIdx.x + it * G, sg, row0);
     const uint8_t* st = stage0 + (long long)s * stage_bytes;
@@ -604,6 +634,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+    if (tid == 0 && it == 0) GEMV_TRACE(5);
 
     // ---- reduce the tile's rows: lanes, then K groups through smem ----
     const int myrow = reduce_row_of<R>(lane);
@@ -650,6 +681,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
       }
     }
   }
+  if (tid == 0) GEMV_TRACE(6);
   if (p.epi == EPI_ARGMAX && wk == 0) {
 #pragma unroll
     for (int b = 0; b < NB; ++b) {

@@ -45,6 +45,7 @@ struct GemvCall {
   unsigned long long* argmax = nullptr;
   int* err = nullptr;
   int force_r = 0;            // 0 = planner's choice
+  unsigned long long* trace = nullptr;   // debug phase timestamps (32 slots)
 };
 
 int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl);

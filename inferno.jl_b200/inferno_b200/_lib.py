@@ -42,7 +42,7 @@ EXPORTS = [
     "inferno_reset_states", "inferno_dump_hidden", "inferno_state_size", "inferno_state_export",
     "inferno_state_import", "inferno_last_decode_ms", "inferno_engine_destroy",
     "inferno_state_save_device", "inferno_state_restore_device", "inferno_kernels_per_token",
-    "inferno_profile_tokens", "inferno_gemv_host_noalloc",
+    "inferno_profile_tokens", "inferno_gemv_host_noalloc", "inferno_debug_trace",
 ]
 
 _lib = None
@@ -88,6 +88,7 @@ def _sig(L0):
     L.inferno_last_decode_ms.restype = f
     L.inferno_engine_destroy.argtypes = [p]
     L.inferno_gemv_host_noalloc.argtypes = [i, p, p, p, i, i]
+    L.inferno_debug_trace.argtypes = [p, p, i]
     L.inferno_state_save_device.argtypes = [p]
     L.inferno_state_restore_device.argtypes = [p]
     L.inferno_kernels_per_token.argtypes = [p]
