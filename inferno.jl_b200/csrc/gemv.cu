@@ -87,7 +87,11 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
   for (int i = 0; i < c.nmats; ++i) wbytes += (long long)c.mats[i].rows * row_bytes;
   // small matrices: lean CTAs (8 consumer warps, <= ~110 KB smem) so that
   // two CTAs -- this kernel's and the next one's -- fit on an SM
-  const int NW = (c.nb > 1 || wbytes > (16ll << 20)) ? 16 : 8;
+  static const int env_nw = getenv("INFERNO_GEMV_FORCE_NW") ? atoi(getenv("INFERNO_GEMV_FORCE_NW")) : 0;
+  // 16 consumer warps: per-tile parallelism matters more on the latency-bound
+  // per-layer matrices than letting the next kernel's CTA co-reside (measured)
+  const int NW = env_nw ? env_nw : 16;
+  (void)wbytes;
   const size_t fixed = 16 * GEMV_MAX_STAGES + 128 * 4 + 256 * 8 + 128;
   const size_t smem_cap = NW == 8 ? 110 * 1024 : 220 * 1024;
   const size_t ring_budget = NW == 8 ? 64 * 1024 : 96 * 1024;
@@ -107,11 +111,14 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
   // warp (activation reuse) and for K groups (cross-warp reduction).
   int best_r = 0, best_g = 1;
   static const int env_force_r = getenv("INFERNO_GEMV_FORCE_R") ? atoi(getenv("INFERNO_GEMV_FORCE_R")) : 0;
-  // single-column calls use 4 rows per warp: one GEMV instantiation per type
+  // single-column calls use 2 rows per warp: one GEMV instantiation per type
   // keeps the engine's instruction working set small (the per-layer kernels
   // are latency-bound and cold code costs microseconds per launch)
-  const int force_r = c.force_r ? c.force_r : (env_force_r ? env_force_r : (c.nb == 1 ? 4 : 0));
+  const int pref_r = c.force_r ? c.force_r : (env_force_r ? env_force_r : (c.nb == 1 ? 2 : 0));
   double best_cost = 1e300;
+  for (int attempt = 0; attempt < 2 && !best_r; ++attempt) {
+  // the preferred R is dropped (planner's choice) if its tiles do not fit
+  const int force_r = (attempt == 0 || c.force_r) ? pref_r : 0;
   for (int R : {4, 2, 1}) {
     if (paired && R < 2) continue;
     if (force_r && R != force_r) continue;
@@ -129,6 +136,7 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
       const double cost = (double)waves * TR * row_bytes * (R == 4 ? 1.0 : R == 2 ? 1.1 : 1.22) * (1.0 + 0.04 * (g - 1));
       if (cost < best_cost) { best_cost = cost; best_r = R; best_g = g; }
     }
+  }
   }
   if (!best_r) return set_error(-1, "gemv: rows of %lld bytes do not fit shared memory", row_bytes);
   const int R = best_r, TR = R * NW / best_g, eff = paired ? TR / 2 : TR;
@@ -160,6 +168,8 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
   p.epi = c.epi;
   p.err = c.err ? c.err : device_error_word(dev);
   p.trace = c.trace;
+  static const bool no_hint = getenv("INFERNO_GEMV_NO_L2HINT") != nullptr;
+  p.l2_evict_first = no_hint ? 0 : 1;
   if (ntiles == 0) return 0;
   const size_t stage_bytes = stage_of(TR);
   int stages = (int)std::min<size_t>(GEMV_MAX_STAGES, std::max<size_t>(2, ring_budget / stage_bytes));

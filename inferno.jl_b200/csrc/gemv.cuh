@@ -67,6 +67,7 @@ struct GemvParams {
   int epi;
   unsigned long long* argmax;     // [nb] packed (ordered value, ~index)
   int* err;
+  int l2_evict_first;             // stream weights with an L2 evict_first policy
   unsigned long long* trace;      // debug: phase timestamps of CTA 0 / last CTA (null = off)
 };
 
@@ -524,7 +525,13 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
         const uint32_t other = __shfl_down_sync(paired ? 3u : 1u, bytes, 1, paired ? 2 : 1);
         if (lane == 0) mbar_arrive_expect_tx(&full[s], bytes + (paired ? other : 0u));
         __syncwarp(paired ? 3u : 1u);
-        if (bytes) tma_load_1d(st + (lane ? p.part1_off : 0), (const void*)a0, bytes, &full[s]);
+        if (bytes) {
+          // weights are read once per token: stream them with evict_first
+          if (p.l2_evict_first)
+            tma_load_1d_hint(st + (lane ? p.part1_off : 0), (const void*)a0, bytes, &full[s], l2_policy_evict_first());
+          else
+            tma_load_1d(st + (lane ? p.part1_off : 0), (const void*)a0, bytes, &full[s]);
+        }
         if (lane == 0 && it == 0) GEMV_TRACE(1);
       }
       // weights stream before the wait; dependents launch only after it
