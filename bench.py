@@ -263,7 +263,10 @@ def run_ours(args):
     tok_gbs = tok_bytes / (ms_step / NDEC / 1000.0) / 1e9 if ws == 1 else tok_bytes / (ms_step / NDEC / 1000.0) / 1e9
     traffic = None
     try:
-        traffic = json.loads((ROOT / "profiles" / "traffic.json").read_text()).get("lm_head_q6k_248320x1024")
+        # DRAM bytes of one lm_head launch from the committed ncu summary
+        for ln in (ROOT / "profiles" / "lm_head_q6k_248320x1024.md").read_text().splitlines():
+            if ln.startswith("dram_bytes_per_launch:"):
+                traffic = int(ln.split(":")[1].strip())
     except Exception:
         pass
     total_prof_ms = sum(v[0] for v in prof.values())

@@ -91,7 +91,6 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
   // 16 consumer warps: per-tile parallelism matters more on the latency-bound
   // per-layer matrices than letting the next kernel's CTA co-reside (measured)
   const int NW = env_nw ? env_nw : 16;
-  (void)wbytes;
   const size_t fixed = 16 * GEMV_MAX_STAGES + 128 * 4 + 256 * 8 + 128;
   const size_t smem_cap = NW == 8 ? 110 * 1024 : 220 * 1024;
   const size_t ring_budget = NW == 8 ? 64 * 1024 : 96 * 1024;
@@ -114,7 +113,7 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
   // single-column calls use 2 rows per warp: one GEMV instantiation per type
   // keeps the engine's instruction working set small (the per-layer kernels
   // are latency-bound and cold code costs microseconds per launch)
-  const int pref_r = c.force_r ? c.force_r : (env_force_r ? env_force_r : (c.nb == 1 ? 2 : 0));
+  const int pref_r = c.force_r ? c.force_r : (env_force_r ? env_force_r : (c.nb == 1 ? (wbytes > (16ll << 20) ? 4 : 2) : 0));
   double best_cost = 1e300;
   for (int attempt = 0; attempt < 2 && !best_r; ++attempt) {
   // the preferred R is dropped (planner's choice) if its tiles do not fit
