@@ -27,6 +27,7 @@
 #include "internal.h"
 #include "gemv.cuh"
 #include "params.h"
+#include "persist.h"
 #include "../../include/inferno_b200.h"
 
 namespace inf {
@@ -107,6 +108,14 @@ struct InfernoEngine {
   float last_ms = 0.f;
   bool dump = false;
   unsigned ablate = 0;           // debug: kernel classes left out (INFERNO_B200_ABLATE)
+  // persistent decode kernel (decode.cu)
+  bool persistent = false;
+  inf::PkStage* pk_stages = nullptr;
+  int pk_nstages = 0;
+  size_t pk_smem = 0;
+  int pk_slot = 0, pk_hidden_pad = 0, pk_inner_pad = 0;
+  unsigned* pk_barrier = nullptr;
+  int* pk_abort = nullptr;
   unsigned long long* trace = nullptr;   // debug: per-GEMV phase stamps (INFERNO_B200_TRACE)
   int trace_idx = 0;
   int launches = 0;              // kernels enqueued by the last enqueue_token
@@ -121,6 +130,9 @@ struct InfernoEngine {
 namespace inf {
 
 namespace {
+
+int build_persistent(InfernoEngine* e);
+int run_persistent(InfernoEngine* e, int tok0, int pos0, int n_prompt, int n_steps);
 
 template <class T>
 int dalloc(InfernoEngine* e, T** p, size_t count, bool state = false) {
@@ -430,8 +442,8 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
   e->dump = d && atoi(d) != 0;
   if (const char* ab = getenv("INFERNO_B200_ABLATE")) e->ablate = (unsigned)strtoul(ab, nullptr, 0);
   if (getenv("INFERNO_B200_TRACE")) {
-    if (cudaMalloc(&e->trace, 32 * 256 * 8) != cudaSuccess) e->trace = nullptr;
-    else cudaMemset(e->trace, 0, 32 * 256 * 8);
+    if (cudaMalloc(&e->trace, 32 * 256 * 8 + 8192 * 8) != cudaSuccess) e->trace = nullptr;
+    else cudaMemset(e->trace, 0, 32 * 256 * 8 + 8192 * 8);
   }
   *out = e;
   return 0;
@@ -550,6 +562,14 @@ int inferno_engine_finalize(InfernoEngine* e) {
     INF_CUDA_TRY(cudaMemcpy(e->rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
     INF_CUDA_TRY(cudaMemcpy(e->rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
   }
+  {
+    const char* pe = getenv("INFERNO_B200_PERSISTENT");
+    // opt-in: the per-stage grid barrier currently costs more than PDL-chained
+    // graph launches (0.96 vs 0.72 ms/token on qwen35-0.8b)
+    e->persistent = !e->dump && (pe && atoi(pe) != 0) && (e->embd->type == T_Q6_K || e->embd->type == T_Q4_K ||
+                                                            e->embd->type == T_Q8_0 || e->embd->type == T_F32);
+    if (e->persistent && (rc = build_persistent(e))) return rc;
+  }
   INF_CUDA_TRY(cudaDeviceSynchronize());
   e->finalized = true;
   if (c.use_graphs && !e->dump) {
@@ -561,6 +581,180 @@ int inferno_engine_finalize(InfernoEngine* e) {
   }
   return 0;
 }
+
+}  // extern "C"
+
+namespace inf {
+namespace {
+
+int pk_add_gemv(InfernoEngine* e, std::vector<PkStage>& v, int type, int inner, std::initializer_list<GemvMat> mats,
+                const float* x, int pro, const float* pro_w, const float* pro_z, int group, int epi, bool embed_row) {
+  GemvCall c;
+  c.type = type;
+  c.inner = inner;
+  for (auto& m : mats) c.mats[c.nmats++] = m;
+  c.x = x;
+  c.pro = pro;
+  c.pro_w = pro_w;
+  c.pro_z = pro_z;
+  c.pro_group = group;
+  c.eps = e->cfg.rms_eps;
+  c.epi = epi;
+  PkStage S{};
+  int rc = pk_plan_gemv(c, e->pk_slot, num_sms(e->dev), &S);
+  if (rc) return rc;
+  S.embed_row = embed_row ? 1 : 0;
+  S.g.err = e->err;
+  S.g.argmax = nullptr;
+  e->pk_inner_pad = std::max(e->pk_inner_pad, (inner + GEMV_CHUNK - 1) / GEMV_CHUNK * GEMV_CHUNK);
+  v.push_back(S);
+  return 0;
+}
+
+// The stage program of one token (see decode.cu).
+int build_persistent(InfernoEngine* e) {
+  const InfernoConfig& c = e->cfg;
+  const int H = c.hidden_size;
+  e->pk_hidden_pad = (H + 31) / 32 * 32;
+  // ring slots: what is left of 227 KB after the activation buffers
+  int max_inner = H;
+  max_inner = std::max(max_inner, e->di);
+  max_inner = std::max(max_inner, c.intermediate_size);
+  max_inner = std::max(max_inner, c.n_heads * c.head_dim);
+  e->pk_inner_pad = (max_inner + GEMV_CHUNK - 1) / GEMV_CHUNK * GEMV_CHUNK;
+  const size_t fixed = pk_smem_bytes(e->pk_hidden_pad, e->pk_inner_pad, 0);
+  long long slot = ((long long)(227 * 1024 - 1024) - (long long)fixed) / 5;
+  slot = slot / 128 * 128;
+  if (slot < 16 * 1024) return set_error(INFERNO_EINVAL, "persistent kernel: no room for weight slots");
+  e->pk_slot = (int)std::min<long long>(slot, 48 * 1024);
+  std::vector<PkStage> v;
+  int rc;
+  for (int li = 0; li < c.num_layers; ++li) {
+    LayerBind& L = e->layers[li];
+    const bool first = li == 0;
+    if (L.ssm) {
+      if (L.in_proj->type != L.gate->type) return set_error(INFERNO_EINVAL, "persistent: in_proj/gate types differ");
+      if ((rc = pk_add_gemv(e, v, L.in_proj->type, H, {M(L.in_proj, e->qkv), M(L.gate, e->z)}, e->x, PRO_RMSNORM,
+                            (const float*)L.attn_norm->d, nullptr, 0, EPI_STORE, first)))
+        return rc;
+      PkStage g{};
+      g.kind = PK_GDN;
+      GdnParams& d = g.d;
+      d.x = e->x;
+      d.in_norm = (const float*)L.attn_norm->d;
+      d.eps = c.rms_eps;
+      d.H = H;
+      d.nv = c.ssm_nv;
+      d.nk = c.ssm_nk;
+      d.dv = c.ssm_dv;
+      d.K = c.ssm_conv_kernel;
+      d.C = e->C;
+      d.qkv = e->qkv;
+      d.conv_w = (const float*)L.conv1d->d;
+      d.ring = L.ring;
+      d.w_alpha = (const float*)L.alpha->d;
+      d.w_beta = (const float*)L.beta->d;
+      d.ssm_a = (const float*)L.ssm_a->d;
+      d.dt_bias = (const float*)L.dt_bias->d;
+      d.S = L.S;
+      d.y = e->y;
+      d.step = L.step;
+      d.done = L.done;
+      if (c.ssm_conv_kernel > 8 || c.ssm_dv % 16) return set_error(INFERNO_EINVAL, "persistent: GDN dims");
+      v.push_back(g);
+      if ((rc = pk_add_gemv(e, v, L.ssm_out->type, e->di, {M(L.ssm_out, e->x)}, e->y, PRO_HEADNORM_GATE,
+                            (const float*)L.ssm_norm->d, e->z, c.ssm_dv, EPI_ADD, false)))
+        return rc;
+    } else {
+      if (L.wq->type != L.wk->type || L.wk->type != L.wv->type)
+        return set_error(INFERNO_EINVAL, "persistent: q/k/v types differ");
+      if ((rc = pk_add_gemv(e, v, L.wq->type, H, {M(L.wq, e->qg), M(L.wk, e->k), M(L.wv, e->v)}, e->x, PRO_RMSNORM,
+                            (const float*)L.attn_norm->d, nullptr, 0, EPI_STORE, first)))
+        return rc;
+      PkStage a{};
+      a.kind = PK_ATTN;
+      AttnParams& p = a.a;
+      p.qg = e->qg;
+      p.k = e->k;
+      p.v = e->v;
+      p.q_norm = (const float*)L.q_norm->d;
+      p.k_norm = (const float*)L.k_norm->d;
+      p.eps = c.rms_eps;
+      p.rope_cos = e->rope_cos;
+      p.rope_sin = e->rope_sin;
+      p.rd = e->rd;
+      p.kc = L.kc;
+      p.vc = L.vc;
+      p.nh = c.n_heads;
+      p.nkv = c.n_kv_heads;
+      p.ctx = c.max_ctx;
+      p.split_len = e->split_len;
+      p.nsplit = e->nsplit;
+      p.part_o = e->part_o;
+      p.part_ml = e->part_ml;
+      p.counters = e->att_counters;
+      p.out = e->o;
+      p.err = e->err;
+      v.push_back(a);
+      if ((rc = pk_add_gemv(e, v, L.wo->type, c.n_heads * c.head_dim, {M(L.wo, e->x)}, e->o, PRO_NONE, nullptr,
+                            nullptr, 0, EPI_ADD, false)))
+        return rc;
+    }
+    if ((rc = pk_add_gemv(e, v, L.ffn_gate->type, H, {M(L.ffn_gate, e->h), M(L.ffn_up, nullptr)}, e->x, PRO_RMSNORM,
+                          (const float*)L.post_norm->d, nullptr, 0, EPI_SWIGLU, false)))
+      return rc;
+    if ((rc = pk_add_gemv(e, v, L.ffn_down->type, c.intermediate_size, {M(L.ffn_down, e->x)}, e->h, PRO_NONE,
+                          nullptr, nullptr, 0, EPI_ADD, false)))
+      return rc;
+  }
+  if ((rc = pk_add_gemv(e, v, e->lm_head->type, H, {M(e->lm_head, e->logits)}, e->x, PRO_RMSNORM,
+                        (const float*)e->out_norm->d, nullptr, 0, EPI_ARGMAX, false)))
+    return rc;
+  for (auto& s : v) s.slot_bytes = e->pk_slot;
+  e->pk_nstages = (int)v.size();
+  e->pk_smem = pk_smem_bytes(e->pk_hidden_pad, e->pk_inner_pad, e->pk_slot);
+  if ((rc = dalloc(e, &e->pk_stages, v.size())) || (rc = dalloc(e, &e->pk_barrier, 1)) ||
+      (rc = dalloc(e, &e->pk_abort, 1)))
+    return rc;
+  INF_CUDA_TRY(cudaMemcpy(e->pk_stages, v.data(), v.size() * sizeof(PkStage), cudaMemcpyHostToDevice));
+  return 0;
+}
+
+int run_persistent(InfernoEngine* e, int tok0, int pos0, int n_prompt, int n_steps) {
+  PkParams P{};
+  P.stages = e->pk_stages;
+  P.n_stages = e->pk_nstages;
+  P.n_steps = n_steps;
+  P.tok0 = tok0;
+  P.pos0 = pos0;
+  P.n_prompt = n_prompt;
+  P.prompt = e->prompt;
+  P.out_tokens = e->out_tokens;
+  P.max_out = e->max_out;
+  P.ctl_last = &e->ctl->last;
+  P.argkey = &e->ctl->argkey;
+  P.barrier = e->pk_barrier;
+  P.abort_flag = e->pk_abort;
+  P.err = e->err;
+  P.x = e->x;
+  P.embd = (const uint8_t*)e->embd->d;
+  P.embd_type = e->embd->type;
+  P.embd_row_bytes = (long long)(e->embd->bytes / e->embd->rows());
+  P.hidden = e->cfg.hidden_size;
+  P.hidden_pad = e->pk_hidden_pad;
+  P.max_inner_pad = e->pk_inner_pad;
+  P.slot_bytes = e->pk_slot;
+  P.trace = e->trace;
+  INF_CUDA_TRY(cudaMemsetAsync(e->pk_barrier, 0, sizeof(unsigned), e->st));
+  INF_CUDA_TRY(cudaMemsetAsync(e->pk_abort, 0, sizeof(int), e->st));
+  INF_CUDA_TRY(cudaMemsetAsync(&e->ctl->argkey, 0, sizeof(unsigned long long), e->st));
+  return pk_launch(P, e->pk_smem, e->st);
+}
+
+}  // namespace
+}  // namespace inf
+
+extern "C" {
 
 static int ready(InfernoEngine* e) {
   if (!e) return set_error(INFERNO_EINVAL, "null engine");
@@ -605,7 +799,11 @@ int inferno_forward_tokens(InfernoEngine* e, const int32_t* tok, int n, int pos0
     if (tok[i] < 0 || tok[i] >= e->cfg.vocab_size) return set_error(INFERNO_EINVAL, "forward_tokens: token %d out of range", tok[i]);
   INF_CUDA_TRY(cudaMemcpyAsync(e->prompt, tok, (size_t)n * 4, cudaMemcpyHostToDevice, e->st));
   if ((rc = set_ctl(e, tok[0], pos0, n))) return rc;
-  if ((rc = run_steps(e, n, logits_out != nullptr))) return rc;
+  if (e->persistent) {
+    if ((rc = run_persistent(e, tok[0], pos0, n, n))) return rc;
+  } else if ((rc = run_steps(e, n, logits_out != nullptr))) {
+    return rc;
+  }
   Ctl h{};
   INF_CUDA_TRY(cudaMemcpyAsync(&h, e->ctl, sizeof h, cudaMemcpyDeviceToHost, e->st));
   if (logits_out)
@@ -627,7 +825,11 @@ int inferno_decode_greedy(InfernoEngine* e, int32_t tok, int pos, int n_steps, i
   if (n_steps > e->max_out) return set_error(INFERNO_EINVAL, "decode_greedy: n_steps too large");
   if ((rc = set_ctl(e, tok, pos, 1))) return rc;
   INF_CUDA_TRY(cudaEventRecord(e->ev0, e->st));
-  if ((rc = run_steps(e, n_steps, false))) return rc;
+  if (e->persistent) {
+    if ((rc = run_persistent(e, tok, pos, 1, n_steps))) return rc;
+  } else if ((rc = run_steps(e, n_steps, false))) {
+    return rc;
+  }
   INF_CUDA_TRY(cudaEventRecord(e->ev1, e->st));
   INF_CUDA_TRY(cudaMemcpyAsync(out_tokens, e->out_tokens, (size_t)n_steps * 4, cudaMemcpyDeviceToHost, e->st));
   INF_CUDA_TRY(cudaStreamSynchronize(e->st));
@@ -720,7 +922,7 @@ int inferno_state_restore_device(InfernoEngine* e) {
 int inferno_kernels_per_token(InfernoEngine* e) {
   int rc;
   if ((rc = ready(e))) return rc;
-  return e->launches;
+  return e->persistent ? 0 : e->launches;
 }
 
 int inferno_profile_tokens(InfernoEngine* e, int32_t tok, int pos, int n_tokens, float* ms_by_class,
@@ -757,7 +959,7 @@ int inferno_debug_trace(InfernoEngine* e, unsigned long long* out, int n) {
   int rc;
   if ((rc = ready(e))) return rc;
   if (!e->trace) return set_error(INFERNO_ESTATE, "engine created without INFERNO_B200_TRACE");
-  if (n > 32 * 256) n = 32 * 256;
+  if (n > 32 * 256 + 8192) n = 32 * 256 + 8192;
   INF_CUDA_TRY(cudaMemcpy(out, e->trace, (size_t)n * 8, cudaMemcpyDeviceToHost));
   return 0;
 }
