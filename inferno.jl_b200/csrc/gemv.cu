@@ -4,6 +4,7 @@
 #include <cstdlib>
 #include "internal.h"
 #include "gemv.cuh"
+#include "gemv_mma.cuh"
 
 namespace inf {
 
@@ -60,6 +61,110 @@ cudaError_t launch_nb(const GemvParams& p, int NB, int R, int NW, int grid, size
   }
 }
 
+template <int TYPE>
+cudaError_t launch_mma(const GemvParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<TYPE, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         227 * 1024);
+    if (e != cudaSuccess) return e;
+    cudaFuncSetAttribute(gemv_mma_kernel<TYPE, 16>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared);
+    attr_done[dev & 63] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(17 * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<TYPE, 16>, p);
+}
+
+// Integer tensor-core path (gemv_mma.cuh) for single-column Q4_K / Q6_K.
+// Returns 1 when the shape does not fit it (the caller falls back).
+int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool pdl) {
+  constexpr int NW = 16;
+  const int bb = bb_of(c.type);
+  const bool paired = c.epi == EPI_SWIGLU;
+  const int nsb = c.inner / 256;
+  const long long row_bytes = (long long)nsb * bb;
+  const size_t smem_cap = 220 * 1024;
+  const size_t fixed = 16 * GEMV_MAX_STAGES + (2 * NW + 4) * 4 + NW * 16 * 4 + (size_t)nsb * 16 * 4 +
+                       (size_t)c.inner * 4 + (size_t)nsb * 8 * MMA_KS_BYTES + 128;
+  auto stage_of = [&](int TR) -> size_t {
+    if (paired) return 2 * (((size_t)(TR / 2) * row_bytes + 32 + 15) / 16 * 16) + 128;
+    return ((size_t)TR * row_bytes + 48 + 127) / 128 * 128;
+  };
+  // cost: tile steps of the busiest CTA (each warp walks ceil(nsb / nkg)
+  // super-blocks per tile) plus the bytes it streams
+  int best_tr = 0;
+  double best = 1e300;
+  for (int TR : {16, 32, 64, 128}) {
+    const int nrg = TR / 16, nkg = NW / nrg;
+    if (fixed + 2 * stage_of(TR) > smem_cap) continue;
+    const int eff = paired ? TR / 2 : TR;
+    long long tiles = 0;
+    for (int i = 0; i < (paired ? 1 : c.nmats); ++i) tiles += (c.mats[i].rows + eff - 1) / eff;
+    const long long waves = (tiles + sms - 1) / sms;
+    const double cost = (double)waves * ((nsb + nkg - 1) / nkg) + (double)waves * TR * row_bytes / 65536.0;
+    if (cost < best) { best = cost; best_tr = TR; }
+  }
+  if (!best_tr) return 1;
+  const int TR = best_tr, eff = paired ? TR / 2 : TR;
+  GemvParams p = {};
+  int ntiles = 0;
+  for (int i = 0; i < c.nmats; ++i) {
+    p.seg[i].W = (const uint8_t*)c.mats[i].W;
+    p.seg[i].y = c.mats[i].y;
+    p.seg[i].rows = c.mats[i].rows;
+    if (paired && i == 1) p.seg[i].tile0 = INT_MAX;
+    else {
+      p.seg[i].tile0 = ntiles;
+      ntiles += (c.mats[i].rows + eff - 1) / eff;
+    }
+  }
+  p.nseg = c.nmats;
+  p.ntiles = ntiles;
+  p.inner = c.inner;
+  p.row_bytes = (int)row_bytes;
+  p.nkc = (c.inner + GEMV_CHUNK - 1) / GEMV_CHUNK;
+  p.TR = TR;
+  p.nkg = NW / (TR / 16);
+  p.nb = 1;
+  p.x = c.x;
+  p.x_stride = c.x_stride;
+  p.y_stride = c.y_stride;
+  p.pro = c.pro;
+  p.pro_w = c.pro_w;
+  p.pro_z = c.pro_z;
+  p.eps = c.eps;
+  p.pro_group = c.pro_group;
+  p.epi = c.epi;
+  p.argmax = c.argmax;
+  p.err = c.err ? c.err : device_error_word(dev);
+  p.trace = c.trace;
+  static const bool no_hint = getenv("INFERNO_GEMV_NO_L2HINT") != nullptr;
+  p.l2_evict_first = no_hint ? 0 : 1;
+  if (ntiles == 0) return 0;
+  const size_t stage_bytes = stage_of(TR);
+  p.stages = (int)std::min<size_t>(GEMV_MAX_STAGES, (smem_cap - fixed) / stage_bytes);
+  p.contig = 1;
+  p.stage_bytes = (int)stage_bytes;
+  p.part1_off = (int)((((size_t)(TR / 2) * row_bytes + 32 + 15) / 16) * 16);
+  const size_t smem = fixed + (size_t)p.stages * stage_bytes;
+  const int grid = std::min(ntiles, sms);
+  cudaError_t e = c.type == T_Q4_K ? launch_mma<T_Q4_K>(p, grid, smem, st, pdl) : launch_mma<T_Q6_K>(p, grid, smem, st, pdl);
+  if (e != cudaSuccess) return set_error(-2, "gemv launch failed: %s", cudaGetErrorString(e));
+  return 0;
+}
+
 }  // namespace
 
 int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
@@ -81,6 +186,11 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = num_sms(dev);
+  static const bool no_mma = getenv("INFERNO_GEMV_NO_MMA") != nullptr;
+  if (!no_mma && !c.force_r && c.nb == 1 && (c.type == T_Q4_K || c.type == T_Q6_K) && c.inner % 256 == 0) {
+    const int rc = plan_launch_mma(c, dev, sms, st, pdl);
+    if (rc <= 0) return rc;
+  }
   const long long row_bytes = (long long)c.inner / qk * bb;
   const int nkc = (c.inner + GEMV_CHUNK - 1) / GEMV_CHUNK;
   long long wbytes = 0;

@@ -470,6 +470,59 @@ __device__ __forceinline__ void tile_locate(const GemvParams& p, int tile, int& 
   row0 = (tile - p.seg[seg].tile0) * half;
 }
 
+// Producer warp of the GEMV kernels: one bulk copy per tile (two for paired
+// gate/up tiles) into the ring of stages.  Weights stream before
+// griddepcontrol.wait; dependents are released only after it.
+__device__ __forceinline__ void gemv_producer(const GemvParams& p, uint64_t* full, uint64_t* empty, uint8_t* stage0,
+                                              int lane, int n_items) {
+  const int G = gridDim.x;
+  const bool paired = (p.epi == EPI_SWIGLU);
+  const int TR = p.TR, half_tr = TR / 2;
+  bool waited = false;
+  for (int it = 0; it < n_items; ++it) {
+    const int s = it % p.stages;
+    if (it >= p.stages) {
+      if (!mbar_wait(&empty[s], ((it / p.stages) - 1) & 1, p.err)) break;
+    }
+    int sg, row0;
+    tile_locate(p, blockIdx.x + it * G, sg, row0);
+    uint8_t* st = stage0 + (long long)s * p.stage_bytes;
+    if (lane < (paired ? 2 : 1)) {
+      const int sgr = paired ? lane : sg;
+      const int nrows = min(paired ? half_tr : TR, p.seg[sgr].rows - row0);
+      uint32_t bytes = 0;
+      uintptr_t a0 = 0;
+      if (nrows > 0) {
+        const uintptr_t src = (uintptr_t)(p.seg[sgr].W + (long long)row0 * p.row_bytes);
+        a0 = src & ~(uintptr_t)15;
+        const uintptr_t a1 = (src + (long long)nrows * p.row_bytes + 15) & ~(uintptr_t)15;
+        bytes = (uint32_t)(a1 - a0);
+      }
+      const uint32_t other = __shfl_down_sync(paired ? 3u : 1u, bytes, 1, paired ? 2 : 1);
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], bytes + (paired ? other : 0u));
+      __syncwarp(paired ? 3u : 1u);
+      if (bytes) {
+        // weights are read once per token: stream them with evict_first
+        if (p.l2_evict_first)
+          tma_load_1d_hint(st + (lane ? p.part1_off : 0), (const void*)a0, bytes, &full[s], l2_policy_evict_first());
+        else
+          tma_load_1d(st + (lane ? p.part1_off : 0), (const void*)a0, bytes, &full[s]);
+      }
+      if (lane == 0 && it == 0) GEMV_TRACE(1);
+    }
+    // weights stream before the wait; dependents launch only after it
+    if ((it == p.stages - 1 || it == n_items - 1) && !waited) {
+      pdl_wait();
+      pdl_trigger();
+      waited = true;
+    }
+  }
+  if (!waited) {
+    pdl_wait();
+    pdl_trigger();
+  }
+}
+
 template <int TYPE, int NB, int R, int NW>
 __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -501,50 +554,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
   const int TR = p.TR, half_tr = TR / 2;
 
   if (warp == NW) {
-    // ---------------- producer warp: one bulk copy per row range ----------------
-    bool waited = false;
-    for (int it = 0; it < n_items; ++it) {
-      const int s = it % p.stages;
-      if (it >= p.stages) {
-        if (!mbar_wait(&empty[s], ((it / p.stages) - 1) & 1, p.err)) break;
-      }
-      int sg, row0;
-      tile_locate(p, blockIdx.x + it * G, sg, row0);
-      uint8_t* st = stage0 + (long long)s * stage_bytes;
-      if (lane < (paired ? 2 : 1)) {
-        const int sgr = paired ? lane : sg;
-        const int nrows = min(paired ? half_tr : TR, p.seg[sgr].rows - row0);
-        uint32_t bytes = 0;
-        uintptr_t a0 = 0;
-        if (nrows > 0) {
-          const uintptr_t src = (uintptr_t)(p.seg[sgr].W + (long long)row0 * p.row_bytes);
-          a0 = src & ~(uintptr_t)15;
-          const uintptr_t a1 = (src + (long long)nrows * p.row_bytes + 15) & ~(uintptr_t)15;
-          bytes = (uint32_t)(a1 - a0);
-        }
-        const uint32_t other = __shfl_down_sync(paired ? 3u : 1u, bytes, 1, paired ? 2 : 1);
-        if (lane == 0) mbar_arrive_expect_tx(&full[s], bytes + (paired ? other : 0u));
-        __syncwarp(paired ? 3u : 1u);
-        if (bytes) {
-          // weights are read once per token: stream them with evict_first
-          if (p.l2_evict_first)
-            tma_load_1d_hint(st + (lane ? p.part1_off : 0), (const void*)a0, bytes, &full[s], l2_policy_evict_first());
-          else
-            tma_load_1d(st + (lane ? p.part1_off : 0), (const void*)a0, bytes, &full[s]);
-        }
-        if (lane == 0 && it == 0) GEMV_TRACE(1);
-      }
-      // weights stream before the wait; dependents launch only after it
-      if ((it == p.stages - 1 || it == n_items - 1) && !waited) {
-        pdl_wait();
-        pdl_trigger();
-        waited = true;
-      }
-    }
-    if (!waited) {
-      pdl_wait();
-      pdl_trigger();
-    }
+    gemv_producer(p, full, empty, stage0, lane, n_items);
     return;
   }
 

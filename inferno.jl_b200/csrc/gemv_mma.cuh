@@ -1,0 +1,444 @@
+// Integer tensor-core GEMV for Q4_K and Q6_K rows (single column).
+//
+// Same operator as gemv_kernel (ModelCPU.mul! / mul_quant_mat_vec, Inferno.jl
+// src/ModelCPU.jl:284-444; dequant formulas of src/Dequant.jl:345-362 and
+// :585-596), restructured so that the per-weight work is a few integer
+// instructions instead of an int->float conversion plus an FMA:
+//
+//  * The activation vector v (after the fused prologue) is written as an
+//    exact fixed-point integer  x'_i = rint(v_i * 2^s)  with |x'| < 2^30
+//    (s from max|v|), split into four balanced int8 "limbs"
+//      x' = t0 + 2^8 t1 + 2^16 t2 + 2^24 t3,   t_l in [-128, 127].
+//    The representation error is 2^-31 of max|v| per element, below fp32
+//    rounding of the reference's own dot products.
+//  * Weight codes (4-bit Q4_K nibbles, 6-bit Q6_K values) are the A operand
+//    of mma.sync.m16n8k32 u8 x s8 -> s32 as they sit in shared memory (one
+//    mask / shift per four codes); the limbs are the B operand.  A warp
+//    multiplies 16 rows by one 32-wide k step per instruction; the 8 B
+//    columns are (limb l, half p): column 2l+p holds limb l of the 16
+//    elements of k-half p and zeros in the other half, so each column's
+//    integer result belongs to one sub-block and takes that sub-block's
+//    integer scale with one IMAD.  All integer sums are exact (bounded by
+//    256 * 63 * 128 * 128 < 2^31 per super-block and row).
+//  * Per super-block and row:  acc += d * float(sum_j sc_j * D_j), and the
+//    offset terms (Q4_K: dmin * sum_j m_j X_j; Q6_K: 32 d sum_j sc_j X_j,
+//    X_j = sum of x' over sub-block j) are accumulated separately in fp32.
+//  * The row total is  2^-s * sum_l 2^{8l} acc_l  (lane c of a quad owns limb
+//    c), times the RMSNorm 1/rms column factor.
+//
+// Tiles, the TMA ring, the producer warp, prologue fusions and epilogues are
+// those of gemv_kernel.  A warp owns 16 rows (SwiGLU: 8 gate rows as MMA rows
+// 0-7 and the matching 8 up rows as rows 8-15) and a K group of super-blocks.
+#pragma once
+#include "gemv.cuh"
+
+namespace inf {
+
+constexpr int MMA_KS_BYTES = 256;     // B bytes per k step (8 columns x 32 k)
+
+__device__ __forceinline__ void imma_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%10,%10,%10};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+template <int K>
+__device__ __forceinline__ int sbyte(uint32_t w) {   // signed byte K of w
+  return (int)(w << (24 - 8 * K)) >> 24;
+}
+// bits 2K, 2K+1 of each byte of a Q6_K qh word, moved to bits 4, 5
+// (k is a constant after unrolling)
+__device__ __forceinline__ uint32_t qh_bits(uint32_t h, int k) {
+  return (k < 2 ? (h << (4 - 2 * k)) : (h >> (2 * k - 4))) & 0x30303030u;
+}
+template <int K>
+__device__ __forceinline__ int ubyte(uint32_t w) {   // unsigned byte K of w
+  return (int)((w >> (8 * K)) & 0xffu);
+}
+
+// Element (within the vector) of k-half p, position t of the quad (ks, cc),
+// and the sub-block sum slot it belongs to.
+template <int TYPE>
+__device__ __forceinline__ int mma_elem(int ks, int cc, int p) {
+  const int sb = ks >> 3, r = ks & 7;
+  if constexpr (TYPE == T_Q4_K) return sb * 256 + (r >> 1) * 64 + 32 * p + 8 * cc + 4 * (r & 1);
+  else return sb * 256 + (r >> 2) * 128 + (r & 3) * 32 + 16 * p + 4 * cc;
+}
+template <int TYPE>
+__device__ __forceinline__ int mma_xsum_slot(int ks, int p) {
+  const int sb = ks >> 3, r = ks & 7;
+  if constexpr (TYPE == T_Q4_K) return sb * 8 + (r >> 1) * 2 + p;          // 32-element sub-blocks
+  else return sb * 16 + (r >> 2) * 8 + (r & 3) * 2 + p;                     // 16-element sub-blocks
+}
+
+// Prologue: v (RMSNorm x*w, head-norm gate, or x) into xf, then the limbs
+// into xq ([ks][8 columns][4 lanes][8 bytes]) and sub-block sums into xsum.
+// Returns the column factor (1/rms or 1) and the 2^-s descale; a non-finite
+// input makes every output NaN (as the reference's fp32 arithmetic would).
+template <int TYPE, int NW>
+__device__ void gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, float* xsum, float* red, int tid,
+                                  float& colscale, float& descale) {
+  const int n = p.inner;
+  const int lane = tid & 31, w = tid >> 5;
+  constexpr int NT = NW * 32;
+  const float* x = p.x;
+  float ss = 0.f, amax = 0.f;
+  if (p.pro == PRO_RMSNORM) {
+    for (int i = tid; i < n; i += NT) {
+      const float v = x[i];
+      ss = fmaf(v, v, ss);
+      const float u = v * p.pro_w[i];
+      amax = fmaxf(amax, fabsf(u));
+      xf[i] = u;
+    }
+  } else if (p.pro == PRO_HEADNORM_GATE) {
+    const int G = p.pro_group;
+    const int per = G >> 5;
+#pragma unroll 1
+    for (int hh = w; hh < n / G; hh += NW) {
+      float yv[8], zv[8], wv[8];
+      float hs = 0.f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const bool ok = q < per;
+        const int i = hh * G + q * 32 + lane;
+        yv[q] = ok ? x[i] : 0.f;
+        zv[q] = ok ? p.pro_z[i] : 0.f;
+        wv[q] = ok ? p.pro_w[q * 32 + lane] : 0.f;
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) hs = fmaf(yv[q], yv[q], hs);
+      hs = warp_sum(hs);
+      const float scale = 1.0f / sqrtf(hs / (float)G + p.eps);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (q >= per) break;
+        const float v = yv[q] * scale * wv[q];
+        const float u = v * zv[q] * (1.0f / (1.0f + expf(-zv[q])));
+        amax = fmaxf(amax, fabsf(u));
+        xf[hh * G + q * 32 + lane] = u;
+      }
+    }
+  } else {
+    for (int i = tid; i < n; i += NT) {
+      const float u = x[i];
+      amax = fmaxf(amax, fabsf(u));
+      xf[i] = u;
+    }
+  }
+  // NaN-propagating max: fmaxf drops NaN, so track it separately
+  ss = warp_sum(ss);
+  amax = warp_max(amax);
+  float bad = 0.f;
+  if (lane == 0) {
+    red[w] = ss;
+    red[NW + w] = amax;
+  }
+  if (tid == 0) *(volatile int*)&red[2 * NW] = 0;   // non-finite input flag
+  named_bar_sync(1, NT);
+  float tss = 0.f, tmax = 0.f;
+#pragma unroll
+  for (int i = 0; i < NW; ++i) {
+    tss += red[i];
+    tmax = fmaxf(tmax, red[NW + i]);
+  }
+  colscale = (p.pro == PRO_RMSNORM) ? 1.0f / sqrtf(tss / (float)n + p.eps) : 1.0f;
+  int e = 0;
+  if (tmax > 0.f && tmax <= 3.0e38f) frexpf(tmax, &e);   // tmax < 2^e
+  else if (!(tmax == 0.f)) bad = 1.f;                     // inf (NaN is caught per element below)
+  const int s = max(-120, min(120, 30 - e));
+  const float up = ldexpf(1.0f, s);
+  descale = ldexpf(1.0f, -s);
+
+  // limbs: one thread per quad (ks, cc) = 4 elements of each k-half
+  const int nq = n >> 3;
+  for (int q = tid; q < nq; q += NT) {
+    const int ks = q >> 2, cc = q & 3;
+    float part[2];
+#pragma unroll
+    for (int hp = 0; hp < 2; ++hp) {
+      const int e0 = mma_elem<TYPE>(ks, cc, hp);
+      const float4 v4 = *(const float4*)&xf[e0];
+      const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+      uint32_t limb[4] = {0u, 0u, 0u, 0u};
+      float sum = 0.f;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        if (vv[t] != vv[t]) bad = 1.f;
+        int xi = __float2int_rn(vv[t] * up);
+        sum += (float)xi;
+#pragma unroll
+        for (int l = 0; l < 3; ++l) {
+          const int d = (int)(int8_t)(xi & 0xff);
+          limb[l] |= (uint32_t)(d & 0xff) << (8 * t);
+          xi = (xi - d) >> 8;
+        }
+        limb[3] |= (uint32_t)(xi & 0xff) << (8 * t);
+      }
+#pragma unroll
+      for (int l = 0; l < 4; ++l) {
+        uint2 v2 = hp == 0 ? make_uint2(limb[l], 0u) : make_uint2(0u, limb[l]);
+        *(uint2*)(xq + (size_t)ks * MMA_KS_BYTES + (2 * l + hp) * 32 + cc * 8) = v2;
+      }
+      part[hp] = sum;
+    }
+    // sub-block sums: Q4_K sums 8 quads (2 ks x 4 cc), Q6_K 4 quads
+#pragma unroll
+    for (int hp = 0; hp < 2; ++hp) {
+      part[hp] += __shfl_xor_sync(0xffffffffu, part[hp], 1);
+      part[hp] += __shfl_xor_sync(0xffffffffu, part[hp], 2);
+      if (TYPE == T_Q4_K) part[hp] += __shfl_xor_sync(0xffffffffu, part[hp], 4);
+    }
+    if ((q & (TYPE == T_Q4_K ? 7 : 3)) == 0) {
+      xsum[mma_xsum_slot<TYPE>(ks, 0)] = part[0];
+      xsum[mma_xsum_slot<TYPE>(ks, 1)] = part[1];
+    }
+  }
+  if (bad != 0.f) *(volatile int*)&red[2 * NW] = 1;
+  named_bar_sync(1, NT);   // also the barrier before the tiles
+  if (*(volatile int*)&red[2 * NW]) descale = __int_as_float(0x7fc00000);
+}
+
+// ---------------------------------------------------------------------------
+// super-block bodies: rows g (ra) and g+8 (rb) of the warp's 16, lane quad c.
+// S[0], S[1]: exact integer sums for the two rows; corr: fp32 offset terms.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mma_sb_q4k(const uint8_t* ra, const uint8_t* rb, const uint8_t* xq_sb,
+                                           const float* xs_sb, int lane, float (&acc)[2], float (&corr)[2]) {
+  const int c = lane & 3;
+  const uint4 ha = *(const uint4*)ra, hb = *(const uint4*)rb;
+  // 6-bit scales s0..s7 and mins m0..m7 as bytes (Dequant.jl:345-362)
+  const uint32_t sla = ha.y & 0x3f3f3f3fu, sha = (ha.w & 0x0f0f0f0fu) | ((ha.y >> 2) & 0x30303030u);
+  const uint32_t slb = hb.y & 0x3f3f3f3fu, shb = (hb.w & 0x0f0f0f0fu) | ((hb.y >> 2) & 0x30303030u);
+  int S0 = 0, S1 = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint2 qa = *(const uint2*)(ra + 16 + 32 * j + 8 * c);
+    const uint2 qb = *(const uint2*)(rb + 16 + 32 * j + 8 * c);
+    const uint32_t wsa = j < 2 ? sla : sha, wsb = j < 2 ? slb : shb;
+    const int s0a = ubyte<0>(wsa >> (16 * (j & 1))), s1a = ubyte<1>(wsa >> (16 * (j & 1)));
+    const int s0b = ubyte<0>(wsb >> (16 * (j & 1))), s1b = ubyte<1>(wsb >> (16 * (j & 1)));
+#pragma unroll
+    for (int wd = 0; wd < 2; ++wd) {
+      const uint32_t wa = wd ? qa.y : qa.x, wb = wd ? qb.y : qb.x;
+      const uint2 bv = *(const uint2*)(xq_sb + (2 * j + wd) * MMA_KS_BYTES + lane * 8);
+      int d[4];
+      imma_k32(d, wa & 0x0f0f0f0fu, wb & 0x0f0f0f0fu, (wa >> 4) & 0x0f0f0f0fu, (wb >> 4) & 0x0f0f0f0fu, bv.x, bv.y);
+      S0 += s0a * d[0] + s1a * d[1];
+      S1 += s0b * d[2] + s1b * d[3];
+    }
+  }
+  const float2 dda = __half22float2(*(const __half2*)&ha.x), ddb = __half22float2(*(const __half2*)&hb.x);
+  acc[0] = fmaf(dda.x, (float)S0, acc[0]);
+  acc[1] = fmaf(ddb.x, (float)S1, acc[1]);
+  // mins of sub-blocks 2c, 2c+1 (this lane's share of the offset term)
+  const uint32_t mla = ha.z & 0x3f3f3f3fu, mha = ((ha.w >> 4) & 0x0f0f0f0fu) | ((ha.z >> 2) & 0x30303030u);
+  const uint32_t mlb = hb.z & 0x3f3f3f3fu, mhb = ((hb.w >> 4) & 0x0f0f0f0fu) | ((hb.z >> 2) & 0x30303030u);
+  const int sh = 16 * (c & 1);
+  const uint32_t ma = (c < 2 ? mla : mha) >> sh, mb = (c < 2 ? mlb : mhb) >> sh;
+  const float2 X = *(const float2*)(xs_sb + 2 * c);
+  corr[0] = fmaf(dda.y, (float)ubyte<0>(ma) * X.x + (float)ubyte<1>(ma) * X.y, corr[0]);
+  corr[1] = fmaf(ddb.y, (float)ubyte<0>(mb) * X.x + (float)ubyte<1>(mb) * X.y, corr[1]);
+}
+
+__device__ __forceinline__ void mma_sb_q6k(const uint8_t* ra, const uint8_t* rb, const uint8_t* xq_sb,
+                                           const float* xs_sb, int lane, float (&acc)[2], float (&corr)[2]) {
+  const int c = lane & 3;
+  int S0 = 0, S1 = 0;
+  // int8 scales sc[0..15] (four words per row)
+  uint32_t sca[4], scb[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    sca[i] = lds_u32_any(ra + 192 + 4 * i);
+    scb[i] = lds_u32_any(rb + 192 + 4 * i);
+  }
+#pragma unroll
+  for (int n6 = 0; n6 < 2; ++n6) {
+    // qh words for l = 4c.. (h = 0) and 16 + 4c.. (h = 1)
+    const uint32_t ha0 = lds_u32_any(ra + 128 + 32 * n6 + 4 * c);
+    const uint32_t ha1 = lds_u32_any(ra + 128 + 32 * n6 + 16 + 4 * c);
+    const uint32_t hb0 = lds_u32_any(rb + 128 + 32 * n6 + 4 * c);
+    const uint32_t hb1 = lds_u32_any(rb + 128 + 32 * n6 + 16 + 4 * c);
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const uint32_t la0 = lds_u32_any(ra + 64 * n6 + 32 * kk + 4 * c);
+      const uint32_t la1 = lds_u32_any(ra + 64 * n6 + 32 * kk + 16 + 4 * c);
+      const uint32_t lb0 = lds_u32_any(rb + 64 * n6 + 32 * kk + 4 * c);
+      const uint32_t lb1 = lds_u32_any(rb + 64 * n6 + 32 * kk + 16 + 4 * c);
+#pragma unroll
+      for (int hi = 0; hi < 2; ++hi) {
+        const int k = kk + 2 * hi;      // q group (Dequant.jl:585-596)
+        const int sh = 4 * hi;
+        const uint32_t ua0 = ((la0 >> sh) & 0x0f0f0f0fu) | qh_bits(ha0, k);
+        const uint32_t ua1 = ((la1 >> sh) & 0x0f0f0f0fu) | qh_bits(ha1, k);
+        const uint32_t ub0 = ((lb0 >> sh) & 0x0f0f0f0fu) | qh_bits(hb0, k);
+        const uint32_t ub1 = ((lb1 >> sh) & 0x0f0f0f0fu) | qh_bits(hb1, k);
+        const uint2 bv = *(const uint2*)(xq_sb + (4 * n6 + k) * MMA_KS_BYTES + lane * 8);
+        int d[4];
+        imma_k32(d, ua0, ub0, ua1, ub1, bv.x, bv.y);
+        const int is = 8 * n6 + 2 * k;  // scale index of h = 0; h = 1 is is + 1
+        const int s0a = sbyte<0>(sca[is >> 2] >> (8 * (is & 3))), s1a = sbyte<0>(sca[is >> 2] >> (8 * (is & 3) + 8));
+        const int s0b = sbyte<0>(scb[is >> 2] >> (8 * (is & 3))), s1b = sbyte<0>(scb[is >> 2] >> (8 * (is & 3) + 8));
+        S0 += s0a * d[0] + s1a * d[1];
+        S1 += s0b * d[2] + s1b * d[3];
+      }
+    }
+  }
+  const float da = h2f_bits(lds_u16_any(ra + 208)), db = h2f_bits(lds_u16_any(rb + 208));
+  acc[0] = fmaf(da, (float)S0, acc[0]);
+  acc[1] = fmaf(db, (float)S1, acc[1]);
+  // offset term 32 * d * sum_j sc_j X_j over sub-blocks 4c..4c+3
+  const float4 X = *(const float4*)(xs_sb + 4 * c);
+  const uint32_t wa = c == 0 ? sca[0] : c == 1 ? sca[1] : c == 2 ? sca[2] : sca[3];
+  const uint32_t wb = c == 0 ? scb[0] : c == 1 ? scb[1] : c == 2 ? scb[2] : scb[3];
+  const float ta = (float)sbyte<0>(wa) * X.x + (float)sbyte<1>(wa) * X.y + (float)sbyte<2>(wa) * X.z +
+                   (float)sbyte<3>(wa) * X.w;
+  const float tb = (float)sbyte<0>(wb) * X.x + (float)sbyte<1>(wb) * X.y + (float)sbyte<2>(wb) * X.z +
+                   (float)sbyte<3>(wb) * X.w;
+  corr[0] = fmaf(32.0f * da, ta, corr[0]);
+  corr[1] = fmaf(32.0f * db, tb, corr[1]);
+}
+
+template <int TYPE, int NW>
+__global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid_constant__ GemvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int BB = TYPE == T_Q4_K ? 144 : 210;
+  constexpr int XS_PER_SB = TYPE == T_Q4_K ? 8 : 16;
+  // layout: [full][empty][red 2*NW+4][kpart NW*16][xsum][xf][xq][stages]
+  uint64_t* full = (uint64_t*)smem;
+  uint64_t* empty = full + GEMV_MAX_STAGES;
+  float* red = (float*)(empty + GEMV_MAX_STAGES);
+  float* kpart = red + 2 * NW + 4;
+  float* xsum = kpart + NW * 16;
+  const int nsb = p.inner >> 8;
+  float* xf = xsum + nsb * 16;
+  uint8_t* xq = (uint8_t*)(xf + p.inner);
+  uint8_t* stage0 = (uint8_t*)(((uintptr_t)(xq + (size_t)nsb * 8 * MMA_KS_BYTES) + 127) & ~(uintptr_t)127);
+
+  if (tid == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int G = gridDim.x;
+  const int n_items = (p.ntiles - (int)blockIdx.x + G - 1) / G;
+  if (warp == NW) {
+    gemv_producer(p, full, empty, stage0, lane, n_items);
+    return;
+  }
+
+  pdl_wait();
+  float colscale, descale;
+  gemv_mma_prologue<TYPE, NW>(p, xf, xq, xsum, red, tid, colscale, descale);
+  const float fscale = colscale * descale;
+
+  const bool paired = (p.epi == EPI_SWIGLU);
+  const int nrg = p.TR >> 4;            // 16-row groups per tile
+  const int nkg = NW / nrg;
+  const int rg = warp % nrg, wk = warp / nrg;
+  const int g = lane >> 2, c = lane & 3;
+  const float limbw = c == 0 ? 1.0f : c == 1 ? 256.0f : c == 2 ? 65536.0f : 16777216.0f;
+  float best_v = -INFINITY;
+  int best_i = 0x7fffffff;
+
+  for (int it = 0; it < n_items; ++it) {
+    const int s = it % p.stages;
+    if (!mbar_wait(&full[s], (it / p.stages) & 1, p.err)) return;
+    int sg, row0;
+    tile_locate(p, blockIdx.x + it * G, sg, row0);
+    const uint8_t* st = stage0 + (long long)s * p.stage_bytes;
+    const uint8_t *ra, *rb;
+    if (paired) {
+      const uint32_t m0 = (uint32_t)((uintptr_t)(p.seg[0].W + (long long)row0 * p.row_bytes) & 15);
+      const uint32_t m1 = (uint32_t)((uintptr_t)(p.seg[1].W + (long long)row0 * p.row_bytes) & 15);
+      ra = st + m0 + (long long)(rg * 8 + g) * p.row_bytes;
+      rb = st + p.part1_off + m1 + (long long)(rg * 8 + g) * p.row_bytes;
+    } else {
+      const uint32_t m0 = (uint32_t)((uintptr_t)(p.seg[sg].W + (long long)row0 * p.row_bytes) & 15);
+      ra = st + m0 + (long long)(rg * 16 + g) * p.row_bytes;
+      rb = ra + 8ll * p.row_bytes;
+    }
+    float acc[2] = {0.f, 0.f}, corr[2] = {0.f, 0.f};
+    for (int sb = wk; sb < nsb; sb += nkg) {
+      if constexpr (TYPE == T_Q4_K)
+        mma_sb_q4k(ra + sb * BB, rb + sb * BB, xq + (size_t)sb * 8 * MMA_KS_BYTES, xsum + sb * XS_PER_SB, lane, acc,
+                   corr);
+      else
+        mma_sb_q6k(ra + sb * BB, rb + sb * BB, xq + (size_t)sb * 8 * MMA_KS_BYTES, xsum + sb * XS_PER_SB, lane, acc,
+                   corr);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+
+    // quad reduction: lane c holds limb c of the integer dots and a share of
+    // the offset terms
+    float ta = limbw * acc[0] - corr[0], tb = limbw * acc[1] - corr[1];
+    ta += __shfl_xor_sync(0xffffffffu, ta, 1);
+    tb += __shfl_xor_sync(0xffffffffu, tb, 1);
+    ta += __shfl_xor_sync(0xffffffffu, ta, 2);
+    tb += __shfl_xor_sync(0xffffffffu, tb, 2);
+    if (nkg > 1) {
+      if (wk > 0 && c == 0) {
+        kpart[(wk * nrg + rg) * 16 + g] = ta;
+        kpart[(wk * nrg + rg) * 16 + g + 8] = tb;
+      }
+      named_bar_sync(2, NW * 32);
+      if (wk == 0 && c == 0)
+        for (int k = 1; k < nkg; ++k) {
+          ta += kpart[(k * nrg + rg) * 16 + g];
+          tb += kpart[(k * nrg + rg) * 16 + g + 8];
+        }
+      named_bar_sync(2, NW * 32);
+    }
+    if (wk != 0 || c != 0) continue;
+    ta *= fscale;
+    tb *= fscale;
+    if (paired) {
+      const int row = row0 + rg * 8 + g;
+      if (row < p.seg[0].rows) {
+        const float sg_ = ta / (1.0f + expf(-ta));      // mlp_forward (src/ModelCPU.jl:455-468)
+        p.seg[0].y[row] = sg_ * tb;
+      }
+    } else {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = row0 + rg * 16 + g + 8 * h;
+        const float t = h ? tb : ta;
+        if (row < p.seg[sg].rows) {
+          if (p.epi == EPI_ARGMAX) {
+            if (t > best_v || (t == best_v && row < best_i)) { best_v = t; best_i = row; }
+            if (p.seg[sg].y) p.seg[sg].y[row] = t;
+          } else {
+            float* y = p.seg[sg].y + row;
+            if (p.epi == EPI_ADD) *y += t;
+            else *y = t;
+          }
+        }
+      }
+    }
+  }
+  if (p.epi == EPI_ARGMAX && wk == 0) {
+    float v = best_v;
+    int i = best_i;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+      if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+    }
+    if (lane == 0 && i != 0x7fffffff) {
+      const unsigned long long key = ((unsigned long long)float_ordered(v) << 32) |
+                                     (unsigned long long)(0xffffffffu - (uint32_t)i);
+      atomicMax(&p.argmax[0], key);
+    }
+  }
+}
+
+}  // namespace inf
