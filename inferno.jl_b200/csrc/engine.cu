@@ -72,6 +72,9 @@ struct LayerBind {
             *beta = nullptr, *ssm_a = nullptr, *dt_bias = nullptr, *ssm_norm = nullptr;
   DevTensor *wq = nullptr, *wk = nullptr, *wv = nullptr, *wo = nullptr, *q_norm = nullptr, *k_norm = nullptr;
   DevTensor *ffn_gate = nullptr, *ffn_up = nullptr, *ffn_down = nullptr;
+  // MoE FFN (config 5): router, routed experts, optional shared expert
+  DevTensor *router = nullptr, *exp_gate = nullptr, *exp_up = nullptr, *exp_down = nullptr;
+  DevTensor *sh_gate = nullptr, *sh_up = nullptr, *sh_down = nullptr;
   float* ring = nullptr;
   float* S = nullptr;
   int* step = nullptr;
@@ -96,6 +99,9 @@ struct InfernoEngine {
         *o = nullptr, *h = nullptr, *logits = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr, *part_o = nullptr, *part_ml = nullptr, *hidden = nullptr;
   int* att_counters = nullptr;
+  // MoE scratch: router logits, selected ids / weights, expert hidden, expert outputs
+  float *moe_logits = nullptr, *moe_w = nullptr, *moe_h = nullptr, *moe_y = nullptr;
+  int* moe_idx = nullptr;
   inf::Ctl* ctl = nullptr;
   int *prompt = nullptr, *out_tokens = nullptr;
   int max_out = 0;
@@ -198,6 +204,71 @@ int gemv(InfernoEngine* e, int type, int inner, std::initializer_list<GemvMat> m
 
 GemvMat M(DevTensor* t, float* y) { return GemvMat{t->d, y, (int)t->rows()}; }
 
+// MoE FFN of one layer (src/Model.jl:478-561 routing, SwiGLU experts):
+// router GEMV -> softmax/top-k -> routed gate/up (experts gathered through the
+// device ids) -> shared gate/up -> one down GEMV over every selected expert,
+// each with its own input slice -> weighted combine into x.
+int enqueue_moe(InfernoEngine* e, LayerBind& L, bool pdl) {
+  const InfernoConfig& c = e->cfg;
+  const int H = c.hidden_size, E = c.n_experts, K = c.n_experts_used, Ie = c.expert_ffn;
+  const bool shared = L.sh_gate != nullptr;
+  const float* pn = (const float*)L.post_norm->d;
+  int rc;
+  if ((rc = gemv(e, L.router->type, H, {M(L.router, e->moe_logits)}, e->x, PRO_RMSNORM, pn, nullptr, 0, EPI_STORE,
+                 nullptr, pdl)))
+    return rc;
+  if ((rc = launch_moe_topk(e->moe_logits, E, K, e->moe_idx, e->moe_w, e->err, e->st, pdl))) return rc;
+  mark(e, K_GEMV);
+  {
+    GemvCall g;
+    g.type = L.exp_gate->type;
+    g.inner = H;
+    g.mats[0] = GemvMat{L.exp_gate->d, e->moe_h, K * Ie, 1, 0};
+    g.mats[1] = GemvMat{L.exp_up->d, nullptr, K * Ie, 1, 0};
+    g.nmats = 2;
+    g.x = e->x;
+    g.x_stride = H;
+    g.pro = PRO_RMSNORM;
+    g.pro_w = pn;
+    g.eps = c.rms_eps;
+    g.epi = EPI_SWIGLU;
+    g.err = e->err;
+    g.eidx = e->moe_idx;
+    g.estride = (long long)(L.exp_gate->bytes / E);
+    g.erows = Ie;
+    g.n_experts = E;
+    if ((rc = launch_gemv(g, e->st, pdl))) return rc;
+    mark(e, K_GEMV);
+  }
+  if (shared && (rc = gemv(e, L.sh_gate->type, H, {M(L.sh_gate, e->moe_h + (size_t)K * Ie), M(L.sh_up, nullptr)}, e->x,
+                           PRO_RMSNORM, pn, nullptr, 0, EPI_SWIGLU, nullptr, pdl)))
+    return rc;
+  {
+    GemvCall g;
+    g.type = L.exp_down->type;
+    g.inner = Ie;
+    g.mats[0] = GemvMat{L.exp_down->d, e->moe_y, K * H, 1, 0};
+    g.nmats = 1;
+    if (shared) g.mats[g.nmats++] = GemvMat{L.sh_down->d, e->moe_y + (size_t)K * H, H, 0, K};
+    g.x = e->moe_h;
+    g.x_stride = Ie;
+    g.nxv = K + (shared ? 1 : 0);
+    g.pro = PRO_NONE;
+    g.eps = c.rms_eps;
+    g.epi = EPI_STORE;
+    g.err = e->err;
+    g.eidx = e->moe_idx;
+    g.estride = (long long)(L.exp_down->bytes / E);
+    g.erows = H;
+    g.n_experts = E;
+    if ((rc = launch_gemv(g, e->st, pdl))) return rc;
+    mark(e, K_GEMV);
+  }
+  if ((rc = launch_moe_combine(e->x, e->moe_y, e->moe_w, K, H, shared ? 1 : 0, e->st, pdl))) return rc;
+  mark(e, K_GEMV);
+  return 0;
+}
+
 int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
   LayerBind& L = e->layers[li];
   const InfernoConfig& c = e->cfg;
@@ -289,6 +360,12 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     if (!(ab & 8) && (rc = gemv(e, L.wo->type, c.n_heads * c.head_dim, {M(L.wo, e->x)}, e->o, PRO_NONE, nullptr, nullptr, 0,
                    EPI_ADD, nullptr, pdl)))
       return rc;
+  }
+  if (c.n_experts) {
+    if ((rc = enqueue_moe(e, L, pdl))) return rc;
+    if (e->dump)
+      INF_CUDA_TRY(cudaMemcpyAsync(e->hidden + (size_t)li * H, e->x, (size_t)H * 4, cudaMemcpyDeviceToDevice, e->st));
+    return 0;
   }
   // FFN: SwiGLU(gate, up) on RMSNorm(x), then down with residual add
   if (L.ffn_gate->type == L.ffn_up->type) {
@@ -425,6 +502,11 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
   if (c.max_ctx <= 0) return set_error(INFERNO_EINVAL, "engine_create: max_ctx must be positive");
   if (c.max_batch > 1) return set_error(INFERNO_EINVAL, "engine_create: max_batch > 1 is not supported yet");
   if (c.tp_size > 1) return set_error(INFERNO_EINVAL, "engine_create: tensor parallel needs the TP build");
+  if (c.n_experts && (c.n_experts > 1024 || c.n_experts_used <= 0 || c.n_experts_used > 16 ||
+                      c.n_experts_used > c.n_experts || c.expert_ffn <= 0 || c.expert_ffn % 256 ||
+                      c.n_experts_used + 1 > 16))
+    return set_error(INFERNO_EINVAL, "engine_create: MoE needs <= 1024 experts, top-k in [1, 15] and an expert "
+                                     "width that is a multiple of 256");
   auto* e = new InfernoEngine();
   e->cfg = c;
   e->dev = c.device;
@@ -528,7 +610,30 @@ int inferno_engine_finalize(InfernoEngine* e) {
       size_t kv = (size_t)c.max_ctx * c.n_kv_heads * c.head_dim;
       if ((rc = dalloc(e, &L.kc, kv, true)) || (rc = dalloc(e, &L.vc, kv, true))) return rc;
     }
-    if (c.n_experts) return set_error(INFERNO_EINVAL, "MoE layers need the MoE build");
+    if (c.n_experts) {
+      const int E = c.n_experts, Ie = c.expert_ffn;
+      if ((rc = require(e, p + "ffn_gate_inp.weight", &L.router, T_F32)) ||
+          (rc = require(e, p + "ffn_gate_exps.weight", &L.exp_gate)) ||
+          (rc = require(e, p + "ffn_up_exps.weight", &L.exp_up)) ||
+          (rc = require(e, p + "ffn_down_exps.weight", &L.exp_down)))
+        return rc;
+      if (L.router->rows() != E || L.router->ne[0] != c.hidden_size || L.exp_gate->ne[0] != c.hidden_size ||
+          L.exp_gate->ne[1] != Ie || L.exp_gate->ne[2] != E || L.exp_up->type != L.exp_gate->type ||
+          L.exp_up->ne[1] != Ie || L.exp_up->ne[2] != E || L.exp_down->ne[0] != Ie ||
+          L.exp_down->ne[1] != c.hidden_size || L.exp_down->ne[2] != E)
+        return set_error(INFERNO_EINVAL, "layer %d: MoE tensor dims do not match the config", i);
+      L.sh_gate = find(e, p + "ffn_gate_shexp.weight");
+      if (L.sh_gate) {
+        if ((rc = require(e, p + "ffn_up_shexp.weight", &L.sh_up)) ||
+            (rc = require(e, p + "ffn_down_shexp.weight", &L.sh_down)))
+          return rc;
+        if (L.sh_gate->rows() != Ie || L.sh_down->ne[0] != Ie || L.sh_down->type != L.exp_down->type ||
+            L.sh_up->type != L.sh_gate->type)
+          return set_error(INFERNO_EINVAL,
+                           "layer %d: the shared expert must have the routed experts' width and down type", i);
+      }
+      continue;
+    }
     if ((rc = require(e, p + "ffn_gate.weight", &L.ffn_gate)) || (rc = require(e, p + "ffn_up.weight", &L.ffn_up)) ||
         (rc = require(e, p + "ffn_down.weight", &L.ffn_down)))
       return rc;
@@ -540,11 +645,19 @@ int inferno_engine_finalize(InfernoEngine* e) {
       (rc = dalloc(e, &e->y, e->di)) || (rc = dalloc(e, &e->qg, (size_t)2 * c.n_heads * c.head_dim)) ||
       (rc = dalloc(e, &e->k, (size_t)c.n_kv_heads * c.head_dim)) ||
       (rc = dalloc(e, &e->v, (size_t)c.n_kv_heads * c.head_dim)) ||
-      (rc = dalloc(e, &e->o, (size_t)c.n_heads * c.head_dim)) || (rc = dalloc(e, &e->h, c.intermediate_size)) ||
+      (rc = dalloc(e, &e->o, (size_t)c.n_heads * c.head_dim)) ||
+      (rc = dalloc(e, &e->h, std::max(1, c.intermediate_size))) ||
       (rc = dalloc(e, &e->logits, c.vocab_size)) || (rc = dalloc(e, &e->hidden, (size_t)c.num_layers * H)) ||
       (rc = dalloc(e, &e->ctl, 1)) || (rc = dalloc(e, &e->prompt, c.max_ctx + 8)) ||
       (rc = dalloc(e, &e->out_tokens, c.max_ctx + 8)) || (rc = dalloc(e, &e->err, 1)))
     return rc;
+  if (c.n_experts) {
+    const int K = c.n_experts_used;
+    if ((rc = dalloc(e, &e->moe_logits, c.n_experts)) || (rc = dalloc(e, &e->moe_idx, K + 1)) ||
+        (rc = dalloc(e, &e->moe_w, K + 1)) || (rc = dalloc(e, &e->moe_h, (size_t)(K + 1) * c.expert_ffn)) ||
+        (rc = dalloc(e, &e->moe_y, (size_t)(K + 1) * H)))
+      return rc;
+  }
   e->max_out = c.max_ctx + 8;
   // attention splits: multiples of 32 positions, at most 128 splits
   e->split_len = 32;
@@ -566,7 +679,7 @@ int inferno_engine_finalize(InfernoEngine* e) {
     const char* pe = getenv("INFERNO_B200_PERSISTENT");
     // opt-in: the per-stage grid barrier currently costs more than PDL-chained
     // graph launches (0.96 vs 0.72 ms/token on qwen35-0.8b)
-    e->persistent = !e->dump && (pe && atoi(pe) != 0) && (e->embd->type == T_Q6_K || e->embd->type == T_Q4_K ||
+    e->persistent = !e->dump && !c.n_experts && (pe && atoi(pe) != 0) && (e->embd->type == T_Q6_K || e->embd->type == T_Q4_K ||
                                                             e->embd->type == T_Q8_0 || e->embd->type == T_F32);
     if (e->persistent && (rc = build_persistent(e))) return rc;
   }

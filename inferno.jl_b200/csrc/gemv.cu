@@ -96,8 +96,11 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
   const int nsb = c.inner / 256;
   const long long row_bytes = (long long)nsb * bb;
   const size_t smem_cap = 220 * 1024;
-  const size_t fixed = 16 * GEMV_MAX_STAGES + (2 * NW + 4) * 4 + NW * 16 * 4 + (size_t)nsb * 16 * 4 +
-                       (size_t)c.inner * 4 + (size_t)nsb * 8 * MMA_KS_BYTES + 128;
+  const int nxv = c.nxv;
+  const size_t fixed = 16 * GEMV_MAX_STAGES + (2 * NW + 4 + 16) * 4 + NW * 16 * 4 +
+                       (size_t)nxv * ((size_t)nsb * 16 * 4 + (size_t)c.inner * 4 + (size_t)nsb * 8 * MMA_KS_BYTES) + 128;
+  bool any_indirect = false;
+  for (int i = 0; i < c.nmats; ++i) any_indirect |= c.mats[i].indirect != 0;
   auto stage_of = [&](int TR) -> size_t {
     if (paired) return 2 * (((size_t)(TR / 2) * row_bytes + 32 + 15) / 16 * 16) + 128;
     return ((size_t)TR * row_bytes + 48 + 127) / 128 * 128;
@@ -110,6 +113,7 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
     const int nrg = TR / 16, nkg = NW / nrg;
     if (fixed + 2 * stage_of(TR) > smem_cap) continue;
     const int eff = paired ? TR / 2 : TR;
+    if ((any_indirect || nxv > 1) && c.erows % eff) continue;   // a tile stays inside one expert / slot
     long long tiles = 0;
     for (int i = 0; i < (paired ? 1 : c.nmats); ++i) tiles += (c.mats[i].rows + eff - 1) / eff;
     const long long waves = (tiles + sms - 1) / sms;
@@ -124,6 +128,8 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
     p.seg[i].W = (const uint8_t*)c.mats[i].W;
     p.seg[i].y = c.mats[i].y;
     p.seg[i].rows = c.mats[i].rows;
+    p.seg[i].indirect = c.mats[i].indirect;
+    p.seg[i].xslot0 = c.mats[i].xslot0;
     if (paired && i == 1) p.seg[i].tile0 = INT_MAX;
     else {
       p.seg[i].tile0 = ntiles;
@@ -134,6 +140,11 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
   p.ntiles = ntiles;
   p.inner = c.inner;
   p.row_bytes = (int)row_bytes;
+  p.eidx = c.eidx;
+  p.estride = c.estride;
+  p.erows = c.erows;
+  p.n_experts = c.n_experts;
+  p.nxv = nxv;
   p.nkc = (c.inner + GEMV_CHUNK - 1) / GEMV_CHUNK;
   p.TR = TR;
   p.nkg = NW / (TR / 16);
@@ -186,11 +197,18 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
   int dev = 0;
   cudaGetDevice(&dev);
   const int sms = num_sms(dev);
+  bool any_indirect = false;
+  for (int i = 0; i < c.nmats; ++i) any_indirect |= c.mats[i].indirect != 0;
+  if (c.nxv < 1 || (c.nxv > 1 && (c.pro != PRO_NONE || c.erows <= 0 || c.nxv > 16)) ||
+      (any_indirect && (!c.eidx || c.erows <= 0 || c.n_experts <= 0 || c.estride <= 0)))
+    return set_error(-1, "gemv: bad expert / multi-vector arguments");
   static const bool no_mma = getenv("INFERNO_GEMV_NO_MMA") != nullptr;
-  if (!no_mma && !c.force_r && c.nb == 1 && (c.type == T_Q4_K || c.type == T_Q6_K) && c.inner % 256 == 0) {
+  const bool mma_ok = !c.force_r && c.nb == 1 && (c.type == T_Q4_K || c.type == T_Q6_K) && c.inner % 256 == 0;
+  if (mma_ok && (!no_mma || c.nxv > 1)) {
     const int rc = plan_launch_mma(c, dev, sms, st, pdl);
     if (rc <= 0) return rc;
   }
+  if (c.nxv > 1) return set_error(-1, "gemv: several input vectors need single-column Q4_K/Q6_K");
   const long long row_bytes = (long long)c.inner / qk * bb;
   const int nkc = (c.inner + GEMV_CHUNK - 1) / GEMV_CHUNK;
   long long wbytes = 0;
@@ -239,6 +257,7 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
       const size_t stg = stage_of(TR);
       if (fixed + xbytes(1) + 2 * stg > smem_cap) continue;
       const int eff = paired ? TR / 2 : TR;
+      if (any_indirect && c.erows % eff) continue;   // a tile stays inside one expert
       long long tiles = 0;
       for (int i = 0; i < (paired ? 1 : c.nmats); ++i) tiles += (c.mats[i].rows + eff - 1) / eff;
       const long long waves = (tiles + sms - 1) / sms;
@@ -256,6 +275,8 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
     p.seg[i].W = (const uint8_t*)c.mats[i].W;
     p.seg[i].y = c.mats[i].y;
     p.seg[i].rows = c.mats[i].rows;
+    p.seg[i].indirect = c.mats[i].indirect;
+    p.seg[i].xslot0 = 0;
     if (paired && i == 1) {
       p.seg[i].tile0 = INT_MAX;
     } else {
@@ -267,6 +288,11 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
   p.ntiles = ntiles;
   p.inner = c.inner;
   p.row_bytes = (int)row_bytes;
+  p.eidx = c.eidx;
+  p.estride = c.estride;
+  p.erows = c.erows;
+  p.n_experts = c.n_experts;
+  p.nxv = 1;
   p.nkc = nkc;
   p.TR = TR;
   p.nkg = best_g;

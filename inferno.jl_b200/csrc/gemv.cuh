@@ -45,6 +45,8 @@ struct GemvSeg {
   float* y;           // output rows (EPI_SWIGLU: only seg[0].y is used)
   int rows;
   int tile0;          // first global tile index of this segment
+  int indirect;       // rows gathered through GemvParams::eidx (MoE experts)
+  int xslot0;         // input-vector slot of row 0 (nxv > 1)
 };
 
 struct GemvParams {
@@ -68,6 +70,11 @@ struct GemvParams {
   unsigned long long* argmax;     // [nb] packed (ordered value, ~index)
   int* err;
   int l2_evict_first;             // stream weights with an L2 evict_first policy
+  const int* eidx;                // MoE: expert id per erows-row block of an indirect segment
+  long long estride;              // bytes between experts
+  int erows;                      // rows per expert block (also the input-slot period)
+  int n_experts;                  // valid ids are [0, n_experts)
+  int nxv;                        // input vectors (tensor-core path, PRO_NONE)
   unsigned long long* trace;      // debug: phase timestamps of CTA 0 / last CTA (null = off)
 };
 
@@ -470,6 +477,21 @@ __device__ __forceinline__ void tile_locate(const GemvParams& p, int tile, int& 
   row0 = (tile - p.seg[seg].tile0) * half;
 }
 
+// Address of row `row0` of segment `sg`.  Indirect (MoE) segments map row r to
+// row r % erows of expert eidx[r / erows]; a tile never straddles two experts.
+// An out-of-range id is reported and replaced by expert 0.
+__device__ __forceinline__ const uint8_t* seg_row_ptr(const GemvParams& p, int sg, int row0) {
+  const GemvSeg& s = p.seg[sg];
+  if (!s.indirect) return s.W + (long long)row0 * p.row_bytes;
+  const int slot = row0 / p.erows;
+  int e = p.eidx[slot];
+  if (e < 0 || e >= p.n_experts) {
+    if (p.err) atomicExch(p.err, DERR_BAD_ARG);
+    e = 0;
+  }
+  return s.W + (long long)e * p.estride + (long long)(row0 - slot * p.erows) * p.row_bytes;
+}
+
 // Producer warp of the GEMV kernels: one bulk copy per tile (two for paired
 // gate/up tiles) into the ring of stages.  Weights stream before
 // griddepcontrol.wait; dependents are released only after it.
@@ -479,6 +501,12 @@ __device__ __forceinline__ void gemv_producer(const GemvParams& p, uint64_t* ful
   const bool paired = (p.epi == EPI_SWIGLU);
   const int TR = p.TR, half_tr = TR / 2;
   bool waited = false;
+  if (p.eidx) {
+    // expert ids come from the preceding kernel: no weight prefetch before the wait
+    pdl_wait();
+    pdl_trigger();
+    waited = true;
+  }
   for (int it = 0; it < n_items; ++it) {
     const int s = it % p.stages;
     if (it >= p.stages) {
@@ -493,7 +521,7 @@ __device__ __forceinline__ void gemv_producer(const GemvParams& p, uint64_t* ful
       uint32_t bytes = 0;
       uintptr_t a0 = 0;
       if (nrows > 0) {
-        const uintptr_t src = (uintptr_t)(p.seg[sgr].W + (long long)row0 * p.row_bytes);
+        const uintptr_t src = (uintptr_t)seg_row_ptr(p, sgr, row0);
         a0 = src & ~(uintptr_t)15;
         const uintptr_t a1 = (src + (long long)nrows * p.row_bytes + 15) & ~(uintptr_t)15;
         bytes = (uint32_t)(a1 - a0);
@@ -605,7 +633,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
     for (int r = 0; r < R; ++r) {
       const int sgr = paired ? (r < R / 2 ? 0 : 1) : sg;
       const int rrel = paired ? wr * (R / 2) + (r % (R >= 2 ? R / 2 : 1)) : wr * R + r;
-      const uint32_t mis = (uint32_t)((uintptr_t)(p.seg[sgr].W + (long long)row0 * p.row_bytes) & 15);
+      const uint32_t mis = (uint32_t)((uintptr_t)seg_row_ptr(p, sgr, row0) & 15);
       rp[r] = st + ((paired && sgr) ? p.part1_off : 0) + mis + (long long)rrel * p.row_bytes;
     }
     float acc[NB][R];

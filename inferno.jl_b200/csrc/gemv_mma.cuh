@@ -75,17 +75,28 @@ __device__ __forceinline__ int mma_xsum_slot(int ks, int p) {
 }
 
 // Prologue: v (RMSNorm x*w, head-norm gate, or x) into xf, then the limbs
-// into xq ([ks][8 columns][4 lanes][8 bytes]) and sub-block sums into xsum.
-// Returns the column factor (1/rms or 1) and the 2^-s descale; a non-finite
-// input makes every output NaN (as the reference's fp32 arithmetic would).
+// into xq ([vector][ks][8 columns][4 lanes][8 bytes]) and sub-block sums into
+// xsum.  vmax[v] receives max|v| of each input vector (its fixed-point scale
+// is derived from it), red[0..NW) the RMSNorm partial sums; returns the column
+// factor (1/rms or 1).  A non-finite input sets the flag red[2*NW] and makes
+// every output NaN (as the reference's fp32 arithmetic would).
+// vmax[] and the flag must be zero on entry.
+__device__ __forceinline__ int mma_exp2_scale(float vmax) {
+  int e = 0;
+  if (vmax > 0.f && vmax <= 3.0e38f) frexpf(vmax, &e);   // vmax < 2^e
+  return max(-120, min(120, 30 - e));
+}
+
 template <int TYPE, int NW>
-__device__ void gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, float* xsum, float* red, int tid,
-                                  float& colscale, float& descale) {
+__device__ float gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, float* xsum, float* red,
+                                   float* vmax, int tid) {
   const int n = p.inner;
   const int lane = tid & 31, w = tid >> 5;
   constexpr int NT = NW * 32;
+  const int nxv = p.nxv;
   const float* x = p.x;
   float ss = 0.f, amax = 0.f;
+  bool bad = false;
   if (p.pro == PRO_RMSNORM) {
     for (int i = tid; i < n; i += NT) {
       const float v = x[i];
@@ -122,6 +133,16 @@ __device__ void gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, f
         xf[hh * G + q * 32 + lane] = u;
       }
     }
+  } else if (nxv > 1) {
+    // several vectors (n % 32 == 0): a warp's 32 elements share one vector
+    for (int i = tid; i < nxv * n; i += NT) {
+      const int v = i / n;
+      const float u = x[(long long)v * p.x_stride + (i - v * n)];
+      xf[i] = u;
+      const float m = warp_max(fabsf(u));
+      if (lane == 0) atomicMax((int*)&vmax[v], __float_as_int(m));
+      if (u != u) bad = true;
+    }
   } else {
     for (int i = tid; i < n; i += NT) {
       const float u = x[i];
@@ -129,45 +150,45 @@ __device__ void gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, f
       xf[i] = u;
     }
   }
-  // NaN-propagating max: fmaxf drops NaN, so track it separately
-  ss = warp_sum(ss);
-  amax = warp_max(amax);
-  float bad = 0.f;
-  if (lane == 0) {
-    red[w] = ss;
-    red[NW + w] = amax;
+  if (nxv == 1 || p.pro != PRO_NONE) {
+    ss = warp_sum(ss);
+    amax = warp_max(amax);      // fmaxf drops NaN: NaN is caught per element below
+    if (lane == 0) {
+      red[w] = ss;
+      atomicMax((int*)&vmax[0], __float_as_int(amax));
+    }
   }
-  if (tid == 0) *(volatile int*)&red[2 * NW] = 0;   // non-finite input flag
   named_bar_sync(1, NT);
-  float tss = 0.f, tmax = 0.f;
+  float colscale = 1.0f;
+  if (p.pro == PRO_RMSNORM) {
+    float tss = 0.f;
 #pragma unroll
-  for (int i = 0; i < NW; ++i) {
-    tss += red[i];
-    tmax = fmaxf(tmax, red[NW + i]);
+    for (int i = 0; i < NW; ++i) tss += red[i];
+    colscale = 1.0f / sqrtf(tss / (float)n + p.eps);
   }
-  colscale = (p.pro == PRO_RMSNORM) ? 1.0f / sqrtf(tss / (float)n + p.eps) : 1.0f;
-  int e = 0;
-  if (tmax > 0.f && tmax <= 3.0e38f) frexpf(tmax, &e);   // tmax < 2^e
-  else if (!(tmax == 0.f)) bad = 1.f;                     // inf (NaN is caught per element below)
-  const int s = max(-120, min(120, 30 - e));
-  const float up = ldexpf(1.0f, s);
-  descale = ldexpf(1.0f, -s);
 
   // limbs: one thread per quad (ks, cc) = 4 elements of each k-half
-  const int nq = n >> 3;
-  for (int q = tid; q < nq; q += NT) {
+  const int nqv = n >> 3;
+  const size_t xq_vec = (size_t)(n >> 8) * 8 * MMA_KS_BYTES;
+  for (int qq = tid; qq < nxv * nqv; qq += NT) {
+    const int v = qq / nqv, q = qq - v * nqv;
+    const float vm = vmax[v];
+    if (!(vm <= 3.0e38f)) bad = true;
+    const float up = ldexpf(1.0f, mma_exp2_scale(vm));
     const int ks = q >> 2, cc = q & 3;
+    const float* xfv = xf + (size_t)v * n;
+    uint8_t* xqv = xq + v * xq_vec;
     float part[2];
 #pragma unroll
     for (int hp = 0; hp < 2; ++hp) {
       const int e0 = mma_elem<TYPE>(ks, cc, hp);
-      const float4 v4 = *(const float4*)&xf[e0];
+      const float4 v4 = *(const float4*)&xfv[e0];
       const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
       uint32_t limb[4] = {0u, 0u, 0u, 0u};
       float sum = 0.f;
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        if (vv[t] != vv[t]) bad = 1.f;
+        if (vv[t] != vv[t]) bad = true;
         int xi = __float2int_rn(vv[t] * up);
         sum += (float)xi;
 #pragma unroll
@@ -181,7 +202,7 @@ __device__ void gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, f
 #pragma unroll
       for (int l = 0; l < 4; ++l) {
         uint2 v2 = hp == 0 ? make_uint2(limb[l], 0u) : make_uint2(0u, limb[l]);
-        *(uint2*)(xq + (size_t)ks * MMA_KS_BYTES + (2 * l + hp) * 32 + cc * 8) = v2;
+        *(uint2*)(xqv + (size_t)ks * MMA_KS_BYTES + (2 * l + hp) * 32 + cc * 8) = v2;
       }
       part[hp] = sum;
     }
@@ -193,13 +214,14 @@ __device__ void gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, f
       if (TYPE == T_Q4_K) part[hp] += __shfl_xor_sync(0xffffffffu, part[hp], 4);
     }
     if ((q & (TYPE == T_Q4_K ? 7 : 3)) == 0) {
-      xsum[mma_xsum_slot<TYPE>(ks, 0)] = part[0];
-      xsum[mma_xsum_slot<TYPE>(ks, 1)] = part[1];
+      float* xs = xsum + (size_t)v * (n >> 8) * 16;
+      xs[mma_xsum_slot<TYPE>(ks, 0)] = part[0];
+      xs[mma_xsum_slot<TYPE>(ks, 1)] = part[1];
     }
   }
-  if (bad != 0.f) *(volatile int*)&red[2 * NW] = 1;
+  if (bad) *(volatile int*)&red[2 * NW] = 1;
   named_bar_sync(1, NT);   // also the barrier before the tiles
-  if (*(volatile int*)&red[2 * NW]) descale = __int_as_float(0x7fc00000);
+  return colscale;
 }
 
 // ---------------------------------------------------------------------------
@@ -308,16 +330,19 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int BB = TYPE == T_Q4_K ? 144 : 210;
   constexpr int XS_PER_SB = TYPE == T_Q4_K ? 8 : 16;
-  // layout: [full][empty][red 2*NW+4][kpart NW*16][xsum][xf][xq][stages]
+  // layout: [full][empty][red 2*NW+4][vmax 16][kpart NW*16][xsum][xf][xq][stages]
   uint64_t* full = (uint64_t*)smem;
   uint64_t* empty = full + GEMV_MAX_STAGES;
   float* red = (float*)(empty + GEMV_MAX_STAGES);
-  float* kpart = red + 2 * NW + 4;
+  float* vmax = red + 2 * NW + 4;
+  float* kpart = vmax + 16;
   float* xsum = kpart + NW * 16;
   const int nsb = p.inner >> 8;
-  float* xf = xsum + nsb * 16;
-  uint8_t* xq = (uint8_t*)(xf + p.inner);
-  uint8_t* stage0 = (uint8_t*)(((uintptr_t)(xq + (size_t)nsb * 8 * MMA_KS_BYTES) + 127) & ~(uintptr_t)127);
+  const int nxv = p.nxv;
+  float* xf = xsum + nxv * nsb * 16;
+  uint8_t* xq = (uint8_t*)(xf + (size_t)nxv * p.inner);
+  const size_t xq_vec = (size_t)nsb * 8 * MMA_KS_BYTES;
+  uint8_t* stage0 = (uint8_t*)(((uintptr_t)(xq + nxv * xq_vec) + 127) & ~(uintptr_t)127);
 
   if (tid == 0) {
     for (int s = 0; s < p.stages; ++s) {
@@ -325,7 +350,9 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
       mbar_init(&empty[s], NW);
     }
     fence_mbar_init();
+    *(volatile int*)&red[2 * NW] = 0;   // non-finite input flag
   }
+  if (tid < 16) vmax[tid] = 0.f;
   __syncthreads();
   const int G = gridDim.x;
   const int n_items = (p.ntiles - (int)blockIdx.x + G - 1) / G;
@@ -335,9 +362,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
   }
 
   pdl_wait();
-  float colscale, descale;
-  gemv_mma_prologue<TYPE, NW>(p, xf, xq, xsum, red, tid, colscale, descale);
-  const float fscale = colscale * descale;
+  const float colscale = gemv_mma_prologue<TYPE, NW>(p, xf, xq, xsum, red, vmax, tid);
+  const bool nonfinite = *(volatile int*)&red[2 * NW] != 0;
 
   const bool paired = (p.epi == EPI_SWIGLU);
   const int nrg = p.TR >> 4;            // 16-row groups per tile
@@ -356,23 +382,29 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
     const uint8_t* st = stage0 + (long long)s * p.stage_bytes;
     const uint8_t *ra, *rb;
     if (paired) {
-      const uint32_t m0 = (uint32_t)((uintptr_t)(p.seg[0].W + (long long)row0 * p.row_bytes) & 15);
-      const uint32_t m1 = (uint32_t)((uintptr_t)(p.seg[1].W + (long long)row0 * p.row_bytes) & 15);
+      const uint32_t m0 = (uint32_t)((uintptr_t)seg_row_ptr(p, 0, row0) & 15);
+      const uint32_t m1 = (uint32_t)((uintptr_t)seg_row_ptr(p, 1, row0) & 15);
       ra = st + m0 + (long long)(rg * 8 + g) * p.row_bytes;
       rb = st + p.part1_off + m1 + (long long)(rg * 8 + g) * p.row_bytes;
     } else {
-      const uint32_t m0 = (uint32_t)((uintptr_t)(p.seg[sg].W + (long long)row0 * p.row_bytes) & 15);
+      const uint32_t m0 = (uint32_t)((uintptr_t)seg_row_ptr(p, sg, row0) & 15);
       ra = st + m0 + (long long)(rg * 16 + g) * p.row_bytes;
       rb = ra + 8ll * p.row_bytes;
     }
+    // input vector of this tile and its fixed-point descale
+    const int slot = nxv > 1 ? p.seg[sg].xslot0 + row0 / p.erows : 0;
+    const uint8_t* xq_t = xq + slot * xq_vec;
+    const float* xsum_t = xsum + slot * nsb * 16;
+    const float fscale = nonfinite ? __int_as_float(0x7fc00000)
+                                   : colscale * ldexpf(1.0f, -mma_exp2_scale(vmax[slot]));
     float acc[2] = {0.f, 0.f}, corr[2] = {0.f, 0.f};
     for (int sb = wk; sb < nsb; sb += nkg) {
       if constexpr (TYPE == T_Q4_K)
-        mma_sb_q4k(ra + sb * BB, rb + sb * BB, xq + (size_t)sb * 8 * MMA_KS_BYTES, xsum + sb * XS_PER_SB, lane, acc,
-                   corr);
+        mma_sb_q4k(ra + sb * BB, rb + sb * BB, xq_t + (size_t)sb * 8 * MMA_KS_BYTES, xsum_t + sb * XS_PER_SB, lane,
+                   acc, corr);
       else
-        mma_sb_q6k(ra + sb * BB, rb + sb * BB, xq + (size_t)sb * 8 * MMA_KS_BYTES, xsum + sb * XS_PER_SB, lane, acc,
-                   corr);
+        mma_sb_q6k(ra + sb * BB, rb + sb * BB, xq_t + (size_t)sb * 8 * MMA_KS_BYTES, xsum_t + sb * XS_PER_SB, lane,
+                   acc, corr);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);

@@ -25,6 +25,8 @@ struct GemvMat {
   const void* W;   // device, 16-byte aligned
   float* y;        // device output rows
   int rows;
+  int indirect = 0;   // rows gathered through GemvCall::eidx (MoE experts)
+  int xslot0 = 0;     // input-vector slot of the first row (GemvCall::nxv > 1)
 };
 
 struct GemvCall {
@@ -45,11 +47,23 @@ struct GemvCall {
   unsigned long long* argmax = nullptr;
   int* err = nullptr;
   int force_r = 0;            // 0 = planner's choice
+  // MoE: for an `indirect` matrix, row r is row (r % erows) of expert
+  // eidx[r / erows] (device ids), experts `estride` bytes apart
+  const int* eidx = nullptr;
+  long long estride = 0;
+  int erows = 0;
+  int n_experts = 0;
+  // several input vectors (x + v * x_stride, v < nxv): rows use vector
+  // xslot0 + r / erows (single-column tensor-core path, PRO_NONE only)
+  int nxv = 1;
   unsigned long long* trace = nullptr;   // debug phase timestamps (32 slots)
 };
 
 int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl);
 int launch_dequant(int type, const void* src, long long n, float* dst, cudaStream_t st);
+int launch_moe_topk(const float* logits, int E, int K, int* idx, float* wts, int* err, cudaStream_t st, bool pdl);
+int launch_moe_combine(float* x, const float* y, const float* wts, int K, int H, int shared, cudaStream_t st,
+                       bool pdl);
 int launch_embed_row(int type, const void* W, long long row_bytes, int inner, const int* row_ptr, float* dst,
                      int vocab, cudaStream_t st, bool pdl);
 
