@@ -218,6 +218,16 @@ int inferno_debug_trace(InfernoEngine* eng, unsigned long long* out, int n);
 /* Device time of the last inferno_decode_greedy call in ms (CUDA events). */
 float inferno_last_decode_ms(InfernoEngine* eng);
 
+/* Tensor parallel: a fresh 128-byte NCCL unique id for InfernoConfig.
+ * nccl_unique_id (made by rank 0 and shared by the host, e.g. through
+ * torch.distributed).  Each rank then creates its engine with its rank and
+ * uploads its shard of the GGUF tensors (inferno_b200/tp.py); the engine
+ * all-reduces the residual stream after ssm_out / attn_output / ffn_down and
+ * the lm_head argmax over NCCL (NVLink).  No reference counterpart: the
+ * reference has no multi-GPU path for this model family. */
+#define INFERNO_TP_UNIQUE_ID_BYTES 128
+int inferno_tp_unique_id(void* out, int nbytes);
+
 int inferno_engine_destroy(InfernoEngine* eng);
 
 #ifdef __cplusplus

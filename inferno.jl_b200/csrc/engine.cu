@@ -24,6 +24,7 @@
 #include <memory>
 #include <string>
 #include <vector>
+#include <nccl.h>
 #include "internal.h"
 #include "gemv.cuh"
 #include "params.h"
@@ -92,6 +93,11 @@ struct InfernoEngine {
   std::map<std::string, inf::DevTensor> tensors;
   std::vector<inf::LayerBind> layers;
   inf::DevTensor *embd = nullptr, *out_norm = nullptr, *lm_head = nullptr;
+  // tensor parallel: rank `tp_rank` of `tp_size` owns a slice of every layer
+  // (sharded by the host) and rows [tp_rank*V/tp, ...) of the lm_head
+  ncclComm_t comm = nullptr;
+  inf::DevTensor lm_view;
+  float* logits_local = nullptr;
   bool finalized = false;
   int C = 0, di = 0, rd = 0, split_len = 64, nsplit = 1;
   // activations
@@ -204,6 +210,18 @@ int gemv(InfernoEngine* e, int type, int inner, std::initializer_list<GemvMat> m
 
 GemvMat M(DevTensor* t, float* y) { return GemvMat{t->d, y, (int)t->rows()}; }
 
+// Residual epilogue of a sublayer's last GEMV.  Tensor parallel: rank 0 adds
+// its partial to x, the other ranks store theirs, and one all-reduce (sum) of
+// x completes x + sum_r partial_r on every rank.
+int residual_epi(InfernoEngine* e) { return (e->cfg.tp_size > 1 && e->cfg.tp_rank != 0) ? EPI_STORE : EPI_ADD; }
+
+int tp_sum_x(InfernoEngine* e) {
+  if (e->cfg.tp_size <= 1) return 0;
+  ncclResult_t r = ncclAllReduce(e->x, e->x, (size_t)e->cfg.hidden_size, ncclFloat, ncclSum, e->comm, e->st);
+  if (r != ncclSuccess) return set_error(INFERNO_ENCCL, "all-reduce of the residual: %s", ncclGetErrorString(r));
+  return 0;
+}
+
 // MoE FFN of one layer (src/Model.jl:478-561 routing, SwiGLU experts):
 // router GEMV -> softmax/top-k -> routed gate/up (experts gathered through the
 // device ids) -> shared gate/up -> one down GEMV over every selected expert,
@@ -314,8 +332,9 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     if (!(ab & 2) && (rc = launch_gdn_step(g, e->st, pdl))) return rc;
     mark(e, K_GDN);
     if (!(ab & 8) && (rc = gemv(e, L.ssm_out->type, e->di, {M(L.ssm_out, e->x)}, e->y, (ab & 128) ? PRO_NONE : PRO_HEADNORM_GATE,
-                   (const float*)L.ssm_norm->d, e->z, c.ssm_dv, EPI_ADD, nullptr, pdl)))
+                   (const float*)L.ssm_norm->d, e->z, c.ssm_dv, residual_epi(e), nullptr, pdl)))
       return rc;
+    if ((rc = tp_sum_x(e))) return rc;
   } else {
     const int qrows = (int)L.wq->rows();
     (void)qrows;
@@ -358,8 +377,9 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     if (!(ab & 4) && (rc = launch_attn_decode(a, e->st, pdl))) return rc;
     mark(e, K_ATTN);
     if (!(ab & 8) && (rc = gemv(e, L.wo->type, c.n_heads * c.head_dim, {M(L.wo, e->x)}, e->o, PRO_NONE, nullptr, nullptr, 0,
-                   EPI_ADD, nullptr, pdl)))
+                   residual_epi(e), nullptr, pdl)))
       return rc;
+    if ((rc = tp_sum_x(e))) return rc;
   }
   if (c.n_experts) {
     if ((rc = enqueue_moe(e, L, pdl))) return rc;
@@ -376,8 +396,9 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     return set_error(INFERNO_EINVAL, "layer %d: ffn_gate and ffn_up must share a type", li);
   }
   if (!(ab & 32) && (rc = gemv(e, L.ffn_down->type, c.intermediate_size, {M(L.ffn_down, e->x)}, e->h, PRO_NONE, nullptr, nullptr,
-                 0, EPI_ADD, nullptr, pdl)))
+                 0, residual_epi(e), nullptr, pdl)))
     return rc;
+  if ((rc = tp_sum_x(e))) return rc;
   if (e->dump)
     INF_CUDA_TRY(cudaMemcpyAsync(e->hidden + (size_t)li * H, e->x, (size_t)H * 4, cudaMemcpyDeviceToDevice, e->st));
   return 0;
@@ -411,6 +432,31 @@ int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
   mark(e, K_EMBED);
   for (int i = 0; i < c.num_layers; ++i)
     if ((rc = enqueue_layer(e, i, pdl))) return rc;
+  if (c.tp_size > 1) {
+    // vocab-split lm_head: local rows, global first-max through a u64 max
+    // all-reduce of the packed (ordered value, ~index) keys
+    GemvCall g;
+    g.type = e->lm_head->type;
+    g.inner = c.hidden_size;
+    g.mats[0] = M(e->lm_head, write_logits ? e->logits_local : nullptr);
+    g.nmats = 1;
+    g.x = e->x;
+    g.x_stride = c.hidden_size;
+    g.pro = PRO_RMSNORM;
+    g.pro_w = (const float*)e->out_norm->d;
+    g.eps = c.rms_eps;
+    g.epi = EPI_ARGMAX;
+    g.argmax = &e->ctl->argkey;
+    g.argmax_row0 = c.tp_rank * (int)e->lm_head->rows();
+    g.err = e->err;
+    if ((rc = launch_gemv(g, e->st, pdl))) return rc;
+    mark(e, K_LMHEAD);
+    ncclResult_t r = ncclAllReduce(&e->ctl->argkey, &e->ctl->argkey, 1, ncclUint64, ncclMax, e->comm, e->st);
+    if (r == ncclSuccess && write_logits)
+      r = ncclAllGather(e->logits_local, e->logits, (size_t)e->lm_head->rows(), ncclFloat, e->comm, e->st);
+    if (r != ncclSuccess) return set_error(INFERNO_ENCCL, "lm_head collectives: %s", ncclGetErrorString(r));
+    return launch_finalize(e, pdl);
+  }
   if (!(e->ablate & 64) && (rc = gemv(e, e->lm_head->type, c.hidden_size, {M(e->lm_head, write_logits ? e->logits : nullptr)}, e->x,
                  PRO_RMSNORM, (const float*)e->out_norm->d, nullptr, 0, EPI_ARGMAX, &e->ctl->argkey, pdl)))
     return rc;
@@ -501,7 +547,10 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
   if (c.ssm_nk <= 0 || c.ssm_nv % c.ssm_nk) return set_error(INFERNO_EINVAL, "engine_create: nv %% nk != 0");
   if (c.max_ctx <= 0) return set_error(INFERNO_EINVAL, "engine_create: max_ctx must be positive");
   if (c.max_batch > 1) return set_error(INFERNO_EINVAL, "engine_create: max_batch > 1 is not supported yet");
-  if (c.tp_size > 1) return set_error(INFERNO_EINVAL, "engine_create: tensor parallel needs the TP build");
+  if (c.tp_size < 1 || c.tp_rank < 0 || c.tp_rank >= c.tp_size)
+    return set_error(INFERNO_EINVAL, "engine_create: tp_rank %d / tp_size %d", c.tp_rank, c.tp_size);
+  if (c.tp_size > 1 && (!c.nccl_unique_id || c.n_experts))
+    return set_error(INFERNO_EINVAL, "engine_create: tensor parallel needs an NCCL unique id and a dense FFN");
   if (c.n_experts && (c.n_experts > 1024 || c.n_experts_used <= 0 || c.n_experts_used > 16 ||
                       c.n_experts_used > c.n_experts || c.expert_ffn <= 0 || c.expert_ffn % 256 ||
                       c.n_experts_used + 1 > 16))
@@ -520,6 +569,17 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
   }
   cudaEventCreate(&e->ev0);
   cudaEventCreate(&e->ev1);
+  if (c.tp_size > 1) {
+    ncclUniqueId id;
+    memcpy(&id, c.nccl_unique_id, sizeof id);
+    ncclResult_t r = ncclCommInitRank(&e->comm, c.tp_size, id, c.tp_rank);
+    if (r != ncclSuccess) {
+      cudaStreamDestroy(e->st);
+      delete e;
+      return set_error(INFERNO_ENCCL, "ncclCommInitRank(rank %d of %d): %s", c.tp_rank, c.tp_size,
+                       ncclGetErrorString(r));
+    }
+  }
   const char* d = getenv("INFERNO_B200_DUMP");
   e->dump = d && atoi(d) != 0;
   if (const char* ab = getenv("INFERNO_B200_ABLATE")) e->ablate = (unsigned)strtoul(ab, nullptr, 0);
@@ -567,6 +627,18 @@ int inferno_engine_finalize(InfernoEngine* e) {
   if ((rc = require(e, "output_norm.weight", &e->out_norm, T_F32))) return rc;
   e->lm_head = find(e, "output.weight");
   if (!e->lm_head) e->lm_head = e->embd;   // tied (src/LoaderCPU.jl:358-371)
+  if (c.tp_size > 1) {
+    if (c.vocab_size % c.tp_size || e->lm_head->rows() != c.vocab_size)
+      return set_error(INFERNO_EINVAL, "tensor parallel: vocab %d not divisible by %d", c.vocab_size, c.tp_size);
+    const int vl = c.vocab_size / c.tp_size;
+    const size_t rb = e->lm_head->bytes / (size_t)c.vocab_size;
+    e->lm_view = *e->lm_head;
+    e->lm_view.d = (uint8_t*)e->lm_head->d + (size_t)c.tp_rank * vl * rb;
+    e->lm_view.ne[1] = vl;
+    e->lm_view.bytes = (size_t)vl * rb;
+    e->lm_head = &e->lm_view;
+    if ((rc = dalloc(e, &e->logits_local, vl))) return rc;
+  }
   if (e->embd->ne[0] != c.hidden_size || e->embd->rows() != c.vocab_size)
     return set_error(INFERNO_EINVAL, "token_embd dims do not match hidden/vocab");
   e->di = c.ssm_nv * c.ssm_dv;
@@ -679,7 +751,7 @@ int inferno_engine_finalize(InfernoEngine* e) {
     const char* pe = getenv("INFERNO_B200_PERSISTENT");
     // opt-in: the per-stage grid barrier currently costs more than PDL-chained
     // graph launches (0.96 vs 0.72 ms/token on qwen35-0.8b)
-    e->persistent = !e->dump && !c.n_experts && (pe && atoi(pe) != 0) && (e->embd->type == T_Q6_K || e->embd->type == T_Q4_K ||
+    e->persistent = !e->dump && !c.n_experts && c.tp_size == 1 && (pe && atoi(pe) != 0) && (e->embd->type == T_Q6_K || e->embd->type == T_Q4_K ||
                                                             e->embd->type == T_Q8_0 || e->embd->type == T_F32);
     if (e->persistent && (rc = build_persistent(e))) return rc;
   }
@@ -1077,6 +1149,16 @@ int inferno_debug_trace(InfernoEngine* e, unsigned long long* out, int n) {
   return 0;
 }
 
+int inferno_tp_unique_id(void* out, int nbytes) {
+  if (!out || nbytes < (int)sizeof(ncclUniqueId))
+    return set_error(INFERNO_EINVAL, "tp_unique_id: buffer must hold %d bytes", (int)sizeof(ncclUniqueId));
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return set_error(INFERNO_ENCCL, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+  memcpy(out, &id, sizeof id);
+  return 0;
+}
+
 int inferno_engine_destroy(InfernoEngine* e) {
   if (!e) return 0;
   cudaSetDevice(e->dev);
@@ -1090,6 +1172,7 @@ int inferno_engine_destroy(InfernoEngine* e) {
   for (void* p : e->allocs) cudaFree(p);
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
+  if (e->comm) ncclCommDestroy(e->comm);
   cudaStreamDestroy(e->st);
   delete e;
   return 0;

@@ -159,6 +159,7 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
   p.pro_group = c.pro_group;
   p.epi = c.epi;
   p.argmax = c.argmax;
+  p.argmax_row0 = c.argmax_row0;
   p.err = c.err ? c.err : device_error_word(dev);
   p.trace = c.trace;
   static const bool no_hint = getenv("INFERNO_GEMV_NO_L2HINT") != nullptr;
@@ -328,6 +329,7 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
     p.pro_z = c.pro_z ? c.pro_z + (long long)done * c.x_stride : nullptr;
     for (int i = 0; i < c.nmats; ++i) p.seg[i].y = c.mats[i].y ? c.mats[i].y + (long long)done * c.y_stride : nullptr;
     p.argmax = c.argmax ? c.argmax + done : nullptr;
+    p.argmax_row0 = c.argmax_row0;
     const int grid = std::min(ntiles, sms);
     const size_t smem = need(NB);
     cudaError_t e;

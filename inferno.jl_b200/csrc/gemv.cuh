@@ -68,6 +68,7 @@ struct GemvParams {
   int pro_group;                  // head size for PRO_HEADNORM_GATE
   int epi;
   unsigned long long* argmax;     // [nb] packed (ordered value, ~index)
+  int argmax_row0;                // global index of row 0 (vocab-split lm_head)
   int* err;
   int l2_evict_first;             // stream weights with an L2 evict_first policy
   const int* eidx;                // MoE: expert id per erows-row block of an indirect segment
@@ -742,7 +743,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
       }
       if (lane == 0 && i != 0x7fffffff) {
         const unsigned long long key = ((unsigned long long)float_ordered(v) << 32) |
-                                       (unsigned long long)(0xffffffffu - (uint32_t)i);
+                                       (unsigned long long)(0xffffffffu - (uint32_t)(i + p.argmax_row0));
         atomicMax(&p.argmax[b], key);
       }
     }

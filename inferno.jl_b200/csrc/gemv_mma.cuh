@@ -467,7 +467,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
     }
     if (lane == 0 && i != 0x7fffffff) {
       const unsigned long long key = ((unsigned long long)float_ordered(v) << 32) |
-                                     (unsigned long long)(0xffffffffu - (uint32_t)i);
+                                     (unsigned long long)(0xffffffffu - (uint32_t)(i + p.argmax_row0));
       atomicMax(&p.argmax[0], key);
     }
   }

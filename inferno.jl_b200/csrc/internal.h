@@ -45,6 +45,7 @@ struct GemvCall {
   int pro_group = 0;
   int epi = 0;
   unsigned long long* argmax = nullptr;
+  int argmax_row0 = 0;        // global index of row 0 of mats[0] (vocab-split lm_head)
   int* err = nullptr;
   int force_r = 0;            // 0 = planner's choice
   // MoE: for an `indirect` matrix, row r is row (r % erows) of expert

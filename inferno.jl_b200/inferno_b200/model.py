@@ -107,17 +107,28 @@ class Model:
     """A Qwen3.5-hybrid model resident on one B200."""
 
     def __init__(self, spec: S.ModelSpec, tensors: dict, device: int = 0, max_ctx: int | None = None,
-                 use_graphs: bool = True, use_pdl: bool = True):
+                 use_graphs: bool = True, use_pdl: bool = True, tp_rank: int = 0, tp_size: int = 1,
+                 tp_uid: bytes | None = None):
+        """tp_size > 1: this process is rank `tp_rank` of a tensor-parallel group;
+        `tensors` is the full model (sharded here, inferno_b200.tp) and
+        `tp_uid` the group's NCCL unique id (Model.tp_unique_id() on rank 0,
+        shared by the caller).  All ranks must construct concurrently."""
         self.spec = spec
+        lspec = spec
+        if tp_size > 1:
+            from . import tp as _tp
+            if tp_uid is None or len(tp_uid) != 128:
+                raise ValueError("tensor parallel needs the group's 128-byte NCCL unique id")
+            lspec, tensors = _tp.shard(spec, tensors, tp_rank, tp_size)
         c = InfernoConfig()
         c.struct_size = C.sizeof(InfernoConfig)
         c.device = device
         c.hidden_size = spec.hidden
-        c.intermediate_size = spec.ffn
+        c.intermediate_size = lspec.ffn
         c.num_layers = spec.layers
         c.vocab_size = spec.vocab
-        c.n_heads, c.n_kv_heads, c.head_dim = spec.n_heads, spec.n_kv, spec.head_dim
-        c.ssm_nv, c.ssm_nk, c.ssm_dk, c.ssm_dv = spec.ssm_nv, spec.ssm_nk, spec.ssm_dk, spec.ssm_dv
+        c.n_heads, c.n_kv_heads, c.head_dim = lspec.n_heads, lspec.n_kv, spec.head_dim
+        c.ssm_nv, c.ssm_nk, c.ssm_dk, c.ssm_dv = lspec.ssm_nv, lspec.ssm_nk, spec.ssm_dk, spec.ssm_dv
         c.ssm_conv_kernel = spec.conv_k
         c.max_ctx = max_ctx or spec.ctx
         c.n_experts, c.n_experts_used = spec.n_experts, spec.n_experts_used
@@ -125,7 +136,10 @@ class Model:
         c.max_batch = 1
         c.rms_eps, c.rope_theta, c.partial_rotary_factor = spec.eps, spec.rope_theta, spec.partial_rotary
         c.use_graphs, c.use_pdl = int(use_graphs), int(use_pdl)
-        c.tp_rank, c.tp_size = 0, 1
+        c.tp_rank, c.tp_size = tp_rank, tp_size
+        if tp_size > 1:
+            self._uid = C.create_string_buffer(bytes(tp_uid), 128)
+            c.nccl_unique_id = C.cast(self._uid, C.c_void_p)
         self.cfg = c
         h = C.c_void_p()
         call("inferno_engine_create", C.byref(c), C.byref(h))
@@ -141,6 +155,13 @@ class Model:
         except Exception:
             self.close()
             raise
+
+    @staticmethod
+    def tp_unique_id() -> bytes:
+        """A fresh NCCL unique id for a tensor-parallel group (call on rank 0)."""
+        buf = C.create_string_buffer(128)
+        call("inferno_tp_unique_id", buf, 128)
+        return buf.raw
 
     @classmethod
     def from_gguf(cls, path, **kw) -> "Model":

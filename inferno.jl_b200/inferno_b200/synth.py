@@ -330,6 +330,11 @@ CONFIGS = {
     # small model with the same kernel shapes (dk=dv=128, head_dim 256, nk != nv)
     "tiny": ModelSpec("tiny", hidden=512, layers=4, n_heads=4, n_kv=2, head_dim=256,
                       ffn=1024, vocab=4096, ssm_nv=4, ssm_nk=2, ctx=256),
+    # tensor-parallel test models: GDN QK groups / heads / FFN split on super-block boundaries
+    "tiny-tp": ModelSpec("tiny-tp", hidden=512, layers=4, n_heads=4, n_kv=2, head_dim=256,
+                         ffn=1024, vocab=4096, ssm_nv=8, ssm_nk=4, ctx=256),
+    "small-tp": ModelSpec("small-tp", hidden=1024, layers=4, n_heads=16, n_kv=4, head_dim=256,
+                          ffn=2048, vocab=8192, ssm_nv=32, ssm_nk=16, ctx=256),
     "tiny-moe": ModelSpec("tiny-moe", hidden=512, layers=4, n_heads=4, n_kv=2, head_dim=256,
                           ffn=0, vocab=4096, ssm_nv=4, ssm_nk=2, ctx=256, n_experts=16,
                           n_experts_used=4, expert_ffn=256, shexp_ffn=256),
