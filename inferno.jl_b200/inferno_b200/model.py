@@ -256,6 +256,8 @@ def algorithmic_bytes_per_token(spec: S.ModelSpec, tensors: dict, pos: int) -> i
     recurrent state and conv state read + write."""
     skip = {"token_embd.weight"} if "output.weight" in tensors else set()
     w = sum(t.nbytes for n, t in tensors.items() if n not in skip and not n.endswith("_exps.weight"))
+    if spec.n_experts:   # routed experts: the top-k of E are read per token
+        w += sum(t.nbytes for n, t in tensors.items() if n.endswith("_exps.weight")) * spec.n_experts_used // spec.n_experts
     if "output.weight" in tensors:
         w += spec.hidden * S.BLOCK[tensors["token_embd.weight"].ggml_type][1] // S.BLOCK[tensors["token_embd.weight"].ggml_type][0]
     n_attn = sum(1 for i in range(spec.layers) if f"blk.{i}.ssm_a" not in tensors)

@@ -255,9 +255,16 @@ def quantize(w: np.ndarray, ggml_type: int, chunk_rows: int = 1 << 14) -> np.nda
 
 
 def random_quant_matrix(rng: np.random.Generator, rows: int, inner: int, ggml_type: int,
-                        std: float = 0.02, chunk_rows: int = 1 << 13) -> np.ndarray:
-    """N(0, std) matrix quantized chunk by chunk (bounded host memory)."""
+                        std: float = 0.02, chunk_rows: int = 1 << 13, pool: int = 0) -> np.ndarray:
+    """N(0, std) matrix quantized chunk by chunk (bounded host memory).
+
+    pool > 0 (throughput runs of the multi-GB configs): quantize `pool` rows
+    and fill the matrix with rows drawn from them at random -- the same value
+    distribution and byte count, without quantizing billions of weights."""
     rb = row_bytes(ggml_type, inner)
+    if pool and rows > pool:
+        base = random_quant_matrix(rng, pool, inner, ggml_type, std, chunk_rows)
+        return base[rng.integers(0, pool, rows)]
     out = np.empty((rows, rb), np.uint8)
     for r0 in range(0, rows, chunk_rows):
         n = min(chunk_rows, rows - r0)
@@ -346,22 +353,27 @@ def _f32_tensor(a: np.ndarray, ne) -> Tensor:
     return Tensor(F32, tuple(ne), a.view(np.uint8).reshape(-1))
 
 
-def _q_tensor(rng, ggml_type, rows, inner, std=0.02) -> Tensor:
-    data = random_quant_matrix(rng, rows, inner, ggml_type, std)
+def _q_tensor(rng, ggml_type, rows, inner, std=0.02, pool=0) -> Tensor:
+    data = random_quant_matrix(rng, rows, inner, ggml_type, std, pool=pool)
     return Tensor(ggml_type, (inner, rows), data.reshape(-1))
 
 
-def make_model(spec: ModelSpec, seed: int = 0, layers: int | None = None) -> dict:
+def make_model(spec: ModelSpec, seed: int = 0, layers: int | None = None, pool: int = 0) -> dict:
     """Return {name: Tensor} for a seeded model of ``spec`` (optionally only the
-    first ``layers`` layers -- used by tests to bound memory)."""
+    first ``layers`` layers -- used by tests to bound memory).  pool > 0 draws
+    the rows of every quantized matrix from `pool` quantized rows (see
+    random_quant_matrix): for throughput runs of the 9B / MoE configs."""
     rng = np.random.Generator(np.random.PCG64(seed))
+
+    def qt(rng, t, rows, inner, std=0.02):
+        return _q_tensor(rng, t, rows, inner, std, pool=pool)
     H = spec.hidden
     T = {}
 
     def norm(n):
         return (1.0 + 0.02 * rng.standard_normal(n)).astype(np.float32)
 
-    T["token_embd.weight"] = _q_tensor(rng, spec.t_embd, spec.vocab, H)
+    T["token_embd.weight"] = qt(rng, spec.t_embd, spec.vocab, H)
     T["output_norm.weight"] = _f32_tensor(norm(H), (H,))
     nl = spec.layers if layers is None else layers
     for i in range(nl):
@@ -370,17 +382,17 @@ def make_model(spec: ModelSpec, seed: int = 0, layers: int | None = None) -> dic
         T[p + "post_attention_norm.weight"] = _f32_tensor(norm(H), (H,))
         if spec.is_attn(i):
             hd = spec.head_dim
-            T[p + "attn_q.weight"] = _q_tensor(rng, spec.t_attn, 2 * spec.n_heads * hd, H)
-            T[p + "attn_k.weight"] = _q_tensor(rng, spec.t_attn, spec.n_kv * hd, H)
-            T[p + "attn_v.weight"] = _q_tensor(rng, spec.t_attn_v, spec.n_kv * hd, H)
-            T[p + "attn_output.weight"] = _q_tensor(rng, spec.t_attn, H, spec.n_heads * hd)
+            T[p + "attn_q.weight"] = qt(rng, spec.t_attn, 2 * spec.n_heads * hd, H)
+            T[p + "attn_k.weight"] = qt(rng, spec.t_attn, spec.n_kv * hd, H)
+            T[p + "attn_v.weight"] = qt(rng, spec.t_attn_v, spec.n_kv * hd, H)
+            T[p + "attn_output.weight"] = qt(rng, spec.t_attn, H, spec.n_heads * hd)
             T[p + "attn_q_norm.weight"] = _f32_tensor(norm(hd), (hd,))
             T[p + "attn_k_norm.weight"] = _f32_tensor(norm(hd), (hd,))
         else:
             cc, di = spec.conv_channels, spec.d_inner
-            T[p + "attn_qkv.weight"] = _q_tensor(rng, spec.t_attn, cc, H)
-            T[p + "attn_gate.weight"] = _q_tensor(rng, spec.t_attn, di, H)
-            T[p + "ssm_out.weight"] = _q_tensor(rng, spec.t_attn, H, di)
+            T[p + "attn_qkv.weight"] = qt(rng, spec.t_attn, cc, H)
+            T[p + "attn_gate.weight"] = qt(rng, spec.t_attn, di, H)
+            T[p + "ssm_out.weight"] = qt(rng, spec.t_attn, H, di)
             conv = (0.5 * rng.standard_normal((cc, spec.conv_k))).astype(np.float32)
             T[p + "ssm_conv1d.weight"] = _f32_tensor(conv, (spec.conv_k, cc))
             T[p + "ssm_alpha.weight"] = _f32_tensor(
@@ -398,17 +410,17 @@ def make_model(spec: ModelSpec, seed: int = 0, layers: int | None = None) -> dic
             for nm, t, rows, inner in (("ffn_gate_exps", spec.t_exp_gu, Ie, H),
                                        ("ffn_up_exps", spec.t_exp_gu, Ie, H),
                                        ("ffn_down_exps", spec.t_exp_down, H, Ie)):
-                data = random_quant_matrix(rng, rows * E, inner, t)
+                data = random_quant_matrix(rng, rows * E, inner, t, pool=pool)
                 T[p + nm + ".weight"] = Tensor(t, (inner, rows, E), data.reshape(-1))
             if spec.shexp_ffn:
                 S = spec.shexp_ffn
-                T[p + "ffn_gate_shexp.weight"] = _q_tensor(rng, Q4_K, S, H)
-                T[p + "ffn_up_shexp.weight"] = _q_tensor(rng, Q4_K, S, H)
-                T[p + "ffn_down_shexp.weight"] = _q_tensor(rng, Q4_K, H, S)
+                T[p + "ffn_gate_shexp.weight"] = qt(rng, Q4_K, S, H)
+                T[p + "ffn_up_shexp.weight"] = qt(rng, Q4_K, S, H)
+                T[p + "ffn_down_shexp.weight"] = qt(rng, Q4_K, H, S)
         else:
-            T[p + "ffn_gate.weight"] = _q_tensor(rng, spec.t_ffn_gu, spec.ffn, H)
-            T[p + "ffn_up.weight"] = _q_tensor(rng, spec.t_ffn_gu, spec.ffn, H)
-            T[p + "ffn_down.weight"] = _q_tensor(rng, spec.t_ffn_down, H, spec.ffn)
+            T[p + "ffn_gate.weight"] = qt(rng, spec.t_ffn_gu, spec.ffn, H)
+            T[p + "ffn_up.weight"] = qt(rng, spec.t_ffn_gu, spec.ffn, H)
+            T[p + "ffn_down.weight"] = qt(rng, spec.t_ffn_down, H, spec.ffn)
     return T
 
 
