@@ -749,6 +749,7 @@ int pk_plan_gemv(const GemvCall& c, int slot_cap, int sms, PkStage* S) {
   const int TR = best_r * PK_NW / best_g, eff = paired ? TR / 2 : TR;
   GemvParams& p = S->g;
   p = GemvParams{};
+  p.xch_wk = p.xch_rk = -1;
   int ntiles = 0;
   for (int i = 0; i < c.nmats; ++i) {
     p.seg[i].W = (const uint8_t*)c.mats[i].W;

@@ -43,9 +43,11 @@ struct Ctl {                 // device-resident step control
   unsigned long long argkey; // packed first-max of the running lm_head
 };
 
-__global__ void finalize_kernel(Ctl* c, const int* prompt, int* out, int max_out) {
+__global__ void finalize_kernel(Ctl* c, const int* prompt, int* out, int max_out, unsigned long long* xch_seq,
+                                int xch_nsync) {
   pdl_wait();
   pdl_trigger();
+  if (xch_seq) *xch_seq += (unsigned long long)xch_nsync;   // sequence base of the next token's sync points
   const unsigned long long key = c->argkey;
   const int am = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull));
   c->last = am;
@@ -98,6 +100,16 @@ struct InfernoEngine {
   ncclComm_t comm = nullptr;
   inf::DevTensor lm_view;
   float* logits_local = nullptr;
+  // fused tensor-parallel exchange over NVLink peer memory (xch); when off
+  // (INFERNO_TP_NCCL=1 or a GEMV outside the tensor-core path) the residual
+  // is summed with ncclAllReduce
+  bool xch = false;
+  float* x2 = nullptr;              // second residual buffer (alternates per sync point)
+  float* xcur = nullptr;            // buffer holding the current residual while enqueueing
+  int xch_k = 0, xch_pending = -1;  // next sync index / sync whose partials are pending
+  unsigned long long* xch_peer[8] = {};   // every rank's [2][N][H] exchange words (own + IPC-mapped)
+  unsigned* xch_done = nullptr;           // setup barrier word
+  unsigned long long* xch_seq = nullptr;
   bool finalized = false;
   int C = 0, di = 0, rd = 0, split_len = 64, nsplit = 1;
   // activations
@@ -186,6 +198,8 @@ void mark(InfernoEngine* e, int kind) {
   e->prof_kind.push_back(kind);
 }
 
+constexpr int EPI_XCH_WRITE = 100;   // engine-level: residual partial to the TP exchange
+
 int gemv(InfernoEngine* e, int type, int inner, std::initializer_list<GemvMat> mats, const float* x, int pro,
          const float* pro_w, const float* pro_z, int group, int epi, unsigned long long* argmax, bool pdl) {
   GemvCall c;
@@ -202,6 +216,21 @@ int gemv(InfernoEngine* e, int type, int inner, std::initializer_list<GemvMat> m
   c.epi = epi;
   c.argmax = argmax;
   c.err = e->err;
+  if (e->xch) {
+    const int n = e->cfg.tp_size;
+    c.xch_n = n;
+    c.xch_rank = e->cfg.tp_rank;
+    c.xch_seq = e->xch_seq;
+    for (int q = 0; q < n; ++q) c.xch_parts[q] = e->xch_peer[q];
+    if (epi == EPI_XCH_WRITE) {
+      c.epi = EPI_STORE;
+      c.xch_wk = e->xch_k;
+      e->xch_pending = e->xch_k++;
+    } else if (pro == PRO_RMSNORM && x == e->xcur && e->xch_pending >= 0) {
+      c.xch_rk = e->xch_pending;
+      c.x_next = e->xcur == e->x ? e->x2 : e->x;
+    }
+  }
   if (e->trace && e->trace_idx < 256) c.trace = e->trace + 32 * (e->trace_idx++);
   int rc = launch_gemv(c, e->st, pdl);
   if (!rc) mark(e, epi == EPI_ARGMAX ? K_LMHEAD : K_GEMV);
@@ -213,10 +242,21 @@ GemvMat M(DevTensor* t, float* y) { return GemvMat{t->d, y, (int)t->rows()}; }
 // Residual epilogue of a sublayer's last GEMV.  Tensor parallel: rank 0 adds
 // its partial to x, the other ranks store theirs, and one all-reduce (sum) of
 // x completes x + sum_r partial_r on every rank.
-int residual_epi(InfernoEngine* e) { return (e->cfg.tp_size > 1 && e->cfg.tp_rank != 0) ? EPI_STORE : EPI_ADD; }
+int residual_epi(InfernoEngine* e) {
+  if (e->xch) return EPI_XCH_WRITE;
+  return (e->cfg.tp_size > 1 && e->cfg.tp_rank != 0) ? EPI_STORE : EPI_ADD;
+}
+
+// After the GEMVs that consumed a pending exchange: the completed residual now
+// lives in the other buffer.
+void xch_commit(InfernoEngine* e) {
+  if (e->xch_pending < 0) return;
+  e->xcur = e->xcur == e->x ? e->x2 : e->x;
+  e->xch_pending = -1;
+}
 
 int tp_sum_x(InfernoEngine* e) {
-  if (e->cfg.tp_size <= 1) return 0;
+  if (e->cfg.tp_size <= 1 || e->xch) return 0;
   ncclResult_t r = ncclAllReduce(e->x, e->x, (size_t)e->cfg.hidden_size, ncclFloat, ncclSum, e->comm, e->st);
   if (r != ncclSuccess) return set_error(INFERNO_ENCCL, "all-reduce of the residual: %s", ncclGetErrorString(r));
   return 0;
@@ -297,19 +337,20 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     // [in_proj | attn_gate] on RMSNorm(x)
     if (ab & 1) {
     } else if (L.in_proj->type == L.gate->type) {
-      if ((rc = gemv(e, L.in_proj->type, H, {M(L.in_proj, e->qkv), M(L.gate, e->z)}, e->x, PRO_RMSNORM,
+      if ((rc = gemv(e, L.in_proj->type, H, {M(L.in_proj, e->qkv), M(L.gate, e->z)}, e->xcur, PRO_RMSNORM,
                      (const float*)L.attn_norm->d, nullptr, 0, EPI_STORE, nullptr, pdl)))
         return rc;
     } else {
-      if ((rc = gemv(e, L.in_proj->type, H, {M(L.in_proj, e->qkv)}, e->x, PRO_RMSNORM, (const float*)L.attn_norm->d,
+      if ((rc = gemv(e, L.in_proj->type, H, {M(L.in_proj, e->qkv)}, e->xcur, PRO_RMSNORM, (const float*)L.attn_norm->d,
                      nullptr, 0, EPI_STORE, nullptr, pdl)))
         return rc;
-      if ((rc = gemv(e, L.gate->type, H, {M(L.gate, e->z)}, e->x, PRO_RMSNORM, (const float*)L.attn_norm->d,
+      if ((rc = gemv(e, L.gate->type, H, {M(L.gate, e->z)}, e->xcur, PRO_RMSNORM, (const float*)L.attn_norm->d,
                      nullptr, 0, EPI_STORE, nullptr, pdl)))
         return rc;
     }
+    xch_commit(e);
     GdnParams g{};
-    g.x = e->x;
+    g.x = e->xcur;
     g.in_norm = (const float*)L.attn_norm->d;
     g.eps = c.rms_eps;
     g.H = H;
@@ -340,17 +381,18 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     (void)qrows;
     if (ab & 1) {
     } else if (L.wq->type == L.wk->type && L.wk->type == L.wv->type) {
-      if ((rc = gemv(e, L.wq->type, H, {M(L.wq, e->qg), M(L.wk, e->k), M(L.wv, e->v)}, e->x, PRO_RMSNORM,
+      if ((rc = gemv(e, L.wq->type, H, {M(L.wq, e->qg), M(L.wk, e->k), M(L.wv, e->v)}, e->xcur, PRO_RMSNORM,
                      (const float*)L.attn_norm->d, nullptr, 0, EPI_STORE, nullptr, pdl)))
         return rc;
     } else {
-      if ((rc = gemv(e, L.wq->type, H, {M(L.wq, e->qg), M(L.wk, e->k)}, e->x, PRO_RMSNORM,
+      if ((rc = gemv(e, L.wq->type, H, {M(L.wq, e->qg), M(L.wk, e->k)}, e->xcur, PRO_RMSNORM,
                      (const float*)L.attn_norm->d, nullptr, 0, EPI_STORE, nullptr, pdl)))
         return rc;
-      if ((rc = gemv(e, L.wv->type, H, {M(L.wv, e->v)}, e->x, PRO_RMSNORM, (const float*)L.attn_norm->d, nullptr,
+      if ((rc = gemv(e, L.wv->type, H, {M(L.wv, e->v)}, e->xcur, PRO_RMSNORM, (const float*)L.attn_norm->d, nullptr,
                      0, EPI_STORE, nullptr, pdl)))
         return rc;
     }
+    xch_commit(e);
     AttnParams a{};
     a.qg = e->qg;
     a.k = e->k;
@@ -389,9 +431,10 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
   }
   // FFN: SwiGLU(gate, up) on RMSNorm(x), then down with residual add
   if (L.ffn_gate->type == L.ffn_up->type) {
-    if (!(ab & 16) && (rc = gemv(e, L.ffn_gate->type, H, {M(L.ffn_gate, e->h), M(L.ffn_up, nullptr)}, e->x, PRO_RMSNORM,
+    if (!(ab & 16) && (rc = gemv(e, L.ffn_gate->type, H, {M(L.ffn_gate, e->h), M(L.ffn_up, nullptr)}, e->xcur, PRO_RMSNORM,
                    (const float*)L.post_norm->d, nullptr, 0, EPI_SWIGLU, nullptr, pdl)))
       return rc;
+    xch_commit(e);
   } else {
     return set_error(INFERNO_EINVAL, "layer %d: ffn_gate and ffn_up must share a type", li);
   }
@@ -414,7 +457,8 @@ int launch_finalize(InfernoEngine* e, bool pdl) {
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t r = cudaLaunchKernelEx(&cfg, finalize_kernel, e->ctl, (const int*)e->prompt, e->out_tokens, e->max_out);
+  cudaError_t r = cudaLaunchKernelEx(&cfg, finalize_kernel, e->ctl, (const int*)e->prompt, e->out_tokens, e->max_out,
+                                     e->xch ? e->xch_seq : (unsigned long long*)nullptr, e->xch_k);
   if (r != cudaSuccess) return set_error(INFERNO_ECUDA, "finalize launch: %s", cudaGetErrorString(r));
   mark(e, K_FINAL);
   return 0;
@@ -423,6 +467,9 @@ int launch_finalize(InfernoEngine* e, bool pdl) {
 int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
   const InfernoConfig& c = e->cfg;
   int rc;
+  e->xcur = e->x;          // the embedding row lands in x
+  e->xch_k = 0;
+  e->xch_pending = -1;
   e->launches = 0;
   e->trace_idx = 0;
   if (e->profiling) mark(e, -1), --e->launches;
@@ -440,7 +487,7 @@ int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
     g.inner = c.hidden_size;
     g.mats[0] = M(e->lm_head, write_logits ? e->logits_local : nullptr);
     g.nmats = 1;
-    g.x = e->x;
+    g.x = e->xcur;
     g.x_stride = c.hidden_size;
     g.pro = PRO_RMSNORM;
     g.pro_w = (const float*)e->out_norm->d;
@@ -449,7 +496,16 @@ int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
     g.argmax = &e->ctl->argkey;
     g.argmax_row0 = c.tp_rank * (int)e->lm_head->rows();
     g.err = e->err;
+    if (e->xch) {
+      g.xch_n = c.tp_size;
+      g.xch_rank = c.tp_rank;
+      g.xch_seq = e->xch_seq;
+      for (int q = 0; q < c.tp_size; ++q) g.xch_parts[q] = e->xch_peer[q];
+      g.xch_rk = e->xch_pending;
+      g.x_next = e->xcur == e->x ? e->x2 : e->x;
+    }
     if ((rc = launch_gemv(g, e->st, pdl))) return rc;
+    xch_commit(e);
     mark(e, K_LMHEAD);
     ncclResult_t r = ncclAllReduce(&e->ctl->argkey, &e->ctl->argkey, 1, ncclUint64, ncclMax, e->comm, e->st);
     if (r == ncclSuccess && write_logits)
@@ -457,7 +513,7 @@ int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
     if (r != ncclSuccess) return set_error(INFERNO_ENCCL, "lm_head collectives: %s", ncclGetErrorString(r));
     return launch_finalize(e, pdl);
   }
-  if (!(e->ablate & 64) && (rc = gemv(e, e->lm_head->type, c.hidden_size, {M(e->lm_head, write_logits ? e->logits : nullptr)}, e->x,
+  if (!(e->ablate & 64) && (rc = gemv(e, e->lm_head->type, c.hidden_size, {M(e->lm_head, write_logits ? e->logits : nullptr)}, e->xcur,
                  PRO_RMSNORM, (const float*)e->out_norm->d, nullptr, 0, EPI_ARGMAX, &e->ctl->argkey, pdl)))
     return rc;
   return launch_finalize(e, pdl);
@@ -531,6 +587,69 @@ void build_rope(int ctx, int rd, float theta, std::vector<float>& cs, std::vecto
 }  // namespace inf
 
 using namespace inf;
+
+namespace inf {
+namespace {
+
+// Fused tensor-parallel exchange: every rank allocates [2 slots][N][H] 64-bit
+// {value, tag} words, the CUDA IPC handles are all-gathered over the engine's
+// NCCL communicator and every peer buffer is mapped.  Used when every
+// residual GEMV and every RMSNorm consumer runs on the tensor-core path.
+int setup_xch(InfernoEngine* e) {
+  const InfernoConfig& c = e->cfg;
+  const int n = c.tp_size, H = c.hidden_size;
+  const char* nc = getenv("INFERNO_TP_NCCL");
+  if ((nc && atoi(nc) != 0) || e->dump || n > 8 || H > 8192) return 0;
+  auto ok = [](const DevTensor* t, int64_t inner) {
+    return t && (t->type == T_Q4_K || t->type == T_Q6_K) && inner % 256 == 0;
+  };
+  bool eligible = ok(e->lm_head, H);
+  for (auto& L : e->layers) {
+    if (L.ssm)
+      eligible = eligible && ok(L.in_proj, H) && ok(L.gate, H) && ok(L.ssm_out, e->di);
+    else
+      eligible = eligible && ok(L.wq, H) && ok(L.wk, H) && ok(L.wv, H) && ok(L.wo, (int64_t)c.n_heads * c.head_dim);
+    eligible = eligible && ok(L.ffn_gate, H) && ok(L.ffn_up, H) && ok(L.ffn_down, c.intermediate_size);
+  }
+  if (!eligible) return 0;
+  int rc;
+  unsigned long long* mine = nullptr;
+  if ((rc = dalloc(e, &mine, (size_t)2 * n * H)) || (rc = dalloc(e, &e->x2, H)) ||
+      (rc = dalloc(e, &e->xch_done, 1)) || (rc = dalloc(e, &e->xch_seq, 1)))
+    return rc;
+  cudaIpcMemHandle_t h;
+  INF_CUDA_TRY(cudaIpcGetMemHandle(&h, mine));
+  uint8_t* dh = nullptr;
+  INF_CUDA_TRY(cudaMalloc(&dh, (size_t)n * sizeof h));
+  INF_CUDA_TRY(cudaMemcpy(dh + (size_t)c.tp_rank * sizeof h, &h, sizeof h, cudaMemcpyHostToDevice));
+  ncclResult_t r = ncclAllGather(dh + (size_t)c.tp_rank * sizeof h, dh, sizeof h, ncclUint8, e->comm, e->st);
+  std::vector<cudaIpcMemHandle_t> all(n);
+  cudaError_t ce = cudaStreamSynchronize(e->st);
+  if (ce == cudaSuccess) ce = cudaMemcpy(all.data(), dh, (size_t)n * sizeof h, cudaMemcpyDeviceToHost);
+  cudaFree(dh);
+  if (r != ncclSuccess) return set_error(INFERNO_ENCCL, "exchange of IPC handles: %s", ncclGetErrorString(r));
+  if (ce != cudaSuccess) return set_error(INFERNO_ECUDA, "exchange of IPC handles: %s", cudaGetErrorString(ce));
+  for (int q = 0; q < n; ++q) {
+    if (q == c.tp_rank) {
+      e->xch_peer[q] = mine;
+      continue;
+    }
+    void* ptr = nullptr;
+    ce = cudaIpcOpenMemHandle(&ptr, all[q], cudaIpcMemLazyEnablePeerAccess);
+    if (ce != cudaSuccess)
+      return set_error(INFERNO_ECUDA, "cudaIpcOpenMemHandle(rank %d): %s", q, cudaGetErrorString(ce));
+    e->xch_peer[q] = (unsigned long long*)ptr;
+  }
+  // every rank mapped every buffer before anyone writes into a peer
+  r = ncclAllReduce(e->xch_done, e->xch_done, 1, ncclUint32, ncclSum, e->comm, e->st);
+  if (r != ncclSuccess) return set_error(INFERNO_ENCCL, "exchange setup barrier: %s", ncclGetErrorString(r));
+  INF_CUDA_TRY(cudaStreamSynchronize(e->st));
+  e->xch = true;
+  return 0;
+}
+
+}  // namespace
+}  // namespace inf
 
 extern "C" {
 
@@ -730,6 +849,8 @@ int inferno_engine_finalize(InfernoEngine* e) {
         (rc = dalloc(e, &e->moe_y, (size_t)(K + 1) * H)))
       return rc;
   }
+  e->xcur = e->x;
+  if (c.tp_size > 1 && (rc = setup_xch(e))) return rc;
   e->max_out = c.max_ctx + 8;
   // attention splits: multiples of 32 positions, at most 128 splits
   e->split_len = 32;
@@ -965,6 +1086,9 @@ int inferno_layer_forward(InfernoEngine* e, int layer, float* x_host, int pos) {
   if (layer < 0 || layer >= e->cfg.num_layers || !x_host) return set_error(INFERNO_EINVAL, "layer_forward: bad layer");
   if (pos < 0 || pos >= e->cfg.max_ctx) return set_error(INFERNO_EINVAL, "layer_forward: pos %d outside [0, %d)", pos, e->cfg.max_ctx);
   const int H = e->cfg.hidden_size;
+  if (e->cfg.tp_size > 1)
+    return set_error(INFERNO_ESTATE, "layer_forward is not available under tensor parallelism (use forward_tokens)");
+  e->xcur = e->x;
   if ((rc = set_ctl(e, 0, pos, 1))) return rc;
   INF_CUDA_TRY(cudaMemcpyAsync(e->x, x_host, (size_t)H * 4, cudaMemcpyHostToDevice, e->st));
   if ((rc = enqueue_layer(e, layer, false))) return rc;
@@ -1172,6 +1296,8 @@ int inferno_engine_destroy(InfernoEngine* e) {
   for (void* p : e->allocs) cudaFree(p);
   if (e->ev0) cudaEventDestroy(e->ev0);
   if (e->ev1) cudaEventDestroy(e->ev1);
+  for (int q = 0; q < 8; ++q)
+    if (e->xch && q != e->cfg.tp_rank && e->xch_peer[q]) cudaIpcCloseMemHandle(e->xch_peer[q]);
   if (e->comm) ncclCommDestroy(e->comm);
   cudaStreamDestroy(e->st);
   delete e;

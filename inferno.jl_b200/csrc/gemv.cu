@@ -111,13 +111,17 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
   double best = 1e300;
   for (int TR : {16, 32, 64, 128}) {
     const int nrg = TR / 16, nkg = NW / nrg;
-    if (fixed + 2 * stage_of(TR) > smem_cap) continue;
+    // a ring of one stage (no weight prefetch past the current tile) only
+    // when two do not fit next to the staged activations of a long row
+    const int nstg = (int)std::min<size_t>(2, (smem_cap - std::min(smem_cap, fixed)) / stage_of(TR));
+    if (nstg < 1) continue;
     const int eff = paired ? TR / 2 : TR;
     if ((any_indirect || nxv > 1) && c.erows % eff) continue;   // a tile stays inside one expert / slot
     long long tiles = 0;
     for (int i = 0; i < (paired ? 1 : c.nmats); ++i) tiles += (c.mats[i].rows + eff - 1) / eff;
     const long long waves = (tiles + sms - 1) / sms;
-    const double cost = (double)waves * ((nsb + nkg - 1) / nkg) + (double)waves * TR * row_bytes / 65536.0;
+    const double cost = (double)waves * ((nsb + nkg - 1) / nkg) + (double)waves * TR * row_bytes / 65536.0 +
+                        (nstg < 2 ? 2.0 * waves : 0.0);
     if (cost < best) { best = cost; best_tr = TR; }
   }
   if (!best_tr) return 1;
@@ -145,6 +149,13 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
   p.erows = c.erows;
   p.n_experts = c.n_experts;
   p.nxv = nxv;
+  p.xch_n = c.xch_n;
+  p.xch_rank = c.xch_rank;
+  p.xch_wk = c.xch_wk;
+  p.xch_rk = c.xch_rk;
+  p.xch_seq = c.xch_seq;
+  for (int q = 0; q < 8; ++q) p.xch_parts[q] = c.xch_parts[q];
+  p.x_next = c.x_next;
   p.nkc = (c.inner + GEMV_CHUNK - 1) / GEMV_CHUNK;
   p.TR = TR;
   p.nkg = NW / (TR / 16);
@@ -205,11 +216,13 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
     return set_error(-1, "gemv: bad expert / multi-vector arguments");
   static const bool no_mma = getenv("INFERNO_GEMV_NO_MMA") != nullptr;
   const bool mma_ok = !c.force_r && c.nb == 1 && (c.type == T_Q4_K || c.type == T_Q6_K) && c.inner % 256 == 0;
-  if (mma_ok && (!no_mma || c.nxv > 1)) {
+  if (mma_ok && (!no_mma || c.nxv > 1 || c.xch_wk >= 0 || c.xch_rk >= 0)) {
     const int rc = plan_launch_mma(c, dev, sms, st, pdl);
     if (rc <= 0) return rc;
   }
   if (c.nxv > 1) return set_error(-1, "gemv: several input vectors need single-column Q4_K/Q6_K");
+  if (c.xch_wk >= 0 || c.xch_rk >= 0)
+    return set_error(-1, "gemv: the tensor-parallel exchange needs single-column Q4_K/Q6_K rows");
   const long long row_bytes = (long long)c.inner / qk * bb;
   const int nkc = (c.inner + GEMV_CHUNK - 1) / GEMV_CHUNK;
   long long wbytes = 0;
@@ -294,6 +307,7 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
   p.erows = c.erows;
   p.n_experts = c.n_experts;
   p.nxv = 1;
+  p.xch_wk = p.xch_rk = -1;
   p.nkc = nkc;
   p.TR = TR;
   p.nkg = best_g;

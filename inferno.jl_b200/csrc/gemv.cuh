@@ -76,6 +76,18 @@ struct GemvParams {
   int erows;                      // rows per expert block (also the input-slot period)
   int n_experts;                  // valid ids are [0, n_experts)
   int nxv;                        // input vectors (tensor-core path, PRO_NONE)
+  // Tensor-parallel residual exchange over NVLink peer memory (tensor-core
+  // path), low-latency protocol: every element travels as one 64-bit word
+  // {fp32 value, 32-bit tag}, tag = *xch_seq + k + 1 for sync point k, so the
+  // data is its own flag (no fences, counters or flag words).
+  // Writer (xch_wk >= 0): the output rows are this rank's partial of sync k
+  // and go to parts[k & 1][rank][row] on every rank.  Reader (xch_rk >= 0):
+  // polls parts[k & 1][r][i] until the tags match, uses x + sum_r partial_r
+  // (rank order: bit-identical on every rank) and CTA 0 stores it in x_next.
+  int xch_n, xch_rank, xch_wk, xch_rk;
+  const unsigned long long* xch_seq;
+  unsigned long long* xch_parts[8];  // each rank's [2][n][H] words
+  float* x_next;
   unsigned long long* trace;      // debug: phase timestamps of CTA 0 / last CTA (null = off)
 };
 

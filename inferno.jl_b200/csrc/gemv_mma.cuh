@@ -59,6 +59,15 @@ __device__ __forceinline__ int ubyte(uint32_t w) {   // unsigned byte K of w
   return (int)((w >> (8 * K)) & 0xffu);
 }
 
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 // Element (within the vector) of k-half p, position t of the quad (ks, cc),
 // and the sub-block sum slot it belongs to.
 template <int TYPE>
@@ -97,7 +106,54 @@ __device__ float gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, 
   const float* x = p.x;
   float ss = 0.f, amax = 0.f;
   bool bad = false;
-  if (p.pro == PRO_RMSNORM) {
+  if (p.pro == PRO_RMSNORM && p.xch_rk >= 0) {
+    // residual stream = x + the ranks' partials of sync point xch_rk, summed
+    // in rank order (bit-identical on every rank); CTA 0 stores it for later
+    // kernels.  Every word is polled until its tag is this sync's (bounded).
+    const uint32_t tag = (uint32_t)(*p.xch_seq + (unsigned long long)p.xch_rk + 1ull);
+    const unsigned long long* parts = p.xch_parts[p.xch_rank] + (size_t)(p.xch_rk & 1) * p.xch_n * n;
+    constexpr int PER = 8192 / NT;          // hidden <= 8192
+    float v[PER];
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int i = tid + j * NT;
+      v[j] = i < n ? __ldcg(x + i) : 0.f;
+    }
+    for (int r = 0; r < p.xch_n; ++r) {
+      unsigned long long w[PER];
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        const int i = tid + j * NT;
+        w[j] = i < n ? ld_relaxed_sys_u64(parts + (size_t)r * n + i) : ((unsigned long long)tag << 32);
+      }
+#pragma unroll
+      for (int j = 0; j < PER; ++j) {
+        const int i = tid + j * NT;
+        unsigned it = 0;
+        while ((uint32_t)(w[j] >> 32) != tag) {
+          if (++it > (1u << 22)) {
+            if (p.err) atomicExch(p.err, DERR_MBAR_TIMEOUT);
+            bad = true;
+            break;
+          }
+          if (it > 1024) __nanosleep(32);
+          w[j] = ld_relaxed_sys_u64(parts + (size_t)r * n + i);
+        }
+        v[j] += __uint_as_float((uint32_t)w[j]);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < PER; ++j) {
+      const int i = tid + j * NT;
+      if (i < n) {
+        if (blockIdx.x == 0) p.x_next[i] = v[j];
+        ss = fmaf(v[j], v[j], ss);
+        const float u = v[j] * p.pro_w[i];
+        amax = fmaxf(amax, fabsf(u));
+        xf[i] = u;
+      }
+    }
+  } else if (p.pro == PRO_RMSNORM) {
     for (int i = tid; i < n; i += NT) {
       const float v = x[i];
       ss = fmaf(v, v, ss);
@@ -328,6 +384,7 @@ template <int TYPE, int NW>
 __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) GEMV_TRACE(0);
   constexpr int BB = TYPE == T_Q4_K ? 144 : 210;
   constexpr int XS_PER_SB = TYPE == T_Q4_K ? 8 : 16;
   // layout: [full][empty][red 2*NW+4][vmax 16][kpart NW*16][xsum][xf][xq][stages]
@@ -362,8 +419,11 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
   }
 
   pdl_wait();
+  if (tid == 0) GEMV_TRACE(2);
   const float colscale = gemv_mma_prologue<TYPE, NW>(p, xf, xq, xsum, red, vmax, tid);
+  if (tid == 0) GEMV_TRACE(3);
   const bool nonfinite = *(volatile int*)&red[2 * NW] != 0;
+  const uint32_t xtag = p.xch_wk >= 0 ? (uint32_t)(*p.xch_seq + (unsigned long long)p.xch_wk + 1ull) : 0u;
 
   const bool paired = (p.epi == EPI_SWIGLU);
   const int nrg = p.TR >> 4;            // 16-row groups per tile
@@ -447,6 +507,11 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
           if (p.epi == EPI_ARGMAX) {
             if (t > best_v || (t == best_v && row < best_i)) { best_v = t; best_i = row; }
             if (p.seg[sg].y) p.seg[sg].y[row] = t;
+          } else if (p.xch_wk >= 0) {
+            // this rank's partial of sync point xch_wk, to every rank, tagged
+            const size_t off = ((size_t)(p.xch_wk & 1) * p.xch_n + p.xch_rank) * p.seg[0].rows + row;
+            const unsigned long long wv = ((unsigned long long)xtag << 32) | __float_as_uint(t);
+            for (int q = 0; q < p.xch_n; ++q) st_relaxed_sys_u64(p.xch_parts[q] + off, wv);
           } else {
             float* y = p.seg[sg].y + row;
             if (p.epi == EPI_ADD) *y += t;
@@ -456,6 +521,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
       }
     }
   }
+  if (tid == 0) GEMV_TRACE(6);
   if (p.epi == EPI_ARGMAX && wk == 0) {
     float v = best_v;
     int i = best_i;

@@ -57,6 +57,11 @@ struct GemvCall {
   // several input vectors (x + v * x_stride, v < nxv): rows use vector
   // xslot0 + r / erows (single-column tensor-core path, PRO_NONE only)
   int nxv = 1;
+  // tensor-parallel residual exchange (see GemvParams::xch_*); -1 = off
+  int xch_n = 0, xch_rank = 0, xch_wk = -1, xch_rk = -1;
+  const unsigned long long* xch_seq = nullptr;
+  unsigned long long* xch_parts[8] = {};
+  float* x_next = nullptr;
   unsigned long long* trace = nullptr;   // debug phase timestamps (32 slots)
 };
 
