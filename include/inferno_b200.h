@@ -115,6 +115,15 @@ int inferno_gemv_ex(int ggml_type, const void* W, const float* x, float* y, int 
 int inferno_gemv_swiglu(int ggml_type, const void* Wg, const void* Wu, const float* x, float* h, int inner,
                         int rows, int batch, const float* norm_w, float eps, void* stream);
 
+/* Gated delta-rule recurrence over T steps (the state
+ * update of GatedDeltaNetCPU, src/ModelCPU.jl:640-674, without projections):
+ * S_h = S_h*exp(g); S_h += beta*(v - S_h k) k^T; y = S_h q, per head and step.
+ * Device pointers: q, k [T][n_heads][dk]; v, y [T][n_heads][dv];
+ * beta, g [T][n_heads]; S [n_heads][dv][dk] fp32, updated in place.
+ * dk = 128, dv % 16 == 0; q, k, S 16-byte aligned. */
+int inferno_gdn_recurrence(int T, int n_heads, int dk, int dv, const float* q, const float* k, const float* v,
+                           const float* beta, const float* g, float* S, float* y, void* stream);
+
 /* ======================= 3. engine tier ==================================== */
 
 /* Model hyper-parameters, filled by the host from GGUF metadata
