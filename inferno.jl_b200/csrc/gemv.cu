@@ -61,16 +61,16 @@ cudaError_t launch_nb(const GemvParams& p, int NB, int R, int NW, int grid, size
   }
 }
 
-template <int TYPE>
-cudaError_t launch_mma(const GemvParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
+template <int TYPE, int MODE>
+cudaError_t launch_mma_mode(const GemvParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_done[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<TYPE, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         227 * 1024);
+    cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<TYPE, 16, MODE>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
-    cudaFuncSetAttribute(gemv_mma_kernel<TYPE, 16>, cudaFuncAttributePreferredSharedMemoryCarveout,
+    cudaFuncSetAttribute(gemv_mma_kernel<TYPE, 16, MODE>, cudaFuncAttributePreferredSharedMemoryCarveout,
                          cudaSharedmemCarveoutMaxShared);
     attr_done[dev & 63] = true;
   }
@@ -84,7 +84,16 @@ cudaError_t launch_mma(const GemvParams& p, int grid, size_t smem, cudaStream_t 
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<TYPE, 16>, p);
+  return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<TYPE, 16, MODE>, p);
+}
+
+template <int TYPE>
+cudaError_t launch_mma(const GemvParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
+  if (p.xch_wk >= 0 || p.xch_rk >= 0) return launch_mma_mode<TYPE, MMA_XCH>(p, grid, smem, st, pdl);
+  bool moe = p.nxv > 1;
+  for (int i = 0; i < p.nseg; ++i) moe |= p.seg[i].indirect != 0;
+  if (moe) return launch_mma_mode<TYPE, MMA_MOE>(p, grid, smem, st, pdl);
+  return launch_mma_mode<TYPE, MMA_PLAIN>(p, grid, smem, st, pdl);
 }
 
 // Integer tensor-core path (gemv_mma.cuh) for single-column Q4_K / Q6_K.

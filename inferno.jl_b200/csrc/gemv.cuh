@@ -493,9 +493,10 @@ __device__ __forceinline__ void tile_locate(const GemvParams& p, int tile, int& 
 // Address of row `row0` of segment `sg`.  Indirect (MoE) segments map row r to
 // row r % erows of expert eidx[r / erows]; a tile never straddles two experts.
 // An out-of-range id is reported and replaced by expert 0.
+template <bool IND = true>
 __device__ __forceinline__ const uint8_t* seg_row_ptr(const GemvParams& p, int sg, int row0) {
   const GemvSeg& s = p.seg[sg];
-  if (!s.indirect) return s.W + (long long)row0 * p.row_bytes;
+  if (!IND || !s.indirect) return s.W + (long long)row0 * p.row_bytes;
   const int slot = row0 / p.erows;
   int e = p.eidx[slot];
   if (e < 0 || e >= p.n_experts) {
@@ -508,13 +509,14 @@ __device__ __forceinline__ const uint8_t* seg_row_ptr(const GemvParams& p, int s
 // Producer warp of the GEMV kernels: one bulk copy per tile (two for paired
 // gate/up tiles) into the ring of stages.  Weights stream before
 // griddepcontrol.wait; dependents are released only after it.
+template <bool IND = true>
 __device__ __forceinline__ void gemv_producer(const GemvParams& p, uint64_t* full, uint64_t* empty, uint8_t* stage0,
                                               int lane, int n_items) {
   const int G = gridDim.x;
   const bool paired = (p.epi == EPI_SWIGLU);
   const int TR = p.TR, half_tr = TR / 2;
   bool waited = false;
-  if (p.eidx) {
+  if (IND && p.eidx) {
     // expert ids come from the preceding kernel: no weight prefetch before the wait
     pdl_wait();
     pdl_trigger();
@@ -534,7 +536,7 @@ __device__ __forceinline__ void gemv_producer(const GemvParams& p, uint64_t* ful
       uint32_t bytes = 0;
       uintptr_t a0 = 0;
       if (nrows > 0) {
-        const uintptr_t src = (uintptr_t)seg_row_ptr(p, sgr, row0);
+        const uintptr_t src = (uintptr_t)seg_row_ptr<IND>(p, sgr, row0);
         a0 = src & ~(uintptr_t)15;
         const uintptr_t a1 = (src + (long long)nrows * p.row_bytes + 15) & ~(uintptr_t)15;
         bytes = (uint32_t)(a1 - a0);

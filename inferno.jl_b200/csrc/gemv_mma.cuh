@@ -35,6 +35,20 @@
 namespace inf {
 
 constexpr int MMA_KS_BYTES = 256;     // B bytes per k step (8 columns x 32 k)
+// Kernel variants: the per-token GEMVs run MMA_PLAIN, whose code holds none
+// of the MoE (expert-indirect rows, several input vectors) or tensor-parallel
+// exchange paths -- every launch fetches its instructions cold, and unused
+// branches inlined into the hot path cost measurable time per launch.
+enum MmaMode : int { MMA_PLAIN = 0, MMA_MOE = 1, MMA_XCH = 2 };
+// Per-phase timestamps (GemvParams::trace) are compiled in only on request
+// (-DINFERNO_MMA_TRACE=1): they sit on the latency-critical path.
+#ifndef INFERNO_MMA_TRACE
+#define INFERNO_MMA_TRACE 0
+#endif
+constexpr bool MMA_TRACE = INFERNO_MMA_TRACE != 0;
+// The super-block bodies' outer loops are not unrolled: the per-layer GEMVs
+// are latency-bound and every launch fetches its code cold, so code size
+// matters more than loop overhead.
 
 __device__ __forceinline__ void imma_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -96,7 +110,7 @@ __device__ __forceinline__ int mma_exp2_scale(float vmax) {
   return max(-120, min(120, 30 - e));
 }
 
-template <int TYPE, int NW>
+template <int TYPE, int NW, int MODE>
 __device__ float gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, float* xsum, float* red,
                                    float* vmax, int tid) {
   const int n = p.inner;
@@ -106,7 +120,7 @@ __device__ float gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, 
   const float* x = p.x;
   float ss = 0.f, amax = 0.f;
   bool bad = false;
-  if (p.pro == PRO_RMSNORM && p.xch_rk >= 0) {
+  if (MODE == MMA_XCH && p.pro == PRO_RMSNORM && p.xch_rk >= 0) {
     // residual stream = x + the ranks' partials of sync point xch_rk, summed
     // in rank order (bit-identical on every rank); CTA 0 stores it for later
     // kernels.  Every word is polled until its tag is this sync's (bounded).
@@ -164,7 +178,7 @@ __device__ float gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, 
   } else if (p.pro == PRO_HEADNORM_GATE) {
     const int G = p.pro_group;
     const int per = G >> 5;
-#pragma unroll 1
+#pragma unroll
     for (int hh = w; hh < n / G; hh += NW) {
       float yv[8], zv[8], wv[8];
       float hs = 0.f;
@@ -189,7 +203,7 @@ __device__ float gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, 
         xf[hh * G + q * 32 + lane] = u;
       }
     }
-  } else if (nxv > 1) {
+  } else if (MODE == MMA_MOE && nxv > 1) {
     // several vectors (n % 32 == 0): a warp's 32 elements share one vector
     for (int i = tid; i < nxv * n; i += NT) {
       const int v = i / n;
@@ -226,11 +240,16 @@ __device__ float gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, 
   // limbs: one thread per quad (ks, cc) = 4 elements of each k-half
   const int nqv = n >> 3;
   const size_t xq_vec = (size_t)(n >> 8) * 8 * MMA_KS_BYTES;
+  const float up0 = ldexpf(1.0f, mma_exp2_scale(vmax[0]));
+  if (!(vmax[0] <= 3.0e38f)) bad = true;
   for (int qq = tid; qq < nxv * nqv; qq += NT) {
-    const int v = qq / nqv, q = qq - v * nqv;
-    const float vm = vmax[v];
-    if (!(vm <= 3.0e38f)) bad = true;
-    const float up = ldexpf(1.0f, mma_exp2_scale(vm));
+    const int v = MODE == MMA_MOE ? qq / nqv : 0, q = qq - v * nqv;
+    float up = up0;
+    if (MODE == MMA_MOE) {
+      const float vm = vmax[v];
+      if (!(vm <= 3.0e38f)) bad = true;
+      up = ldexpf(1.0f, mma_exp2_scale(vm));
+    }
     const int ks = q >> 2, cc = q & 3;
     const float* xfv = xf + (size_t)v * n;
     uint8_t* xqv = xq + v * xq_vec;
@@ -380,11 +399,11 @@ __device__ __forceinline__ void mma_sb_q6k(const uint8_t* ra, const uint8_t* rb,
   corr[1] = fmaf(32.0f * db, tb, corr[1]);
 }
 
-template <int TYPE, int NW>
+template <int TYPE, int NW, int MODE>
 __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid == 0) GEMV_TRACE(0);
+  if (MMA_TRACE && tid == 0) GEMV_TRACE(0);
   constexpr int BB = TYPE == T_Q4_K ? 144 : 210;
   constexpr int XS_PER_SB = TYPE == T_Q4_K ? 8 : 16;
   // layout: [full][empty][red 2*NW+4][vmax 16][kpart NW*16][xsum][xf][xq][stages]
@@ -395,7 +414,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
   float* kpart = vmax + 16;
   float* xsum = kpart + NW * 16;
   const int nsb = p.inner >> 8;
-  const int nxv = p.nxv;
+  const int nxv = MODE == MMA_MOE ? p.nxv : 1;
   float* xf = xsum + nxv * nsb * 16;
   uint8_t* xq = (uint8_t*)(xf + (size_t)nxv * p.inner);
   const size_t xq_vec = (size_t)nsb * 8 * MMA_KS_BYTES;
@@ -414,16 +433,18 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
   const int G = gridDim.x;
   const int n_items = (p.ntiles - (int)blockIdx.x + G - 1) / G;
   if (warp == NW) {
-    gemv_producer(p, full, empty, stage0, lane, n_items);
+    gemv_producer<MODE == MMA_MOE>(p, full, empty, stage0, lane, n_items);
     return;
   }
 
   pdl_wait();
-  if (tid == 0) GEMV_TRACE(2);
-  const float colscale = gemv_mma_prologue<TYPE, NW>(p, xf, xq, xsum, red, vmax, tid);
-  if (tid == 0) GEMV_TRACE(3);
+  if (MMA_TRACE && tid == 0) GEMV_TRACE(2);
+  const float colscale = gemv_mma_prologue<TYPE, NW, MODE>(p, xf, xq, xsum, red, vmax, tid);
+  if (MMA_TRACE && tid == 0) GEMV_TRACE(3);
   const bool nonfinite = *(volatile int*)&red[2 * NW] != 0;
-  const uint32_t xtag = p.xch_wk >= 0 ? (uint32_t)(*p.xch_seq + (unsigned long long)p.xch_wk + 1ull) : 0u;
+  const uint32_t xtag =
+      (MODE == MMA_XCH && p.xch_wk >= 0) ? (uint32_t)(*p.xch_seq + (unsigned long long)p.xch_wk + 1ull) : 0u;
+  const float fscale0 = nonfinite ? __int_as_float(0x7fc00000) : colscale * ldexpf(1.0f, -mma_exp2_scale(vmax[0]));
 
   const bool paired = (p.epi == EPI_SWIGLU);
   const int nrg = p.TR >> 4;            // 16-row groups per tile
@@ -437,26 +458,28 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
   for (int it = 0; it < n_items; ++it) {
     const int s = it % p.stages;
     if (!mbar_wait(&full[s], (it / p.stages) & 1, p.err)) return;
+    if (MMA_TRACE && tid == 0 && it == 0) GEMV_TRACE(4);
     int sg, row0;
     tile_locate(p, blockIdx.x + it * G, sg, row0);
     const uint8_t* st = stage0 + (long long)s * p.stage_bytes;
     const uint8_t *ra, *rb;
     if (paired) {
-      const uint32_t m0 = (uint32_t)((uintptr_t)seg_row_ptr(p, 0, row0) & 15);
-      const uint32_t m1 = (uint32_t)((uintptr_t)seg_row_ptr(p, 1, row0) & 15);
+      const uint32_t m0 = (uint32_t)((uintptr_t)seg_row_ptr<MODE == MMA_MOE>(p, 0, row0) & 15);
+      const uint32_t m1 = (uint32_t)((uintptr_t)seg_row_ptr<MODE == MMA_MOE>(p, 1, row0) & 15);
       ra = st + m0 + (long long)(rg * 8 + g) * p.row_bytes;
       rb = st + p.part1_off + m1 + (long long)(rg * 8 + g) * p.row_bytes;
     } else {
-      const uint32_t m0 = (uint32_t)((uintptr_t)seg_row_ptr(p, sg, row0) & 15);
+      const uint32_t m0 = (uint32_t)((uintptr_t)seg_row_ptr<MODE == MMA_MOE>(p, sg, row0) & 15);
       ra = st + m0 + (long long)(rg * 16 + g) * p.row_bytes;
       rb = ra + 8ll * p.row_bytes;
     }
     // input vector of this tile and its fixed-point descale
-    const int slot = nxv > 1 ? p.seg[sg].xslot0 + row0 / p.erows : 0;
+    const int slot = (MODE == MMA_MOE && nxv > 1) ? p.seg[sg].xslot0 + row0 / p.erows : 0;
     const uint8_t* xq_t = xq + slot * xq_vec;
     const float* xsum_t = xsum + slot * nsb * 16;
-    const float fscale = nonfinite ? __int_as_float(0x7fc00000)
-                                   : colscale * ldexpf(1.0f, -mma_exp2_scale(vmax[slot]));
+    const float fscale = (MODE == MMA_MOE && slot) ? (nonfinite ? __int_as_float(0x7fc00000)
+                                                                : colscale * ldexpf(1.0f, -mma_exp2_scale(vmax[slot])))
+                                                   : fscale0;
     float acc[2] = {0.f, 0.f}, corr[2] = {0.f, 0.f};
     for (int sb = wk; sb < nsb; sb += nkg) {
       if constexpr (TYPE == T_Q4_K)
@@ -468,6 +491,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
+    if (MMA_TRACE && tid == 0 && it == 0) GEMV_TRACE(5);
 
     // quad reduction: lane c holds limb c of the integer dots and a share of
     // the offset terms
@@ -507,7 +531,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
           if (p.epi == EPI_ARGMAX) {
             if (t > best_v || (t == best_v && row < best_i)) { best_v = t; best_i = row; }
             if (p.seg[sg].y) p.seg[sg].y[row] = t;
-          } else if (p.xch_wk >= 0) {
+          } else if (MODE == MMA_XCH && p.xch_wk >= 0) {
             // this rank's partial of sync point xch_wk, to every rank, tagged
             const size_t off = ((size_t)(p.xch_wk & 1) * p.xch_n + p.xch_rank) * p.seg[0].rows + row;
             const unsigned long long wv = ((unsigned long long)xtag << 32) | __float_as_uint(t);
@@ -521,7 +545,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
       }
     }
   }
-  if (tid == 0) GEMV_TRACE(6);
+  if (MMA_TRACE && tid == 0) GEMV_TRACE(6);
   if (p.epi == EPI_ARGMAX && wk == 0) {
     float v = best_v;
     int i = best_i;
