@@ -10,13 +10,16 @@ namespace inf {
 
 // ggml type ids (GGUF spec; Inferno.jl src/GGUF.jl:25-60)
 enum GgmlType : int {
-  T_F32 = 0, T_F16 = 1, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16
+  T_F32 = 0, T_F16 = 1, T_Q8_0 = 8, T_Q4_K = 12, T_Q5_K = 13, T_Q6_K = 14, T_IQ2_XXS = 16,
+  // engine-internal: Q6_K bytes regrouped per 16 rows for the tensor-core
+  // GEMV (gemv_mma.cuh); same size, never visible at the C ABI
+  T_Q6_KR = 114
 };
 
 __host__ __device__ constexpr int qk_of(int t) { return t == T_Q8_0 ? 32 : (t == T_F32 || t == T_F16) ? 1 : 256; }
 __host__ __device__ constexpr int bb_of(int t) {
   return t == T_F32 ? 4 : t == T_F16 ? 2 : t == T_Q8_0 ? 34 : t == T_Q4_K ? 144 : t == T_Q5_K ? 176
-       : t == T_Q6_K ? 210 : t == T_IQ2_XXS ? 66 : 0;
+       : (t == T_Q6_K || t == T_Q6_KR) ? 210 : t == T_IQ2_XXS ? 66 : 0;
 }
 inline bool type_supported(int t) {
   return t == T_F32 || t == T_Q8_0 || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K || t == T_IQ2_XXS;

@@ -99,6 +99,7 @@ struct InfernoEngine {
   // (sharded by the host) and rows [tp_rank*V/tp, ...) of the lm_head
   ncclComm_t comm = nullptr;
   inf::DevTensor lm_view;
+  inf::DevTensor lm_packed;         // tied lm_head regrouped for the tensor-core GEMV (T_Q6_KR)
   float* logits_local = nullptr;
   // fused tensor-parallel exchange over NVLink peer memory (xch); when off
   // (INFERNO_TP_NCCL=1 or a GEMV outside the tensor-core path) the residual
@@ -134,6 +135,7 @@ struct InfernoEngine {
   unsigned ablate = 0;           // debug: kernel classes left out (INFERNO_B200_ABLATE)
   // persistent decode kernel (decode.cu)
   bool persistent = false;
+  bool repack = false;           // Q6_K GEMV matrices regrouped (T_Q6_KR)
   inf::PkStage* pk_stages = nullptr;
   int pk_nstages = 0;
   size_t pk_smem = 0;
@@ -601,7 +603,7 @@ int setup_xch(InfernoEngine* e) {
   const char* nc = getenv("INFERNO_TP_NCCL");
   if ((nc && atoi(nc) != 0) || e->dump || n > 8 || H > 8192) return 0;
   auto ok = [](const DevTensor* t, int64_t inner) {
-    return t && (t->type == T_Q4_K || t->type == T_Q6_K) && inner % 256 == 0;
+    return t && (t->type == T_Q4_K || t->type == T_Q6_K || t->type == T_Q6_KR) && inner % 256 == 0;
   };
   bool eligible = ok(e->lm_head, H);
   for (auto& L : e->layers) {
@@ -746,6 +748,26 @@ int inferno_engine_finalize(InfernoEngine* e) {
   if ((rc = require(e, "output_norm.weight", &e->out_norm, T_F32))) return rc;
   e->lm_head = find(e, "output.weight");
   if (!e->lm_head) e->lm_head = e->embd;   // tied (src/LoaderCPU.jl:358-371)
+  // Q6_K matrices of the single-column GEMVs are regrouped per 16 rows for
+  // the tensor-core path (aligned 16-byte loads; the same bytes and results).
+  // The persistent kernel reads GGUF rows: no regrouping there.
+  {
+    const char* nr = getenv("INFERNO_NO_REPACK");
+    const char* pe = getenv("INFERNO_B200_PERSISTENT");
+    e->repack = !(nr && atoi(nr) != 0) && !(pe && atoi(pe) != 0);
+  }
+  if (e->repack && e->lm_head->type == T_Q6_K && e->lm_head->rows() % 16 == 0 && c.hidden_size % 256 == 0 &&
+      (c.tp_size == 1 || (c.vocab_size / c.tp_size) % 16 == 0)) {
+    e->lm_packed = *e->lm_head;
+    void* d = nullptr;
+    if (cudaMalloc(&d, (e->lm_head->bytes + 255) / 256 * 256) != cudaSuccess)
+      return set_error(INFERNO_ENOMEM, "lm_head regrouping: cudaMalloc(%zu) failed", e->lm_head->bytes);
+    e->allocs.push_back(d);
+    if ((rc = launch_repack_q6k(e->lm_head->d, d, (int)e->lm_head->rows(), c.hidden_size, e->st))) return rc;
+    e->lm_packed.d = d;
+    e->lm_packed.type = T_Q6_KR;
+    e->lm_head = &e->lm_packed;
+  }
   if (c.tp_size > 1) {
     if (c.vocab_size % c.tp_size || e->lm_head->rows() != c.vocab_size)
       return set_error(INFERNO_EINVAL, "tensor parallel: vocab %d not divisible by %d", c.vocab_size, c.tp_size);
@@ -830,6 +852,19 @@ int inferno_engine_finalize(InfernoEngine* e) {
       return rc;
     if (L.ffn_gate->rows() != c.intermediate_size || L.ffn_down->ne[0] != c.intermediate_size)
       return set_error(INFERNO_EINVAL, "layer %d: FFN dims do not match the config", i);
+    if (e->repack && L.ffn_down->type == T_Q6_K && L.ffn_down->rows() % 16 == 0 && c.intermediate_size % 256 == 0) {
+      void* d = nullptr;
+      if (cudaMalloc(&d, (L.ffn_down->bytes + 255) / 256 * 256) != cudaSuccess)
+        return set_error(INFERNO_ENOMEM, "ffn_down regrouping: cudaMalloc failed");
+      if ((rc = launch_repack_q6k(L.ffn_down->d, d, (int)L.ffn_down->rows(), c.intermediate_size, e->st))) {
+        cudaFree(d);
+        return rc;
+      }
+      INF_CUDA_TRY(cudaStreamSynchronize(e->st));
+      cudaFree(L.ffn_down->d);
+      L.ffn_down->d = d;
+      L.ffn_down->type = T_Q6_KR;
+    }
   }
   const int H = c.hidden_size;
   if ((rc = dalloc(e, &e->x, H)) || (rc = dalloc(e, &e->qkv, e->C)) || (rc = dalloc(e, &e->z, e->di)) ||

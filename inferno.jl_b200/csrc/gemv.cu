@@ -192,14 +192,35 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
   p.part1_off = (int)((((size_t)(TR / 2) * row_bytes + 32 + 15) / 16) * 16);
   const size_t smem = fixed + (size_t)p.stages * stage_bytes;
   const int grid = std::min(ntiles, sms);
-  cudaError_t e = c.type == T_Q4_K ? launch_mma<T_Q4_K>(p, grid, smem, st, pdl) : launch_mma<T_Q6_K>(p, grid, smem, st, pdl);
+  cudaError_t e = c.type == T_Q4_K   ? launch_mma<T_Q4_K>(p, grid, smem, st, pdl)
+                  : c.type == T_Q6_KR ? launch_mma<T_Q6_KR>(p, grid, smem, st, pdl)
+                                      : launch_mma<T_Q6_K>(p, grid, smem, st, pdl);
   if (e != cudaSuccess) return set_error(-2, "gemv launch failed: %s", cudaGetErrorString(e));
   return 0;
 }
 
 }  // namespace
 
+int launch_repack_q6k(const void* src, void* dst, int rows, int inner, cudaStream_t st) {
+  if (rows <= 0 || rows % 16 || inner <= 0 || inner % 256)
+    return set_error(-1, "repack: Q6_K %d x %d is not a multiple of 16 rows x 256 columns", rows, inner);
+  repack_q6k_kernel<<<dim3(rows / 16, inner / 256), 32, 0, st>>>((const uint8_t*)src, (uint8_t*)dst, inner / 256);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : set_error(-2, "repack launch: %s", cudaGetErrorString(e));
+}
+
 int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
+  if (c.type == T_Q6_KR) {
+    // regrouped Q6_K exists only for the single-column tensor-core path
+    if (c.nb != 1 || c.epi == EPI_SWIGLU || c.inner % 256 || c.nxv != 1)
+      return set_error(-1, "gemv: regrouped Q6_K needs a single-column, non-paired call");
+    for (int i = 0; i < c.nmats; ++i)
+      if (c.mats[i].rows % 16 || c.mats[i].indirect) return set_error(-1, "gemv: regrouped Q6_K rows");
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int rc = plan_launch_mma(c, dev, num_sms(dev), st, pdl);
+    return rc > 0 ? set_error(-1, "gemv: regrouped Q6_K %d-column rows do not fit shared memory", c.inner) : rc;
+  }
   if (!type_supported(c.type) || c.nmats < 1 || c.nmats > GEMV_MAX_SEG || c.nb < 1)
     return set_error(-1, "gemv: bad type/mats/batch (type=%d nmats=%d nb=%d)", c.type, c.nmats, c.nb);
   const int qk = qk_of(c.type), bb = bb_of(c.type);

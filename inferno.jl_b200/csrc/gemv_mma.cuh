@@ -399,12 +399,113 @@ __device__ __forceinline__ void mma_sb_q6k(const uint8_t* ra, const uint8_t* rb,
   corr[1] = fmaf(32.0f * db, tb, corr[1]);
 }
 
+// Q6_K regrouped per 16 rows (T_Q6_KR): for row group G and super-block sb a
+// 3360-byte block (= 16 x 210) holds
+//   [6 chunks][32 lanes][16 B]  the ql / qh words lane (g, c) reads for rows
+//                               g and g + 8 (12 words each, order below),
+//   [16 rows][16 B]             int8 scales,   [16 rows][2 B]  fp16 d.
+// Word w of a row: w < 8 -> ql at 64*(w>>2) + 32*((w>>1)&1) + 16*(w&1) + 4c,
+// w >= 8 -> qh at 128 + 32*((w-8)>>1) + 16*((w-8)&1) + 4c (Dequant.jl:585-596
+// offsets).  Every load is an aligned, conflict-free 16-byte access.
+constexpr int Q6R_BLOCK = 3360;
+
+__device__ __forceinline__ void mma_sb_q6kr(const uint8_t* gb, const uint8_t* xq_sb, const float* xs_sb, int lane,
+                                            float (&acc)[2], float (&corr)[2]) {
+  const int c = lane & 3, g = lane >> 2;
+  uint32_t wa[12], wb[12];
+  {
+    const uint4* ch = (const uint4*)gb;
+    uint4 t[6];
+#pragma unroll
+    for (int i = 0; i < 6; ++i) t[i] = ch[i * 32 + lane];
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      wa[4 * i] = t[i].x; wa[4 * i + 1] = t[i].y; wa[4 * i + 2] = t[i].z; wa[4 * i + 3] = t[i].w;
+      wb[4 * i] = t[3 + i].x; wb[4 * i + 1] = t[3 + i].y; wb[4 * i + 2] = t[3 + i].z; wb[4 * i + 3] = t[3 + i].w;
+    }
+  }
+  const uint4 sa4 = *(const uint4*)(gb + 3072 + g * 16), sb4 = *(const uint4*)(gb + 3072 + (g + 8) * 16);
+  const uint32_t sca[4] = {sa4.x, sa4.y, sa4.z, sa4.w}, scb[4] = {sb4.x, sb4.y, sb4.z, sb4.w};
+  int S0 = 0, S1 = 0;
+#pragma unroll
+  for (int n6 = 0; n6 < 2; ++n6) {
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+#pragma unroll
+      for (int hi = 0; hi < 2; ++hi) {
+        const int k = kk + 2 * hi;
+        const int sh = 4 * hi;
+        const uint32_t la0 = wa[n6 * 4 + kk * 2], la1 = wa[n6 * 4 + kk * 2 + 1];
+        const uint32_t lb0 = wb[n6 * 4 + kk * 2], lb1 = wb[n6 * 4 + kk * 2 + 1];
+        const uint32_t ua0 = ((la0 >> sh) & 0x0f0f0f0fu) | qh_bits(wa[8 + n6 * 2], k);
+        const uint32_t ua1 = ((la1 >> sh) & 0x0f0f0f0fu) | qh_bits(wa[8 + n6 * 2 + 1], k);
+        const uint32_t ub0 = ((lb0 >> sh) & 0x0f0f0f0fu) | qh_bits(wb[8 + n6 * 2], k);
+        const uint32_t ub1 = ((lb1 >> sh) & 0x0f0f0f0fu) | qh_bits(wb[8 + n6 * 2 + 1], k);
+        const uint2 bv = *(const uint2*)(xq_sb + (4 * n6 + k) * MMA_KS_BYTES + lane * 8);
+        int d[4];
+        imma_k32(d, ua0, ub0, ua1, ub1, bv.x, bv.y);
+        const int is = 8 * n6 + 2 * k;
+        const int s0a = sbyte<0>(sca[is >> 2] >> (8 * (is & 3))), s1a = sbyte<0>(sca[is >> 2] >> (8 * (is & 3) + 8));
+        const int s0b = sbyte<0>(scb[is >> 2] >> (8 * (is & 3))), s1b = sbyte<0>(scb[is >> 2] >> (8 * (is & 3) + 8));
+        S0 += s0a * d[0] + s1a * d[1];
+        S1 += s0b * d[2] + s1b * d[3];
+      }
+    }
+  }
+  const float da = h2f_bits(*(const uint16_t*)(gb + 3328 + g * 2));
+  const float db = h2f_bits(*(const uint16_t*)(gb + 3328 + (g + 8) * 2));
+  acc[0] = fmaf(da, (float)S0, acc[0]);
+  acc[1] = fmaf(db, (float)S1, acc[1]);
+  const float4 X = *(const float4*)(xs_sb + 4 * c);
+  const uint32_t wsa = c == 0 ? sca[0] : c == 1 ? sca[1] : c == 2 ? sca[2] : sca[3];
+  const uint32_t wsb = c == 0 ? scb[0] : c == 1 ? scb[1] : c == 2 ? scb[2] : scb[3];
+  const float ta = (float)sbyte<0>(wsa) * X.x + (float)sbyte<1>(wsa) * X.y + (float)sbyte<2>(wsa) * X.z +
+                   (float)sbyte<3>(wsa) * X.w;
+  const float tb = (float)sbyte<0>(wsb) * X.x + (float)sbyte<1>(wsb) * X.y + (float)sbyte<2>(wsb) * X.z +
+                   (float)sbyte<3>(wsb) * X.w;
+  corr[0] = fmaf(32.0f * da, ta, corr[0]);
+  corr[1] = fmaf(32.0f * db, tb, corr[1]);
+}
+
+// Regroup a Q6_K matrix (rows % 16 == 0) into the T_Q6_KR layout: one CTA of
+// 32 threads per (16-row group, super-block).
+__global__ void __launch_bounds__(32) repack_q6k_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                                        int nsb) {
+  const int G = blockIdx.x, sb = blockIdx.y, L = threadIdx.x;
+  const int g = L >> 2, c = L & 3;
+  const size_t rb = (size_t)nsb * 210;
+  uint8_t* out = dst + ((size_t)G * nsb + sb) * Q6R_BLOCK;
+  auto word = [&](int row, int w) -> uint32_t {
+    const uint8_t* b = src + (size_t)row * rb + (size_t)sb * 210;
+    const int off = w < 8 ? 64 * (w >> 2) + 32 * ((w >> 1) & 1) + 16 * (w & 1) + 4 * c
+                          : 128 + 32 * ((w - 8) >> 1) + 16 * ((w - 8) & 1) + 4 * c;
+    return (uint32_t)b[off] | ((uint32_t)b[off + 1] << 8) | ((uint32_t)b[off + 2] << 16) | ((uint32_t)b[off + 3] << 24);
+  };
+  const int ra = 16 * G + g, rbw = ra + 8;
+#pragma unroll
+  for (int i = 0; i < 6; ++i) {
+    uint32_t v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int w = 4 * i + j;
+      v[j] = w < 12 ? word(ra, w) : word(rbw, w - 12);
+    }
+    *(uint4*)(out + (i * 32 + L) * 16) = make_uint4(v[0], v[1], v[2], v[3]);
+  }
+  if (L < 16) {
+    const uint8_t* b = src + (size_t)(16 * G + L) * rb + (size_t)sb * 210;
+    for (int j = 0; j < 16; ++j) out[3072 + L * 16 + j] = b[192 + j];
+    out[3328 + L * 2] = b[208];
+    out[3328 + L * 2 + 1] = b[209];
+  }
+}
+
 template <int TYPE, int NW, int MODE>
 __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (MMA_TRACE && tid == 0) GEMV_TRACE(0);
-  constexpr int BB = TYPE == T_Q4_K ? 144 : 210;
+  constexpr int BB = TYPE == T_Q4_K ? 144 : TYPE == T_Q6_KR ? Q6R_BLOCK : 210;
   constexpr int XS_PER_SB = TYPE == T_Q4_K ? 8 : 16;
   // layout: [full][empty][red 2*NW+4][vmax 16][kpart NW*16][xsum][xf][xq][stages]
   uint64_t* full = (uint64_t*)smem;
@@ -468,6 +569,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
       const uint32_t m1 = (uint32_t)((uintptr_t)seg_row_ptr<MODE == MMA_MOE>(p, 1, row0) & 15);
       ra = st + m0 + (long long)(rg * 8 + g) * p.row_bytes;
       rb = st + p.part1_off + m1 + (long long)(rg * 8 + g) * p.row_bytes;
+    } else if (TYPE == T_Q6_KR) {
+      // 16-row groups of nsb 3360-byte blocks, 16-byte aligned
+      ra = st + (long long)rg * nsb * Q6R_BLOCK;
+      rb = ra;
     } else {
       const uint32_t m0 = (uint32_t)((uintptr_t)seg_row_ptr<MODE == MMA_MOE>(p, sg, row0) & 15);
       ra = st + m0 + (long long)(rg * 16 + g) * p.row_bytes;
@@ -485,6 +590,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
       if constexpr (TYPE == T_Q4_K)
         mma_sb_q4k(ra + sb * BB, rb + sb * BB, xq_t + (size_t)sb * 8 * MMA_KS_BYTES, xsum_t + sb * XS_PER_SB, lane,
                    acc, corr);
+      else if constexpr (TYPE == T_Q6_KR)
+        mma_sb_q6kr(ra + sb * BB, xq_t + (size_t)sb * 8 * MMA_KS_BYTES, xsum_t + sb * XS_PER_SB, lane, acc, corr);
       else
         mma_sb_q6k(ra + sb * BB, rb + sb * BB, xq_t + (size_t)sb * 8 * MMA_KS_BYTES, xsum_t + sb * XS_PER_SB, lane,
                    acc, corr);

@@ -118,3 +118,21 @@ def test_config1_greedy_identity():
     orc = O.OracleModel(spec, T)
     want = orc.generate(prompt, 64)
     assert got == want
+
+
+def test_q6k_regrouping_is_bitwise_neutral(tiny, monkeypatch):
+    """The engine regroups Q6_K ffn_down / lm_head bytes per 16 rows for the
+    tensor-core GEMV (T_Q6_KR): the same arithmetic in the same order, so
+    logits are bit-identical to the GGUF-layout path."""
+    spec, T, _ = tiny
+    prompt = S.tokens(13, 6, spec.vocab)
+    monkeypatch.setenv("INFERNO_NO_REPACK", "1")
+    m = Model(spec, T)
+    am0, lg0 = m.forward(prompt, 0)
+    m.close()
+    monkeypatch.delenv("INFERNO_NO_REPACK")
+    m = Model(spec, T)
+    am1, lg1 = m.forward(prompt, 0)
+    m.close()
+    assert am0 == am1
+    assert np.array_equal(lg0, lg1)
