@@ -299,6 +299,144 @@ __device__ float gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, 
   return colscale;
 }
 
+// Register prologue (RMSNorm or plain input, one vector): thread u holds the
+// four consecutive elements 4u..4u+3 from the load to the limb stores, so no
+// fp32 staging pass is needed; the sub-blocks (32 elements for Q4_K, 16 for
+// Q6_K) are 8 / 4 consecutive lanes, summed with shuffles.  Same outputs as
+// gemv_mma_prologue.
+template <int TYPE, int NW, int MODE>
+__device__ float gemv_mma_prologue_reg(const GemvParams& p, uint8_t* xq, float* xsum, float* red, float* vmax,
+                                       int tid) {
+  constexpr int NT = NW * 32;
+  constexpr int IT = 8192 / 4 / NT;          // float4 items per thread (n <= 8192)
+  const int n = p.inner, nf4 = n >> 2;
+  const int lane = tid & 31, w = tid >> 5;
+  const bool rms = p.pro == PRO_RMSNORM;
+  const bool xch = MODE == MMA_XCH && p.xch_rk >= 0;
+  bool bad = false;
+  float4 v[IT];
+  float ss = 0.f, amax = 0.f;
+  uint32_t tag = 0;
+  const unsigned long long* parts = nullptr;
+  if (xch) {
+    tag = (uint32_t)(*p.xch_seq + (unsigned long long)p.xch_rk + 1ull);
+    parts = p.xch_parts[p.xch_rank] + (size_t)(p.xch_rk & 1) * p.xch_n * n;
+  }
+#pragma unroll
+  for (int j = 0; j < IT; ++j) {
+    const int u = tid + j * NT;
+    v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (u < nf4) v[j] = xch ? __ldcg((const float4*)p.x + u) : ((const float4*)p.x)[u];
+  }
+  if (xch) {
+    // residual = x + the ranks' tagged partials of sync xch_rk (rank order)
+    for (int r = 0; r < p.xch_n; ++r) {
+#pragma unroll
+      for (int j = 0; j < IT; ++j) {
+        const int u = tid + j * NT;
+        if (u >= nf4) continue;
+        float pr[4];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const unsigned long long* a = parts + (size_t)r * n + 4 * u + t;
+          unsigned long long wv = ld_relaxed_sys_u64(a);
+          unsigned it = 0;
+          while ((uint32_t)(wv >> 32) != tag) {
+            if (++it > (1u << 22)) {
+              if (p.err) atomicExch(p.err, DERR_MBAR_TIMEOUT);
+              bad = true;
+              break;
+            }
+            if (it > 1024) __nanosleep(32);
+            wv = ld_relaxed_sys_u64(a);
+          }
+          pr[t] = __uint_as_float((uint32_t)wv);
+        }
+        v[j].x += pr[0]; v[j].y += pr[1]; v[j].z += pr[2]; v[j].w += pr[3];
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < IT; ++j) {
+    const int u = tid + j * NT;
+    if (u >= nf4) continue;
+    if (xch && blockIdx.x == 0) ((float4*)p.x_next)[u] = v[j];
+    if (rms) {
+      ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
+      const float4 w4 = ((const float4*)p.pro_w)[u];
+      v[j].x *= w4.x; v[j].y *= w4.y; v[j].z *= w4.z; v[j].w *= w4.w;
+    }
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+  }
+  ss = warp_sum(ss);
+  amax = warp_max(amax);
+  if (lane == 0) {
+    red[w] = ss;
+    atomicMax((int*)&vmax[0], __float_as_int(amax));
+  }
+  named_bar_sync(1, NT);
+  float colscale = 1.0f;
+  if (rms) {
+    float tss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NW; ++i) tss += red[i];
+    colscale = 1.0f / sqrtf(tss / (float)n + p.eps);
+  }
+  const float vm = vmax[0];
+  if (!(vm <= 3.0e38f)) bad = true;
+  const float up = ldexpf(1.0f, mma_exp2_scale(vm));
+#pragma unroll
+  for (int j = 0; j < IT; ++j) {
+    const int u = tid + j * NT;
+    if (j * NT >= nf4) break;                // whole warps leave together
+    const bool ok = u < nf4;
+    const int e0 = 4 * u;
+    // (k step, lane quad, k half) of elements e0..e0+3 (inverse of mma_elem)
+    const int sb = e0 >> 8, r = e0 & 255;
+    int ks, cc, hp;
+    if (TYPE == T_Q4_K) {
+      ks = sb * 8 + 2 * (r >> 6) + ((r >> 2) & 1);
+      cc = (r >> 3) & 3;
+      hp = (r >> 5) & 1;
+    } else {
+      ks = sb * 8 + 4 * (r >> 7) + ((r >> 5) & 3);
+      cc = (r >> 2) & 3;
+      hp = (r >> 4) & 1;
+    }
+    const float vv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+    uint32_t limb[4] = {0u, 0u, 0u, 0u};
+    float sum = 0.f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      if (vv[t] != vv[t]) bad = true;
+      int xi = __float2int_rn(vv[t] * up);
+      sum += (float)xi;
+#pragma unroll
+      for (int l = 0; l < 3; ++l) {
+        const int d = (int)(int8_t)(xi & 0xff);
+        limb[l] |= (uint32_t)(d & 0xff) << (8 * t);
+        xi = (xi - d) >> 8;
+      }
+      limb[3] |= (uint32_t)(xi & 0xff) << (8 * t);
+    }
+    if (ok) {
+#pragma unroll
+      for (int l = 0; l < 4; ++l) {
+        const uint2 v2 = hp == 0 ? make_uint2(limb[l], 0u) : make_uint2(0u, limb[l]);
+        *(uint2*)(xq + (size_t)ks * MMA_KS_BYTES + (2 * l + hp) * 32 + cc * 8) = v2;
+      }
+    }
+    // sub-block sum: 8 (Q4_K) / 4 (Q6_K) consecutive items
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if (TYPE == T_Q4_K) sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    if (ok && (u & (TYPE == T_Q4_K ? 7 : 3)) == 0) xsum[TYPE == T_Q4_K ? (e0 >> 5) : (e0 >> 4)] = sum;
+  }
+  if (bad) *(volatile int*)&red[2 * NW] = 1;
+  named_bar_sync(1, NT);
+  return colscale;
+}
+
 // ---------------------------------------------------------------------------
 // super-block bodies: rows g (ra) and g+8 (rb) of the warp's 16, lane quad c.
 // S[0], S[1]: exact integer sums for the two rows; corr: fp32 offset terms.
@@ -540,7 +678,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
 
   pdl_wait();
   if (MMA_TRACE && tid == 0) GEMV_TRACE(2);
-  const float colscale = gemv_mma_prologue<TYPE, NW, MODE>(p, xf, xq, xsum, red, vmax, tid);
+  const bool reg_pro = MODE != MMA_MOE && (p.pro == PRO_RMSNORM || p.pro == PRO_NONE);
+  const float colscale = reg_pro ? gemv_mma_prologue_reg<TYPE == T_Q6_KR ? T_Q6_K : TYPE, NW, MODE>(p, xq, xsum, red,
+                                                                                                     vmax, tid)
+                                 : gemv_mma_prologue<TYPE, NW, MODE>(p, xf, xq, xsum, red, vmax, tid);
   if (MMA_TRACE && tid == 0) GEMV_TRACE(3);
   const bool nonfinite = *(volatile int*)&red[2 * NW] != 0;
   const uint32_t xtag =
