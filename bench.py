@@ -300,10 +300,11 @@ BIG = {
     # tensor parallel over the launched ranks (strong scaling: one sequence)
     "config4": dict(spec="qwen35-9b", prompt=2048, ndec=256, ctx=32768 + 128, tp=True,
                     metric="decode tokens/s @batch1 (Qwen3.5-9B-shaped hybrid, Q4_K_M mix, tensor parallel)"),
-    # 35B-A3B-shaped MoE hybrid at batch 1, ctx 4096; one
-    # engine per GPU (expert parallelism is not built: N replicas)
-    "config5": dict(spec="qwen35-35b-a3b", prompt=32, ndec=128, ctx=4096 + 128, tp=False,
-                    metric="decode tokens/s @batch1 (Qwen3.5-35B-A3B-shaped MoE hybrid, IQ2_XXS/Q4_K experts)"),
+    # 35B-A3B-shaped MoE hybrid at batch 1, ctx 4096;
+    # expert parallel over the launched ranks (strong scaling: one sequence)
+    "config5": dict(spec="qwen35-35b-a3b", prompt=32, ndec=128, ctx=4096 + 128, tp=True,
+                    metric="decode tokens/s @batch1 (Qwen3.5-35B-A3B-shaped MoE hybrid, IQ2_XXS/Q4_K experts, "
+                           "expert parallel)"),
 }
 
 
@@ -378,7 +379,8 @@ def run_big(args):
             "data": "synthetic (seeded; rows of each matrix drawn from 256 quantized N(0,0.02) rows)",
             "config": {"workload": f"{W['spec']}: {P}-token prompt (untimed), {ND} greedy decode tokens @batch1",
                        "model": W["spec"], "global_batch": 1, "seq_len": P + ND,
-                       "parallelism": f"tp{ws}" if tp else ("replicas" if ws > 1 else "single"),
+                       "parallelism": (("ep" if spec.n_experts else "tp") + str(ws)) if tp else
+                                      ("replicas" if ws > 1 else "single"),
                        "l2": "weights per token >> 126 MB L2 (no flush needed)"},
             "clocks": clk, "gpu_launches": m.kernels_per_token() * ND,
             "token_roofline": {"algorithmic_bytes_per_token": tok_bytes, "achieved_gbs_per_gpu": per_gpu_gbs,

@@ -104,6 +104,8 @@ struct InfernoEngine {
   // fused tensor-parallel exchange over NVLink peer memory (xch); when off
   // (INFERNO_TP_NCCL=1 or a GEMV outside the tensor-core path) the residual
   // is summed with ncclAllReduce
+  bool ep = false;                  // expert parallel: ranks split the MoE experts, the rest is replicated
+  bool tp = false;                  // tensor parallel: ranks hold shards of every layer
   bool xch = false;
   float* x2 = nullptr;              // second residual buffer (alternates per sync point)
   float* xcur = nullptr;            // buffer holding the current residual while enqueueing
@@ -246,7 +248,7 @@ GemvMat M(DevTensor* t, float* y) { return GemvMat{t->d, y, (int)t->rows()}; }
 // x completes x + sum_r partial_r on every rank.
 int residual_epi(InfernoEngine* e) {
   if (e->xch) return EPI_XCH_WRITE;
-  return (e->cfg.tp_size > 1 && e->cfg.tp_rank != 0) ? EPI_STORE : EPI_ADD;
+  return (e->tp && e->cfg.tp_rank != 0) ? EPI_STORE : EPI_ADD;
 }
 
 // After the GEMVs that consumed a pending exchange: the completed residual now
@@ -258,7 +260,7 @@ void xch_commit(InfernoEngine* e) {
 }
 
 int tp_sum_x(InfernoEngine* e) {
-  if (e->cfg.tp_size <= 1 || e->xch) return 0;
+  if (!e->tp || e->xch) return 0;
   ncclResult_t r = ncclAllReduce(e->x, e->x, (size_t)e->cfg.hidden_size, ncclFloat, ncclSum, e->comm, e->st);
   if (r != ncclSuccess) return set_error(INFERNO_ENCCL, "all-reduce of the residual: %s", ncclGetErrorString(r));
   return 0;
@@ -271,13 +273,16 @@ int tp_sum_x(InfernoEngine* e) {
 int enqueue_moe(InfernoEngine* e, LayerBind& L, bool pdl) {
   const InfernoConfig& c = e->cfg;
   const int H = c.hidden_size, E = c.n_experts, K = c.n_experts_used, Ie = c.expert_ffn;
+  // expert parallel: this rank holds experts [ebase, ebase + El)
+  const int El = e->ep ? E / c.tp_size : E, ebase = e->ep ? c.tp_rank * El : 0;
+  const bool lead = !e->ep || c.tp_rank == 0;
   const bool shared = L.sh_gate != nullptr;
   const float* pn = (const float*)L.post_norm->d;
   int rc;
   if ((rc = gemv(e, L.router->type, H, {M(L.router, e->moe_logits)}, e->x, PRO_RMSNORM, pn, nullptr, 0, EPI_STORE,
                  nullptr, pdl)))
     return rc;
-  if ((rc = launch_moe_topk(e->moe_logits, E, K, e->moe_idx, e->moe_w, e->err, e->st, pdl))) return rc;
+  if ((rc = launch_moe_topk(e->moe_logits, E, K, e->moe_idx, e->moe_w, e->err, ebase, El, e->st, pdl))) return rc;
   mark(e, K_GEMV);
   {
     GemvCall g;
@@ -294,9 +299,9 @@ int enqueue_moe(InfernoEngine* e, LayerBind& L, bool pdl) {
     g.epi = EPI_SWIGLU;
     g.err = e->err;
     g.eidx = e->moe_idx;
-    g.estride = (long long)(L.exp_gate->bytes / E);
+    g.estride = (long long)(L.exp_gate->bytes / El);
     g.erows = Ie;
-    g.n_experts = E;
+    g.n_experts = El;
     if ((rc = launch_gemv(g, e->st, pdl))) return rc;
     mark(e, K_GEMV);
   }
@@ -318,14 +323,21 @@ int enqueue_moe(InfernoEngine* e, LayerBind& L, bool pdl) {
     g.epi = EPI_STORE;
     g.err = e->err;
     g.eidx = e->moe_idx;
-    g.estride = (long long)(L.exp_down->bytes / E);
+    g.estride = (long long)(L.exp_down->bytes / El);
     g.erows = H;
-    g.n_experts = E;
+    g.n_experts = El;
     if ((rc = launch_gemv(g, e->st, pdl))) return rc;
     mark(e, K_GEMV);
   }
-  if ((rc = launch_moe_combine(e->x, e->moe_y, e->moe_w, K, H, shared ? 1 : 0, e->st, pdl))) return rc;
+  if ((rc = launch_moe_combine(e->x, e->moe_y, e->moe_w, e->moe_idx, K, H, (shared && lead) ? 1 : 0, lead ? 1 : 0,
+                                e->st, pdl)))
+    return rc;
   mark(e, K_GEMV);
+  if (e->ep) {
+    // x = x + sum over ranks of their experts' partials
+    ncclResult_t r = ncclAllReduce(e->x, e->x, (size_t)H, ncclFloat, ncclSum, e->comm, e->st);
+    if (r != ncclSuccess) return set_error(INFERNO_ENCCL, "expert-parallel all-reduce: %s", ncclGetErrorString(r));
+  }
   return 0;
 }
 
@@ -481,7 +493,7 @@ int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
   mark(e, K_EMBED);
   for (int i = 0; i < c.num_layers; ++i)
     if ((rc = enqueue_layer(e, i, pdl))) return rc;
-  if (c.tp_size > 1) {
+  if (e->tp) {
     // vocab-split lm_head: local rows, global first-max through a u64 max
     // all-reduce of the packed (ordered value, ~index) keys
     GemvCall g;
@@ -670,8 +682,10 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
   if (c.max_batch > 1) return set_error(INFERNO_EINVAL, "engine_create: max_batch > 1 is not supported yet");
   if (c.tp_size < 1 || c.tp_rank < 0 || c.tp_rank >= c.tp_size)
     return set_error(INFERNO_EINVAL, "engine_create: tp_rank %d / tp_size %d", c.tp_rank, c.tp_size);
-  if (c.tp_size > 1 && (!c.nccl_unique_id || c.n_experts))
-    return set_error(INFERNO_EINVAL, "engine_create: tensor parallel needs an NCCL unique id and a dense FFN");
+  if (c.tp_size > 1 && !c.nccl_unique_id)
+    return set_error(INFERNO_EINVAL, "engine_create: tensor / expert parallel needs an NCCL unique id");
+  if (c.tp_size > 1 && c.n_experts && c.n_experts % c.tp_size)
+    return set_error(INFERNO_EINVAL, "engine_create: %d experts not divisible by %d ranks", c.n_experts, c.tp_size);
   if (c.n_experts && (c.n_experts > 1024 || c.n_experts_used <= 0 || c.n_experts_used > 16 ||
                       c.n_experts_used > c.n_experts || c.expert_ffn <= 0 || c.expert_ffn % 256 ||
                       c.n_experts_used + 1 > 16))
@@ -679,6 +693,8 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
                                      "width that is a multiple of 256");
   auto* e = new InfernoEngine();
   e->cfg = c;
+  e->ep = c.tp_size > 1 && c.n_experts > 0;
+  e->tp = c.tp_size > 1 && !e->ep;
   e->dev = c.device;
   if (cudaSetDevice(e->dev) != cudaSuccess) {
     delete e;
@@ -757,7 +773,7 @@ int inferno_engine_finalize(InfernoEngine* e) {
     e->repack = !(nr && atoi(nr) != 0) && !(pe && atoi(pe) != 0);
   }
   if (e->repack && e->lm_head->type == T_Q6_K && e->lm_head->rows() % 16 == 0 && c.hidden_size % 256 == 0 &&
-      (c.tp_size == 1 || (c.vocab_size / c.tp_size) % 16 == 0)) {
+      (!e->tp || (c.vocab_size / c.tp_size) % 16 == 0)) {
     e->lm_packed = *e->lm_head;
     void* d = nullptr;
     if (cudaMalloc(&d, (e->lm_head->bytes + 255) / 256 * 256) != cudaSuccess)
@@ -768,7 +784,7 @@ int inferno_engine_finalize(InfernoEngine* e) {
     e->lm_packed.type = T_Q6_KR;
     e->lm_head = &e->lm_packed;
   }
-  if (c.tp_size > 1) {
+  if (e->tp) {
     if (c.vocab_size % c.tp_size || e->lm_head->rows() != c.vocab_size)
       return set_error(INFERNO_EINVAL, "tensor parallel: vocab %d not divisible by %d", c.vocab_size, c.tp_size);
     const int vl = c.vocab_size / c.tp_size;
@@ -825,15 +841,16 @@ int inferno_engine_finalize(InfernoEngine* e) {
     }
     if (c.n_experts) {
       const int E = c.n_experts, Ie = c.expert_ffn;
+      const int El = e->ep ? E / c.tp_size : E;   // experts held by this rank
       if ((rc = require(e, p + "ffn_gate_inp.weight", &L.router, T_F32)) ||
           (rc = require(e, p + "ffn_gate_exps.weight", &L.exp_gate)) ||
           (rc = require(e, p + "ffn_up_exps.weight", &L.exp_up)) ||
           (rc = require(e, p + "ffn_down_exps.weight", &L.exp_down)))
         return rc;
       if (L.router->rows() != E || L.router->ne[0] != c.hidden_size || L.exp_gate->ne[0] != c.hidden_size ||
-          L.exp_gate->ne[1] != Ie || L.exp_gate->ne[2] != E || L.exp_up->type != L.exp_gate->type ||
-          L.exp_up->ne[1] != Ie || L.exp_up->ne[2] != E || L.exp_down->ne[0] != Ie ||
-          L.exp_down->ne[1] != c.hidden_size || L.exp_down->ne[2] != E)
+          L.exp_gate->ne[1] != Ie || L.exp_gate->ne[2] != El || L.exp_up->type != L.exp_gate->type ||
+          L.exp_up->ne[1] != Ie || L.exp_up->ne[2] != El || L.exp_down->ne[0] != Ie ||
+          L.exp_down->ne[1] != c.hidden_size || L.exp_down->ne[2] != El)
         return set_error(INFERNO_EINVAL, "layer %d: MoE tensor dims do not match the config", i);
       L.sh_gate = find(e, p + "ffn_gate_shexp.weight");
       if (L.sh_gate) {
@@ -885,7 +902,7 @@ int inferno_engine_finalize(InfernoEngine* e) {
       return rc;
   }
   e->xcur = e->x;
-  if (c.tp_size > 1 && (rc = setup_xch(e))) return rc;
+  if (e->tp && (rc = setup_xch(e))) return rc;
   e->max_out = c.max_ctx + 8;
   // attention splits: multiples of 32 positions, at most 128 splits
   e->split_len = 32;

@@ -499,11 +499,19 @@ __device__ __forceinline__ const uint8_t* seg_row_ptr(const GemvParams& p, int s
   if (!IND || !s.indirect) return s.W + (long long)row0 * p.row_bytes;
   const int slot = row0 / p.erows;
   int e = p.eidx[slot];
-  if (e < 0 || e >= p.n_experts) {
+  if (e >= p.n_experts) {
     if (p.err) atomicExch(p.err, DERR_BAD_ARG);
     e = 0;
   }
+  if (e < 0) e = 0;     // an expert of another rank (seg_skipped): never read
   return s.W + (long long)e * p.estride + (long long)(row0 - slot * p.erows) * p.row_bytes;
+}
+
+// Expert parallelism: a negative id marks a selected expert held by another
+// rank; its tiles are neither copied nor computed and their outputs are 0.
+template <bool IND = true>
+__device__ __forceinline__ bool seg_skipped(const GemvParams& p, int sg, int row0) {
+  return IND && p.seg[sg].indirect && p.eidx[row0 / p.erows] < 0;
 }
 
 // Producer warp of the GEMV kernels: one bulk copy per tile (two for paired
@@ -532,7 +540,7 @@ __device__ __forceinline__ void gemv_producer(const GemvParams& p, uint64_t* ful
     uint8_t* st = stage0 + (long long)s * p.stage_bytes;
     if (lane < (paired ? 2 : 1)) {
       const int sgr = paired ? lane : sg;
-      const int nrows = min(paired ? half_tr : TR, p.seg[sgr].rows - row0);
+      const int nrows = seg_skipped<IND>(p, sgr, row0) ? 0 : min(paired ? half_tr : TR, p.seg[sgr].rows - row0);
       uint32_t bytes = 0;
       uintptr_t a0 = 0;
       if (nrows > 0) {
@@ -656,7 +664,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
     for (int b = 0; b < NB; ++b)
 #pragma unroll
       for (int r = 0; r < R; ++r) acc[b][r] = 0.f;
-    for (int kc = wk; kc < p.nkc; kc += p.nkg) {
+    const bool skip_tile = seg_skipped(p, sg, row0);
+    for (int kc = wk; kc < p.nkc && !skip_tile; kc += p.nkg) {
       const int ce = min(GEMV_CHUNK, p.inner - kc * GEMV_CHUNK);
       if ((x0 & blk_mask) >= ce) continue;
       const long long coff = (long long)kc * (GEMV_CHUNK / qk_of(TYPE)) * bb_of(TYPE);

@@ -727,7 +727,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
                                                                 : colscale * ldexpf(1.0f, -mma_exp2_scale(vmax[slot])))
                                                    : fscale0;
     float acc[2] = {0.f, 0.f}, corr[2] = {0.f, 0.f};
-    for (int sb = wk; sb < nsb; sb += nkg) {
+    const bool skip_tile = seg_skipped<MODE == MMA_MOE>(p, sg, row0);
+    for (int sb = wk; sb < nsb && !skip_tile; sb += nkg) {
       if constexpr (TYPE == T_Q4_K)
         mma_sb_q4k(ra + sb * BB, rb + sb * BB, xq_t + (size_t)sb * 8 * MMA_KS_BYTES, xsum_t + sb * XS_PER_SB, lane,
                    acc, corr);

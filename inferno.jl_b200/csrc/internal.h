@@ -69,9 +69,10 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl);
 // Q6_K -> the engine-internal 16-row-group layout T_Q6_KR (same byte count)
 int launch_repack_q6k(const void* src, void* dst, int rows, int inner, cudaStream_t st);
 int launch_dequant(int type, const void* src, long long n, float* dst, cudaStream_t st);
-int launch_moe_topk(const float* logits, int E, int K, int* idx, float* wts, int* err, cudaStream_t st, bool pdl);
-int launch_moe_combine(float* x, const float* y, const float* wts, int K, int H, int shared, cudaStream_t st,
-                       bool pdl);
+int launch_moe_topk(const float* logits, int E, int K, int* idx, float* wts, int* err, int ebase, int eloc,
+                    cudaStream_t st, bool pdl);
+int launch_moe_combine(float* x, const float* y, const float* wts, const int* idx, int K, int H, int shared,
+                       int add_x, cudaStream_t st, bool pdl);
 int launch_embed_row(int type, const void* W, long long row_bytes, int inner, const int* row_ptr, float* dst,
                      int vocab, cudaStream_t st, bool pdl);
 

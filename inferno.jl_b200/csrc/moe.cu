@@ -19,7 +19,7 @@ constexpr int MOE_MAX_K = 16;
 
 // One warp: softmax over E logits, stable top-k, renormalised weights.
 __global__ void __launch_bounds__(32) moe_topk_kernel(const float* logits, int E, int K, int* idx, float* wts,
-                                                      int* err) {
+                                                      int* err, int ebase, int eloc) {
   __shared__ float p[MOE_MAX_E];
   __shared__ float sum_s;
   const int lane = threadIdx.x;
@@ -73,8 +73,11 @@ __global__ void __launch_bounds__(32) moe_topk_kernel(const float* logits, int E
   if (lane == 0) {
     float ts = 0.0f;
     for (int r = 0; r < K; ++r) ts += pv[r];
+    // expert parallelism: ids local to this rank's experts [ebase, ebase +
+    // eloc), -1 for experts held by another rank
     for (int r = 0; r < K; ++r) {
-      idx[r] = chosen[r];
+      const int id = chosen[r] - ebase;
+      idx[r] = (id >= 0 && id < eloc) ? id : -1;
       wts[r] = pv[r] / ts;
     }
   }
@@ -82,15 +85,20 @@ __global__ void __launch_bounds__(32) moe_topk_kernel(const float* logits, int E
 
 // x[j] += sum_i w_i * y[i][j] (+ y[K][j] for the shared expert), expert order
 // fixed (deterministic).
-__global__ void moe_combine_kernel(float* x, const float* y, const float* wts, int K, int H, int shared) {
+// Expert parallelism (partial = 1): only this rank's experts contribute and
+// rank 0 (add_x = 1) adds the residual and the shared expert; the caller then
+// sums x over the ranks.
+__global__ void moe_combine_kernel(float* x, const float* y, const float* wts, const int* idx, int K, int H, int shared,
+                                   int add_x) {
   pdl_wait();
   pdl_trigger();
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= H) return;
   float acc = 0.0f;
-  for (int i = 0; i < K; ++i) acc = __fadd_rn(acc, __fmul_rn(wts[i], y[(long long)i * H + j]));
+  for (int i = 0; i < K; ++i)
+    if (idx[i] >= 0) acc = __fadd_rn(acc, __fmul_rn(wts[i], y[(long long)i * H + j]));
   if (shared) acc = __fadd_rn(acc, y[(long long)K * H + j]);
-  x[j] = __fadd_rn(x[j], acc);
+  x[j] = add_x ? __fadd_rn(x[j], acc) : acc;
 }
 
 namespace {
@@ -110,15 +118,17 @@ int launch_pdl(F kern, dim3 grid, dim3 block, cudaStream_t st, bool pdl, A... ar
 }
 }  // namespace
 
-int launch_moe_topk(const float* logits, int E, int K, int* idx, float* wts, int* err, cudaStream_t st, bool pdl) {
+int launch_moe_topk(const float* logits, int E, int K, int* idx, float* wts, int* err, int ebase, int eloc,
+                    cudaStream_t st, bool pdl) {
   if (E <= 0 || E > MOE_MAX_E || K <= 0 || K > MOE_MAX_K || K > E)
     return set_error(INFERNO_EINVAL, "moe: %d experts / top-%d unsupported (max %d / %d)", E, K, MOE_MAX_E, MOE_MAX_K);
-  return launch_pdl(moe_topk_kernel, dim3(1), dim3(32), st, pdl, logits, E, K, idx, wts, err);
+  return launch_pdl(moe_topk_kernel, dim3(1), dim3(32), st, pdl, logits, E, K, idx, wts, err, ebase, eloc);
 }
 
-int launch_moe_combine(float* x, const float* y, const float* wts, int K, int H, int shared, cudaStream_t st,
-                       bool pdl) {
-  return launch_pdl(moe_combine_kernel, dim3((H + 255) / 256), dim3(256), st, pdl, x, y, wts, K, H, shared);
+int launch_moe_combine(float* x, const float* y, const float* wts, const int* idx, int K, int H, int shared,
+                       int add_x, cudaStream_t st, bool pdl) {
+  return launch_pdl(moe_combine_kernel, dim3((H + 255) / 256), dim3(256), st, pdl, x, y, wts, idx, K, H, shared,
+                    add_x);
 }
 
 }  // namespace inf

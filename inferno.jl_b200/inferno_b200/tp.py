@@ -106,10 +106,35 @@ def gdn_local_heads(spec: S.ModelSpec, rank: int, n: int) -> list:
     return [g0 + gl + j * nk for j in range(nv // nk) for gl in range(nk_l)]
 
 
+def shard_experts(spec: S.ModelSpec, tensors: dict, rank: int, n: int) -> dict:
+    """Expert parallelism for MoE models: rank r keeps
+    routed experts [r*E/n, (r+1)*E/n) of every ffn_{gate,up,down}_exps tensor
+    (GGUF ne = [in, out, E], experts contiguous); every other tensor -- router,
+    shared expert, attention, GDN, embedding -- is replicated.  The engine
+    computes the router and top-k on every rank, evaluates only its own
+    selected experts and sums the ranks' partial FFN outputs."""
+    E = spec.n_experts
+    if E % n:
+        raise ValueError(f"{E} experts over {n} ranks")
+    el = E // n
+    out = {}
+    for name, t in tensors.items():
+        if name.endswith("_exps.weight"):
+            per = t.nbytes // E
+            a = t.data.reshape(E, per)[rank * el:(rank + 1) * el]
+            t = S.Tensor(t.ggml_type, tuple(t.ne[:2]) + (el,), np.ascontiguousarray(a).reshape(-1))
+        out[name] = t
+    return out
+
+
 def shard(spec: S.ModelSpec, tensors: dict, rank: int, n: int):
-    """(local spec, local tensors) of `rank` in an n-way split."""
+    """(local spec, local tensors) of `rank` in an n-way split: tensor
+    parallel for dense models, expert parallel for MoE models (the local spec
+    then keeps the global dimensions)."""
     if n == 1:
         return spec, dict(tensors)
+    if spec.n_experts:
+        return spec, shard_experts(spec, tensors, rank, n)
     ls = local_spec(spec, n)
     H, dk, dv, hd = spec.hidden, spec.ssm_dk, spec.ssm_dv, spec.head_dim
     nk, nk_l = spec.ssm_nk, ls.ssm_nk

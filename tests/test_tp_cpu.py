@@ -72,3 +72,17 @@ def test_unsplittable_shapes_are_rejected():
         tp.check(S.CONFIGS["qwen35-9b"], 16)
     with pytest.raises(ValueError):
         tp.check(S.CONFIGS["tiny-moe"], 2)
+
+
+def test_expert_shards_cover_every_expert_once():
+    spec = S.CONFIGS["tiny-moe"]
+    T = S.make_model(spec, seed=33)
+    for n in (2, 4):
+        parts = [tp.shard(spec, T, r, n)[1] for r in range(n)]
+        for name, t in T.items():
+            if name.endswith("_exps.weight"):
+                joined = np.concatenate([p[name].data for p in parts])
+                assert np.array_equal(joined, t.data), name
+                assert all(p[name].ne[2] == spec.n_experts // n for p in parts)
+            else:
+                assert all(p[name] is t for p in parts), name

@@ -1,6 +1,7 @@
-"""Tensor-parallel decode on 2+ GPUs (one process per GPU, NCCL over NVLink):
-the sharded engine's argmax, logits and greedy tokens equal the unsharded
-engine's and the oracle's.  Skipped on boxes with fewer GPUs."""
+"""Tensor-parallel (dense models) and expert-parallel (tiny-moe) decode on 2+
+GPUs (one process per GPU, NCCL over NVLink): the sharded engine's argmax,
+logits and greedy tokens equal the unsharded engine's and the oracle's.
+Skipped on boxes with fewer GPUs."""
 import os
 import subprocess
 import sys
@@ -21,7 +22,8 @@ def _ngpus():
 
 
 @pytest.mark.parametrize("mode", ["peer-exchange", "nccl"])
-@pytest.mark.parametrize("model,n", [("tiny-tp", 2), ("small-tp", 2), ("small-tp", 4), ("small-tp", 8)])
+@pytest.mark.parametrize("model,n", [("tiny-tp", 2), ("small-tp", 2), ("small-tp", 4), ("small-tp", 8),
+                                     ("tiny-moe", 2), ("tiny-moe", 4)])
 def test_tp_matches_single_gpu(model, n, mode):
     """peer-exchange: the residual partials go to every rank's memory from the
     GEMV epilogue and are summed in the next GEMV's prologue; nccl: the same
