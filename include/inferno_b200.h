@@ -124,6 +124,25 @@ int inferno_gemv_swiglu(int ggml_type, const void* Wg, const void* Wu, const flo
 int inferno_gdn_recurrence(int T, int n_heads, int dk, int dv, const float* q, const float* k, const float* v,
                            const float* beta, const float* g, float* S, float* y, void* stream);
 
+/* Sampling parameters of generate_cpu / softmax_sample
+ * (src/ModelCPU.jl:1123-1225): temperature 0 = greedy. */
+typedef struct InfernoSampling {
+  float temperature;
+  float top_p;               /* 1 = off */
+  int32_t top_k;             /* 0 = off (the nucleus is then searched within the 1024 most probable tokens) */
+  float min_p;               /* 0 = off; relative to the largest probability */
+  float repetition_penalty;  /* 1 = off */
+  float presence_penalty;    /* 0 = off */
+  uint64_t seed;             /* Philox-4x32-10 key; the counter is the step */
+} InfernoSampling;
+
+/* Samples one token from device logits[vocab] with softmax_sample's
+ * semantics; seen (device, vocab bytes, may be NULL) marks the tokens the
+ * penalties apply to; u in [0, 1) is the uniform draw (u < 0: Philox(seed, 0)).
+ * out_token is a device pointer. */
+int inferno_sample_logits(const float* logits, int vocab, const InfernoSampling* s, const uint8_t* seen, float u,
+                          int32_t* out_token, void* stream);
+
 /* ======================= 3. engine tier ==================================== */
 
 /* Model hyper-parameters, filled by the host from GGUF metadata
@@ -190,6 +209,13 @@ int inferno_forward_tokens(InfernoEngine* eng, const int32_t* tok, int n, int po
  * The generation loop of test/benchmark_e2e.jl:43-59 / Engine.generate
  * (src/Engine.jl:327-344) with temperature 0. */
 int inferno_decode_greedy(InfernoEngine* eng, int32_t tok, int pos, int n_steps, int32_t* out_tokens);
+
+/* Sampled decode on the device: like inferno_decode_greedy, but each token is
+ * drawn by the sampler of generate_cpu (src/ModelCPU.jl:1236-1254) with the
+ * penalties applied to seen_tokens (host, may be NULL) and every generated
+ * token; the draws come from Philox(s->seed, step). */
+int inferno_decode_sample(InfernoEngine* eng, int32_t tok, int pos, int n_steps, const InfernoSampling* s,
+                          const int32_t* seen_tokens, int n_seen, int32_t* out_tokens);
 
 /* Zero GDN conv + recurrent state and the KV cache (src/ModelCPU.jl:525-529). */
 int inferno_reset_states(InfernoEngine* eng);

@@ -144,6 +144,10 @@ struct InfernoEngine {
   int pk_slot = 0, pk_hidden_pad = 0, pk_inner_pad = 0;
   unsigned* pk_barrier = nullptr;
   int* pk_abort = nullptr;
+  // sampled decode: parameters of the graph being captured (null = greedy) and
+  // the tokens the penalties apply to
+  const inf::SampleArgs* sampling = nullptr;
+  uint8_t* seen = nullptr;
   unsigned long long* trace = nullptr;   // debug: per-GEMV phase stamps (INFERNO_B200_TRACE)
   int trace_idx = 0;
   int launches = 0;              // kernels enqueued by the last enqueue_token
@@ -493,6 +497,7 @@ int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
   mark(e, K_EMBED);
   for (int i = 0; i < c.num_layers; ++i)
     if ((rc = enqueue_layer(e, i, pdl))) return rc;
+  if (e->sampling) write_logits = true;
   if (e->tp) {
     // vocab-split lm_head: local rows, global first-max through a u64 max
     // all-reduce of the packed (ordered value, ~index) keys
@@ -525,10 +530,17 @@ int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
     if (r == ncclSuccess && write_logits)
       r = ncclAllGather(e->logits_local, e->logits, (size_t)e->lm_head->rows(), ncclFloat, e->comm, e->st);
     if (r != ncclSuccess) return set_error(INFERNO_ENCCL, "lm_head collectives: %s", ncclGetErrorString(r));
+    if (e->sampling && (rc = launch_sample(e->logits, c.vocab_size, *e->sampling, e->seen, -1.0f, &e->ctl->step,
+                                           nullptr, &e->ctl->argkey, e->seen, e->st, pdl)))
+      return rc;
     return launch_finalize(e, pdl);
   }
   if (!(e->ablate & 64) && (rc = gemv(e, e->lm_head->type, c.hidden_size, {M(e->lm_head, write_logits ? e->logits : nullptr)}, e->xcur,
                  PRO_RMSNORM, (const float*)e->out_norm->d, nullptr, 0, EPI_ARGMAX, &e->ctl->argkey, pdl)))
+    return rc;
+  // sampled decode: the drawn token replaces the argmax key (finalize reads it)
+  if (e->sampling && (rc = launch_sample(e->logits, c.vocab_size, *e->sampling, e->seen, -1.0f, &e->ctl->step, nullptr,
+                                         &e->ctl->argkey, e->seen, e->st, pdl)))
     return rc;
   return launch_finalize(e, pdl);
 }
@@ -1199,6 +1211,45 @@ int inferno_decode_greedy(InfernoEngine* e, int32_t tok, int pos, int n_steps, i
 }
 
 float inferno_last_decode_ms(InfernoEngine* e) { return e ? e->last_ms : -1.f; }
+
+int inferno_decode_sample(InfernoEngine* e, int32_t tok, int pos, int n_steps, const InfernoSampling* s,
+                          const int32_t* seen_tokens, int n_seen, int32_t* out_tokens) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  const InfernoConfig& c = e->cfg;
+  if (!s || n_steps <= 0 || !out_tokens || n_seen < 0 || (n_seen && !seen_tokens))
+    return set_error(INFERNO_EINVAL, "decode_sample: bad arguments");
+  if (s->temperature < 0.f || s->top_p <= 0.f || s->top_p > 1.f || s->min_p < 0.f || s->min_p >= 1.f ||
+      s->repetition_penalty <= 0.f)
+    return set_error(INFERNO_EINVAL, "decode_sample: sampling parameter out of range");
+  if (pos < 0 || pos + n_steps > c.max_ctx)
+    return set_error(INFERNO_EINVAL, "decode_sample: positions [%d, %d) exceed max_ctx %d", pos, pos + n_steps, c.max_ctx);
+  if (tok < 0 || tok >= c.vocab_size || n_steps > e->max_out) return set_error(INFERNO_EINVAL, "decode_sample: bad token / n_steps");
+  if (e->persistent) return set_error(INFERNO_ESTATE, "decode_sample: not available with the persistent kernel");
+  if (!e->seen && (rc = dalloc(e, &e->seen, c.vocab_size))) return rc;
+  std::vector<uint8_t> mark(c.vocab_size, 0);
+  for (int i = 0; i < n_seen; ++i)
+    if (seen_tokens[i] >= 0 && seen_tokens[i] < c.vocab_size) mark[seen_tokens[i]] = 1;
+  INF_CUDA_TRY(cudaMemcpyAsync(e->seen, mark.data(), mark.size(), cudaMemcpyHostToDevice, e->st));
+  SampleArgs a{s->temperature, s->top_p, s->min_p, s->presence_penalty, s->repetition_penalty, s->top_k, s->seed};
+  if ((rc = set_ctl(e, tok, pos, 1))) return rc;
+  // one graph per call: the parameters are kernel arguments of the sampler
+  e->sampling = &a;
+  cudaGraphExec_t g = nullptr;
+  rc = capture(e, 1, true, &g);
+  e->sampling = nullptr;
+  if (rc) return rc;
+  INF_CUDA_TRY(cudaEventRecord(e->ev0, e->st));
+  for (int t = 0; t < n_steps && !rc; ++t)
+    if (cudaGraphLaunch(g, e->st) != cudaSuccess) rc = set_error(INFERNO_ECUDA, "decode_sample: graph launch failed");
+  INF_CUDA_TRY(cudaEventRecord(e->ev1, e->st));
+  INF_CUDA_TRY(cudaStreamSynchronize(e->st));
+  cudaGraphExecDestroy(g);
+  if (rc) return rc;
+  cudaEventElapsedTime(&e->last_ms, e->ev0, e->ev1);
+  INF_CUDA_TRY(cudaMemcpy(out_tokens, e->out_tokens, (size_t)n_steps * 4, cudaMemcpyDeviceToHost));
+  return check_device_error(e);
+}
 
 int inferno_reset_states(InfernoEngine* e) {
   int rc;

@@ -69,6 +69,14 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl);
 // Q6_K -> the engine-internal 16-row-group layout T_Q6_KR (same byte count)
 int launch_repack_q6k(const void* src, void* dst, int rows, int inner, cudaStream_t st);
 int launch_dequant(int type, const void* src, long long n, float* dst, cudaStream_t st);
+// sampler parameters (sample.cu; InfernoSampling without the ABI padding)
+struct SampleArgs {
+  float temperature, top_p, min_p, presence, repetition;
+  int top_k;
+  unsigned long long seed;
+};
+int launch_sample(const float* logits, int V, const SampleArgs& a, const uint8_t* seen, float u, const int* step,
+                  int* out_tok, unsigned long long* out_key, uint8_t* mark_seen, cudaStream_t st, bool pdl);
 int launch_moe_topk(const float* logits, int E, int K, int* idx, float* wts, int* err, int ebase, int eloc,
                     cudaStream_t st, bool pdl);
 int launch_moe_combine(float* x, const float* y, const float* wts, const int* idx, int K, int H, int shared,

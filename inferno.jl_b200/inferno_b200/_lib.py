@@ -43,7 +43,7 @@ EXPORTS = [
     "inferno_state_import", "inferno_last_decode_ms", "inferno_engine_destroy",
     "inferno_state_save_device", "inferno_state_restore_device", "inferno_kernels_per_token",
     "inferno_profile_tokens", "inferno_gemv_host_noalloc", "inferno_debug_trace", "inferno_tp_unique_id",
-    "inferno_gdn_recurrence",
+    "inferno_gdn_recurrence", "inferno_sample_logits", "inferno_decode_sample",
 ]
 
 _lib = None

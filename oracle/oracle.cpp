@@ -619,6 +619,77 @@ void orc_gdn_recurrence(int T, int H, int dk, int dv, const float* q, const floa
   }
 }
 
+// src/ModelCPU.jl:1202-1225 (penalties for the seen tokens) then
+// softmax_sample (:1123-1200) with the uniform draw r given; 0-based result.
+int orc_softmax_sample(const float* logits_in, int V, float temperature, float top_p, int top_k, float min_p,
+                       float presence, float repetition, const int* seen, int n_seen, float r) {
+  std::vector<float> l(logits_in, logits_in + V);
+  std::vector<char> mark(V, 0);
+  for (int i = 0; i < n_seen; ++i)
+    if (seen[i] >= 0 && seen[i] < V) mark[seen[i]] = 1;
+  if (presence != 0.0f)
+    for (int i = 0; i < V; ++i)
+      if (mark[i]) l[i] -= presence;
+  if (repetition != 1.0f)
+    for (int i = 0; i < V; ++i)
+      if (mark[i]) l[i] = l[i] > 0 ? l[i] / repetition : l[i] * repetition;
+  if (temperature == 0.0f) return (int)(std::max_element(l.begin(), l.end()) - l.begin());   // first max
+  if (temperature != 1.0f)
+    for (auto& v : l) v = v / temperature;
+  // stable descending order: ties keep the lower index first (sortperm rev=true)
+  auto desc = [](const std::vector<float>& a) {
+    std::vector<int> idx(a.size());
+    std::iota(idx.begin(), idx.end(), 0);
+    std::stable_sort(idx.begin(), idx.end(), [&](int x, int y) { return a[x] > a[y]; });
+    return idx;
+  };
+  if (top_k > 0) {
+    std::vector<int> idx = desc(l);
+    std::vector<char> keep(V, 0);
+    for (int i = 0; i < std::min(top_k, V); ++i) keep[idx[i]] = 1;
+    for (int i = 0; i < V; ++i)
+      if (!keep[i]) l[i] = -INFINITY;
+  }
+  const float mx = *std::max_element(l.begin(), l.end());
+  std::vector<float> p(V);
+  float s = 0.0f;
+  for (int i = 0; i < V; ++i) { p[i] = std::exp(l[i] - mx); s += p[i]; }
+  for (auto& v : p) v = v / s;
+  if (top_p < 1.0f) {
+    std::vector<int> idx = desc(p);
+    std::vector<char> keep(V, 0);
+    float c = 0.0f;
+    for (int i : idx) {
+      keep[i] = 1;
+      c += p[i];
+      if (c >= top_p) break;
+    }
+    float t = 0.0f;
+    for (int i = 0; i < V; ++i) {
+      if (!keep[i]) p[i] = 0.0f;
+      t += p[i];
+    }
+    if (t > 0.0f)
+      for (auto& v : p) v = v / t;
+  }
+  if (min_p > 0.0f) {
+    const float th = *std::max_element(p.begin(), p.end()) * min_p;
+    float t = 0.0f;
+    for (int i = 0; i < V; ++i) {
+      if (p[i] < th) p[i] = 0.0f;
+      t += p[i];
+    }
+    if (t > 0.0f)
+      for (auto& v : p) v = v / t;
+  }
+  float c = 0.0f;
+  for (int i = 0; i < V; ++i) {
+    c += p[i];
+    if (r <= c) return i;
+  }
+  return V - 1;
+}
+
 // ---- model ------------------------------------------------------------------
 // ip: [hidden, layers, n_heads, n_kv, head_dim, ffn, vocab, nv, nk, dk, dv,
 //      conv_k, ctx, n_experts, n_used, expert_ffn, shexp_ffn, dequant_at_load]

@@ -93,6 +93,18 @@ def gdn_recurrence(q, k, v, beta, g, S):
     return y
 
 
+def softmax_sample(logits, temperature, top_p=1.0, top_k=0, min_p=0.0, presence=0.0, repetition=1.0,
+                   seen=(), r=0.5):
+    """src/ModelCPU.jl:1123-1225 with the uniform draw r given; 0-based token."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    sn = np.ascontiguousarray(seen, dtype=np.int32) if len(seen) else np.zeros(1, np.int32)
+    L = lib()
+    L.orc_softmax_sample.restype = C.c_int
+    return int(L.orc_softmax_sample(_ptr(lg), lg.size, C.c_float(temperature), C.c_float(top_p), int(top_k),
+                                    C.c_float(min_p), C.c_float(presence), C.c_float(repetition), _ptr(sn),
+                                    len(seen), C.c_float(r)))
+
+
 class OracleModel:
     """The reference CPU model (load_model_cpu + forward_cpu!) restated."""
 
