@@ -75,6 +75,7 @@ struct LayerBind {
             *beta = nullptr, *ssm_a = nullptr, *dt_bias = nullptr, *ssm_norm = nullptr;
   DevTensor *wq = nullptr, *wk = nullptr, *wv = nullptr, *wo = nullptr, *q_norm = nullptr, *k_norm = nullptr;
   DevTensor *ffn_gate = nullptr, *ffn_up = nullptr, *ffn_down = nullptr;
+  DevTensor ffn_down_raw;      // GGUF-layout copy when ffn_down is regrouped (batched prefill GEMVs)
   // MoE FFN (config 5): router, routed experts, optional shared expert
   DevTensor *router = nullptr, *exp_gate = nullptr, *exp_up = nullptr, *exp_down = nullptr;
   DevTensor *sh_gate = nullptr, *sh_up = nullptr, *sh_down = nullptr;
@@ -120,6 +121,10 @@ struct InfernoEngine {
         *o = nullptr, *h = nullptr, *logits = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr, *part_o = nullptr, *part_ml = nullptr, *hidden = nullptr;
   int* att_counters = nullptr;
+  // chunked prefill: activations of up to PF_MAX_T tokens ([t][...] rows)
+  bool prefill = false;
+  float *xb = nullptr, *qkvb = nullptr, *zb = nullptr, *yb = nullptr, *qgb = nullptr, *kb = nullptr,
+        *vb = nullptr, *ob = nullptr, *hb = nullptr;
   // MoE scratch: router logits, selected ids / weights, expert hidden, expert outputs
   float *moe_logits = nullptr, *moe_w = nullptr, *moe_h = nullptr, *moe_y = nullptr;
   int* moe_idx = nullptr;
@@ -463,6 +468,126 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
   if (e->dump)
     INF_CUDA_TRY(cudaMemcpyAsync(e->hidden + (size_t)li * H, e->x, (size_t)H * 4, cudaMemcpyDeviceToDevice, e->st));
   return 0;
+}
+
+// batched GEMV over T token columns (x rows x_stride apart, y rows y_stride apart)
+int bgemv(InfernoEngine* e, const DevTensor* W, int inner, std::initializer_list<GemvMat> mats, const float* x,
+          int T, long long x_stride, long long y_stride, int pro, const float* pro_w, const float* pro_z, int group,
+          int epi) {
+  GemvCall c;
+  c.type = W->type;
+  c.inner = inner;
+  for (auto& m : mats) c.mats[c.nmats++] = m;
+  c.nb = T;
+  c.x = x;
+  c.x_stride = x_stride;
+  c.y_stride = y_stride;
+  c.pro = pro;
+  c.pro_w = pro_w;
+  c.pro_z = pro_z;
+  c.pro_group = group;
+  c.eps = e->cfg.rms_eps;
+  c.epi = epi;
+  c.err = e->err;
+  const int rc = launch_gemv(c, e->st, false);
+  if (!rc) mark(e, K_GEMV);
+  return rc;
+}
+
+// One prefill chunk: T <= PF_MAX_T prompt tokens (device ids) at positions
+// pos0.. through every layer with batched GEMVs and the chunk kernels of
+// prefill.cu; the last chunk also runs the lm_head on its last token.
+int enqueue_prefill_chunk(InfernoEngine* e, const int* toks, int T, int pos0, bool last, bool logits) {
+  const InfernoConfig& c = e->cfg;
+  const int H = c.hidden_size, I = c.intermediate_size, hdq = c.n_heads * c.head_dim;
+  int rc;
+  for (int t = 0; t < T; ++t)
+    if ((rc = launch_embed_row(e->embd->type, e->embd->d, (long long)e->embd->bytes / e->embd->rows(), H, toks + t,
+                               e->xb + (size_t)t * H, c.vocab_size, e->st, false)))
+      return set_error(INFERNO_ECUDA, "prefill embedding launch failed (%d)", rc);
+  for (int li = 0; li < c.num_layers; ++li) {
+    LayerBind& L = e->layers[li];
+    const float* an = (const float*)L.attn_norm->d;
+    if (L.ssm) {
+      if ((rc = bgemv(e, L.in_proj, H, {M(L.in_proj, e->qkvb)}, e->xb, T, H, e->C, PRO_RMSNORM, an, nullptr, 0,
+                      EPI_STORE)) ||
+          (rc = bgemv(e, L.gate, H, {M(L.gate, e->zb)}, e->xb, T, H, e->di, PRO_RMSNORM, an, nullptr, 0, EPI_STORE)))
+        return rc;
+      GdnParams g{};
+      g.x = e->xb;
+      g.in_norm = an;
+      g.eps = c.rms_eps;
+      g.H = H;
+      g.nv = c.ssm_nv;
+      g.nk = c.ssm_nk;
+      g.dv = c.ssm_dv;
+      g.K = c.ssm_conv_kernel;
+      g.C = e->C;
+      g.qkv = e->qkvb;
+      g.conv_w = (const float*)L.conv1d->d;
+      g.ring = L.ring;
+      g.w_alpha = (const float*)L.alpha->d;
+      g.w_beta = (const float*)L.beta->d;
+      g.ssm_a = (const float*)L.ssm_a->d;
+      g.dt_bias = (const float*)L.dt_bias->d;
+      g.S = L.S;
+      g.y = e->yb;
+      g.step = L.step;
+      g.done = L.done;
+      if ((rc = launch_gdn_chunk(g, T, e->st))) return rc;
+      mark(e, K_GDN);
+      if ((rc = bgemv(e, L.ssm_out, e->di, {M(L.ssm_out, e->xb)}, e->yb, T, e->di, H, PRO_HEADNORM_GATE,
+                      (const float*)L.ssm_norm->d, e->zb, c.ssm_dv, EPI_ADD)))
+        return rc;
+    } else {
+      const int kvd = c.n_kv_heads * c.head_dim;
+      if ((rc = bgemv(e, L.wq, H, {M(L.wq, e->qgb)}, e->xb, T, H, 2 * hdq, PRO_RMSNORM, an, nullptr, 0, EPI_STORE)))
+        return rc;
+      if (L.wk->type == L.wv->type) {
+        if ((rc = bgemv(e, L.wk, H, {M(L.wk, e->kb), M(L.wv, e->vb)}, e->xb, T, H, kvd, PRO_RMSNORM, an, nullptr, 0,
+                        EPI_STORE)))
+          return rc;
+      } else if ((rc = bgemv(e, L.wk, H, {M(L.wk, e->kb)}, e->xb, T, H, kvd, PRO_RMSNORM, an, nullptr, 0, EPI_STORE)) ||
+                 (rc = bgemv(e, L.wv, H, {M(L.wv, e->vb)}, e->xb, T, H, kvd, PRO_RMSNORM, an, nullptr, 0, EPI_STORE))) {
+        return rc;
+      }
+      AttnParams a{};
+      a.qg = e->qgb;
+      a.k = e->kb;
+      a.v = e->vb;
+      a.q_norm = (const float*)L.q_norm->d;
+      a.k_norm = (const float*)L.k_norm->d;
+      a.eps = c.rms_eps;
+      a.rope_cos = e->rope_cos;
+      a.rope_sin = e->rope_sin;
+      a.rd = e->rd;
+      a.kc = L.kc;
+      a.vc = L.vc;
+      a.nh = c.n_heads;
+      a.nkv = c.n_kv_heads;
+      a.ctx = c.max_ctx;
+      a.split_len = e->split_len;
+      a.nsplit = e->nsplit;
+      a.part_o = e->part_o;
+      a.part_ml = e->part_ml;
+      a.counters = e->att_counters;
+      a.out = e->ob;
+      a.err = e->err;
+      if ((rc = launch_attn_chunk(a, pos0, T, e->st))) return rc;
+      mark(e, K_ATTN);
+      if ((rc = bgemv(e, L.wo, hdq, {M(L.wo, e->xb)}, e->ob, T, hdq, H, PRO_NONE, nullptr, nullptr, 0, EPI_ADD)))
+        return rc;
+    }
+    DevTensor* down = L.ffn_down->type == T_Q6_KR ? &L.ffn_down_raw : L.ffn_down;
+    if ((rc = bgemv(e, L.ffn_gate, H, {M(L.ffn_gate, e->hb), M(L.ffn_up, nullptr)}, e->xb, T, H, I, PRO_RMSNORM,
+                    (const float*)L.post_norm->d, nullptr, 0, EPI_SWIGLU)) ||
+        (rc = bgemv(e, down, I, {M(down, e->xb)}, e->hb, T, I, H, PRO_NONE, nullptr, nullptr, 0, EPI_ADD)))
+      return rc;
+  }
+  if (!last) return 0;
+  e->xch_pending = -1;
+  return gemv(e, e->lm_head->type, H, {M(e->lm_head, logits ? e->logits : nullptr)}, e->xb + (size_t)(T - 1) * H,
+              PRO_RMSNORM, (const float*)e->out_norm->d, nullptr, 0, EPI_ARGMAX, &e->ctl->argkey, false);
 }
 
 int launch_finalize(InfernoEngine* e, bool pdl) {
@@ -890,7 +1015,8 @@ int inferno_engine_finalize(InfernoEngine* e) {
         return rc;
       }
       INF_CUDA_TRY(cudaStreamSynchronize(e->st));
-      cudaFree(L.ffn_down->d);
+      L.ffn_down_raw = *L.ffn_down;          // kept for the batched (prefill) GEMVs
+      e->allocs.push_back(L.ffn_down_raw.d);
       L.ffn_down->d = d;
       L.ffn_down->type = T_Q6_KR;
     }
@@ -915,6 +1041,20 @@ int inferno_engine_finalize(InfernoEngine* e) {
   }
   e->xcur = e->x;
   if (e->tp && (rc = setup_xch(e))) return rc;
+  {
+    const char* np = getenv("INFERNO_B200_NO_PREFILL");
+    e->prefill = !(np && atoi(np) != 0) && c.tp_size == 1 && !c.n_experts && !e->dump;
+    if (e->prefill) {
+      const size_t T = PF_MAX_T;
+      if ((rc = dalloc(e, &e->xb, T * H)) || (rc = dalloc(e, &e->qkvb, T * e->C)) ||
+          (rc = dalloc(e, &e->zb, T * e->di)) || (rc = dalloc(e, &e->yb, T * e->di)) ||
+          (rc = dalloc(e, &e->qgb, T * 2 * c.n_heads * c.head_dim)) ||
+          (rc = dalloc(e, &e->kb, T * c.n_kv_heads * c.head_dim)) ||
+          (rc = dalloc(e, &e->vb, T * c.n_kv_heads * c.head_dim)) ||
+          (rc = dalloc(e, &e->ob, T * c.n_heads * c.head_dim)) || (rc = dalloc(e, &e->hb, T * c.intermediate_size)))
+        return rc;
+    }
+  }
   e->max_out = c.max_ctx + 8;
   // attention splits: multiples of 32 positions, at most 128 splits
   e->split_len = 32;
@@ -922,9 +1062,10 @@ int inferno_engine_finalize(InfernoEngine* e) {
   e->nsplit = (c.max_ctx + e->split_len - 1) / e->split_len;
   e->rd = (int)std::lround(c.head_dim * (double)c.partial_rotary_factor);   // src/LoaderCPU.jl:375
   if (any_attn) {
-    if ((rc = dalloc(e, &e->part_o, (size_t)c.n_heads * e->nsplit * c.head_dim)) ||
-        (rc = dalloc(e, &e->part_ml, (size_t)c.n_heads * e->nsplit * 2)) ||
-        (rc = dalloc(e, &e->att_counters, c.n_heads)))
+    // [PF_MAX_T] x the decode sizes: the chunked prefill runs T queries at once
+    if ((rc = dalloc(e, &e->part_o, (size_t)PF_MAX_T * c.n_heads * e->nsplit * c.head_dim)) ||
+        (rc = dalloc(e, &e->part_ml, (size_t)PF_MAX_T * c.n_heads * e->nsplit * 2)) ||
+        (rc = dalloc(e, &e->att_counters, (size_t)PF_MAX_T * c.n_heads)))
       return rc;
     std::vector<float> cs, sn;
     build_rope(c.max_ctx, e->rd, c.rope_theta, cs, sn);
@@ -1172,7 +1313,26 @@ int inferno_forward_tokens(InfernoEngine* e, const int32_t* tok, int n, int pos0
     if (tok[i] < 0 || tok[i] >= e->cfg.vocab_size) return set_error(INFERNO_EINVAL, "forward_tokens: token %d out of range", tok[i]);
   INF_CUDA_TRY(cudaMemcpyAsync(e->prompt, tok, (size_t)n * 4, cudaMemcpyHostToDevice, e->st));
   if ((rc = set_ctl(e, tok[0], pos0, n))) return rc;
-  if (e->persistent) {
+  if (e->prefill && !e->persistent && n > 1) {
+    // chunked prefill; afterwards the control block reads as if n decode
+    // steps had run (position, step, last token = first-max of the last logits)
+    for (int off = 0; off < n; off += PF_MAX_T) {
+      const int T = std::min(PF_MAX_T, n - off);
+      if ((rc = enqueue_prefill_chunk(e, e->prompt + off, T, pos0 + off, off + T == n, logits_out != nullptr)))
+        return rc;
+    }
+    Ctl h{};
+    INF_CUDA_TRY(cudaMemcpyAsync(&h, e->ctl, sizeof h, cudaMemcpyDeviceToHost, e->st));
+    INF_CUDA_TRY(cudaStreamSynchronize(e->st));
+    const int am = (int)(0xffffffffu - (uint32_t)(h.argkey & 0xffffffffull));
+    h.tok = am;
+    h.last = am;
+    h.pos = pos0 + n;
+    h.step = n;
+    h.n_prompt = n;
+    h.argkey = 0ull;
+    INF_CUDA_TRY(cudaMemcpyAsync(e->ctl, &h, sizeof h, cudaMemcpyHostToDevice, e->st));
+  } else if (e->persistent) {
     if ((rc = run_persistent(e, tok[0], pos0, n, n))) return rc;
   } else if ((rc = run_steps(e, n, logits_out != nullptr))) {
     return rc;

@@ -69,6 +69,13 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl);
 // Q6_K -> the engine-internal 16-row-group layout T_Q6_KR (same byte count)
 int launch_repack_q6k(const void* src, void* dst, int rows, int inner, cudaStream_t st);
 int launch_dequant(int type, const void* src, long long n, float* dst, cudaStream_t st);
+// chunked prefill (prefill.cu): tokens per chunk = the batched GEMV's columns
+constexpr int PF_MAX_T = 8;
+struct GdnParams;
+struct AttnParams;
+int launch_gdn_chunk(const GdnParams& p, int T, cudaStream_t st);
+int launch_attn_chunk(const AttnParams& p, int pos0, int T, cudaStream_t st);
+
 // sampler parameters (sample.cu; InfernoSampling without the ABI padding)
 struct SampleArgs {
   float temperature, top_p, min_p, presence, repetition;

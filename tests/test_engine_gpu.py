@@ -136,3 +136,29 @@ def test_q6k_regrouping_is_bitwise_neutral(tiny, monkeypatch):
     m.close()
     assert am0 == am1
     assert np.array_equal(lg0, lg1)
+
+
+@pytest.mark.parametrize("n", [2, 8, 21])
+def test_chunked_prefill_matches_token_loop(tiny, monkeypatch, n):
+    """forward_tokens runs prompts in chunks of up to 8 tokens (batched GEMVs,
+    chunk GDN / attention kernels); logits, argmax and the state it leaves
+    (checked through the greedy continuation) match the token-by-token path
+    and the oracle."""
+    spec, T, orc = tiny
+    prompt = S.tokens(17, n, spec.vocab)
+    monkeypatch.setenv("INFERNO_B200_NO_PREFILL", "1")
+    m0 = Model(spec, T)
+    am0, lg0 = m0.forward(prompt, 0)
+    cont0 = m0.decode_greedy(am0, n, 12).tolist()
+    m0.close()
+    monkeypatch.delenv("INFERNO_B200_NO_PREFILL")
+    m1 = Model(spec, T)
+    am1, lg1 = m1.forward(prompt, 0)
+    cont1 = m1.decode_greedy(am1, n, 12).tolist()
+    m1.close()
+    assert rel(lg1, lg0) < 1e-4, rel(lg1, lg0)
+    assert am1 == am0
+    assert cont1 == cont0
+    orc.reset()
+    am_o, lg_o = orc.forward(prompt, 0)
+    assert am1 == am_o and rel(lg1, lg_o) < LOGIT_RTOL
