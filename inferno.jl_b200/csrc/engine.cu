@@ -123,6 +123,10 @@ struct InfernoEngine {
   int* att_counters = nullptr;
   // chunked prefill: activations of up to PF_MAX_T tokens ([t][...] rows)
   bool prefill = false;
+  // prefill graphs by (tokens, first position, logits): built on the second
+  // call with the same key (the first runs eagerly)
+  std::map<long long, cudaGraphExec_t> pf_graphs;
+  std::map<long long, int> pf_seen;
   float *xb = nullptr, *qkvb = nullptr, *zb = nullptr, *yb = nullptr, *qgb = nullptr, *kb = nullptr,
         *vb = nullptr, *ob = nullptr, *hb = nullptr;
   // MoE scratch: router logits, selected ids / weights, expert hidden, expert outputs
@@ -1316,10 +1320,36 @@ int inferno_forward_tokens(InfernoEngine* e, const int32_t* tok, int n, int pos0
   if (e->prefill && !e->persistent && n > 1) {
     // chunked prefill; afterwards the control block reads as if n decode
     // steps had run (position, step, last token = first-max of the last logits)
-    for (int off = 0; off < n; off += PF_MAX_T) {
-      const int T = std::min(PF_MAX_T, n - off);
-      if ((rc = enqueue_prefill_chunk(e, e->prompt + off, T, pos0 + off, off + T == n, logits_out != nullptr)))
+    auto enqueue_all = [&]() -> int {
+      for (int off = 0; off < n; off += PF_MAX_T) {
+        const int T = std::min(PF_MAX_T, n - off);
+        const int r = enqueue_prefill_chunk(e, e->prompt + off, T, pos0 + off, off + T == n, logits_out != nullptr);
+        if (r) return r;
+      }
+      return 0;
+    };
+    const long long key = ((long long)n << 32) | ((long long)pos0 << 1) | (logits_out ? 1 : 0);
+    auto it = e->pf_graphs.find(key);
+    if (it == e->pf_graphs.end() && e->cfg.use_graphs && e->pf_seen[key]++ > 0 && e->pf_graphs.size() < 16) {
+      cudaGraph_t g = nullptr;
+      cudaGraphExec_t ge = nullptr;
+      INF_CUDA_TRY(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+      rc = enqueue_all();
+      cudaError_t r1 = cudaStreamEndCapture(e->st, &g);
+      if (rc) {
+        if (g) cudaGraphDestroy(g);
         return rc;
+      }
+      if (r1 != cudaSuccess) return set_error(INFERNO_ECUDA, "prefill capture: %s", cudaGetErrorString(r1));
+      r1 = cudaGraphInstantiate(&ge, g, 0);
+      cudaGraphDestroy(g);
+      if (r1 != cudaSuccess) return set_error(INFERNO_ECUDA, "prefill graph: %s", cudaGetErrorString(r1));
+      it = e->pf_graphs.emplace(key, ge).first;
+    }
+    if (it != e->pf_graphs.end()) {
+      INF_CUDA_TRY(cudaGraphLaunch(it->second, e->st));
+    } else if ((rc = enqueue_all())) {
+      return rc;
     }
     Ctl h{};
     INF_CUDA_TRY(cudaMemcpyAsync(&h, e->ctl, sizeof h, cudaMemcpyDeviceToHost, e->st));
@@ -1553,6 +1583,7 @@ int inferno_engine_destroy(InfernoEngine* e) {
   if (e->g1) cudaGraphExecDestroy(e->g1);
   if (e->g1_logits) cudaGraphExecDestroy(e->g1_logits);
   if (e->g8) cudaGraphExecDestroy(e->g8);
+  for (auto& kv : e->pf_graphs) cudaGraphExecDestroy(kv.second);
   if (e->snapshot) cudaFree(e->snapshot);
   if (e->trace) cudaFree(e->trace);
   for (auto& kv : e->tensors) cudaFree(kv.second.d);

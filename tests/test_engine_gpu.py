@@ -162,3 +162,25 @@ def test_chunked_prefill_matches_token_loop(tiny, monkeypatch, n):
     orc.reset()
     am_o, lg_o = orc.forward(prompt, 0)
     assert am1 == am_o and rel(lg1, lg_o) < LOGIT_RTOL
+
+
+def test_prefill_graph_replays_match_eager(tiny):
+    """The second forward_tokens call with the same (tokens, position) key is
+    captured into a CUDA graph and later calls replay it: same results as the
+    eager first call, for a new prompt of the same length too."""
+    spec, T, _ = tiny
+    m = Model(spec, T)
+    p1 = S.tokens(19, 12, spec.vocab)
+    p2 = S.tokens(20, 12, spec.vocab)
+    outs = []
+    for p in (p1, p1, p1, p2):
+        m.reset()
+        outs.append(m.forward(p, 0))
+    m.reset()
+    m2 = Model(spec, T)
+    ref2 = m2.forward(p2, 0)
+    m2.close()
+    m.close()
+    assert outs[0][0] == outs[1][0] == outs[2][0]
+    assert np.array_equal(outs[0][1], outs[1][1]) and np.array_equal(outs[1][1], outs[2][1])
+    assert outs[3][0] == ref2[0] and np.array_equal(outs[3][1], ref2[1])
