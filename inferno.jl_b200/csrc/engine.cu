@@ -159,7 +159,8 @@ struct InfernoEngine {
   uint8_t* seen = nullptr;
   unsigned long long* trace = nullptr;   // debug: per-GEMV phase stamps (INFERNO_B200_TRACE)
   int trace_idx = 0;
-  int launches = 0;              // kernels enqueued by the last enqueue_token
+  int launches = 0;              // kernels enqueued since the last enqueue_token began
+  int token_launches = 0;        // kernels of one decode token (set by enqueue_token)
   void* snapshot = nullptr;      // device copy of the state arena
   size_t state_bytes = 0;
   // profiling: events between the kernels of one eager token
@@ -662,7 +663,9 @@ int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
     if (e->sampling && (rc = launch_sample(e->logits, c.vocab_size, *e->sampling, e->seen, -1.0f, &e->ctl->step,
                                            nullptr, &e->ctl->argkey, e->seen, e->st, pdl)))
       return rc;
-    return launch_finalize(e, pdl);
+    rc = launch_finalize(e, pdl);
+    e->token_launches = e->launches;
+    return rc;
   }
   if (!(e->ablate & 64) && (rc = gemv(e, e->lm_head->type, c.hidden_size, {M(e->lm_head, write_logits ? e->logits : nullptr)}, e->xcur,
                  PRO_RMSNORM, (const float*)e->out_norm->d, nullptr, 0, EPI_ARGMAX, &e->ctl->argkey, pdl)))
@@ -671,7 +674,9 @@ int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
   if (e->sampling && (rc = launch_sample(e->logits, c.vocab_size, *e->sampling, e->seen, -1.0f, &e->ctl->step, nullptr,
                                          &e->ctl->argkey, e->seen, e->st, pdl)))
     return rc;
-  return launch_finalize(e, pdl);
+  rc = launch_finalize(e, pdl);
+  e->token_launches = e->launches;
+  return rc;
 }
 
 int capture(InfernoEngine* e, int ntok, bool logits, cudaGraphExec_t* out) {
@@ -1524,7 +1529,7 @@ int inferno_state_restore_device(InfernoEngine* e) {
 int inferno_kernels_per_token(InfernoEngine* e) {
   int rc;
   if ((rc = ready(e))) return rc;
-  return e->persistent ? 0 : e->launches;
+  return e->persistent ? 0 : e->token_launches;
 }
 
 int inferno_profile_tokens(InfernoEngine* e, int32_t tok, int pos, int n_tokens, float* ms_by_class,

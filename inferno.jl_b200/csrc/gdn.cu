@@ -106,18 +106,39 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(const __grid_cons
 
   // ---------------- alpha / beta of RMSNorm(x) ----------------
   // alpha = sum_i Wa[i] * (x[i]*scale*w[i]) = scale * sum_i Wa[i]*w[i]*x[i]
-  __syncthreads();   // smem weights visible
-  float acc3[3] = {0.f, 0.f, 0.f};
-  for (int i = tid; i < H; i += GDN_THREADS) {
-    const float xv = p.x[i];
-    const float xw = xv * wn_s[i];
-    acc3[0] = fmaf(xv, xv, acc3[0]);
-    acc3[1] = fmaf(wa_s[i], xw, acc3[1]);
-    acc3[2] = fmaf(wb_s[i], xw, acc3[2]);
-  }
-  // conv1d + SiLU on this thread's channels (newest input last, :555-564)
+  // Every load that depends on the preceding kernel is issued here, before
+  // the first barrier, so their L2 round trips overlap.
   const float nq = p.qkv[cq], nk_ = p.qkv[ck];
   const float nv_ = tid < GDN_ROWS ? p.qkv[cv] : 0.f;
+  constexpr int XPT = 8;                 // x elements per thread per batch
+  float xr[XPT];
+#pragma unroll
+  for (int j = 0; j < XPT; ++j) {
+    const int i = tid + j * GDN_THREADS;
+    xr[j] = i < H ? p.x[i] : 0.f;
+  }
+  __syncthreads();   // smem weights visible
+  float acc3[3] = {0.f, 0.f, 0.f};
+  for (int i0 = 0; i0 < H; i0 += XPT * GDN_THREADS) {
+    if (i0) {
+#pragma unroll
+      for (int j = 0; j < XPT; ++j) {
+        const int i = i0 + tid + j * GDN_THREADS;
+        xr[j] = i < H ? p.x[i] : 0.f;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < XPT; ++j) {
+      const int i = i0 + tid + j * GDN_THREADS;
+      if (i < H) {
+        const float xv = xr[j], xw = xv * wn_s[i];
+        acc3[0] = fmaf(xv, xv, acc3[0]);
+        acc3[1] = fmaf(wa_s[i], xw, acc3[1]);
+        acc3[2] = fmaf(wb_s[i], xw, acc3[2]);
+      }
+    }
+  }
+  // conv1d + SiLU on this thread's channels (newest input last, :555-564)
   float vq = 0.f, vk = 0.f, vvv = 0.f;
 #pragma unroll
   for (int k = 0; k < GDN_MAXK; ++k) {
