@@ -76,6 +76,7 @@ struct LayerBind {
   DevTensor *wq = nullptr, *wk = nullptr, *wv = nullptr, *wo = nullptr, *q_norm = nullptr, *k_norm = nullptr;
   DevTensor *ffn_gate = nullptr, *ffn_up = nullptr, *ffn_down = nullptr;
   DevTensor ffn_down_raw;      // GGUF-layout copy when ffn_down is regrouped (batched prefill GEMVs)
+  void* wperm = nullptr;       // fused in_proj + GDN: head-regrouped [q|k|v|z] rows (Q4_K)
   // MoE FFN (config 5): router, routed experts, optional shared expert
   DevTensor *router = nullptr, *exp_gate = nullptr, *exp_up = nullptr, *exp_down = nullptr;
   DevTensor *sh_gate = nullptr, *sh_up = nullptr, *sh_down = nullptr;
@@ -361,7 +362,37 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
   const int H = c.hidden_size;
   int rc;
   const unsigned ab = e->ablate;   // timing experiments only: results are wrong when set
-  if (L.ssm) {
+  if (L.ssm && L.wperm) {
+    // [in_proj | attn_gate] GEMV and the GDN step as one cluster kernel
+    GdnParams g{};
+    g.in_norm = (const float*)L.attn_norm->d;
+    g.eps = c.rms_eps;
+    g.H = H;
+    g.nv = c.ssm_nv;
+    g.nk = c.ssm_nk;
+    g.dv = c.ssm_dv;
+    g.K = c.ssm_conv_kernel;
+    g.C = e->C;
+    g.conv_w = (const float*)L.conv1d->d;
+    g.ring = L.ring;
+    g.w_alpha = (const float*)L.alpha->d;
+    g.w_beta = (const float*)L.beta->d;
+    g.ssm_a = (const float*)L.ssm_a->d;
+    g.dt_bias = (const float*)L.dt_bias->d;
+    g.S = L.S;
+    g.y = e->y;
+    g.step = L.step;
+    g.done = L.done;
+    if ((rc = launch_fused_inproj_gdn(L.wperm, H, e->xcur, (const float*)L.attn_norm->d, c.rms_eps, g, e->z, e->err,
+                                      e->st, pdl)))
+      return rc;
+    mark(e, K_GDN);
+    xch_commit(e);
+    if (!(ab & 8) && (rc = gemv(e, L.ssm_out->type, e->di, {M(L.ssm_out, e->x)}, e->y, (ab & 128) ? PRO_NONE : PRO_HEADNORM_GATE,
+                   (const float*)L.ssm_norm->d, e->z, c.ssm_dv, residual_epi(e), nullptr, pdl)))
+      return rc;
+    if ((rc = tp_sum_x(e))) return rc;
+  } else if (L.ssm) {
     // [in_proj | attn_gate] on RMSNorm(x)
     if (ab & 1) {
     } else if (L.in_proj->type == L.gate->type) {
@@ -1047,6 +1078,32 @@ int inferno_engine_finalize(InfernoEngine* e) {
         (rc = dalloc(e, &e->moe_w, K + 1)) || (rc = dalloc(e, &e->moe_h, (size_t)(K + 1) * c.expert_ffn)) ||
         (rc = dalloc(e, &e->moe_y, (size_t)(K + 1) * H)))
       return rc;
+  }
+  {
+    // fused in_proj + GDN (one value head per q/k group, Q4_K projections):
+    // opt-in -- its cluster launch cannot overlap the preceding kernel under
+    // programmatic dependent launch and measured slower than the two kernels
+    // (0.79 vs 0.67 ms/token on qwen35-0.8b)
+    const char* nf = getenv("INFERNO_B200_FUSED_GDN");
+    const char* pe = getenv("INFERNO_B200_PERSISTENT");
+    const bool want = (nf && atoi(nf) != 0) && !(pe && atoi(pe) != 0) && c.tp_size == 1 && !e->dump &&
+                      c.ssm_nk == c.ssm_nv && c.ssm_dk == 128 && c.ssm_dv == 128 && c.ssm_conv_kernel <= 4 &&
+                      H % 256 == 0 && H <= 8192;
+    for (auto& L : e->layers) {
+      if (!want || !L.ssm || L.in_proj->type != T_Q4_K || L.gate->type != T_Q4_K) continue;
+      const size_t rb = (size_t)(H / 256) * 144, blk = 128 * rb;
+      const int nv = c.ssm_nv, nk = c.ssm_nk;
+      if ((rc = dalloc(e, (uint8_t**)&L.wperm, (size_t)nv * 512 * rb))) return rc;
+      const uint8_t* ip = (const uint8_t*)L.in_proj->d;
+      const uint8_t* gp = (const uint8_t*)L.gate->d;
+      uint8_t* dst = (uint8_t*)L.wperm;
+      for (int h = 0; h < nv; ++h) {
+        INF_CUDA_TRY(cudaMemcpyAsync(dst + (size_t)(4 * h + 0) * blk, ip + (size_t)h * blk, blk, cudaMemcpyDeviceToDevice, e->st));
+        INF_CUDA_TRY(cudaMemcpyAsync(dst + (size_t)(4 * h + 1) * blk, ip + (size_t)(nk + h) * blk, blk, cudaMemcpyDeviceToDevice, e->st));
+        INF_CUDA_TRY(cudaMemcpyAsync(dst + (size_t)(4 * h + 2) * blk, ip + (size_t)(2 * nk + h) * blk, blk, cudaMemcpyDeviceToDevice, e->st));
+        INF_CUDA_TRY(cudaMemcpyAsync(dst + (size_t)(4 * h + 3) * blk, gp + (size_t)h * blk, blk, cudaMemcpyDeviceToDevice, e->st));
+      }
+    }
   }
   e->xcur = e->x;
   if (e->tp && (rc = setup_xch(e))) return rc;

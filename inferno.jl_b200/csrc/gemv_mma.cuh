@@ -605,39 +605,6 @@ __device__ __forceinline__ void mma_sb_q6kr(const uint8_t* gb, const uint8_t* xq
   corr[1] = fmaf(32.0f * db, tb, corr[1]);
 }
 
-// Regroup a Q6_K matrix (rows % 16 == 0) into the T_Q6_KR layout: one CTA of
-// 32 threads per (16-row group, super-block).
-__global__ void __launch_bounds__(32) repack_q6k_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
-                                                        int nsb) {
-  const int G = blockIdx.x, sb = blockIdx.y, L = threadIdx.x;
-  const int g = L >> 2, c = L & 3;
-  const size_t rb = (size_t)nsb * 210;
-  uint8_t* out = dst + ((size_t)G * nsb + sb) * Q6R_BLOCK;
-  auto word = [&](int row, int w) -> uint32_t {
-    const uint8_t* b = src + (size_t)row * rb + (size_t)sb * 210;
-    const int off = w < 8 ? 64 * (w >> 2) + 32 * ((w >> 1) & 1) + 16 * (w & 1) + 4 * c
-                          : 128 + 32 * ((w - 8) >> 1) + 16 * ((w - 8) & 1) + 4 * c;
-    return (uint32_t)b[off] | ((uint32_t)b[off + 1] << 8) | ((uint32_t)b[off + 2] << 16) | ((uint32_t)b[off + 3] << 24);
-  };
-  const int ra = 16 * G + g, rbw = ra + 8;
-#pragma unroll
-  for (int i = 0; i < 6; ++i) {
-    uint32_t v[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int w = 4 * i + j;
-      v[j] = w < 12 ? word(ra, w) : word(rbw, w - 12);
-    }
-    *(uint4*)(out + (i * 32 + L) * 16) = make_uint4(v[0], v[1], v[2], v[3]);
-  }
-  if (L < 16) {
-    const uint8_t* b = src + (size_t)(16 * G + L) * rb + (size_t)sb * 210;
-    for (int j = 0; j < 16; ++j) out[3072 + L * 16 + j] = b[192 + j];
-    out[3328 + L * 2] = b[208];
-    out[3328 + L * 2 + 1] = b[209];
-  }
-}
-
 template <int TYPE, int NW, int MODE>
 __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];

@@ -69,6 +69,13 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl);
 // Q6_K -> the engine-internal 16-row-group layout T_Q6_KR (same byte count)
 int launch_repack_q6k(const void* src, void* dst, int rows, int inner, cudaStream_t st);
 int launch_dequant(int type, const void* src, long long n, float* dst, cudaStream_t st);
+struct GdnParams;
+struct AttnParams;
+// fused [in_proj | attn_gate] GEMV + GDN step (fused_gdn.cu); Wperm holds the
+// head-regrouped rows [q_h | k_h | v_h | z_h] x nv
+int launch_fused_inproj_gdn(const void* Wperm, int H, const float* x, const float* attn_norm, float eps,
+                            const GdnParams& g, float* z, int* err, cudaStream_t st, bool pdl);
+
 // chunked prefill (prefill.cu): tokens per chunk = the batched GEMV's columns
 constexpr int PF_MAX_T = 8;
 struct GdnParams;
