@@ -184,3 +184,26 @@ def test_prefill_graph_replays_match_eager(tiny):
     assert outs[0][0] == outs[1][0] == outs[2][0]
     assert np.array_equal(outs[0][1], outs[1][1]) and np.array_equal(outs[1][1], outs[2][1])
     assert outs[3][0] == ref2[0] and np.array_equal(outs[3][1], ref2[1])
+
+
+def test_fused_inproj_gdn_opt_in(monkeypatch):
+    """INFERNO_B200_FUSED_GDN=1 (configs with one value head per q/k group):
+    the 8-CTA cluster kernel replaces the in_proj GEMV + GDN step; logits and
+    greedy tokens match the two-kernel path and the oracle."""
+    import dataclasses
+    spec = dataclasses.replace(S.CONFIGS["tiny"], ssm_nk=4)      # nv == nk == 4
+    T = S.make_model(spec, seed=23)
+    prompt = S.tokens(23, 9, spec.vocab)
+    m0 = Model(spec, T)
+    want = m0.generate(prompt, 12)
+    am0, lg0 = m0.forward(prompt, 0)
+    m0.close()
+    monkeypatch.setenv("INFERNO_B200_FUSED_GDN", "1")
+    m1 = Model(spec, T)
+    got = m1.generate(prompt, 12)
+    am1, lg1 = m1.forward(prompt, 0)
+    m1.close()
+    assert got == want and am1 == am0
+    assert rel(lg1, lg0) < 1e-4
+    orc = O.OracleModel(spec, T)
+    assert got == orc.generate(prompt, 12)
