@@ -158,3 +158,61 @@ def test_oracle_greedy_first_max():
     m = O.OracleModel(spec, T)
     tok, lg = m.forward([7], 0)
     assert np.all(lg == lg[0]) and tok == 0
+
+
+# ---- sampler restatement (src/ModelCPU.jl:1123-1225) -------------------------
+def _np_softmax_sample(logits, temperature, top_p=1.0, top_k=0, min_p=0.0, presence=0.0, repetition=1.0,
+                       seen=(), r=0.5):
+    """Independent numpy statement of generate_cpu's penalties + softmax_sample."""
+    l = np.asarray(logits, np.float64).copy()
+    for t in set(int(s) for s in seen):
+        l[t] -= presence
+        if repetition != 1.0:
+            l[t] = l[t] / repetition if l[t] > 0 else l[t] * repetition
+    if temperature == 0:
+        return int(np.argmax(l))
+    l = l / temperature
+    if top_k > 0:
+        keep = np.argsort(-l, kind="stable")[:top_k]
+        m = np.full_like(l, -np.inf)
+        m[keep] = l[keep]
+        l = m
+    p = np.exp(l - l.max())
+    p /= p.sum()
+    if top_p < 1.0:
+        order = np.argsort(-p, kind="stable")
+        c = np.cumsum(p[order])
+        cut = int(np.searchsorted(c, top_p)) + 1
+        q = np.zeros_like(p)
+        q[order[:cut]] = p[order[:cut]]
+        p = q / q.sum()
+    if min_p > 0:
+        p[p < p.max() * min_p] = 0
+        p /= p.sum()
+    c = np.cumsum(p)
+    i = int(np.searchsorted(c, r))
+    return min(i, len(p) - 1)
+
+
+@pytest.mark.parametrize("kw", [dict(temperature=0.0), dict(temperature=1.0, top_k=1),
+                                dict(temperature=0.8, top_k=10), dict(temperature=1.2, top_p=0.7),
+                                dict(temperature=0.9, top_k=50, top_p=0.9, min_p=0.1),
+                                dict(temperature=1.0, presence=1.5, repetition=1.2, top_k=20)])
+def test_oracle_sampler_vs_numpy(kw):
+    rng = np.random.default_rng(9)
+    agree = 0
+    for _ in range(40):
+        logits = (rng.standard_normal(2000) * 3).astype(np.float32)
+        seen = rng.integers(0, 2000, 30)
+        r = float(rng.random())
+        a = O.softmax_sample(logits, kw.get("temperature", 1.0), kw.get("top_p", 1.0), kw.get("top_k", 0),
+                             kw.get("min_p", 0.0), kw.get("presence", 0.0), kw.get("repetition", 1.0), seen, r)
+        b = _np_softmax_sample(logits, seen=seen, r=r, **kw)
+        agree += a == b
+    assert agree >= 39     # fp32 vs fp64 can move a draw that lands on a boundary
+
+
+def test_oracle_sampler_first_max_and_ties():
+    l = np.array([1, 5, 5, 2], np.float32)
+    assert O.softmax_sample(l, 0.0) == 1                       # argmax: first maximum
+    assert O.softmax_sample(l, 1.0, top_k=1, r=0.99) == 1      # stable top-k keeps the lower index
