@@ -62,6 +62,18 @@ void q4_k_gemv(const uint8_t* weight, const float* x, float* out, void* q8_buf, 
 void q5_k_gemv(const uint8_t* weight, const float* x, float* out, void* q8_buf, int inner_dim, int outer_dim);
 void q6_k_gemv(const uint8_t* weight, const float* x, float* out, void* q8_buf, int inner_dim, int outer_dim);
 void q8_0_gemv(const uint8_t* weight, const float* x, float* out, int inner_dim, int outer_dim);
+/* The Q8_K helpers QuantizedKernels.jl also binds (QuantizedKernels.jl:148-175,
+ * replacing quant_kernels.c:166-196, :204-519, :531-559), computed on the
+ * device from host pointers and bit-identical to the reference's AVX2 + FMA
+ * build.  y of quantize_row_q8_K receives k / 256 blocks of 292 bytes
+ * {float d; int8 qs[256]; int16 bsums[16]}.  x of vec_dot_* are nb weight
+ * blocks, y nb block_q8_K (block_q8_0 for vec_dot_q8_0_q8_0).  A failing
+ * vec_dot returns NaN; the message is in inferno_last_error(). */
+void quantize_row_q8_K(const float* x, void* y, int64_t k);
+float vec_dot_q4_K_q8_K(const void* x, const void* y, int nb);
+float vec_dot_q5_K_q8_K(const void* x, const void* y, int nb);
+float vec_dot_q6_K_q8_K(const void* x, const void* y, int nb);
+float vec_dot_q8_0_q8_0(const void* x, const void* y, int nb);
 /* frees the cached device copies of compatibility-tier weights */
 int inferno_compat_release(void);
 

@@ -68,6 +68,7 @@ struct CompatState {
   std::unordered_map<const void*, W> weights;
   float* dx = nullptr; size_t dx_cap = 0;
   float* dy = nullptr; size_t dy_cap = 0;
+  uint8_t* db = nullptr; size_t db_cap = 0;   // block bytes of the Q8_K helpers
 };
 CompatState g_compat;
 std::mutex g_compat_mu;
@@ -143,6 +144,68 @@ static int compat_gemv(int type, const uint8_t* W, const float* x, float* out, i
   INF_CUDA_TRY(cudaMemcpyAsync(out, g_compat.dy, (size_t)outer * 4, cudaMemcpyDeviceToHost, g_compat.stream));
   INF_CUDA_TRY(cudaStreamSynchronize(g_compat.stream));
   return 0;
+}
+
+static int grow_bytes(uint8_t** p, size_t* cap, size_t n) {
+  if (*cap >= n) return 0;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  INF_CUDA_TRY(cudaMalloc(p, n));
+  *cap = n;
+  return 0;
+}
+
+// quantize_row_q8_K on the device: host x[k] -> host block_q8_K[k / 256]
+static int compat_quantize_q8k(const float* x, void* y, int64_t k) {
+  std::lock_guard<std::mutex> lk(g_compat_mu);
+  int rc;
+  // QuantizedKernels.jl:151-152 passes k as a Cint, so the upper half of the
+  // 64-bit argument is not defined there: read the low 32 bits in that case
+  if (k < 0 || k > 0x7fffffffLL) k = (int64_t)(uint32_t)k;
+  if (!x || !y) return set_error(INFERNO_EINVAL, "quantize_row_q8_K: null pointer");
+  if (k < 0 || k % 256) return set_error(INFERNO_EINVAL, "quantize_row_q8_K: k = %lld is not a multiple of 256",
+                                         (long long)k);
+  if (!k) return 0;
+  if ((rc = compat_init())) return rc;
+  INF_CUDA_TRY(cudaSetDevice(g_compat.device));
+  const size_t ybytes = (size_t)(k / 256) * 292;
+  if ((rc = grow(&g_compat.dx, &g_compat.dx_cap, (size_t)k))) return rc;
+  if ((rc = grow_bytes(&g_compat.db, &g_compat.db_cap, ybytes))) return rc;
+  INF_CUDA_TRY(cudaMemcpyAsync(g_compat.dx, x, (size_t)k * 4, cudaMemcpyHostToDevice, g_compat.stream));
+  if ((rc = launch_quantize_q8k(g_compat.dx, g_compat.db, k / 256, g_compat.stream))) return rc;
+  INF_CUDA_TRY(cudaMemcpyAsync(y, g_compat.db, ybytes, cudaMemcpyDeviceToHost, g_compat.stream));
+  INF_CUDA_TRY(cudaStreamSynchronize(g_compat.stream));
+  return 0;
+}
+
+// one block-row dot product x (weight blocks) . y (Q8_K or Q8_0 blocks), host pointers
+static int compat_vec_dot(int type, const void* x, const void* y, int nb, float* out) {
+  std::lock_guard<std::mutex> lk(g_compat_mu);
+  int rc;
+  *out = 0.0f;
+  if (nb < 0 || (nb && (!x || !y))) return set_error(INFERNO_EINVAL, "vec_dot: bad arguments (nb = %d)", nb);
+  if (!nb) return 0;
+  if ((rc = compat_init())) return rc;
+  INF_CUDA_TRY(cudaSetDevice(g_compat.device));
+  const size_t xb = (size_t)nb * bb_of(type), yb = (size_t)nb * (type == T_Q8_0 ? 34 : 292);
+  const size_t yoff = (xb + 15) / 16 * 16;
+  if ((rc = grow_bytes(&g_compat.db, &g_compat.db_cap, yoff + yb))) return rc;
+  if ((rc = grow(&g_compat.dy, &g_compat.dy_cap, 1))) return rc;
+  INF_CUDA_TRY(cudaMemcpyAsync(g_compat.db, x, xb, cudaMemcpyHostToDevice, g_compat.stream));
+  INF_CUDA_TRY(cudaMemcpyAsync(g_compat.db + yoff, y, yb, cudaMemcpyHostToDevice, g_compat.stream));
+  if ((rc = launch_vec_dot_q8k(type, g_compat.db, g_compat.db + yoff, nb, g_compat.dy, g_compat.stream))) return rc;
+  INF_CUDA_TRY(cudaMemcpyAsync(out, g_compat.dy, 4, cudaMemcpyDeviceToHost, g_compat.stream));
+  INF_CUDA_TRY(cudaStreamSynchronize(g_compat.stream));
+  return 0;
+}
+
+static float compat_dot_report(int type, const void* x, const void* y, int nb, const char* what) {
+  float r = 0.0f;
+  if (compat_vec_dot(type, x, y, nb, &r)) {
+    fprintf(stderr, "libinferno_b200: %s: %s\n", what, last_error());
+    return NAN;
+  }
+  return r;
 }
 
 }  // namespace inf
@@ -258,6 +321,22 @@ void q8_0_gemv(const uint8_t* weight, const float* x, float* out, int inner_dim,
   compat_report(compat_gemv(T_Q8_0, weight, x, out, inner_dim, outer_dim), "q8_0_gemv");
 }
 
+void quantize_row_q8_K(const float* x, void* y, int64_t k) {
+  compat_report(compat_quantize_q8k(x, y, k), "quantize_row_q8_K");
+}
+float vec_dot_q4_K_q8_K(const void* x, const void* y, int nb) {
+  return compat_dot_report(T_Q4_K, x, y, nb, "vec_dot_q4_K_q8_K");
+}
+float vec_dot_q5_K_q8_K(const void* x, const void* y, int nb) {
+  return compat_dot_report(T_Q5_K, x, y, nb, "vec_dot_q5_K_q8_K");
+}
+float vec_dot_q6_K_q8_K(const void* x, const void* y, int nb) {
+  return compat_dot_report(T_Q6_K, x, y, nb, "vec_dot_q6_K_q8_K");
+}
+float vec_dot_q8_0_q8_0(const void* x, const void* y, int nb) {
+  return compat_dot_report(T_Q8_0, x, y, nb, "vec_dot_q8_0_q8_0");
+}
+
 int inferno_compat_release(void) {
   std::lock_guard<std::mutex> lk(g_compat_mu);
   if (!g_compat.init) return 0;
@@ -266,8 +345,10 @@ int inferno_compat_release(void) {
   g_compat.weights.clear();
   if (g_compat.dx) cudaFree(g_compat.dx);
   if (g_compat.dy) cudaFree(g_compat.dy);
+  if (g_compat.db) cudaFree(g_compat.db);
   g_compat.dx = g_compat.dy = nullptr;
-  g_compat.dx_cap = g_compat.dy_cap = 0;
+  g_compat.db = nullptr;
+  g_compat.dx_cap = g_compat.dy_cap = g_compat.db_cap = 0;
   return 0;
 }
 

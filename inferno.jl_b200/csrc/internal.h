@@ -69,6 +69,9 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl);
 // Q6_K -> the engine-internal 16-row-group layout T_Q6_KR (same byte count)
 int launch_repack_q6k(const void* src, void* dst, int rows, int inner, cudaStream_t st);
 int launch_dequant(int type, const void* src, long long n, float* dst, cudaStream_t st);
+// Q8_K helpers of the compatibility tier (q8k.cu)
+int launch_quantize_q8k(const float* x, void* y, long long nblocks, cudaStream_t st);
+int launch_vec_dot_q8k(int type, const void* x, const void* y, int nb, float* out, cudaStream_t st);
 struct GdnParams;
 struct AttnParams;
 // fused [in_proj | attn_gate] GEMV + GDN step (fused_gdn.cu); Wperm holds the

@@ -36,6 +36,7 @@ class InfernoConfig(C.Structure):
 EXPORTS = [
     "inferno_last_error", "inferno_version", "inferno_device_error",
     "q4_k_gemv", "q5_k_gemv", "q6_k_gemv", "q8_0_gemv", "inferno_compat_release",
+    "quantize_row_q8_K", "vec_dot_q4_K_q8_K", "vec_dot_q5_K_q8_K", "vec_dot_q6_K_q8_K", "vec_dot_q8_0_q8_0",
     "inferno_dequantize", "inferno_gemv", "inferno_gemv_ex", "inferno_gemv_swiglu",
     "inferno_engine_create", "inferno_engine_upload_tensor", "inferno_engine_finalize",
     "inferno_layer_forward", "inferno_forward_tokens", "inferno_decode_greedy",
@@ -69,6 +70,11 @@ def _sig(L0):
         getattr(L, nm).restype = None
     L.q8_0_gemv.argtypes = [p, p, p, i, i]
     L.q8_0_gemv.restype = None
+    L.quantize_row_q8_K.argtypes = [p, p, i64]
+    L.quantize_row_q8_K.restype = None
+    for nm in ("vec_dot_q4_K_q8_K", "vec_dot_q5_K_q8_K", "vec_dot_q6_K_q8_K", "vec_dot_q8_0_q8_0"):
+        getattr(L, nm).argtypes = [p, p, i]
+        getattr(L, nm).restype = f
     L.inferno_dequantize.argtypes = [i, p, i64, p, p]
     L.inferno_gemv.argtypes = [i, p, p, p, i, i, i, p]
     L.inferno_gemv_ex.argtypes = [i, p, p, p, i, i, i, i, p, f, i, p, i, p]

@@ -562,7 +562,174 @@ void layer_forward(Model& m, int li, float* x, int pos) {
 
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// The reference's Q8_K activation path (src/kernels/quant_kernels.c), restated
+// scalar with the lane structure of its AVX2 + FMA build: 256-bit integer
+// lane k of a 32-byte chunk covers bytes 4k..4k+3, so a block contributes
+// eight exact int32 lane sums; each lane keeps its own float accumulator
+// (fma over the blocks in order) and the eight accumulators are combined in
+// hsum_float_8's order (quant_kernels.c:91-98).
+// ---------------------------------------------------------------------------
+namespace q8k {
+
+constexpr int QK = 256;
+constexpr int Q8K_BYTES = 292;  // float d; int8 qs[256]; int16 bsums[16]
+
+float hsum8(const float a[8]) {
+  float s0 = a[4] + a[0], s1 = a[5] + a[1], s2 = a[6] + a[2], s3 = a[7] + a[3];
+  return (s0 + s2) + (s1 + s3);
+}
+
+// 6-bit scale / min of sub-block j (the utmp shuffle of quant_kernels.c:224-230)
+void k4_scale_min(const uint8_t* s, int j, int* sc, int* m) {
+  if (j < 4) { *sc = s[j] & 63; *m = s[j + 4] & 63; }
+  else { *sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4); *m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4); }
+}
+
+// Q4_K / Q5_K (quant_kernels.c:204-255, :311-398): lane k of block i is
+// sum_j sc[2j] * sum_{b=4k..4k+3} lo_j[b] q8[64j+b] + sc[2j+1] * sum hi_j[b] q8[64j+32+b]
+template <bool Q5>
+float vec_dot_k45(const uint8_t* x, const uint8_t* y, int nb) {
+  const int bb = Q5 ? 176 : 144;
+  float acc[8] = {0}, accm[4] = {0}, summs = 0.0f;
+  for (int i = 0; i < nb; ++i) {
+    const uint8_t* xb = x + (size_t)i * bb;
+    const uint8_t* yb = y + (size_t)i * Q8K_BYTES;
+    float yd;
+    memcpy(&yd, yb, 4);
+    const int8_t* q8 = (const int8_t*)(yb + 4);
+    int16_t bs[16];
+    memcpy(bs, yb + 260, 32);
+    const float d = yd * h2f(rd16(xb)), dmin = -yd * h2f(rd16(xb + 2));
+    const uint8_t* sc6 = xb + 4;
+    const uint8_t* qh = Q5 ? xb + 16 : nullptr;
+    const uint8_t* qs = xb + (Q5 ? 48 : 16);
+    int sc[8], mn[8];
+    for (int j = 0; j < 8; ++j) k4_scale_min(sc6, j, &sc[j], &mn[j]);
+    int32_t lane[8] = {0};
+    for (int j = 0; j < 4; ++j)
+      for (int k = 0; k < 8; ++k) {
+        int lo = 0, hi = 0;
+        for (int b = 4 * k; b < 4 * k + 4; ++b) {
+          int ql = qs[32 * j + b] & 15, qhh = qs[32 * j + b] >> 4;
+          if (Q5) { ql |= ((qh[b] >> (2 * j)) & 1) << 4; qhh |= ((qh[b] >> (2 * j + 1)) & 1) << 4; }
+          lo += ql * q8[64 * j + b];
+          hi += qhh * q8[64 * j + 32 + b];
+        }
+        lane[k] += sc[2 * j] * lo + sc[2 * j + 1] * hi;
+      }
+    for (int k = 0; k < 8; ++k) acc[k] = fmaf(d, (float)lane[k], acc[k]);
+    int32_t prod[4];
+    for (int l = 0; l < 4; ++l) {
+      const int16_t s0 = (int16_t)(bs[4 * l] + bs[4 * l + 1]), s1 = (int16_t)(bs[4 * l + 2] + bs[4 * l + 3]);
+      prod[l] = mn[2 * l] * s0 + mn[2 * l + 1] * s1;
+    }
+    if (Q5) {
+      // scalar `summs += dmin * hsum` of the FMA build is contracted to an fma
+      summs = fmaf(dmin, (float)((prod[0] + prod[1]) + (prod[2] + prod[3])), summs);
+    } else {
+      for (int l = 0; l < 4; ++l) accm[l] = fmaf(dmin, (float)prod[l], accm[l]);
+    }
+  }
+  if (Q5) return hsum8(acc) + summs;
+  return hsum8(acc) + ((accm[0] + accm[2]) + (accm[1] + accm[3]));
+}
+
+// Q6_K (quant_kernels.c:440-519): chunk t of half j holds values
+// 128j + 32t + b with scales 8j+2t (bytes 0-15) and 8j+2t+1 (bytes 16-31)
+float vec_dot_q6(const uint8_t* x, const uint8_t* y, int nb) {
+  float acc[8] = {0};
+  for (int i = 0; i < nb; ++i) {
+    const uint8_t* xb = x + (size_t)i * 210;
+    const uint8_t* yb = y + (size_t)i * Q8K_BYTES;
+    float yd;
+    memcpy(&yd, yb, 4);
+    const int8_t* q8 = (const int8_t*)(yb + 4);
+    const uint8_t *ql = xb, *qh = xb + 128;
+    const int8_t* sc = (const int8_t*)(xb + 192);
+    const float d = yd * h2f(rd16(xb + 208));
+    int32_t lane[8] = {0};
+    for (int j = 0; j < 2; ++j)
+      for (int t = 0; t < 4; ++t)
+        for (int k = 0; k < 8; ++k) {
+          int s = 0;
+          for (int b = 4 * k; b < 4 * k + 4; ++b) {
+            const uint8_t lb = ql[64 * j + (t & 1) * 32 + b];
+            const int q = ((t < 2 ? lb : lb >> 4) & 15) | (((qh[32 * j + b] >> (2 * t)) & 3) << 4);
+            s += (q - 32) * q8[128 * j + 32 * t + b];
+          }
+          lane[k] += sc[8 * j + 2 * t + (k >= 4)] * s;
+        }
+    for (int k = 0; k < 8; ++k) acc[k] = fmaf(d, (float)lane[k], acc[k]);
+  }
+  return hsum8(acc);
+}
+
+// Q8_0 x Q8_0 (quant_kernels.c:531-559, mul_sum_i8_pairs_float :146-158):
+// |x| times y carrying x's sign (int8 wrap of -(-128)), pair sums saturated to int16
+float vec_dot_q80(const uint8_t* x, const uint8_t* y, int nb) {
+  float acc[8] = {0};
+  for (int i = 0; i < nb; ++i) {
+    const uint8_t* xb = x + (size_t)i * 34;
+    const uint8_t* yb = y + (size_t)i * 34;
+    const float d = h2f(rd16(xb)) * h2f(rd16(yb));
+    const int8_t *qx = (const int8_t*)(xb + 2), *qy = (const int8_t*)(yb + 2);
+    for (int k = 0; k < 8; ++k) {
+      int32_t s = 0;
+      for (int p = 0; p < 2; ++p) {
+        int pair = 0;
+        for (int b = 4 * k + 2 * p; b < 4 * k + 2 * p + 2; ++b) {
+          const int ax = qx[b] < 0 ? -(int)qx[b] : qx[b];
+          const int sy = qx[b] < 0 ? (int8_t)(-qy[b]) : (qx[b] == 0 ? 0 : qy[b]);
+          pair += ax * sy;
+        }
+        s += std::min(32767, std::max(-32768, pair));
+      }
+      acc[k] = fmaf(d, (float)s, acc[k]);
+    }
+  }
+  return hsum8(acc);
+}
+
+// quantize_row_q8_K (quant_kernels.c:166-196)
+void quantize_q8k(const float* x, uint8_t* y, int64_t k) {
+  for (int64_t i = 0; i < k / QK; ++i) {
+    const float* src = x + i * QK;
+    uint8_t* yb = y + i * Q8K_BYTES;
+    float amax = 0.0f;
+    for (int j = 0; j < QK; ++j) {
+      float ax = fabsf(src[j]);
+      if (ax > amax) amax = ax;
+    }
+    const float d = amax / 127.0f, id = d != 0.0f ? 1.0f / d : 0.0f;
+    memcpy(yb, &d, 4);
+    for (int j = 0; j < QK; j += 16) {
+      int sum = 0;
+      for (int l = 0; l < 16; ++l) {
+        const int8_t q = (int8_t)roundf(src[j + l] * id);
+        yb[4 + j + l] = (uint8_t)q;
+        sum += q;
+      }
+      const int16_t s16 = (int16_t)sum;
+      memcpy(yb + 260 + 2 * (j / 16), &s16, 2);
+    }
+  }
+}
+
+}  // namespace q8k
+
 extern "C" {
+
+void orc_quantize_row_q8_K(const float* x, uint8_t* y, int64_t k) { q8k::quantize_q8k(x, y, k); }
+float orc_vec_dot_q8k(int type, const uint8_t* x, const uint8_t* y, int nb) {
+  switch (type) {
+    case 12: return q8k::vec_dot_k45<false>(x, y, nb);
+    case 13: return q8k::vec_dot_k45<true>(x, y, nb);
+    case 14: return q8k::vec_dot_q6(x, y, nb);
+    case 8: return q8k::vec_dot_q80(x, y, nb);
+  }
+  return NAN;
+}
 
 int orc_dequant(int type, const uint8_t* src, int64_t n, float* dst) { return dequant(type, src, n, dst); }
 

@@ -36,6 +36,9 @@ def lib():
         L.orc_gemv.argtypes = [i, p, p, p, i, i, i]
         L.orc_flash_attention.argtypes = [p, p, p, p, i, i, C.c_float, i, i]
         L.orc_standard_attention.argtypes = [p, p, p, p, i, i, C.c_float, i, i]
+        L.orc_quantize_row_q8_K.argtypes = [p, p, i64]
+        L.orc_vec_dot_q8k.argtypes = [i, p, p, i]
+        L.orc_vec_dot_q8k.restype = C.c_float
         L.orc_gdn_recurrence.argtypes = [i, i, i, i, p, p, p, p, p, p, p]
         L.orc_model_create.restype = p
         L.orc_model_create.argtypes = [p, p]
@@ -73,6 +76,25 @@ def gemv(ggml_type: int, W: np.ndarray, x: np.ndarray, inner: int, outer: int) -
     if rc:
         raise ValueError(f"orc_gemv rc={rc}")
     return y
+
+
+Q8K_BYTES = 292     # block_q8_K: float d, int8 qs[256], int16 bsums[16]
+
+
+def quantize_q8k(x) -> np.ndarray:
+    """quantize_row_q8_K (src/kernels/quant_kernels.c:166-196) -> raw block bytes."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.zeros(x.size // 256 * Q8K_BYTES, np.uint8)
+    lib().orc_quantize_row_q8_K(_ptr(x), _ptr(y), x.size)
+    return y
+
+
+def vec_dot_q8k(ggml_type: int, xblocks, yblocks, nb: int) -> float:
+    """vec_dot_q{4,5,6}_K_q8_K / vec_dot_q8_0_q8_0 (quant_kernels.c:204-559),
+    restated with the lane and accumulation order of the AVX2 + FMA build."""
+    xb = np.ascontiguousarray(xblocks, dtype=np.uint8)
+    yb = np.ascontiguousarray(yblocks, dtype=np.uint8)
+    return float(lib().orc_vec_dot_q8k(ggml_type, _ptr(xb), _ptr(yb), nb))
 
 
 def flash_attention(q, ck, cv, kvh, seq_len, scale, hd, nkv, standard=False):
@@ -182,6 +204,10 @@ def ref_lib():
     for nm in ("q4_k_gemv", "q5_k_gemv", "q6_k_gemv"):
         getattr(L, nm).argtypes = [p, p, p, p, i, i]
     L.q8_0_gemv.argtypes = [p, p, p, i, i]
+    L.quantize_row_q8_K.argtypes = [p, p, C.c_int64]
+    for nm in ("vec_dot_q4_K_q8_K", "vec_dot_q5_K_q8_K", "vec_dot_q6_K_q8_K", "vec_dot_q8_0_q8_0"):
+        getattr(L, nm).argtypes = [p, p, i]
+        getattr(L, nm).restype = C.c_float
     return L
 
 

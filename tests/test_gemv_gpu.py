@@ -164,3 +164,28 @@ def test_compat_tier_host_pointers(t):
             fn = {S.Q4_K: lib().q4_k_gemv, S.Q6_K: lib().q6_k_gemv}[t]
             fn(P(q.ctypes.data), P(x.ctypes.data), P(y.ctypes.data), None, inner, rows)
         assert _rel(y, ref) < GEMV_RTOL
+
+
+# ---- Q8_K helpers of the compatibility tier vs the oracle (bit-exact) -------
+def test_compat_quantize_row_q8k_bitwise():
+    rng = np.random.default_rng(21)
+    for n, scale in ((256, 1.0), (4096, 1e-3), (65536, 30.0)):
+        x = (rng.standard_normal(n) * scale).astype(np.float32)
+        x[256:512] = 0.0 if n > 256 else x[256:512]
+        y = np.zeros(n // 256 * O.Q8K_BYTES, np.uint8)
+        lib().quantize_row_q8_K(x.ctypes.data, y.ctypes.data, n)
+        assert np.array_equal(y, O.quantize_q8k(x))
+
+
+@pytest.mark.parametrize("t", [S.Q4_K, S.Q5_K, S.Q6_K, S.Q8_0])
+def test_compat_vec_dot_bitwise(t):
+    from q8k_cases import random_blocks, random_q8k
+    rng = np.random.default_rng(100 + t)
+    fn = {S.Q4_K: lib().vec_dot_q4_K_q8_K, S.Q5_K: lib().vec_dot_q5_K_q8_K, S.Q6_K: lib().vec_dot_q6_K_q8_K,
+          S.Q8_0: lib().vec_dot_q8_0_q8_0}[t]
+    for nb in [1, 2, 31, 32, 33, 64, 200] + [int(v) for v in rng.integers(1, 100, 40)]:
+        x = random_blocks(rng, t, nb)
+        y = random_blocks(rng, S.Q8_0, nb) if t == S.Q8_0 else random_q8k(rng, nb)
+        a = np.float32(fn(x.ctypes.data, y.ctypes.data, nb))
+        b = np.float32(O.vec_dot_q8k(t, x, y, nb))
+        assert a.view(np.uint32) == b.view(np.uint32), (nb, a, b)

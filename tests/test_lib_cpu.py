@@ -3,6 +3,7 @@ the library loads, exports every function the header declares, rejects bad
 arguments with a status + message, and the host-side GGUF / config / byte
 accounting matches the reference's loader conventions."""
 import ctypes as C
+import math
 import re
 from pathlib import Path
 
@@ -11,6 +12,7 @@ import pytest
 
 from inferno_b200 import synth as S
 from inferno_b200._lib import EXPORTS, InfernoConfig, lib
+import oracle as O
 
 ROOT = Path(__file__).resolve().parent.parent
 HEADER = ROOT / "include" / "inferno_b200.h"
@@ -18,7 +20,7 @@ HEADER = ROOT / "include" / "inferno_b200.h"
 
 def header_functions():
     txt = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
-    return sorted(set(re.findall(r"\b([a-z_][a-z0-9_]*)\s*\([^;{]*\)\s*;", txt)) - {"sizeof"})
+    return sorted(set(re.findall(r"\b([a-z_][A-Za-z0-9_]*)\s*\([^;{]*\)\s*;", txt)) - {"sizeof"})
 
 
 def test_library_exports_every_header_symbol():
@@ -30,10 +32,30 @@ def test_library_exports_every_header_symbol():
     assert set(EXPORTS) <= set(fns)
 
 
+COMPAT = ("q4_k_gemv", "q5_k_gemv", "q6_k_gemv", "q8_0_gemv", "quantize_row_q8_K",
+          "vec_dot_q4_K_q8_K", "vec_dot_q5_K_q8_K", "vec_dot_q6_K_q8_K", "vec_dot_q8_0_q8_0")
+
+
 def test_compat_symbols_match_reference_names():
-    # src/kernels/quant_kernels.c:602-697 / src/QuantizedKernels.jl:88-143
-    for f in ("q4_k_gemv", "q5_k_gemv", "q6_k_gemv", "q8_0_gemv"):
+    # src/kernels/quant_kernels.c:166-697 / src/QuantizedKernels.jl:88-176
+    for f in COMPAT:
         assert hasattr(lib(), f)
+    ref = O.ref_lib()
+    if ref is not None:      # every symbol the reference's library exports is here too
+        import subprocess
+        out = subprocess.run(["nm", "-D", "--defined-only", str(O.REF_LIB_PATH)], capture_output=True, text=True)
+        names = {ln.split()[-1] for ln in out.stdout.splitlines() if " T " in ln}
+        assert names == set(COMPAT), names
+
+
+def test_q8k_helpers_argument_errors_without_gpu():
+    L = lib()
+    assert math.isnan(L.vec_dot_q4_K_q8_K(None, None, -1))
+    assert b"nb = -1" in L.inferno_last_error()
+    x, y = np.zeros(100, np.float32), np.zeros(292, np.uint8)
+    L.quantize_row_q8_K(x.ctypes.data, y.ctypes.data, 100)
+    assert b"multiple of 256" in L.inferno_last_error()
+    assert L.vec_dot_q6_K_q8_K(None, None, 0) == 0.0       # empty row: no device work
 
 
 def test_argument_errors_without_gpu():

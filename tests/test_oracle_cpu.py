@@ -216,3 +216,41 @@ def test_oracle_sampler_first_max_and_ties():
     l = np.array([1, 5, 5, 2], np.float32)
     assert O.softmax_sample(l, 0.0) == 1                       # argmax: first maximum
     assert O.softmax_sample(l, 1.0, top_k=1, r=0.99) == 1      # stable top-k keeps the lower index
+
+
+# ---- Q8_K activation path of quant_kernels.c, pinned to the reference's own build
+from q8k_cases import random_blocks as _random_blocks, random_q8k as _random_q8k
+
+
+@pytest.fixture(scope="module")
+def ref():
+    L = O.ref_lib()
+    if L is None:
+        pytest.skip("oracle/_ref not built (reference sources absent)")
+    return L
+
+
+def test_quantize_q8k_matches_reference_bitwise(ref):
+    rng = np.random.default_rng(3)
+    for n, scale in ((256, 1.0), (1024, 1e-3), (4096, 50.0)):
+        x = (rng.standard_normal(n) * scale).astype(np.float32)
+        x[:256] = 0.0 if n == 1024 else x[:256]      # an all-zero block: d = 0, id = 0
+        a = O.quantize_q8k(x)
+        b = np.zeros_like(a)
+        ref.quantize_row_q8_K(O._ptr(x), O._ptr(b), n)
+        assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("ggml_type", [12, 13, 14, 8])
+def test_vec_dot_matches_reference_bitwise(ref, ggml_type):
+    rng = np.random.default_rng(ggml_type)
+    fn = {12: ref.vec_dot_q4_K_q8_K, 13: ref.vec_dot_q5_K_q8_K, 14: ref.vec_dot_q6_K_q8_K,
+          8: ref.vec_dot_q8_0_q8_0}[ggml_type]
+    # 400 draws: enough to separate fused from unfused multiply-adds
+    for nb in [1, 3, 4, 16, 57] + list(rng.integers(1, 40, 400)):
+        nb = int(nb)
+        x = _random_blocks(rng, ggml_type, nb)
+        y = _random_blocks(rng, 8, nb) if ggml_type == 8 else _random_q8k(rng, nb)
+        a = np.float32(O.vec_dot_q8k(ggml_type, x, y, nb))
+        b = np.float32(fn(O._ptr(x), O._ptr(y), nb))
+        assert a.view(np.uint32) == b.view(np.uint32), (nb, a, b)
