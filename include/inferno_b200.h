@@ -54,8 +54,11 @@ int inferno_device_error(int device, int clear);
  * the ccalls at src/QuantizedKernels.jl:88-90, 106-108, 125-127, 141-143.
  * Host pointers in, host results out (each call copies x in and y out; a
  * weight array is uploaded on first sight and cached by host pointer, size
- * and a content signature).  Numerics: fp32 activations (the reference
- * quantizes x to Q8_K); q8_buf is accepted and ignored.  void returns as in
+ * and a content signature).  Numerics: by default those of the replaced
+ * library, bit for bit (x quantized to Q8_K on the device, the AVX2 build's
+ * lane and fma order; Q8_0 with fp32 x); with INFERNO_COMPAT_FP32=1 in the
+ * environment, fp32 activations through the engine's GEMV.  q8_buf is
+ * accepted and not written.  void returns as in
  * the reference; failures are printed to stderr and kept in
  * inferno_last_error(). */
 void q4_k_gemv(const uint8_t* weight, const float* x, float* out, void* q8_buf, int inner_dim, int outer_dim);

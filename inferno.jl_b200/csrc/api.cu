@@ -122,6 +122,15 @@ static int grow(float** p, size_t* cap, size_t n) {
   return 0;
 }
 
+static int grow_bytes(uint8_t** p, size_t* cap, size_t n) {
+  if (*cap >= n) return 0;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  INF_CUDA_TRY(cudaMalloc(p, n));
+  *cap = n;
+  return 0;
+}
+
 static int compat_gemv(int type, const uint8_t* W, const float* x, float* out, int inner, int outer) {
   std::lock_guard<std::mutex> lk(g_compat_mu);
   int rc;
@@ -134,6 +143,17 @@ static int compat_gemv(int type, const uint8_t* W, const float* x, float* out, i
   if ((rc = grow(&g_compat.dx, &g_compat.dx_cap, inner))) return rc;
   if ((rc = grow(&g_compat.dy, &g_compat.dy_cap, outer))) return rc;
   INF_CUDA_TRY(cudaMemcpyAsync(g_compat.dx, x, (size_t)inner * 4, cudaMemcpyHostToDevice, g_compat.stream));
+  const char* fp32 = getenv("INFERNO_COMPAT_FP32");
+  if (!(fp32 && fp32[0] == '1') && type != T_IQ2_XXS && type != T_F32) {
+    // default: the replaced library's numerics, bit for bit
+    if (type != T_Q8_0 && (rc = grow_bytes(&g_compat.db, &g_compat.db_cap, (size_t)(inner / 256) * 292)))
+      return rc;
+    if ((rc = launch_ref_gemv(type, dW, g_compat.dx, g_compat.db, inner, outer, g_compat.dy, g_compat.stream)))
+      return rc;
+    INF_CUDA_TRY(cudaMemcpyAsync(out, g_compat.dy, (size_t)outer * 4, cudaMemcpyDeviceToHost, g_compat.stream));
+    INF_CUDA_TRY(cudaStreamSynchronize(g_compat.stream));
+    return 0;
+  }
   GemvCall c;
   c.type = type;
   c.inner = inner;
@@ -143,15 +163,6 @@ static int compat_gemv(int type, const uint8_t* W, const float* x, float* out, i
   if ((rc = launch_gemv(c, g_compat.stream, false))) return rc;
   INF_CUDA_TRY(cudaMemcpyAsync(out, g_compat.dy, (size_t)outer * 4, cudaMemcpyDeviceToHost, g_compat.stream));
   INF_CUDA_TRY(cudaStreamSynchronize(g_compat.stream));
-  return 0;
-}
-
-static int grow_bytes(uint8_t** p, size_t* cap, size_t n) {
-  if (*cap >= n) return 0;
-  if (*p) cudaFree(*p);
-  *p = nullptr;
-  INF_CUDA_TRY(cudaMalloc(p, n));
-  *cap = n;
   return 0;
 }
 

@@ -72,6 +72,10 @@ int launch_dequant(int type, const void* src, long long n, float* dst, cudaStrea
 // Q8_K helpers of the compatibility tier (q8k.cu)
 int launch_quantize_q8k(const float* x, void* y, long long nblocks, cudaStream_t st);
 int launch_vec_dot_q8k(int type, const void* x, const void* y, int nb, float* out, cudaStream_t st);
+// q*_gemv with the reference C kernels' numerics (Q8_K activations for the
+// K-quants, AVX2 lane order); y8 holds inner / 256 block_q8_K of scratch
+int launch_ref_gemv(int type, const void* W, const float* x, void* y8, int inner, int rows, float* out,
+                    cudaStream_t st);
 struct GdnParams;
 struct AttnParams;
 // fused [in_proj | attn_gate] GEMV + GDN step (fused_gdn.cu); Wperm holds the

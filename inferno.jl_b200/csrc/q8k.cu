@@ -179,7 +179,119 @@ __global__ void __launch_bounds__(256) q8k_vec_dot_kernel(const uint8_t* __restr
   }
 }
 
+// q{4,5,6}_k_gemv of the reference (quant_kernels.c:602-650): out[row] =
+// vec_dot(row, quantize_row_q8_K(x)).  One warp per row; lane (b, k) = (lane
+// / 8, lane % 8) computes integer lane k of block c0 + b, and every thread
+// with lane % 8 == k replays the fma chain of lane k in block order through
+// shuffles, so each row's result equals the reference's vec_dot bit for bit.
+template <int TYPE>
+__global__ void __launch_bounds__(256) q8k_gemv_kernel(const uint8_t* __restrict__ W,
+                                                       const uint8_t* __restrict__ y8, int nb, int rows,
+                                                       float* __restrict__ out) {
+  constexpr int XB = TYPE == T_Q4_K ? 144 : TYPE == T_Q5_K ? 176 : 210;
+  constexpr bool MINS = TYPE == T_Q4_K || TYPE == T_Q5_K;
+  const int lane = threadIdx.x & 31, b = lane >> 3, k = lane & 7;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const uint8_t* wr = W + (size_t)row * nb * XB;
+  float acc = 0.0f, accm = 0.0f;
+  for (int c0 = 0; c0 < nb; c0 += 4) {
+    const int i = c0 + b;
+    int32_t v = 0, m = 0;
+    float d = 0.0f, dmin = 0.0f;
+    if (i < nb) {
+      const uint8_t *xb = wr + (size_t)i * XB, *yb = y8 + (size_t)i * Q8K_BYTES;
+      v = lane_sum<TYPE>(xb, yb, k, &m);
+      d = __fmul_rn(q_ldf(yb), h2f_bits(q_ld16(xb + (TYPE == T_Q6_K ? 208 : 0))));
+      if (MINS) dmin = -__fmul_rn(q_ldf(yb), h2f_bits(q_ld16(xb + 2)));
+    }
+    const int n = min(4, nb - c0);
+    for (int bb = 0; bb < 4; ++bb) {
+      const int vb = __shfl_sync(0xffffffffu, v, bb * 8 + k);
+      const float db = __shfl_sync(0xffffffffu, d, bb * 8);
+      int mb = 0;
+      float dmb = 0.0f;
+      if (MINS) {
+        dmb = __shfl_sync(0xffffffffu, dmin, bb * 8);
+        if (TYPE == T_Q4_K) {
+          mb = __shfl_sync(0xffffffffu, m, bb * 8 + (k & 3));
+        } else {
+          const int m0 = __shfl_sync(0xffffffffu, m, bb * 8), m1 = __shfl_sync(0xffffffffu, m, bb * 8 + 1);
+          const int m2 = __shfl_sync(0xffffffffu, m, bb * 8 + 2), m3 = __shfl_sync(0xffffffffu, m, bb * 8 + 3);
+          mb = (m0 + m1) + (m2 + m3);
+        }
+      }
+      if (bb < n) {
+        acc = fmaf(db, (float)vb, acc);
+        if (MINS) accm = fmaf(dmb, (float)mb, accm);
+      }
+    }
+  }
+  float a[8], am[4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) a[j] = __shfl_sync(0xffffffffu, acc, j);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) am[j] = __shfl_sync(0xffffffffu, accm, j);
+  if (lane == 0) {
+    const float s0 = a[4] + a[0], s1 = a[5] + a[1], s2 = a[6] + a[2], s3 = a[7] + a[3];
+    float r = (s0 + s2) + (s1 + s3);
+    if (TYPE == T_Q4_K) r = r + ((am[0] + am[2]) + (am[1] + am[3]));
+    if (TYPE == T_Q5_K) r = r + am[0];
+    out[row] = r;
+  }
+}
+
+// q8_0_gemv of the reference (quant_kernels.c:658-680), fp32 activations:
+// lane k of the accumulator takes, per block and per 8-value chunk c in
+// order, fma(d, q[8c + k] * x[8c + k], acc).  One warp per row; thread
+// (c, k) forms the product of chunk c, the chain replays through shuffles.
+__global__ void __launch_bounds__(256) q80_ref_gemv_kernel(const uint8_t* __restrict__ W,
+                                                           const float* __restrict__ x, int nb, int rows,
+                                                           float* __restrict__ out) {
+  const int lane = threadIdx.x & 31, c = lane >> 3, k = lane & 7;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const uint8_t* wr = W + (size_t)row * nb * 34;
+  float acc = 0.0f;
+  for (int i = 0; i < nb; ++i) {
+    const uint8_t* blk = wr + (size_t)i * 34;
+    const float d = h2f_bits(q_ld16(blk));
+    const float p = __fmul_rn((float)(int8_t)blk[2 + 8 * c + k], x[(size_t)i * 32 + 8 * c + k]);
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) acc = fmaf(d, __shfl_sync(0xffffffffu, p, cc * 8 + k), acc);
+  }
+  float a[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) a[j] = __shfl_sync(0xffffffffu, acc, j);
+  if (lane == 0) {
+    const float s0 = a[4] + a[0], s1 = a[5] + a[1], s2 = a[6] + a[2], s3 = a[7] + a[3];
+    out[row] = (s0 + s2) + (s1 + s3);
+  }
+}
+
 }  // namespace
+
+int launch_ref_gemv(int type, const void* W, const float* x, void* y8, int inner, int rows, float* out,
+                    cudaStream_t st) {
+  if (rows <= 0) return 0;
+  const unsigned grid = (unsigned)((rows + 7) / 8);
+  const uint8_t* w = (const uint8_t*)W;
+  if (type == T_Q8_0) {
+    q80_ref_gemv_kernel<<<grid, 256, 0, st>>>(w, x, inner / 32, rows, out);
+  } else {
+    int rc = launch_quantize_q8k(x, y8, inner / 256, st);
+    if (rc) return rc;
+    const uint8_t* y = (const uint8_t*)y8;
+    switch (type) {
+      case T_Q4_K: q8k_gemv_kernel<T_Q4_K><<<grid, 256, 0, st>>>(w, y, inner / 256, rows, out); break;
+      case T_Q5_K: q8k_gemv_kernel<T_Q5_K><<<grid, 256, 0, st>>>(w, y, inner / 256, rows, out); break;
+      case T_Q6_K: q8k_gemv_kernel<T_Q6_K><<<grid, 256, 0, st>>>(w, y, inner / 256, rows, out); break;
+      default: return set_error(-1, "reference-numerics gemv: unsupported type %d", type);
+    }
+  }
+  INF_CUDA_TRY(cudaGetLastError());
+  return 0;
+}
 
 int launch_quantize_q8k(const float* x, void* y, long long nblocks, cudaStream_t st) {
   if (nblocks <= 0) return 0;

@@ -716,11 +716,45 @@ void quantize_q8k(const float* x, uint8_t* y, int64_t k) {
   }
 }
 
+// q*_k_gemv / q8_0_gemv (quant_kernels.c:602-697): the reference library's
+// GEMV numerics -- x quantized once to Q8_K, one vec_dot per row; Q8_0 keeps
+// fp32 x and lane k takes fma(d, q[8c+k] * x[8c+k], acc) per block and chunk c.
+void ref_gemv(int type, const uint8_t* W, const float* x, float* out, int inner, int outer) {
+  if (type == 8) {
+    const int nb = inner / 32;
+    for (int r = 0; r < outer; ++r) {
+      float acc[8] = {0};
+      for (int b = 0; b < nb; ++b) {
+        const uint8_t* blk = W + ((size_t)r * nb + b) * 34;
+        const float d = h2f(rd16(blk));
+        for (int c = 0; c < 4; ++c)
+          for (int k = 0; k < 8; ++k) {
+            const float p = (float)(int8_t)blk[2 + 8 * c + k] * x[b * 32 + 8 * c + k];
+            acc[k] = fmaf(d, p, acc[k]);
+          }
+      }
+      out[r] = hsum8(acc);
+    }
+    return;
+  }
+  const int nb = inner / QK, bb = type == 12 ? 144 : type == 13 ? 176 : 210;
+  std::vector<uint8_t> y8((size_t)nb * Q8K_BYTES);
+  quantize_q8k(x, y8.data(), inner);
+  for (int r = 0; r < outer; ++r) {
+    const uint8_t* w = W + (size_t)r * nb * bb;
+    out[r] = type == 12 ? vec_dot_k45<false>(w, y8.data(), nb)
+             : type == 13 ? vec_dot_k45<true>(w, y8.data(), nb) : vec_dot_q6(w, y8.data(), nb);
+  }
+}
+
 }  // namespace q8k
 
 extern "C" {
 
 void orc_quantize_row_q8_K(const float* x, uint8_t* y, int64_t k) { q8k::quantize_q8k(x, y, k); }
+void orc_ref_gemv(int type, const uint8_t* W, const float* x, float* out, int inner, int outer) {
+  q8k::ref_gemv(type, W, x, out, inner, outer);
+}
 float orc_vec_dot_q8k(int type, const uint8_t* x, const uint8_t* y, int nb) {
   switch (type) {
     case 12: return q8k::vec_dot_k45<false>(x, y, nb);

@@ -39,6 +39,7 @@ def lib():
         L.orc_quantize_row_q8_K.argtypes = [p, p, i64]
         L.orc_vec_dot_q8k.argtypes = [i, p, p, i]
         L.orc_vec_dot_q8k.restype = C.c_float
+        L.orc_ref_gemv.argtypes = [i, p, p, p, i, i]
         L.orc_gdn_recurrence.argtypes = [i, i, i, i, p, p, p, p, p, p, p]
         L.orc_model_create.restype = p
         L.orc_model_create.argtypes = [p, p]
@@ -95,6 +96,16 @@ def vec_dot_q8k(ggml_type: int, xblocks, yblocks, nb: int) -> float:
     xb = np.ascontiguousarray(xblocks, dtype=np.uint8)
     yb = np.ascontiguousarray(yblocks, dtype=np.uint8)
     return float(lib().orc_vec_dot_q8k(ggml_type, _ptr(xb), _ptr(yb), nb))
+
+
+def ref_numerics_gemv(ggml_type: int, W, x, inner: int, outer: int) -> np.ndarray:
+    """q*_k_gemv / q8_0_gemv of the reference library (quant_kernels.c:602-697)
+    restated: Q8_K activations for the K-quants, the AVX2 lane order."""
+    W = np.ascontiguousarray(W, dtype=np.uint8)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(outer, np.float32)
+    lib().orc_ref_gemv(ggml_type, _ptr(W), _ptr(x), _ptr(y), inner, outer)
+    return y
 
 
 def flash_attention(q, ck, cv, kvh, seq_len, scale, hd, nkv, standard=False):

@@ -148,22 +148,34 @@ def test_gemv_swiglu():
     assert _rel(dh.cpu().numpy(), ref) < 1e-4
 
 
-@pytest.mark.parametrize("t", [S.Q4_K, S.Q6_K, S.Q8_0])
-def test_compat_tier_host_pointers(t):
-    """q*_gemv with host pointers (the QuantizedKernels.jl ccall signature)."""
+@pytest.mark.parametrize("t", [S.Q4_K, S.Q5_K, S.Q6_K, S.Q8_0])
+@pytest.mark.parametrize("numerics", ["reference", "fp32"])
+def test_compat_tier_host_pointers(t, numerics, monkeypatch):
+    """q*_gemv with host pointers (the QuantizedKernels.jl ccall signature).
+    Default: the replaced library's numerics (Q8_K activations, AVX2 lane
+    order), bit-identical to its restatement; INFERNO_COMPAT_FP32=1: fp32
+    activations through the engine's GEMV."""
     rows, inner = 1024, 2048
     q = _matrix(t, rows, inner, 13)
     x = np.random.default_rng(14).standard_normal(inner).astype(np.float32)
     y = np.zeros(rows, np.float32)
-    ref = O.gemv(t, q, x[None], inner, rows)[0]
+    if numerics == "fp32":
+        monkeypatch.setenv("INFERNO_COMPAT_FP32", "1")
+        ref = O.gemv(t, q, x[None], inner, rows)[0]
+    else:
+        monkeypatch.delenv("INFERNO_COMPAT_FP32", raising=False)
+        ref = O.ref_numerics_gemv(t, q, x, inner, rows)
     P = C.c_void_p
     for _ in range(2):   # second call hits the weight cache
         if t == S.Q8_0:
             lib().q8_0_gemv(P(q.ctypes.data), P(x.ctypes.data), P(y.ctypes.data), inner, rows)
         else:
-            fn = {S.Q4_K: lib().q4_k_gemv, S.Q6_K: lib().q6_k_gemv}[t]
+            fn = {S.Q4_K: lib().q4_k_gemv, S.Q5_K: lib().q5_k_gemv, S.Q6_K: lib().q6_k_gemv}[t]
             fn(P(q.ctypes.data), P(x.ctypes.data), P(y.ctypes.data), None, inner, rows)
-        assert _rel(y, ref) < GEMV_RTOL
+        if numerics == "fp32":
+            assert _rel(y, ref) < GEMV_RTOL
+        else:
+            assert np.array_equal(y.view(np.uint32), ref.view(np.uint32))
 
 
 # ---- Q8_K helpers of the compatibility tier vs the oracle (bit-exact) -------

@@ -254,3 +254,16 @@ def test_vec_dot_matches_reference_bitwise(ref, ggml_type):
         a = np.float32(O.vec_dot_q8k(ggml_type, x, y, nb))
         b = np.float32(fn(O._ptr(x), O._ptr(y), nb))
         assert a.view(np.uint32) == b.view(np.uint32), (nb, a, b)
+
+
+@pytest.mark.parametrize("ggml_type", [12, 13, 14, 8])
+def test_ref_numerics_gemv_matches_reference_bitwise(ref, ggml_type):
+    """The compatibility tier's default numerics, restated, equal the reference
+    library's q*_gemv output bit for bit (quant_kernels.c:602-697)."""
+    rng = np.random.default_rng(40 + ggml_type)
+    for rows, inner in ((64, 256), (100, 2048), (300, 1024)):
+        W = S.random_quant_matrix(rng, rows, inner, ggml_type)
+        x = (rng.standard_normal(inner) * 2).astype(np.float32)
+        a = O.ref_numerics_gemv(ggml_type, W, x, inner, rows)
+        b = O.ref_gemv(ggml_type, W, x, inner, rows, ref)
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))

@@ -6,7 +6,8 @@ sandbox without allocation rights.  For them the library stages the weight
 and vectors in a static device array instead of cudaMalloc'd buffers.  This
 test calls that entry through the C ABI twice in a row (the array keeps the
 previous call's contents) and checks each result against the allocating
-compatibility entry (q4_k_gemv / q6_k_gemv) on the same host inputs.  It sits
+compatibility entry (q4_k_gemv / q6_k_gemv, with INFERNO_COMPAT_FP32=1 so both
+use fp32 activations) on the same host inputs.  It sits
 in a file of its own, collected last.
 """
 import ctypes as C
@@ -44,7 +45,8 @@ def _noalloc(t, q, x, rows, inner):
     return y
 
 
-def test_noalloc_gemv_matches_allocating_entry_twice():
+def test_noalloc_gemv_matches_allocating_entry_twice(monkeypatch):
+    monkeypatch.setenv("INFERNO_COMPAT_FP32", "1")
     cases = [(S.Q4_K, 3584, 1024, 1), (S.Q6_K, 1024, 3584, 2)]   # two different calls in a row
     for t, rows, inner, seed in cases:
         q, x = _case(t, rows, inner, seed)
