@@ -5,6 +5,7 @@
 #include "internal.h"
 #include "gemv.cuh"
 #include "gemv_mma.cuh"
+#include "gemv_mma_batch.cuh"
 
 namespace inf {
 
@@ -199,6 +200,118 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
   return 0;
 }
 
+template <int TYPE>
+cudaError_t launch_mma_batch(const GemvParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_done[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_mma_batch_kernel<TYPE, MMA_NBT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    cudaFuncSetAttribute(gemv_mma_batch_kernel<TYPE, MMA_NBT>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared);
+    attr_done[dev & 63] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3((MMA_NBT + 1) * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemv_mma_batch_kernel<TYPE, MMA_NBT>, p);
+}
+
+// Batched (several columns) Q4_K / Q6_K calls on the tensor-core path
+// (gemv_mma_batch.cuh), MMA_NBT columns per launch.  Returns 1 when the call
+// does not fit it (the caller falls back to the CUDA-core kernel).
+int plan_launch_mma_batch(const GemvCall& c, int dev, int sms, cudaStream_t st, bool pdl) {
+  constexpr int NW = MMA_NBT;
+  const int bb = bb_of(c.type);
+  const bool paired = c.epi == EPI_SWIGLU;
+  const int nsb = c.inner / 256;
+  const long long row_bytes = (long long)nsb * bb;
+  const size_t smem_cap = 220 * 1024;
+  if (c.epi == EPI_ARGMAX || c.x_stride % 4 || (c.pro_z && c.x_stride % 4)) return 1;
+  if (c.pro == PRO_HEADNORM_GATE && c.inner / c.pro_group > MMA_MAX_HEADS) return 1;
+  for (int i = 0; i < c.nmats; ++i)
+    if (c.mats[i].indirect) return 1;
+  const size_t xq_col = (size_t)nsb * 8 * MMA_KSC_BYTES;
+  const size_t fixed = mma_batch_fixed_bytes<NW>() + (size_t)MMA_NBT * nsb * 16 * 4 + MMA_NBT * xq_col + 128;
+  auto stage_of = [&](int TR) -> size_t {
+    if (paired) return 2 * (((size_t)(TR / 2) * row_bytes + 32 + 15) / 16 * 16) + 128;
+    return ((size_t)TR * row_bytes + 48 + 127) / 128 * 128;
+  };
+  int best_tr = 0;
+  double best = 1e300;
+  for (int TR : {16, 32, 64, 128}) {
+    const int nrg = TR / 16;
+    if (nrg > NW) continue;
+    const int nkg = NW / nrg;
+    if (fixed > smem_cap || (smem_cap - fixed) / stage_of(TR) < 2) continue;
+    const int eff = paired ? TR / 2 : TR;
+    long long tiles = 0;
+    for (int i = 0; i < (paired ? 1 : c.nmats); ++i) tiles += (c.mats[i].rows + eff - 1) / eff;
+    const long long waves = (tiles + sms - 1) / sms;
+    const double cost = (double)waves * ((nsb + nkg - 1) / nkg) + (double)waves * TR * row_bytes / 65536.0;
+    if (cost < best) { best = cost; best_tr = TR; }
+  }
+  if (!best_tr) return 1;
+  const int TR = best_tr, eff = paired ? TR / 2 : TR;
+  GemvParams p = {};
+  int ntiles = 0;
+  for (int i = 0; i < c.nmats; ++i) {
+    p.seg[i].W = (const uint8_t*)c.mats[i].W;
+    p.seg[i].rows = c.mats[i].rows;
+    if (paired && i == 1) p.seg[i].tile0 = INT_MAX;
+    else {
+      p.seg[i].tile0 = ntiles;
+      ntiles += (c.mats[i].rows + eff - 1) / eff;
+    }
+  }
+  p.nseg = c.nmats;
+  p.ntiles = ntiles;
+  p.inner = c.inner;
+  p.row_bytes = (int)row_bytes;
+  p.nxv = 1;
+  p.xch_wk = p.xch_rk = -1;
+  p.nkc = (c.inner + GEMV_CHUNK - 1) / GEMV_CHUNK;
+  p.TR = TR;
+  p.nkg = NW / (TR / 16);
+  p.x_stride = c.x_stride;
+  p.y_stride = c.y_stride;
+  p.pro = c.pro;
+  p.pro_w = c.pro_w;
+  p.eps = c.eps;
+  p.pro_group = c.pro_group;
+  p.epi = c.epi;
+  p.err = c.err ? c.err : device_error_word(dev);
+  static const bool no_hint = getenv("INFERNO_GEMV_NO_L2HINT") != nullptr;
+  p.l2_evict_first = no_hint ? 0 : 1;
+  if (ntiles == 0) return 0;
+  const size_t stage_bytes = stage_of(TR);
+  p.stages = (int)std::min<size_t>(GEMV_MAX_STAGES, (smem_cap - fixed) / stage_bytes);
+  p.contig = 1;
+  p.stage_bytes = (int)stage_bytes;
+  p.part1_off = (int)((((size_t)(TR / 2) * row_bytes + 32 + 15) / 16) * 16);
+  const size_t smem = fixed + (size_t)p.stages * stage_bytes;
+  const int grid = std::min(ntiles, sms);
+  for (int done = 0; done < c.nb; done += MMA_NBT) {
+    p.nb = std::min(MMA_NBT, c.nb - done);
+    p.x = c.x + (long long)done * c.x_stride;
+    p.pro_z = c.pro_z ? c.pro_z + (long long)done * c.x_stride : nullptr;
+    for (int i = 0; i < c.nmats; ++i) p.seg[i].y = c.mats[i].y ? c.mats[i].y + (long long)done * c.y_stride : nullptr;
+    cudaError_t e = c.type == T_Q4_K ? launch_mma_batch<T_Q4_K>(p, grid, smem, st, pdl)
+                                     : launch_mma_batch<T_Q6_K>(p, grid, smem, st, pdl);
+    if (e != cudaSuccess) return set_error(-2, "batched gemv launch failed: %s", cudaGetErrorString(e));
+  }
+  return 0;
+}
+
 }  // namespace
 
 // Regroup a Q6_K matrix (rows % 16 == 0) into the T_Q6_KR layout: one CTA of
@@ -281,6 +394,12 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
   const bool mma_ok = !c.force_r && c.nb == 1 && (c.type == T_Q4_K || c.type == T_Q6_K) && c.inner % 256 == 0;
   if (mma_ok && (!no_mma || c.nxv > 1 || c.xch_wk >= 0 || c.xch_rk >= 0)) {
     const int rc = plan_launch_mma(c, dev, sms, st, pdl);
+    if (rc <= 0) return rc;
+  }
+  static const bool no_mma_batch = getenv("INFERNO_GEMV_NO_MMA_BATCH") != nullptr;
+  if (!no_mma && !no_mma_batch && !c.force_r && c.nb > 1 && c.nxv == 1 && (c.type == T_Q4_K || c.type == T_Q6_K) &&
+      c.inner % 256 == 0) {
+    const int rc = plan_launch_mma_batch(c, dev, sms, st, pdl);
     if (rc <= 0) return rc;
   }
   if (c.nxv > 1) return set_error(-1, "gemv: several input vectors need single-column Q4_K/Q6_K");

@@ -178,6 +178,70 @@ def test_compat_tier_host_pointers(t, numerics, monkeypatch):
             assert np.array_equal(y.view(np.uint32), ref.view(np.uint32))
 
 
+# ---- batched tensor-core path (prefill chunks): several columns per launch ----
+def _rms_ref(x, w, eps=np.float32(1e-6)):
+    ss = (x.astype(np.float32) ** 2).sum(axis=-1, keepdims=True).astype(np.float32)
+    return (x * (np.float32(1) / np.sqrt(ss / np.float32(x.shape[-1]) + eps)) * w).astype(np.float32)
+
+
+@pytest.mark.parametrize("t", [S.Q4_K, S.Q6_K], ids=["Q4_K", "Q6_K"])
+@pytest.mark.parametrize("batch", [2, 8, 11])
+@pytest.mark.parametrize("shape", [(1024, 1024), (6144, 1024), (1024, 3584), (100, 2048)],
+                         ids=["1024x1024", "6144x1024", "1024x3584", "100x2048"])
+def test_gemv_batch_rmsnorm_residual(t, batch, shape):
+    """RMSNorm prologue + residual epilogue over `batch` columns (the prefill
+    GEMVs): every column against the fp32 oracle of its own normalised input."""
+    rows, inner = shape
+    q = _matrix(t, rows, inner, 31)
+    rng = np.random.default_rng(32)
+    x = (rng.standard_normal((batch, inner)) * rng.uniform(0.1, 10, (batch, 1))).astype(np.float32)
+    w = (1 + 0.02 * rng.standard_normal(inner)).astype(np.float32)
+    ref = O.gemv(t, q, _rms_ref(x, w), inner, rows)
+    y0 = rng.standard_normal((batch, rows)).astype(np.float32)
+    dW, dx, dw, dy = _dev(q), _dev(x), _dev(w), _dev(y0)
+    call("inferno_gemv_ex", t, C.c_void_p(dW.data_ptr()), C.c_void_p(dx.data_ptr()), C.c_void_p(dy.data_ptr()),
+         inner, rows, batch, 1, C.c_void_p(dw.data_ptr()), C.c_float(1e-6), 1, None, 0, _stream())
+    _sync()
+    got = dy.cpu().numpy() - y0
+    for v in range(batch):
+        assert _rel(got[v], ref[v]) < 1e-4, (v, _rel(got[v], ref[v]))
+
+
+@pytest.mark.parametrize("batch", [3, 8])
+def test_gemv_batch_swiglu(batch):
+    rows, inner, t = 3584, 1024, S.Q4_K
+    g, u = _matrix(t, rows, inner, 33), _matrix(t, rows, inner, 34)
+    x = np.random.default_rng(35).standard_normal((batch, inner)).astype(np.float32)
+    rg, ru = O.gemv(t, g, x, inner, rows), O.gemv(t, u, x, inner, rows)
+    ref = rg / (1 + np.exp(-rg)) * ru
+    dg, du, dx = _dev(g), _dev(u), _dev(x)
+    dh = _dev(np.zeros((batch, rows), np.float32))
+    call("inferno_gemv_swiglu", t, C.c_void_p(dg.data_ptr()), C.c_void_p(du.data_ptr()), C.c_void_p(dx.data_ptr()),
+         C.c_void_p(dh.data_ptr()), inner, rows, batch, None, C.c_float(0), _stream())
+    _sync()
+    got = dh.cpu().numpy()
+    for v in range(batch):
+        assert _rel(got[v], ref[v]) < 1e-4
+
+
+def test_gemv_batch_nonfinite_column_is_isolated():
+    """A NaN in one column makes that column's outputs NaN and leaves the others exact."""
+    rows, inner, t, batch = 512, 1024, S.Q4_K, 8
+    q = _matrix(t, rows, inner, 36)
+    x = np.random.default_rng(37).standard_normal((batch, inner)).astype(np.float32)
+    x[3, 17] = np.nan
+    dW, dx = _dev(q), _dev(x)
+    dy = _dev(np.zeros((batch, rows), np.float32))
+    call("inferno_gemv", t, C.c_void_p(dW.data_ptr()), C.c_void_p(dx.data_ptr()), C.c_void_p(dy.data_ptr()),
+         inner, rows, batch, _stream())
+    _sync()
+    got = dy.cpu().numpy()
+    assert np.isnan(got[3]).all()
+    ok = [v for v in range(batch) if v != 3]
+    ref = O.gemv(t, q, x[ok], inner, rows)
+    assert _rel(got[ok], ref) < GEMV_RTOL
+
+
 # ---- Q8_K helpers of the compatibility tier vs the oracle (bit-exact) -------
 def test_compat_quantize_row_q8k_bitwise():
     rng = np.random.default_rng(21)
