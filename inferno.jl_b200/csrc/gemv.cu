@@ -237,12 +237,7 @@ int plan_launch_mma_batch(const GemvCall& c, int dev, int sms, cudaStream_t st, 
   const long long row_bytes = (long long)nsb * bb;
   const size_t smem_cap = 220 * 1024;
   if (c.epi == EPI_ARGMAX || c.x_stride % 4 || (c.pro_z && c.x_stride % 4)) return 1;
-  // head norm: a chunk row of 128 elements lies in one head, and a head's
-  // rows fit one prologue chunk
-  if (c.pro == PRO_HEADNORM_GATE &&
-      (c.inner / c.pro_group > MMA_MAX_HEADS || c.pro_group % 128 || c.pro_group > 128 * MMA_PCH ||
-       MMA_PCH % (c.pro_group / 128)))
-    return 1;
+  if (c.pro == PRO_HEADNORM_GATE && c.inner / c.pro_group > MMA_MAX_HEADS) return 1;
   for (int i = 0; i < c.nmats; ++i)
     if (c.mats[i].indirect) return 1;
   const size_t xq_col = (size_t)nsb * 8 * MMA_KSC_BYTES;

@@ -27,14 +27,21 @@ __device__ __forceinline__ uint2 mma_bfrag(const uint8_t* xq_ks, int lane) {
   return ((lane >> 2) & 1) ? make_uint2(0u, w) : make_uint2(w, 0u);
 }
 
-// Prologue fusion of element quad u (elements 4u..4u+3) of one column:
-// RMSNorm weight, head norm + SiLU gate (scale = the quad's head scale), or
-// none.  a = raw input, z = gate input (head norm only).
-__device__ __forceinline__ float4 mma_batch_fuse(const GemvParams& p, float4 a, float4 z, float4 w4, float scale) {
+// Input value of element quad u (elements 4u..4u+3) of column v after the
+// prologue fusion (RMSNorm weight, head norm + SiLU gate, or none).  `hsc`
+// holds the column's per-head scales (head-norm only).
+__device__ __forceinline__ float4 mma_batch_u(const GemvParams& p, int v, int u, const float* hsc) {
+  const float* x = p.x + (long long)v * p.x_stride;
+  float4 a = ((const float4*)x)[u];
   if (p.pro == PRO_RMSNORM) {
+    const float4 w4 = ((const float4*)p.pro_w)[u];
     a.x *= w4.x; a.y *= w4.y; a.z *= w4.z; a.w *= w4.w;
   } else if (p.pro == PRO_HEADNORM_GATE) {
-    const float vv[4] = {a.x, a.y, a.z, a.w}, zz[4] = {z.x, z.y, z.z, z.w}, ww[4] = {w4.x, w4.y, w4.z, w4.w};
+    const int G = p.pro_group, e0 = 4 * u, hh = e0 / G, i0 = e0 - hh * G;
+    const float scale = hsc[hh];
+    const float4 z4 = ((const float4*)(p.pro_z + (long long)v * p.x_stride))[u];
+    const float4 w4 = *(const float4*)(p.pro_w + i0);
+    const float vv[4] = {a.x, a.y, a.z, a.w}, zz[4] = {z4.x, z4.y, z4.z, z4.w}, ww[4] = {w4.x, w4.y, w4.z, w4.w};
     float o[4];
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
@@ -46,127 +53,82 @@ __device__ __forceinline__ float4 mma_batch_fuse(const GemvParams& p, float4 a, 
   return a;
 }
 
-// The chunk's loads: input, gate input (head norm) and norm weights of quads
-// base + 32 j + lane, all issued before any is used.
-__device__ __forceinline__ void mma_batch_load(const GemvParams& p, const float4* xv, const float4* zv, int base,
-                                               int lane, int nf4, float4 (&a)[8], float4 (&z)[8], float4 (&w)[8]) {
-  const bool hn = p.pro == PRO_HEADNORM_GATE, rms = p.pro == PRO_RMSNORM;
-  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int u = base + 32 * j + lane;
-    const bool ok = u < nf4;
-    a[j] = ok ? xv[u] : zero;
-    z[j] = (hn && ok) ? zv[u] : zero;
-    w[j] = (rms && ok) ? ((const float4*)p.pro_w)[u]
-                       : (hn && ok) ? *(const float4*)(p.pro_w + (4 * u) % p.pro_group) : zero;
-  }
-}
-
-// Warp `v` prepares column v in chunks of MMA_PCH quads per lane (all loads
-// of a chunk in flight together): pass 1 gathers the statistics (sum of
-// squares, per-head norms, max|u|), pass 2 re-reads the chunk and writes the
-// limbs and sub-block sums.  cs[v] gets the column factor (1/rms or 1),
-// vmax[v] max|u|, bad[v] a non-finite flag.  Head norm needs pro_group a
-// multiple of 128 (one chunk row of 32 quads lies in one head).
-constexpr int MMA_PCH = 8;   // = the arrays of mma_batch_load
+// Warp `v` prepares column v: statistics pass (sum of squares / head norms,
+// max|u|), then the limbs and sub-block sums.  cs[v] gets the column factor
+// (1/rms or 1), vmax[v] max|u|; bad[v] flags a non-finite input.
 template <int TYPE>
 __device__ void gemv_mma_batch_prologue(const GemvParams& p, uint8_t* xq, float* xsum, float* cs, float* vmax,
                                         float* hsc_all, int* bad_all, int v, int lane) {
   const int n = p.inner, nf4 = n >> 2;
   const int nsb = n >> 8;
-  const float4* xv = (const float4*)(p.x + (long long)v * p.x_stride);
-  const bool hn = p.pro == PRO_HEADNORM_GATE;
-  const float4* zv = hn ? (const float4*)(p.pro_z + (long long)v * p.x_stride) : nullptr;
-  const int rph = hn ? p.pro_group >> 7 : 1;         // chunk rows (32 quads) per head
   float* hsc = hsc_all + v * MMA_MAX_HEADS;
   bool bad = false;
   float ss = 0.f, amax = 0.f;
-  // nf4 is a multiple of 64 (n % 256 == 0): whole rows of 32 quads
-  for (int base = 0; base < nf4; base += 32 * MMA_PCH) {
-    float4 a[MMA_PCH], z[MMA_PCH], w[MMA_PCH];
-    mma_batch_load(p, xv, zv, base, lane, nf4, a, z, w);
-    float rs[MMA_PCH];
-#pragma unroll
-    for (int j = 0; j < MMA_PCH; ++j)
-      rs[j] = fmaf(a[j].x, a[j].x, fmaf(a[j].y, a[j].y, fmaf(a[j].z, a[j].z, a[j].w * a[j].w)));
-    if (hn) {
-#pragma unroll
-      for (int j = 0; j < MMA_PCH; ++j) rs[j] = warp_sum(rs[j]);
-    }
-#pragma unroll
-    for (int j = 0; j < MMA_PCH; ++j) {
-      if (base + 32 * j >= nf4) break;
-      float scale = 1.f;
-      if (hn) {
-        // head of this row: rows j0 .. j0 + rph - 1 of the chunk (rph | MMA_PCH or one head spans chunks)
-        const int row = (base >> 5) + j, head = row / rph;
-        float hs = 0.f;
-        if (rph <= MMA_PCH) {
-          const int j0 = j - (row - head * rph);
-#pragma unroll
-          for (int r = 0; r < MMA_PCH; ++r)
-            if (r >= j0 && r < j0 + rph) hs += rs[r];
-          scale = 1.0f / sqrtf(hs / (float)p.pro_group + p.eps);
-          if (lane == 0 && row == head * rph) hsc[head] = scale;
-        }
-      } else {
-        ss += rs[j];
+  if (p.pro == PRO_HEADNORM_GATE) {
+    const int G = p.pro_group, per = G >> 2;     // float4 items per head
+    const float* x = p.x + (long long)v * p.x_stride;
+    for (int hh = 0; hh < n / G; ++hh) {
+      float hs = 0.f;
+      for (int i = lane; i < per; i += 32) {
+        const float4 a = ((const float4*)(x + hh * G))[i];
+        hs = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, hs))));
       }
-      const float4 f = mma_batch_fuse(p, a[j], z[j], w[j], scale);
-      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+      hs = warp_sum(hs);
+      if (lane == 0) hsc[hh] = 1.0f / sqrtf(hs / (float)G + p.eps);
     }
+    __syncwarp();
   }
-  __syncwarp();
+  for (int u = lane; u < nf4; u += 32) {
+    const float4 a = mma_batch_u(p, v, u, hsc);
+    if (p.pro == PRO_RMSNORM) {
+      const float4 r = ((const float4*)(p.x + (long long)v * p.x_stride))[u];
+      ss = fmaf(r.x, r.x, fmaf(r.y, r.y, fmaf(r.z, r.z, fmaf(r.w, r.w, ss))));
+    }
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+  }
   ss = warp_sum(ss);
   amax = warp_max(amax);
   if (!(amax <= 3.0e38f)) bad = true;
   const float up = ldexpf(1.0f, mma_exp2_scale(amax));
   uint8_t* xqv = xq + (size_t)v * nsb * 8 * MMA_KSC_BYTES;
   float* xs = xsum + (size_t)v * nsb * 16;
-  for (int base = 0; base < nf4; base += 32 * MMA_PCH) {
-    float4 a[MMA_PCH], z[MMA_PCH], w[MMA_PCH];
-    mma_batch_load(p, xv, zv, base, lane, nf4, a, z, w);
-#pragma unroll
-    for (int j = 0; j < MMA_PCH; ++j) {
-      const int u = base + 32 * j + lane;
-      if (base + 32 * j >= nf4) break;
-      const float4 f = mma_batch_fuse(p, a[j], z[j], w[j], hn ? hsc[((base >> 5) + j) / rph] : 1.f);
-      const int e0 = 4 * u, sb = e0 >> 8, r = e0 & 255;
-      int ks, cc, hp;
-      if (TYPE == T_Q4_K) {
-        ks = sb * 8 + 2 * (r >> 6) + ((r >> 2) & 1);
-        cc = (r >> 3) & 3;
-        hp = (r >> 5) & 1;
-      } else {
-        ks = sb * 8 + 4 * (r >> 7) + ((r >> 5) & 3);
-        cc = (r >> 2) & 3;
-        hp = (r >> 4) & 1;
-      }
-      const float vv[4] = {f.x, f.y, f.z, f.w};
-      uint32_t limb[4] = {0u, 0u, 0u, 0u};
-      float sum = 0.f;
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        if (vv[t] != vv[t]) bad = true;
-        int xi = __float2int_rn(vv[t] * up);
-        sum += (float)xi;
-#pragma unroll
-        for (int l = 0; l < 3; ++l) {
-          const int d = (int)(int8_t)(xi & 0xff);
-          limb[l] |= (uint32_t)(d & 0xff) << (8 * t);
-          xi = (xi - d) >> 8;
-        }
-        limb[3] |= (uint32_t)(xi & 0xff) << (8 * t);
-      }
-#pragma unroll
-      for (int l = 0; l < 4; ++l)
-        *(uint32_t*)(xqv + (size_t)ks * MMA_KSC_BYTES + ((2 * l + hp) * 4 + cc) * 4) = limb[l];
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      if (TYPE == T_Q4_K) sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-      if ((u & (TYPE == T_Q4_K ? 7 : 3)) == 0) xs[TYPE == T_Q4_K ? (e0 >> 5) : (e0 >> 4)] = sum;
+  // nf4 is a multiple of 64 (n % 256 == 0): every lane runs every iteration
+  for (int u = lane; u < nf4; u += 32) {
+    const float4 a = mma_batch_u(p, v, u, hsc);
+    const int e0 = 4 * u, sb = e0 >> 8, r = e0 & 255;
+    int ks, cc, hp;
+    if (TYPE == T_Q4_K) {
+      ks = sb * 8 + 2 * (r >> 6) + ((r >> 2) & 1);
+      cc = (r >> 3) & 3;
+      hp = (r >> 5) & 1;
+    } else {
+      ks = sb * 8 + 4 * (r >> 7) + ((r >> 5) & 3);
+      cc = (r >> 2) & 3;
+      hp = (r >> 4) & 1;
     }
+    const float vv[4] = {a.x, a.y, a.z, a.w};
+    uint32_t limb[4] = {0u, 0u, 0u, 0u};
+    float sum = 0.f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      if (vv[t] != vv[t]) bad = true;
+      int xi = __float2int_rn(vv[t] * up);
+      sum += (float)xi;
+#pragma unroll
+      for (int l = 0; l < 3; ++l) {
+        const int d = (int)(int8_t)(xi & 0xff);
+        limb[l] |= (uint32_t)(d & 0xff) << (8 * t);
+        xi = (xi - d) >> 8;
+      }
+      limb[3] |= (uint32_t)(xi & 0xff) << (8 * t);
+    }
+#pragma unroll
+    for (int l = 0; l < 4; ++l)
+      *(uint32_t*)(xqv + (size_t)ks * MMA_KSC_BYTES + ((2 * l + hp) * 4 + cc) * 4) = limb[l];
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if (TYPE == T_Q4_K) sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    if ((u & (TYPE == T_Q4_K ? 7 : 3)) == 0) xs[TYPE == T_Q4_K ? (e0 >> 5) : (e0 >> 4)] = sum;
   }
   bad = __any_sync(0xffffffffu, bad);
   if (lane == 0) {
