@@ -135,7 +135,6 @@ __device__ bool pk_gemv_tiles(const PkStage& S, PkRing& rg, const float* xs, con
   const int G = gridDim.x;
   const int n_items = (p.ntiles - (int)blockIdx.x + G - 1) / G;
   const bool paired = p.epi == EPI_SWIGLU;
-  const int TR = p.TR, half_tr = TR / 2;
   float colscale = 1.0f;
   if (p.pro == PRO_RMSNORM) {
     float ss = 0.f;
@@ -277,7 +276,6 @@ __device__ void pk_gdn(const GdnParams& p, float* sm) {
   float* kn = sm + PK_DK;
   float* vrow = sm + 2 * PK_DK;
   float* red = vrow + PK_GDN_ROWS;      // [3][4]
-  float* gate_s = red + 12;
   const int t = __ldcg(p.step);
   const int cur = t % K;
   const int cq = g * PK_DK + tid, ck = p.nk * PK_DK + g * PK_DK + tid;

@@ -602,7 +602,6 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
   const int G = gridDim.x;
   const int n_items = (p.ntiles - (int)blockIdx.x + G - 1) / G;   // one item = one tile, all of K
   const bool paired = (p.epi == EPI_SWIGLU);
-  const int TR = p.TR, half_tr = TR / 2;
 
   if (warp == NW) {
     gemv_producer(p, full, empty, stage0, lane, n_items);

@@ -76,8 +76,7 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const float* __rest
   __shared__ unsigned redu[32];
   __shared__ float cs[SMP_MAXK];
   __shared__ int ci[SMP_MAXK];
-  __shared__ unsigned sh_prefix, sh_remaining, sh_count, sh_eqbase;
-  __shared__ float sh_sum;
+  __shared__ unsigned sh_prefix, sh_remaining, sh_count;
   __shared__ int sh_pick;
   const int tid = threadIdx.x;
   pdl_wait();
@@ -209,7 +208,6 @@ __global__ void __launch_bounds__(SMP_THREADS) sample_kernel(const float* __rest
         if (t2 > 0.f)
           for (int j = 0; j < keep; ++j) cs[j] /= t2;
       }
-      sh_sum = 0.f;
     }
     __syncthreads();
     // draw over the candidates in index order: sort by index ascending

@@ -251,7 +251,7 @@ class Model:
 
 
 def algorithmic_bytes_per_token(spec: S.ModelSpec, tensors: dict, pos: int) -> int:
-    """Bytes a decode token must move (SURVEY 8d accounting): every weight
+    """Bytes a decode token must move (the roofline accounting): every weight
     read once, KV read of pos+1 rows + write of 1 row per attention layer, GDN
     recurrent state and conv state read + write."""
     skip = {"token_embd.weight"} if "output.weight" in tensors else set()
