@@ -34,6 +34,8 @@ extern "C" {
 #define INFERNO_ESTATE (-4)  /* call not valid in the engine's state        */
 #define INFERNO_EDEVICE (-5) /* a kernel reported an error (timeout, ...)   */
 #define INFERNO_ENCCL (-6)   /* NCCL error                                  */
+#define INFERNO_ENOTFOUND (-7) /* metadata key not present                   */
+#define INFERNO_EFORMAT (-8) /* malformed GGUF file                         */
 
 /* ggml type ids accepted (GGUF spec; src/GGUF.jl:25-60) */
 #define INFERNO_F32 0
@@ -279,6 +281,43 @@ float inferno_last_decode_ms(InfernoEngine* eng);
 int inferno_tp_unique_id(void* out, int nbytes);
 
 int inferno_engine_destroy(InfernoEngine* eng);
+
+/* ============================ GGUF files =================================
+ * Replaces GGUF.read_gguf (src/GGUF.jl:119-165) and the keep_quantized tensor
+ * view of LoaderCPU.extract_tensor_cpu (src/LoaderCPU.jl:131-155).  The file
+ * is memory-mapped read-only and parsed in place (version 2 or 3, strings up
+ * to 1 MiB as in the reference, data aligned to general.alignment, default
+ * 32); every read is bounds-checked and a malformed file returns
+ * INFERNO_EFORMAT.  Returned names / strings / data pointers stay valid until
+ * inferno_gguf_close. */
+typedef struct InfernoGguf InfernoGguf;
+int inferno_gguf_open(const char* path, InfernoGguf** out);
+int inferno_gguf_close(InfernoGguf* g);
+int inferno_gguf_version(const InfernoGguf* g);
+int64_t inferno_gguf_n_tensors(const InfernoGguf* g);
+int64_t inferno_gguf_n_kv(const InfernoGguf* g);
+int64_t inferno_gguf_data_offset(const InfernoGguf* g);
+/* key i in file order (NULL when out of range) */
+const char* inferno_gguf_key(const InfernoGguf* g, int64_t i);
+/* tensor i in file order: name, ggml type, ne[4] (missing dims = 1), data
+ * bytes (0 when the type's block size is unknown) and a pointer to the bytes
+ * in the mapping; any output may be NULL */
+int inferno_gguf_tensor_info(const InfernoGguf* g, int64_t i, const char** name, int* ggml_type, int64_t ne[4],
+                             uint64_t* nbytes, const void** data);
+/* metadata by key: integer (any integer or bool type; uint64 bit for bit),
+ * number (float32/64 or an integer), string, array (element type, length,
+ * pointer to the first element; NULL for string arrays).  A missing key
+ * returns INFERNO_ENOTFOUND, a value of another kind INFERNO_EINVAL. */
+int inferno_gguf_get_int(const InfernoGguf* g, const char* key, int64_t* out);
+int inferno_gguf_get_float(const InfernoGguf* g, const char* key, double* out);
+int inferno_gguf_get_string(const InfernoGguf* g, const char* key, const char** out);
+int inferno_gguf_get_array(const InfernoGguf* g, const char* key, int* elem_type, int64_t* len, const void** data);
+/* Uploads every tensor of the file to the engine by its GGUF name, from the
+ * mapping through pinned double-buffered staging (the engine-tier
+ * equivalent of calling inferno_engine_upload_tensor per tensor).  Every
+ * tensor must have a type the engine takes (F32, Q8_0, Q4_K, Q5_K, Q6_K,
+ * IQ2_XXS); call before inferno_engine_finalize. */
+int inferno_engine_load_gguf(InfernoEngine* eng, const InfernoGguf* g);
 
 #ifdef __cplusplus
 }

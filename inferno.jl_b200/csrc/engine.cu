@@ -29,6 +29,7 @@
 #include "gemv.cuh"
 #include "params.h"
 #include "persist.h"
+#include "gguf_internal.h"
 #include "../../include/inferno_b200.h"
 
 namespace inf {
@@ -928,6 +929,74 @@ int inferno_engine_upload_tensor(InfernoEngine* e, const char* name, int ggml_ty
   auto it = e->tensors.find(name);
   if (it != e->tensors.end()) cudaFree(it->second.d);
   e->tensors[name] = t;
+  return 0;
+}
+
+// Every tensor of a parsed GGUF file to the device, straight from the file
+// mapping (the raw-bytes view of LoaderCPU.extract_tensor_cpu with
+// keep_quantized, src/LoaderCPU.jl:131-155): the bytes go through two pinned
+// staging buffers, so reading the mapping (page faults included) overlaps
+// the DMA of the previous chunk.
+int inferno_engine_load_gguf(InfernoEngine* e, const InfernoGguf* g) {
+  if (!e || !g) return set_error(INFERNO_EINVAL, "load_gguf: null argument");
+  if (e->finalized) return set_error(INFERNO_ESTATE, "load_gguf after finalize");
+  for (const GgufTensor& t : g->tensors) {
+    if (!type_supported(t.type) || !t.nbytes || t.ne[0] % qk_of(t.type))
+      return set_error(INFERNO_EINVAL, "load_gguf: tensor %s has type %d / dims the engine does not take",
+                       t.name.c_str(), t.type);
+  }
+  INF_CUDA_TRY(cudaSetDevice(e->dev));
+  constexpr size_t CHUNK = 32u << 20;
+  struct Staging {
+    void* buf[2] = {nullptr, nullptr};
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    bool used[2] = {false, false};
+    ~Staging() {
+      for (int k = 0; k < 2; ++k) {
+        if (ev[k]) { cudaEventSynchronize(ev[k]); cudaEventDestroy(ev[k]); }
+        if (buf[k]) cudaFreeHost(buf[k]);
+      }
+    }
+  } stg;
+  for (int k = 0; k < 2; ++k) {
+    if (cudaHostAlloc(&stg.buf[k], CHUNK, cudaHostAllocDefault) != cudaSuccess)
+      return set_error(INFERNO_ENOMEM, "load_gguf: pinned staging allocation failed");
+    INF_CUDA_TRY(cudaEventCreateWithFlags(&stg.ev[k], cudaEventDisableTiming));
+  }
+  int k = 0;
+  for (const GgufTensor& t : g->tensors) {
+    DevTensor dt;
+    dt.type = t.type;
+    for (int d = 0; d < 4; ++d) dt.ne[d] = t.ne[d];
+    dt.bytes = t.nbytes;
+    if (cudaMalloc(&dt.d, (t.nbytes + 255) / 256 * 256) != cudaSuccess)
+      return set_error(INFERNO_ENOMEM, "load_gguf %s: cudaMalloc(%llu) failed", t.name.c_str(),
+                       (unsigned long long)t.nbytes);
+    const uint8_t* src = g->map + g->data_offset + t.offset;
+    for (size_t off = 0; off < t.nbytes; off += CHUNK) {
+      const size_t n = std::min<size_t>(CHUNK, t.nbytes - off);
+      if (stg.used[k] && cudaEventSynchronize(stg.ev[k]) != cudaSuccess) {
+        cudaFree(dt.d);
+        return set_error(INFERNO_ECUDA, "load_gguf %s: staging copy failed", t.name.c_str());
+      }
+      memcpy(stg.buf[k], src + off, n);
+      if (cudaMemcpyAsync((uint8_t*)dt.d + off, stg.buf[k], n, cudaMemcpyHostToDevice, e->st) != cudaSuccess ||
+          cudaEventRecord(stg.ev[k], e->st) != cudaSuccess) {
+        cudaStreamSynchronize(e->st);
+        cudaFree(dt.d);
+        return set_error(INFERNO_ECUDA, "load_gguf %s: host-to-device copy failed", t.name.c_str());
+      }
+      stg.used[k] = true;
+      k ^= 1;
+    }
+    auto it = e->tensors.find(t.name);
+    if (it != e->tensors.end()) {
+      cudaStreamSynchronize(e->st);
+      cudaFree(it->second.d);
+    }
+    e->tensors[t.name] = dt;
+  }
+  INF_CUDA_TRY(cudaStreamSynchronize(e->st));
   return 0;
 }
 

@@ -45,6 +45,9 @@ EXPORTS = [
     "inferno_state_save_device", "inferno_state_restore_device", "inferno_kernels_per_token",
     "inferno_profile_tokens", "inferno_gemv_host_noalloc", "inferno_debug_trace", "inferno_tp_unique_id",
     "inferno_gdn_recurrence", "inferno_sample_logits", "inferno_decode_sample",
+    "inferno_gguf_open", "inferno_gguf_close", "inferno_gguf_version", "inferno_gguf_n_tensors", "inferno_gguf_n_kv",
+    "inferno_gguf_data_offset", "inferno_gguf_key", "inferno_gguf_tensor_info", "inferno_gguf_get_int",
+    "inferno_gguf_get_float", "inferno_gguf_get_string", "inferno_gguf_get_array", "inferno_engine_load_gguf",
 ]
 
 _lib = None
@@ -100,6 +103,20 @@ def _sig(L0):
     L.inferno_state_restore_device.argtypes = [p]
     L.inferno_kernels_per_token.argtypes = [p]
     L.inferno_profile_tokens.argtypes = [p, C.c_int32, i, i, p, p]
+    L.inferno_gguf_open.argtypes = [C.c_char_p, p]
+    L.inferno_gguf_close.argtypes = [p]
+    L.inferno_gguf_version.argtypes = [p]
+    for nm in ("inferno_gguf_n_tensors", "inferno_gguf_n_kv", "inferno_gguf_data_offset"):
+        getattr(L, nm).argtypes = [p]
+        getattr(L, nm).restype = i64
+    L.inferno_gguf_key.argtypes = [p, i64]
+    L.inferno_gguf_key.restype = C.c_char_p
+    L.inferno_gguf_tensor_info.argtypes = [p, i64, p, p, p, p, p]
+    L.inferno_gguf_get_int.argtypes = [p, C.c_char_p, p]
+    L.inferno_gguf_get_float.argtypes = [p, C.c_char_p, p]
+    L.inferno_gguf_get_string.argtypes = [p, C.c_char_p, p]
+    L.inferno_gguf_get_array.argtypes = [p, C.c_char_p, p, p, p]
+    L.inferno_engine_load_gguf.argtypes = [p, p]
 
 
 def lib():

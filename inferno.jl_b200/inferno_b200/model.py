@@ -108,13 +108,17 @@ class Model:
 
     def __init__(self, spec: S.ModelSpec, tensors: dict, device: int = 0, max_ctx: int | None = None,
                  use_graphs: bool = True, use_pdl: bool = True, tp_rank: int = 0, tp_size: int = 1,
-                 tp_uid: bytes | None = None):
+                 tp_uid: bytes | None = None, gguf=None):
         """tp_size > 1: this process is rank `tp_rank` of a tensor-parallel group;
         `tensors` is the full model (sharded here, inferno_b200.tp) and
         `tp_uid` the group's NCCL unique id (Model.tp_unique_id() on rank 0,
-        shared by the caller).  All ranks must construct concurrently."""
+        shared by the caller).  All ranks must construct concurrently.
+        `gguf` (a gguf_file.GgufFile, one GPU): the weights are uploaded from
+        the file mapping by the library itself and `tensors` is not used."""
         self.spec = spec
         lspec = spec
+        if gguf is not None and tp_size > 1:
+            raise ValueError("the native GGUF upload loads whole tensors; shard through `tensors` for tp_size > 1")
         if tp_size > 1:
             from . import tp as _tp
             if tp_uid is None or len(tp_uid) != 128:
@@ -145,6 +149,9 @@ class Model:
         call("inferno_engine_create", C.byref(c), C.byref(h))
         self.h = h
         try:
+            if gguf is not None:
+                call("inferno_engine_load_gguf", self.h, gguf.h)
+                tensors = {}
             for name, t in tensors.items():
                 ne = np.ones(4, np.int64)
                 ne[:len(t.ne)] = t.ne
@@ -164,7 +171,21 @@ class Model:
         return buf.raw
 
     @classmethod
-    def from_gguf(cls, path, **kw) -> "Model":
+    def from_gguf(cls, path, native: bool = True, **kw) -> "Model":
+        """load_model_cpu (src/LoaderCPU.jl:450-643) from a GGUF file.  native:
+        the library parses the file and uploads the tensors from its mapping
+        (inferno_gguf_open + inferno_engine_load_gguf); otherwise gguf-py reads
+        it and each tensor goes through inferno_engine_upload_tensor (needed
+        for tp_size > 1, where the host shards the tensors)."""
+        if native and kw.get("tp_size", 1) == 1:
+            from .gguf_file import GgufFile
+            g = GgufFile(path)
+            try:
+                infos = {t.name: t for t in g.tensors()}
+                spec = spec_from_config(config_from_metadata(g.metadata(), infos), Path(path).stem)
+                return cls(spec, None, gguf=g, **kw)
+            finally:
+                g.close()
         md, tensors = read_gguf(path)
         return cls(spec_from_config(config_from_metadata(md, tensors), Path(path).stem), tensors, **kw)
 

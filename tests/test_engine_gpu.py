@@ -207,3 +207,25 @@ def test_fused_inproj_gdn_opt_in(monkeypatch):
     assert rel(lg1, lg0) < 1e-4
     orc = O.OracleModel(spec, T)
     assert got == orc.generate(prompt, 12)
+
+
+def test_native_gguf_upload_matches_python_upload(tiny, tmp_path):
+    """Model.from_gguf through the library's reader and pinned staging
+    (inferno_engine_load_gguf) generates the same tokens and logits as the
+    same weights uploaded tensor by tensor from Python, and as the oracle."""
+    spec, T, orc = tiny
+    path = tmp_path / "tiny.gguf"
+    S.write_gguf(path, spec, T)
+    prompt = S.tokens(12, 10, spec.vocab)
+    a = Model.from_gguf(path, native=True)
+    b = Model(spec, T)
+    assert a.spec.vocab == spec.vocab and a.spec.layers == spec.layers
+    _, la = a.forward(prompt, 0)
+    _, lb = b.forward(prompt, 0)
+    assert np.array_equal(la, lb)
+    a.reset()
+    b.reset()
+    got = a.generate(prompt, 16)
+    assert got == b.generate(prompt, 16) == orc.generate(prompt, 16)
+    a.close()
+    b.close()

@@ -1,0 +1,148 @@
+"""Native GGUF reader (inferno_gguf_*) against gguf-py on seeded files, plus
+the reference reader's error cases (src/GGUF.jl:76-165): bad magic, strings
+over 1 MiB, truncation, unknown value types, tensor data past the end."""
+import struct
+
+import numpy as np
+import pytest
+
+from inferno_b200 import synth as S
+from inferno_b200._lib import InfernoError
+from inferno_b200.gguf_file import GgufFile
+from inferno_b200.model import config_from_metadata, read_gguf, spec_from_config
+
+
+@pytest.fixture(scope="module")
+def tiny_gguf(tmp_path_factory):
+    spec = S.CONFIGS["tiny"]
+    T = S.make_model(spec, seed=9)
+    path = tmp_path_factory.mktemp("g") / "tiny.gguf"
+    S.write_gguf(path, spec, T)
+    return spec, T, path
+
+
+def test_tensors_match_gguf_py(tiny_gguf):
+    spec, T, path = tiny_gguf
+    md, T2 = read_gguf(path)
+    with GgufFile(path) as g:
+        assert g.version == 3
+        assert len(g) == len(T2)
+        infos = g.tensors()
+        assert [t.name for t in infos] == list(T2)           # file order
+        for i, t in enumerate(infos):
+            ref = T2[t.name]
+            assert t.ggml_type == ref.ggml_type
+            assert t.ne == tuple(ref.ne)
+            assert t.nbytes == ref.data.nbytes
+            assert np.array_equal(g.tensor_bytes(i), ref.data.reshape(-1)), t.name
+            assert np.array_equal(g.tensor_bytes(i), T[t.name].data.reshape(-1)), t.name
+        assert g.data_offset % 32 == 0
+
+
+def test_metadata_and_config_match_gguf_py(tiny_gguf):
+    spec, T, path = tiny_gguf
+    md, T2 = read_gguf(path)
+    with GgufFile(path) as g:
+        nat = g.metadata()
+        for k, v in md.items():
+            if isinstance(v, (list, tuple)) or k.startswith("GGUF."):   # gguf-py's header pseudo-keys
+                continue
+            assert k in nat, k
+            if isinstance(v, float):
+                assert nat[k] == pytest.approx(v, rel=1e-7), k
+            else:
+                assert nat[k] == v, k
+        assert g.get("no.such.key", 123) == 123
+        assert "general.architecture" in g and "no.such.key" not in g
+        infos = {t.name: t for t in g.tensors()}
+        s_nat = spec_from_config(config_from_metadata(nat, infos))
+        s_py = spec_from_config(config_from_metadata(md, T2))
+        assert s_nat == s_py
+
+
+# ---- hand-made files for the error paths ------------------------------------
+def _s(x: bytes) -> bytes:
+    return struct.pack("<Q", len(x)) + x
+
+
+def _file(kvs=b"", nkv=0, tinfo=b"", nt=0, data=b"", magic=b"GGUF", version=3, align=32):
+    head = magic + struct.pack("<IQQ", version, nt, nkv) + kvs + tinfo
+    pad = (-len(head)) % align
+    return head + b"\0" * pad + data
+
+
+def _kv_u32(key, v):
+    return _s(key) + struct.pack("<II", 4, v)
+
+
+def _tensor(name, ne, ggml_type, offset):
+    return _s(name) + struct.pack("<I", len(ne)) + b"".join(struct.pack("<Q", d) for d in ne) + \
+        struct.pack("<IQ", ggml_type, offset)
+
+
+def _open(tmp_path, blob):
+    p = tmp_path / "x.gguf"
+    p.write_bytes(blob)
+    return GgufFile(p)
+
+
+def test_minimal_file_and_alignment(tmp_path):
+    data = np.arange(64, dtype=np.float32).tobytes()
+    blob = _file(kvs=_kv_u32(b"general.alignment", 64), nkv=1, tinfo=_tensor(b"w", (16, 4), 0, 0), nt=1,
+                 data=data, align=64)
+    with _open(tmp_path, blob) as g:
+        assert g.data_offset % 64 == 0
+        assert g.get("general.alignment") == 64
+        t = g.tensor(0)
+        assert (t.name, t.ggml_type, t.ne, t.nbytes) == ("w", 0, (16, 4), 256)
+        assert np.array_equal(g.tensor_bytes(0).view(np.float32), np.arange(64, dtype=np.float32))
+
+
+def test_value_types(tmp_path):
+    kvs = (_s(b"a.u8") + struct.pack("<IB", 0, 200) + _s(b"a.i16") + struct.pack("<Ih", 3, -5) +
+           _s(b"a.f32") + struct.pack("<If", 6, 0.25) + _s(b"a.bool") + struct.pack("<IB", 7, 1) +
+           _s(b"a.str") + struct.pack("<I", 8) + _s(b"hello") +
+           _s(b"a.u64") + struct.pack("<IQ", 10, 2**63 + 5) + _s(b"a.f64") +
+           struct.pack("<Id", 12, 1.5) +
+           _s(b"a.arr") + struct.pack("<IIQ", 9, 5, 3) + struct.pack("<3i", 1, 2, 3) +
+           _s(b"a.sarr") + struct.pack("<IIQ", 9, 8, 2) + _s(b"x") + _s(b"yz"))
+    with _open(tmp_path, _file(kvs=kvs, nkv=9)) as g:
+        assert g.get("a.u8") == 200 and g.get("a.i16") == -5 and g.get("a.bool") == 1
+        assert g.get("a.f32") == 0.25 and g.get("a.f64") == 1.5 and g.get("a.str") == "hello"
+        assert g.get("a.u64") == (2**63 + 5) - 2**64          # uint64 bit for bit in an int64
+        assert g.get("a.arr") == (5, 3) and g.get("a.sarr") == (8, 2)
+        assert g.keys()[0] == "a.u8" and len(g.keys()) == 9
+
+
+@pytest.mark.parametrize("case", ["magic", "version", "long_string", "truncated", "bad_type", "past_end", "dims"])
+def test_malformed_files_are_rejected(tmp_path, case):
+    if case == "magic":
+        blob = _file(magic=b"GGUG")
+    elif case == "version":
+        blob = _file(version=1)
+    elif case == "long_string":                 # src/GGUF.jl:78-81: > 1 MiB is an error
+        blob = _file(kvs=_s(b"k") + struct.pack("<I", 8) + struct.pack("<Q", (1 << 20) + 1) + b"a" * ((1 << 20) + 1),
+                     nkv=1)
+    elif case == "truncated":
+        blob = _file(kvs=_kv_u32(b"key", 1), nkv=1)[:30]   # cut inside the first key
+    elif case == "bad_type":
+        blob = _file(kvs=_s(b"k") + struct.pack("<II", 13, 0), nkv=1)
+    elif case == "past_end":
+        blob = _file(tinfo=_tensor(b"w", (256, 4), 0, 0), nt=1, data=b"\0" * 100)
+    else:
+        blob = _file(tinfo=_s(b"w") + struct.pack("<I", 5) + b"\0" * 60, nt=1)
+    with pytest.raises(InfernoError) as ei:
+        _open(tmp_path, blob)
+    assert ei.value.rc == -8
+
+
+def test_missing_file_and_bad_key_types(tmp_path):
+    with pytest.raises(InfernoError):
+        GgufFile(tmp_path / "absent.gguf")
+    from inferno_b200._lib import lib
+    import ctypes as C
+    with _open(tmp_path, _file(kvs=_kv_u32(b"k", 7), nkv=1)) as g:
+        s = C.c_char_p()
+        assert lib().inferno_gguf_get_string(g.h, b"k", C.byref(s)) == -1
+        v = C.c_int64()
+        assert lib().inferno_gguf_get_int(g.h, b"nope", C.byref(v)) == -7
