@@ -32,6 +32,12 @@ class InfernoConfig(C.Structure):
         ("tp_size", C.c_int32), ("nccl_unique_id", C.c_void_p)]
 
 
+class InfernoSampling(C.Structure):
+    """include/inferno_b200.h InfernoSampling (softmax_sample's parameters)."""
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_int32), ("min_p", C.c_float),
+                ("repetition_penalty", C.c_float), ("presence_penalty", C.c_float), ("seed", C.c_uint64)]
+
+
 # every symbol the header declares (checked by the CPU tests)
 EXPORTS = [
     "inferno_last_error", "inferno_version", "inferno_device_error",
@@ -103,6 +109,7 @@ def _sig(L0):
     L.inferno_state_restore_device.argtypes = [p]
     L.inferno_kernels_per_token.argtypes = [p]
     L.inferno_profile_tokens.argtypes = [p, C.c_int32, i, i, p, p]
+    L.inferno_decode_sample.argtypes = [p, C.c_int32, i, i, p, p, i, p]
     L.inferno_gguf_open.argtypes = [C.c_char_p, p]
     L.inferno_gguf_close.argtypes = [p]
     L.inferno_gguf_version.argtypes = [p]

@@ -16,7 +16,7 @@ from pathlib import Path
 import numpy as np
 
 from . import synth as S
-from ._lib import InfernoConfig, call, check, lib
+from ._lib import InfernoConfig, InfernoSampling, call, check, lib
 
 
 def _p(a: np.ndarray):
@@ -230,6 +230,36 @@ class Model:
             return [tok]
         rest = self.decode_greedy(tok, len(prompt), n_steps - 1)
         return [tok] + [int(t) for t in rest]
+
+    def decode_sample(self, tok: int, pos: int, n: int, *, temperature: float = 1.0, top_p: float = 1.0,
+                      top_k: int = 0, min_p: float = 0.0, repetition_penalty: float = 1.0,
+                      presence_penalty: float = 0.0, seed: int = 0, seen=()) -> np.ndarray:
+        """n sampled tokens on the device: tok is fed at pos, every later token
+        is drawn by softmax_sample (src/ModelCPU.jl:1123-1225) from the
+        previous token's logits after the presence / repetition penalties on
+        `seen` (0-based ids) and on the tokens drawn so far; draws come from
+        Philox(seed, step), so a seed reproduces a sequence."""
+        s = InfernoSampling(temperature, top_p, top_k, min_p, repetition_penalty, presence_penalty, seed)
+        ids = np.ascontiguousarray(np.asarray(seen, dtype=np.int32).reshape(-1))
+        out = np.zeros(n, np.int32)
+        call("inferno_decode_sample", self.h, int(tok), int(pos), int(n), C.byref(s),
+             _p(ids) if ids.size else None, int(ids.size), _p(out))
+        return out
+
+    def generate_sampled(self, prompt, n_steps: int, **sampling) -> list:
+        """generate_stream_cpu's sampled loop (src/ModelCPU.jl:1277-1370) with
+        the corrected positions: the prompt but its last token is prefilled,
+        the last prompt token is fed at position P-1 and its logits give the
+        first sampled token; the penalties count the prompt tokens and every
+        sampled token.  Keyword arguments as decode_sample."""
+        prompt = np.asarray(prompt, dtype=np.int32).reshape(-1)
+        if prompt.size == 0 or n_steps <= 0:
+            raise ValueError("generate_sampled needs a prompt and n_steps > 0")
+        self.reset()
+        if prompt.size > 1:
+            self.forward(prompt[:-1], 0, want_logits=False)
+        out = self.decode_sample(int(prompt[-1]), int(prompt.size) - 1, n_steps, seen=prompt, **sampling)
+        return [int(t) for t in out]
 
     def reset(self):
         call("inferno_reset_states", self.h)

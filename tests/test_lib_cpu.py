@@ -144,3 +144,31 @@ def test_block_sizes(t):
     # src/QuantsCPU.jl:22-25 and the IQ2_XXS 66-byte block
     assert S.row_bytes(t, 256 if t != S.Q8_0 else 32) == {S.Q4_K: 144, S.Q5_K: 176, S.Q6_K: 210,
                                                            S.Q8_0: 34, S.IQ2_XXS: 66}[t]
+
+
+def test_struct_layouts_match_the_c_header(tmp_path):
+    """InfernoConfig / InfernoSampling field offsets of the Python binding equal
+    what a C compiler makes of include/inferno_b200.h."""
+    import shutil
+    import subprocess
+    from inferno_b200._lib import InfernoSampling
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    structs = {"InfernoConfig": InfernoConfig, "InfernoSampling": InfernoSampling}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "inferno_b200.h"', 'int main(void) {']
+    for sname, cls in structs.items():
+        lines.append(f'  printf("{sname} sizeof %zu\\n", sizeof({sname}));')
+        for f, _ in cls._fields_:
+            lines.append(f'  printf("{sname} {f} %zu\\n", offsetof({sname}, {f}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split("\n")
+    got = {(a, b): int(c) for a, b, c in (ln.split() for ln in out if ln.strip())}
+    for sname, cls in structs.items():
+        assert got[(sname, "sizeof")] == C.sizeof(cls), sname
+        for f, _ in cls._fields_:
+            assert got[(sname, f)] == getattr(cls, f).offset, (sname, f)

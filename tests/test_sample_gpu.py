@@ -91,3 +91,20 @@ def test_engine_sampled_decode():
     greedy = m.decode_greedy(tok, len(prompt), 16).tolist()
     assert run(temperature=0.0) == greedy
     m.close()
+
+
+def test_generate_sampled_host_api():
+    """Model.generate_sampled: temperature 0 is greedy (oracle tokens), a seed
+    reproduces a sampled sequence and another seed changes it."""
+    import oracle as O
+    spec = S.CONFIGS["tiny"]
+    T = S.make_model(spec, seed=11)
+    prompt = S.tokens(13, 9, spec.vocab)
+    m = Model(spec, T)
+    want = O.OracleModel(spec, T).generate(prompt, 12)
+    assert m.generate_sampled(prompt, 12, temperature=0.0) == want
+    a = m.generate_sampled(prompt, 12, temperature=0.8, top_p=0.9, seed=5, repetition_penalty=1.1)
+    b = m.generate_sampled(prompt, 12, temperature=0.8, top_p=0.9, seed=5, repetition_penalty=1.1)
+    c = m.generate_sampled(prompt, 12, temperature=0.8, top_p=0.9, seed=6, repetition_penalty=1.1)
+    assert a == b and a != c and all(0 <= t < spec.vocab for t in a)
+    m.close()
