@@ -63,7 +63,7 @@ class GgufFile:
 
     def keys(self) -> list:
         n = call("inferno_gguf_n_kv", self.h)
-        return [lib().inferno_gguf_key(self.h, i).decode() for i in range(n)]
+        return [lib().inferno_gguf_key(self.h, i).decode(errors="replace") for i in range(n)]
 
     def __contains__(self, key: str) -> bool:
         v = C.c_int64()
@@ -98,7 +98,7 @@ class GgufFile:
         dims = [int(d) for d in ne]
         while len(dims) > 1 and dims[-1] == 1:
             dims.pop()
-        return TensorInfo(name.value.decode(), int(t.value), tuple(dims), int(nb.value))
+        return TensorInfo(name.value.decode(errors="replace"), int(t.value), tuple(dims), int(nb.value))
 
     def tensors(self) -> list:
         return [self.tensor(i) for i in range(len(self))]

@@ -146,3 +146,34 @@ def test_missing_file_and_bad_key_types(tmp_path):
         assert lib().inferno_gguf_get_string(g.h, b"k", C.byref(s)) == -1
         v = C.c_int64()
         assert lib().inferno_gguf_get_int(g.h, b"nope", C.byref(v)) == -7
+
+
+def test_corrupted_headers_never_read_out_of_bounds(tiny_gguf, tmp_path):
+    """Random byte flips and truncations of the header / metadata / tensor
+    table: the reader either parses the file or reports it malformed."""
+    _, _, path = tiny_gguf
+    blob = bytearray(path.read_bytes())
+    with GgufFile(path) as g:
+        head = g.data_offset
+    rng = np.random.default_rng(77)
+    outcomes = {"ok": 0, "error": 0}
+    for trial in range(300):
+        b = bytearray(blob[: head + 4096]) if trial % 3 else bytearray(blob)
+        for _ in range(int(rng.integers(1, 6))):
+            b[int(rng.integers(0, head))] = int(rng.integers(0, 256))
+        if trial % 5 == 0:
+            b = b[: int(rng.integers(24, len(b)))]
+        p = tmp_path / f"c{trial}.gguf"
+        p.write_bytes(bytes(b))
+        try:
+            with GgufFile(p) as g:
+                for i in range(len(g)):
+                    t = g.tensor(i)
+                    if t.nbytes:
+                        g.tensor_bytes(i)          # must stay inside the mapping
+                g.metadata()
+            outcomes["ok"] += 1
+        except InfernoError:
+            outcomes["error"] += 1
+        p.unlink()
+    assert outcomes["error"] > 0 and sum(outcomes.values()) == 300
