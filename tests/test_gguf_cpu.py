@@ -177,3 +177,45 @@ def test_corrupted_headers_never_read_out_of_bounds(tiny_gguf, tmp_path):
             outcomes["error"] += 1
         p.unlink()
     assert outcomes["error"] > 0 and sum(outcomes.values()) == 300
+
+
+def test_plain_c_consumer(tiny_gguf, tmp_path):
+    """The header compiles as C99 and a C program links against the library
+    and reads the GGUF table through the C ABI (no GPU call)."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+    cc = shutil.which("gcc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    root = Path(__file__).resolve().parents[1]
+    libdir = root / "inferno.jl_b200" / "lib"
+    _, T, path = tiny_gguf
+    src = tmp_path / "reader.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include "inferno_b200.h"
+int main(int argc, char** argv) {
+  InfernoGguf* g = 0;
+  if (inferno_gguf_open(argv[1], &g)) { printf("error %s\n", inferno_last_error()); return 1; }
+  const char* arch = 0;
+  inferno_gguf_get_string(g, "general.architecture", &arch);
+  long long n = (long long)inferno_gguf_n_tensors(g);
+  unsigned long long total = 0;
+  for (long long i = 0; i < n; ++i) {
+    uint64_t nb = 0;
+    inferno_gguf_tensor_info(g, i, 0, 0, 0, &nb, 0);
+    total += nb;
+  }
+  printf("%s %lld %llu\n", arch, n, total);
+  inferno_gguf_close(g);
+  return 0;
+}
+''')
+    exe = tmp_path / "reader"
+    subprocess.run([cc, "-std=c99", "-Wall", "-Werror", "-I", str(root / "include"), str(src), "-o", str(exe),
+                    "-L", str(libdir), "-linferno_b200", f"-Wl,-rpath,{libdir}"], check=True)
+    out = subprocess.run([str(exe), str(path)], capture_output=True, text=True, check=True).stdout.split()
+    assert out[0] == "qwen35"
+    assert int(out[1]) == len(T)
+    assert int(out[2]) == sum(t.data.nbytes for t in T.values())
