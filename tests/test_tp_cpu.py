@@ -86,3 +86,31 @@ def test_expert_shards_cover_every_expert_once():
                 assert all(p[name].ne[2] == spec.n_experts // n for p in parts)
             else:
                 assert all(p[name] is t for p in parts), name
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_config4_splits_as_planned(n):
+    """The 9B shape over 2 / 4 / 8 ranks: QK groups, V heads (modulo map),
+    query heads, KV heads (replicated once N exceeds them), FFN columns in
+    whole super-blocks, vocab rows of the lm_head."""
+    spec = S.CONFIGS["qwen35-9b"]
+    tp.check(spec, n)
+    ls = tp.local_spec(spec, n)
+    assert ls.ssm_nk == 16 // n and ls.ssm_nv == 32 // n
+    assert ls.n_heads == 16 // n
+    assert ls.n_kv == (4 // n if n <= 4 else 1)
+    assert ls.ffn == 12288 // n and ls.ffn % 256 == 0
+    assert spec.vocab % n == 0
+    heads = sorted(h for r in range(n) for h in tp.gdn_local_heads(spec, r, n))
+    assert heads == list(range(spec.ssm_nv))
+    # every rank's ssm_out column runs are super-block aligned
+    nk_l = spec.ssm_nk // n
+    assert (nk_l * spec.ssm_dv) % 256 == 0
+
+
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_config5_expert_split(n):
+    spec = S.CONFIGS["qwen35-35b-a3b"]
+    assert spec.n_experts % n == 0
+    with pytest.raises(ValueError):
+        tp.check(spec, n)                       # MoE layers are expert-parallel, not tensor-parallel
