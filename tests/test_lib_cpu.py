@@ -172,3 +172,17 @@ def test_struct_layouts_match_the_c_header(tmp_path):
         assert got[(sname, "sizeof")] == C.sizeof(cls), sname
         for f, _ in cls._fields_:
             assert got[(sname, f)] == getattr(cls, f).offset, (sname, f)
+
+
+def test_missing_library_fails_loudly(tmp_path):
+    """No CPU fallback: without the built library every entry point raises."""
+    import subprocess
+    import sys
+    code = ("import sys; sys.path.insert(0, 'inferno.jl_b200')\n"
+            "from inferno_b200 import _lib\n"
+            "try:\n    _lib.lib()\nexcept RuntimeError as e:\n    print('raised', 'not built' in str(e))\n"
+            "else:\n    print('loaded')\n")
+    env = dict(__import__("os").environ, INFERNO_B200_LIB=str(tmp_path / "absent.so"))
+    out = subprocess.run([sys.executable, "-c", code], cwd=str(ROOT), env=env, capture_output=True, text=True,
+                         check=True).stdout.strip()
+    assert out == "raised True"
