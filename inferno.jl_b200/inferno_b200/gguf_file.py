@@ -90,6 +90,22 @@ class GgufFile:
         call("inferno_gguf_get_array", self.h, k, C.byref(et), C.byref(n), None)
         return (int(et.value), int(n.value))
 
+    _ARRAY_DTYPES = {0: np.uint8, 1: np.int8, 2: np.uint16, 3: np.int16, 4: np.uint32, 5: np.int32,
+                     6: np.float32, 7: np.bool_, 10: np.uint64, 11: np.int64, 12: np.float64}
+
+    def get_array(self, key: str) -> np.ndarray:
+        """A numeric array value as a numpy copy (string arrays: ValueError)."""
+        et, n, data = C.c_int(), C.c_int64(), C.c_void_p()
+        call("inferno_gguf_get_array", self.h, key.encode(), C.byref(et), C.byref(n), C.byref(data))
+        dt = self._ARRAY_DTYPES.get(int(et.value))
+        if dt is None:
+            raise ValueError(f"{key}: array of element type {et.value} has no numeric view")
+        if n.value == 0:
+            return np.zeros(0, dt)
+        nbytes = int(n.value) * np.dtype(dt).itemsize
+        raw = np.ctypeslib.as_array(C.cast(data, C.POINTER(C.c_uint8)), shape=(nbytes,))
+        return raw.copy().view(dt)
+
     def tensor(self, i: int) -> TensorInfo:
         name, t, nb = C.c_char_p(), C.c_int(), C.c_uint64()
         ne = np.ones(4, np.int64)

@@ -219,3 +219,60 @@ int main(int argc, char** argv) {
     assert out[0] == "qwen35"
     assert int(out[1]) == len(T)
     assert int(out[2]) == sum(t.data.nbytes for t in T.values())
+
+
+# ---- the reference's GGUF unit cases (tests/unit/test_gguf.jl:53-282), as files
+def _kv(key: bytes, vtype: int, payload: bytes) -> bytes:
+    return _s(key) + struct.pack("<I", vtype) + payload
+
+
+def test_reference_string_cases(tmp_path):
+    """read_string (:53-118): short, empty, UTF-8, 1 MiB - 1 and exactly
+    1 MiB accepted; 1 MiB + 1, 100 MiB and 2^64 - 1 lengths rejected."""
+    ok = [b"Hello", b"", "Hello 世界!".encode(), b"a" * 1048575, b"b" * 1048576]
+    kvs = b"".join(_kv(f"s{i}".encode(), 8, _s(v)) for i, v in enumerate(ok))
+    with _open(tmp_path, _file(kvs=kvs, nkv=len(ok))) as g:
+        for i, v in enumerate(ok):
+            assert g.get(f"s{i}") == v.decode()
+    for bad_len in (1048577, 100 * 1048576, 2**64 - 1):
+        blob = _file(kvs=_s(b"k") + struct.pack("<IQ", 8, bad_len) + b"x" * 64, nkv=1)
+        with pytest.raises(InfernoError) as ei:
+            _open(tmp_path, blob)
+        assert ei.value.rc == -8
+
+
+def test_reference_value_cases(tmp_path):
+    """read_value (:120-272): every scalar type, strings, int32 / string /
+    empty arrays; an unknown type is an error."""
+    cases = [(b"u8", 0, struct.pack("<B", 42), 42), (b"i8", 1, struct.pack("<b", -42), -42),
+             (b"u16", 2, struct.pack("<H", 1000), 1000), (b"i16", 3, struct.pack("<h", -1000), -1000),
+             (b"u32", 4, struct.pack("<I", 100000), 100000), (b"i32", 5, struct.pack("<i", -100000), -100000),
+             (b"u64", 10, struct.pack("<Q", 10000000000), 10000000000),
+             (b"i64", 11, struct.pack("<q", -10000000000), -10000000000),
+             (b"t", 7, b"\x01", 1), (b"f", 7, b"\x00", 0), (b"w", 8, _s(b"World"), "World")]
+    kvs = b"".join(_kv(k, t, p) for k, t, p, _ in cases)
+    kvs += _kv(b"f32", 6, struct.pack("<f", 3.14159)) + _kv(b"f64", 12, struct.pack("<d", 3.14159265358979))
+    kvs += _kv(b"ai", 9, struct.pack("<IQ", 5, 3) + struct.pack("<3i", 1, 2, 3))
+    kvs += _kv(b"as", 9, struct.pack("<IQ", 8, 2) + _s(b"Hi") + _s(b"World"))
+    kvs += _kv(b"ae", 9, struct.pack("<IQ", 5, 0))
+    with _open(tmp_path, _file(kvs=kvs, nkv=len(cases) + 5)) as g:
+        for k, _, _, want in cases:
+            assert g.get(k.decode()) == want, k
+        assert abs(g.get("f32") - 3.14159) < 1e-5
+        assert abs(g.get("f64") - 3.14159265358979) < 1e-14
+        assert g.get_array("ai").tolist() == [1, 2, 3]
+        assert g.get("as") == (8, 2)
+        with pytest.raises(ValueError):
+            g.get_array("as")
+        assert g.get_array("ae").size == 0
+    with pytest.raises(InfernoError):
+        _open(tmp_path, _file(kvs=_kv(b"k", 999, b"\0" * 16), nkv=1))
+
+
+def test_reference_invalid_magic(tmp_path):
+    """read_gguf (:282-290): magic 0x12345678 is not a GGUF file."""
+    p = tmp_path / "bad.gguf"
+    p.write_bytes(struct.pack("<I", 0x12345678) + b"\0" * 60)
+    with pytest.raises(InfernoError) as ei:
+        GgufFile(p)
+    assert ei.value.rc == -8 and "magic" in str(ei.value)
