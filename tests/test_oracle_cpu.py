@@ -267,3 +267,45 @@ def test_ref_numerics_gemv_matches_reference_bitwise(ref, ggml_type):
         a = O.ref_numerics_gemv(ggml_type, W, x, inner, rows)
         b = O.ref_gemv(ggml_type, W, x, inner, rows, ref)
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+# ---- the reference's sampler unit expectations (tests/unit/test_engine.jl:45-227)
+# stated for softmax_sample (0-based ids) over a sweep of uniform draws r in
+# (0, 1).  (r == 0 exactly -- probability 2^-24 for rand(Float32) -- returns
+# index 0 in the reference's `r <= cumsum` walk even when its probability is 0;
+# the restatement keeps that, and the sweep leaves it out.)
+_RS = [(i + 0.5) / 64 for i in range(64)] + [0.999999]
+
+
+def _support(logits, **kw):
+    return {O.softmax_sample(np.asarray(logits, np.float32), r=r, **kw) for r in _RS}
+
+
+def test_sampler_reference_argmax_cases():
+    """:45-80 temperature 0 = argmax, first occurrence on ties."""
+    assert O.softmax_sample(np.float32([1, 5, 2, 4]), 0.0) == 1
+    assert O.softmax_sample(np.float32([-10, -5, -1]), 0.0) == 2
+    assert O.softmax_sample(np.float32([1, 5, 2, 5]), 0.0) == 1
+    assert O.softmax_sample(np.float32([42]), 0.0) == 0
+    assert O.softmax_sample(np.float32([3, 3, 3]), 0.0) == 0
+    assert O.softmax_sample(np.float32([100, 500, 1000]), 0.0) == 2
+    assert O.softmax_sample(np.float32([-1e4, -1e5, -1e3]), 0.0) == 2
+
+
+def test_sampler_reference_topk_topp_cases():
+    """:82-126 and :219-227: top-k / top-p supports."""
+    assert _support([1, 10, 2, 9], temperature=0.7, top_k=2) <= {1, 3}
+    assert _support([1, 5, 3], temperature=0.7, top_k=1) == {1}
+    assert _support([1, 2, 3], temperature=0.5, top_k=100) <= {0, 1, 2}       # k beyond the vocabulary
+    assert _support([10, 1, 1, 1], temperature=0.5, top_k=0) <= {0, 1, 2, 3}
+    assert _support([1, 100, 2], temperature=0.5, top_p=0.01) == {1}
+    s = [O.softmax_sample(np.float32([1, 2, 3, 10]), 0.5, top_p=0.5, r=r) for r in _RS]
+    assert s.count(3) > len(s) // 2
+    assert _support([1, 10, 2, 9, 3, 8], temperature=0.5, top_p=0.8, top_k=3) <= {1, 3, 5}
+
+
+def test_sampler_reference_temperature_cases():
+    """:128-146: high temperature spreads, low temperature concentrates."""
+    assert len(_support([1, 10, 2], temperature=2.0)) >= 2
+    low = [O.softmax_sample(np.float32([1, 10, 2]), 0.1, r=r) for r in _RS]
+    assert low.count(1) > 0.75 * len(low)
