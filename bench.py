@@ -141,6 +141,33 @@ def cpu_baseline(spec, T, tokens_to_decode=6, prefill=2) -> dict:
                       f"OpenMP over {O.cpu_count()} threads"}
 
 
+def reference_kernel_gbs(T, reps=5) -> dict | None:
+    """The reference's own quantized GEMV (src/kernels/quant_kernels.c
+    q6_k_gemv, compiled from source into oracle/_ref) on the dominant kernel's
+    shape -- the tied lm_head, Q6_K 248320 x 1024 -- on the host cores, for
+    comparison with the GPU kernel's `roofline.achieved`.  None when the
+    reference library is not built."""
+    try:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle as O
+        L = O.ref_lib()
+        if L is None:
+            return None
+        t = T["token_embd.weight"]
+        inner, rows = int(t.ne[0]), int(t.ne[1])
+        x = np.random.default_rng(SEED).standard_normal(inner).astype(np.float32)
+        O.ref_gemv(14, t.data, x, inner, rows, L)                  # warm-up
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            O.ref_gemv(14, t.data, x, inner, rows, L)
+        dt = (time.perf_counter() - t0) / reps
+        return {"kernel": "reference q6_k_gemv (Q8_K activations, AVX2 + FMA, OpenMP)", "shape": [rows, inner],
+                "ms": 1e3 * dt, "gbs": t.data.nbytes / dt / 1e9, "threads": O.cpu_count(),
+                "note": "the reference's own C kernel on the lm_head bytes, host cores"}
+    except Exception:
+        return None
+
+
 def run_reference(args):
     ws, rank, _ = dist_env()
     if rank != 0:
@@ -302,6 +329,9 @@ def run_ours(args):
             "wall_s": wall}
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(spec, T)
+        ref_k = reference_kernel_gbs(T)
+        if ref_k:
+            line["cpu_reference_kernel"] = ref_k
     if rank == 0:
         print(json.dumps(line), flush=True)
     m.close()
