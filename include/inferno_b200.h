@@ -82,20 +82,23 @@ float vec_dot_q8_0_q8_0(const void* x, const void* y, int nb);
 /* frees the cached device copies of compatibility-tier weights */
 int inferno_compat_release(void);
 
-/* Allocation-free host-pointer GEMV: out[r] = sum_i W[r,i] * x[i], same
- * kernel and numerics as q*_gemv above, but it never calls cudaMalloc (or
+/* Allocation-free host-pointer GEMV: out[r] = sum_i W[r,i] * x[i] with the
+ * numerics of q*_gemv above (the replaced library's Q8_K path by default,
+ * fp32 activations with INFERNO_COMPAT_FP32=1; IQ2_XXS and F32, which have no
+ * q*_gemv, always use fp32 activations), but it never calls cudaMalloc (or
  * any allocating routine).  It is for callers that cannot let a library
  * allocate device memory -- a host runtime that owns the device allocator or
  * enforces a hard memory budget, or a sandboxed plugin without allocation
  * rights.  This entry has no counterpart in the reference.
- * Weight, x and y are staged in one static device array of
- * INFERNO_NOALLOC_SCRATCH_BYTES that every GPU loading the library keeps
- * until exit; weight + x + y (each rounded up to 256 B, plus 256 B) must fit,
- * else INFERNO_EINVAL.  The array is shared by all calls and keeps the last
- * call's contents; calls are synchronous and serialised by a mutex, but
- * overlapping GPU work on the array from elsewhere would race.  The first
- * call on a device looks up the array's address; make it before any stream
- * capture.  Returns 0 or a negative status. */
+ * It runs on the calling thread's current CUDA device (unlike q*_gemv, which
+ * select INFERNO_B200_DEVICE).  Weight, x, y and x's Q8_K blocks are staged
+ * in one static device array of INFERNO_NOALLOC_SCRATCH_BYTES that every GPU
+ * loading the library keeps until exit; their sum (each rounded up to 256 B,
+ * plus 256 B) must fit, else INFERNO_EINVAL.  The array is shared by all
+ * calls and keeps the last call's contents; calls are synchronous and
+ * serialised by a mutex, but overlapping GPU work on the array from elsewhere
+ * would race.  The first call on a device looks up the array's address; make
+ * it before any stream capture.  Returns 0 or a negative status. */
 #define INFERNO_NOALLOC_SCRATCH_BYTES (32u << 20)
 int inferno_gemv_host_noalloc(int ggml_type, const uint8_t* weight, const float* x, float* out, int inner_dim,
                               int outer_dim);
@@ -140,6 +143,25 @@ int inferno_gemv_swiglu(int ggml_type, const void* Wg, const void* Wu, const flo
  * dk = 128, dv % 16 == 0; q, k, S 16-byte aligned. */
 int inferno_gdn_recurrence(int T, int n_heads, int dk, int dv, const float* q, const float* k, const float* v,
                            const float* beta, const float* g, float* S, float* y, void* stream);
+
+/* One gated full-attention decode step of one layer at position pos: the
+ * part of FullAttentionCPU after its q/k/v projections
+ * (src/ModelCPU.jl:766-851): rmsnorm_rotary! of q and k (:187-231, NeoX
+ * half-split RoPE on the first rope_dim dims, tables as :134-153),
+ * update_kv_cache! (:245-258), flash_attention_cpu! per query head
+ * (src/FlashAttention.jl:16-74, blocked GQA kv = h / (n_heads/n_kv_heads))
+ * and the sigmoid gate (:846-851).  Device pointers: qg [n_heads][2*head_dim]
+ * (q then gate per head, as the wq projection lays it out), k, v
+ * [n_kv_heads][head_dim] (pre-norm), q_norm, k_norm [head_dim], caches
+ * [max_ctx][n_kv_heads][head_dim] (rows < pos hold earlier positions; row pos
+ * is written), out [n_heads][head_dim].  head_dim 256; split_len = positions
+ * per split-K CTA (a multiple of 32; 0 = the engine's choice for max_ctx).
+ * The call is synchronous on `stream` (it stages the RoPE rows and the split
+ * scratch with stream-ordered allocation). */
+int inferno_attention_step(const float* qg, const float* k, const float* v, const float* q_norm, const float* k_norm,
+                           float eps, int n_heads, int n_kv_heads, int head_dim, int rope_dim, float rope_theta,
+                           float* k_cache, float* v_cache, int max_ctx, int pos, int split_len, float* out,
+                           void* stream);
 
 /* Sampling parameters of generate_cpu / softmax_sample
  * (src/ModelCPU.jl:1123-1225): temperature 0 = greedy. */
@@ -260,11 +282,15 @@ int inferno_kernels_per_token(InfernoEngine* eng);
 int inferno_profile_tokens(InfernoEngine* eng, int32_t tok, int pos, int n_tokens, float* ms_by_class,
                            int32_t* launches_by_class);
 
-/* Debug: with INFERNO_B200_TRACE set at engine creation, each GEMV of a
- * token records %globaltimer stamps (32 slots per GEMV, in launch order:
- * CTA 0 at [0..15], last CTA at [16..31]; 0 entry, 1 first weight copy
- * issued, 2 griddepcontrol.wait returned, 3 prologue done, 4 first tile
- * arrived, 5 first tile consumed, 6 all tiles done).  Copies n stamps out. */
+/* Debug: with INFERNO_B200_TRACE set at engine creation and a library built
+ * with -DINFERNO_KTRACE=1, every GEMV, GDN and attention launch of a token
+ * folds the %globaltimer stamps of all its CTAs into 8 u64 slots (launch
+ * order): [0] kind (1 CUDA-core GEMV, 2 tensor-core GEMV, 3 GDN step,
+ * 4 attention), [1] ~first CTA entry, [2] ~first CTA past
+ * griddepcontrol.wait, [3] last CTA past the wait, [4] last prologue done,
+ * [5] last first weight tile, [6] last CTA exit ("~": stored complemented).
+ * out == NULL clears the stamps (call before the token to record); else
+ * copies n u64 out. */
 int inferno_debug_trace(InfernoEngine* eng, unsigned long long* out, int n);
 
 /* Device time of the last inferno_decode_greedy call in ms (CUDA events). */
@@ -279,6 +305,16 @@ float inferno_last_decode_ms(InfernoEngine* eng);
  * reference has no multi-GPU path for this model family. */
 #define INFERNO_TP_UNIQUE_ID_BYTES 128
 int inferno_tp_unique_id(void* out, int nbytes);
+
+/* Failure-path check of the tensor-parallel residual exchange on one GPU
+ * (debug / tests): runs the tensor-core GEMV as an exchange reader against
+ * partial buffers that nothing writes, with a poll limit of spin_limit
+ * (1 .. 2^22) per word.  Expected result: INFERNO_EDEVICE with
+ * *device_error_out = 1 (bounded wait timed out), the kernel having returned
+ * and the context still usable.  The engine's own limit is set with
+ * INFERNO_XCH_SPIN at engine creation (default 2^22 polls).  No reference
+ * counterpart. */
+int inferno_debug_xch_timeout(int spin_limit, int* device_error_out);
 
 int inferno_engine_destroy(InfernoEngine* eng);
 

@@ -282,8 +282,6 @@ int inferno_gemv_ex(int ggml_type, const void* W, const float* x, float* y, int 
   c.epi = epilogue;
   c.argmax = argmax;
   c.force_r = force_rows_per_warp;
-  // debug: INFERNO_GEMV_TRACE=<device address of 32 u64> records phase times
-  if (const char* tr = getenv("INFERNO_GEMV_TRACE")) c.trace = (unsigned long long*)strtoull(tr, nullptr, 0);
   if (prologue == PRO_RMSNORM && !norm_w) return set_error(INFERNO_EINVAL, "gemv_ex: RMSNorm needs a weight");
   if (epilogue == EPI_ARGMAX && !argmax) return set_error(INFERNO_EINVAL, "gemv_ex: argmax output missing");
   if (epilogue == EPI_SWIGLU) return set_error(INFERNO_EINVAL, "gemv_ex: use inferno_gemv_swiglu");
@@ -364,3 +362,63 @@ int inferno_compat_release(void) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Failure-path check of the tensor-parallel exchange reader on one GPU: the
+// tensor-core GEMV runs in reader mode (RMSNorm prologue that polls the
+// ranks' tagged partials) against two "peer" partial buffers that nothing
+// writes, so every tag stays stale; with a poll limit of spin_limit per word
+// the kernel must record DERR_MBAR_TIMEOUT, skip the remaining waits and
+// return.  No reference counterpart (the reference has no multi-GPU path).
+// ---------------------------------------------------------------------------
+extern "C" int inferno_debug_xch_timeout(int spin_limit, int* device_error_out) {
+  if (spin_limit <= 0 || spin_limit > (1 << 22))
+    return set_error(INFERNO_EINVAL, "debug_xch_timeout: spin_limit must be in [1, 2^22]");
+  constexpr int H = 1024, ROWS = 64, NR = 2;
+  const size_t wbytes = (size_t)ROWS * (H / 256) * 144;
+  const size_t bytes = wbytes + 4 * H * 3 + 8 * (size_t)2 * NR * H + 256 * 4;
+  uint8_t* buf = nullptr;
+  INF_CUDA_TRY(cudaMalloc(&buf, bytes));
+  cudaError_t e = cudaMemset(buf, 0, bytes);   // Q4_K blocks with d = dmin = 0, x = 0, tags 0
+  int rc = 0;
+  if (e != cudaSuccess) rc = set_error(INFERNO_ECUDA, "debug_xch_timeout: %s", cudaGetErrorString(e));
+  uint8_t* q = buf + wbytes;
+  float* x = (float*)q;
+  float* normw = x + H;
+  float* y = normw + H;
+  unsigned long long* parts = (unsigned long long*)(y + H);
+  unsigned long long* seq = parts + 2 * NR * H;   // sequence base 0: the expected tag is 1
+  float* x_next = (float*)(seq + 8);
+  int* err = (int*)(x_next + H);
+  if (!rc) {
+    GemvCall c;
+    c.type = T_Q4_K;
+    c.inner = H;
+    c.mats[0] = {buf, y, ROWS};
+    c.nmats = 1;
+    c.x = x;
+    c.x_stride = H;
+    c.pro = PRO_RMSNORM;
+    c.pro_w = normw;
+    c.err = err;
+    c.xch_n = NR;
+    c.xch_rank = 0;
+    c.xch_rk = 0;
+    c.xch_spin = (unsigned)spin_limit;
+    c.xch_seq = seq;
+    c.xch_parts[0] = parts;
+    c.xch_parts[1] = parts;
+    c.x_next = x_next;
+    rc = launch_gemv(c, (cudaStream_t)0, false);
+  }
+  int h = 0;
+  if (!rc) {
+    e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(&h, err, 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) rc = set_error(INFERNO_ECUDA, "debug_xch_timeout: %s", cudaGetErrorString(e));
+  }
+  cudaFree(buf);
+  if (rc) return rc;
+  if (device_error_out) *device_error_out = h;
+  return h ? set_error(INFERNO_EDEVICE, "exchange reader timed out (device error %d)", h) : 0;
+}

@@ -20,6 +20,8 @@
 //
 // Cache layout: [ctx][n_kv][head_dim] fp32 (the reference's (hd, nkv, seq)
 // column-major array, element (d, h, p) at d + hd*(h + nkv*p)).
+#include <cmath>
+#include <vector>
 #include "internal.h"
 #include "common.cuh"
 #include "params.h"
@@ -58,6 +60,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
   const int h = blockIdx.x, s = blockIdx.y, d = threadIdx.x;
   const int kvh = h / (p.nh / p.nkv);
   const int lane = d & 31, warp = d >> 5;
+  if (d == 0) {
+    KT_KIND(p.trace, KT_ATTN);
+    KT_FIRST(p.trace, 1);
+  }
 
   // ---------------- pre-wait: position and the first K/V chunk ----------------
   const int pos = *p.pos;     // written by the previous step's finalize
@@ -75,6 +81,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
   if (s < nact) load_chunk(p, kvh, j0, min(j0 + ATT_CHUNK, j1), pos, kreg, vreg);
   pdl_wait();
   pdl_trigger();
+  if (d == 0) {
+    KT_FIRST(p.trace, 2);
+    KT_LAST(p.trace, 3);
+  }
   if (s >= nact) return;
 
   // ---------------- q (and the new k) : RMSNorm + RoPE ----------------
@@ -166,6 +176,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
   __syncthreads();
   if (d == 0) ticket = atomicAdd(&p.counters[h], 1);
   __syncthreads();
+  if (d == 0) KT_LAST(p.trace, 6);
   if (ticket != nact - 1) return;
   __threadfence();
   if (d == 0) p.counters[h] = 0;
@@ -180,18 +191,19 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
   }
   const float g = p.qg[(long long)h * 2 * ATT_HD + ATT_HD + d];
   p.out[(long long)h * ATT_HD + d] = (num / den) * (1.0f / (1.0f + expf(-g)));
+  if (d == 0) KT_LAST(p.trace, 6);
 }
 
 int launch_attn_decode(const AttnParams& p, cudaStream_t st, bool pdl) {
   if (p.nh % p.nkv || p.split_len % ATT_CHUNK || p.split_len < ATT_CHUNK || p.rd > ATT_HD || p.rd % 2)
     return set_error(INFERNO_EINVAL, "attention: unsupported shape (nh=%d nkv=%d split=%d rd=%d)", p.nh, p.nkv,
                      p.split_len, p.rd);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                         cudaSharedmemCarveoutMaxShared);
-    attr = true;
-  }
+  static DeviceOnce once;
+  cudaError_t ea = once.run([] {
+    return cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                cudaSharedmemCarveoutMaxShared);
+  });
+  if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "attention attribute: %s", cudaGetErrorString(ea));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.nh, p.nsplit);
   cfg.blockDim = dim3(ATT_THREADS);
@@ -206,3 +218,110 @@ int launch_attn_decode(const AttnParams& p, cudaStream_t st, bool pdl) {
 }
 
 }  // namespace inf
+
+namespace inf {
+
+void build_rope(int ctx, int rd, float theta, std::vector<float>& cs, std::vector<float>& sn) {
+  // src/ModelCPU.jl:134-153: inv_freq in Float64 rounded to Float32, angle in
+  // Float32, cos/sin of that Float32 angle (correctly rounded here).
+  const int half = rd / 2;
+  cs.assign((size_t)ctx * half, 0.f);
+  sn.assign((size_t)ctx * half, 0.f);
+  for (int i = 0; i < half; ++i) {
+    float inv = (float)(1.0 / std::pow((double)theta, (2.0 * i) / (double)rd));
+    for (int p = 0; p < ctx; ++p) {
+      float f = inv * (float)p;
+      cs[(size_t)p * half + i] = (float)std::cos((double)f);
+      sn[(size_t)p * half + i] = (float)std::sin((double)f);
+    }
+  }
+}
+
+int attn_split_len(int max_ctx) {
+  int sl = ATT_CHUNK;
+  while ((max_ctx + sl - 1) / sl > 128) sl += ATT_CHUNK;
+  return sl;
+}
+
+}  // namespace inf
+
+using namespace inf;
+
+extern "C" int inferno_attention_step(const float* qg, const float* k, const float* v, const float* q_norm,
+                                      const float* k_norm, float eps, int n_heads, int n_kv_heads, int head_dim,
+                                      int rope_dim, float rope_theta, float* k_cache, float* v_cache, int max_ctx,
+                                      int pos, int split_len, float* out, void* stream) {
+  if (!qg || !k || !v || !q_norm || !k_norm || !k_cache || !v_cache || !out)
+    return set_error(INFERNO_EINVAL, "attention_step: null pointer");
+  if (head_dim != ATT_HD) return set_error(INFERNO_EINVAL, "attention_step: head_dim must be %d", ATT_HD);
+  if (n_heads < 1 || n_kv_heads < 1 || n_heads % n_kv_heads || rope_dim < 0 || rope_dim > head_dim || rope_dim % 2)
+    return set_error(INFERNO_EINVAL, "attention_step: bad heads (%d / %d) or rope_dim %d", n_heads, n_kv_heads,
+                     rope_dim);
+  if (max_ctx < 1 || pos < 0 || pos >= max_ctx)
+    return set_error(INFERNO_EINVAL, "attention_step: pos %d outside [0, %d)", pos, max_ctx);
+  if (split_len == 0) split_len = attn_split_len(max_ctx);
+  if (split_len < ATT_CHUNK || split_len % ATT_CHUNK)
+    return set_error(INFERNO_EINVAL, "attention_step: split_len %d is not a positive multiple of %d", split_len,
+                     ATT_CHUNK);
+  cudaStream_t st = (cudaStream_t)stream;
+  int dev = 0;
+  INF_CUDA_TRY(cudaGetDevice(&dev));
+  // RoPE rows 0..pos (the kernel reads row pos) and the split-K scratch
+  std::vector<float> cs, sn;
+  const int half = rope_dim / 2;
+  build_rope(pos + 1, rope_dim, rope_theta, cs, sn);
+  const int nsplit = (max_ctx + split_len - 1) / split_len;
+  const size_t n_rope = (size_t)(pos + 1) * half, n_po = (size_t)n_heads * nsplit * ATT_HD,
+               n_ml = (size_t)n_heads * nsplit * 2;
+  const size_t bytes = (2 * n_rope + n_po + n_ml) * 4 + (size_t)(n_heads + 1) * 4 + 256;
+  char* scratch = nullptr;
+  INF_CUDA_TRY(cudaMallocAsync((void**)&scratch, bytes, st));
+  float* rc = (float*)scratch;
+  float* rs = rc + n_rope;
+  float* po = rs + n_rope;
+  float* ml = po + n_po;
+  int* counters = (int*)(ml + n_ml);
+  int* dpos = counters + n_heads;
+  int rc_ = 0;
+  cudaError_t e = cudaSuccess;
+  if (n_rope) {
+    e = cudaMemcpyAsync(rc, cs.data(), n_rope * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(rs, sn.data(), n_rope * 4, cudaMemcpyHostToDevice, st);
+  }
+  if (e == cudaSuccess) e = cudaMemsetAsync(counters, 0, (size_t)n_heads * 4, st);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(dpos, &pos, 4, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) rc_ = set_error(INFERNO_ECUDA, "attention_step set-up: %s", cudaGetErrorString(e));
+  if (!rc_) {
+    AttnParams a{};
+    a.qg = qg;
+    a.k = k;
+    a.v = v;
+    a.q_norm = q_norm;
+    a.k_norm = k_norm;
+    a.eps = eps;
+    a.rope_cos = rc;
+    a.rope_sin = rs;
+    a.rd = rope_dim;
+    a.kc = k_cache;
+    a.vc = v_cache;
+    a.nh = n_heads;
+    a.nkv = n_kv_heads;
+    a.ctx = max_ctx;
+    a.split_len = split_len;
+    a.nsplit = nsplit;
+    a.pos = dpos;
+    a.part_o = po;
+    a.part_ml = ml;
+    a.counters = counters;
+    a.out = out;
+    a.err = device_error_word(dev);
+    rc_ = launch_attn_decode(a, st, false);
+  }
+  // the host vectors must outlive the copies: wait before returning
+  cudaError_t ef = cudaFreeAsync(scratch, st);
+  cudaError_t es = cudaStreamSynchronize(st);
+  if (rc_) return rc_;
+  if (ef != cudaSuccess || es != cudaSuccess)
+    return set_error(INFERNO_ECUDA, "attention_step: %s", cudaGetErrorString(ef != cudaSuccess ? ef : es));
+  return 0;
+}

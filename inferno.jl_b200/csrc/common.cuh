@@ -94,6 +94,31 @@ __device__ __forceinline__ void tma_load_1d_hint(void* dst, const void* src, uin
       : "memory");
 }
 
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Kernel timeline stamps, compiled in only with -DINFERNO_KTRACE=1 (they sit
+// on the latency-critical path).  With INFERNO_B200_TRACE set at engine
+// creation every launch of a token gets 8 u64 slots (`trace`); thread 0 of
+// every CTA folds its %globaltimer into them with atomicMax, earliest-of
+// stamps stored complemented so that one zeroed buffer serves both:
+//   0 kernel kind, 1 ~first CTA entry, 2 ~first CTA past griddepcontrol.wait,
+//   3 last CTA past the wait, 4 last prologue done, 5 last first weight tile,
+//   6 last CTA exit.
+#ifndef INFERNO_KTRACE
+#define INFERNO_KTRACE 0
+#endif
+enum KtKind : int { KT_GEMV = 1, KT_GEMV_MMA = 2, KT_GDN = 3, KT_ATTN = 4 };
+#define KT_FIRST(tr, s) \
+  do { if (INFERNO_KTRACE && (tr)) atomicMax((tr) + (s), ~gtimer()); } while (0)
+#define KT_LAST(tr, s) \
+  do { if (INFERNO_KTRACE && (tr)) atomicMax((tr) + (s), gtimer()); } while (0)
+#define KT_KIND(tr, k) \
+  do { if (INFERNO_KTRACE && (tr) && blockIdx.x == 0 && blockIdx.y == 0) (tr)[0] = (k); } while (0)
+
 // Programmatic dependent launch (no-ops when the launch did not enable it).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

@@ -788,14 +788,12 @@ size_t pk_smem_bytes(int hidden_pad, int max_inner_pad, int slot_bytes) {
 }
 
 int pk_launch(const PkParams& P, size_t smem, cudaStream_t st) {
-  static size_t attr_smem = 0;
-  if (attr_smem < smem) {
-    cudaError_t e = cudaFuncSetAttribute(decode_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess)
-      return set_error(INFERNO_ECUDA, "persistent kernel attribute (%zu B smem): %s", smem, cudaGetErrorString(e));
-    attr_smem = smem;
-  }
+  static DeviceOnce once;
+  cudaError_t ea = once.run([] {
+    return cudaFuncSetAttribute(decode_persistent_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  if (ea != cudaSuccess)
+    return set_error(INFERNO_ECUDA, "persistent kernel attribute: %s", cudaGetErrorString(ea));
   int dev = 0;
   cudaGetDevice(&dev);
   int per_sm = 0;

@@ -116,6 +116,7 @@ struct InfernoEngine {
   unsigned long long* xch_peer[8] = {};   // every rank's [2][N][H] exchange words (own + IPC-mapped)
   unsigned* xch_done = nullptr;           // setup barrier word
   unsigned long long* xch_seq = nullptr;
+  unsigned xch_spin = 0;            // reader polls per word before a timeout (INFERNO_XCH_SPIN; 0 = 2^22)
   bool finalized = false;
   int C = 0, di = 0, rd = 0, split_len = 64, nsplit = 1;
   // activations
@@ -159,7 +160,7 @@ struct InfernoEngine {
   // the tokens the penalties apply to
   const inf::SampleArgs* sampling = nullptr;
   uint8_t* seen = nullptr;
-  unsigned long long* trace = nullptr;   // debug: per-GEMV phase stamps (INFERNO_B200_TRACE)
+  unsigned long long* trace = nullptr;   // debug: per-launch timeline slots (INFERNO_B200_TRACE)
   int trace_idx = 0;
   int launches = 0;              // kernels enqueued since the last enqueue_token began
   int token_launches = 0;        // kernels of one decode token (set by enqueue_token)
@@ -218,6 +219,13 @@ void mark(InfernoEngine* e, int kind) {
   e->prof_kind.push_back(kind);
 }
 
+// debug timeline: 8 slots per launch of a token (INFERNO_B200_TRACE)
+constexpr int TRACE_SLOTS = 8, TRACE_LAUNCHES = 1024;
+unsigned long long* trace_slot(InfernoEngine* e) {
+  if (!e->trace || e->trace_idx >= TRACE_LAUNCHES) return nullptr;
+  return e->trace + TRACE_SLOTS * (e->trace_idx++);
+}
+
 constexpr int EPI_XCH_WRITE = 100;   // engine-level: residual partial to the TP exchange
 
 int gemv(InfernoEngine* e, int type, int inner, std::initializer_list<GemvMat> mats, const float* x, int pro,
@@ -241,6 +249,7 @@ int gemv(InfernoEngine* e, int type, int inner, std::initializer_list<GemvMat> m
     c.xch_n = n;
     c.xch_rank = e->cfg.tp_rank;
     c.xch_seq = e->xch_seq;
+    c.xch_spin = e->xch_spin;
     for (int q = 0; q < n; ++q) c.xch_parts[q] = e->xch_peer[q];
     if (epi == EPI_XCH_WRITE) {
       c.epi = EPI_STORE;
@@ -251,7 +260,7 @@ int gemv(InfernoEngine* e, int type, int inner, std::initializer_list<GemvMat> m
       c.x_next = e->xcur == e->x ? e->x2 : e->x;
     }
   }
-  if (e->trace && e->trace_idx < 256) c.trace = e->trace + 32 * (e->trace_idx++);
+  c.trace = trace_slot(e);
   int rc = launch_gemv(c, e->st, pdl);
   if (!rc) mark(e, epi == EPI_ARGMAX ? K_LMHEAD : K_GEMV);
   return rc;
@@ -430,6 +439,7 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     g.y = e->y;
     g.step = L.step;
     g.done = L.done;
+    g.trace = trace_slot(e);
     if (!(ab & 2) && (rc = launch_gdn_step(g, e->st, pdl))) return rc;
     mark(e, K_GDN);
     if (!(ab & 8) && (rc = gemv(e, L.ssm_out->type, e->di, {M(L.ssm_out, e->x)}, e->y, (ab & 128) ? PRO_NONE : PRO_HEADNORM_GATE,
@@ -476,6 +486,7 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     a.counters = e->att_counters;
     a.out = e->o;
     a.err = e->err;
+    a.trace = trace_slot(e);
     if (!(ab & 4) && (rc = launch_attn_decode(a, e->st, pdl))) return rc;
     mark(e, K_ATTN);
     if (!(ab & 8) && (rc = gemv(e, L.wo->type, c.n_heads * c.head_dim, {M(L.wo, e->x)}, e->o, PRO_NONE, nullptr, nullptr, 0,
@@ -681,6 +692,7 @@ int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
       g.xch_n = c.tp_size;
       g.xch_rank = c.tp_rank;
       g.xch_seq = e->xch_seq;
+      g.xch_spin = e->xch_spin;
       for (int q = 0; q < c.tp_size; ++q) g.xch_parts[q] = e->xch_peer[q];
       g.xch_rk = e->xch_pending;
       g.x_next = e->xcur == e->x ? e->x2 : e->x;
@@ -757,22 +769,6 @@ int run_steps(InfernoEngine* e, int n, bool logits_last) {
       if ((rc = enqueue_token(e, logits_last && t == n - 1, e->cfg.use_pdl != 0))) return rc;
   }
   return 0;
-}
-
-void build_rope(int ctx, int rd, float theta, std::vector<float>& cs, std::vector<float>& sn) {
-  // src/ModelCPU.jl:134-153: inv_freq in Float64 rounded to Float32, angle in
-  // Float32, cos/sin of that Float32 angle (correctly rounded here).
-  const int half = rd / 2;
-  cs.assign((size_t)ctx * half, 0.f);
-  sn.assign((size_t)ctx * half, 0.f);
-  for (int i = 0; i < half; ++i) {
-    float inv = (float)(1.0 / std::pow((double)theta, (2.0 * i) / (double)rd));
-    for (int p = 0; p < ctx; ++p) {
-      float f = inv * (float)p;
-      cs[(size_t)p * half + i] = (float)std::cos((double)f);
-      sn[(size_t)p * half + i] = (float)std::sin((double)f);
-    }
-  }
 }
 
 }  // namespace
@@ -895,12 +891,13 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
                        ncclGetErrorString(r));
     }
   }
+  if (const char* sp = getenv("INFERNO_XCH_SPIN")) e->xch_spin = (unsigned)strtoul(sp, nullptr, 0);
   const char* d = getenv("INFERNO_B200_DUMP");
   e->dump = d && atoi(d) != 0;
   if (const char* ab = getenv("INFERNO_B200_ABLATE")) e->ablate = (unsigned)strtoul(ab, nullptr, 0);
   if (getenv("INFERNO_B200_TRACE")) {
-    if (cudaMalloc(&e->trace, 32 * 256 * 8 + 8192 * 8) != cudaSuccess) e->trace = nullptr;
-    else cudaMemset(e->trace, 0, 32 * 256 * 8 + 8192 * 8);
+    if (cudaMalloc(&e->trace, 8 * 8192) != cudaSuccess) e->trace = nullptr;
+    else cudaMemset(e->trace, 0, 8 * 8192);
   }
   *out = e;
   return 0;
@@ -1192,8 +1189,7 @@ int inferno_engine_finalize(InfernoEngine* e) {
   }
   e->max_out = c.max_ctx + 8;
   // attention splits: multiples of 32 positions, at most 128 splits
-  e->split_len = 32;
-  while ((c.max_ctx + e->split_len - 1) / e->split_len > 128) e->split_len += 32;
+  e->split_len = attn_split_len(c.max_ctx);
   e->nsplit = (c.max_ctx + e->split_len - 1) / e->split_len;
   e->rd = (int)std::lround(c.head_dim * (double)c.partial_rotary_factor);   // src/LoaderCPU.jl:375
   if (any_attn) {
@@ -1692,7 +1688,12 @@ int inferno_debug_trace(InfernoEngine* e, unsigned long long* out, int n) {
   int rc;
   if ((rc = ready(e))) return rc;
   if (!e->trace) return set_error(INFERNO_ESTATE, "engine created without INFERNO_B200_TRACE");
-  if (n > 32 * 256 + 8192) n = 32 * 256 + 8192;
+  if (!out) {   // clear: the stamps of the next token start from zero
+    INF_CUDA_TRY(cudaDeviceSynchronize());
+    INF_CUDA_TRY(cudaMemset(e->trace, 0, 8 * 8192));
+    return 0;
+  }
+  if (n > 8192) n = 8192;
   INF_CUDA_TRY(cudaMemcpy(out, e->trace, (size_t)n * 8, cudaMemcpyDeviceToHost));
   return 0;
 }

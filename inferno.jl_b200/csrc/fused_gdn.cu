@@ -287,13 +287,11 @@ int launch_fused_inproj_gdn(const void* Wperm, int H, const float* x, const floa
   p.nxv = 1;
   p.xch_wk = p.xch_rk = -1;
   const size_t smem = fused_gdn_smem(H);
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(fused_inproj_gdn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return set_error(INFERNO_ECUDA, "fused in_proj + GDN attribute: %s", cudaGetErrorString(e));
-    attr = true;
-  }
+  static DeviceOnce once;
+  cudaError_t ea = once.run([] {
+    return cudaFuncSetAttribute(fused_inproj_gdn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "fused in_proj + GDN attribute: %s", cudaGetErrorString(ea));
   FusedGdnArgs fa{z};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(g.nv * FG_CLUSTER);

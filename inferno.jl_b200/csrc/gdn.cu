@@ -59,6 +59,10 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(const __grid_cons
   const int warp = tid >> 5, lane = tid & 31;
   const int g = h % p.nk;
   const int K = p.K, C = p.C, H = p.H;
+  if (tid == 0) {
+    KT_KIND(p.trace, KT_GDN);
+    KT_FIRST(p.trace, 1);
+  }
 
   // ---------------- pre-wait: state and constants ----------------
   const int t = *p.step;            // written by this layer's previous step
@@ -103,6 +107,10 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(const __grid_cons
 
   pdl_wait();
   pdl_trigger();
+  if (tid == 0) {
+    KT_FIRST(p.trace, 2);
+    KT_LAST(p.trace, 3);
+  }
 
   // ---------------- alpha / beta of RMSNorm(x) ----------------
   // alpha = sum_i Wa[i] * (x[i]*scale*w[i]) = scale * sum_i Wa[i]*w[i]*x[i]
@@ -215,19 +223,21 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(const __grid_cons
       *p.step = t + 1;
       __threadfence();
     }
+    KT_LAST(p.trace, 6);
   }
 }
 
 int launch_gdn_step(const GdnParams& p, cudaStream_t st, bool pdl) {
   if (p.dv % GDN_ROWS || p.K < 1 || p.K > GDN_MAXK || p.H % 4 || p.H > GDN_MAX_H)
     return set_error(INFERNO_EINVAL, "gdn: unsupported dims (dv=%d, K=%d, H=%d)", p.dv, p.K, p.H);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(gdn_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 3 * GDN_MAX_H * 4);
-    cudaFuncSetAttribute(gdn_step_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                         cudaSharedmemCarveoutMaxShared);
-    attr = true;
-  }
+  static DeviceOnce once;
+  cudaError_t ea = once.run([] {
+    cudaError_t e = cudaFuncSetAttribute(gdn_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 3 * GDN_MAX_H * 4);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(gdn_step_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                cudaSharedmemCarveoutMaxShared);
+  });
+  if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "GDN step attribute: %s", cudaGetErrorString(ea));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.nv, p.dv / GDN_ROWS);
   cfg.blockDim = dim3(GDN_THREADS);

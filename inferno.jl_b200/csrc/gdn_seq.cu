@@ -130,12 +130,11 @@ extern "C" int inferno_gdn_recurrence(int T, int n_heads, int dk, int dv, const 
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)S) & 15)
     return set_error(INFERNO_EINVAL, "gdn_recurrence: q, k and S must be 16-byte aligned");
   const size_t smem = 2 * sizeof(GsBuf);
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(gdn_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return set_error(INFERNO_ECUDA, "gdn_recurrence: %s", cudaGetErrorString(e));
-    attr = true;
-  }
+  static DeviceOnce once;
+  cudaError_t ea = once.run([] {
+    return cudaFuncSetAttribute(gdn_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "gdn_recurrence: %s", cudaGetErrorString(ea));
   gdn_seq_kernel<<<dim3(n_heads, dv / GS_ROWS), GS_THREADS, smem, (cudaStream_t)stream>>>(T, n_heads, dv, q, k, v,
                                                                                            beta, g, S, y);
   cudaError_t e = cudaGetLastError();

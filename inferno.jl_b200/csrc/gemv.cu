@@ -13,19 +13,16 @@ namespace {
 
 template <int TYPE, int NB, int R, int NW>
 cudaError_t launch_one(const GemvParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
-  static bool attr_done[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_done[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<TYPE, NB, R, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         227 * 1024);
+  // one carve-out for every kernel of the engine: no L1 / shared-memory
+  // reconfiguration between back-to-back launches
+  static DeviceOnce once;
+  cudaError_t ea = once.run([] {
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<TYPE, NB, R, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
-    // one carve-out for every kernel of the engine: no L1/shared
-    // reconfiguration between back-to-back launches
-    cudaFuncSetAttribute(gemv_kernel<TYPE, NB, R, NW>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                         cudaSharedmemCarveoutMaxShared);
-    attr_done[dev & 63] = true;
-  }
+    return cudaFuncSetAttribute(gemv_kernel<TYPE, NB, R, NW>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                cudaSharedmemCarveoutMaxShared);
+  });
+  if (ea != cudaSuccess) return ea;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3((NW + 1) * 32);
@@ -62,22 +59,21 @@ cudaError_t launch_nb(const GemvParams& p, int NB, int R, int NW, int grid, size
   }
 }
 
-template <int TYPE, int MODE>
+template <int TYPE, int MODE, int NW>
 cudaError_t launch_mma_mode(const GemvParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
-  static bool attr_done[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_done[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<TYPE, 16, MODE>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  // one carve-out for every kernel of the engine: no L1 / shared-memory
+  // reconfiguration between back-to-back launches
+  static DeviceOnce once;
+  cudaError_t ea = once.run([] {
+    cudaError_t e = cudaFuncSetAttribute(gemv_mma_kernel<TYPE, NW, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
-    cudaFuncSetAttribute(gemv_mma_kernel<TYPE, 16, MODE>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                         cudaSharedmemCarveoutMaxShared);
-    attr_done[dev & 63] = true;
-  }
+    return cudaFuncSetAttribute(gemv_mma_kernel<TYPE, NW, MODE>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                cudaSharedmemCarveoutMaxShared);
+  });
+  if (ea != cudaSuccess) return ea;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(17 * 32);
+  cfg.blockDim = dim3((NW + 1) * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
@@ -85,36 +81,55 @@ cudaError_t launch_mma_mode(const GemvParams& p, int grid, size_t smem, cudaStre
   at[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<TYPE, 16, MODE>, p);
+  return cudaLaunchKernelEx(&cfg, gemv_mma_kernel<TYPE, NW, MODE>, p);
+}
+
+template <int TYPE, int NW>
+cudaError_t launch_mma_nw(const GemvParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
+  if (p.xch_wk >= 0 || p.xch_rk >= 0) return launch_mma_mode<TYPE, MMA_XCH, NW>(p, grid, smem, st, pdl);
+  bool moe = p.nxv > 1;
+  for (int i = 0; i < p.nseg; ++i) moe |= p.seg[i].indirect != 0;
+  if (moe) return launch_mma_mode<TYPE, MMA_MOE, NW>(p, grid, smem, st, pdl);
+  return launch_mma_mode<TYPE, MMA_PLAIN, NW>(p, grid, smem, st, pdl);
 }
 
 template <int TYPE>
-cudaError_t launch_mma(const GemvParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
-  if (p.xch_wk >= 0 || p.xch_rk >= 0) return launch_mma_mode<TYPE, MMA_XCH>(p, grid, smem, st, pdl);
-  bool moe = p.nxv > 1;
-  for (int i = 0; i < p.nseg; ++i) moe |= p.seg[i].indirect != 0;
-  if (moe) return launch_mma_mode<TYPE, MMA_MOE>(p, grid, smem, st, pdl);
-  return launch_mma_mode<TYPE, MMA_PLAIN>(p, grid, smem, st, pdl);
+cudaError_t launch_mma(const GemvParams& p, int nw, int grid, size_t smem, cudaStream_t st, bool pdl) {
+  return nw == 8 ? launch_mma_nw<TYPE, 8>(p, grid, smem, st, pdl) : launch_mma_nw<TYPE, 16>(p, grid, smem, st, pdl);
 }
 
 // Integer tensor-core path (gemv_mma.cuh) for single-column Q4_K / Q6_K.
 // Returns 1 when the shape does not fit it (the caller falls back).
 int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool pdl) {
-  constexpr int NW = 16;
   const int bb = bb_of(c.type);
   const bool paired = c.epi == EPI_SWIGLU;
   const int nsb = c.inner / 256;
   const long long row_bytes = (long long)nsb * bb;
-  const size_t smem_cap = 220 * 1024;
+  long long wbytes = 0;
+  for (int i = 0; i < c.nmats; ++i) wbytes += (long long)c.mats[i].rows * row_bytes;
+  // Per-layer matrices (<= 64 MB): lean CTAs (8 consumer warps, <= 110 KB of
+  // shared memory), so that this kernel's CTA and the next kernel's fit on
+  // one SM together; with the early trigger the next kernel's weights then
+  // stream in while this one computes.  The lm_head keeps 16 warps and the
+  // whole shared memory (it is throughput-bound).
+  static const int env_lean = getenv("INFERNO_MMA_LEAN") ? atoi(getenv("INFERNO_MMA_LEAN")) : 0;
+  static const int env_early = getenv("INFERNO_PDL_EARLY") ? atoi(getenv("INFERNO_PDL_EARLY")) : 0;
   const int nxv = c.nxv;
-  const size_t fixed = 16 * GEMV_MAX_STAGES + (2 * NW + 4 + 16) * 4 + NW * 16 * 4 +
-                       (size_t)nxv * ((size_t)nsb * 16 * 4 + (size_t)c.inner * 4 + (size_t)nsb * 8 * MMA_KS_BYTES) + 128;
-  bool any_indirect = false;
-  for (int i = 0; i < c.nmats; ++i) any_indirect |= c.mats[i].indirect != 0;
+  auto fixed_of = [&](int nw) -> size_t {
+    return 16 * GEMV_MAX_STAGES + (2 * nw + 4 + 16) * 4 + nw * 16 * 4 +
+           (size_t)nxv * ((size_t)nsb * 16 * 4 + (size_t)c.inner * 4 + (size_t)nsb * 8 * MMA_KS_BYTES) + 128;
+  };
   auto stage_of = [&](int TR) -> size_t {
     if (paired) return 2 * (((size_t)(TR / 2) * row_bytes + 32 + 15) / 16 * 16) + 128;
     return ((size_t)TR * row_bytes + 48 + 127) / 128 * 128;
   };
+  // lean only when two stages of the smallest tile fit next to the staged
+  // activations (long rows, e.g. 12288 inputs, keep the full CTA)
+  const int NW = (env_lean && wbytes <= (64ll << 20) && fixed_of(8) + 2 * stage_of(16) <= 110 * 1024) ? 8 : 16;
+  const size_t smem_cap = NW == 8 ? 110 * 1024 : 220 * 1024;
+  const size_t fixed = fixed_of(NW);
+  bool any_indirect = false;
+  for (int i = 0; i < c.nmats; ++i) any_indirect |= c.mats[i].indirect != 0;
   // cost: tile steps of the busiest CTA (each warp walks ceil(nsb / nkg)
   // super-blocks per tile) plus the bytes it streams
   int best_tr = 0;
@@ -163,6 +178,7 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
   p.xch_rank = c.xch_rank;
   p.xch_wk = c.xch_wk;
   p.xch_rk = c.xch_rk;
+  p.xch_spin = c.xch_spin ? c.xch_spin : (1u << 22);
   p.xch_seq = c.xch_seq;
   for (int q = 0; q < 8; ++q) p.xch_parts[q] = c.xch_parts[q];
   p.x_next = c.x_next;
@@ -185,6 +201,7 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
   p.trace = c.trace;
   static const bool no_hint = getenv("INFERNO_GEMV_NO_L2HINT") != nullptr;
   p.l2_evict_first = no_hint ? 0 : 1;
+  p.early_trigger = env_early;
   if (ntiles == 0) return 0;
   const size_t stage_bytes = stage_of(TR);
   p.stages = (int)std::min<size_t>(GEMV_MAX_STAGES, (smem_cap - fixed) / stage_bytes);
@@ -193,26 +210,25 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
   p.part1_off = (int)((((size_t)(TR / 2) * row_bytes + 32 + 15) / 16) * 16);
   const size_t smem = fixed + (size_t)p.stages * stage_bytes;
   const int grid = std::min(ntiles, sms);
-  cudaError_t e = c.type == T_Q4_K   ? launch_mma<T_Q4_K>(p, grid, smem, st, pdl)
-                  : c.type == T_Q6_KR ? launch_mma<T_Q6_KR>(p, grid, smem, st, pdl)
-                                      : launch_mma<T_Q6_K>(p, grid, smem, st, pdl);
+  cudaError_t e = c.type == T_Q4_K   ? launch_mma<T_Q4_K>(p, NW, grid, smem, st, pdl)
+                  : c.type == T_Q6_KR ? launch_mma<T_Q6_KR>(p, NW, grid, smem, st, pdl)
+                                      : launch_mma<T_Q6_K>(p, NW, grid, smem, st, pdl);
   if (e != cudaSuccess) return set_error(-2, "gemv launch failed: %s", cudaGetErrorString(e));
   return 0;
 }
 
 template <int TYPE>
 cudaError_t launch_mma_batch(const GemvParams& p, int grid, size_t smem, cudaStream_t st, bool pdl) {
-  static bool attr_done[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_done[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_mma_batch_kernel<TYPE, MMA_NBT>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  // one carve-out for every kernel of the engine: no L1 / shared-memory
+  // reconfiguration between back-to-back launches
+  static DeviceOnce once;
+  cudaError_t ea = once.run([] {
+    cudaError_t e = cudaFuncSetAttribute(gemv_mma_batch_kernel<TYPE, MMA_NBT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
-    cudaFuncSetAttribute(gemv_mma_batch_kernel<TYPE, MMA_NBT>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                         cudaSharedmemCarveoutMaxShared);
-    attr_done[dev & 63] = true;
-  }
+    return cudaFuncSetAttribute(gemv_mma_batch_kernel<TYPE, MMA_NBT>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                cudaSharedmemCarveoutMaxShared);
+  });
+  if (ea != cudaSuccess) return ea;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3((MMA_NBT + 1) * 32);

@@ -71,6 +71,11 @@ struct GemvParams {
   int argmax_row0;                // global index of row 0 (vocab-split lm_head)
   int* err;
   int l2_evict_first;             // stream weights with an L2 evict_first policy
+  // 1: the producer warp lets the next kernel launch at once (it reads only
+  // weights, which no kernel writes), so under programmatic dependent launch
+  // the next kernel's CTAs become resident and start streaming their own
+  // weights while this kernel still computes
+  int early_trigger;
   const int* eidx;                // MoE: expert id per erows-row block of an indirect segment
   long long estride;              // bytes between experts
   int erows;                      // rows per expert block (also the input-slot period)
@@ -85,23 +90,12 @@ struct GemvParams {
   // polls parts[k & 1][r][i] until the tags match, uses x + sum_r partial_r
   // (rank order: bit-identical on every rank) and CTA 0 stores it in x_next.
   int xch_n, xch_rank, xch_wk, xch_rk;
+  unsigned xch_spin;              // polls of one word before the reader gives up (DERR_MBAR_TIMEOUT)
   const unsigned long long* xch_seq;
   unsigned long long* xch_parts[8];  // each rank's [2][n][H] words
   float* x_next;
-  unsigned long long* trace;      // debug: phase timestamps of CTA 0 / last CTA (null = off)
+  unsigned long long* trace;      // debug: 8 timeline slots of this launch (KT_*; null = off)
 };
-
-__device__ __forceinline__ unsigned long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-// debug phase stamps (INFERNO_GEMV_TRACE): CTA 0 -> slots 0..15, last CTA -> 16..31
-#define GEMV_TRACE(slot)                                                            \
-  do {                                                                              \
-    if (p.trace && (blockIdx.x == 0 || blockIdx.x == gridDim.x - 1))                \
-      p.trace[(blockIdx.x == 0 ? 0 : 16) + (slot)] = gtimer();                      \
-  } while (0)
 
 __device__ __constant__ uint64_t c_iq2xxs_grid_init[256] = {
 #include "iq2xxs_grid.inc"
@@ -524,6 +518,10 @@ __device__ __forceinline__ void gemv_producer(const GemvParams& p, uint64_t* ful
   const bool paired = (p.epi == EPI_SWIGLU);
   const int TR = p.TR, half_tr = TR / 2;
   bool waited = false;
+  if (p.early_trigger && !(IND && p.eidx)) {
+    pdl_trigger();
+    waited = true;
+  }
   if (IND && p.eidx) {
     // expert ids come from the preceding kernel: no weight prefetch before the wait
     pdl_wait();
@@ -559,7 +557,6 @@ __device__ __forceinline__ void gemv_producer(const GemvParams& p, uint64_t* ful
         else
           tma_load_1d(st + (lane ? p.part1_off : 0), (const void*)a0, bytes, &full[s]);
       }
-      if (lane == 0 && it == 0) GEMV_TRACE(1);
     }
     // weights stream before the wait; dependents launch only after it
     if ((it == p.stages - 1 || it == n_items - 1) && !waited) {
@@ -578,7 +575,10 @@ template <int TYPE, int NB, int R, int NW>
 __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid == 0) GEMV_TRACE(0);
+  if (tid == 0) {
+    KT_KIND(p.trace, KT_GEMV);
+    KT_FIRST(p.trace, 1);
+  }
   constexpr bool SUMS = Frag<TYPE>::kNeedSums;
   // layout: [full bars][empty bars][red NB*NW][kpart][grid 2KB][xs][stages]
   uint64_t* full = (uint64_t*)smem;
@@ -610,7 +610,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
 
   // ---------------- consumer warps ----------------
   pdl_wait();
-  if (tid == 0) GEMV_TRACE(2);
+  if (tid == 0) {
+    KT_FIRST(p.trace, 2);
+    KT_LAST(p.trace, 3);
+  }
   if (TYPE == T_IQ2_XXS) {
     for (int i = tid; i < 256; i += NW * 32) {
       const uint64_t g = c_iq2xxs_grid_init[i];
@@ -618,7 +621,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
     }
   }
   gemv_prologue<TYPE, NW>(p, xs, red, tid);
-  if (tid == 0) GEMV_TRACE(3);
+  if (tid == 0) KT_LAST(p.trace, 4);
   // per-column factor applied to the row dots (1/rms for RMSNorm, else 1)
   float colscale[NB];
 #pragma unroll
@@ -645,7 +648,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
   for (int it = 0; it < n_items; ++it) {
     const int s = it % p.stages;
     if (!mbar_wait(&full[s], (it / p.stages) & 1, p.err)) return;
-    if (tid == 0 && it == 0) GEMV_TRACE(4);
+    if (tid == 0 && it == 0) KT_LAST(p.trace, 5);
     int sg, row0;
     tile_locate(p, blockIdx.x + it * G, sg, row0);
     const uint8_t* st = stage0 + (long long)s * stage_bytes;
@@ -702,7 +705,6 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    if (tid == 0 && it == 0) GEMV_TRACE(5);
 
     // ---- reduce the tile's rows: lanes, then K groups through smem ----
     const int myrow = reduce_row_of<R>(lane);
@@ -749,7 +751,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_kernel(co
       }
     }
   }
-  if (tid == 0) GEMV_TRACE(6);
+  if (tid == 0) KT_LAST(p.trace, 6);
   if (p.epi == EPI_ARGMAX && wk == 0) {
 #pragma unroll
     for (int b = 0; b < NB; ++b) {

@@ -40,12 +40,6 @@ constexpr int MMA_KS_BYTES = 256;     // B bytes per k step (8 columns x 32 k)
 // exchange paths -- every launch fetches its instructions cold, and unused
 // branches inlined into the hot path cost measurable time per launch.
 enum MmaMode : int { MMA_PLAIN = 0, MMA_MOE = 1, MMA_XCH = 2 };
-// Per-phase timestamps (GemvParams::trace) are compiled in only on request
-// (-DINFERNO_MMA_TRACE=1): they sit on the latency-critical path.
-#ifndef INFERNO_MMA_TRACE
-#define INFERNO_MMA_TRACE 0
-#endif
-constexpr bool MMA_TRACE = INFERNO_MMA_TRACE != 0;
 // The super-block bodies' outer loops are not unrolled: the per-layer GEMVs
 // are latency-bound and every launch fetches its code cold, so code size
 // matters more than loop overhead.
@@ -144,8 +138,9 @@ __device__ float gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, 
       for (int j = 0; j < PER; ++j) {
         const int i = tid + j * NT;
         unsigned it = 0;
-        while ((uint32_t)(w[j] >> 32) != tag) {
-          if (++it > (1u << 22)) {
+        // after one word timed out the others are not waited for
+        while (!bad && (uint32_t)(w[j] >> 32) != tag) {
+          if (++it > p.xch_spin) {
             if (p.err) atomicExch(p.err, DERR_MBAR_TIMEOUT);
             bad = true;
             break;
@@ -341,8 +336,9 @@ __device__ float gemv_mma_prologue_reg(const GemvParams& p, uint8_t* xq, float* 
           const unsigned long long* a = parts + (size_t)r * n + 4 * u + t;
           unsigned long long wv = ld_relaxed_sys_u64(a);
           unsigned it = 0;
-          while ((uint32_t)(wv >> 32) != tag) {
-            if (++it > (1u << 22)) {
+          // after one word timed out the others are not waited for
+          while (!bad && (uint32_t)(wv >> 32) != tag) {
+            if (++it > p.xch_spin) {
               if (p.err) atomicExch(p.err, DERR_MBAR_TIMEOUT);
               bad = true;
               break;
@@ -606,10 +602,13 @@ __device__ __forceinline__ void mma_sb_q6kr(const uint8_t* gb, const uint8_t* xq
 }
 
 template <int TYPE, int NW, int MODE>
-__global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kernel(const __grid_constant__ GemvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (MMA_TRACE && tid == 0) GEMV_TRACE(0);
+  if (tid == 0) {
+    KT_KIND(p.trace, KT_GEMV_MMA);
+    KT_FIRST(p.trace, 1);
+  }
   constexpr int BB = TYPE == T_Q4_K ? 144 : TYPE == T_Q6_KR ? Q6R_BLOCK : 210;
   constexpr int XS_PER_SB = TYPE == T_Q4_K ? 8 : 16;
   // layout: [full][empty][red 2*NW+4][vmax 16][kpart NW*16][xsum][xf][xq][stages]
@@ -644,12 +643,15 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
   }
 
   pdl_wait();
-  if (MMA_TRACE && tid == 0) GEMV_TRACE(2);
+  if (tid == 0) {
+    KT_FIRST(p.trace, 2);
+    KT_LAST(p.trace, 3);
+  }
   const bool reg_pro = MODE != MMA_MOE && (p.pro == PRO_RMSNORM || p.pro == PRO_NONE);
   const float colscale = reg_pro ? gemv_mma_prologue_reg<TYPE == T_Q6_KR ? T_Q6_K : TYPE, NW, MODE>(p, xq, xsum, red,
                                                                                                      vmax, tid)
                                  : gemv_mma_prologue<TYPE, NW, MODE>(p, xf, xq, xsum, red, vmax, tid);
-  if (MMA_TRACE && tid == 0) GEMV_TRACE(3);
+  if (tid == 0) KT_LAST(p.trace, 4);
   const bool nonfinite = *(volatile int*)&red[2 * NW] != 0;
   const uint32_t xtag =
       (MODE == MMA_XCH && p.xch_wk >= 0) ? (uint32_t)(*p.xch_seq + (unsigned long long)p.xch_wk + 1ull) : 0u;
@@ -667,7 +669,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
   for (int it = 0; it < n_items; ++it) {
     const int s = it % p.stages;
     if (!mbar_wait(&full[s], (it / p.stages) & 1, p.err)) return;
-    if (MMA_TRACE && tid == 0 && it == 0) GEMV_TRACE(4);
+    if (tid == 0 && it == 0) KT_LAST(p.trace, 5);
     int sg, row0;
     tile_locate(p, blockIdx.x + it * G, sg, row0);
     const uint8_t* st = stage0 + (long long)s * p.stage_bytes;
@@ -707,7 +709,6 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    if (MMA_TRACE && tid == 0 && it == 0) GEMV_TRACE(5);
 
     // quad reduction: lane c holds limb c of the integer dots and a share of
     // the offset terms
@@ -761,7 +762,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_kernel(const __grid
       }
     }
   }
-  if (MMA_TRACE && tid == 0) GEMV_TRACE(6);
+  if (tid == 0) KT_LAST(p.trace, 6);
   if (p.epi == EPI_ARGMAX && wk == 0) {
     float v = best_v;
     int i = best_i;

@@ -2,7 +2,9 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <mutex>
 #include <string>
+#include <vector>
 
 namespace inf {
 
@@ -19,6 +21,28 @@ const char* last_error();
   } while (0)
 
 int num_sms(int device);
+
+// One-time kernel set-up per device (cudaFuncSetAttribute and the like): the
+// function attributes belong to the current device's context, so a second
+// engine on another device needs its own call.  run(f) calls f() on the
+// current device the first time, under a lock, and remembers success; a
+// failure is returned and retried on the next call.
+struct DeviceOnce {
+  std::mutex mu;
+  bool done[64] = {};
+  template <class F>
+  cudaError_t run(F&& f) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> g(mu);
+    if (done[dev]) return cudaSuccess;
+    e = f();
+    if (e == cudaSuccess) done[dev] = true;
+    return e;
+  }
+};
 
 // ---- kernel launchers (return 0 or a negative status) ---------------------
 struct GemvMat {
@@ -59,6 +83,7 @@ struct GemvCall {
   int nxv = 1;
   // tensor-parallel residual exchange (see GemvParams::xch_*); -1 = off
   int xch_n = 0, xch_rank = 0, xch_wk = -1, xch_rk = -1;
+  unsigned xch_spin = 0;      // reader poll limit per word (0 = 2^22)
   const unsigned long long* xch_seq = nullptr;
   unsigned long long* xch_parts[8] = {};
   float* x_next = nullptr;
@@ -102,6 +127,12 @@ int launch_moe_topk(const float* logits, int E, int K, int* idx, float* wts, int
                     cudaStream_t st, bool pdl);
 int launch_moe_combine(float* x, const float* y, const float* wts, const int* idx, int K, int H, int shared,
                        int add_x, cudaStream_t st, bool pdl);
+// RoPE tables cos / sin [ctx][rd/2] (src/ModelCPU.jl:134-153: inv_freq in
+// Float64 rounded to Float32, angle in Float32, correctly rounded cos / sin)
+void build_rope(int ctx, int rd, float theta, std::vector<float>& cs, std::vector<float>& sn);
+// positions per split-K attention CTA for a cache of max_ctx positions (a
+// multiple of 32 giving at most 128 splits)
+int attn_split_len(int max_ctx);
 int launch_embed_row(int type, const void* W, long long row_bytes, int inner, const int* row_ptr, float* dst,
                      int vocab, cudaStream_t st, bool pdl);
 

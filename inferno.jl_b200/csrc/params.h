@@ -21,6 +21,7 @@ struct GdnParams {
   float* y;                // [nv*dv] pre-norm output
   int* step;               // per-layer step counter
   int* done;               // per-layer CTA completion counter
+  unsigned long long* trace = nullptr;   // debug timeline slots (KT_*, common.cuh)
 };
 
 struct AttnParams {
@@ -42,6 +43,7 @@ struct AttnParams {
   int* counters;         // [nkv]
   float* out;            // [nh*hd] gated attention output
   int* err;
+  unsigned long long* trace = nullptr;   // debug timeline slots (KT_*, common.cuh)
 };
 
 int launch_gdn_step(const GdnParams& p, cudaStream_t st, bool pdl);

@@ -325,11 +325,10 @@ int pf_launch(F kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, A... 
 int launch_gdn_chunk(const GdnParams& p, int T, cudaStream_t st) {
   if (T < 1 || T > PF_MAX_T || p.dv % PF_ROWS || p.K < 1 || p.K > PF_MAXK || p.H % 4)
     return set_error(INFERNO_EINVAL, "gdn chunk: unsupported dims");
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(gdn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 3 * 8192 * 4);
-    attr = true;
-  }
+  static DeviceOnce once;
+  cudaError_t ea = once.run(
+      [] { return cudaFuncSetAttribute(gdn_chunk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 3 * 8192 * 4); });
+  if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "GDN chunk attribute: %s", cudaGetErrorString(ea));
   int rc;
   if ((rc = pf_launch(gdn_chunk_kernel, dim3(p.nv, p.dv / PF_ROWS), dim3(PF_THREADS), (size_t)3 * p.H * 4, st, p, T)))
     return rc;

@@ -367,39 +367,69 @@ std::vector<float> f32vec(const std::vector<uint8_t>& raw) {
 }
 
 // src/ModelCPU.jl:134-153 (inv_freq in Float64 rounded to Float32; angle in
-// Float32; cos/sin of the Float32 angle, correctly rounded)
+// Float32; cos/sin of the Float32 angle, correctly rounded): row of position p
+void rope_row(float theta, int rd, int p, float* c, float* s) {
+  for (int i = 0; i < rd / 2; ++i) {
+    float inv = (float)(1.0 / std::pow((double)theta, (2.0 * i) / (double)rd));
+    float f = inv * (float)p;
+    c[i] = (float)std::cos((double)f);
+    s[i] = (float)std::sin((double)f);
+  }
+}
+
 void build_rope(Model& m) {
   int half = m.rd / 2;
   m.rope_cos.assign((size_t)half * m.ctx, 0.0f);
   m.rope_sin.assign((size_t)half * m.ctx, 0.0f);
-  for (int i = 0; i < half; ++i) {
-    float inv = (float)(1.0 / std::pow((double)m.theta, (2.0 * i) / (double)m.rd));
-    for (int p = 0; p < m.ctx; ++p) {
-      float f = inv * (float)p;
-      m.rope_cos[(size_t)p * half + i] = (float)std::cos((double)f);
-      m.rope_sin[(size_t)p * half + i] = (float)std::sin((double)f);
-    }
-  }
+  for (int p = 0; p < m.ctx; ++p)
+    rope_row(m.theta, m.rd, p, m.rope_cos.data() + (size_t)p * half, m.rope_sin.data() + (size_t)p * half);
 }
 
-// src/ModelCPU.jl:187-231
-void rmsnorm_rotary(Model& m, float* x, int nheads, int pos, const float* w) {
-  int half = m.rd / 2;
-  const float* c = m.rope_cos.data() + (size_t)pos * half;
-  const float* s = m.rope_sin.data() + (size_t)pos * half;
+// src/ModelCPU.jl:187-231 on nheads heads of hd, with the RoPE row (c, s)
+// of the current position
+void rmsnorm_rotary_row(float* x, int nheads, int hd, int rd, const float* c, const float* s, const float* w,
+                        float eps) {
+  int half = rd / 2;
   for (int h = 0; h < nheads; ++h) {
-    float* v = x + (size_t)h * m.hd;
+    float* v = x + (size_t)h * hd;
     float ss = 0.0f;
-    for (int i = 0; i < m.hd; ++i) ss += v[i] * v[i];
-    float rms = std::sqrt(ss / (float)m.hd + m.eps);
+    for (int i = 0; i < hd; ++i) ss += v[i] * v[i];
+    float rms = std::sqrt(ss / (float)hd + eps);
     float inv = 1.0f / rms;
-    for (int i = 0; i < m.hd; ++i) v[i] = v[i] * inv * w[i];
+    for (int i = 0; i < hd; ++i) v[i] = v[i] * inv * w[i];
     for (int i = 0; i < half; ++i) {
       float x1 = v[i], x2 = v[i + half];
       v[i] = x1 * c[i] - x2 * s[i];
       v[i + half] = x1 * s[i] + x2 * c[i];
     }
   }
+}
+
+// src/ModelCPU.jl:766-851 after the q/k/v projections: q/k RMSNorm + partial
+// RoPE, KV-cache append at pos, flash attention per query head (blocked GQA
+// kv = h / (nh/nkv)), sigmoid gate.  qg holds [q | gate] per head; the cache
+// is (hd, nkv, ctx) column-major.
+void attention_step(const float* qg, const float* k_in, const float* v_in, const float* q_norm,
+                    const float* k_norm, float eps, int nh, int nkv, int hd, int rd, const float* rc,
+                    const float* rs, float* kc, float* vc, int pos, float* out) {
+  std::vector<float> k(k_in, k_in + (size_t)nkv * hd), q(nh * hd), gt(nh * hd);
+  for (int h = 0; h < nh; ++h)
+    for (int i = 0; i < hd; ++i) {
+      q[h * hd + i] = qg[h * 2 * hd + i];
+      gt[h * hd + i] = qg[h * 2 * hd + hd + i];
+    }
+  rmsnorm_rotary_row(q.data(), nh, hd, rd, rc, rs, q_norm, eps);
+  rmsnorm_rotary_row(k.data(), nkv, hd, rd, rc, rs, k_norm, eps);
+  for (int h = 0; h < nkv; ++h)
+    for (int d = 0; d < hd; ++d) {
+      kc[d + (size_t)hd * (h + (size_t)nkv * pos)] = k[h * hd + d];
+      vc[d + (size_t)hd * (h + (size_t)nkv * pos)] = v_in[h * hd + d];
+    }
+  int gqa = nh / nkv;
+  float scale = 1.0f / std::sqrt((float)hd);
+  for (int h = 0; h < nh; ++h)
+    flash_attention(out + (size_t)h * hd, q.data() + h * hd, kc, vc, h / gqa, pos + 1, scale, hd, nkv);
+  for (size_t i = 0; i < gt.size(); ++i) out[i] *= 1.0f / (1.0f + std::exp(-gt[i]));
 }
 
 // src/ModelCPU.jl:447-473
@@ -516,32 +546,14 @@ void gdn(Model& m, Layer& ly, const float* x, float* out) {
 
 // src/ModelCPU.jl:756-856
 void attention(Model& m, Layer& ly, const float* x, int pos, float* out) {
-  int nh = m.nh, nkv = m.nkv, hd = m.hd;
-  std::vector<float> qg(2 * nh * hd), k(nkv * hd), v(nkv * hd), q(nh * hd), gt(nh * hd), o(nh * hd, 0.0f);
+  int nh = m.nh, nkv = m.nkv, hd = m.hd, half = m.rd / 2;
+  std::vector<float> qg(2 * nh * hd), k(nkv * hd), v(nkv * hd), o(nh * hd, 0.0f);
   ly.wq.gemv(x, qg.data());
   ly.wk.gemv(x, k.data());
   ly.wv.gemv(x, v.data());
-  for (int h = 0; h < nh; ++h)
-    for (int i = 0; i < hd; ++i) {
-      q[h * hd + i] = qg[h * 2 * hd + i];
-      gt[h * hd + i] = qg[h * 2 * hd + hd + i];
-    }
-  rmsnorm_rotary(m, q.data(), nh, pos, ly.q_norm.data());
-  rmsnorm_rotary(m, k.data(), nkv, pos, ly.k_norm.data());
-  for (int h = 0; h < nkv; ++h)
-    for (int d = 0; d < hd; ++d) {
-      ly.kc[d + (size_t)hd * (h + (size_t)nkv * pos)] = k[h * hd + d];
-      ly.vc[d + (size_t)hd * (h + (size_t)nkv * pos)] = v[h * hd + d];
-    }
-  int gqa = nh / nkv;
-  float scale = 1.0f / std::sqrt((float)hd);
-  for (int h = 0; h < nh; ++h) {
-    int kvh = h / gqa;  // blocked GQA
-    flash_attention(o.data() + h * hd, q.data() + h * hd, ly.kc.data(), ly.vc.data(), kvh, pos + 1,
-                    scale, hd, nkv);
-  }
-  for (auto& g : gt) g = 1.0f / (1.0f + std::exp(-g));
-  for (size_t i = 0; i < o.size(); ++i) o[i] *= gt[i];
+  attention_step(qg.data(), k.data(), v.data(), ly.q_norm.data(), ly.k_norm.data(), m.eps, nh, nkv, hd, m.rd,
+                 m.rope_cos.data() + (size_t)pos * half, m.rope_sin.data() + (size_t)pos * half, ly.kc.data(),
+                 ly.vc.data(), pos, o.data());
   ly.wo.gemv(o.data(), out);
 }
 
@@ -786,6 +798,15 @@ int orc_gemv(int type, const uint8_t* W, const float* x, float* y, int inner, in
 void orc_flash_attention(float* out, const float* q, const float* ck, const float* cv, int kvh, int seq_len,
                          float scale, int hd, int nkv) {
   flash_attention(out, q, ck, cv, kvh, seq_len, scale, hd, nkv);
+}
+// one gated attention step (attention_step above) at position pos; the RoPE
+// row of pos is built from theta as build_rope does
+void orc_attention_step(const float* qg, const float* k, const float* v, const float* q_norm, const float* k_norm,
+                        float eps, int nh, int nkv, int hd, int rd, float theta, float* kc, float* vc, int pos,
+                        float* out) {
+  std::vector<float> c(rd / 2), s(rd / 2);
+  rope_row(theta, rd, pos, c.data(), s.data());
+  attention_step(qg, k, v, q_norm, k_norm, eps, nh, nkv, hd, rd, c.data(), s.data(), kc, vc, pos, out);
 }
 void orc_standard_attention(float* out, const float* q, const float* ck, const float* cv, int kvh, int seq_len,
                             float scale, int hd, int nkv) {

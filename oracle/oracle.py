@@ -36,6 +36,7 @@ def lib():
         L.orc_gemv.argtypes = [i, p, p, p, i, i, i]
         L.orc_flash_attention.argtypes = [p, p, p, p, i, i, C.c_float, i, i]
         L.orc_standard_attention.argtypes = [p, p, p, p, i, i, C.c_float, i, i]
+        L.orc_attention_step.argtypes = [p, p, p, p, p, C.c_float, i, i, i, i, C.c_float, p, p, i, p]
         L.orc_quantize_row_q8_K.argtypes = [p, p, i64]
         L.orc_vec_dot_q8k.argtypes = [i, p, p, i]
         L.orc_vec_dot_q8k.restype = C.c_float
@@ -112,6 +113,18 @@ def flash_attention(q, ck, cv, kvh, seq_len, scale, hd, nkv, standard=False):
     out = np.empty(hd, np.float32)
     f = lib().orc_standard_attention if standard else lib().orc_flash_attention
     f(_ptr(out), _ptr(q), _ptr(ck), _ptr(cv), kvh, seq_len, scale, hd, nkv)
+    return out
+
+
+def attention_step(qg, k, v, q_norm, k_norm, eps, nh, nkv, hd, rd, theta, kc, vc, pos):
+    """One gated attention step after the projections (src/ModelCPU.jl:766-851):
+    qg [nh][2*hd], k/v [nkv][hd]; kc/vc [ctx][nkv][hd] are updated at pos.
+    Returns the gated output [nh*hd]."""
+    out = np.empty(nh * hd, np.float32)
+    args = [np.ascontiguousarray(a, dtype=np.float32) for a in (qg, k, v, q_norm, k_norm)]
+    assert kc.dtype == np.float32 and kc.flags.c_contiguous and vc.dtype == np.float32 and vc.flags.c_contiguous
+    lib().orc_attention_step(*[_ptr(a) for a in args], eps, nh, nkv, hd, rd, theta, _ptr(kc), _ptr(vc), pos,
+                             _ptr(out))
     return out
 
 

@@ -4,11 +4,12 @@ import numpy as np
 
 import oracle as O
 
-_BB = {12: 144, 13: 176, 14: 210, 8: 34}
+_BB = {12: 144, 13: 176, 14: 210, 8: 34, 16: 66}
 
 
 def random_blocks(rng, ggml_type, nb):
-    """Raw weight blocks with arbitrary quant bytes and finite fp16 scales."""
+    """Raw weight blocks with arbitrary quant bytes and finite fp16 scales
+    (IQ2_XXS: any grid / sign index byte is valid, d is the leading fp16)."""
     bb = _BB[ggml_type]
     a = rng.integers(0, 256, (nb, bb), dtype=np.uint8)
     halves = (rng.standard_normal((nb, 2)) * 0.01).astype(np.float16).view(np.uint8).reshape(nb, 4)

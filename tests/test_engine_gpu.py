@@ -105,19 +105,45 @@ def test_errors_are_reported(tiny):
         Model(spec, bad)                            # layer 0 becomes attention without its tensors
 
 
-@pytest.mark.skipif(os.environ.get("INFERNO_SKIP_08B") == "1", reason="config-1 test disabled")
-def test_config1_greedy_identity():
-    """Config 1 (0.8B-shaped hybrid): 32-token prompt, 64 greedy tokens
-    identical to the oracle's (north_star asks >= 64)."""
+@pytest.fixture(scope="module")
+def config1():
+    if os.environ.get("INFERNO_SKIP_08B") == "1":
+        pytest.skip("config-1 tests disabled")
     spec = S.CONFIGS["qwen35-0.8b"]
     T = S.make_model(spec, seed=0)
+    return spec, T, O.OracleModel(spec, T)
+
+
+def test_config1_greedy_identity(config1):
+    """Config 1 (0.8B-shaped hybrid): 32-token prompt, 64 greedy tokens
+    identical to the oracle's (north_star asks >= 64)."""
+    spec, T, orc = config1
     prompt = S.tokens(0, 32, spec.vocab)
     m = Model(spec, T, max_ctx=512)
     got = m.generate(prompt, 64)
     m.close()
-    orc = O.OracleModel(spec, T)
     want = orc.generate(prompt, 64)
     assert got == want
+
+
+def test_config1_per_layer_hidden(config1, monkeypatch):
+    """Config 1: hidden state after every one of the 24 layers for the last
+    of the 32 prompt tokens, and its logits, within rel 2e-3 of the oracle
+    (north_star's per-layer bound; fp32 activations, exact-integer tensor-core
+    dots)."""
+    spec, T, orc = config1
+    monkeypatch.setenv("INFERNO_B200_DUMP", "1")
+    prompt = S.tokens(0, 32, spec.vocab)
+    m = Model(spec, T, max_ctx=512)
+    m.reset()
+    am_g, lg_g = m.forward(prompt, 0)
+    orc.reset()
+    am_o, lg_o = orc.forward(prompt, 0)
+    worst = max(rel(m.hidden(i), orc.hidden(i)) for i in range(spec.layers))
+    m.close()
+    assert worst < LAYER_RTOL, worst
+    assert rel(lg_g, lg_o) < LOGIT_RTOL
+    assert am_g == am_o
 
 
 def test_q6k_regrouping_is_bitwise_neutral(tiny, monkeypatch):

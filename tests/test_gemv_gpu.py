@@ -75,6 +75,48 @@ def test_gemv_parity(t, shape, batch):
     assert _rel(got, ref) < GEMV_RTOL, _rel(got, ref)
 
 
+# BASELINE config-2 shapes (out x in): the large ones, every type, batch 1 /
+# 4 / 16 (and 128 on 12288x4096).  Weights are seeded random GGUF blocks
+# (arbitrary quant bytes, finite fp16 scales): quantizing a 254M-element
+# matrix to IQ2_XXS in numpy takes minutes, and the GEMV's parity does not
+# depend on where the block bytes came from.  Reference: the oracle's
+# Dequant.jl dequantization followed by an fp32 matmul.
+CONFIG2_BIG = [(12288, 4096), (4096, 12288), (248320, 1024)]
+_BIG_CACHE = {}
+
+
+def _big_matrix(t, rows, inner):
+    key = (t, rows, inner)
+    if key not in _BIG_CACHE:
+        from q8k_cases import random_blocks
+        _BIG_CACHE.clear()
+        qk, bb = S.BLOCK[t]
+        nb = rows * inner // qk
+        rng = np.random.default_rng(1000 + 7 * t + rows)
+        _BIG_CACHE[key] = random_blocks(rng, t, nb).reshape(rows, inner // qk * bb)
+    return _BIG_CACHE[key]
+
+
+@pytest.mark.parametrize("batch", [1, 4, 16, 128])
+@pytest.mark.parametrize("shape", CONFIG2_BIG, ids=[f"{o}x{i}" for o, i in CONFIG2_BIG])
+@pytest.mark.parametrize("t", TYPES[:5], ids=[S.TYPE_NAME[t] for t in TYPES[:5]])
+def test_gemv_parity_config2(t, shape, batch):
+    rows, inner = shape
+    if batch == 128 and shape != (12288, 4096):
+        pytest.skip("batch 128 runs on the 12288x4096 shape only")
+    q = _big_matrix(t, rows, inner)
+    x = np.random.default_rng(50 + batch).standard_normal((batch, inner)).astype(np.float32)
+    ref = O.gemv(t, q, x, inner, rows)
+    dW, dx = _dev(q), _dev(x)
+    dy = _dev(np.full((batch, rows), np.nan, np.float32))
+    call("inferno_gemv", t, C.c_void_p(dW.data_ptr()), C.c_void_p(dx.data_ptr()), C.c_void_p(dy.data_ptr()),
+         inner, rows, batch, _stream())
+    _sync()
+    got = dy.cpu().numpy()
+    for v in range(batch):
+        assert _rel(got[v], ref[v]) < GEMV_RTOL, (v, _rel(got[v], ref[v]))
+
+
 @pytest.mark.parametrize("force_r", [1, 2, 4])
 def test_gemv_rows_per_warp(force_r):
     rows, inner, t = 777, 2048, S.Q4_K

@@ -2,6 +2,7 @@
 reference's known-answer tests, against gguf-py golden vectors, and against an
 independent numpy restatement of the forward pass."""
 import math
+import os
 from pathlib import Path
 
 import numpy as np
@@ -11,7 +12,10 @@ import oracle as O
 from inferno_b200 import synth as S
 
 GOLDEN = Path(__file__).resolve().parent / "golden" / "dequant_golden.npz"
-REF_QUANTSDATA = Path("/root/reference/src/QuantsData.jl")
+# the reference source tree (INFERNO_REFERENCE_ROOT, else a checkout beside
+# this repository); tests that read it skip when it is absent
+REF_ROOT = Path(os.environ.get("INFERNO_REFERENCE_ROOT", Path(__file__).resolve().parents[2] / "reference"))
+REF_QUANTSDATA = REF_ROOT / "src" / "QuantsData.jl"
 
 
 # ---- tests/unit/core_components.jl:114-122 (IQ2_XXS known answers) --------
