@@ -186,27 +186,87 @@ def run_reference(args):
             pos += 1
         return tok, pos
 
+    # the workload's schedule: the 32-token prompt (untimed), then greedy
+    # decode from position 32; a step decodes `per_step` tokens, continuing
+    # the same sequence (positions stay inside the 32..159 window for the
+    # default --steps / --warmup; later steps wrap back to the prompt state)
     m.reset()
-    tok, _ = m.forward(prompt[:4], 0, want_logits=False)
-    pos = 4
+    tok, _ = m.forward(prompt, 0, want_logits=False)
+    pos = PROMPT
+    snap = (tok, pos)
     for _ in range(args.warmup):
         tok, pos = step(tok, pos)
-    t0 = time.perf_counter()
+    dt = 0.0
     for _ in range(args.steps):
+        if pos + per_step > PROMPT + NDEC:
+            # window exhausted: replay the post-prompt state (untimed)
+            m.reset()
+            tok, _ = m.forward(prompt, 0, want_logits=False)
+            pos = PROMPT
+        t0 = time.perf_counter()
         tok, pos = step(tok, pos)
-    dt = time.perf_counter() - t0
+        dt += time.perf_counter() - t0
     v = per_step * args.steps / dt
     line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt * 1000 / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
             "config": dict(CONFIG, parallelism="host CPU"), "impl": "reference",
             "cpu_baseline": {"value": v, "unit": UNIT, "cores": O.cpu_count(), "kind": "port",
-                             "sample": f"{per_step} greedy decode tokens per step from position 4 on, "
-                                       "F32 dequantized weights, all host threads (the reference's "
-                                       "default load_model_cpu path, restated)"},
+                             "sample": f"{per_step} greedy decode tokens per step after the {PROMPT}-token "
+                                       f"prompt (positions {PROMPT}..{PROMPT + NDEC - 1}), F32 dequantized "
+                                       "weights, all host threads (the reference's default load_model_cpu "
+                                       "path, restated)"},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
+
+
+# Kernel classes of the per-token graph, with the INFERNO_B200_ABLATE bits
+# that leave them out: the marginal device time of a class inside the
+# PDL-chained graph is (token time) - (token time without the class).
+# Ablated runs compute garbage; only their timing is used.
+GRAPH_CLASSES = {"q4k_gemv": 1 | 8 | 16, "q6k_ffn_down": 32, "gdn": 2, "attention": 4, "lm_head": 64}
+
+
+def q4k_launch_bytes(spec, T):
+    """Algorithmic bytes of the config-1 Q4_K per-layer GEMVs of one token:
+    weights once plus fp32 input and output vectors, and their launch count."""
+    tot, n = 0, 0
+    for i in range(spec.layers):
+        p = f"blk.{i}."
+        groups = ([["attn_qkv.weight", "attn_gate.weight"], ["ssm_out.weight"]] if p + "ssm_a" in T else
+                  [["attn_q.weight", "attn_k.weight", "attn_v.weight"], ["attn_output.weight"]])
+        groups.append(["ffn_gate.weight", "ffn_up.weight"])
+        for g in groups:
+            ts = [T[p + nm] for nm in g]
+            assert all(t.ggml_type == 12 for t in ts), g
+            inner, rows = int(ts[0].ne[0]), sum(int(t.ne[1]) for t in ts)
+            if g[0] == "ffn_gate.weight":
+                rows //= 2            # SwiGLU writes one vector of the two products
+            tot += sum(t.nbytes for t in ts) + 4 * (inner + rows)
+            n += 1
+    return tot, n
+
+
+def graph_class_times(spec, T, prompt, tok0, device, base_ms, reps=3):
+    """Per-token marginal device time (ms) of each kernel class in the graph."""
+    from inferno_b200.model import Model
+    out = {}
+    for name, bits in GRAPH_CLASSES.items():
+        os.environ["INFERNO_B200_ABLATE"] = str(bits)
+        try:
+            m = Model(spec, T, device=device, max_ctx=CTX)
+        finally:
+            del os.environ["INFERNO_B200_ABLATE"]
+        m.reset()
+        best = 1e30
+        for _ in range(reps + 1):
+            m.reset()
+            m.decode_greedy(tok0, PROMPT, NDEC)
+            best = min(best, m.last_decode_ms())
+        m.close()
+        out[name] = (base_ms - best) / NDEC
+    return out
 
 
 def run_ours(args):
@@ -286,13 +346,6 @@ def run_ours(args):
     t3 = time.perf_counter()
     e2e["breakdown_ms"] = {"reset": 1e3 * (t1 - t0), "prefill": 1e3 * (t2 - t1), "decode": 1e3 * (t3 - t2)}
 
-    # ---- roofline: dominant kernel (lm_head Q6_K GEMV + argmax), profiled
-    # live on the engine stream with CUDA events (eager pass, same inputs) ----
-    m.restore_device()
-    prof = m.profile(tok0, PROMPT, 16)
-    lm_ms, lm_n = prof["lm_head"]
-    lm_bytes = T["token_embd.weight"].nbytes + spec.hidden * 4 * 2
-    achieved = lm_bytes / (lm_ms / lm_n / 1000.0) / 1e9
     peaks = {}
     try:
         peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
@@ -300,32 +353,63 @@ def run_ours(args):
         pass
     peak = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    pos_mid = PROMPT + NDEC // 2
-    tok_bytes = algorithmic_bytes_per_token(spec, T, pos_mid)
-    tok_gbs = tok_bytes / (ms_step / NDEC / 1000.0) / 1e9 if ws == 1 else tok_bytes / (ms_step / NDEC / 1000.0) / 1e9
+
+    # ---- where the token goes inside the graph: marginal device time of each
+    # kernel class (ablation, CUDA events around the same graph replays) ----
+    tok_ms = ms_step / NDEC
+    graph_ms = graph_class_times(spec, T, prompt, tok0, local, ms_step)
+    # dominant class: the 72 Q4_K per-layer tensor-core GEMVs of a token
+    q4_bytes, q4_n = q4k_launch_bytes(spec, T)
+    q4_ms = graph_ms["q4k_gemv"] / q4_n
+    q4_achieved = q4_bytes / q4_n / (q4_ms / 1000.0) / 1e9
     traffic = None
     try:
-        # DRAM bytes of one lm_head launch from the committed ncu summary
-        for ln in (ROOT / "profiles" / "lm_head_q6k_248320x1024.md").read_text().splitlines():
+        for ln in (ROOT / "profiles" / "gemv_q4k_6144x1024.md").read_text().splitlines():
             if ln.startswith("dram_bytes_per_launch:"):
                 traffic = int(ln.split(":")[1].strip())
     except Exception:
         pass
-    total_prof_ms = sum(v[0] for v in prof.values())
+
+    # ---- lm_head (Q6_K 248320x1024 GEMV + argmax) alone, live on the engine
+    # stream with CUDA events (eager pass, same inputs) ----
+    m.restore_device()
+    prof = m.profile(tok0, PROMPT, 16)
+    lm_ms, lm_n = prof["lm_head"]
+    lm_bytes = T["token_embd.weight"].nbytes + spec.hidden * 4 * 2
+    achieved = lm_bytes / (lm_ms / lm_n / 1000.0) / 1e9
+    pos_mid = PROMPT + NDEC // 2
+    tok_bytes = algorithmic_bytes_per_token(spec, T, pos_mid)
+    tok_gbs = tok_bytes / (ms_step / NDEC / 1000.0) / 1e9
+    lm_traffic = None
+    try:
+        # DRAM bytes of one lm_head launch from the committed ncu summary
+        for ln in (ROOT / "profiles" / "lm_head_q6k_248320x1024.md").read_text().splitlines():
+            if ln.startswith("dram_bytes_per_launch:"):
+                lm_traffic = int(ln.split(":")[1].strip())
+    except Exception:
+        pass
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32 (fp32 activations, Q4_K/Q6_K weights)",
             "data": "synthetic (seeded N(0,0.02) weights quantized to GGUF blocks; seeded token ids)",
             "config": CONFIG, "clocks": clk, "e2e": e2e,
             "gpu_launches": m.kernels_per_token() * NDEC,
-            "roofline": {"bound": "hbm", "kernel": "lm_head Q6_K 248320x1024 GEMV + argmax",
-                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "roofline": {"bound": "hbm", "kernel": "Q4_K per-layer tensor-core GEMV (gemv_mma_kernel<12>), "
+                                                  f"{q4_n} launches per token",
+                         "achieved": q4_achieved, "peak": peak, "unit": "GB/s", "frac": q4_achieved / peak,
                          "peak_source": peak_src, "traffic": traffic,
-                         "algorithmic_bytes_per_launch": lm_bytes,
-                         "launch_ms": lm_ms / lm_n},
+                         "algorithmic_bytes_per_launch": q4_bytes / q4_n, "launch_ms": q4_ms,
+                         "timing": "marginal in-graph device time per launch: token time with and without "
+                                   "the class (CUDA events around the same graph replays), / launches"},
+            "lm_head_roofline": {"bound": "hbm", "kernel": "lm_head Q6_K 248320x1024 GEMV + argmax",
+                                 "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                                 "traffic": lm_traffic, "algorithmic_bytes_per_launch": lm_bytes,
+                                 "launch_ms": lm_ms / lm_n, "timing": "CUDA events around the launch (eager)"},
             "token_roofline": {"algorithmic_bytes_per_token": tok_bytes, "achieved_gbs": tok_gbs,
                                "frac": tok_gbs / peak, "peak": peak},
-            "kernel_time_share": {k: round(v[0] / total_prof_ms, 4) for k, v in prof.items()},
+            "kernel_time_share": {k: round(v / tok_ms, 4) for k, v in graph_ms.items()},
+            "kernel_time_share_note": "marginal in-graph time of each class / token time (ablation); the rest "
+                                      "is embedding, finalize and the dependency chain between kernels",
             "wall_s": wall}
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(spec, T)

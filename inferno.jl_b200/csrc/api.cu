@@ -376,7 +376,8 @@ extern "C" int inferno_debug_xch_timeout(int spin_limit, int* device_error_out) 
     return set_error(INFERNO_EINVAL, "debug_xch_timeout: spin_limit must be in [1, 2^22]");
   constexpr int H = 1024, ROWS = 64, NR = 2;
   const size_t wbytes = (size_t)ROWS * (H / 256) * 144;
-  const size_t bytes = wbytes + 4 * H * 3 + 8 * (size_t)2 * NR * H + 256 * 4;
+  // [W][x][norm w][y][partials 2 x NR x H words][seq 8 words][x_next][error word]
+  const size_t bytes = wbytes + 4 * H * 3 + 8 * (size_t)2 * NR * H + 8 * 8 + 4 * H + 256;
   uint8_t* buf = nullptr;
   INF_CUDA_TRY(cudaMalloc(&buf, bytes));
   cudaError_t e = cudaMemset(buf, 0, bytes);   // Q4_K blocks with d = dmin = 0, x = 0, tags 0

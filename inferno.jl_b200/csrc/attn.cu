@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
     p.vc[off] = vnew[d];
   }
 
+  if (d == 0) KT_LAST(p.trace, 4);
   // ---------------- online softmax over 32-key chunks ----------------
   const float scale = 1.0f / sqrtf((float)ATT_HD);
   const int kk = d >> 3, part = d & 7;
@@ -165,6 +166,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
     }
     m = mn;
   }
+  if (d == 0) KT_LAST(p.trace, 5);
   p.part_o[((long long)h * p.nsplit + s) * ATT_HD + d] = o;
   if (d == 0) {
     p.part_ml[((long long)h * p.nsplit + s) * 2 + 0] = m;

@@ -45,9 +45,13 @@ struct Ctl {                 // device-resident step control
 };
 
 __global__ void finalize_kernel(Ctl* c, const int* prompt, int* out, int max_out, unsigned long long* xch_seq,
-                                int xch_nsync) {
+                                int xch_nsync, int* steps, int nsteps) {
   pdl_wait();
   pdl_trigger();
+  // the Gated DeltaNet layers' step counters (their kernels ran with
+  // self_advance = 0 in this token)
+  for (int i = threadIdx.x; i < nsteps; i += blockDim.x) steps[i] += 1;
+  if (threadIdx.x) return;
   if (xch_seq) *xch_seq += (unsigned long long)xch_nsync;   // sequence base of the next token's sync points
   const unsigned long long key = c->argkey;
   const int am = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull));
@@ -161,6 +165,12 @@ struct InfernoEngine {
   const inf::SampleArgs* sampling = nullptr;
   uint8_t* seen = nullptr;
   unsigned long long* trace = nullptr;   // debug: per-launch timeline slots (INFERNO_B200_TRACE)
+  // Gated DeltaNet step counters of every layer, contiguous; while a decode
+  // token is enqueued (in_token) the GDN kernels leave them to the token's
+  // finalize kernel (token_steps; off when a fused in_proj + GDN layer
+  // advances its own)
+  int* gdn_steps = nullptr;
+  bool in_token = false, token_steps = false;
   int trace_idx = 0;
   int launches = 0;              // kernels enqueued since the last enqueue_token began
   int token_launches = 0;        // kernels of one decode token (set by enqueue_token)
@@ -440,6 +450,7 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     g.step = L.step;
     g.done = L.done;
     g.trace = trace_slot(e);
+    g.self_advance = (e->in_token && e->token_steps) ? 0 : 1;
     if (!(ab & 2) && (rc = launch_gdn_step(g, e->st, pdl))) return rc;
     mark(e, K_GDN);
     if (!(ab & 8) && (rc = gemv(e, L.ssm_out->type, e->di, {M(L.ssm_out, e->x)}, e->y, (ab & 128) ? PRO_NONE : PRO_HEADNORM_GATE,
@@ -649,7 +660,9 @@ int launch_finalize(InfernoEngine* e, bool pdl) {
   cfg.attrs = at;
   cfg.numAttrs = pdl ? 1 : 0;
   cudaError_t r = cudaLaunchKernelEx(&cfg, finalize_kernel, e->ctl, (const int*)e->prompt, e->out_tokens, e->max_out,
-                                     e->xch ? e->xch_seq : (unsigned long long*)nullptr, e->xch_k);
+                                     e->xch ? e->xch_seq : (unsigned long long*)nullptr, e->xch_k,
+                                     e->token_steps ? e->gdn_steps : (int*)nullptr,
+                                     e->token_steps ? e->cfg.num_layers : 0);
   if (r != cudaSuccess) return set_error(INFERNO_ECUDA, "finalize launch: %s", cudaGetErrorString(r));
   mark(e, K_FINAL);
   return 0;
@@ -663,6 +676,11 @@ int enqueue_token(InfernoEngine* e, bool write_logits, bool pdl) {
   e->xch_pending = -1;
   e->launches = 0;
   e->trace_idx = 0;
+  e->in_token = true;
+  struct InTokenReset {
+    InfernoEngine* e;
+    ~InTokenReset() { e->in_token = false; }
+  } in_token_reset{e};
   if (e->profiling) mark(e, -1), --e->launches;
   if ((rc = launch_embed_row(e->embd->type, e->embd->d, (long long)e->embd->bytes / e->embd->rows(), c.hidden_size,
                              &e->ctl->tok, e->x, c.vocab_size, e->st, pdl)))
@@ -1066,9 +1084,10 @@ int inferno_engine_finalize(InfernoEngine* e) {
           L.ssm_norm->ne[0] != c.ssm_dv)
         return set_error(INFERNO_EINVAL, "layer %d: GDN tensor dims do not match the config", i);
       if ((rc = dalloc(e, &L.ring, (size_t)c.ssm_conv_kernel * e->C, true)) ||
-          (rc = dalloc(e, &L.S, (size_t)c.ssm_nv * c.ssm_dv * c.ssm_dk, true)) || (rc = dalloc(e, &L.step, 4, true)) ||
-          (rc = dalloc(e, &L.done, 4)))
+          (rc = dalloc(e, &L.S, (size_t)c.ssm_nv * c.ssm_dv * c.ssm_dk, true)) || (rc = dalloc(e, &L.done, 4)))
         return rc;
+      if (!e->gdn_steps && (rc = dalloc(e, &e->gdn_steps, (size_t)c.num_layers, true))) return rc;
+      L.step = e->gdn_steps + i;
     } else {
       any_attn = true;
       if ((rc = require(e, p + "attn_q.weight", &L.wq)) || (rc = require(e, p + "attn_k.weight", &L.wk)) ||
@@ -1171,6 +1190,11 @@ int inferno_engine_finalize(InfernoEngine* e) {
       }
     }
   }
+  // the decode token's finalize kernel advances the GDN step counters unless a
+  // fused in_proj + GDN layer advances its own
+  e->token_steps = e->gdn_steps != nullptr;
+  for (auto& L : e->layers)
+    if (L.wperm) e->token_steps = false;
   e->xcur = e->x;
   if (e->tp && (rc = setup_xch(e))) return rc;
   {

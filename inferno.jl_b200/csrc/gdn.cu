@@ -171,6 +171,7 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(const __grid_cons
   if (tid < GDN_ROWS) p.ring[(long long)cur * C + cv] = nv_;
 
   block_sum_n<3>(acc3, red);
+  if (tid == 0) KT_LAST(p.trace, 4);
   const float scale = 1.0f / sqrtf(acc3[0] / (float)H + p.eps);
   const float alpha = acc3[1] * scale, beta_raw = acc3[2] * scale;
   // gates in Float64 (src/ModelCPU.jl:618-636), one thread, overlapped with
@@ -194,6 +195,7 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(const __grid_cons
   qn[tid] = qv * qnv;
   kn[tid] = kv * knv;
   __syncthreads();
+  if (tid == 0) KT_LAST(p.trace, 5);
   const float dec = gate_s[0], bg = gate_s[1];
 
   // ---------------- delta rule ----------------
@@ -213,7 +215,12 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(const __grid_cons
   }
 
   // ---------------- advance the layer's step counter ----------------
+  if (!p.self_advance) {
+    if (tid == 0) KT_LAST(p.trace, 6);
+    return;
+  }
   __syncthreads();
+  if (tid == 0) KT_LAST(p.trace, 7);
   if (tid == 0) {
     __threadfence();
     const int total = gridDim.x * gridDim.y;

@@ -412,6 +412,10 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
     const int rc = plan_launch_mma(c, dev, sms, st, pdl);
     if (rc <= 0) return rc;
   }
+  if (c.nb >= 16) {   // many columns: the tensor-core GEMM (qgemm_tc.cu)
+    const int rc = qgemm_from_gemv(c, st);
+    if (rc <= 0) return rc;
+  }
   static const bool no_mma_batch = getenv("INFERNO_GEMV_NO_MMA_BATCH") != nullptr;
   if (!no_mma && !no_mma_batch && !c.force_r && c.nb > 1 && c.nxv == 1 && (c.type == T_Q4_K || c.type == T_Q6_K) &&
       c.inner % 256 == 0) {

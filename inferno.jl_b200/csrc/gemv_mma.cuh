@@ -299,11 +299,28 @@ __device__ float gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, 
 // fp32 staging pass is needed; the sub-blocks (32 elements for Q4_K, 16 for
 // Q6_K) are 8 / 4 consecutive lanes, summed with shuffles.  Same outputs as
 // gemv_mma_prologue.
+template <int NW>
+constexpr int mma_pro_items() { return 8192 / 4 / (NW * 32); }   // float4 items per thread (n <= 8192)
+
+// RMSNorm weights of the register prologue: constants, so they are loaded
+// before griddepcontrol.wait (their L2 round trip overlaps the previous kernel)
+template <int NW>
+__device__ __forceinline__ void gemv_mma_prologue_weights(const GemvParams& p, int tid,
+                                                          float4 (&w4)[mma_pro_items<NW>()]) {
+  constexpr int NT = NW * 32, IT = mma_pro_items<NW>();
+  const int nf4 = p.inner >> 2;
+#pragma unroll
+  for (int j = 0; j < IT; ++j) {
+    const int u = tid + j * NT;
+    w4[j] = (p.pro == PRO_RMSNORM && u < nf4) ? ((const float4*)p.pro_w)[u] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
 template <int TYPE, int NW, int MODE>
 __device__ float gemv_mma_prologue_reg(const GemvParams& p, uint8_t* xq, float* xsum, float* red, float* vmax,
-                                       int tid) {
+                                       int tid, const float4 (&wpre)[mma_pro_items<NW>()]) {
   constexpr int NT = NW * 32;
-  constexpr int IT = 8192 / 4 / NT;          // float4 items per thread (n <= 8192)
+  constexpr int IT = mma_pro_items<NW>();
   const int n = p.inner, nf4 = n >> 2;
   const int lane = tid & 31, w = tid >> 5;
   const bool rms = p.pro == PRO_RMSNORM;
@@ -359,11 +376,12 @@ __device__ float gemv_mma_prologue_reg(const GemvParams& p, uint8_t* xq, float* 
     if (xch && blockIdx.x == 0) ((float4*)p.x_next)[u] = v[j];
     if (rms) {
       ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
-      const float4 w4 = ((const float4*)p.pro_w)[u];
+      const float4 w4 = wpre[j];
       v[j].x *= w4.x; v[j].y *= w4.y; v[j].z *= w4.z; v[j].w *= w4.w;
     }
     amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
   }
+  if (tid == 0) KT_LAST(p.trace, 7);
   ss = warp_sum(ss);
   amax = warp_max(amax);
   if (lane == 0) {
@@ -642,14 +660,16 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
     return;
   }
 
+  const bool reg_pro = MODE != MMA_MOE && (p.pro == PRO_RMSNORM || p.pro == PRO_NONE);
+  float4 wpre[mma_pro_items<NW>()];
+  if (reg_pro) gemv_mma_prologue_weights<NW>(p, tid, wpre);
   pdl_wait();
   if (tid == 0) {
     KT_FIRST(p.trace, 2);
     KT_LAST(p.trace, 3);
   }
-  const bool reg_pro = MODE != MMA_MOE && (p.pro == PRO_RMSNORM || p.pro == PRO_NONE);
   const float colscale = reg_pro ? gemv_mma_prologue_reg<TYPE == T_Q6_KR ? T_Q6_K : TYPE, NW, MODE>(p, xq, xsum, red,
-                                                                                                     vmax, tid)
+                                                                                                     vmax, tid, wpre)
                                  : gemv_mma_prologue<TYPE, NW, MODE>(p, xf, xq, xsum, red, vmax, tid);
   if (tid == 0) KT_LAST(p.trace, 4);
   const bool nonfinite = *(volatile int*)&red[2 * NW] != 0;

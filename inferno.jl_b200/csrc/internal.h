@@ -1,6 +1,7 @@
 // Host-side internal declarations shared by the engine's translation units.
 #pragma once
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 #include <mutex>
 #include <string>
@@ -91,6 +92,41 @@ struct GemvCall {
 };
 
 int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl);
+
+// Tensor-core quantized GEMM (qgemm_tc.cu) for T >= 16 token columns:
+// y[t][r] = sum_k W[r][k] x[t][k].  The activations come as fp16 hi / lo rows
+// [T][K] with a per-token power-of-two exponent (launch_qgemm_act), the
+// weight scale from a bound of |w| (launch_qgemm_wbound).
+struct QgemmCall {
+  int type = 0;
+  int K = 0;
+  GemvMat mats[4];
+  int nmats = 0;
+  int T = 0;
+  const void* xhi = nullptr;   // __half [T][K]
+  const void* xlo = nullptr;   // __half [T][K] (split)
+  const float* xexp = nullptr; // [T]
+  long long y_stride = 0;
+  int epi = 0;                 // 0 store, 1 add, 2 SwiGLU (mats[0] gate, mats[1] up -> mats[0].y)
+  const float* wbound = nullptr;
+  int* err = nullptr;
+  bool split = true;           // hi/lo fp16 operand pairs (three MMAs) for fp32-level results
+};
+bool qgemm_supported(int type);
+// token tile of the GEMM for T columns, and T rounded up to whole tiles (the
+// activation buffers hold that many rows)
+int qgemm_bn(int T);
+int qgemm_rows_padded(int T);
+int launch_qgemm(const QgemmCall& c, cudaStream_t st, bool pdl);
+int launch_qgemm_act(const float* x, long long x_stride, int K, int T, int pro, const float* pro_w,
+                     const float* pro_z, int group, float eps, __half* xhi, __half* xlo, float* xexp,
+                     cudaStream_t st, bool pdl);
+// bound of |w| over a matrix into *out (reset: start from 0, else fold in with max)
+int launch_qgemm_wbound(int type, const void* W, long long rows, int K, float* out, cudaStream_t st, bool reset);
+// a batched GemvCall (nb >= 16, store / add epilogue, plain or RMSNorm input)
+// on the tensor-core GEMM with stream-ordered scratch; returns 1 when the
+// call does not fit that path
+int qgemm_from_gemv(const GemvCall& c, cudaStream_t st);
 // Q6_K -> the engine-internal 16-row-group layout T_Q6_KR (same byte count)
 int launch_repack_q6k(const void* src, void* dst, int rows, int inner, cudaStream_t st);
 int launch_dequant(int type, const void* src, long long n, float* dst, cudaStream_t st);

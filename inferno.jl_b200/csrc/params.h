@@ -21,6 +21,9 @@ struct GdnParams {
   float* y;                // [nv*dv] pre-norm output
   int* step;               // per-layer step counter
   int* done;               // per-layer CTA completion counter
+  // 1: the last CTA advances *step (via `done`); 0: the caller advances it
+  // after the kernel (the decode token's finalize kernel does it for every layer)
+  int self_advance = 1;
   unsigned long long* trace = nullptr;   // debug timeline slots (KT_*, common.cuh)
 };
 

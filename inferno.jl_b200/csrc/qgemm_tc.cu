@@ -1,0 +1,748 @@
+// Quantized GEMM on the 5th-generation tensor cores (tcgen05), for the
+// batched / prefill products Y[t][r] = sum_k W[r][k] * X[t][k] with T >= 16
+// token columns: the prompt loop of forward_cpu! (Inferno.jl
+// src/ModelCPU.jl:970-986, every mul! of src/ModelCPU.jl:435-444 run for many
+// tokens at once) and the config-2 batched GEMM.
+//
+// Per CTA: a 128-row tile of W (one matrix segment; for the SwiGLU pair 64
+// gate + 64 up rows) against a BN-token tile of X, K walked in steps of 64.
+//   warp 0      producer: raw GGUF super-blocks of the 128 rows by 1-D bulk
+//               copies (cp.async.bulk, aligned supersets for rows that do not
+//               start on 16 bytes), and the fp16 activation tiles by 2-D TMA
+//               (cp.async.bulk.tensor, SWIZZLE_128B, zero fill past T);
+//   warp 1      allocates the TMEM accumulator (BN fp32 columns x 128 lanes)
+//               and issues tcgen05.mma from one thread;
+//   warps 2-5   dequantize: thread = weight row, 64 weights per K step with
+//               the fp32 arithmetic of Dequant.jl, written as fp16 into the
+//               canonical K-major SWIZZLE_128B operand tile; afterwards they
+//               drain the accumulator with tcgen05.ld and apply the epilogue.
+// Rings: raw super-blocks (2), dequantized A tiles (2), activation tiles
+// (NBS); every hand-off is an mbarrier, MMA completion is signalled with
+// tcgen05.commit.  All waits are bounded and report DERR_MBAR_TIMEOUT.
+//
+// Precision: with `split` the fp32 weight w and activation x are carried as
+// fp16 pairs (hi = fp16(w), lo = fp16(w - hi)) and the product is
+// hi*hi + hi*lo + lo*hi (three MMAs, about 22 significant bits: the fp32
+// GEMV's results to ~1e-6 relative); without it one fp16 MMA (11 bits).
+// Weights are scaled by a power of two per matrix and activations per token
+// (both undone in the epilogue) so that hi and lo stay normal fp16 numbers.
+#include <algorithm>
+#include <climits>
+#include <cstring>
+#include <mutex>
+#include "internal.h"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "tc.cuh"
+#include "../../include/inferno_b200.h"
+
+namespace inf {
+
+constexpr int QG_M = 128;             // weight rows per tile (TMEM lanes)
+constexpr int QG_BK = 64;             // K per step (one 128-byte fp16 row)
+constexpr int QG_THREADS = 192;       // 6 warps
+constexpr int QG_ATILE = QG_M * 128;  // bytes of one fp16 A tile (16 KB)
+
+struct QgSeg {
+  const uint8_t* W;
+  float* y;
+  int rows;
+  int mtile0;       // first M tile of this segment
+};
+
+struct QgParams {
+  QgSeg seg[4];
+  int nseg, n_mtiles;
+  int K, nsb;
+  long long row_bytes;
+  int slot;              // bytes per row of one raw stage
+  int T;
+  long long y_stride;    // floats between token rows of y
+  int epi;               // QG_STORE / QG_ADD / QG_SWIGLU
+  int nbs;               // activation ring stages
+  int split;
+  const float* xexp;     // [T] power-of-two exponent applied to each token's fp16 activations
+  const float* wbound;   // bound of |w| over the matrix (weight scale)
+  int* err;
+};
+enum { QG_STORE = 0, QG_ADD = 1, QG_SWIGLU = 2 };
+
+struct alignas(64) QgMaps {
+  CUtensorMap hi, lo;
+};
+
+template <int TYPE>
+struct QgBlk;
+template <>
+struct QgBlk<T_Q4_K> { static constexpr int BB = 144; };
+template <>
+struct QgBlk<T_Q5_K> { static constexpr int BB = 176; };
+template <>
+struct QgBlk<T_Q6_K> { static constexpr int BB = 210; };
+template <>
+struct QgBlk<T_Q8_0> { static constexpr int BB = 272; };   // 8 blocks of 34 bytes per 256 inputs
+
+__device__ __forceinline__ uint32_t ld_u32(const uint8_t* p) { return lds_u32_any(p); }
+
+// 6-bit scale / min j of a K-quant super-block (src/Dequant.jl:345-362)
+__device__ __forceinline__ void qg_kscale(const uint8_t* sc, int j, float& s, float& m) {
+  const uint32_t w0 = ld_u32(sc), w1 = ld_u32(sc + 4), w2 = ld_u32(sc + 8);
+  const uint8_t* b = nullptr;
+  (void)b;
+  uint32_t sj, mj;
+  if (j < 4) {
+    sj = (w0 >> (8 * j)) & 63;
+    mj = (w1 >> (8 * j)) & 63;
+  } else {
+    const int q = j - 4;
+    const uint32_t hi = (w2 >> (8 * q)) & 0xff;        // sc[j + 4]
+    sj = (hi & 0x0f) | (((w0 >> (8 * q + 6)) & 3) << 4);
+    mj = (hi >> 4) | (((w1 >> (8 * q + 6)) & 3) << 4);
+  }
+  s = (float)sj;
+  m = (float)mj;
+}
+
+// 64 fp32 weights of K step ks (0..3) of one super-block, with the
+// oracle's / Dequant.jl's rounding order.
+template <int TYPE>
+__device__ __forceinline__ void qg_dequant(const uint8_t* rp, int ks, float (&w)[64]) {
+  if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) {
+    const float d = h2f_bits((uint16_t)(ld_u32(rp) & 0xffff)), dmin = h2f_bits((uint16_t)(ld_u32(rp) >> 16));
+    float s1, m1, s2, m2;
+    qg_kscale(rp + 4, 2 * ks, s1, m1);
+    qg_kscale(rp + 4, 2 * ks + 1, s2, m2);
+    const float d1 = d * s1, mn1 = dmin * m1, d2 = d * s2, mn2 = dmin * m2;
+    const uint8_t* qs = rp + (TYPE == T_Q4_K ? 16 : 48) + 32 * ks;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint32_t v = ld_u32(qs + 4 * q);
+      uint32_t h = 0;
+      if constexpr (TYPE == T_Q5_K) h = ld_u32(rp + 16 + 4 * q);
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        uint32_t lo = (v >> (8 * b)) & 15, hi = (v >> (8 * b + 4)) & 15;
+        if constexpr (TYPE == T_Q5_K) {
+          const uint32_t hb = (h >> (8 * b)) & 0xff;
+          lo += ((hb >> (2 * ks)) & 1) << 4;
+          hi += ((hb >> (2 * ks + 1)) & 1) << 4;
+        }
+        w[4 * q + b] = d1 * (float)lo - mn1;
+        w[32 + 4 * q + b] = d2 * (float)hi - mn2;
+      }
+    }
+  } else if constexpr (TYPE == T_Q6_K) {
+    const int ns = ks >> 1, hi = ks & 1;
+    const uint8_t* L = rp + 64 * ns;
+    const uint8_t* Hh = rp + 128 + 32 * ns;
+    const int8_t* S = (const int8_t*)(rp + 192 + 8 * ns);
+    const float d = h2f_bits((uint16_t)(rp[208] | (rp[209] << 8)));
+    const float sa0 = d * (float)S[4 * hi + 0], sa1 = d * (float)S[4 * hi + 1];
+    const float sb0 = d * (float)S[4 * hi + 2], sb1 = d * (float)S[4 * hi + 3];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint32_t la = ld_u32(L + 4 * q), lb = ld_u32(L + 32 + 4 * q), hh = ld_u32(Hh + 4 * q);
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int l = 4 * q + b;
+        const uint32_t hv = (hh >> (8 * b)) & 0xff;
+        const uint32_t a = (la >> (8 * b)) & 0xff, bb = (lb >> (8 * b)) & 0xff;
+        int q1, q2;
+        if (hi == 0) {
+          q1 = (int)((a & 15) | ((hv & 3) << 4)) - 32;
+          q2 = (int)((bb & 15) | (((hv >> 2) & 3) << 4)) - 32;
+        } else {
+          q1 = (int)((a >> 4) | (((hv >> 4) & 3) << 4)) - 32;
+          q2 = (int)((bb >> 4) | (((hv >> 6) & 3) << 4)) - 32;
+        }
+        w[l] = (l < 16 ? sa0 : sa1) * (float)q1;
+        w[32 + l] = (l < 16 ? sb0 : sb1) * (float)q2;
+      }
+    }
+  } else {   // Q8_0: blocks 2ks, 2ks+1 of the eight 34-byte blocks
+#pragma unroll
+    for (int hb = 0; hb < 2; ++hb) {
+      const uint8_t* b = rp + 34 * (2 * ks + hb);
+      const float d = h2f_bits((uint16_t)(b[0] | (b[1] << 8)));
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint32_t v = ld_u32(b + 2 + 4 * q);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w[32 * hb + 4 * q + e] = d * (float)(int8_t)((v >> (8 * e)) & 0xff);
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ int qg_exp_for(float bound) {
+  // power of two that brings `bound` just under 2^14 (fp16 max is 65504)
+  if (!(bound > 0.f) || !(bound <= 3.0e38f)) return 0;
+  int e = 0;
+  frexpf(bound, &e);             // bound < 2^e
+  return max(-120, min(120, 14 - e));
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *(const uint32_t*)&h;
+}
+
+template <int TYPE, int BN>
+__global__ void __launch_bounds__(QG_THREADS, 1)
+    qgemm_tc_kernel(const __grid_constant__ QgParams p, const __grid_constant__ QgMaps maps) {
+  extern __shared__ uint8_t qg_smem_raw[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int split = p.split;
+  const int nsplit = split ? 2 : 1;
+  // ---- shared memory carve-up (1024-byte aligned operand tiles) ----
+  uint8_t* base = (uint8_t*)(((uintptr_t)qg_smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* sA = base;                                        // [2][nsplit][16 KB]
+  uint8_t* sB = sA + 2 * nsplit * QG_ATILE;                  // [nbs][nsplit][BN * 128]
+  const int btile = BN * 128;
+  uint8_t* sRaw = sB + (size_t)p.nbs * nsplit * btile;       // [2][128][slot]
+  uint64_t* bars = (uint64_t*)(sRaw + 2 * QG_M * p.slot);
+  uint64_t* raw_full = bars;        // 2
+  uint64_t* raw_empty = bars + 2;   // 2
+  uint64_t* a_full = bars + 4;      // 2
+  uint64_t* a_empty = bars + 6;     // 2
+  uint64_t* acc_full = bars + 8;    // 1
+  uint64_t* b_full = bars + 9;      // nbs
+  uint64_t* b_empty = b_full + p.nbs;
+  uint32_t* s_tmem = (uint32_t*)(b_empty + p.nbs);
+
+  // ---- tile coordinates ----
+  const int mt = blockIdx.x, t0 = blockIdx.y * BN;
+  int sg = 0;
+  while (sg + 1 < p.nseg && mt >= p.seg[sg + 1].mtile0) ++sg;
+  const bool swiglu = p.epi == QG_SWIGLU;
+  const int rows_per_tile = swiglu ? QG_M / 2 : QG_M;
+  const int r0 = (mt - p.seg[sg].mtile0) * rows_per_tile;
+  const int nk = p.K / QG_BK;
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&raw_full[i], 1);
+      mbar_init(&raw_empty[i], 4);
+      mbar_init(&a_full[i], 4);
+      mbar_init(&a_empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    for (int i = 0; i < p.nbs; ++i) {
+      mbar_init(&b_full[i], 1);
+      mbar_init(&b_empty[i], 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(s_tmem, BN < 32 ? 32 : BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *s_tmem;
+  // activations, token exponents and (in the engine) residual rows come from
+  // the preceding kernels: every thread waits for them
+  pdl_wait();
+
+  if (warp == 0) {
+    // ================= producer =================
+    // row r of the tile -> (matrix, row) and the bytes to copy
+    const uint32_t bx = (uint32_t)btile;
+    for (int sb = 0; sb < p.nsb; ++sb) {
+      const int rs = sb & 1;
+      if (sb >= 2 && !mbar_wait(&raw_empty[rs], ((sb >> 1) - 1) & 1, p.err)) break;
+      uint32_t bytes = 0;
+      uintptr_t src[4];
+      uint32_t len[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int r = lane + 32 * j;
+        int s = sg, row = r0 + r;
+        if (swiglu) {
+          s = r < 64 ? 0 : 1;
+          row = r0 + (r & 63);
+        }
+        len[j] = 0;
+        src[j] = 0;
+        if (row < p.seg[s].rows) {
+          const uintptr_t a = (uintptr_t)(p.seg[s].W + (long long)row * p.row_bytes + (long long)sb * QgBlk<TYPE>::BB);
+          const uintptr_t a0 = a & ~(uintptr_t)15, a1 = (a + QgBlk<TYPE>::BB + 15) & ~(uintptr_t)15;
+          src[j] = a0;
+          len[j] = (uint32_t)(a1 - a0);
+          bytes += len[j];
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
+      if (lane == 0) mbar_arrive_expect_tx(&raw_full[rs], bytes);
+      __syncwarp();
+      uint8_t* dst = sRaw + (size_t)rs * QG_M * p.slot;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (len[j]) tma_load_1d(dst + (size_t)(lane + 32 * j) * p.slot, (const void*)src[j], len[j], &raw_full[rs]);
+      // the four activation tiles of this super-block
+      if (lane == 0) {
+        for (int ks = 0; ks < 4; ++ks) {
+          const int i = 4 * sb + ks, bs = i % p.nbs;
+          if (i >= p.nbs && !mbar_wait(&b_empty[bs], ((i / p.nbs) - 1) & 1, p.err)) break;
+          mbar_arrive_expect_tx(&b_full[bs], bx * nsplit);
+          uint8_t* bd = sB + (size_t)bs * nsplit * btile;
+          tma_load_2d(bd, &maps.hi, i * QG_BK, t0, &b_full[bs]);
+          if (split) tma_load_2d(bd + btile, &maps.lo, i * QG_BK, t0, &b_full[bs]);
+        }
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    // ================= MMA issuer =================
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(QG_M, BN);
+      bool ok = true;
+      for (int i = 0; i < nk && ok; ++i) {
+        const int as = i & 1, bs = i % p.nbs;
+        ok = mbar_wait(&a_full[as], (i >> 1) & 1, p.err) && mbar_wait(&b_full[bs], (i / p.nbs) & 1, p.err);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t a_hi = smem_u32(sA + (size_t)as * nsplit * QG_ATILE);
+        const uint32_t b_hi = smem_u32(sB + (size_t)bs * nsplit * btile);
+        const uint64_t dah = umma_desc_sw128(a_hi), dbh = umma_desc_sw128(b_hi);
+        const uint64_t dal = umma_desc_sw128(a_hi + QG_ATILE), dbl = umma_desc_sw128(b_hi + btile);
+#pragma unroll
+        for (int kk = 0; kk < QG_BK / 16; ++kk) {
+          const uint64_t o = (uint64_t)(2 * kk);     // +32 bytes along K
+          umma_f16(tbase, dah + o, dbh + o, idesc, (i | kk) != 0);
+          if (split) {
+            umma_f16(tbase, dah + o, dbl + o, idesc, 1);
+            umma_f16(tbase, dal + o, dbh + o, idesc, 1);
+          }
+        }
+        umma_commit(&a_empty[as]);
+        umma_commit(&b_empty[bs]);
+      }
+      umma_commit(acc_full);
+    }
+    __syncwarp();
+  } else {
+    // ================= dequantize, then epilogue =================
+    const int q = warp & 3;                 // TMEM lane quarter of this warp
+    const int r = 32 * q + lane;            // tile row of this thread
+    int s = sg, row = r0 + r;
+    if (swiglu) {
+      s = r < 64 ? 0 : 1;
+      row = r0 + (r & 63);
+    }
+    const bool valid = row < p.seg[s].rows;
+    const uintptr_t rowsrc = valid ? (uintptr_t)(p.seg[s].W + (long long)row * p.row_bytes) : 0;
+    const int sw = qg_exp_for(*p.wbound);
+    const float wscale = ldexpf(1.0f, sw);
+    bool ok = true;
+    for (int i = 0; i < nk && ok; ++i) {
+      const int sb = i >> 2, ks = i & 3, rs = sb & 1, as = i & 1;
+      if (ks == 0) ok = mbar_wait(&raw_full[rs], (sb >> 1) & 1, p.err);
+      if (ok && i >= 2) ok = mbar_wait(&a_empty[as], ((i >> 1) - 1) & 1, p.err);
+      if (!ok) break;
+      uint8_t* ah = sA + (size_t)as * nsplit * QG_ATILE;
+      float w[64];
+      if (valid) {
+        const uintptr_t a = rowsrc + (uintptr_t)sb * QgBlk<TYPE>::BB;
+        const uint8_t* rp = sRaw + ((size_t)rs * QG_M + r) * p.slot + (a & 15);
+        qg_dequant<TYPE>(rp, ks, w);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) w[e] = 0.f;
+      }
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float x0 = w[8 * c + 2 * e] * wscale, x1 = w[8 * c + 2 * e + 1] * wscale;
+          const __half2 hh = __floats2half2_rn(x0, x1);
+          const float2 hf = __half22float2(hh);
+          h[e] = *(const uint32_t*)&hh;
+          l[e] = pack_h2(x0 - hf.x, x1 - hf.y);
+        }
+        *(uint4*)(ah + sw128_off(r, c)) = make_uint4(h[0], h[1], h[2], h[3]);
+        if (split) *(uint4*)(ah + QG_ATILE + sw128_off(r, c)) = make_uint4(l[0], l[1], l[2], l[3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&a_full[as]);
+        if (ks == 3) mbar_arrive(&raw_empty[rs]);
+      }
+    }
+    // ---- epilogue ----
+    if (ok) ok = mbar_wait(acc_full, 0, p.err);
+    tc_fence_after();
+    float* xch = (float*)sA;                 // SwiGLU: up rows [64][BN] (A ring is free now)
+    const uint32_t taddr = tbase + ((uint32_t)(32 * q) << 16);
+    for (int c0 = 0; c0 < BN; c0 += 8) {
+      uint32_t v[8];
+      tmem_ld_x8(taddr + (uint32_t)c0, v);
+      tmem_wait_ld();
+      if (!ok) continue;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int t = t0 + c0 + j;
+        if (t >= p.T) break;
+        const float val = __uint_as_float(v[j]) * ldexpf(1.0f, -sw) * ldexpf(1.0f, -(int)p.xexp[t]);
+        if (swiglu) {
+          if (r >= 64) xch[(r - 64) * BN + c0 + j] = val;
+          else xch[(64 + r) * BN + c0 + j] = val;   // gate values beside the up values
+        } else if (valid) {
+          float* y = p.seg[s].y + (long long)t * p.y_stride + row;
+          if (p.epi == QG_ADD) *y += val;
+          else *y = val;
+        }
+      }
+    }
+    if (swiglu) {
+      named_bar_sync(1, 128);
+      if (r < 64 && valid && ok) {
+        for (int c = 0; c < BN; ++c) {
+          const int t = t0 + c;
+          if (t >= p.T) break;
+          const float g = xch[(64 + r) * BN + c], u = xch[r * BN + c];
+          p.seg[0].y[(long long)t * p.y_stride + row] = g / (1.0f + expf(-g)) * u;   // src/ModelCPU.jl:455-468
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, BN < 32 ? 32 : BN);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// activations -> fp16 hi / lo rows with a per-token power-of-two scale
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) qg_act_kernel(const float* x, long long x_stride, int K, int pro,
+                                                     const float* pro_w, const float* pro_z, int group, float eps,
+                                                     __half* xhi, __half* xlo, float* xexp, int T) {
+  __shared__ float red[2][8];
+  const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  if (t >= T) {    // padding rows of the last token tile
+    pdl_wait();
+    pdl_trigger();
+    for (int i = 2 * tid; i < K; i += 512) {
+      *(__half2*)&xhi[(long long)t * K + i] = __floats2half2_rn(0.f, 0.f);
+      *(__half2*)&xlo[(long long)t * K + i] = __floats2half2_rn(0.f, 0.f);
+    }
+    if (tid == 0) xexp[t] = 0.f;
+    return;
+  }
+  const float* xr = x + (long long)t * x_stride;
+  const float* zr = pro_z ? pro_z + (long long)t * x_stride : nullptr;
+  pdl_wait();
+  pdl_trigger();
+  // pass 1: RMSNorm statistics and max|v|
+  float ss = 0.f;
+  if (pro == PRO_RMSNORM)
+    for (int i = tid; i < K; i += 256) ss = fmaf(xr[i], xr[i], ss);
+  ss = warp_sum(ss);
+  if (lane == 0) red[0][w] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < 8; ++i) tot += red[0][i];
+  const float inv = pro == PRO_RMSNORM ? 1.0f / sqrtf(tot / (float)K + eps) : 1.0f;
+  auto value = [&](int i) -> float {
+    if (pro == PRO_RMSNORM) return xr[i] * inv * pro_w[i];
+    return xr[i];
+  };
+  // head-norm x SiLU(z) (the ssm_out input): one warp per head group
+  extern __shared__ float qa_v[];
+  float amax = 0.f;
+  if (pro == PRO_HEADNORM_GATE) {
+    for (int h = w; h < K / group; h += 8) {
+      float hs = 0.f;
+      for (int e = lane; e < group; e += 32) hs = fmaf(xr[h * group + e], xr[h * group + e], hs);
+      hs = warp_sum(hs);
+      const float sc = 1.0f / sqrtf(hs / (float)group + eps);
+      for (int e = lane; e < group; e += 32) {
+        const int i = h * group + e;
+        const float z = zr[i];
+        const float v = xr[i] * sc * pro_w[e] * (z / (1.0f + expf(-z)));
+        qa_v[i] = v;
+        amax = fmaxf(amax, fabsf(v));
+      }
+    }
+  } else {
+    for (int i = tid; i < K; i += 256) {
+      const float v = value(i);
+      qa_v[i] = v;
+      amax = fmaxf(amax, fabsf(v));
+    }
+  }
+  amax = warp_max(amax);
+  __syncthreads();
+  if (lane == 0) red[1][w] = amax;
+  __syncthreads();
+  float m = 0.f;
+  for (int i = 0; i < 8; ++i) m = fmaxf(m, red[1][i]);
+  const int e = qg_exp_for(m);
+  const float sc = ldexpf(1.0f, e);
+  for (int i = 2 * tid; i < K; i += 512) {
+    const float a = qa_v[i] * sc, b = qa_v[i + 1] * sc;
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(h);
+    *(__half2*)&xhi[(long long)t * K + i] = h;
+    *(__half2*)&xlo[(long long)t * K + i] = __floats2half2_rn(a - hf.x, b - hf.y);
+  }
+  if (tid == 0) xexp[t] = (float)e;
+}
+
+// bound of |w| over the weight blocks of a matrix: |d| * 63 * 63 + |dmin| * 63
+// for the K-quants (covers Q4_K / Q5_K / Q6_K codes), |d| * 128 for Q8_0
+__global__ void qg_wbound_kernel(const uint8_t* W, long long nblocks, int type, float* out) {
+  float m = 0.f;
+  for (long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x; b < nblocks;
+       b += (long long)gridDim.x * blockDim.x) {
+    float v;
+    if (type == T_Q6_K) {
+      const uint8_t* p = W + b * 210 + 208;
+      v = fabsf(h2f_bits((uint16_t)(p[0] | (p[1] << 8)))) * 128.f * 32.f;
+    } else if (type == T_Q8_0) {
+      const uint8_t* p = W + b * 34;
+      v = fabsf(h2f_bits((uint16_t)(p[0] | (p[1] << 8)))) * 128.f;
+    } else {
+      const uint8_t* p = W + b * (type == T_Q4_K ? 144 : 176);
+      v = fabsf(h2f_bits((uint16_t)(p[0] | (p[1] << 8)))) * 63.f * 31.f +
+          fabsf(h2f_bits((uint16_t)(p[2] | (p[3] << 8)))) * 63.f;
+    }
+    if (v == v) m = fmaxf(m, v);
+  }
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) atomicMax((int*)out, __float_as_int(m));
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+  });
+  return fn;
+}
+
+// [T][K] fp16 rows, box = 64 x BN, SWIZZLE_128B, zero fill past T
+int make_act_map(CUtensorMap* m, const __half* base, int K, int T, int BN) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(INFERNO_ECUDA, "qgemm: cuTensorMapEncodeTiled is not available");
+  if (((uintptr_t)base & 15) || K % QG_BK)
+    return set_error(INFERNO_EINVAL, "qgemm: activation rows must be 16-byte aligned with K %% 64 == 0");
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)T};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)QG_BK, (cuuint32_t)BN};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(INFERNO_ECUDA, "qgemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return 0;
+}
+
+template <int TYPE, int BN>
+cudaError_t qg_launch_bn(const QgParams& p, const QgMaps& maps, dim3 grid, size_t smem, cudaStream_t st, bool pdl) {
+  static DeviceOnce once;
+  cudaError_t ea = once.run([] {
+    return cudaFuncSetAttribute(qgemm_tc_kernel<TYPE, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  if (ea != cudaSuccess) return ea;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(QG_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, qgemm_tc_kernel<TYPE, BN>, p, maps);
+}
+
+template <int TYPE>
+cudaError_t qg_launch(const QgParams& p, const QgMaps& maps, int BN, dim3 grid, size_t smem, cudaStream_t st,
+                      bool pdl) {
+  switch (BN) {
+    case 32: return qg_launch_bn<TYPE, 32>(p, maps, grid, smem, st, pdl);
+    case 64: return qg_launch_bn<TYPE, 64>(p, maps, grid, smem, st, pdl);
+    default: return qg_launch_bn<TYPE, 128>(p, maps, grid, smem, st, pdl);
+  }
+}
+
+}  // namespace
+
+bool qgemm_supported(int type) { return type == T_Q4_K || type == T_Q5_K || type == T_Q6_K || type == T_Q8_0; }
+
+int qgemm_bn(int T) { return T <= 32 ? 32 : T <= 64 ? 64 : 128; }
+int qgemm_rows_padded(int T) {
+  const int bn = qgemm_bn(T);
+  return (T + bn - 1) / bn * bn;
+}
+
+int launch_qgemm_act(const float* x, long long x_stride, int K, int T, int pro, const float* pro_w,
+                     const float* pro_z, int group, float eps, __half* xhi, __half* xlo, float* xexp,
+                     cudaStream_t st, bool pdl) {
+  if (T <= 0) return 0;
+  if (K % 2 || K > 16384) return set_error(INFERNO_EINVAL, "qgemm activations: K %d", K);
+  static DeviceOnce once;
+  cudaError_t ea = once.run(
+      [] { return cudaFuncSetAttribute(qg_act_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024); });
+  if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "qgemm activations attribute: %s", cudaGetErrorString(ea));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(qgemm_rows_padded(T));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = (size_t)K * 4;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, qg_act_kernel, x, x_stride, K, pro, pro_w, pro_z, group, eps, xhi, xlo,
+                                     xexp, T);
+  return e == cudaSuccess ? 0 : set_error(INFERNO_ECUDA, "qgemm activations launch: %s", cudaGetErrorString(e));
+}
+
+int launch_qgemm_wbound(int type, const void* W, long long rows, int K, float* out, cudaStream_t st, bool reset) {
+  const long long nblocks = rows * (K / (type == T_Q8_0 ? 32 : 256));
+  cudaError_t e = reset ? cudaMemsetAsync(out, 0, 4, st) : cudaSuccess;
+  if (e != cudaSuccess) return set_error(INFERNO_ECUDA, "qgemm weight bound: %s", cudaGetErrorString(e));
+  const int grid = (int)std::min<long long>(1184, (nblocks + 255) / 256);
+  if (grid > 0) qg_wbound_kernel<<<grid, 256, 0, st>>>((const uint8_t*)W, nblocks, type, out);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : set_error(INFERNO_ECUDA, "qgemm weight bound: %s", cudaGetErrorString(e));
+}
+
+int launch_qgemm(const QgemmCall& c, cudaStream_t st, bool pdl) {
+  if (!qgemm_supported(c.type)) return set_error(INFERNO_EINVAL, "qgemm: type %d has no tensor-core path", c.type);
+  if (c.K % 256 || c.K <= 0) return set_error(INFERNO_EINVAL, "qgemm: K %d not a multiple of 256", c.K);
+  if (c.T <= 0) return 0;
+  if (c.nmats < 1 || c.nmats > 4 || (c.epi == QG_SWIGLU && c.nmats != 2))
+    return set_error(INFERNO_EINVAL, "qgemm: bad matrix count %d", c.nmats);
+  const int BN = qgemm_bn(c.T);
+  QgParams p = {};
+  const int rows_per_tile = c.epi == QG_SWIGLU ? QG_M / 2 : QG_M;
+  int mt = 0;
+  for (int i = 0; i < c.nmats; ++i) {
+    p.seg[i].W = (const uint8_t*)c.mats[i].W;
+    p.seg[i].y = c.mats[i].y;
+    p.seg[i].rows = c.mats[i].rows;
+    p.seg[i].mtile0 = mt;
+    if (!(c.epi == QG_SWIGLU && i == 1)) mt += (c.mats[i].rows + rows_per_tile - 1) / rows_per_tile;
+    else p.seg[i].mtile0 = INT_MAX;
+  }
+  if (c.epi == QG_SWIGLU && c.mats[0].rows != c.mats[1].rows)
+    return set_error(INFERNO_EINVAL, "qgemm: SwiGLU matrices differ in rows");
+  p.nseg = c.nmats;
+  p.n_mtiles = mt;
+  p.K = c.K;
+  p.nsb = c.K / 256;
+  const int bb = c.type == T_Q4_K ? 144 : c.type == T_Q5_K ? 176 : c.type == T_Q6_K ? 210 : 272;
+  p.row_bytes = (long long)p.nsb * bb;
+  p.slot = (bb + 15) / 16 * 16 + 16;           // aligned superset of one super-block
+  p.T = c.T;
+  p.y_stride = c.y_stride;
+  p.epi = c.epi;
+  p.split = c.split ? 1 : 0;
+  p.xexp = c.xexp;
+  p.wbound = c.wbound;
+  p.err = c.err;
+  const int nsplit = p.split ? 2 : 1;
+  const size_t fixed = 1024 + 2 * nsplit * QG_ATILE + 2 * (size_t)QG_M * p.slot + 256;
+  const size_t bstage = (size_t)nsplit * BN * 128;
+  const size_t cap = 227 * 1024;
+  int nbs = (int)std::min<size_t>(4, (cap - fixed) / bstage);
+  if (nbs < 2) return set_error(INFERNO_EINVAL, "qgemm: tiles do not fit shared memory");
+  p.nbs = nbs;
+  const size_t smem = fixed + nbs * bstage;
+  QgMaps maps;
+  memset(&maps, 0, sizeof maps);
+  int rc;
+  // the activation rows are padded (zeros) to whole BN tiles
+  const int Tpad = qgemm_rows_padded(c.T);
+  if ((rc = make_act_map(&maps.hi, (const __half*)c.xhi, c.K, Tpad, BN))) return rc;
+  if ((rc = make_act_map(&maps.lo, (const __half*)(c.split ? c.xlo : c.xhi), c.K, Tpad, BN))) return rc;
+  const dim3 grid(mt, (c.T + BN - 1) / BN);
+  cudaError_t e;
+  switch (c.type) {
+    case T_Q4_K: e = qg_launch<T_Q4_K>(p, maps, BN, grid, smem, st, pdl); break;
+    case T_Q5_K: e = qg_launch<T_Q5_K>(p, maps, BN, grid, smem, st, pdl); break;
+    case T_Q6_K: e = qg_launch<T_Q6_K>(p, maps, BN, grid, smem, st, pdl); break;
+    default: e = qg_launch<T_Q8_0>(p, maps, BN, grid, smem, st, pdl); break;
+  }
+  return e == cudaSuccess ? 0 : set_error(INFERNO_ECUDA, "qgemm launch: %s", cudaGetErrorString(e));
+}
+
+}  // namespace inf
+
+namespace inf {
+
+int qgemm_from_gemv(const GemvCall& c, cudaStream_t st) {
+  static const bool off = getenv("INFERNO_NO_TC_GEMM") != nullptr;
+  static const bool fast = getenv("INFERNO_TC_GEMM_FP16") != nullptr;
+  if (off || c.nb < 16 || !qgemm_supported(c.type) || c.inner % 256 || c.nxv != 1 || c.xch_wk >= 0 ||
+      c.xch_rk >= 0 || c.force_r || (c.pro != PRO_NONE && c.pro != PRO_RMSNORM) ||
+      (c.epi != EPI_STORE && c.epi != EPI_ADD && c.epi != EPI_SWIGLU) || c.x_stride % 2)
+    return 1;
+  for (int i = 0; i < c.nmats; ++i)
+    if (c.mats[i].indirect || !c.mats[i].y && !(c.epi == EPI_SWIGLU && i == 1)) return 1;
+  const int T = c.nb, K = c.inner, Tpad = qgemm_rows_padded(T);
+  // stream-ordered scratch: fp16 hi / lo activations (padded to whole token
+  // tiles), token exponents, the weight bound
+  const size_t act = (size_t)Tpad * K * 2;
+  const size_t bytes = 2 * act + (size_t)Tpad * 4 + 256;
+  char* buf = nullptr;
+  INF_CUDA_TRY(cudaMallocAsync((void**)&buf, bytes, st));
+  __half* xhi = (__half*)buf;
+  __half* xlo = (__half*)(buf + act);
+  float* xexp = (float*)(buf + 2 * act);
+  float* wb = xexp + Tpad;
+  int rc = launch_qgemm_act(c.x, c.x_stride, K, T, c.pro, c.pro_w, c.pro_z, c.pro_group, c.eps, xhi, xlo, xexp, st,
+                            false);
+  // one bound over every matrix of the call (a common weight scale): the
+  // bound kernel folds into its output with atomicMax
+  for (int i = 0; i < c.nmats && !rc; ++i)
+    rc = launch_qgemm_wbound(c.type, c.mats[i].W, c.mats[i].rows, K, wb, st, i == 0);
+  if (!rc) {
+    QgemmCall q;
+    q.type = c.type;
+    q.K = K;
+    for (int i = 0; i < c.nmats; ++i) q.mats[i] = c.mats[i];
+    q.nmats = c.nmats;
+    q.T = T;
+    q.xhi = xhi;
+    q.xlo = xlo;
+    q.xexp = xexp;
+    q.y_stride = c.y_stride ? c.y_stride : c.mats[0].rows;
+    q.epi = c.epi == EPI_ADD ? 1 : c.epi == EPI_SWIGLU ? 2 : 0;
+    q.wbound = wb;
+    q.err = c.err ? c.err : device_error_word(0);
+    q.split = !fast;
+    rc = launch_qgemm(q, st, false);
+  }
+  cudaError_t ef = cudaFreeAsync(buf, st);
+  if (!rc && ef != cudaSuccess) rc = set_error(INFERNO_ECUDA, "qgemm scratch: %s", cudaGetErrorString(ef));
+  return rc;
+}
+
+}  // namespace inf
