@@ -243,6 +243,14 @@ int inferno_layer_forward(InfernoEngine* eng, int layer, float* x_host, int pos)
 int inferno_forward_tokens(InfernoEngine* eng, const int32_t* tok, int n, int pos0, float* logits_out,
                            int32_t* argmax_out);
 
+/* Logits (vocab floats per position, may be NULL) and first-max argmax of
+ * EVERY position of tok[0..n) at positions pos0..: the full_logits forward
+ * that mtp_verify_step! runs over draft tokens (src/ModelCPU.jl:1914-1930;
+ * the caller compares argmax_out[i] with tok[i+1]).  Like the reference, the
+ * recurrent state and KV cache advance over all n tokens. */
+int inferno_forward_tokens_all(InfernoEngine* eng, const int32_t* tok, int n, int pos0, float* logits_out,
+                               int32_t* argmax_out);
+
 /* Greedy decode on the device: feeds `tok` at `pos`, then each argmax at the
  * next position, n_steps times; out_tokens[i] = token produced at step i.
  * The generation loop of test/benchmark_e2e.jl:43-59 / Engine.generate

@@ -18,6 +18,7 @@
 //   finalize (next token, position, output slot)
 // All control state (token, position, step) lives in device memory so the
 // same graph replays for prompt tokens and for greedy decode.
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -70,6 +71,7 @@ struct DevTensor {
   int64_t ne[4] = {1, 1, 1, 1};
   void* d = nullptr;
   size_t bytes = 0;
+  float* wb = nullptr;   // bound of |w| shared by this tensor's tensor-core GEMM group (prefill)
   int64_t rows() const { return ne[1] * ne[2] * ne[3]; }
 };
 
@@ -136,6 +138,12 @@ struct InfernoEngine {
   std::map<long long, int> pf_seen;
   float *xb = nullptr, *qkvb = nullptr, *zb = nullptr, *yb = nullptr, *qgb = nullptr, *kb = nullptr,
         *vb = nullptr, *ob = nullptr, *hb = nullptr;
+  // tensor-core prefill: fp16 hi / lo activation rows [PF_MAX_T][max inner],
+  // token exponents, the GDN prep rows and the weight bounds
+  __half *pf_xhi = nullptr, *pf_xlo = nullptr;
+  float* pf_xexp = nullptr;
+  inf::GdnScratch pf_gdn{};
+  float* pf_wbounds = nullptr;
   // MoE scratch: router logits, selected ids / weights, expert hidden, expert outputs
   float *moe_logits = nullptr, *moe_w = nullptr, *moe_h = nullptr, *moe_y = nullptr;
   int* moe_idx = nullptr;
@@ -548,6 +556,28 @@ int bgemv(InfernoEngine* e, const DevTensor* W, int inner, std::initializer_list
   c.eps = e->cfg.rms_eps;
   c.epi = epi;
   c.err = e->err;
+  if (T >= PF_TC_MIN_T && e->pf_xhi && W->wb && qgemm_supported(W->type) && epi != EPI_ARGMAX && inner % 256 == 0) {
+    // fp16 hi / lo activations with the prologue applied, then the tcgen05 GEMM
+    int rc = launch_qgemm_act(x, x_stride, inner, T, pro, pro_w, pro_z, group, e->cfg.rms_eps, e->pf_xhi,
+                              e->pf_xlo, e->pf_xexp, e->st, false);
+    if (rc) return rc;
+    mark(e, K_GEMV);
+    QgemmCall q;
+    q.type = W->type;
+    q.K = inner;
+    for (auto& m : mats) q.mats[q.nmats++] = m;
+    q.T = T;
+    q.xhi = e->pf_xhi;
+    q.xlo = e->pf_xlo;
+    q.xexp = e->pf_xexp;
+    q.y_stride = y_stride;
+    q.epi = epi == EPI_ADD ? 1 : epi == EPI_SWIGLU ? 2 : 0;
+    q.wbound = W->wb;
+    q.err = e->err;
+    rc = launch_qgemm(q, e->st, false);
+    if (!rc) mark(e, K_GEMV);
+    return rc;
+  }
   const int rc = launch_gemv(c, e->st, false);
   if (!rc) mark(e, K_GEMV);
   return rc;
@@ -593,7 +623,11 @@ int enqueue_prefill_chunk(InfernoEngine* e, const int* toks, int T, int pos0, bo
       g.y = e->yb;
       g.step = L.step;
       g.done = L.done;
-      if ((rc = launch_gdn_chunk(g, T, e->st))) return rc;
+      if (T >= PF_TC_MIN_T && e->pf_gdn.qn) {
+        if ((rc = launch_gdn_prefill(g, T, e->pf_gdn, e->st))) return rc;
+      } else if ((rc = launch_gdn_chunk(g, T, e->st))) {
+        return rc;
+      }
       mark(e, K_GDN);
       if ((rc = bgemv(e, L.ssm_out, e->di, {M(L.ssm_out, e->xb)}, e->yb, T, e->di, H, PRO_HEADNORM_GATE,
                       (const float*)L.ssm_norm->d, e->zb, c.ssm_dv, EPI_ADD)))
@@ -858,6 +892,62 @@ int setup_xch(InfernoEngine* e) {
 }  // namespace inf
 
 extern "C" {
+
+namespace inf {
+namespace {
+
+// Tensor-core prefill: activation staging and, per GEMM group of a prefill
+// chunk, one bound of |w| (the GEMM's power-of-two weight scale).
+int setup_tc_prefill(InfernoEngine* e) {
+  const char* off = getenv("INFERNO_NO_TC_GEMM");
+  if (off && atoi(off) != 0) return 0;
+  const InfernoConfig& c = e->cfg;
+  const int H = c.hidden_size;
+  const size_t kmax = std::max<size_t>({(size_t)H, (size_t)e->di, (size_t)c.intermediate_size,
+                                        (size_t)c.n_heads * c.head_dim});
+  const size_t rows = (size_t)qgemm_rows_padded(PF_MAX_T);
+  int rc;
+  if ((rc = dalloc(e, (uint16_t**)&e->pf_xhi, rows * kmax)) || (rc = dalloc(e, (uint16_t**)&e->pf_xlo, rows * kmax)) ||
+      (rc = dalloc(e, &e->pf_xexp, rows)))
+    return rc;
+  if (e->C) {
+    const size_t n = (size_t)PF_MAX_T * c.ssm_nv;
+    if ((rc = dalloc(e, &e->pf_gdn.qn, n * 128)) || (rc = dalloc(e, &e->pf_gdn.kn, n * 128)) ||
+        (rc = dalloc(e, &e->pf_gdn.vv, n * c.ssm_dv)) || (rc = dalloc(e, &e->pf_gdn.beta, n)) ||
+        (rc = dalloc(e, &e->pf_gdn.g, n)))
+      return rc;
+  }
+  std::vector<std::vector<DevTensor*>> groups;
+  for (auto& L : e->layers) {
+    if (L.ssm) {
+      groups.push_back({L.in_proj});
+      groups.push_back({L.gate});
+      groups.push_back({L.ssm_out});
+    } else {
+      groups.push_back({L.wq});
+      if (L.wk->type == L.wv->type) groups.push_back({L.wk, L.wv});
+      else groups.push_back({L.wk}), groups.push_back({L.wv});
+      groups.push_back({L.wo});
+    }
+    if (L.ffn_gate) groups.push_back({L.ffn_gate, L.ffn_up});
+    if (L.ffn_down) groups.push_back({L.ffn_down->type == T_Q6_KR ? &L.ffn_down_raw : L.ffn_down});
+  }
+  if ((rc = dalloc(e, &e->pf_wbounds, groups.size()))) return rc;
+  for (size_t gi = 0; gi < groups.size(); ++gi) {
+    float* wb = e->pf_wbounds + gi;
+    bool first = true;
+    for (DevTensor* t : groups[gi]) {
+      if (!t || !qgemm_supported(t->type)) continue;
+      if ((rc = launch_qgemm_wbound(t->type, t->d, t->rows(), (int)t->ne[0], wb, e->st, first))) return rc;
+      first = false;
+      t->wb = wb;
+    }
+  }
+  return 0;
+}
+
+}  // namespace
+}  // namespace inf
 
 int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
   if (!cfg || !out) return set_error(INFERNO_EINVAL, "engine_create: null argument");
@@ -1209,6 +1299,7 @@ int inferno_engine_finalize(InfernoEngine* e) {
           (rc = dalloc(e, &e->vb, T * c.n_kv_heads * c.head_dim)) ||
           (rc = dalloc(e, &e->ob, T * c.n_heads * c.head_dim)) || (rc = dalloc(e, &e->hb, T * c.intermediate_size)))
         return rc;
+      if ((rc = setup_tc_prefill(e))) return rc;
     }
   }
   e->max_out = c.max_ctx + 8;
@@ -1525,6 +1616,23 @@ int inferno_forward_tokens(InfernoEngine* e, const int32_t* tok, int n, int pos0
   INF_CUDA_TRY(cudaStreamSynchronize(e->st));
   if ((rc = check_device_error(e))) return rc;
   if (argmax_out) *argmax_out = h.last;
+  return 0;
+}
+
+// Every position's logits / first-max argmax over n tokens (the full_logits
+// forward of mtp_verify_step!, src/ModelCPU.jl:1914-1930): the tokens run one
+// at a time through the single-token graph with logits, so each position's
+// result is exactly that of the decode path; the state advances over all n.
+int inferno_forward_tokens_all(InfernoEngine* e, const int32_t* tok, int n, int pos0, float* logits_out,
+                               int32_t* argmax_out) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  if (!tok || n <= 0 || !argmax_out) return set_error(INFERNO_EINVAL, "forward_tokens_all: no tokens or output");
+  const size_t V = (size_t)e->cfg.vocab_size;
+  for (int i = 0; i < n; ++i)
+    if ((rc = inferno_forward_tokens(e, tok + i, 1, pos0 + i, logits_out ? logits_out + (size_t)i * V : nullptr,
+                                     argmax_out + i)))
+      return rc;
   return 0;
 }
 

@@ -114,6 +114,19 @@ __global__ void __launch_bounds__(GS_THREADS) gdn_seq_kernel(int T, int H, int d
     *((float4*)(S + ((size_t)h * dv + r0 + warp + GS_WARPS * j) * GS_DK) + lane) = s[j];
 }
 
+int launch_gdn_seq(int T, int n_heads, int dv, const float* q, const float* k, const float* v, const float* beta,
+                   const float* g, float* S, float* y, cudaStream_t st) {
+  const size_t smem = 2 * sizeof(GsBuf);
+  static DeviceOnce once;
+  cudaError_t ea = once.run([] {
+    return cudaFuncSetAttribute(gdn_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "gdn_recurrence: %s", cudaGetErrorString(ea));
+  gdn_seq_kernel<<<dim3(n_heads, dv / GS_ROWS), GS_THREADS, smem, st>>>(T, n_heads, dv, q, k, v, beta, g, S, y);
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : set_error(INFERNO_ECUDA, "gdn_recurrence launch: %s", cudaGetErrorString(e));
+}
+
 }  // namespace inf
 
 using namespace inf;
@@ -129,14 +142,5 @@ extern "C" int inferno_gdn_recurrence(int T, int n_heads, int dk, int dv, const 
     return set_error(INFERNO_EINVAL, "gdn_recurrence: dk must be %d and dv a multiple of %d", GS_DK, GS_ROWS);
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)S) & 15)
     return set_error(INFERNO_EINVAL, "gdn_recurrence: q, k and S must be 16-byte aligned");
-  const size_t smem = 2 * sizeof(GsBuf);
-  static DeviceOnce once;
-  cudaError_t ea = once.run([] {
-    return cudaFuncSetAttribute(gdn_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  });
-  if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "gdn_recurrence: %s", cudaGetErrorString(ea));
-  gdn_seq_kernel<<<dim3(n_heads, dv / GS_ROWS), GS_THREADS, smem, (cudaStream_t)stream>>>(T, n_heads, dv, q, k, v,
-                                                                                           beta, g, S, y);
-  cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? 0 : set_error(INFERNO_ECUDA, "gdn_recurrence launch: %s", cudaGetErrorString(e));
+  return launch_gdn_seq(T, n_heads, dv, q, k, v, beta, g, S, y, (cudaStream_t)stream);
 }

@@ -145,10 +145,26 @@ int launch_fused_inproj_gdn(const void* Wperm, int H, const float* x, const floa
                             const GdnParams& g, float* z, int* err, cudaStream_t st, bool pdl);
 
 // chunked prefill (prefill.cu): tokens per chunk = the batched GEMV's columns
-constexpr int PF_MAX_T = 8;
+constexpr int PF_MAX_T = 128;
+// chunks of at least this many tokens run their products on the tensor-core
+// GEMM (qgemm_tc.cu) and the GDN as token-parallel prep + recurrence;
+// shorter chunks use the batched GEMV and the chunk-sequential GDN kernel
+constexpr int PF_TC_MIN_T = 16;
 struct GdnParams;
 struct AttnParams;
 int launch_gdn_chunk(const GdnParams& p, int T, cudaStream_t st);
+// the delta-rule recurrence of T steps (gdn_seq.cu): q, k [T][H][128], v, y
+// [T][H][dv], beta, g [T][H], S [H][dv][128]
+int launch_gdn_seq(int T, int n_heads, int dv, const float* q, const float* k, const float* v, const float* beta,
+                   const float* g, float* S, float* y, cudaStream_t st);
+// Prefill form of the GDN step for T tokens: per-token projections' conv,
+// gates and norms in parallel over (token, head) into the scratch rows
+// (qn, kn [T][nv][128], vv [T][nv][dv], beta, g [T][nv]), the conv ring and
+// step counter update, then the sequential recurrence (launch_gdn_seq)
+struct GdnScratch {
+  float *qn, *kn, *vv, *beta, *g;
+};
+int launch_gdn_prefill(const GdnParams& p, int T, const GdnScratch& s, cudaStream_t st);
 int launch_attn_chunk(const AttnParams& p, int pos0, int T, cudaStream_t st);
 
 // sampler parameters (sample.cu; InfernoSampling without the ABI padding)

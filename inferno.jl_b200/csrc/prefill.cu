@@ -313,6 +313,75 @@ __global__ void __launch_bounds__(PF_HD) attn_chunk_kernel(const __grid_constant
   p.out[(long long)t * p.nh * PF_HD + (long long)h * PF_HD + d] = (num / den) * (1.0f / (1.0f + expf(-gte)));
 }
 
+// ---------------------------------------------------------------------------
+// GDN prefill, token-parallel part: for token t of the chunk and value head h
+// the conv1d + SiLU of its q / k / v channels (inputs of tokens t-K+1..t from
+// the chunk or, before it, from the conv ring), the L2-normalised q (times
+// 1/sqrt(dk)) and k, and the Float64 gates of GatedDeltaNetCPU
+// (src/ModelCPU.jl:555-636): decay g = a_h * softplus(alpha + dt_h) and
+// beta = sigmoid(beta_raw), alpha / beta_raw = w . RMSNorm(x_t).  Grid (T, nv),
+// 128 threads (one q / k / v channel each).  The recurrence then runs in
+// gdn_seq_kernel.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(PF_DK) gdn_prep_kernel(const __grid_constant__ GdnParams p, int T, GdnScratch o) {
+  __shared__ float red[5][4];
+  const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int g = h % p.nk, K = p.K, C = p.C, H = p.H;
+  pdl_wait();
+  pdl_trigger();
+  const int t0 = *p.step;
+  const float* x = p.x + (long long)t * H;
+  float acc[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int i = tid; i < H; i += PF_DK) {
+    const float xv = x[i], xw = xv * p.in_norm[i];
+    acc[0] = fmaf(xv, xv, acc[0]);
+    acc[1] = fmaf(p.w_alpha[(long long)h * H + i], xw, acc[1]);
+    acc[2] = fmaf(p.w_beta[(long long)h * H + i], xw, acc[2]);
+  }
+  const int cq = g * PF_DK + tid, ck = p.nk * PF_DK + g * PF_DK + tid;
+  const int cv = 2 * p.nk * PF_DK + h * p.dv + tid;       // valid for tid < dv
+  float vq = 0.f, vk = 0.f, vvv = 0.f;
+  for (int k = 0; k < K; ++k) {
+    const int tau = t - (K - 1) + k;
+    float iq, ik, iv = 0.f;
+    if (tau >= 0) {
+      const float* q = p.qkv + (long long)tau * C;
+      iq = q[cq];
+      ik = q[ck];
+      if (tid < p.dv) iv = q[cv];
+    } else {      // history: input of time t0 + tau, kept in ring slot (t0 + tau) mod K
+      int slot = (t0 + tau) % K;
+      if (slot < 0) slot += K;
+      const float* r = p.ring + (long long)slot * C;
+      iq = r[cq];
+      ik = r[ck];
+      if (tid < p.dv) iv = r[cv];
+    }
+    vq += iq * p.conv_w[(long long)cq * K + k];
+    vk += ik * p.conv_w[(long long)ck * K + k];
+    if (tid < p.dv) vvv += iv * p.conv_w[(long long)cv * K + k];
+  }
+  const float qv = vq / (1.0f + expf(-vq));
+  const float kv = vk / (1.0f + expf(-vk));
+  acc[3] = qv * qv;
+  acc[4] = kv * kv;
+  pf_block_sum(acc, 5, red);
+  const long long row = (long long)t * p.nv + h;
+  o.qn[row * PF_DK + tid] = qv * (1.0f / (sqrtf(acc[3]) + 1.0e-6f) * (1.0f / sqrtf((float)PF_DK)));
+  o.kn[row * PF_DK + tid] = kv * (1.0f / (sqrtf(acc[4]) + 1.0e-6f));
+  if (tid < p.dv) o.vv[row * p.dv + tid] = vvv / (1.0f + expf(-vvv));
+  if (tid == 0) {
+    const float scale = 1.0f / sqrtf(acc[0] / (float)H + p.eps);
+    const float alpha = acc[1] * scale, beta_raw = acc[2] * scale;
+    double a = (double)alpha + (double)p.dt_bias[h];
+    a = fmin(20.0, fmax(-20.0, a));
+    const double sp = log(1.0 + exp(a));
+    o.g[row] = (float)((double)p.ssm_a[h] * sp);
+    const double bv = fmin(20.0, fmax(-20.0, (double)beta_raw));
+    o.beta[row] = (float)(1.0 / (1.0 + exp(-bv)));
+  }
+}
+
 namespace {
 template <class F, class... A>
 int pf_launch(F kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, A... args) {
@@ -336,6 +405,18 @@ int launch_gdn_chunk(const GdnParams& p, int T, cudaStream_t st) {
                       p.qkv, p.step, p.C, p.K, T)))
     return rc;
   return pf_launch(step_advance_kernel, dim3(1), dim3(1), 0, st, p.step, T);
+}
+
+int launch_gdn_prefill(const GdnParams& p, int T, const GdnScratch& o, cudaStream_t st) {
+  if (T < 1 || p.dv % PF_ROWS || p.dv > PF_DK || p.K < 1 || p.K > PF_MAXK || p.H % 4)
+    return set_error(INFERNO_EINVAL, "gdn prefill: unsupported dims");
+  int rc;
+  if ((rc = pf_launch(gdn_prep_kernel, dim3(T, p.nv), dim3(PF_DK), 0, st, p, T, o))) return rc;
+  if ((rc = pf_launch(conv_ring_chunk_kernel, dim3(std::max(1, (std::min(T, p.K) * p.C + 255) / 256)), dim3(256), 0,
+                      st, p.ring, p.qkv, p.step, p.C, p.K, T)))
+    return rc;
+  if ((rc = pf_launch(step_advance_kernel, dim3(1), dim3(1), 0, st, p.step, T))) return rc;
+  return launch_gdn_seq(T, p.nv, p.dv, o.qn, o.kn, o.vv, o.beta, o.g, p.S, p.y, st);
 }
 
 int launch_attn_chunk(const AttnParams& p, int pos0, int T, cudaStream_t st) {

@@ -87,8 +87,6 @@ __device__ __forceinline__ uint32_t ld_u32(const uint8_t* p) { return lds_u32_an
 // 6-bit scale / min j of a K-quant super-block (src/Dequant.jl:345-362)
 __device__ __forceinline__ void qg_kscale(const uint8_t* sc, int j, float& s, float& m) {
   const uint32_t w0 = ld_u32(sc), w1 = ld_u32(sc + 4), w2 = ld_u32(sc + 8);
-  const uint8_t* b = nullptr;
-  (void)b;
   uint32_t sj, mj;
   if (j < 4) {
     sj = (w0 >> (8 * j)) & 63;

@@ -216,6 +216,31 @@ class Model:
              _p(logits) if want_logits else None, _p(am))
         return int(am[0]), logits
 
+    def forward_all(self, tokens, pos: int, want_logits: bool = True):
+        """forward_cpu! with full_logits: (argmax of every position, logits
+        [n][vocab] or None); the state advances over all tokens."""
+        toks = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        am = np.zeros(toks.size, np.int32)
+        logits = np.empty((toks.size, self.spec.vocab), np.float32) if want_logits else None
+        call("inferno_forward_tokens_all", self.h, _p(toks), int(toks.size), int(pos),
+             _p(logits) if want_logits else None, _p(am))
+        return am, logits
+
+    def mtp_verify_step(self, draft_tokens, pos: int):
+        """mtp_verify_step! (src/ModelCPU.jl:1914-1930): run the draft tokens
+        at pos.. with every position's logits and count the leading drafts
+        that equal the argmax of the previous position.  Returns (accepted,
+        logits [n][vocab])."""
+        draft = np.asarray(draft_tokens, dtype=np.int32).reshape(-1)
+        am, logits = self.forward_all(draft, pos, want_logits=True)
+        accepted = 0
+        for i in range(draft.size - 1):
+            if int(am[i]) == int(draft[i + 1]):
+                accepted += 1
+            else:
+                break
+        return accepted, logits
+
     def decode_greedy(self, tok: int, pos: int, n: int) -> np.ndarray:
         out = np.zeros(n, np.int32)
         call("inferno_decode_greedy", self.h, int(tok), int(pos), int(n), _p(out))

@@ -164,12 +164,14 @@ def test_q6k_regrouping_is_bitwise_neutral(tiny, monkeypatch):
     assert np.array_equal(lg0, lg1)
 
 
-@pytest.mark.parametrize("n", [2, 8, 21])
+@pytest.mark.parametrize("n", [2, 8, 21, 64, 150])
 def test_chunked_prefill_matches_token_loop(tiny, monkeypatch, n):
-    """forward_tokens runs prompts in chunks of up to 8 tokens (batched GEMVs,
-    chunk GDN / attention kernels); logits, argmax and the state it leaves
-    (checked through the greedy continuation) match the token-by-token path
-    and the oracle."""
+    """forward_tokens runs prompts in chunks of up to 128 tokens: chunks of
+    >= 16 tokens on the tcgen05 GEMM with the token-parallel GDN prep + the
+    sequential recurrence, shorter ones on the batched GEMV and the chunk GDN
+    kernel (150 = 128 + 22, 2 and 8 the short path); logits, argmax and the
+    state it leaves (checked through the greedy continuation) match the
+    token-by-token path and the oracle."""
     spec, T, orc = tiny
     prompt = S.tokens(17, n, spec.vocab)
     monkeypatch.setenv("INFERNO_B200_NO_PREFILL", "1")
