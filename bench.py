@@ -411,6 +411,20 @@ def run_ours(args):
             "kernel_time_share_note": "marginal in-graph time of each class / token time (ablation); the rest "
                                       "is embedding, finalize and the dependency chain between kernels",
             "wall_s": wall}
+    # the sharded configs over the same launched ranks (config 4 tensor
+    # parallel, config 5 expert parallel): the 1 -> N curve north_star asks
+    # for, next to the config-1 replicas headline
+    if not args.no_sharded:
+        m.close()
+        for wl, key in (("config4", "tp_config4"), ("config5", "ep_config5")):
+            try:
+                sub_line = measure_big(wl, 2, 1, ws, rank, local)
+                line[key] = {k: sub_line[k] for k in ("value", "unit", "ms_per_token", "prefill_s",
+                                                      "prefill_tokens_per_s", "comm", "token_roofline")}
+                line[key]["n_gpus"] = ws
+                line[key]["parallelism"] = sub_line["config"]["parallelism"]
+            except Exception as ex:          # reported, never fatal to the headline line
+                line[key] = {"error": str(ex)[:200]}
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(spec, T)
         ref_k = reference_kernel_gbs(T)
@@ -418,7 +432,8 @@ def run_ours(args):
             line["cpu_reference_kernel"] = ref_k
     if rank == 0:
         print(json.dumps(line), flush=True)
-    m.close()
+    if args.no_sharded:
+        m.close()
     if ws > 1:
         torch.distributed.destroy_process_group()
     return 0
@@ -443,11 +458,24 @@ def run_big(args):
     distribution, generated in seconds)."""
     import torch
     import torch.distributed as dist
-    W = BIG[args.workload]
     ws, rank, local = dist_env()
     torch.cuda.set_device(local)
     if ws > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    line = measure_big(args.workload, args.steps, args.warmup, ws, rank, local)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if ws > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def measure_big(workload, steps, warmup, ws, rank, local):
+    """One config-4 / config-5 measurement over the launched ranks (tensor /
+    expert parallel when ws > 1); returns the JSON-line dict (rank 0's)."""
+    import torch
+    import torch.distributed as dist
+    W = BIG[workload]
     from inferno_b200 import synth as S
     from inferno_b200.model import Model, algorithmic_bytes_per_token
     spec = S.CONFIGS[W["spec"]]
@@ -472,7 +500,7 @@ def run_big(args):
         m.restore_device()
         return m.decode_greedy(tok0, P, ND)
 
-    for _ in range(args.warmup):
+    for _ in range(max(1, warmup)):
         ref = step()
 
     def barrier():
@@ -485,13 +513,14 @@ def run_big(args):
     clocks.start()
     barrier()
     t_dev = 0.0
-    for _ in range(args.steps):
+    for _ in range(steps):
         out = step()
         t_dev += m.last_decode_ms()
     barrier()
     clk = clocks.stop()
     assert np.array_equal(out, ref), "decode is not deterministic across steps"
-    ms_step = max_over_ranks(t_dev / args.steps)
+    ms_step = max_over_ranks(t_dev / steps)
+    prefill_s = max_over_ranks(prefill_s)
     seqs = 1 if tp else ws
     value = seqs * ND / (ms_step / 1000.0)
     peaks = {}
@@ -501,8 +530,8 @@ def run_big(args):
         pass
     peak = float(peaks.get("hbm_gbs", 6650.0))
     per_gpu_gbs = tok_bytes / (ws if tp else 1) / (ms_step / ND / 1000.0) / 1e9
-    line = {"metric": W["metric"], "value": value, "unit": UNIT, "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+    line = {"metric": W["metric"], "value": value, "unit": UNIT, "n_gpus": ws, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong" if tp else "weak", "vs_baseline": None,
             "dtype": "f32 (fp32 activations, GGUF block weights)",
             "data": "synthetic (seeded; rows of each matrix drawn from 256 quantized N(0,0.02) rows)",
@@ -514,13 +543,13 @@ def run_big(args):
             "clocks": clk, "gpu_launches": m.kernels_per_token() * ND,
             "token_roofline": {"algorithmic_bytes_per_token": tok_bytes, "achieved_gbs_per_gpu": per_gpu_gbs,
                                "frac": per_gpu_gbs / peak, "peak": peak},
-            "ms_per_token": ms_step / ND, "prefill_s": prefill_s}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+            "ms_per_token": ms_step / ND, "prefill_s": prefill_s,
+            "prefill_tokens_per_s": P / prefill_s,
+            "comm": ("NCCL all-reduce of the residual after each expert FFN" if spec.n_experts else
+                     ("fused peer-memory residual exchange in the GEMV epilogue / prologue" if not
+                      os.environ.get("INFERNO_TP_NCCL") else "NCCL all-reduce of the residual")) if tp else None}
     m.close()
-    if ws > 1:
-        dist.destroy_process_group()
-    return 0
+    return line
 
 
 def run_gdn(args):
@@ -647,6 +676,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the config-4 (tensor parallel) / config-5 (expert parallel) keys of the config-1 line")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

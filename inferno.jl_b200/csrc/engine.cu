@@ -179,6 +179,7 @@ struct InfernoEngine {
   // advances its own)
   int* gdn_steps = nullptr;
   bool in_token = false, token_steps = false;
+  bool gdn_head = true;          // whole-head GDN kernel in decode tokens (INFERNO_GDN_HEAD=0: per-row-block)
   int trace_idx = 0;
   int launches = 0;              // kernels enqueued since the last enqueue_token began
   int token_launches = 0;        // kernels of one decode token (set by enqueue_token)
@@ -459,9 +460,17 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     g.done = L.done;
     g.trace = trace_slot(e);
     g.self_advance = (e->in_token && e->token_steps) ? 0 : 1;
-    if (!(ab & 2) && (rc = launch_gdn_step(g, e->st, pdl))) return rc;
+    // whole-head step (output norm + gate fused, ssm_out reads a plain input)
+    // inside decode tokens, where the finalize kernel advances the counters
+    const bool head = e->gdn_head && !g.self_advance;
+    if (head) {
+      g.z = e->z;
+      g.out_norm = (const float*)L.ssm_norm->d;
+    }
+    if (!(ab & 2) && (rc = head ? launch_gdn_head(g, e->st, pdl) : launch_gdn_step(g, e->st, pdl))) return rc;
     mark(e, K_GDN);
-    if (!(ab & 8) && (rc = gemv(e, L.ssm_out->type, e->di, {M(L.ssm_out, e->x)}, e->y, (ab & 128) ? PRO_NONE : PRO_HEADNORM_GATE,
+    const int sp = (head || (ab & 128)) ? PRO_NONE : PRO_HEADNORM_GATE;
+    if (!(ab & 8) && (rc = gemv(e, L.ssm_out->type, e->di, {M(L.ssm_out, e->x)}, e->y, sp,
                    (const float*)L.ssm_norm->d, e->z, c.ssm_dv, residual_epi(e), nullptr, pdl)))
       return rc;
     if ((rc = tp_sum_x(e))) return rc;
@@ -1000,6 +1009,7 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
     }
   }
   if (const char* sp = getenv("INFERNO_XCH_SPIN")) e->xch_spin = (unsigned)strtoul(sp, nullptr, 0);
+  if (const char* gh = getenv("INFERNO_GDN_HEAD")) e->gdn_head = atoi(gh) != 0;
   const char* d = getenv("INFERNO_B200_DUMP");
   e->dump = d && atoi(d) != 0;
   if (const char* ab = getenv("INFERNO_B200_ABLATE")) e->ablate = (unsigned)strtoul(ab, nullptr, 0);
@@ -1221,7 +1231,11 @@ int inferno_engine_finalize(InfernoEngine* e) {
       return rc;
     if (L.ffn_gate->rows() != c.intermediate_size || L.ffn_down->ne[0] != c.intermediate_size)
       return set_error(INFERNO_EINVAL, "layer %d: FFN dims do not match the config", i);
-    if (e->repack && L.ffn_down->type == T_Q6_K && L.ffn_down->rows() % 16 == 0 && c.intermediate_size % 256 == 0) {
+    // (rows of more than 8192 inputs do not fit the tensor-core GEMV's shared
+    // memory next to their staged activations: they stay GGUF-layout Q6_K on
+    // the CUDA-core path)
+    if (e->repack && L.ffn_down->type == T_Q6_K && L.ffn_down->rows() % 16 == 0 && c.intermediate_size % 256 == 0 &&
+        c.intermediate_size <= 8192) {
       void* d = nullptr;
       if (cudaMalloc(&d, (L.ffn_down->bytes + 255) / 256 * 256) != cudaSuccess)
         return set_error(INFERNO_ENOMEM, "ffn_down regrouping: cudaMalloc failed");

@@ -24,6 +24,10 @@ struct GdnParams {
   // 1: the last CTA advances *step (via `done`); 0: the caller advances it
   // after the kernel (the decode token's finalize kernel does it for every layer)
   int self_advance = 1;
+  // whole-head kernel (gdn_head_kernel): the per-head output RMSNorm and
+  // SiLU(z) gate are applied in the step, y then holds the gated output
+  const float* z = nullptr;        // [nv*dv] attn_gate GEMV output
+  const float* out_norm = nullptr; // [dv] ssm_norm weight
   unsigned long long* trace = nullptr;   // debug timeline slots (KT_*, common.cuh)
 };
 
@@ -50,6 +54,9 @@ struct AttnParams {
 };
 
 int launch_gdn_step(const GdnParams& p, cudaStream_t st, bool pdl);
+// one CTA per head, output norm + gate fused (y = gated output); the caller
+// advances the step counter
+int launch_gdn_head(const GdnParams& p, cudaStream_t st, bool pdl);
 int launch_attn_decode(const AttnParams& p, cudaStream_t st, bool pdl);
 
 }  // namespace inf
