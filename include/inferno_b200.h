@@ -163,6 +163,16 @@ int inferno_attention_step(const float* qg, const float* k, const float* v, cons
                            float* k_cache, float* v_cache, int max_ctx, int pos, int split_len, float* out,
                            void* stream);
 
+/* The same recurrence in its chunked (WY / UT-transform) form for prefill:
+ * chunks of `chunk` = 64 tokens, within a chunk the products are dense
+ * matrices (K K^T, the unit-triangular solve, W = T diag(e^G) K, U = T V,
+ * Q K^T) and only the 16-row blocks of S walk the chunks in order.  Same
+ * arguments and layouts as inferno_gdn_recurrence (dk = 128, dv a multiple of
+ * 16 up to 128); results agree with the sequential form to fp32 reordering.
+ * Stream-ordered scratch of about T * n_heads * 1.3 KB. */
+int inferno_gdn_chunked(int T, int n_heads, int dk, int dv, const float* q, const float* k, const float* v,
+                        const float* beta, const float* g, float* S, float* y, int chunk, void* stream);
+
 /* Sampling parameters of generate_cpu / softmax_sample
  * (src/ModelCPU.jl:1123-1225): temperature 0 = greedy. */
 typedef struct InfernoSampling {

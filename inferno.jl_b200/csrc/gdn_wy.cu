@@ -1,0 +1,262 @@
+// Chunked (WY / UT-transform) form of the gated delta-rule recurrence for
+// prefill: the same map as gdn_seq.cu (src/ModelCPU.jl:640-674 for every
+// token: S = S*exp(g); S += beta*(v - S k) k^T; y = S q), reorganised so that
+// most of the work is dense matrix products over chunks of C = 64 tokens.
+//
+// Within a chunk (tokens t = 0..C-1, state S_0 on entry, G_t = g_0+..+g_t):
+//   S_t = e^{G_t} S_0 + sum_{j<=t} e^{G_t - G_j} d_j k_j^T, and the residuals
+//   d_t = beta_t (v_t - e^{G_t} S_0 k_t - sum_{j<t} e^{G_t-G_j} (k_j.k_t) d_j)
+// solve the unit lower-triangular system (I + A) D = diag(beta)(V - diag(e^G) K S_0^T),
+// A[t][j] = beta_t e^{G_t-G_j} k_t.k_j (j < t).  With T = (I + A)^-1 diag(beta):
+//   D = U - W S_0^T,   U = T V,   W = T diag(e^G) K            (no S_0: parallel)
+//   Y = diag(e^G) Q S_0^T + (Q K^T o E) D,   E[t][j] = e^{G_t-G_j} (j <= t)
+//   S_C = e^{G_{C-1}} S_0 + D^T diag(e^{G_{C-1}-G}) K
+// Kernel 1 (grid chunks x heads) builds W, U and P = Q K^T o E per chunk;
+// kernel 2 (grid heads x 16-row blocks of S) walks the chunks in order with
+// its rows of S in shared memory.  The decay ratios are formed as
+// e^{G_t - G_j} (never e^{G_t} / e^{G_j}), so strong decays underflow to 0
+// instead of producing 0/0.
+#include <algorithm>
+#include "internal.h"
+#include "common.cuh"
+#include "../../include/inferno_b200.h"
+
+namespace inf {
+
+constexpr int WY_C = 64;          // tokens per chunk
+constexpr int WY_DK = 128;
+constexpr int WY_THREADS = 256;
+constexpr int WY_ROWS = 16;       // state rows per CTA of kernel 2
+
+struct WyScratch {
+  float* W;   // [nch][H][C][dk]
+  float* U;   // [nch][H][C][dv]
+  float* P;   // [nch][H][C][C]
+  float* G;   // [nch][H][C]
+};
+
+// smem: K, Q [C][dk+1] (padded rows), V [C][dv], A/T [C][C+1], G, beta
+__global__ void __launch_bounds__(WY_THREADS) gdn_wy_prep_kernel(int T, int H, int dv, const float* __restrict__ q,
+                                                                 const float* __restrict__ k,
+                                                                 const float* __restrict__ v,
+                                                                 const float* __restrict__ beta,
+                                                                 const float* __restrict__ g, WyScratch o) {
+  extern __shared__ float wsm[];
+  constexpr int KP = WY_DK + 1, AP = WY_C + 1;
+  float* Ks = wsm;                       // [C][KP]
+  float* Qs = Ks + WY_C * KP;            // [C][KP]
+  float* Vs = Qs + WY_C * KP;            // [C][dv]
+  float* As = Vs + WY_C * dv;            // [C][AP]  A, then T
+  float* Gs = As + WY_C * AP;            // [C]
+  float* Bs = Gs + WY_C;                 // [C]
+  const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int t0 = c * WY_C, n = min(WY_C, T - t0);
+  for (int i = tid; i < WY_C * WY_DK; i += WY_THREADS) {
+    const int t = i / WY_DK, d = i % WY_DK;
+    const bool ok = t < n;
+    Ks[t * KP + d] = ok ? k[((size_t)(t0 + t) * H + h) * WY_DK + d] : 0.f;
+    Qs[t * KP + d] = ok ? q[((size_t)(t0 + t) * H + h) * WY_DK + d] : 0.f;
+  }
+  for (int i = tid; i < WY_C * dv; i += WY_THREADS) {
+    const int t = i / dv, e = i % dv;
+    Vs[i] = t < n ? v[((size_t)(t0 + t) * H + h) * dv + e] : 0.f;
+  }
+  if (tid < WY_C) {
+    const bool ok = tid < n;
+    Gs[tid] = ok ? g[(size_t)(t0 + tid) * H + h] : 0.f;
+    Bs[tid] = ok ? beta[(size_t)(t0 + tid) * H + h] : 0.f;
+  }
+  __syncthreads();
+  // inclusive prefix sum of g (one warp, two tokens per lane)
+  if (tid < 32) {
+    float a = Gs[2 * tid], b = Gs[2 * tid + 1];
+    b += a;
+    float s = b;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float u = __shfl_up_sync(0xffffffffu, s, off);
+      if (tid >= off) s += u;
+    }
+    const float excl = s - b;
+    Gs[2 * tid] = excl + a;
+    Gs[2 * tid + 1] = s;
+  }
+  __syncthreads();
+  // A (strictly lower) and P = (Q K^T) o E (lower incl. diagonal)
+  float* Pg = o.P + ((size_t)c * H + h) * WY_C * WY_C;
+  for (int i = tid; i < WY_C * WY_C; i += WY_THREADS) {
+    const int t = i / WY_C, j = i % WY_C;
+    float a = 0.f, p = 0.f;
+    if (j <= t) {
+      float kk = 0.f, qk = 0.f;
+      for (int d = 0; d < WY_DK; ++d) {
+        const float kj = Ks[j * KP + d];
+        kk = fmaf(Ks[t * KP + d], kj, kk);
+        qk = fmaf(Qs[t * KP + d], kj, qk);
+      }
+      const float e = expf(Gs[t] - Gs[j]);
+      p = qk * e;
+      if (j < t) a = Bs[t] * e * kk;
+    }
+    As[t * AP + j] = a;
+    Pg[i] = p;
+  }
+  __syncthreads();
+  // T = (I + A)^-1 diag(beta), row by row in place over A's storage:
+  // X[t][:] = beta_t e_t - sum_{j<t} A[t][j] X[j][:]  (X[j] only has columns <= j)
+  // Thread = column; row t's old entries are read before the row is rewritten.
+  for (int t = 0; t < WY_C; ++t) {
+    float x = 0.f;
+    if (tid < WY_C && tid <= t) {
+      x = tid == t ? Bs[t] : 0.f;
+      for (int j = tid; j < t; ++j) x = fmaf(-As[t * AP + j], As[j * AP + tid], x);
+    }
+    __syncthreads();
+    if (tid < WY_C) As[t * AP + tid] = tid <= t ? x : 0.f;
+    __syncthreads();
+  }
+  // W = T diag(e^G) K, U = T V
+  float* Wg = o.W + ((size_t)c * H + h) * WY_C * WY_DK;
+  float* Ug = o.U + ((size_t)c * H + h) * WY_C * dv;
+  for (int i = tid; i < WY_C * WY_DK; i += WY_THREADS) {
+    const int t = i / WY_DK, d = i % WY_DK;
+    float w = 0.f;
+    for (int j = 0; j <= t; ++j) w = fmaf(As[t * AP + j] * expf(Gs[j]), Ks[j * KP + d], w);
+    Wg[i] = w;
+  }
+  for (int i = tid; i < WY_C * dv; i += WY_THREADS) {
+    const int t = i / dv, e = i % dv;
+    float u = 0.f;
+    for (int j = 0; j <= t; ++j) u = fmaf(As[t * AP + j], Vs[j * dv + e], u);
+    Ug[i] = u;
+  }
+  if (tid < WY_C) o.G[((size_t)c * H + h) * WY_C + tid] = Gs[tid];
+}
+
+// Grid (H, dv / 16), 256 threads.  Rows r0..r0+15 of S_h live in shared
+// memory across the chunks.
+__global__ void __launch_bounds__(WY_THREADS) gdn_wy_state_kernel(int T, int H, int dv, const float* __restrict__ q,
+                                                                  const float* __restrict__ k, float* S, float* y,
+                                                                  WyScratch o) {
+  extern __shared__ float wsm[];
+  constexpr int KP = WY_DK + 1;
+  float* Ss = wsm;                          // [16][KP]
+  float* Ws = Ss + WY_ROWS * KP;            // [C][KP]
+  float* Ks = Ws + WY_C * KP;               // [C][KP]
+  float* Qs = Ks + WY_C * KP;               // [C][KP]
+  float* Ds = Qs + WY_C * KP;               // [C][16]  D rows of this CTA
+  float* Ps = Ds + WY_C * WY_ROWS;          // [C][C]
+  float* Gs = Ps + WY_C * WY_C;             // [C]
+  const int h = blockIdx.x, r0 = blockIdx.y * WY_ROWS, tid = threadIdx.x;
+  for (int i = tid; i < WY_ROWS * WY_DK; i += WY_THREADS) {
+    const int r = i / WY_DK, d = i % WY_DK;
+    Ss[r * KP + d] = S[((size_t)h * dv + r0 + r) * WY_DK + d];
+  }
+  const int nch = (T + WY_C - 1) / WY_C;
+  for (int c = 0; c < nch; ++c) {
+    const int t0 = c * WY_C, n = min(WY_C, T - t0);
+    __syncthreads();
+    const float* Wg = o.W + ((size_t)c * H + h) * WY_C * WY_DK;
+    for (int i = tid; i < WY_C * WY_DK; i += WY_THREADS) {
+      const int t = i / WY_DK, d = i % WY_DK;
+      const bool ok = t < n;
+      Ws[t * KP + d] = Wg[i];
+      Ks[t * KP + d] = ok ? k[((size_t)(t0 + t) * H + h) * WY_DK + d] : 0.f;
+      Qs[t * KP + d] = ok ? q[((size_t)(t0 + t) * H + h) * WY_DK + d] : 0.f;
+    }
+    const float* Pg = o.P + ((size_t)c * H + h) * WY_C * WY_C;
+    for (int i = tid; i < WY_C * WY_C; i += WY_THREADS) Ps[i] = Pg[i];
+    if (tid < WY_C) Gs[tid] = o.G[((size_t)c * H + h) * WY_C + tid];
+    __syncthreads();
+    // D[t][i] = U[t][i] - W[t] . S[i]   (1024 entries, 4 per thread)
+    const float* Ug = o.U + ((size_t)c * H + h) * WY_C * dv;
+    for (int e = tid; e < WY_C * WY_ROWS; e += WY_THREADS) {
+      const int t = e / WY_ROWS, i = e % WY_ROWS;
+      float acc = Ug[t * dv + r0 + i];
+      for (int d = 0; d < WY_DK; ++d) acc = fmaf(-Ws[t * KP + d], Ss[i * KP + d], acc);
+      Ds[t * WY_ROWS + i] = acc;
+    }
+    __syncthreads();
+    // Y[t][i] = e^{G_t} Q[t] . S[i] + sum_{j<=t} P[t][j] D[j][i]
+    for (int e = tid; e < WY_C * WY_ROWS; e += WY_THREADS) {
+      const int t = e / WY_ROWS, i = e % WY_ROWS;
+      if (t >= n) continue;
+      float qs = 0.f;
+      for (int d = 0; d < WY_DK; ++d) qs = fmaf(Qs[t * KP + d], Ss[i * KP + d], qs);
+      float acc = expf(Gs[t]) * qs;
+      for (int j = 0; j <= t; ++j) acc = fmaf(Ps[t * WY_C + j], Ds[j * WY_ROWS + i], acc);
+      y[((size_t)(t0 + t) * H + h) * dv + r0 + i] = acc;
+    }
+    __syncthreads();
+    // S[i][d] = e^{G_last} S[i][d] + sum_j e^{G_last - G_j} D[j][i] K[j][d]
+    const float gl = Gs[n - 1];
+    for (int e = tid; e < WY_ROWS * WY_DK; e += WY_THREADS) {
+      const int i = e / WY_DK, d = e % WY_DK;
+      float acc = expf(gl) * Ss[i * KP + d];
+      for (int j = 0; j < n; ++j) acc = fmaf(expf(gl - Gs[j]) * Ds[j * WY_ROWS + i], Ks[j * KP + d], acc);
+      Ss[i * KP + d] = acc;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < WY_ROWS * WY_DK; i += WY_THREADS) {
+    const int r = i / WY_DK, d = i % WY_DK;
+    S[((size_t)h * dv + r0 + r) * WY_DK + d] = Ss[r * KP + d];
+  }
+}
+
+size_t gdn_wy_scratch_bytes(int T, int H, int dv) {
+  const size_t nch = (size_t)(T + WY_C - 1) / WY_C;
+  return nch * H * WY_C * ((size_t)WY_DK + dv + WY_C + 1) * 4 + 1024;
+}
+
+int launch_gdn_wy(int T, int H, int dv, const float* q, const float* k, const float* v, const float* beta,
+                  const float* g, float* S, float* y, void* scratch, cudaStream_t st) {
+  if (T <= 0) return 0;
+  if (dv % WY_ROWS || dv > WY_DK) return set_error(INFERNO_EINVAL, "gdn chunked: dv %d", dv);
+  const size_t nch = (size_t)(T + WY_C - 1) / WY_C;
+  float* base = (float*)(((uintptr_t)scratch + 255) & ~(uintptr_t)255);
+  WyScratch o;
+  o.W = base;
+  o.U = o.W + nch * H * WY_C * WY_DK;
+  o.P = o.U + nch * H * WY_C * dv;
+  o.G = o.P + nch * H * WY_C * WY_C;
+  const size_t smem1 = ((size_t)2 * WY_C * (WY_DK + 1) + (size_t)WY_C * dv + (size_t)WY_C * (WY_C + 1) + 2 * WY_C) * 4;
+  const size_t smem2 = ((size_t)WY_ROWS * (WY_DK + 1) + 3 * (size_t)WY_C * (WY_DK + 1) + (size_t)WY_C * WY_ROWS +
+                        (size_t)WY_C * WY_C + WY_C) * 4;
+  static DeviceOnce once;
+  cudaError_t ea = once.run([] {
+    cudaError_t e = cudaFuncSetAttribute(gdn_wy_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    return cudaFuncSetAttribute(gdn_wy_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "gdn chunked attribute: %s", cudaGetErrorString(ea));
+  gdn_wy_prep_kernel<<<dim3((unsigned)nch, H), WY_THREADS, smem1, st>>>(T, H, dv, q, k, v, beta, g, o);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(INFERNO_ECUDA, "gdn chunked prep: %s", cudaGetErrorString(e));
+  gdn_wy_state_kernel<<<dim3(H, dv / WY_ROWS), WY_THREADS, smem2, st>>>(T, H, dv, q, k, S, y, o);
+  e = cudaGetLastError();
+  return e == cudaSuccess ? 0 : set_error(INFERNO_ECUDA, "gdn chunked state: %s", cudaGetErrorString(e));
+}
+
+}  // namespace inf
+
+using namespace inf;
+
+/* The recurrence of inferno_gdn_recurrence in its chunked (WY) form, chunks
+ * of 64 tokens; stream-ordered scratch of gdn_wy_scratch_bytes(). */
+extern "C" int inferno_gdn_chunked(int T, int n_heads, int dk, int dv, const float* q, const float* k,
+                                   const float* v, const float* beta, const float* g, float* S, float* y, int chunk,
+                                   void* stream) {
+  if (T <= 0 || n_heads <= 0 || !q || !k || !v || !beta || !g || !S || !y)
+    return set_error(INFERNO_EINVAL, "gdn_chunked: bad arguments");
+  if (dk != WY_DK || dv % WY_ROWS || dv > WY_DK || chunk != WY_C)
+    return set_error(INFERNO_EINVAL, "gdn_chunked: dk must be %d, dv a multiple of %d up to %d, chunk %d", WY_DK,
+                     WY_ROWS, WY_DK, WY_C);
+  cudaStream_t st = (cudaStream_t)stream;
+  void* scratch = nullptr;
+  INF_CUDA_TRY(cudaMallocAsync(&scratch, gdn_wy_scratch_bytes(T, n_heads, dv), st));
+  const int rc = launch_gdn_wy(T, n_heads, dv, q, k, v, beta, g, S, y, scratch, st);
+  cudaError_t ef = cudaFreeAsync(scratch, st);
+  if (rc) return rc;
+  return ef == cudaSuccess ? 0 : set_error(INFERNO_ECUDA, "gdn_chunked: %s", cudaGetErrorString(ef));
+}

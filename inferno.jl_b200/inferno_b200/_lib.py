@@ -50,7 +50,7 @@ EXPORTS = [
     "inferno_state_import", "inferno_last_decode_ms", "inferno_engine_destroy",
     "inferno_state_save_device", "inferno_state_restore_device", "inferno_kernels_per_token",
     "inferno_profile_tokens", "inferno_gemv_host_noalloc", "inferno_debug_trace", "inferno_tp_unique_id",
-    "inferno_gdn_recurrence", "inferno_attention_step", "inferno_forward_tokens_all", "inferno_debug_xch_timeout", "inferno_sample_logits", "inferno_decode_sample",
+    "inferno_gdn_recurrence", "inferno_gdn_chunked", "inferno_attention_step", "inferno_forward_tokens_all", "inferno_debug_xch_timeout", "inferno_sample_logits", "inferno_decode_sample",
     "inferno_gguf_open", "inferno_gguf_close", "inferno_gguf_version", "inferno_gguf_n_tensors", "inferno_gguf_n_kv",
     "inferno_gguf_data_offset", "inferno_gguf_key", "inferno_gguf_tensor_info", "inferno_gguf_get_int",
     "inferno_gguf_get_float", "inferno_gguf_get_string", "inferno_gguf_get_array", "inferno_engine_load_gguf",
