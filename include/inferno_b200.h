@@ -217,7 +217,7 @@ typedef struct InfernoConfig {
   int32_t n_experts_used;
   int32_t expert_ffn;
   int32_t shared_expert_ffn;
-  int32_t max_batch;             /* sequences per step (1 for batch-1 decode) */
+  int32_t max_batch;             /* state slices for batched decode (0 or 1: one sequence) */
   float rms_eps;
   float rope_theta;
   float partial_rotary_factor;
@@ -273,6 +273,23 @@ int inferno_decode_greedy(InfernoEngine* eng, int32_t tok, int pos, int n_steps,
  * token; the draws come from Philox(s->seed, step). */
 int inferno_decode_sample(InfernoEngine* eng, int32_t tok, int pos, int n_steps, const InfernoSampling* s,
                           const int32_t* seen_tokens, int n_seen, int32_t* out_tokens);
+
+/* Batched decode (InfernoConfig.max_batch = B_max > 1; dense models on one
+ * GPU): the engine keeps B_max slices of recurrent state and KV cache, one
+ * per sequence.  inferno_select_sequence(eng, b) points every single-sequence
+ * call (forward_tokens, decode_greedy, layer_forward, ...) at slice b -- e.g.
+ * to prefill each sequence's own prompt.  inferno_decode_batch then decodes
+ * sequences 0..B-1 in lockstep, greedily: sequence b feeds toks[b] at pos[b],
+ * then each step's first-max argmax at the next position; out_tokens[t*B + b]
+ * is sequence b's token of step t.  Every GEMV runs once per step over the B
+ * sequences (one weight read per step; B >= 16 on the tensor-core GEMM),
+ * the GDN and attention kernels index each sequence's own slice.  The token
+ * loop of the reference (src/ModelCPU.jl:945-989, MoE over tokens at
+ * src/Model.jl:478-561) run for B independent sequences; no reference
+ * counterpart for the batching itself. */
+int inferno_select_sequence(InfernoEngine* eng, int seq);
+int inferno_decode_batch(InfernoEngine* eng, const int32_t* toks, const int32_t* pos, int B, int n_steps,
+                         int32_t* out_tokens);
 
 /* Zero GDN conv + recurrent state and the KV cache (src/ModelCPU.jl:525-529). */
 int inferno_reset_states(InfernoEngine* eng);

@@ -33,12 +33,12 @@ constexpr int ATT_HD = 256;          // head_dim (one thread per dim)
 constexpr int ATT_THREADS = 256;
 constexpr int ATT_CHUNK = 32;        // keys per pass (8 threads per key)
 
-__device__ __forceinline__ void load_chunk(const AttnParams& p, int kvh, int j0, int jend, int pos, float4 (&kreg)[8],
-                                           float (&vreg)[ATT_CHUNK]) {
+__device__ __forceinline__ void load_chunk(const AttnParams& p, const float* KC, const float* VC, int kvh, int j0,
+                                           int jend, int pos, float4 (&kreg)[8], float (&vreg)[ATT_CHUNK]) {
   const int t = threadIdx.x, kk = t >> 3, part = t & 7;
   const int j = j0 + kk;
   if (j < jend && j != pos) {
-    const float4* kr = (const float4*)(p.kc + ((long long)j * p.nkv + kvh) * ATT_HD + part * 32);
+    const float4* kr = (const float4*)(KC + ((long long)j * p.nkv + kvh) * ATT_HD + part * 32);
 #pragma unroll
     for (int i = 0; i < 8; ++i) kreg[i] = kr[i];
   } else {
@@ -48,7 +48,7 @@ __device__ __forceinline__ void load_chunk(const AttnParams& p, int kvh, int j0,
 #pragma unroll
   for (int q = 0; q < ATT_CHUNK; ++q) {
     const int jj = j0 + q;
-    vreg[q] = (jj < jend && jj != pos) ? p.vc[((long long)jj * p.nkv + kvh) * ATT_HD + t] : 0.f;
+    vreg[q] = (jj < jend && jj != pos) ? VC[((long long)jj * p.nkv + kvh) * ATT_HD + t] : 0.f;
   }
 }
 
@@ -58,6 +58,15 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
   __shared__ float red[2][ATT_THREADS / 32];
   __shared__ int ticket;
   const int h = blockIdx.x, s = blockIdx.y, d = threadIdx.x;
+  const int sq = blockIdx.z;                       // sequence (batched decode)
+  float* KC = p.kc + sq * p.caches;
+  float* VC = p.vc + sq * p.caches;
+  const float* QG = p.qg + sq * p.qgs;
+  const float* KN = p.k + sq * p.kvs;
+  const float* VN = p.v + sq * p.kvs;
+  float* PO = p.part_o + (long long)sq * p.nh * p.nsplit * ATT_HD;
+  float* PML = p.part_ml + (long long)sq * p.nh * p.nsplit * 2;
+  int* CNT = p.counters + (long long)sq * p.nh;
   const int kvh = h / (p.nh / p.nkv);
   const int lane = d & 31, warp = d >> 5;
   if (d == 0) {
@@ -66,7 +75,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
   }
 
   // ---------------- pre-wait: position and the first K/V chunk ----------------
-  const int pos = *p.pos;     // written by the previous step's finalize
+  const int pos = p.pos[sq];     // written by the previous step's finalize
   if (pos < 0 || pos >= p.ctx) {
     pdl_wait();
     pdl_trigger();
@@ -78,7 +87,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
   const int j0 = s * p.split_len, j1 = min(j0 + p.split_len, L);
   float4 kreg[8];
   float vreg[ATT_CHUNK];
-  if (s < nact) load_chunk(p, kvh, j0, min(j0 + ATT_CHUNK, j1), pos, kreg, vreg);
+  if (s < nact) load_chunk(p, KC, VC, kvh, j0, min(j0 + ATT_CHUNK, j1), pos, kreg, vreg);
   pdl_wait();
   pdl_trigger();
   if (d == 0) {
@@ -89,9 +98,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
 
   // ---------------- q (and the new k) : RMSNorm + RoPE ----------------
   const bool has_new = (pos >= j0 && pos < j1);
-  const float qv = p.qg[(long long)h * 2 * ATT_HD + d];
-  const float kv = has_new ? p.k[kvh * ATT_HD + d] : 0.f;
-  if (has_new) vnew[d] = p.v[kvh * ATT_HD + d];
+  const float qv = QG[(long long)h * 2 * ATT_HD + d];
+  const float kv = has_new ? KN[kvh * ATT_HD + d] : 0.f;
+  if (has_new) vnew[d] = VN[kvh * ATT_HD + d];
   float a = warp_sum(qv * qv), b = warp_sum(kv * kv);
   if (lane == 0) { red[0][warp] = a; red[1][warp] = b; }
   __syncthreads();
@@ -120,8 +129,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
   __syncthreads();
   if (has_new && (h % (p.nh / p.nkv)) == 0) {
     const long long off = ((long long)pos * p.nkv + kvh) * ATT_HD + d;
-    p.kc[off] = knew[d];
-    p.vc[off] = vnew[d];
+    KC[off] = knew[d];
+    VC[off] = vnew[d];
   }
 
   if (d == 0) KT_LAST(p.trace, 4);
@@ -134,7 +143,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
   float m = -INFINITY, l = 0.f, o = 0.f;
   for (int c0 = j0; c0 < j1; c0 += ATT_CHUNK) {
     const int cend = min(c0 + ATT_CHUNK, j1);
-    if (c0 != j0) load_chunk(p, kvh, c0, cend, pos, kreg, vreg);
+    if (c0 != j0) load_chunk(p, KC, VC, kvh, c0, cend, pos, kreg, vreg);
     // the new row at pos comes from shared memory
     if (c0 + kk == pos) {
 #pragma unroll
@@ -167,36 +176,36 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
     m = mn;
   }
   if (d == 0) KT_LAST(p.trace, 5);
-  p.part_o[((long long)h * p.nsplit + s) * ATT_HD + d] = o;
+  PO[((long long)h * p.nsplit + s) * ATT_HD + d] = o;
   if (d == 0) {
-    p.part_ml[((long long)h * p.nsplit + s) * 2 + 0] = m;
-    p.part_ml[((long long)h * p.nsplit + s) * 2 + 1] = l;
+    PML[((long long)h * p.nsplit + s) * 2 + 0] = m;
+    PML[((long long)h * p.nsplit + s) * 2 + 1] = l;
   }
 
   // ---------------- last CTA of this head merges the splits ----------------
   __threadfence();
   __syncthreads();
-  if (d == 0) ticket = atomicAdd(&p.counters[h], 1);
+  if (d == 0) ticket = atomicAdd(&CNT[h], 1);
   __syncthreads();
   if (d == 0) KT_LAST(p.trace, 6);
   if (ticket != nact - 1) return;
   __threadfence();
-  if (d == 0) p.counters[h] = 0;
-  const float* mlp = p.part_ml + (long long)h * p.nsplit * 2;
+  if (d == 0) CNT[h] = 0;
+  const float* mlp = PML + (long long)h * p.nsplit * 2;
   float M = -INFINITY;
   for (int t = 0; t < nact; ++t) M = fmaxf(M, __ldcg(mlp + 2 * t));
   float num = 0.f, den = 0.f;
   for (int t = 0; t < nact; ++t) {
     const float w = expf(__ldcg(mlp + 2 * t) - M);
-    num = fmaf(w, __ldcg(p.part_o + ((long long)h * p.nsplit + t) * ATT_HD + d), num);
+    num = fmaf(w, __ldcg(PO + ((long long)h * p.nsplit + t) * ATT_HD + d), num);
     den = fmaf(w, __ldcg(mlp + 2 * t + 1), den);
   }
-  const float g = p.qg[(long long)h * 2 * ATT_HD + ATT_HD + d];
-  p.out[(long long)h * ATT_HD + d] = (num / den) * (1.0f / (1.0f + expf(-g)));
+  const float g = QG[(long long)h * 2 * ATT_HD + ATT_HD + d];
+  p.out[sq * p.outs + (long long)h * ATT_HD + d] = (num / den) * (1.0f / (1.0f + expf(-g)));
   if (d == 0) KT_LAST(p.trace, 6);
 }
 
-int launch_attn_decode(const AttnParams& p, cudaStream_t st, bool pdl) {
+int launch_attn_decode(const AttnParams& p, cudaStream_t st, bool pdl, int nseq) {
   if (p.nh % p.nkv || p.split_len % ATT_CHUNK || p.split_len < ATT_CHUNK || p.rd > ATT_HD || p.rd % 2)
     return set_error(INFERNO_EINVAL, "attention: unsupported shape (nh=%d nkv=%d split=%d rd=%d)", p.nh, p.nkv,
                      p.split_len, p.rd);
@@ -207,7 +216,7 @@ int launch_attn_decode(const AttnParams& p, cudaStream_t st, bool pdl) {
   });
   if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "attention attribute: %s", cudaGetErrorString(ea));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.nh, p.nsplit);
+  cfg.gridDim = dim3(p.nh, p.nsplit, nseq);
   cfg.blockDim = dim3(ATT_THREADS);
   cfg.stream = st;
   cudaLaunchAttribute at[1];

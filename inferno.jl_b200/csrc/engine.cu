@@ -93,6 +93,8 @@ struct LayerBind {
   int* done = nullptr;
   float* kc = nullptr;
   float* vc = nullptr;
+  // sequence 0's slices (batched decode keeps one slice per sequence)
+  float *ring0 = nullptr, *S0 = nullptr, *kc0 = nullptr, *vc0 = nullptr;
 };
 
 }  // namespace inf
@@ -109,6 +111,7 @@ struct InfernoEngine {
   ncclComm_t comm = nullptr;
   inf::DevTensor lm_view;
   inf::DevTensor lm_packed;         // tied lm_head regrouped for the tensor-core GEMV (T_Q6_KR)
+  inf::DevTensor* lm_raw = nullptr;  // the lm_head in GGUF layout
   float* logits_local = nullptr;
   // fused tensor-parallel exchange over NVLink peer memory (xch); when off
   // (INFERNO_TP_NCCL=1 or a GEMV outside the tensor-core path) the residual
@@ -180,6 +183,13 @@ struct InfernoEngine {
   int* gdn_steps = nullptr;
   bool in_token = false, token_steps = false;
   bool gdn_head = true;          // whole-head GDN kernel in decode tokens (INFERNO_GDN_HEAD=0: per-row-block)
+  // batched decode: nseq = max_batch state slices; `cur_seq` is the slice the
+  // single-sequence calls use; per batch size B one captured step graph
+  int nseq = 1, cur_seq = 0;
+  int *bt_tok = nullptr, *bt_pos = nullptr, *bt_out = nullptr, *bt_step = nullptr;
+  unsigned long long* bt_keys = nullptr;
+  int bt_out_cap = 0;
+  std::map<int, cudaGraphExec_t> bt_graphs;
   int trace_idx = 0;
   int launches = 0;              // kernels enqueued since the last enqueue_token began
   int token_launches = 0;        // kernels of one decode token (set by enqueue_token)
@@ -704,7 +714,7 @@ int launch_finalize(InfernoEngine* e, bool pdl) {
   cfg.numAttrs = pdl ? 1 : 0;
   cudaError_t r = cudaLaunchKernelEx(&cfg, finalize_kernel, e->ctl, (const int*)e->prompt, e->out_tokens, e->max_out,
                                      e->xch ? e->xch_seq : (unsigned long long*)nullptr, e->xch_k,
-                                     e->token_steps ? e->gdn_steps : (int*)nullptr,
+                                     e->token_steps ? e->gdn_steps + (size_t)e->cur_seq * e->cfg.num_layers : (int*)nullptr,
                                      e->token_steps ? e->cfg.num_layers : 0);
   if (r != cudaSuccess) return set_error(INFERNO_ECUDA, "finalize launch: %s", cudaGetErrorString(r));
   mark(e, K_FINAL);
@@ -813,8 +823,11 @@ int check_device_error(InfernoEngine* e) {
 }
 
 // run `n` steps: graph replays (8-token graph for bulk) or eager launches
+int capture_token_graphs(InfernoEngine* e);
+
 int run_steps(InfernoEngine* e, int n, bool logits_last) {
   int rc;
+  if (e->cfg.use_graphs && !e->dump && !e->g1 && (rc = capture_token_graphs(e))) return rc;
   if (e->cfg.use_graphs && !e->dump) {
     int left = n;
     while (left >= 8 + (logits_last ? 1 : 0)) {
@@ -970,7 +983,10 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
   if (c.ssm_dk != 128) return set_error(INFERNO_EINVAL, "engine_create: ssm state size %d unsupported (128)", c.ssm_dk);
   if (c.ssm_nk <= 0 || c.ssm_nv % c.ssm_nk) return set_error(INFERNO_EINVAL, "engine_create: nv %% nk != 0");
   if (c.max_ctx <= 0) return set_error(INFERNO_EINVAL, "engine_create: max_ctx must be positive");
-  if (c.max_batch > 1) return set_error(INFERNO_EINVAL, "engine_create: max_batch > 1 is not supported yet");
+  if (c.max_batch < 0 || c.max_batch > PF_MAX_T)
+    return set_error(INFERNO_EINVAL, "engine_create: max_batch %d outside [1, %d]", c.max_batch, PF_MAX_T);
+  if (c.max_batch > 1 && (c.tp_size > 1 || c.n_experts))
+    return set_error(INFERNO_EINVAL, "engine_create: batched decode needs a dense model on one GPU");
   if (c.tp_size < 1 || c.tp_rank < 0 || c.tp_rank >= c.tp_size)
     return set_error(INFERNO_EINVAL, "engine_create: tp_rank %d / tp_size %d", c.tp_rank, c.tp_size);
   if (c.tp_size > 1 && !c.nccl_unique_id)
@@ -984,6 +1000,7 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
                                      "width that is a multiple of 256");
   auto* e = new InfernoEngine();
   e->cfg = c;
+  e->nseq = c.max_batch > 1 ? c.max_batch : 1;
   e->ep = c.tp_size > 1 && c.n_experts > 0;
   e->tp = c.tp_size > 1 && !e->ep;
   e->dev = c.device;
@@ -1125,6 +1142,7 @@ int inferno_engine_finalize(InfernoEngine* e) {
   if ((rc = require(e, "output_norm.weight", &e->out_norm, T_F32))) return rc;
   e->lm_head = find(e, "output.weight");
   if (!e->lm_head) e->lm_head = e->embd;   // tied (src/LoaderCPU.jl:358-371)
+  e->lm_raw = e->lm_head;                  // GGUF layout (batched lm_head)
   // Q6_K matrices of the single-column GEMVs are regrouped per 16 rows for
   // the tensor-core path (aligned 16-byte loads; the same bytes and results).
   // The persistent kernel reads GGUF rows: no regrouping there.
@@ -1183,11 +1201,16 @@ int inferno_engine_finalize(InfernoEngine* e) {
           L.conv1d->ne[0] != c.ssm_conv_kernel || L.conv1d->ne[1] != e->C || L.alpha->rows() != c.ssm_nv ||
           L.ssm_norm->ne[0] != c.ssm_dv)
         return set_error(INFERNO_EINVAL, "layer %d: GDN tensor dims do not match the config", i);
-      if ((rc = dalloc(e, &L.ring, (size_t)c.ssm_conv_kernel * e->C, true)) ||
-          (rc = dalloc(e, &L.S, (size_t)c.ssm_nv * c.ssm_dv * c.ssm_dk, true)) || (rc = dalloc(e, &L.done, 4)))
+      // one slice of state per sequence of a batched decode (max_batch);
+      // the single-sequence paths use the selected slice (sequence 0 by default)
+      if ((rc = dalloc(e, &L.ring, (size_t)e->nseq * c.ssm_conv_kernel * e->C, true)) ||
+          (rc = dalloc(e, &L.S, (size_t)e->nseq * c.ssm_nv * c.ssm_dv * c.ssm_dk, true)) ||
+          (rc = dalloc(e, &L.done, 4)))
         return rc;
-      if (!e->gdn_steps && (rc = dalloc(e, &e->gdn_steps, (size_t)c.num_layers, true))) return rc;
+      if (!e->gdn_steps && (rc = dalloc(e, &e->gdn_steps, (size_t)e->nseq * c.num_layers, true))) return rc;
       L.step = e->gdn_steps + i;
+      L.ring0 = L.ring;
+      L.S0 = L.S;
     } else {
       any_attn = true;
       if ((rc = require(e, p + "attn_q.weight", &L.wq)) || (rc = require(e, p + "attn_k.weight", &L.wk)) ||
@@ -1199,7 +1222,9 @@ int inferno_engine_finalize(InfernoEngine* e) {
           L.wo->ne[0] != (int64_t)c.n_heads * c.head_dim)
         return set_error(INFERNO_EINVAL, "layer %d: attention tensor dims do not match the config", i);
       size_t kv = (size_t)c.max_ctx * c.n_kv_heads * c.head_dim;
-      if ((rc = dalloc(e, &L.kc, kv, true)) || (rc = dalloc(e, &L.vc, kv, true))) return rc;
+      if ((rc = dalloc(e, &L.kc, kv * e->nseq, true)) || (rc = dalloc(e, &L.vc, kv * e->nseq, true))) return rc;
+      L.kc0 = L.kc;
+      L.vc0 = L.vc;
     }
     if (c.n_experts) {
       const int E = c.n_experts, Ie = c.expert_ffn;
@@ -1304,7 +1329,7 @@ int inferno_engine_finalize(InfernoEngine* e) {
   {
     const char* np = getenv("INFERNO_B200_NO_PREFILL");
     e->prefill = !(np && atoi(np) != 0) && c.tp_size == 1 && !c.n_experts && !e->dump;
-    if (e->prefill) {
+    if (e->prefill || e->nseq > 1) {
       const size_t T = PF_MAX_T;
       if ((rc = dalloc(e, &e->xb, T * H)) || (rc = dalloc(e, &e->qkvb, T * e->C)) ||
           (rc = dalloc(e, &e->zb, T * e->di)) || (rc = dalloc(e, &e->yb, T * e->di)) ||
@@ -1337,20 +1362,301 @@ int inferno_engine_finalize(InfernoEngine* e) {
     const char* pe = getenv("INFERNO_B200_PERSISTENT");
     // opt-in: the per-stage grid barrier currently costs more than PDL-chained
     // graph launches (0.96 vs 0.72 ms/token on qwen35-0.8b)
-    e->persistent = !e->dump && !c.n_experts && c.tp_size == 1 && (pe && atoi(pe) != 0) && (e->embd->type == T_Q6_K || e->embd->type == T_Q4_K ||
+    e->persistent = !e->dump && !c.n_experts && c.tp_size == 1 && e->nseq == 1 && (pe && atoi(pe) != 0) && (e->embd->type == T_Q6_K || e->embd->type == T_Q4_K ||
                                                             e->embd->type == T_Q8_0 || e->embd->type == T_F32);
     if (e->persistent && (rc = build_persistent(e))) return rc;
   }
   INF_CUDA_TRY(cudaDeviceSynchronize());
   e->finalized = true;
-  if (c.use_graphs && !e->dump) {
-    if ((rc = capture(e, 1, false, &e->g1)) || (rc = capture(e, 1, true, &e->g1_logits)) ||
-        (rc = capture(e, 8, false, &e->g8))) {
-      e->finalized = false;
-      return rc;
-    }
+  if (c.use_graphs && !e->dump && (rc = capture_token_graphs(e))) {
+    e->finalized = false;
+    return rc;
   }
   return 0;
+}
+
+}  // extern "C"
+
+namespace inf {
+namespace {
+
+int capture_token_graphs(InfernoEngine* e) {
+  int rc;
+  if ((rc = capture(e, 1, false, &e->g1)) || (rc = capture(e, 1, true, &e->g1_logits)) ||
+      (rc = capture(e, 8, false, &e->g8)))
+    return rc;
+  return 0;
+}
+
+void drop_graphs(InfernoEngine* e) {
+  for (cudaGraphExec_t* g : {&e->g1, &e->g1_logits, &e->g8})
+    if (*g) {
+      cudaGraphExecDestroy(*g);
+      *g = nullptr;
+    }
+  for (auto& kv : e->pf_graphs) cudaGraphExecDestroy(kv.second);
+  e->pf_graphs.clear();
+  e->pf_seen.clear();
+}
+
+// Bind the single-sequence calls (forward, decode, layer) to state slice b.
+// The captured graphs hold the previous slice's pointers: they are dropped
+// and captured again on next use.
+int select_seq(InfernoEngine* e, int b) {
+  if (b < 0 || b >= e->nseq) return set_error(INFERNO_EINVAL, "sequence %d outside [0, %d)", b, e->nseq);
+  if (b == e->cur_seq) return 0;
+  const InfernoConfig& c = e->cfg;
+  const size_t kv = (size_t)c.max_ctx * c.n_kv_heads * c.head_dim;
+  for (int i = 0; i < c.num_layers; ++i) {
+    LayerBind& L = e->layers[i];
+    if (L.ssm) {
+      L.ring = L.ring0 + (size_t)b * c.ssm_conv_kernel * e->C;
+      L.S = L.S0 + (size_t)b * c.ssm_nv * c.ssm_dv * c.ssm_dk;
+      L.step = e->gdn_steps + (size_t)b * c.num_layers + i;
+    } else {
+      L.kc = L.kc0 + (size_t)b * kv;
+      L.vc = L.vc0 + (size_t)b * kv;
+    }
+  }
+  INF_CUDA_TRY(cudaStreamSynchronize(e->st));
+  drop_graphs(e);
+  e->cur_seq = b;
+  return 0;
+}
+
+// After a batched step: per sequence the argmax becomes its next token, its
+// output slot is written and its position and GDN step counters advance.
+__global__ void batch_finalize_kernel(int B, int nl, unsigned long long* keys, int* tok, int* pos, int* out,
+                                      int* step_ctr, int* steps) {
+  pdl_wait();
+  pdl_trigger();
+  const int st = *step_ctr;
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const unsigned long long key = keys[b];
+    const int am = (int)(0xffffffffu - (uint32_t)(key & 0xffffffffull));
+    tok[b] = am;
+    out[st * B + b] = am;
+    pos[b] += 1;
+    keys[b] = 0ull;
+  }
+  if (steps)
+    for (int i = threadIdx.x; i < B * nl; i += blockDim.x) steps[i] += 1;
+  __syncthreads();
+  if (threadIdx.x == 0) *step_ctr = st + 1;
+}
+
+// One lockstep decode step of sequences 0..B-1 (tokens bt_tok, positions
+// bt_pos): the prefill machinery with one column per sequence, the GDN and
+// attention kernels indexing each sequence's own state slice.
+int enqueue_batch_step(InfernoEngine* e, int B) {
+  const InfernoConfig& c = e->cfg;
+  const int H = c.hidden_size, I = c.intermediate_size, hdq = c.n_heads * c.head_dim;
+  const int kvd = c.n_kv_heads * c.head_dim;
+  const size_t kvs = (size_t)c.max_ctx * kvd;
+  int rc;
+  for (int b = 0; b < B; ++b)
+    if ((rc = launch_embed_row(e->embd->type, e->embd->d, (long long)e->embd->bytes / e->embd->rows(), H,
+                               e->bt_tok + b, e->xb + (size_t)b * H, c.vocab_size, e->st, false)))
+      return set_error(INFERNO_ECUDA, "batch embedding launch failed (%d)", rc);
+  for (int li = 0; li < c.num_layers; ++li) {
+    LayerBind& L = e->layers[li];
+    const float* an = (const float*)L.attn_norm->d;
+    if (L.ssm) {
+      if ((rc = bgemv(e, L.in_proj, H, {M(L.in_proj, e->qkvb)}, e->xb, B, H, e->C, PRO_RMSNORM, an, nullptr, 0,
+                      EPI_STORE)) ||
+          (rc = bgemv(e, L.gate, H, {M(L.gate, e->zb)}, e->xb, B, H, e->di, PRO_RMSNORM, an, nullptr, 0, EPI_STORE)))
+        return rc;
+      GdnParams g{};
+      g.x = e->xb;
+      g.in_norm = an;
+      g.eps = c.rms_eps;
+      g.H = H;
+      g.nv = c.ssm_nv;
+      g.nk = c.ssm_nk;
+      g.dv = c.ssm_dv;
+      g.K = c.ssm_conv_kernel;
+      g.C = e->C;
+      g.qkv = e->qkvb;
+      g.conv_w = (const float*)L.conv1d->d;
+      g.ring = L.ring0;
+      g.w_alpha = (const float*)L.alpha->d;
+      g.w_beta = (const float*)L.beta->d;
+      g.ssm_a = (const float*)L.ssm_a->d;
+      g.dt_bias = (const float*)L.dt_bias->d;
+      g.S = L.S0;
+      g.y = e->yb;
+      g.step = e->gdn_steps + li;
+      g.done = L.done;
+      g.self_advance = 0;
+      g.z = e->zb;
+      g.out_norm = (const float*)L.ssm_norm->d;
+      g.xs = H;
+      g.qkvs = e->C;
+      g.zys = e->di;
+      g.Ss = (long long)c.ssm_nv * c.ssm_dv * c.ssm_dk;
+      g.rings = (long long)c.ssm_conv_kernel * e->C;
+      g.steps_stride = c.num_layers;
+      if ((rc = launch_gdn_head(g, e->st, false, B))) return rc;
+      mark(e, K_GDN);
+      if ((rc = bgemv(e, L.ssm_out, e->di, {M(L.ssm_out, e->xb)}, e->yb, B, e->di, H, PRO_NONE, nullptr, nullptr, 0,
+                      EPI_ADD)))
+        return rc;
+    } else {
+      if ((rc = bgemv(e, L.wq, H, {M(L.wq, e->qgb)}, e->xb, B, H, 2 * hdq, PRO_RMSNORM, an, nullptr, 0, EPI_STORE)))
+        return rc;
+      if (L.wk->type == L.wv->type) {
+        if ((rc = bgemv(e, L.wk, H, {M(L.wk, e->kb), M(L.wv, e->vb)}, e->xb, B, H, kvd, PRO_RMSNORM, an, nullptr, 0,
+                        EPI_STORE)))
+          return rc;
+      } else if ((rc = bgemv(e, L.wk, H, {M(L.wk, e->kb)}, e->xb, B, H, kvd, PRO_RMSNORM, an, nullptr, 0, EPI_STORE)) ||
+                 (rc = bgemv(e, L.wv, H, {M(L.wv, e->vb)}, e->xb, B, H, kvd, PRO_RMSNORM, an, nullptr, 0, EPI_STORE))) {
+        return rc;
+      }
+      AttnParams a{};
+      a.qg = e->qgb;
+      a.k = e->kb;
+      a.v = e->vb;
+      a.q_norm = (const float*)L.q_norm->d;
+      a.k_norm = (const float*)L.k_norm->d;
+      a.eps = c.rms_eps;
+      a.rope_cos = e->rope_cos;
+      a.rope_sin = e->rope_sin;
+      a.rd = e->rd;
+      a.kc = L.kc0;
+      a.vc = L.vc0;
+      a.nh = c.n_heads;
+      a.nkv = c.n_kv_heads;
+      a.ctx = c.max_ctx;
+      a.split_len = e->split_len;
+      a.nsplit = e->nsplit;
+      a.pos = e->bt_pos;
+      a.part_o = e->part_o;
+      a.part_ml = e->part_ml;
+      a.counters = e->att_counters;
+      a.out = e->ob;
+      a.err = e->err;
+      a.qgs = 2LL * hdq;
+      a.kvs = kvd;
+      a.outs = hdq;
+      a.caches = (long long)kvs;
+      if ((rc = launch_attn_decode(a, e->st, false, B))) return rc;
+      mark(e, K_ATTN);
+      if ((rc = bgemv(e, L.wo, hdq, {M(L.wo, e->xb)}, e->ob, B, hdq, H, PRO_NONE, nullptr, nullptr, 0, EPI_ADD)))
+        return rc;
+    }
+    DevTensor* down = L.ffn_down->type == T_Q6_KR ? &L.ffn_down_raw : L.ffn_down;
+    if ((rc = bgemv(e, L.ffn_gate, H, {M(L.ffn_gate, e->hb), M(L.ffn_up, nullptr)}, e->xb, B, H, I, PRO_RMSNORM,
+                    (const float*)L.post_norm->d, nullptr, 0, EPI_SWIGLU)) ||
+        (rc = bgemv(e, down, I, {M(down, e->xb)}, e->hb, B, I, H, PRO_NONE, nullptr, nullptr, 0, EPI_ADD)))
+      return rc;
+  }
+  // lm_head + first-max argmax per sequence (GGUF-layout rows, B columns)
+  {
+    GemvCall g;
+    g.type = e->lm_raw->type;
+    g.inner = H;
+    g.mats[0] = GemvMat{e->lm_raw->d, nullptr, (int)e->lm_raw->rows()};
+    g.nmats = 1;
+    g.nb = B;
+    g.x = e->xb;
+    g.x_stride = H;
+    g.y_stride = c.vocab_size;
+    g.pro = PRO_RMSNORM;
+    g.pro_w = (const float*)e->out_norm->d;
+    g.eps = c.rms_eps;
+    g.epi = EPI_ARGMAX;
+    g.argmax = e->bt_keys;
+    g.err = e->err;
+    if ((rc = launch_gemv(g, e->st, false))) return rc;
+    mark(e, K_LMHEAD);
+  }
+  batch_finalize_kernel<<<1, 128, 0, e->st>>>(B, c.num_layers, e->bt_keys, e->bt_tok, e->bt_pos, e->bt_out,
+                                              e->bt_step, e->gdn_steps);
+  INF_CUDA_TRY(cudaGetLastError());
+  return 0;
+}
+
+}  // namespace
+}  // namespace inf
+
+extern "C" {
+
+int inferno_select_sequence(InfernoEngine* e, int seq) {
+  if (!e || !e->finalized) return set_error(INFERNO_ESTATE, "select_sequence: engine not finalized");
+  INF_CUDA_TRY(cudaSetDevice(e->dev));
+  return inf::select_seq(e, seq);
+}
+
+int inferno_decode_batch(InfernoEngine* e, const int32_t* toks, const int32_t* pos, int B, int n_steps,
+                         int32_t* out_tokens) {
+  using namespace inf;
+  if (!e || !e->finalized) return set_error(INFERNO_ESTATE, "decode_batch: engine not finalized");
+  INF_CUDA_TRY(cudaSetDevice(e->dev));
+  const InfernoConfig& c = e->cfg;
+  if (!toks || !pos || !out_tokens || B < 1 || B > e->nseq || n_steps < 1)
+    return set_error(INFERNO_EINVAL, "decode_batch: B must be in [1, max_batch = %d]", e->nseq);
+  if (!e->xb) return set_error(INFERNO_ESTATE, "decode_batch: the batched buffers are not allocated");
+  for (int b = 0; b < B; ++b) {
+    if (toks[b] < 0 || toks[b] >= c.vocab_size) return set_error(INFERNO_EINVAL, "decode_batch: token out of range");
+    if (pos[b] < 0 || pos[b] + n_steps > c.max_ctx)
+      return set_error(INFERNO_EINVAL, "decode_batch: sequence %d positions exceed max_ctx", b);
+  }
+  int rc;
+  if (!e->bt_tok) {
+    if ((rc = dalloc(e, &e->bt_tok, e->nseq)) || (rc = dalloc(e, &e->bt_pos, e->nseq)) ||
+        (rc = dalloc(e, &e->bt_keys, e->nseq)) || (rc = dalloc(e, &e->bt_step, 1)))
+      return rc;
+  }
+  if (e->bt_out_cap < n_steps * B) {
+    if ((rc = dalloc(e, &e->bt_out, (size_t)n_steps * B))) return rc;
+    e->bt_out_cap = n_steps * B;
+  }
+  // the batched kernels address every sequence's slice from sequence 0's
+  if ((rc = select_seq(e, 0))) return rc;
+  INF_CUDA_TRY(cudaMemcpyAsync(e->bt_tok, toks, (size_t)B * 4, cudaMemcpyHostToDevice, e->st));
+  INF_CUDA_TRY(cudaMemcpyAsync(e->bt_pos, pos, (size_t)B * 4, cudaMemcpyHostToDevice, e->st));
+  INF_CUDA_TRY(cudaMemsetAsync(e->bt_keys, 0, (size_t)B * 8, e->st));
+  INF_CUDA_TRY(cudaMemsetAsync(e->bt_step, 0, 4, e->st));
+  cudaGraphExec_t ge = nullptr;
+  if (c.use_graphs) {
+    auto it = e->bt_graphs.find(B);
+    if (it == e->bt_graphs.end()) {
+      // first call for this B runs eagerly (kernel attributes, scratch), the
+      // step is captured once that worked
+      if ((rc = enqueue_batch_step(e, B))) return rc;
+      INF_CUDA_TRY(cudaStreamSynchronize(e->st));
+      cudaGraph_t g = nullptr;
+      INF_CUDA_TRY(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+      rc = enqueue_batch_step(e, B);
+      cudaError_t r1 = cudaStreamEndCapture(e->st, &g);
+      if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+      }
+      if (r1 != cudaSuccess) return set_error(INFERNO_ECUDA, "batch capture: %s", cudaGetErrorString(r1));
+      r1 = cudaGraphInstantiate(&ge, g, 0);
+      cudaGraphDestroy(g);
+      if (r1 != cudaSuccess) return set_error(INFERNO_ECUDA, "batch graph: %s", cudaGetErrorString(r1));
+      e->bt_graphs[B] = ge;
+      --n_steps;     // the eager step already ran
+    } else {
+      ge = it->second;
+    }
+  }
+  INF_CUDA_TRY(cudaEventRecord(e->ev0, e->st));
+  for (int t = 0; t < n_steps; ++t) {
+    if (ge) INF_CUDA_TRY(cudaGraphLaunch(ge, e->st));
+    else if ((rc = enqueue_batch_step(e, B))) return rc;
+  }
+  INF_CUDA_TRY(cudaEventRecord(e->ev1, e->st));
+  INF_CUDA_TRY(cudaStreamSynchronize(e->st));
+  float ms = 0.f;
+  cudaEventElapsedTime(&ms, e->ev0, e->ev1);
+  e->last_ms = ms;
+  int done_steps = 0;
+  INF_CUDA_TRY(cudaMemcpy(&done_steps, e->bt_step, 4, cudaMemcpyDeviceToHost));
+  INF_CUDA_TRY(cudaMemcpy(out_tokens, e->bt_out, (size_t)done_steps * B * 4, cudaMemcpyDeviceToHost));
+  return check_device_error(e);
 }
 
 }  // extern "C"

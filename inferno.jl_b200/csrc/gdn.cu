@@ -253,13 +253,21 @@ __global__ void __launch_bounds__(GH_THREADS, 1) gdn_head_kernel(const __grid_co
   __shared__ float red2[GH_THREADS / 32];
   __shared__ float gate_s[2];
   const int h = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int sb = blockIdx.y;                       // sequence (batched decode)
+  const float* X = p.x + sb * p.xs;
+  const float* QKV = p.qkv + sb * p.qkvs;
+  const float* Z = p.z + sb * p.zys;
+  float* Y = p.y + sb * p.zys;
+  float* SS = p.S + sb * p.Ss;
+  float* RING = p.ring + sb * p.rings;
+  const int* STEP = p.step + sb * p.steps_stride;
   const int g = h % p.nk, K = p.K, C = p.C, H = p.H, dv = p.dv;
   if (tid == 0) {
     KT_KIND(p.trace, KT_GDN);
     KT_FIRST(p.trace, 1);
   }
   // ---------------- pre-wait: state, weights, conv history ----------------
-  const int t = *p.step;
+  const int t = *STEP;
   const int cur = t % K;
   float* wa_s = gsm;
   float* wb_s = gsm + H;
@@ -272,7 +280,7 @@ __global__ void __launch_bounds__(GH_THREADS, 1) gdn_head_kernel(const __grid_co
   const int row = warp * 8 + (lane >> 2), seg = lane & 3;    // state row / 32-column segment
   const bool row_ok = row < dv;
   float4 s[8];
-  const float4* srow = (const float4*)(p.S + ((long long)h * dv + (row_ok ? row : 0)) * GDN_DK + 32 * seg);
+  const float4* srow = (const float4*)(SS + ((long long)h * dv + (row_ok ? row : 0)) * GDN_DK + 32 * seg);
 #pragma unroll
   for (int j = 0; j < 8; ++j) s[j] = row_ok ? srow[j] : make_float4(0.f, 0.f, 0.f, 0.f);
   // this thread's conv channel (q, k or v) and its history
@@ -289,7 +297,7 @@ __global__ void __launch_bounds__(GH_THREADS, 1) gdn_head_kernel(const __grid_co
       if (k < K - 1) {
         int slot = (t - (K - 1) + k) % K;
         if (slot < 0) slot += K;
-        hist[k] = p.ring[(long long)slot * C + ch];
+        hist[k] = RING[(long long)slot * C + ch];
       }
     }
   }
@@ -303,15 +311,15 @@ __global__ void __launch_bounds__(GH_THREADS, 1) gdn_head_kernel(const __grid_co
     KT_LAST(p.trace, 3);
   }
   // ---------------- everything that depends on the previous kernels ----------------
-  const float xin = ch >= 0 ? p.qkv[ch] : 0.f;
-  const float zr = (row_ok && seg == 0) ? p.z[h * dv + row] : 0.f;
+  const float xin = ch >= 0 ? QKV[ch] : 0.f;
+  const float zr = (row_ok && seg == 0) ? Z[h * dv + row] : 0.f;
   constexpr int XPT = GDN_MAX_H / GH_THREADS;   // x elements per thread (H <= 8192)
   float acc[5] = {0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int j = 0; j < XPT; ++j) {
     const int i = tid + j * GH_THREADS;
     if (i < H) {
-      const float xv = p.x[i], xw = xv * wn_s[i];
+      const float xv = X[i], xw = xv * wn_s[i];
       acc[0] = fmaf(xv, xv, acc[0]);
       acc[1] = fmaf(wa_s[i], xw, acc[1]);
       acc[2] = fmaf(wb_s[i], xw, acc[2]);
@@ -329,7 +337,7 @@ __global__ void __launch_bounds__(GH_THREADS, 1) gdn_head_kernel(const __grid_co
   else if (tid < 2 * GDN_DK) acc[4] = act * act;
   else if (ch >= 0) vrow[tid - 2 * GDN_DK] = act;
   // ring update (q / k channels by the group's first head only; no CTA reads slot `cur` in this step)
-  if (ch >= 0 && (tid >= 2 * GDN_DK || h == g)) p.ring[(long long)cur * C + ch] = xin;
+  if (ch >= 0 && (tid >= 2 * GDN_DK || h == g)) RING[(long long)cur * C + ch] = xin;
 #pragma unroll
   for (int i = 0; i < 5; ++i) acc[i] = warp_sum(acc[i]);
   if (lane == 0)
@@ -381,7 +389,7 @@ __global__ void __launch_bounds__(GH_THREADS, 1) gdn_head_kernel(const __grid_co
   y += __shfl_xor_sync(0xffffffffu, y, 1);
   y += __shfl_xor_sync(0xffffffffu, y, 2);
   if (row_ok) {
-    float4* so = (float4*)(p.S + ((long long)h * dv + row) * GDN_DK + 32 * seg);
+    float4* so = (float4*)(SS + ((long long)h * dv + row) * GDN_DK + 32 * seg);
 #pragma unroll
     for (int j = 0; j < 8; ++j) so[j] = s[j];
   }
@@ -396,12 +404,12 @@ __global__ void __launch_bounds__(GH_THREADS, 1) gdn_head_kernel(const __grid_co
   if (row_ok && seg == 0) {
     const float sc = 1.0f / sqrtf(ys / (float)dv + p.eps);
     const float v = y * sc * nw;
-    p.y[h * dv + row] = v * zr * (1.0f / (1.0f + expf(-zr)));
+    Y[h * dv + row] = v * zr * (1.0f / (1.0f + expf(-zr)));
   }
   if (tid == 0) KT_LAST(p.trace, 6);
 }
 
-int launch_gdn_head(const GdnParams& p, cudaStream_t st, bool pdl) {
+int launch_gdn_head(const GdnParams& p, cudaStream_t st, bool pdl, int nseq) {
   if (p.dv > GDN_DK || p.dv % 8 || p.K < 1 || p.K > GDN_MAXK || p.H % 4 || p.H > GDN_MAX_H || !p.z || !p.out_norm)
     return set_error(INFERNO_EINVAL, "gdn head: unsupported dims (dv=%d, K=%d, H=%d)", p.dv, p.K, p.H);
   static DeviceOnce once;
@@ -410,7 +418,7 @@ int launch_gdn_head(const GdnParams& p, cudaStream_t st, bool pdl) {
   });
   if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "GDN head attribute: %s", cudaGetErrorString(ea));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.nv);
+  cfg.gridDim = dim3(p.nv, nseq);
   cfg.blockDim = dim3(GH_THREADS);
   cfg.dynamicSmemBytes = (size_t)3 * p.H * 4;
   cfg.stream = st;

@@ -28,6 +28,11 @@ struct GdnParams {
   // SiLU(z) gate are applied in the step, y then holds the gated output
   const float* z = nullptr;        // [nv*dv] attn_gate GEMV output
   const float* out_norm = nullptr; // [dv] ssm_norm weight
+  // batched decode (gdn_head_kernel, blockIdx.y = sequence b): sequence b's
+  // x / qkv / z / y rows, state, conv ring and step counter sit these many
+  // elements after sequence 0's
+  long long xs = 0, qkvs = 0, zys = 0, Ss = 0, rings = 0;
+  int steps_stride = 0;
   unsigned long long* trace = nullptr;   // debug timeline slots (KT_*, common.cuh)
 };
 
@@ -50,13 +55,17 @@ struct AttnParams {
   int* counters;         // [nkv]
   float* out;            // [nh*hd] gated attention output
   int* err;
+  // batched decode (blockIdx.z = sequence b): b's qg / k / v / out rows and
+  // KV cache lie these many floats after sequence 0's; pos[b] is its position;
+  // part_o / part_ml / counters hold one block per sequence
+  long long qgs = 0, kvs = 0, outs = 0, caches = 0;
   unsigned long long* trace = nullptr;   // debug timeline slots (KT_*, common.cuh)
 };
 
 int launch_gdn_step(const GdnParams& p, cudaStream_t st, bool pdl);
 // one CTA per head, output norm + gate fused (y = gated output); the caller
 // advances the step counter
-int launch_gdn_head(const GdnParams& p, cudaStream_t st, bool pdl);
-int launch_attn_decode(const AttnParams& p, cudaStream_t st, bool pdl);
+int launch_gdn_head(const GdnParams& p, cudaStream_t st, bool pdl, int nseq = 1);
+int launch_attn_decode(const AttnParams& p, cudaStream_t st, bool pdl, int nseq = 1);
 
 }  // namespace inf

@@ -50,7 +50,7 @@ EXPORTS = [
     "inferno_state_import", "inferno_last_decode_ms", "inferno_engine_destroy",
     "inferno_state_save_device", "inferno_state_restore_device", "inferno_kernels_per_token",
     "inferno_profile_tokens", "inferno_gemv_host_noalloc", "inferno_debug_trace", "inferno_tp_unique_id",
-    "inferno_gdn_recurrence", "inferno_gdn_chunked", "inferno_attention_step", "inferno_forward_tokens_all", "inferno_debug_xch_timeout", "inferno_sample_logits", "inferno_decode_sample",
+    "inferno_gdn_recurrence", "inferno_gdn_chunked", "inferno_attention_step", "inferno_select_sequence", "inferno_decode_batch", "inferno_forward_tokens_all", "inferno_debug_xch_timeout", "inferno_sample_logits", "inferno_decode_sample",
     "inferno_gguf_open", "inferno_gguf_close", "inferno_gguf_version", "inferno_gguf_n_tensors", "inferno_gguf_n_kv",
     "inferno_gguf_data_offset", "inferno_gguf_key", "inferno_gguf_tensor_info", "inferno_gguf_get_int",
     "inferno_gguf_get_float", "inferno_gguf_get_string", "inferno_gguf_get_array", "inferno_engine_load_gguf",
@@ -94,6 +94,8 @@ def _sig(L0):
     L.inferno_layer_forward.argtypes = [p, i, p, i]
     L.inferno_forward_tokens.argtypes = [p, p, i, i, p, p]
     L.inferno_forward_tokens_all.argtypes = [p, p, i, i, p, p]
+    L.inferno_select_sequence.argtypes = [p, i]
+    L.inferno_decode_batch.argtypes = [p, p, p, i, i, p]
     L.inferno_decode_greedy.argtypes = [p, C.c_int32, i, i, p]
     L.inferno_reset_states.argtypes = [p]
     L.inferno_dump_hidden.argtypes = [p, i, p]

@@ -108,13 +108,14 @@ class Model:
 
     def __init__(self, spec: S.ModelSpec, tensors: dict, device: int = 0, max_ctx: int | None = None,
                  use_graphs: bool = True, use_pdl: bool = True, tp_rank: int = 0, tp_size: int = 1,
-                 tp_uid: bytes | None = None, gguf=None):
+                 tp_uid: bytes | None = None, gguf=None, max_batch: int = 1):
         """tp_size > 1: this process is rank `tp_rank` of a tensor-parallel group;
         `tensors` is the full model (sharded here, inferno_b200.tp) and
         `tp_uid` the group's NCCL unique id (Model.tp_unique_id() on rank 0,
         shared by the caller).  All ranks must construct concurrently.
         `gguf` (a gguf_file.GgufFile, one GPU): the weights are uploaded from
-        the file mapping by the library itself and `tensors` is not used."""
+        the file mapping by the library itself and `tensors` is not used.
+        `max_batch` > 1 keeps that many sequences' states for decode_batch."""
         self.spec = spec
         lspec = spec
         if gguf is not None and tp_size > 1:
@@ -137,7 +138,7 @@ class Model:
         c.max_ctx = max_ctx or spec.ctx
         c.n_experts, c.n_experts_used = spec.n_experts, spec.n_experts_used
         c.expert_ffn, c.shared_expert_ffn = spec.expert_ffn, spec.shexp_ffn
-        c.max_batch = 1
+        c.max_batch = int(max_batch)
         c.rms_eps, c.rope_theta, c.partial_rotary_factor = spec.eps, spec.rope_theta, spec.partial_rotary
         c.use_graphs, c.use_pdl = int(use_graphs), int(use_pdl)
         c.tp_rank, c.tp_size = tp_rank, tp_size
@@ -240,6 +241,22 @@ class Model:
             else:
                 break
         return accepted, logits
+
+    def select_sequence(self, seq: int):
+        """Point the single-sequence calls (forward, decode_greedy, layer,
+        reset excepted -- it clears every sequence) at state slice `seq`."""
+        call("inferno_select_sequence", self.h, int(seq))
+
+    def decode_batch(self, toks, positions, n: int) -> np.ndarray:
+        """Greedy decode of sequences 0..B-1 in lockstep: sequence b feeds
+        toks[b] at positions[b]; returns [n][B] tokens."""
+        t = np.ascontiguousarray(toks, dtype=np.int32).reshape(-1)
+        p = np.ascontiguousarray(positions, dtype=np.int32).reshape(-1)
+        if t.size != p.size:
+            raise ValueError("one token and one position per sequence")
+        out = np.zeros((n, t.size), np.int32)
+        call("inferno_decode_batch", self.h, _p(t), _p(p), int(t.size), int(n), _p(out))
+        return out
 
     def decode_greedy(self, tok: int, pos: int, n: int) -> np.ndarray:
         out = np.zeros(n, np.int32)
