@@ -446,6 +446,10 @@ BIG = {
                     metric="decode tokens/s @batch1 (Qwen3.5-9B-shaped hybrid, Q4_K_M mix, tensor parallel)"),
     # 35B-A3B-shaped MoE hybrid at batch 1, ctx 4096;
     # expert parallel over the launched ranks (strong scaling: one sequence)
+    # BASELINE configs[3] at batch 8: eight sequences (own 2048-token prompts)
+    # decoded in lockstep, one weight read per step for all eight
+    "config4-b8": dict(spec="qwen35-9b", prompt=2048, ndec=256, ctx=2048 + 256 + 64, tp=False, batch=8,
+                       metric="decode tokens/s @batch8 (Qwen3.5-9B-shaped hybrid, Q4_K_M mix, 8 sequences)"),
     "config5": dict(spec="qwen35-35b-a3b", prompt=32, ndec=128, ctx=4096 + 128, tp=True,
                     metric="decode tokens/s @batch1 (Qwen3.5-35B-A3B-shaped MoE hybrid, IQ2_XXS/Q4_K experts, "
                            "expert parallel)"),
@@ -486,19 +490,33 @@ def measure_big(workload, steps, warmup, ws, rank, local):
         uid = [Model.tp_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         kw = dict(tp_rank=rank, tp_size=ws, tp_uid=uid[0])
-    m = Model(spec, T, device=local, max_ctx=W["ctx"], **kw)
+    B = W.get("batch", 1)
+    m = Model(spec, T, device=local, max_ctx=W["ctx"], max_batch=B, **kw)
     P, ND = W["prompt"], W["ndec"]
     tok_bytes = algorithmic_bytes_per_token(spec, T, P + ND // 2)
     del T
-    prompt = S.tokens(SEED, P, spec.vocab)
-    t0 = time.perf_counter()
-    tok0, _ = m.forward(prompt, 0, want_logits=False)
-    prefill_s = time.perf_counter() - t0
+    if B == 1:
+        prompt = S.tokens(SEED, P, spec.vocab)
+        t0 = time.perf_counter()
+        tok0, _ = m.forward(prompt, 0, want_logits=False)
+        prefill_s = time.perf_counter() - t0
+    else:
+        # each sequence its own seeded prompt, prefilled into its own slice
+        toks0 = []
+        t0 = time.perf_counter()
+        for b in range(B):
+            m.select_sequence(b)
+            tb, _ = m.forward(S.tokens(SEED + b, P, spec.vocab), 0, want_logits=False)
+            toks0.append(tb)
+        prefill_s = (time.perf_counter() - t0) / B
+        m.select_sequence(0)
     m.save_device()
 
     def step():
         m.restore_device()
-        return m.decode_greedy(tok0, P, ND)
+        if B == 1:
+            return m.decode_greedy(tok0, P, ND)
+        return m.decode_batch(toks0, [P] * B, ND)
 
     for _ in range(max(1, warmup)):
         ref = step()
@@ -521,7 +539,7 @@ def measure_big(workload, steps, warmup, ws, rank, local):
     assert np.array_equal(out, ref), "decode is not deterministic across steps"
     ms_step = max_over_ranks(t_dev / steps)
     prefill_s = max_over_ranks(prefill_s)
-    seqs = 1 if tp else ws
+    seqs = (1 if tp else ws) * B
     value = seqs * ND / (ms_step / 1000.0)
     peaks = {}
     try:
@@ -529,14 +547,15 @@ def measure_big(workload, steps, warmup, ws, rank, local):
     except Exception:
         pass
     peak = float(peaks.get("hbm_gbs", 6650.0))
+    # weights are read once per batched step: bytes per step, not per token
     per_gpu_gbs = tok_bytes / (ws if tp else 1) / (ms_step / ND / 1000.0) / 1e9
     line = {"metric": W["metric"], "value": value, "unit": UNIT, "n_gpus": ws, "steps": steps,
             "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong" if tp else "weak", "vs_baseline": None,
             "dtype": "f32 (fp32 activations, GGUF block weights)",
             "data": "synthetic (seeded; rows of each matrix drawn from 256 quantized N(0,0.02) rows)",
-            "config": {"workload": f"{W['spec']}: {P}-token prompt (untimed), {ND} greedy decode tokens @batch1",
-                       "model": W["spec"], "global_batch": 1, "seq_len": P + ND,
+            "config": {"workload": f"{W['spec']}: {P}-token prompt (untimed), {ND} greedy decode tokens @batch{B}",
+                       "model": W["spec"], "global_batch": B, "seq_len": P + ND,
                        "parallelism": (("ep" if spec.n_experts else "tp") + str(ws)) if tp else
                                       ("replicas" if ws > 1 else "single"),
                        "l2": "weights per token >> 126 MB L2 (no flush needed)"},

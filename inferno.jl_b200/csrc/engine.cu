@@ -182,7 +182,11 @@ struct InfernoEngine {
   // advances its own)
   int* gdn_steps = nullptr;
   bool in_token = false, token_steps = false;
-  bool gdn_head = true;          // whole-head GDN kernel in decode tokens (INFERNO_GDN_HEAD=0: per-row-block)
+  // whole-head GDN kernel in batch-1 decode tokens (INFERNO_GDN_HEAD=1); off by
+  // default: 16 CTAs of 512 threads measured slower than 128 row-block CTAs
+  // plus the head-norm prologue of ssm_out (0.70 vs 0.66 ms/token, config 1).
+  // Batched decode always uses it (one CTA per head and sequence).
+  bool gdn_head = false;
   // batched decode: nseq = max_batch state slices; `cur_seq` is the slice the
   // single-sequence calls use; per batch size B one captured step graph
   int nseq = 1, cur_seq = 0;
@@ -301,7 +305,9 @@ GemvMat M(DevTensor* t, float* y) { return GemvMat{t->d, y, (int)t->rows()}; }
 // its partial to x, the other ranks store theirs, and one all-reduce (sum) of
 // x completes x + sum_r partial_r on every rank.
 int residual_epi(InfernoEngine* e) {
-  if (e->xch) return EPI_XCH_WRITE;
+  // expert parallel: the attention / GDN sublayers are replicated (local
+  // residual add); only the expert FFN's partial sums are exchanged
+  if (e->xch && e->tp) return EPI_XCH_WRITE;
   return (e->tp && e->cfg.tp_rank != 0) ? EPI_STORE : EPI_ADD;
 }
 
@@ -333,7 +339,7 @@ int enqueue_moe(InfernoEngine* e, LayerBind& L, bool pdl) {
   const bool shared = L.sh_gate != nullptr;
   const float* pn = (const float*)L.post_norm->d;
   int rc;
-  if ((rc = gemv(e, L.router->type, H, {M(L.router, e->moe_logits)}, e->x, PRO_RMSNORM, pn, nullptr, 0, EPI_STORE,
+  if ((rc = gemv(e, L.router->type, H, {M(L.router, e->moe_logits)}, e->xcur, PRO_RMSNORM, pn, nullptr, 0, EPI_STORE,
                  nullptr, pdl)))
     return rc;
   if ((rc = launch_moe_topk(e->moe_logits, E, K, e->moe_idx, e->moe_w, e->err, ebase, El, e->st, pdl))) return rc;
@@ -345,7 +351,7 @@ int enqueue_moe(InfernoEngine* e, LayerBind& L, bool pdl) {
     g.mats[0] = GemvMat{L.exp_gate->d, e->moe_h, K * Ie, 1, 0};
     g.mats[1] = GemvMat{L.exp_up->d, nullptr, K * Ie, 1, 0};
     g.nmats = 2;
-    g.x = e->x;
+    g.x = e->xcur;
     g.x_stride = H;
     g.pro = PRO_RMSNORM;
     g.pro_w = pn;
@@ -359,7 +365,7 @@ int enqueue_moe(InfernoEngine* e, LayerBind& L, bool pdl) {
     if ((rc = launch_gemv(g, e->st, pdl))) return rc;
     mark(e, K_GEMV);
   }
-  if (shared && (rc = gemv(e, L.sh_gate->type, H, {M(L.sh_gate, e->moe_h + (size_t)K * Ie), M(L.sh_up, nullptr)}, e->x,
+  if (shared && (rc = gemv(e, L.sh_gate->type, H, {M(L.sh_gate, e->moe_h + (size_t)K * Ie), M(L.sh_up, nullptr)}, e->xcur,
                            PRO_RMSNORM, pn, nullptr, 0, EPI_SWIGLU, nullptr, pdl)))
     return rc;
   {
@@ -383,7 +389,22 @@ int enqueue_moe(InfernoEngine* e, LayerBind& L, bool pdl) {
     if ((rc = launch_gemv(g, e->st, pdl))) return rc;
     mark(e, K_GEMV);
   }
-  if ((rc = launch_moe_combine(e->x, e->moe_y, e->moe_w, e->moe_idx, K, H, (shared && lead) ? 1 : 0, lead ? 1 : 0,
+  if (e->ep && e->xch) {
+    // partial sums to every rank's exchange buffer; the next RMSNorm GEMV adds them
+    MoeXch xc{};
+    for (int q = 0; q < c.tp_size; ++q) xc.parts[q] = e->xch_peer[q];
+    xc.seq = e->xch_seq;
+    xc.n = c.tp_size;
+    xc.rank = c.tp_rank;
+    xc.k = e->xch_k;
+    if ((rc = launch_moe_combine_xch(e->moe_y, e->moe_w, e->moe_idx, K, H, (shared && lead) ? 1 : 0, xc, e->st,
+                                     pdl)))
+      return rc;
+    mark(e, K_GEMV);
+    e->xch_pending = e->xch_k++;
+    return 0;
+  }
+  if ((rc = launch_moe_combine(e->xcur, e->moe_y, e->moe_w, e->moe_idx, K, H, (shared && lead) ? 1 : 0, lead ? 1 : 0,
                                 e->st, pdl)))
     return rc;
   mark(e, K_GEMV);
@@ -427,7 +448,7 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
       return rc;
     mark(e, K_GDN);
     xch_commit(e);
-    if (!(ab & 8) && (rc = gemv(e, L.ssm_out->type, e->di, {M(L.ssm_out, e->x)}, e->y, (ab & 128) ? PRO_NONE : PRO_HEADNORM_GATE,
+    if (!(ab & 8) && (rc = gemv(e, L.ssm_out->type, e->di, {M(L.ssm_out, e->xcur)}, e->y, (ab & 128) ? PRO_NONE : PRO_HEADNORM_GATE,
                    (const float*)L.ssm_norm->d, e->z, c.ssm_dv, residual_epi(e), nullptr, pdl)))
       return rc;
     if ((rc = tp_sum_x(e))) return rc;
@@ -480,7 +501,7 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     if (!(ab & 2) && (rc = head ? launch_gdn_head(g, e->st, pdl) : launch_gdn_step(g, e->st, pdl))) return rc;
     mark(e, K_GDN);
     const int sp = (head || (ab & 128)) ? PRO_NONE : PRO_HEADNORM_GATE;
-    if (!(ab & 8) && (rc = gemv(e, L.ssm_out->type, e->di, {M(L.ssm_out, e->x)}, e->y, sp,
+    if (!(ab & 8) && (rc = gemv(e, L.ssm_out->type, e->di, {M(L.ssm_out, e->xcur)}, e->y, sp,
                    (const float*)L.ssm_norm->d, e->z, c.ssm_dv, residual_epi(e), nullptr, pdl)))
       return rc;
     if ((rc = tp_sum_x(e))) return rc;
@@ -527,7 +548,7 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
     a.trace = trace_slot(e);
     if (!(ab & 4) && (rc = launch_attn_decode(a, e->st, pdl))) return rc;
     mark(e, K_ATTN);
-    if (!(ab & 8) && (rc = gemv(e, L.wo->type, c.n_heads * c.head_dim, {M(L.wo, e->x)}, e->o, PRO_NONE, nullptr, nullptr, 0,
+    if (!(ab & 8) && (rc = gemv(e, L.wo->type, c.n_heads * c.head_dim, {M(L.wo, e->xcur)}, e->o, PRO_NONE, nullptr, nullptr, 0,
                    residual_epi(e), nullptr, pdl)))
       return rc;
     if ((rc = tp_sum_x(e))) return rc;
@@ -535,7 +556,7 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
   if (c.n_experts) {
     if ((rc = enqueue_moe(e, L, pdl))) return rc;
     if (e->dump)
-      INF_CUDA_TRY(cudaMemcpyAsync(e->hidden + (size_t)li * H, e->x, (size_t)H * 4, cudaMemcpyDeviceToDevice, e->st));
+      INF_CUDA_TRY(cudaMemcpyAsync(e->hidden + (size_t)li * H, e->xcur, (size_t)H * 4, cudaMemcpyDeviceToDevice, e->st));
     return 0;
   }
   // FFN: SwiGLU(gate, up) on RMSNorm(x), then down with residual add
@@ -547,12 +568,12 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
   } else {
     return set_error(INFERNO_EINVAL, "layer %d: ffn_gate and ffn_up must share a type", li);
   }
-  if (!(ab & 32) && (rc = gemv(e, L.ffn_down->type, c.intermediate_size, {M(L.ffn_down, e->x)}, e->h, PRO_NONE, nullptr, nullptr,
+  if (!(ab & 32) && (rc = gemv(e, L.ffn_down->type, c.intermediate_size, {M(L.ffn_down, e->xcur)}, e->h, PRO_NONE, nullptr, nullptr,
                  0, residual_epi(e), nullptr, pdl)))
     return rc;
   if ((rc = tp_sum_x(e))) return rc;
   if (e->dump)
-    INF_CUDA_TRY(cudaMemcpyAsync(e->hidden + (size_t)li * H, e->x, (size_t)H * 4, cudaMemcpyDeviceToDevice, e->st));
+    INF_CUDA_TRY(cudaMemcpyAsync(e->hidden + (size_t)li * H, e->xcur, (size_t)H * 4, cudaMemcpyDeviceToDevice, e->st));
   return 0;
 }
 
@@ -865,13 +886,18 @@ int setup_xch(InfernoEngine* e) {
   auto ok = [](const DevTensor* t, int64_t inner) {
     return t && (t->type == T_Q4_K || t->type == T_Q6_K || t->type == T_Q6_KR) && inner % 256 == 0;
   };
+  // every GEMV that reads the exchanged residual (RMSNorm inputs) and, under
+  // tensor parallelism, every one that writes a partial runs on the
+  // tensor-core path; expert parallelism exchanges after the expert FFN,
+  // whose next reader is the next layer's first GEMV (or the lm_head)
   bool eligible = ok(e->lm_head, H);
   for (auto& L : e->layers) {
     if (L.ssm)
-      eligible = eligible && ok(L.in_proj, H) && ok(L.gate, H) && ok(L.ssm_out, e->di);
+      eligible = eligible && ok(L.in_proj, H) && ok(L.gate, H) && (e->ep || ok(L.ssm_out, e->di));
     else
-      eligible = eligible && ok(L.wq, H) && ok(L.wk, H) && ok(L.wv, H) && ok(L.wo, (int64_t)c.n_heads * c.head_dim);
-    eligible = eligible && ok(L.ffn_gate, H) && ok(L.ffn_up, H) && ok(L.ffn_down, c.intermediate_size);
+      eligible = eligible && ok(L.wq, H) && ok(L.wk, H) && ok(L.wv, H) &&
+                 (e->ep || ok(L.wo, (int64_t)c.n_heads * c.head_dim));
+    if (!e->ep) eligible = eligible && ok(L.ffn_gate, H) && ok(L.ffn_up, H) && ok(L.ffn_down, c.intermediate_size);
   }
   if (!eligible) return 0;
   int rc;
@@ -1325,7 +1351,7 @@ int inferno_engine_finalize(InfernoEngine* e) {
   for (auto& L : e->layers)
     if (L.wperm) e->token_steps = false;
   e->xcur = e->x;
-  if (e->tp && (rc = setup_xch(e))) return rc;
+  if ((e->tp || e->ep) && (rc = setup_xch(e))) return rc;
   {
     const char* np = getenv("INFERNO_B200_NO_PREFILL");
     e->prefill = !(np && atoi(np) != 0) && c.tp_size == 1 && !c.n_experts && !e->dump;
@@ -1780,7 +1806,7 @@ int build_persistent(InfernoEngine* e) {
     if ((rc = pk_add_gemv(e, v, L.ffn_gate->type, H, {M(L.ffn_gate, e->h), M(L.ffn_up, nullptr)}, e->x, PRO_RMSNORM,
                           (const float*)L.post_norm->d, nullptr, 0, EPI_SWIGLU, false)))
       return rc;
-    if ((rc = pk_add_gemv(e, v, L.ffn_down->type, c.intermediate_size, {M(L.ffn_down, e->x)}, e->h, PRO_NONE,
+    if ((rc = pk_add_gemv(e, v, L.ffn_down->type, c.intermediate_size, {M(L.ffn_down, e->xcur)}, e->h, PRO_NONE,
                           nullptr, nullptr, 0, EPI_ADD, false)))
       return rc;
   }

@@ -49,6 +49,7 @@ __global__ void __launch_bounds__(WY_THREADS) gdn_wy_prep_kernel(int T, int H, i
   float* As = Vs + WY_C * dv;            // [C][AP]  A, then T
   float* Gs = As + WY_C * AP;            // [C]
   float* Bs = Gs + WY_C;                 // [C]
+  float* Es = Bs + WY_C;                 // [C] e^{G_t}
   const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const int t0 = c * WY_C, n = min(WY_C, T - t0);
   for (int i = tid; i < WY_C * WY_DK; i += WY_THREADS) {
@@ -82,6 +83,7 @@ __global__ void __launch_bounds__(WY_THREADS) gdn_wy_prep_kernel(int T, int H, i
     Gs[2 * tid + 1] = s;
   }
   __syncthreads();
+  if (tid < WY_C) Es[tid] = expf(Gs[tid]);
   // A (strictly lower) and P = (Q K^T) o E (lower incl. diagonal)
   float* Pg = o.P + ((size_t)c * H + h) * WY_C * WY_C;
   for (int i = tid; i < WY_C * WY_C; i += WY_THREADS) {
@@ -121,7 +123,7 @@ __global__ void __launch_bounds__(WY_THREADS) gdn_wy_prep_kernel(int T, int H, i
   for (int i = tid; i < WY_C * WY_DK; i += WY_THREADS) {
     const int t = i / WY_DK, d = i % WY_DK;
     float w = 0.f;
-    for (int j = 0; j <= t; ++j) w = fmaf(As[t * AP + j] * expf(Gs[j]), Ks[j * KP + d], w);
+    for (int j = 0; j <= t; ++j) w = fmaf(As[t * AP + j] * Es[j], Ks[j * KP + d], w);
     Wg[i] = w;
   }
   for (int i = tid; i < WY_C * dv; i += WY_THREADS) {
@@ -147,6 +149,8 @@ __global__ void __launch_bounds__(WY_THREADS) gdn_wy_state_kernel(int T, int H, 
   float* Ds = Qs + WY_C * KP;               // [C][16]  D rows of this CTA
   float* Ps = Ds + WY_C * WY_ROWS;          // [C][C]
   float* Gs = Ps + WY_C * WY_C;             // [C]
+  float* EGs = Gs + WY_C;                   // [C] e^{G_t}
+  float* DEs = EGs + WY_C;                  // [C] e^{G_last - G_j}
   const int h = blockIdx.x, r0 = blockIdx.y * WY_ROWS, tid = threadIdx.x;
   for (int i = tid; i < WY_ROWS * WY_DK; i += WY_THREADS) {
     const int r = i / WY_DK, d = i % WY_DK;
@@ -166,7 +170,13 @@ __global__ void __launch_bounds__(WY_THREADS) gdn_wy_state_kernel(int T, int H, 
     }
     const float* Pg = o.P + ((size_t)c * H + h) * WY_C * WY_C;
     for (int i = tid; i < WY_C * WY_C; i += WY_THREADS) Ps[i] = Pg[i];
-    if (tid < WY_C) Gs[tid] = o.G[((size_t)c * H + h) * WY_C + tid];
+    if (tid < WY_C) {
+      const float gt = o.G[((size_t)c * H + h) * WY_C + tid];
+      const float glast = o.G[((size_t)c * H + h) * WY_C + (n - 1)];
+      Gs[tid] = gt;
+      EGs[tid] = expf(gt);
+      DEs[tid] = tid < n ? expf(glast - gt) : 0.f;
+    }
     __syncthreads();
     // D[t][i] = U[t][i] - W[t] . S[i]   (1024 entries, 4 per thread)
     const float* Ug = o.U + ((size_t)c * H + h) * WY_C * dv;
@@ -183,17 +193,17 @@ __global__ void __launch_bounds__(WY_THREADS) gdn_wy_state_kernel(int T, int H, 
       if (t >= n) continue;
       float qs = 0.f;
       for (int d = 0; d < WY_DK; ++d) qs = fmaf(Qs[t * KP + d], Ss[i * KP + d], qs);
-      float acc = expf(Gs[t]) * qs;
+      float acc = EGs[t] * qs;
       for (int j = 0; j <= t; ++j) acc = fmaf(Ps[t * WY_C + j], Ds[j * WY_ROWS + i], acc);
       y[((size_t)(t0 + t) * H + h) * dv + r0 + i] = acc;
     }
     __syncthreads();
     // S[i][d] = e^{G_last} S[i][d] + sum_j e^{G_last - G_j} D[j][i] K[j][d]
-    const float gl = Gs[n - 1];
+    const float egl = EGs[n - 1];
     for (int e = tid; e < WY_ROWS * WY_DK; e += WY_THREADS) {
       const int i = e / WY_DK, d = e % WY_DK;
-      float acc = expf(gl) * Ss[i * KP + d];
-      for (int j = 0; j < n; ++j) acc = fmaf(expf(gl - Gs[j]) * Ds[j * WY_ROWS + i], Ks[j * KP + d], acc);
+      float acc = egl * Ss[i * KP + d];
+      for (int j = 0; j < n; ++j) acc = fmaf(DEs[j] * Ds[j * WY_ROWS + i], Ks[j * KP + d], acc);
       Ss[i * KP + d] = acc;
     }
   }
@@ -220,9 +230,9 @@ int launch_gdn_wy(int T, int H, int dv, const float* q, const float* k, const fl
   o.U = o.W + nch * H * WY_C * WY_DK;
   o.P = o.U + nch * H * WY_C * dv;
   o.G = o.P + nch * H * WY_C * WY_C;
-  const size_t smem1 = ((size_t)2 * WY_C * (WY_DK + 1) + (size_t)WY_C * dv + (size_t)WY_C * (WY_C + 1) + 2 * WY_C) * 4;
+  const size_t smem1 = ((size_t)2 * WY_C * (WY_DK + 1) + (size_t)WY_C * dv + (size_t)WY_C * (WY_C + 1) + 3 * WY_C) * 4;
   const size_t smem2 = ((size_t)WY_ROWS * (WY_DK + 1) + 3 * (size_t)WY_C * (WY_DK + 1) + (size_t)WY_C * WY_ROWS +
-                        (size_t)WY_C * WY_C + WY_C) * 4;
+                        (size_t)WY_C * WY_C + 3 * WY_C) * 4;
   static DeviceOnce once;
   cudaError_t ea = once.run([] {
     cudaError_t e = cudaFuncSetAttribute(gdn_wy_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);

@@ -179,6 +179,14 @@ int launch_moe_topk(const float* logits, int E, int K, int* idx, float* wts, int
                     cudaStream_t st, bool pdl);
 int launch_moe_combine(float* x, const float* y, const float* wts, const int* idx, int K, int H, int shared,
                        int add_x, cudaStream_t st, bool pdl);
+// expert-parallel combine into the residual exchange (sync point k)
+struct MoeXch {
+  unsigned long long* parts[8];
+  const unsigned long long* seq;
+  int n, rank, k;
+};
+int launch_moe_combine_xch(const float* y, const float* wts, const int* idx, int K, int H, int shared,
+                           const MoeXch& xc, cudaStream_t st, bool pdl);
 // RoPE tables cos / sin [ctx][rd/2] (src/ModelCPU.jl:134-153: inv_freq in
 // Float64 rounded to Float32, angle in Float32, correctly rounded cos / sin)
 void build_rope(int ctx, int rd, float theta, std::vector<float>& cs, std::vector<float>& sn);

@@ -101,6 +101,28 @@ __global__ void moe_combine_kernel(float* x, const float* y, const float* wts, c
   x[j] = add_x ? __fadd_rn(x[j], acc) : acc;
 }
 
+// Expert parallelism over the fused residual exchange: this rank's partial
+// sum_i w_i y_i (+ the shared expert on rank 0), without x, goes to every
+// rank's exchange buffer as 64-bit {value, tag} words (sync point k, tag
+// *seq + k + 1); the next RMSNorm GEMV of every rank polls the tags and adds
+// x + sum over ranks in rank order (bit-identical on all ranks).
+__global__ void moe_combine_xch_kernel(const float* y, const float* wts, const int* idx, int K, int H, int shared,
+                                       MoeXch xc) {
+  pdl_wait();
+  pdl_trigger();
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= H) return;
+  float acc = 0.0f;
+  for (int i = 0; i < K; ++i)
+    if (idx[i] >= 0) acc = __fadd_rn(acc, __fmul_rn(wts[i], y[(long long)i * H + j]));
+  if (shared) acc = __fadd_rn(acc, y[(long long)K * H + j]);
+  const uint32_t tag = (uint32_t)(*xc.seq + (unsigned long long)xc.k + 1ull);
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(acc);
+  const size_t off = ((size_t)(xc.k & 1) * xc.n + xc.rank) * H + j;
+  for (int q = 0; q < xc.n; ++q)
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(xc.parts[q] + off), "l"(w) : "memory");
+}
+
 namespace {
 template <class F, class... A>
 int launch_pdl(F kern, dim3 grid, dim3 block, cudaStream_t st, bool pdl, A... args) {
@@ -129,6 +151,11 @@ int launch_moe_combine(float* x, const float* y, const float* wts, const int* id
                        int add_x, cudaStream_t st, bool pdl) {
   return launch_pdl(moe_combine_kernel, dim3((H + 255) / 256), dim3(256), st, pdl, x, y, wts, idx, K, H, shared,
                     add_x);
+}
+
+int launch_moe_combine_xch(const float* y, const float* wts, const int* idx, int K, int H, int shared,
+                           const MoeXch& xc, cudaStream_t st, bool pdl) {
+  return launch_pdl(moe_combine_xch_kernel, dim3((H + 255) / 256), dim3(256), st, pdl, y, wts, idx, K, H, shared, xc);
 }
 
 }  // namespace inf

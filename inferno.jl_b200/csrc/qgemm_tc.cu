@@ -40,7 +40,8 @@ namespace inf {
 
 constexpr int QG_M = 128;             // weight rows per tile (TMEM lanes)
 constexpr int QG_BK = 64;             // K per step (one 128-byte fp16 row)
-constexpr int QG_THREADS = 192;       // 6 warps
+constexpr int QG_DQ_WARPS = 16;       // dequantizing warps: four threads per weight row
+constexpr int QG_THREADS = 64 + 32 * QG_DQ_WARPS;
 constexpr int QG_ATILE = QG_M * 128;  // bytes of one fp16 A tile (16 KB)
 
 struct QgSeg {
@@ -172,6 +173,60 @@ __device__ __forceinline__ void qg_dequant(const uint8_t* rp, int ks, float (&w)
   }
 }
 
+// 16 fp32 weights of K step ks (0..3) of one super-block, segment seg (0..3)
+// of the step's 64: values 16*seg..16*seg+15, Dequant.jl's rounding order.
+template <int TYPE>
+__device__ __forceinline__ void qg_dequant16(const uint8_t* rp, int ks, int seg, float (&w)[16]) {
+  const int off = 16 * (seg & 1), half = seg >> 1;
+  if constexpr (TYPE == T_Q4_K || TYPE == T_Q5_K) {
+    const uint32_t dd = ld_u32(rp);
+    const float d = h2f_bits((uint16_t)(dd & 0xffff)), dmin = h2f_bits((uint16_t)(dd >> 16));
+    float sc, mn;
+    qg_kscale(rp + 4, 2 * ks + half, sc, mn);
+    const float d1 = d * sc, m1 = dmin * mn;
+    const uint8_t* qs = rp + (TYPE == T_Q4_K ? 16 : 48) + 32 * ks + off;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t v = ld_u32(qs + 4 * q);
+      uint32_t h = 0;
+      if constexpr (TYPE == T_Q5_K) h = ld_u32(rp + 16 + off + 4 * q);
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        uint32_t c = (v >> (8 * b + 4 * half)) & 15;
+        if constexpr (TYPE == T_Q5_K) c += ((h >> (8 * b + 2 * ks + half)) & 1) << 4;
+        w[4 * q + b] = d1 * (float)c - m1;
+      }
+    }
+  } else if constexpr (TYPE == T_Q6_K) {
+    const int ns = ks >> 1, hi = ks & 1;
+    const uint8_t* L = rp + 64 * ns + 32 * half + off;
+    const uint8_t* Hh = rp + 128 + 32 * ns + off;
+    const int8_t sci = (int8_t)rp[192 + 8 * ns + 4 * hi + 2 * half + (seg & 1)];
+    const float d = h2f_bits((uint16_t)(rp[208] | (rp[209] << 8)));
+    const float sd = d * (float)sci;
+    const int qsh = 4 * hi, hsh = 2 * half + 4 * hi;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t la = ld_u32(L + 4 * q), hh = ld_u32(Hh + 4 * q);
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t a = (la >> (8 * b)) & 0xff, hv = (hh >> (8 * b)) & 0xff;
+        const int qv = (int)(((a >> qsh) & 15) | (((hv >> hsh) & 3) << 4)) - 32;
+        w[4 * q + b] = sd * (float)qv;
+      }
+    }
+  } else {   // Q8_0: block 2ks + half of the eight 34-byte blocks
+    const uint8_t* b = rp + 34 * (2 * ks + half);
+    const float d = h2f_bits((uint16_t)(b[0] | (b[1] << 8)));
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t v = ld_u32(b + 2 + off + 4 * q);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) w[4 * q + e] = d * (float)(int8_t)((v >> (8 * e)) & 0xff);
+    }
+  }
+}
+
 __device__ __forceinline__ int qg_exp_for(float bound) {
   // power of two that brings `bound` just under 2^14 (fp16 max is 65504)
   if (!(bound > 0.f) || !(bound <= 3.0e38f)) return 0;
@@ -220,8 +275,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&raw_full[i], 1);
-      mbar_init(&raw_empty[i], 4);
-      mbar_init(&a_full[i], 4);
+      mbar_init(&raw_empty[i], QG_DQ_WARPS);
+      mbar_init(&a_full[i], QG_DQ_WARPS);
       mbar_init(&a_empty[i], 1);
     }
     mbar_init(acc_full, 1);
@@ -323,15 +378,15 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     __syncwarp();
   } else {
     // ================= dequantize, then epilogue =================
-    const int q = warp & 3;                 // TMEM lane quarter of this warp
-    const int r = 32 * q + lane;            // tile row of this thread
-    int s = sg, row = r0 + r;
+    // dequantization: thread (row dr, segment dseg) of warps 2..17
+    const int du = tid - 64, dr = du >> 2, dseg = du & 3;
+    int ds = sg, drow = r0 + dr;
     if (swiglu) {
-      s = r < 64 ? 0 : 1;
-      row = r0 + (r & 63);
+      ds = dr < 64 ? 0 : 1;
+      drow = r0 + (dr & 63);
     }
-    const bool valid = row < p.seg[s].rows;
-    const uintptr_t rowsrc = valid ? (uintptr_t)(p.seg[s].W + (long long)row * p.row_bytes) : 0;
+    const bool dvalid = drow < p.seg[ds].rows;
+    const uintptr_t rowsrc = dvalid ? (uintptr_t)(p.seg[ds].W + (long long)drow * p.row_bytes) : 0;
     const int sw = qg_exp_for(*p.wbound);
     const float wscale = ldexpf(1.0f, sw);
     bool ok = true;
@@ -341,28 +396,29 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       if (ok && i >= 2) ok = mbar_wait(&a_empty[as], ((i >> 1) - 1) & 1, p.err);
       if (!ok) break;
       uint8_t* ah = sA + (size_t)as * nsplit * QG_ATILE;
-      float w[64];
-      if (valid) {
+      float w[16];
+      if (dvalid) {
         const uintptr_t a = rowsrc + (uintptr_t)sb * QgBlk<TYPE>::BB;
-        const uint8_t* rp = sRaw + ((size_t)rs * QG_M + r) * p.slot + (a & 15);
-        qg_dequant<TYPE>(rp, ks, w);
+        const uint8_t* rp = sRaw + ((size_t)rs * QG_M + dr) * p.slot + (a & 15);
+        qg_dequant16<TYPE>(rp, ks, dseg, w);
       } else {
 #pragma unroll
-        for (int e = 0; e < 64; ++e) w[e] = 0.f;
+        for (int e = 0; e < 16; ++e) w[e] = 0.f;
       }
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int cc = 0; cc < 2; ++cc) {
         uint32_t h[4], l[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float x0 = w[8 * c + 2 * e] * wscale, x1 = w[8 * c + 2 * e + 1] * wscale;
+          const float x0 = w[8 * cc + 2 * e] * wscale, x1 = w[8 * cc + 2 * e + 1] * wscale;
           const __half2 hh = __floats2half2_rn(x0, x1);
           const float2 hf = __half22float2(hh);
           h[e] = *(const uint32_t*)&hh;
           l[e] = pack_h2(x0 - hf.x, x1 - hf.y);
         }
-        *(uint4*)(ah + sw128_off(r, c)) = make_uint4(h[0], h[1], h[2], h[3]);
-        if (split) *(uint4*)(ah + QG_ATILE + sw128_off(r, c)) = make_uint4(l[0], l[1], l[2], l[3]);
+        const int c = 2 * dseg + cc;
+        *(uint4*)(ah + sw128_off(dr, c)) = make_uint4(h[0], h[1], h[2], h[3]);
+        if (split) *(uint4*)(ah + QG_ATILE + sw128_off(dr, c)) = make_uint4(l[0], l[1], l[2], l[3]);
       }
       fence_proxy_async_smem();
       __syncwarp();
@@ -371,6 +427,16 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         if (ks == 3) mbar_arrive(&raw_empty[rs]);
       }
     }
+    // the epilogue: warps 2..5, one TMEM lane quarter each (thread = tile row)
+    const int q = warp & 3;
+    const int r = 32 * q + lane;
+    int s = sg, row = r0 + r;
+    if (swiglu) {
+      s = r < 64 ? 0 : 1;
+      row = r0 + (r & 63);
+    }
+    const bool valid = row < p.seg[s].rows;
+    if (warp < 6) {
     // ---- epilogue ----
     if (ok) ok = mbar_wait(acc_full, 0, p.err);
     tc_fence_after();
@@ -407,6 +473,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         }
       }
     }
+    }   // warp < 6
   }
   tc_fence_before();
   __syncthreads();
