@@ -450,6 +450,10 @@ BIG = {
     # decoded in lockstep, one weight read per step for all eight
     "config4-b8": dict(spec="qwen35-9b", prompt=2048, ndec=256, ctx=2048 + 256 + 64, tp=False, batch=8,
                        metric="decode tokens/s @batch8 (Qwen3.5-9B-shaped hybrid, Q4_K_M mix, 8 sequences)"),
+    # BASELINE configs[4] at batch 16: sixteen sequences in lockstep (attention /
+    # GDN / router batched over the sequences, each token's experts its own)
+    "config5-b16": dict(spec="qwen35-35b-a3b", prompt=32, ndec=128, ctx=4096 + 128, tp=False, batch=16,
+                        metric="decode tokens/s @batch16 (Qwen3.5-35B-A3B-shaped MoE hybrid, 16 sequences)"),
     "config5": dict(spec="qwen35-35b-a3b", prompt=32, ndec=128, ctx=4096 + 128, tp=True,
                     metric="decode tokens/s @batch1 (Qwen3.5-35B-A3B-shaped MoE hybrid, IQ2_XXS/Q4_K experts, "
                            "expert parallel)"),
@@ -690,6 +694,79 @@ def run_gdn(args):
     return 0
 
 
+GEMM_TYPES = {"Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "Q8_0": 8, "IQ2_XXS": 16}
+
+
+def run_gemm(args):
+    """the quantized GEMV / GEMM microbench.  One shape
+    (--shape OUTxIN), type and batch; seeded random GGUF blocks; y = W x for
+    `batch` columns through inferno_gemv (batch >= 16 of Q4_K / Q5_K / Q6_K /
+    Q8_0 runs the tcgen05 GEMM).  Reports weight GB/s against the HBM peak
+    and, for batch >= 16, TFLOP/s against the bf16 tensor peak."""
+    import ctypes as C
+    import torch
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    sys.path.insert(0, str(ROOT / "tests"))
+    from q8k_cases import random_blocks
+    from inferno_b200._lib import call
+    rows, inner = (int(v) for v in args.shape.split("x"))
+    t = GEMM_TYPES[args.type]
+    qk, bb = (32, 34) if t == 8 else (256, {12: 144, 13: 176, 14: 210, 16: 66}[t])
+    rng = np.random.default_rng(SEED)
+    W = random_blocks(rng, t, rows * inner // qk)
+    x = rng.standard_normal((args.batch, inner)).astype(np.float32)
+    dW, dx = torch.from_numpy(W).cuda(), torch.from_numpy(x).cuda()
+    dy = torch.empty((args.batch, rows), dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream()
+    P = lambda a: C.c_void_p(a.data_ptr())  # noqa: E731
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")     # > L2 (126 MB)
+
+    def step():
+        call("inferno_gemv", t, P(dW), P(dx), P(dy), inner, rows, args.batch, C.c_void_p(st.cuda_stream))
+
+    for _ in range(args.warmup):
+        step()
+    clocks = ClockSampler(local)
+    clocks.start()
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        step()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    clk = clocks.stop()
+    ms = max_over_ranks(float(np.median(times)))
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    wbytes = W.nbytes + 4 * args.batch * (inner + rows)
+    gbs = wbytes / (ms / 1000.0) / 1e9
+    tflops = 2.0 * rows * inner * args.batch / (ms / 1000.0) / 1e12
+    tc = args.batch >= 16 and t != 16
+    line = {"metric": f"quantized GEMV/GEMM {args.type} {rows}x{inner} batch {args.batch}",
+            "value": ws * gbs if not tc else ws * tflops, "unit": "GB/s" if not tc else "TFLOP/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16 hi/lo split (tensor cores)" if tc else "f32",
+            "data": "synthetic (seeded random GGUF blocks, N(0,1) activations)",
+            "config": {"workload": f"config2 {args.type} {rows}x{inner} @batch{args.batch}", "model": "gemm",
+                       "global_batch": args.batch, "seq_len": 1, "parallelism": "replicas",
+                       "l2": "256 MB written between timed launches (L2 flush)"},
+            "clocks": clk, "weight_gbs": gbs, "tflops": tflops,
+            "hbm_frac": gbs / float(peaks.get("hbm_gbs", 6650.0)),
+            "tensor_frac": (tflops / float(peaks.get("bf16_tflops", 1590.0)) / 3.0) if tc else None,
+            "tensor_note": "three fp16 MMAs per product (hi*hi + hi*lo + lo*hi): tensor_frac counts the "
+                           "issued MMA work against the bf16 peak" if tc else None}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_prefill(args):
     """Prompt processing of the config-1 model: Model.forward over the 32-token
     seeded prompt (chunked prefill, 8 tokens per chunk).  The first call runs
@@ -736,7 +813,7 @@ def run_prefill(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", default="config1", choices=["config1", "config3", "prefill1"] + sorted(BIG),
+    ap.add_argument("--workload", default="config1", choices=["config1", "config3", "prefill1", "gemm"] + sorted(BIG),
                     help="config1 (the headline metric, default), config3 / config4 / config5, or prefill1 "
                          "(config-1 prompt processing)")
     ap.add_argument("--gpus", type=int, default=1)
@@ -744,6 +821,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shape", default="12288x4096", help="gemm workload: OUTxIN")
+    ap.add_argument("--type", default="Q4_K", choices=sorted(GEMM_TYPES), help="gemm workload: weight type")
+    ap.add_argument("--batch", type=int, default=128, help="gemm workload: columns")
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the config-4 (tensor parallel) / config-5 (expert parallel) keys of the config-1 line")
     args = ap.parse_args()
@@ -753,6 +833,8 @@ def main():
         return run_gdn(args)
     if args.workload == "prefill1":
         return run_prefill(args)
+    if args.workload == "gemm":
+        return run_gemm(args)
     if args.workload != "config1":
         return run_big(args)
     return run_ours(args)

@@ -578,9 +578,11 @@ int enqueue_layer(InfernoEngine* e, int li, bool pdl) {
 }
 
 // batched GEMV over T token columns (x rows x_stride apart, y rows y_stride apart)
+// (reuse_act: the previous bgemv converted the same input with the same
+// prologue; its fp16 activation rows are used again)
 int bgemv(InfernoEngine* e, const DevTensor* W, int inner, std::initializer_list<GemvMat> mats, const float* x,
           int T, long long x_stride, long long y_stride, int pro, const float* pro_w, const float* pro_z, int group,
-          int epi) {
+          int epi, bool reuse_act = false) {
   GemvCall c;
   c.type = W->type;
   c.inner = inner;
@@ -598,10 +600,13 @@ int bgemv(InfernoEngine* e, const DevTensor* W, int inner, std::initializer_list
   c.err = e->err;
   if (T >= PF_TC_MIN_T && e->pf_xhi && W->wb && qgemm_supported(W->type) && epi != EPI_ARGMAX && inner % 256 == 0) {
     // fp16 hi / lo activations with the prologue applied, then the tcgen05 GEMM
-    int rc = launch_qgemm_act(x, x_stride, inner, T, pro, pro_w, pro_z, group, e->cfg.rms_eps, e->pf_xhi,
-                              e->pf_xlo, e->pf_xexp, e->st, false);
-    if (rc) return rc;
-    mark(e, K_GEMV);
+    int rc = 0;
+    if (!reuse_act) {
+      rc = launch_qgemm_act(x, x_stride, inner, T, pro, pro_w, pro_z, group, e->cfg.rms_eps, e->pf_xhi, e->pf_xlo,
+                            e->pf_xexp, e->st, false);
+      if (rc) return rc;
+      mark(e, K_GEMV);
+    }
     QgemmCall q;
     q.type = W->type;
     q.K = inner;
@@ -640,7 +645,8 @@ int enqueue_prefill_chunk(InfernoEngine* e, const int* toks, int T, int pos0, bo
     if (L.ssm) {
       if ((rc = bgemv(e, L.in_proj, H, {M(L.in_proj, e->qkvb)}, e->xb, T, H, e->C, PRO_RMSNORM, an, nullptr, 0,
                       EPI_STORE)) ||
-          (rc = bgemv(e, L.gate, H, {M(L.gate, e->zb)}, e->xb, T, H, e->di, PRO_RMSNORM, an, nullptr, 0, EPI_STORE)))
+          (rc = bgemv(e, L.gate, H, {M(L.gate, e->zb)}, e->xb, T, H, e->di, PRO_RMSNORM, an, nullptr, 0, EPI_STORE,
+                      L.in_proj->wb && L.gate->wb)))
         return rc;
       GdnParams g{};
       g.x = e->xb;
@@ -678,7 +684,7 @@ int enqueue_prefill_chunk(InfernoEngine* e, const int* toks, int T, int pos0, bo
         return rc;
       if (L.wk->type == L.wv->type) {
         if ((rc = bgemv(e, L.wk, H, {M(L.wk, e->kb), M(L.wv, e->vb)}, e->xb, T, H, kvd, PRO_RMSNORM, an, nullptr, 0,
-                        EPI_STORE)))
+                        EPI_STORE, L.wq->wb && L.wk->wb)))
           return rc;
       } else if ((rc = bgemv(e, L.wk, H, {M(L.wk, e->kb)}, e->xb, T, H, kvd, PRO_RMSNORM, an, nullptr, 0, EPI_STORE)) ||
                  (rc = bgemv(e, L.wv, H, {M(L.wv, e->vb)}, e->xb, T, H, kvd, PRO_RMSNORM, an, nullptr, 0, EPI_STORE))) {
@@ -1011,8 +1017,8 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
   if (c.max_ctx <= 0) return set_error(INFERNO_EINVAL, "engine_create: max_ctx must be positive");
   if (c.max_batch < 0 || c.max_batch > PF_MAX_T)
     return set_error(INFERNO_EINVAL, "engine_create: max_batch %d outside [1, %d]", c.max_batch, PF_MAX_T);
-  if (c.max_batch > 1 && (c.tp_size > 1 || c.n_experts))
-    return set_error(INFERNO_EINVAL, "engine_create: batched decode needs a dense model on one GPU");
+  if (c.max_batch > 1 && c.tp_size > 1)
+    return set_error(INFERNO_EINVAL, "engine_create: batched decode runs on one GPU (tp_size 1)");
   if (c.tp_size < 1 || c.tp_rank < 0 || c.tp_rank >= c.tp_size)
     return set_error(INFERNO_EINVAL, "engine_create: tp_rank %d / tp_size %d", c.tp_rank, c.tp_size);
   if (c.tp_size > 1 && !c.nccl_unique_id)
@@ -1490,7 +1496,8 @@ int enqueue_batch_step(InfernoEngine* e, int B) {
     if (L.ssm) {
       if ((rc = bgemv(e, L.in_proj, H, {M(L.in_proj, e->qkvb)}, e->xb, B, H, e->C, PRO_RMSNORM, an, nullptr, 0,
                       EPI_STORE)) ||
-          (rc = bgemv(e, L.gate, H, {M(L.gate, e->zb)}, e->xb, B, H, e->di, PRO_RMSNORM, an, nullptr, 0, EPI_STORE)))
+          (rc = bgemv(e, L.gate, H, {M(L.gate, e->zb)}, e->xb, B, H, e->di, PRO_RMSNORM, an, nullptr, 0, EPI_STORE,
+                      L.in_proj->wb && L.gate->wb)))
         return rc;
       GdnParams g{};
       g.x = e->xb;
@@ -1532,7 +1539,7 @@ int enqueue_batch_step(InfernoEngine* e, int B) {
         return rc;
       if (L.wk->type == L.wv->type) {
         if ((rc = bgemv(e, L.wk, H, {M(L.wk, e->kb), M(L.wv, e->vb)}, e->xb, B, H, kvd, PRO_RMSNORM, an, nullptr, 0,
-                        EPI_STORE)))
+                        EPI_STORE, L.wq->wb && L.wk->wb)))
           return rc;
       } else if ((rc = bgemv(e, L.wk, H, {M(L.wk, e->kb)}, e->xb, B, H, kvd, PRO_RMSNORM, an, nullptr, 0, EPI_STORE)) ||
                  (rc = bgemv(e, L.wv, H, {M(L.wv, e->vb)}, e->xb, B, H, kvd, PRO_RMSNORM, an, nullptr, 0, EPI_STORE))) {
@@ -1569,6 +1576,20 @@ int enqueue_batch_step(InfernoEngine* e, int B) {
       mark(e, K_ATTN);
       if ((rc = bgemv(e, L.wo, hdq, {M(L.wo, e->xb)}, e->ob, B, hdq, H, PRO_NONE, nullptr, nullptr, 0, EPI_ADD)))
         return rc;
+    }
+    if (c.n_experts) {
+      // MoE FFN per sequence (each token routes to its own experts, as the
+      // reference's token loop does, src/Model.jl:478-561): the
+      // single-token expert chain on column b
+      for (int b = 0; b < B; ++b) {
+        e->xcur = e->xb + (size_t)b * H;
+        if ((rc = enqueue_moe(e, L, false))) {
+          e->xcur = e->x;
+          return rc;
+        }
+      }
+      e->xcur = e->x;
+      continue;
     }
     DevTensor* down = L.ffn_down->type == T_Q6_KR ? &L.ffn_down_raw : L.ffn_down;
     if ((rc = bgemv(e, L.ffn_gate, H, {M(L.ffn_gate, e->hb), M(L.ffn_up, nullptr)}, e->xb, B, H, I, PRO_RMSNORM,

@@ -41,3 +41,27 @@ def test_decode_batch_matches_oracle_per_sequence(tiny, B):
     m.close()
     for b in range(B):
         assert out[:, b].tolist() == want[b], b
+
+
+def test_decode_batch_moe_matches_oracle_per_sequence():
+    """tiny-moe at B = 4: every sequence's token routes to its own experts."""
+    spec = S.CONFIGS["tiny-moe"]
+    T = S.make_model(spec, seed=43)
+    orc = O.OracleModel(spec, T)
+    B, n = 4, 10
+    m = Model(spec, T, max_batch=B)
+    m.reset()
+    toks, pos, want = [], [], []
+    for b in range(B):
+        prompt = S.tokens(200 + b, 4 + 3 * b, spec.vocab)
+        m.select_sequence(b)
+        first, _ = m.forward(prompt, 0, want_logits=False)
+        toks.append(first)
+        pos.append(len(prompt))
+        ref = orc.generate(prompt, n + 1)
+        assert ref[0] == first
+        want.append(ref[1:])
+    out = m.decode_batch(toks, pos, n)
+    m.close()
+    for b in range(B):
+        assert out[:, b].tolist() == want[b], b
