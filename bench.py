@@ -446,6 +446,9 @@ BIG = {
                     metric="decode tokens/s @batch1 (Qwen3.5-9B-shaped hybrid, Q4_K_M mix, tensor parallel)"),
     # 35B-A3B-shaped MoE hybrid at batch 1, ctx 4096;
     # expert parallel over the launched ranks (strong scaling: one sequence)
+    # the config-1 model at batch 8 (eight sequences, own 32-token prompts)
+    "config1-b8": dict(spec="qwen35-0.8b", prompt=32, ndec=128, ctx=512, tp=False, batch=8,
+                       metric="decode tokens/s @batch8 (Qwen3.5-0.8B-shaped hybrid, 8 sequences)"),
     # BASELINE configs[3] at batch 8: eight sequences (own 2048-token prompts)
     # decoded in lockstep, one weight read per step for all eight
     "config4-b8": dict(spec="qwen35-9b", prompt=2048, ndec=256, ctx=2048 + 256 + 64, tp=False, batch=8,

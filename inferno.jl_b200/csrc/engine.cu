@@ -1059,6 +1059,11 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
   }
   if (const char* sp = getenv("INFERNO_XCH_SPIN")) e->xch_spin = (unsigned)strtoul(sp, nullptr, 0);
   if (const char* gh = getenv("INFERNO_GDN_HEAD")) e->gdn_head = atoi(gh) != 0;
+  // the per-layer hidden dump (INFERNO_B200_DUMP) uses the row-block GDN
+  // kernel: with the whole-head kernel the dumped run came out wrong (layer 0
+  // at 5e-2) while the same kernel matched the oracle in graph replays and in
+  // batched decode; the cause is not identified
+  if (e->dump) e->gdn_head = false;
   const char* d = getenv("INFERNO_B200_DUMP");
   e->dump = d && atoi(d) != 0;
   if (const char* ab = getenv("INFERNO_B200_ABLATE")) e->ablate = (unsigned)strtoul(ab, nullptr, 0);
