@@ -144,6 +144,8 @@ struct InfernoEngine {
   // tensor-core prefill: fp16 hi / lo activation rows [PF_MAX_T][max inner],
   // token exponents, the GDN prep rows and the weight bounds
   __half *pf_xhi = nullptr, *pf_xlo = nullptr;
+  float* qg_ws = nullptr;          // split-K workspace of the tensor-core GEMM
+  int* qg_tickets = nullptr;
   float* pf_xexp = nullptr;
   inf::GdnScratch pf_gdn{};
   float* pf_wbounds = nullptr;
@@ -619,6 +621,8 @@ int bgemv(InfernoEngine* e, const DevTensor* W, int inner, std::initializer_list
     q.epi = epi == EPI_ADD ? 1 : epi == EPI_SWIGLU ? 2 : 0;
     q.wbound = W->wb;
     q.err = e->err;
+    q.ws = e->qg_ws;
+    q.tickets = e->qg_tickets;
     rc = launch_qgemm(q, e->st, false);
     if (!rc) mark(e, K_GEMV);
     return rc;
@@ -962,7 +966,8 @@ int setup_tc_prefill(InfernoEngine* e) {
   const size_t rows = (size_t)qgemm_rows_padded(PF_MAX_T);
   int rc;
   if ((rc = dalloc(e, (uint16_t**)&e->pf_xhi, rows * kmax)) || (rc = dalloc(e, (uint16_t**)&e->pf_xlo, rows * kmax)) ||
-      (rc = dalloc(e, &e->pf_xexp, rows)))
+      (rc = dalloc(e, &e->pf_xexp, rows)) || (rc = dalloc(e, &e->qg_ws, qgemm_ws_bytes() / 4)) ||
+      (rc = dalloc(e, &e->qg_tickets, QGEMM_TICKETS)))
     return rc;
   if (e->C) {
     const size_t n = (size_t)PF_MAX_T * c.ssm_nv;
@@ -1059,11 +1064,6 @@ int inferno_engine_create(const InfernoConfig* cfg, InfernoEngine** out) {
   }
   if (const char* sp = getenv("INFERNO_XCH_SPIN")) e->xch_spin = (unsigned)strtoul(sp, nullptr, 0);
   if (const char* gh = getenv("INFERNO_GDN_HEAD")) e->gdn_head = atoi(gh) != 0;
-  // the per-layer hidden dump (INFERNO_B200_DUMP) uses the row-block GDN
-  // kernel: with the whole-head kernel the dumped run came out wrong (layer 0
-  // at 5e-2) while the same kernel matched the oracle in graph replays and in
-  // batched decode; the cause is not identified
-  if (e->dump) e->gdn_head = false;
   const char* d = getenv("INFERNO_B200_DUMP");
   e->dump = d && atoi(d) != 0;
   if (const char* ab = getenv("INFERNO_B200_ABLATE")) e->ablate = (unsigned)strtoul(ab, nullptr, 0);

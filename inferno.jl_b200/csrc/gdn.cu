@@ -306,6 +306,7 @@ __global__ void __launch_bounds__(GH_THREADS, 1) gdn_head_kernel(const __grid_co
 
   pdl_wait();
   pdl_trigger();
+  __syncthreads();   // the shared-memory weight rows (other threads' stores) are visible
   if (tid == 0) {
     KT_FIRST(p.trace, 2);
     KT_LAST(p.trace, 3);

@@ -111,7 +111,11 @@ struct QgemmCall {
   const float* wbound = nullptr;
   int* err = nullptr;
   bool split = true;           // hi/lo fp16 operand pairs (three MMAs) for fp32-level results
+  float* ws = nullptr;         // split-K workspace (qgemm_ws_bytes(); null: no split K)
+  int* tickets = nullptr;      // split-K tickets (QGEMM_TICKETS ints, zeroed once)
 };
+constexpr int QGEMM_TICKETS = 256;
+size_t qgemm_ws_bytes();
 bool qgemm_supported(int type);
 // token tile of the GEMM for T columns, and T rounded up to whole tiles (the
 // activation buffers hold that many rows)

@@ -6,19 +6,25 @@
 //
 // Per CTA: a 128-row tile of W (one matrix segment; for the SwiGLU pair 64
 // gate + 64 up rows) against a BN-token tile of X, K walked in steps of 64.
-//   warp 0      producer: raw GGUF super-blocks of the 128 rows by 1-D bulk
-//               copies (cp.async.bulk, aligned supersets for rows that do not
-//               start on 16 bytes), and the fp16 activation tiles by 2-D TMA
-//               (cp.async.bulk.tensor, SWIZZLE_128B, zero fill past T);
+//   warp 0      raw producer: the GGUF super-blocks of the 128 rows by
+//               16-byte cp.async (aligned supersets for rows that do not
+//               start on 16 bytes), lane = row, completion on an mbarrier;
 //   warp 1      allocates the TMEM accumulator (BN fp32 columns x 128 lanes)
 //               and issues tcgen05.mma from one thread;
-//   warps 2-5   dequantize: thread = weight row, 64 weights per K step with
-//               the fp32 arithmetic of Dequant.jl, written as fp16 into the
-//               canonical K-major SWIZZLE_128B operand tile; afterwards they
-//               drain the accumulator with tcgen05.ld and apply the epilogue.
-// Rings: raw super-blocks (2), dequantized A tiles (2), activation tiles
-// (NBS); every hand-off is an mbarrier, MMA completion is signalled with
+//   warp 2      activation producer: fp16 tiles by 2-D TMA
+//               (cp.async.bulk.tensor, SWIZZLE_128B, zero fill past T);
+//   warps 3-18  dequantize: four threads per weight row, 16 weights each per
+//               K step with the fp32 arithmetic of Dequant.jl, written as
+//               fp16 into the canonical K-major SWIZZLE_128B operand tile;
+//               warps 3-6 then drain the accumulator with tcgen05.ld and
+//               apply the epilogue.
+// Rings: raw super-blocks (NR), dequantized A tiles (NA), activation tiles
+// (NB); every hand-off is an mbarrier, MMA completion is signalled with
 // tcgen05.commit.  All waits are bounded and report DERR_MBAR_TIMEOUT.
+// Split K (grid.z slices of the super-blocks) fills the SMs when the output
+// has few tiles: each slice parks its fp32 tile in a workspace and the last
+// slice to arrive (atomic ticket) sums them in slice order and applies the
+// epilogue, so results do not depend on arrival order.
 //
 // Precision: with `split` the fp32 weight w and activation x are carried as
 // fp16 pairs (hi = fp16(w), lo = fp16(w - hi)) and the product is
@@ -41,7 +47,8 @@ namespace inf {
 constexpr int QG_M = 128;             // weight rows per tile (TMEM lanes)
 constexpr int QG_BK = 64;             // K per step (one 128-byte fp16 row)
 constexpr int QG_DQ_WARPS = 16;       // dequantizing warps: four threads per weight row
-constexpr int QG_THREADS = 64 + 32 * QG_DQ_WARPS;
+constexpr int QG_THREADS = 96 + 32 * QG_DQ_WARPS;
+constexpr int QG_WS_CTAS = 160;       // split-K is used while tiles x slices <= this (workspace bound)
 constexpr int QG_ATILE = QG_M * 128;  // bytes of one fp16 A tile (16 KB)
 
 struct QgSeg {
@@ -60,8 +67,11 @@ struct QgParams {
   int T;
   long long y_stride;    // floats between token rows of y
   int epi;               // QG_STORE / QG_ADD / QG_SWIGLU
-  int nbs;               // activation ring stages
+  int nbs, nas, nrs;     // ring stages: activation tiles, dequantized A tiles, raw super-blocks
   int split;
+  int trace;             // debug: %globaltimer stamps of CTA (0,0,0) into qg_trace
+  float* ws;             // split K: [tile][slice][BN][128] fp32 partial tiles
+  int* tickets;          // split K: arrivals per output tile (zero between launches)
   const float* xexp;     // [T] power-of-two exponent applied to each token's fp16 activations
   const float* wbound;   // bound of |w| over the matrix (weight scale)
   int* err;
@@ -240,6 +250,13 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *(const uint32_t*)&h;
 }
 
+// debug timeline of one CTA (QgParams::trace): 16 %globaltimer stamps
+__device__ unsigned long long qg_trace[16];
+#define QG_STAMP(i)                                                                          \
+  do {                                                                                       \
+    if (p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) qg_trace[i] = gtimer(); \
+  } while (0)
+
 template <int TYPE, int BN>
 __global__ void __launch_bounds__(QG_THREADS, 1)
     qgemm_tc_kernel(const __grid_constant__ QgParams p, const __grid_constant__ QgMaps maps) {
@@ -247,43 +264,49 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = p.split;
   const int nsplit = split ? 2 : 1;
+  const int NA = p.nas, NR = p.nrs, NB = p.nbs;
   // ---- shared memory carve-up (1024-byte aligned operand tiles) ----
   uint8_t* base = (uint8_t*)(((uintptr_t)qg_smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* sA = base;                                        // [2][nsplit][16 KB]
-  uint8_t* sB = sA + 2 * nsplit * QG_ATILE;                  // [nbs][nsplit][BN * 128]
+  uint8_t* sA = base;                                        // [NA][nsplit][16 KB]
+  uint8_t* sB = sA + (size_t)NA * nsplit * QG_ATILE;         // [NB][nsplit][BN * 128]
   const int btile = BN * 128;
-  uint8_t* sRaw = sB + (size_t)p.nbs * nsplit * btile;       // [2][128][slot]
-  uint64_t* bars = (uint64_t*)(sRaw + 2 * QG_M * p.slot);
-  uint64_t* raw_full = bars;        // 2
-  uint64_t* raw_empty = bars + 2;   // 2
-  uint64_t* a_full = bars + 4;      // 2
-  uint64_t* a_empty = bars + 6;     // 2
-  uint64_t* acc_full = bars + 8;    // 1
-  uint64_t* b_full = bars + 9;      // nbs
-  uint64_t* b_empty = b_full + p.nbs;
-  uint32_t* s_tmem = (uint32_t*)(b_empty + p.nbs);
+  uint8_t* sRaw = sB + (size_t)NB * nsplit * btile;          // [NR][128][slot]
+  uint64_t* bars = (uint64_t*)(sRaw + (size_t)NR * QG_M * p.slot);
+  uint64_t* raw_full = bars;             // NR
+  uint64_t* raw_empty = raw_full + NR;   // NR
+  uint64_t* a_full = raw_empty + NR;     // NA
+  uint64_t* a_empty = a_full + NA;       // NA
+  uint64_t* b_full = a_empty + NA;       // NB
+  uint64_t* b_empty = b_full + NB;       // NB
+  uint64_t* acc_full = b_empty + NB;     // 1
+  uint32_t* s_tmem = (uint32_t*)(acc_full + 1);
+  int* s_last = (int*)(s_tmem + 1);
 
-  // ---- tile coordinates ----
-  const int mt = blockIdx.x, t0 = blockIdx.y * BN;
+  // ---- tile coordinates; blockIdx.z = slice of the K super-blocks ----
+  const int mt = blockIdx.x, t0 = blockIdx.y * BN, kz = blockIdx.z, nz = gridDim.z;
   int sg = 0;
   while (sg + 1 < p.nseg && mt >= p.seg[sg + 1].mtile0) ++sg;
   const bool swiglu = p.epi == QG_SWIGLU;
   const int rows_per_tile = swiglu ? QG_M / 2 : QG_M;
   const int r0 = (mt - p.seg[sg].mtile0) * rows_per_tile;
-  const int nk = p.K / QG_BK;
+  if (tid == 0) QG_STAMP(0);
+  const int sb0 = (int)((long long)kz * p.nsb / nz), sb1 = (int)((long long)(kz + 1) * p.nsb / nz);
+  const int nsbz = sb1 - sb0, nk = 4 * nsbz;
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&raw_full[i], 1);
+    for (int i = 0; i < NR; ++i) {
+      mbar_init(&raw_full[i], 32);       // one cp.async arrival per producer lane
       mbar_init(&raw_empty[i], QG_DQ_WARPS);
+    }
+    for (int i = 0; i < NA; ++i) {
       mbar_init(&a_full[i], QG_DQ_WARPS);
       mbar_init(&a_empty[i], 1);
     }
-    mbar_init(acc_full, 1);
-    for (int i = 0; i < p.nbs; ++i) {
+    for (int i = 0; i < NB; ++i) {
       mbar_init(&b_full[i], 1);
       mbar_init(&b_empty[i], 1);
     }
+    mbar_init(acc_full, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
@@ -294,69 +317,68 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *s_tmem;
-  // activations, token exponents and (in the engine) residual rows come from
-  // the preceding kernels: every thread waits for them
-  pdl_wait();
 
   if (warp == 0) {
-    // ================= producer =================
-    // row r of the tile -> (matrix, row) and the bytes to copy
-    const uint32_t bx = (uint32_t)btile;
-    for (int sb = 0; sb < p.nsb; ++sb) {
-      const int rs = sb & 1;
-      if (sb >= 2 && !mbar_wait(&raw_empty[rs], ((sb >> 1) - 1) & 1, p.err)) break;
-      uint32_t bytes = 0;
-      uintptr_t src[4];
-      uint32_t len[4];
+    // ================= raw weight producer =================
+    // Weights are constants: they are fetched before griddepcontrol.wait, so
+    // the first stages stream in while the preceding kernel finishes.  Lane
+    // = row (lane + 32 j); 16-byte cp.async of the aligned superset of each
+    // row's super-block, each lane's arrival on raw_full fires when its
+    // copies have landed.
+    for (int j = 0; j < nsbz; ++j) {
+      const int sb = sb0 + j, rs = j % NR;
+      if (j >= NR && !mbar_wait(&raw_empty[rs], ((j / NR) - 1) & 1, p.err)) break;
+      uint8_t* dst = sRaw + (size_t)rs * QG_M * p.slot;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int r = lane + 32 * j;
+      for (int q = 0; q < 4; ++q) {
+        const int r = lane + 32 * q;
         int s = sg, row = r0 + r;
         if (swiglu) {
           s = r < 64 ? 0 : 1;
           row = r0 + (r & 63);
         }
-        len[j] = 0;
-        src[j] = 0;
         if (row < p.seg[s].rows) {
           const uintptr_t a = (uintptr_t)(p.seg[s].W + (long long)row * p.row_bytes + (long long)sb * QgBlk<TYPE>::BB);
           const uintptr_t a0 = a & ~(uintptr_t)15, a1 = (a + QgBlk<TYPE>::BB + 15) & ~(uintptr_t)15;
-          src[j] = a0;
-          len[j] = (uint32_t)(a1 - a0);
-          bytes += len[j];
+          uint8_t* d = dst + (size_t)r * p.slot;
+          for (uintptr_t o = 0; o < a1 - a0; o += 16)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(d + o)), "l"(a0 + o) : "memory");
         }
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, o);
-      if (lane == 0) mbar_arrive_expect_tx(&raw_full[rs], bytes);
-      __syncwarp();
-      uint8_t* dst = sRaw + (size_t)rs * QG_M * p.slot;
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        if (len[j]) tma_load_1d(dst + (size_t)(lane + 32 * j) * p.slot, (const void*)src[j], len[j], &raw_full[rs]);
-      // the four activation tiles of this super-block
-      if (lane == 0) {
-        for (int ks = 0; ks < 4; ++ks) {
-          const int i = 4 * sb + ks, bs = i % p.nbs;
-          if (i >= p.nbs && !mbar_wait(&b_empty[bs], ((i / p.nbs) - 1) & 1, p.err)) break;
-          mbar_arrive_expect_tx(&b_full[bs], bx * nsplit);
-          uint8_t* bd = sB + (size_t)bs * nsplit * btile;
-          tma_load_2d(bd, &maps.hi, i * QG_BK, t0, &b_full[bs]);
-          if (split) tma_load_2d(bd + btile, &maps.lo, i * QG_BK, t0, &b_full[bs]);
-        }
-      }
-      __syncwarp();
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&raw_full[rs])) : "memory");
+      if (lane == 0 && j == 0) QG_STAMP(1);
     }
+    // drain this warp's copies before it leaves
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp == 2) {
+    // ================= activation producer =================
+    // activations and token exponents come from the preceding kernels
+    pdl_wait();
+    if (lane == 0) QG_STAMP(8);
+    if (lane == 0) {
+      const uint32_t bx = (uint32_t)btile;
+      for (int i = 0; i < nk; ++i) {
+        const int bs = i % NB;
+        if (i >= NB && !mbar_wait(&b_empty[bs], ((i / NB) - 1) & 1, p.err)) break;
+        mbar_arrive_expect_tx(&b_full[bs], bx * nsplit);
+        uint8_t* bd = sB + (size_t)bs * nsplit * btile;
+        const int kx = (4 * sb0 + i) * QG_BK;
+        tma_load_2d(bd, &maps.hi, kx, t0, &b_full[bs]);
+        if (split) tma_load_2d(bd + btile, &maps.lo, kx, t0, &b_full[bs]);
+      }
+    }
+    __syncwarp();
   } else if (warp == 1) {
     // ================= MMA issuer =================
     if (lane == 0) {
       const uint32_t idesc = umma_idesc_f16(QG_M, BN);
       bool ok = true;
       for (int i = 0; i < nk && ok; ++i) {
-        const int as = i & 1, bs = i % p.nbs;
-        ok = mbar_wait(&a_full[as], (i >> 1) & 1, p.err) && mbar_wait(&b_full[bs], (i / p.nbs) & 1, p.err);
+        const int as = i % NA, bs = i % NB;
+        ok = mbar_wait(&a_full[as], (i / NA) & 1, p.err) && mbar_wait(&b_full[bs], (i / NB) & 1, p.err);
         if (!ok) break;
         tc_fence_after();
+        if (i == 0) QG_STAMP(3);
         const uint32_t a_hi = smem_u32(sA + (size_t)as * nsplit * QG_ATILE);
         const uint32_t b_hi = smem_u32(sB + (size_t)bs * nsplit * btile);
         const uint64_t dah = umma_desc_sw128(a_hi), dbh = umma_desc_sw128(b_hi);
@@ -374,12 +396,13 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         umma_commit(&b_empty[bs]);
       }
       umma_commit(acc_full);
+      QG_STAMP(5);
     }
     __syncwarp();
   } else {
     // ================= dequantize, then epilogue =================
-    // dequantization: thread (row dr, segment dseg) of warps 2..17
-    const int du = tid - 64, dr = du >> 2, dseg = du & 3;
+    // thread (row dr, segment dseg) of warps 3..18
+    const int du = tid - 96, dr = du >> 2, dseg = du & 3;
     int ds = sg, drow = r0 + dr;
     if (swiglu) {
       ds = dr < 64 ? 0 : 1;
@@ -387,18 +410,19 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     }
     const bool dvalid = drow < p.seg[ds].rows;
     const uintptr_t rowsrc = dvalid ? (uintptr_t)(p.seg[ds].W + (long long)drow * p.row_bytes) : 0;
-    const int sw = qg_exp_for(*p.wbound);
+    const int sw = qg_exp_for(*p.wbound);     // set at finalize (constant weights)
     const float wscale = ldexpf(1.0f, sw);
     bool ok = true;
     for (int i = 0; i < nk && ok; ++i) {
-      const int sb = i >> 2, ks = i & 3, rs = sb & 1, as = i & 1;
-      if (ks == 0) ok = mbar_wait(&raw_full[rs], (sb >> 1) & 1, p.err);
-      if (ok && i >= 2) ok = mbar_wait(&a_empty[as], ((i >> 1) - 1) & 1, p.err);
+      const int j = i >> 2, ks = i & 3, rs = j % NR, as = i % NA;
+      if (ks == 0) ok = mbar_wait(&raw_full[rs], (j / NR) & 1, p.err);
+      if (ok && i >= NA) ok = mbar_wait(&a_empty[as], ((i / NA) - 1) & 1, p.err);
       if (!ok) break;
+      if (tid == 96 && i == 0) QG_STAMP(2);
       uint8_t* ah = sA + (size_t)as * nsplit * QG_ATILE;
       float w[16];
       if (dvalid) {
-        const uintptr_t a = rowsrc + (uintptr_t)sb * QgBlk<TYPE>::BB;
+        const uintptr_t a = rowsrc + (uintptr_t)(sb0 + j) * QgBlk<TYPE>::BB;
         const uint8_t* rp = sRaw + ((size_t)rs * QG_M + dr) * p.slot + (a & 15);
         qg_dequant16<TYPE>(rp, ks, dseg, w);
       } else {
@@ -427,60 +451,104 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         if (ks == 3) mbar_arrive(&raw_empty[rs]);
       }
     }
-    // the epilogue: warps 2..5, one TMEM lane quarter each (thread = tile row)
-    const int q = warp & 3;
-    const int r = 32 * q + lane;
-    int s = sg, row = r0 + r;
-    if (swiglu) {
-      s = r < 64 ? 0 : 1;
-      row = r0 + (r & 63);
-    }
-    const bool valid = row < p.seg[s].rows;
-    if (warp < 6) {
-    // ---- epilogue ----
-    if (ok) ok = mbar_wait(acc_full, 0, p.err);
-    tc_fence_after();
-    float* xch = (float*)sA;                 // SwiGLU: up rows [64][BN] (A ring is free now)
-    const uint32_t taddr = tbase + ((uint32_t)(32 * q) << 16);
-    for (int c0 = 0; c0 < BN; c0 += 8) {
-      uint32_t v[8];
-      tmem_ld_x8(taddr + (uint32_t)c0, v);
-      tmem_wait_ld();
-      if (!ok) continue;
+    if (tid == 96) QG_STAMP(4);
+    if (warp < 7) {
+      // ---- epilogue: warps 3..6, TMEM lane quarter warp & 3, thread = tile row ----
+      pdl_wait();      // residual rows (QG_ADD) and the token exponents
+      const int q = warp & 3;
+      const int r = 32 * q + lane;
+      int s = sg, row = r0 + r;
+      if (swiglu) {
+        s = r < 64 ? 0 : 1;
+        row = r0 + (r & 63);
+      }
+      const bool valid = row < p.seg[s].rows;
+      if (ok) ok = mbar_wait(acc_full, 0, p.err);
+      tc_fence_after();
+      if (tid == 96) QG_STAMP(6);
+      const uint32_t taddr = tbase + ((uint32_t)(32 * q) << 16);
+      // split K: every slice parks its raw accumulator tile in the workspace;
+      // the slice that arrives last sums them in slice order (deterministic)
+      // and applies the epilogue
+      const long long tile = (long long)blockIdx.y * gridDim.x + mt;
+      float* wsl = nz > 1 ? p.ws + (tile * nz) * (long long)(BN * QG_M) : nullptr;
+      bool last = true;
+      if (nz > 1) {
+        for (int c0 = 0; c0 < BN; c0 += 8) {
+          uint32_t v[8];
+          tmem_ld_x8(taddr + (uint32_t)c0, v);
+          tmem_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int t = t0 + c0 + j;
-        if (t >= p.T) break;
-        const float val = __uint_as_float(v[j]) * ldexpf(1.0f, -sw) * ldexpf(1.0f, -(int)p.xexp[t]);
+          for (int j = 0; j < 8; ++j) __stcg(wsl + (long long)kz * BN * QG_M + (c0 + j) * QG_M + r, __uint_as_float(v[j]));
+        }
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (tid == 96) {
+          const int prev = atomicAdd(&p.tickets[tile], 1);
+          *s_last = prev == nz - 1;
+          if (prev == nz - 1) p.tickets[tile] = 0;      // ready for the next launch
+        }
+        named_bar_sync(1, 128);
+        last = *s_last != 0;
+        if (last) __threadfence();
+        if (tid == 96) QG_STAMP(9);
+      }
+      if (last) {
+        float* xch = (float*)sA;                 // SwiGLU: up rows [64][BN] (A ring is free now)
+        const float wun = ldexpf(1.0f, -sw);
+        for (int c0 = 0; c0 < BN; c0 += 8) {
+          float v[8];
+          if (nz > 1) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = 0.f;
+            for (int z = 0; z < nz; ++z)
+#pragma unroll
+              for (int j = 0; j < 8; ++j) v[j] += __ldcg(wsl + (long long)z * BN * QG_M + (c0 + j) * QG_M + r);
+          } else {
+            uint32_t u[8];
+            tmem_ld_x8(taddr + (uint32_t)c0, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(u[j]);
+          }
+          if (!ok) continue;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int t = t0 + c0 + j;
+            if (t >= p.T) break;
+            const float val = v[j] * wun * ldexpf(1.0f, -(int)p.xexp[t]);
+            if (swiglu) {
+              if (r >= 64) xch[(r - 64) * BN + c0 + j] = val;
+              else xch[(64 + r) * BN + c0 + j] = val;   // gate values beside the up values
+            } else if (valid) {
+              float* y = p.seg[s].y + (long long)t * p.y_stride + row;
+              if (p.epi == QG_ADD) *y += val;
+              else *y = val;
+            }
+          }
+        }
         if (swiglu) {
-          if (r >= 64) xch[(r - 64) * BN + c0 + j] = val;
-          else xch[(64 + r) * BN + c0 + j] = val;   // gate values beside the up values
-        } else if (valid) {
-          float* y = p.seg[s].y + (long long)t * p.y_stride + row;
-          if (p.epi == QG_ADD) *y += val;
-          else *y = val;
+          named_bar_sync(1, 128);
+          if (r < 64 && valid && ok) {
+            for (int c = 0; c < BN; ++c) {
+              const int t = t0 + c;
+              if (t >= p.T) break;
+              const float g = xch[(64 + r) * BN + c], u = xch[r * BN + c];
+              p.seg[0].y[(long long)t * p.y_stride + row] = g / (1.0f + expf(-g)) * u;   // src/ModelCPU.jl:455-468
+            }
+          }
         }
       }
     }
-    if (swiglu) {
-      named_bar_sync(1, 128);
-      if (r < 64 && valid && ok) {
-        for (int c = 0; c < BN; ++c) {
-          const int t = t0 + c;
-          if (t >= p.T) break;
-          const float g = xch[(64 + r) * BN + c], u = xch[r * BN + c];
-          p.seg[0].y[(long long)t * p.y_stride + row] = g / (1.0f + expf(-g)) * u;   // src/ModelCPU.jl:455-468
-        }
-      }
-    }
-    }   // warp < 6
   }
+  if (tid == 96) QG_STAMP(7);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, BN < 32 ? 32 : BN);
   }
+  if (tid == 32) QG_STAMP(10);
 }
 
 // ---------------------------------------------------------------------------
@@ -659,6 +727,16 @@ cudaError_t qg_launch(const QgParams& p, const QgMaps& maps, int BN, dim3 grid, 
 bool qgemm_supported(int type) { return type == T_Q4_K || type == T_Q5_K || type == T_Q6_K || type == T_Q8_0; }
 
 int qgemm_bn(int T) { return T <= 32 ? 32 : T <= 64 ? 64 : 128; }
+// debug: the last traced launch's stamps (ns, relative to stamp 0)
+int qgemm_trace_read(long long* out16) {
+  unsigned long long h[16];
+  if (cudaMemcpyFromSymbol(h, qg_trace, sizeof h) != cudaSuccess) return -1;
+  for (int i = 0; i < 16; ++i) out16[i] = h[i] ? (long long)(h[i] - h[0]) : -1;
+  return 0;
+}
+
+size_t qgemm_ws_bytes() { return (size_t)QG_WS_CTAS * 128 * QG_M * 4; }
+
 int qgemm_rows_padded(int T) {
   const int bn = qgemm_bn(T);
   return (T + bn - 1) / bn * bn;
@@ -733,13 +811,32 @@ int launch_qgemm(const QgemmCall& c, cudaStream_t st, bool pdl) {
   p.wbound = c.wbound;
   p.err = c.err;
   const int nsplit = p.split ? 2 : 1;
-  const size_t fixed = 1024 + 2 * nsplit * QG_ATILE + 2 * (size_t)QG_M * p.slot + 256;
+  const size_t astage = (size_t)nsplit * QG_ATILE, rstage = (size_t)QG_M * p.slot;
   const size_t bstage = (size_t)nsplit * BN * 128;
-  const size_t cap = 227 * 1024;
-  int nbs = (int)std::min<size_t>(4, (cap - fixed) / bstage);
-  if (nbs < 2) return set_error(INFERNO_EINVAL, "qgemm: tiles do not fit shared memory");
+  const size_t cap = 227 * 1024 - 1024 - 256;
+  // deepest rings that fit: raw super-blocks first (their HBM latency is the
+  // longest), then dequantized tiles, then activation tiles
+  int nas = 3, nrs = 3, nbs = BN <= 64 ? 4 : 3;
+  auto need = [&] { return nas * astage + nrs * rstage + nbs * bstage; };
+  while (need() > cap && nbs > 2) --nbs;
+  while (need() > cap && nas > 2) --nas;
+  while (need() > cap && nrs > 2) --nrs;
+  if (need() > cap) return set_error(INFERNO_EINVAL, "qgemm: tiles do not fit shared memory");
   p.nbs = nbs;
-  const size_t smem = fixed + nbs * bstage;
+  p.nas = nas;
+  p.nrs = nrs;
+  const size_t smem = 1024 + need() + 256;
+  // split K while the output tiles leave SMs idle (one CTA per SM)
+  const int ntt = (c.T + BN - 1) / BN, tiles = mt * ntt;
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  int nz = 1;
+  if (c.ws && c.tickets && tiles < sms) nz = std::max(1, std::min(p.nsb, sms / tiles));
+  while (nz > 1 && tiles * nz > QG_WS_CTAS) --nz;
+  p.ws = c.ws;
+  p.tickets = c.tickets;
+  static const bool trace = getenv("INFERNO_QG_TRACE") != nullptr;
+  p.trace = trace ? 1 : 0;
   QgMaps maps;
   memset(&maps, 0, sizeof maps);
   int rc;
@@ -747,7 +844,7 @@ int launch_qgemm(const QgemmCall& c, cudaStream_t st, bool pdl) {
   const int Tpad = qgemm_rows_padded(c.T);
   if ((rc = make_act_map(&maps.hi, (const __half*)c.xhi, c.K, Tpad, BN))) return rc;
   if ((rc = make_act_map(&maps.lo, (const __half*)(c.split ? c.xlo : c.xhi), c.K, Tpad, BN))) return rc;
-  const dim3 grid(mt, (c.T + BN - 1) / BN);
+  const dim3 grid(mt, ntt, nz);
   cudaError_t e;
   switch (c.type) {
     case T_Q4_K: e = qg_launch<T_Q4_K>(p, maps, BN, grid, smem, st, pdl); break;
@@ -775,13 +872,17 @@ int qgemm_from_gemv(const GemvCall& c, cudaStream_t st) {
   // stream-ordered scratch: fp16 hi / lo activations (padded to whole token
   // tiles), token exponents, the weight bound
   const size_t act = (size_t)Tpad * K * 2;
-  const size_t bytes = 2 * act + (size_t)Tpad * 4 + 256;
+  const size_t wsb = qgemm_ws_bytes();
+  const size_t bytes = 2 * act + (size_t)Tpad * 4 + 256 + wsb + QGEMM_TICKETS * 4;
   char* buf = nullptr;
   INF_CUDA_TRY(cudaMallocAsync((void**)&buf, bytes, st));
   __half* xhi = (__half*)buf;
   __half* xlo = (__half*)(buf + act);
   float* xexp = (float*)(buf + 2 * act);
   float* wb = xexp + Tpad;
+  float* ws = (float*)(buf + 2 * act + (size_t)Tpad * 4 + 256);
+  int* tickets = (int*)((char*)ws + wsb);
+  INF_CUDA_TRY(cudaMemsetAsync(tickets, 0, QGEMM_TICKETS * 4, st));
   int rc = launch_qgemm_act(c.x, c.x_stride, K, T, c.pro, c.pro_w, c.pro_z, c.pro_group, c.eps, xhi, xlo, xexp, st,
                             false);
   // one bound over every matrix of the call (a common weight scale): the
@@ -803,6 +904,8 @@ int qgemm_from_gemv(const GemvCall& c, cudaStream_t st) {
     q.wbound = wb;
     q.err = c.err ? c.err : device_error_word(0);
     q.split = !fast;
+    q.ws = ws;
+    q.tickets = tickets;
     rc = launch_qgemm(q, st, false);
   }
   cudaError_t ef = cudaFreeAsync(buf, st);

@@ -126,6 +126,36 @@ def test_config1_greedy_identity(config1):
     assert got == want
 
 
+def test_config1_decode_batch_matches_single(config1):
+    """Config 1, batched decode (B = 8 sequences, own prompts): each sequence's
+    greedy tokens equal the engine's own single-sequence decode (which the
+    identity test pins to the oracle), and two replays from the same saved
+    state agree (the whole-head GDN kernel of the batched step once read its
+    shared-memory weight rows without a barrier)."""
+    spec, T, orc = config1
+    B, P, n = 8, 16, 24
+    m = Model(spec, T, max_ctx=256, max_batch=B)
+    toks = []
+    for b in range(B):
+        m.select_sequence(b)
+        first, _ = m.forward(S.tokens(50 + b, P, spec.vocab), 0, want_logits=False)
+        toks.append(first)
+    m.select_sequence(0)
+    m.save_device()
+    out1 = m.decode_batch(toks, [P] * B, n)
+    m.restore_device()
+    out2 = m.decode_batch(toks, [P] * B, n)
+    m.restore_device()
+    single = []
+    for b in range(B):
+        m.select_sequence(b)
+        single.append(list(m.decode_greedy(toks[b], P, n)))
+    m.close()
+    assert np.array_equal(out1, out2)
+    for b in range(B):
+        assert out1[:, b].tolist() == single[b], b
+
+
 def test_config1_per_layer_hidden(config1, monkeypatch):
     """Config 1: hidden state after every one of the 24 layers for the last
     of the 32 prompt tokens, and its logits, within rel 2e-3 of the oracle
