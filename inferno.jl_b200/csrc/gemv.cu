@@ -207,6 +207,8 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
   static const bool no_hint = getenv("INFERNO_GEMV_NO_L2HINT") != nullptr;
   p.l2_evict_first = no_hint ? 0 : 1;
   p.early_trigger = env_early;
+  static const bool env_dbg = getenv("INFERNO_GEMV_DBG") != nullptr;
+  p.dbg = env_dbg ? atoi(getenv("INFERNO_GEMV_DBG")) : 0;
   if (ntiles == 0) return 0;
   const size_t stage_bytes = stage_of(TR);
   p.stages = (int)std::min<size_t>(GEMV_MAX_STAGES, (smem_cap - fixed) / stage_bytes);
@@ -568,4 +570,11 @@ int launch_gemv(const GemvCall& c, cudaStream_t st, bool pdl) {
   return 0;
 }
 
+}  // namespace inf
+
+namespace inf {
+// debug: the tensor-core GEMV timeline stamps (INFERNO_GEMV_DBG=1)
+int gemv_dbg_read(unsigned long long* out32) {
+  return cudaMemcpyFromSymbol(out32, gemv_dbg, 32 * sizeof(unsigned long long)) == cudaSuccess ? 0 : -1;
+}
 }  // namespace inf

@@ -95,7 +95,20 @@ struct GemvParams {
   unsigned long long* xch_parts[8];  // each rank's [2][n][H] words
   float* x_next;
   unsigned long long* trace;      // debug: 8 timeline slots of this launch (KT_*; null = off)
+  int dbg;                        // debug: stamps of CTA 0 / the last CTA into gemv_dbg (INFERNO_GEMV_DBG)
 };
+
+// debug timeline of the tensor-core GEMV (GemvParams::dbg): slots 0-15 CTA 0,
+// 16-31 the last CTA, %globaltimer ns; slot 30 = the previous launch's
+// last-CTA exit as seen after this launch's griddepcontrol.wait
+static __device__ unsigned long long gemv_dbg[32];
+#define GEMV_DBG(p, i)                                                             \
+  do {                                                                             \
+    if ((p).dbg) {                                                                 \
+      if (blockIdx.x == 0) gemv_dbg[i] = gtimer();                                 \
+      else if (blockIdx.x == gridDim.x - 1) gemv_dbg[16 + (i)] = gtimer();         \
+    }                                                                              \
+  } while (0)
 
 __device__ __constant__ uint64_t c_iq2xxs_grid_init[256] = {
 #include "iq2xxs_grid.inc"
@@ -558,6 +571,7 @@ __device__ __forceinline__ void gemv_producer(const GemvParams& p, uint64_t* ful
           tma_load_1d(st + (lane ? p.part1_off : 0), (const void*)a0, bytes, &full[s]);
       }
     }
+    if (lane == 0 && it == 0) GEMV_DBG(p, 1);
     // weights stream before the wait; dependents launch only after it
     if ((it == p.stages - 1 || it == n_items - 1) && !waited) {
       pdl_wait();

@@ -382,6 +382,7 @@ __device__ float gemv_mma_prologue_reg(const GemvParams& p, uint8_t* xq, float* 
     amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
   }
   if (tid == 0) KT_LAST(p.trace, 7);
+  if (tid == 0) GEMV_DBG(p, 3);
   ss = warp_sum(ss);
   amax = warp_max(amax);
   if (lane == 0) {
@@ -626,6 +627,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
   if (tid == 0) {
     KT_KIND(p.trace, KT_GEMV_MMA);
     KT_FIRST(p.trace, 1);
+    GEMV_DBG(p, 0);
   }
   constexpr int BB = TYPE == T_Q4_K ? 144 : TYPE == T_Q6_KR ? Q6R_BLOCK : 210;
   constexpr int XS_PER_SB = TYPE == T_Q4_K ? 8 : 16;
@@ -667,11 +669,14 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
   if (tid == 0) {
     KT_FIRST(p.trace, 2);
     KT_LAST(p.trace, 3);
+    if (p.dbg && blockIdx.x == 0) gemv_dbg[30] = gemv_dbg[16 + 7];
+    GEMV_DBG(p, 2);
   }
   const float colscale = reg_pro ? gemv_mma_prologue_reg<TYPE == T_Q6_KR ? T_Q6_K : TYPE, NW, MODE>(p, xq, xsum, red,
                                                                                                      vmax, tid, wpre)
                                  : gemv_mma_prologue<TYPE, NW, MODE>(p, xf, xq, xsum, red, vmax, tid);
   if (tid == 0) KT_LAST(p.trace, 4);
+  if (tid == 0) GEMV_DBG(p, 4);
   const bool nonfinite = *(volatile int*)&red[2 * NW] != 0;
   const uint32_t xtag =
       (MODE == MMA_XCH && p.xch_wk >= 0) ? (uint32_t)(*p.xch_seq + (unsigned long long)p.xch_wk + 1ull) : 0u;
@@ -690,6 +695,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
     const int s = it % p.stages;
     if (!mbar_wait(&full[s], (it / p.stages) & 1, p.err)) return;
     if (tid == 0 && it == 0) KT_LAST(p.trace, 5);
+    if (tid == 0 && it == 0) GEMV_DBG(p, 5);
     int sg, row0;
     tile_locate(p, blockIdx.x + it * G, sg, row0);
     const uint8_t* st = stage0 + (long long)s * p.stage_bytes;
@@ -783,6 +789,17 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
     }
   }
   if (tid == 0) KT_LAST(p.trace, 6);
+  if (tid == 0) GEMV_DBG(p, 6);
+  if (p.dbg == 2 && reg_pro) {
+    // debug: the register prologue once more, with its code now in the
+    // instruction cache (slots 8 / 9 around it)
+    named_bar_sync(1, NW * 32);
+    if (tid == 0) GEMV_DBG(p, 8);
+    GemvParams q = p;
+    q.dbg = 0;
+    (void)gemv_mma_prologue_reg<TYPE == T_Q6_KR ? T_Q6_K : TYPE, NW, MODE>(q, xq, xsum, red, vmax, tid, wpre);
+    if (tid == 0) GEMV_DBG(p, 9);
+  }
   if (p.epi == EPI_ARGMAX && wk == 0) {
     float v = best_v;
     int i = best_i;
@@ -798,6 +815,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
       atomicMax(&p.argmax[0], key);
     }
   }
+  if (tid == 0) GEMV_DBG(p, 7);
 }
 
 }  // namespace inf

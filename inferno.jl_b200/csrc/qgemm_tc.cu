@@ -47,7 +47,7 @@ namespace inf {
 constexpr int QG_M = 128;             // weight rows per tile (TMEM lanes)
 constexpr int QG_BK = 64;             // K per step (one 128-byte fp16 row)
 constexpr int QG_DQ_WARPS = 16;       // dequantizing warps: four threads per weight row
-constexpr int QG_THREADS = 96 + 32 * QG_DQ_WARPS;
+constexpr int QG_THREADS = 64 + 32 * QG_DQ_WARPS;
 constexpr int QG_WS_CTAS = 160;       // split-K is used while tiles x slices <= this (workspace bound)
 constexpr int QG_ATILE = QG_M * 128;  // bytes of one fp16 A tile (16 KB)
 
@@ -70,6 +70,7 @@ struct QgParams {
   int nbs, nas, nrs;     // ring stages: activation tiles, dequantized A tiles, raw super-blocks
   int split;
   int trace;             // debug: %globaltimer stamps of CTA (0,0,0) into qg_trace
+  int dbgmode;           // debug timing only (wrong results): 1 = no MMAs, 2 = no dequantization
   float* ws;             // split K: [tile][slice][BN][128] fp32 partial tiles
   int* tickets;          // split K: arrivals per output tile (zero between launches)
   const float* xexp;     // [T] power-of-two exponent applied to each token's fp16 activations
@@ -237,6 +238,91 @@ __device__ __forceinline__ void qg_dequant16(const uint8_t* rp, int ks, int seg,
   }
 }
 
+// fp32 weight pair -> fp16 hi pair and fp16 lo pair (lo = w - hi, rounded)
+__device__ __forceinline__ void qg_split2(f2_t w2, uint32_t& h, uint32_t& l) {
+  const float2 w = upk2(w2);
+  const __half2 hh = __floats2half2_rn(w.x, w.y);
+  const float2 hf = __half22float2(hh);
+  const float2 d = upk2(fsub2(w2, pk2f(hf.x, hf.y)));
+  const __half2 ll = __floats2half2_rn(d.x, d.y);
+  h = *(const uint32_t*)&hh;
+  l = *(const uint32_t*)&ll;
+}
+
+// 4 aligned words covering the 16 bytes at a 2-byte aligned shared address
+__device__ __forceinline__ void lds_16_any(const uint8_t* p, uint32_t (&o)[4]) {
+  const uintptr_t a = (uintptr_t)p;
+  const uint32_t* q = (const uint32_t*)(a & ~(uintptr_t)3);
+  const uint32_t sh = (uint32_t)(a & 3) * 8u;
+  uint32_t w[5];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) w[i] = q[i];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] = __funnelshift_r(w[i], w[i + 1], sh);
+}
+
+// 16 weights of K step ks, segment seg, times the matrix's power-of-two
+// scale, as fp16 hi / lo pairs (h[e], l[e] hold weights 2e, 2e+1).  Same
+// fp32 values as qg_dequant16 (Dequant.jl's rounding order; the products
+// are exact, scaling by a power of two commutes with the rounding); the
+// codes become floats through the 2^23 magic-number trick and the
+// arithmetic runs on fp32 pairs.
+template <int TYPE>
+__device__ __forceinline__ void qg_dq16_split(const uint8_t* rp, int ks, int seg, float wscale, uint32_t (&h)[8],
+                                              uint32_t (&l)[8]) {
+  const int off = 16 * (seg & 1), half = seg >> 1;
+  if constexpr (TYPE == T_Q4_K) {
+    // rows of Q4_K super-blocks (144 bytes) start on 16 bytes
+    const uint4 hd = *(const uint4*)rp;
+    const float d = h2f_bits((uint16_t)(hd.x & 0xffff)), dmin = h2f_bits((uint16_t)(hd.x >> 16));
+    const int j = 2 * ks + half;
+    uint32_t sj, mj;
+    if (j < 4) {
+      sj = (hd.y >> (8 * j)) & 63;
+      mj = (hd.z >> (8 * j)) & 63;
+    } else {
+      const int q = j - 4;
+      const uint32_t hi = (hd.w >> (8 * q)) & 0xff;
+      sj = (hi & 0x0f) | (((hd.y >> (8 * q + 6)) & 3) << 4);
+      mj = (hi >> 4) | (((hd.z >> (8 * q + 6)) & 3) << 4);
+    }
+    const float D = d * (float)sj * wscale, M = dmin * (float)mj * wscale;
+    const f2_t D2 = pk2f(D, D), nM2 = pk2f(-M, -M), mg = pk2f(MAGIC, MAGIC);
+    const uint4 q4 = *(const uint4*)(rp + 16 + 32 * ks + off);
+    const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t nib = (qw[i] >> (4 * half)) & 0x0f0f0f0fu;
+      qg_split2(ffma2(D2, bytes2<0>(nib, mg), nM2), h[2 * i], l[2 * i]);
+      qg_split2(ffma2(D2, bytes2<2>(nib, mg), nM2), h[2 * i + 1], l[2 * i + 1]);
+    }
+  } else if constexpr (TYPE == T_Q6_K) {
+    const int ns = ks >> 1, hi = ks & 1;
+    const int8_t sci = (int8_t)rp[192 + 8 * ns + 4 * hi + 2 * half + (seg & 1)];
+    const float d = h2f_bits(lds_u16_any(rp + 208));
+    const float sd = d * (float)sci * wscale;
+    const f2_t S2 = pk2f(sd, sd), mg = pk2f(MAGIC + 32.0f, MAGIC + 32.0f);
+    uint32_t la[4], hh[4];
+    lds_16_any(rp + 64 * ns + 32 * half + off, la);
+    lds_16_any(rp + 128 + 32 * ns + off, hh);
+    const int qsh = 4 * hi, hsh = 2 * half + 4 * hi;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t q6 = ((la[i] >> qsh) & 0x0f0f0f0fu) | (((hh[i] >> hsh) & 0x03030303u) << 4);
+      const f2_t lo2 = bytes2<0>(q6, mg), hi2 = bytes2<2>(q6, mg);   // q - 32, exact
+      const float2 a = upk2(lo2), b = upk2(hi2);
+      qg_split2(pk2f(a.x * sd, a.y * sd), h[2 * i], l[2 * i]);
+      qg_split2(pk2f(b.x * sd, b.y * sd), h[2 * i + 1], l[2 * i + 1]);
+      (void)S2;
+    }
+  } else {
+    float w[16];
+    qg_dequant16<TYPE>(rp, ks, seg, w);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) qg_split2(pk2f(w[2 * e] * wscale, w[2 * e + 1] * wscale), h[e], l[e]);
+  }
+}
+
 __device__ __forceinline__ int qg_exp_for(float bound) {
   // power of two that brings `bound` just under 2^14 (fp16 max is 65504)
   if (!(bound > 0.f) || !(bound <= 3.0e38f)) return 0;
@@ -272,9 +358,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   const int btile = BN * 128;
   uint8_t* sRaw = sB + (size_t)NB * nsplit * btile;          // [NR][128][slot]
   uint64_t* bars = (uint64_t*)(sRaw + (size_t)NR * QG_M * p.slot);
-  uint64_t* raw_full = bars;             // NR
-  uint64_t* raw_empty = raw_full + NR;   // NR
-  uint64_t* a_full = raw_empty + NR;     // NA
+  uint64_t* a_full = bars;               // NA
   uint64_t* a_empty = a_full + NA;       // NA
   uint64_t* b_full = a_empty + NA;       // NB
   uint64_t* b_empty = b_full + NB;       // NB
@@ -294,10 +378,6 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   const int nsbz = sb1 - sb0, nk = 4 * nsbz;
 
   if (tid == 0) {
-    for (int i = 0; i < NR; ++i) {
-      mbar_init(&raw_full[i], 32);       // one cp.async arrival per producer lane
-      mbar_init(&raw_empty[i], QG_DQ_WARPS);
-    }
     for (int i = 0; i < NA; ++i) {
       mbar_init(&a_full[i], QG_DQ_WARPS);
       mbar_init(&a_empty[i], 1);
@@ -319,38 +399,6 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   const uint32_t tbase = *s_tmem;
 
   if (warp == 0) {
-    // ================= raw weight producer =================
-    // Weights are constants: they are fetched before griddepcontrol.wait, so
-    // the first stages stream in while the preceding kernel finishes.  Lane
-    // = row (lane + 32 j); 16-byte cp.async of the aligned superset of each
-    // row's super-block, each lane's arrival on raw_full fires when its
-    // copies have landed.
-    for (int j = 0; j < nsbz; ++j) {
-      const int sb = sb0 + j, rs = j % NR;
-      if (j >= NR && !mbar_wait(&raw_empty[rs], ((j / NR) - 1) & 1, p.err)) break;
-      uint8_t* dst = sRaw + (size_t)rs * QG_M * p.slot;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int r = lane + 32 * q;
-        int s = sg, row = r0 + r;
-        if (swiglu) {
-          s = r < 64 ? 0 : 1;
-          row = r0 + (r & 63);
-        }
-        if (row < p.seg[s].rows) {
-          const uintptr_t a = (uintptr_t)(p.seg[s].W + (long long)row * p.row_bytes + (long long)sb * QgBlk<TYPE>::BB);
-          const uintptr_t a0 = a & ~(uintptr_t)15, a1 = (a + QgBlk<TYPE>::BB + 15) & ~(uintptr_t)15;
-          uint8_t* d = dst + (size_t)r * p.slot;
-          for (uintptr_t o = 0; o < a1 - a0; o += 16)
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(d + o)), "l"(a0 + o) : "memory");
-        }
-      }
-      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&raw_full[rs])) : "memory");
-      if (lane == 0 && j == 0) QG_STAMP(1);
-    }
-    // drain this warp's copies before it leaves
-    asm volatile("cp.async.wait_all;" ::: "memory");
-  } else if (warp == 2) {
     // ================= activation producer =================
     // activations and token exponents come from the preceding kernels
     pdl_wait();
@@ -385,6 +433,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         const uint64_t dal = umma_desc_sw128(a_hi + QG_ATILE), dbl = umma_desc_sw128(b_hi + btile);
 #pragma unroll
         for (int kk = 0; kk < QG_BK / 16; ++kk) {
+          if (p.dbgmode == 1) break;
           const uint64_t o = (uint64_t)(2 * kk);     // +32 bytes along K
           umma_f16(tbase, dah + o, dbh + o, idesc, (i | kk) != 0);
           if (split) {
@@ -401,8 +450,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     __syncwarp();
   } else {
     // ================= dequantize, then epilogue =================
-    // thread (row dr, segment dseg) of warps 3..18
-    const int du = tid - 96, dr = du >> 2, dseg = du & 3;
+    // thread (row dr, segment dseg) of warps 2..17.  The four threads of a
+    // row stage its super-blocks themselves (16-byte cp.async of the aligned
+    // superset, chunks dseg, dseg + 4, ...) into an NR-stage ring, and wait
+    // for them with cp.async.wait_group: no producer warp, no mbarrier, and
+    // the weights (constants) stream in before griddepcontrol.wait.
+    const int du = tid - 64, dr = du >> 2, dseg = du & 3;
     int ds = sg, drow = r0 + dr;
     if (swiglu) {
       ds = dr < 64 ? 0 : 1;
@@ -410,50 +463,58 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     }
     const bool dvalid = drow < p.seg[ds].rows;
     const uintptr_t rowsrc = dvalid ? (uintptr_t)(p.seg[ds].W + (long long)drow * p.row_bytes) : 0;
+    uint8_t* myraw = sRaw + (size_t)dr * p.slot;
+    auto stage_raw = [&](int j) {
+      if (dvalid && j < nsbz) {
+        const uintptr_t a = rowsrc + (uintptr_t)(sb0 + j) * QgBlk<TYPE>::BB;
+        const uintptr_t a0 = a & ~(uintptr_t)15, a1 = (a + QgBlk<TYPE>::BB + 15) & ~(uintptr_t)15;
+        uint8_t* d = myraw + (size_t)(j % NR) * QG_M * p.slot;
+        for (uintptr_t o = 16 * dseg; o < a1 - a0; o += 64)
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(d + o)), "l"(a0 + o) : "memory");
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    for (int j = 0; j < NR - 1; ++j) stage_raw(j);
     const int sw = qg_exp_for(*p.wbound);     // set at finalize (constant weights)
     const float wscale = ldexpf(1.0f, sw);
     bool ok = true;
     for (int i = 0; i < nk && ok; ++i) {
       const int j = i >> 2, ks = i & 3, rs = j % NR, as = i % NA;
-      if (ks == 0) ok = mbar_wait(&raw_full[rs], (j / NR) & 1, p.err);
-      if (ok && i >= NA) ok = mbar_wait(&a_empty[as], ((i / NA) - 1) & 1, p.err);
+      if (ks == 0) {
+        __syncwarp();                 // the row's threads are done with stage (j - 1) % NR
+        stage_raw(j + NR - 1);
+        if (NR == 3) asm volatile("cp.async.wait_group 2;" ::: "memory");
+        else asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncwarp();                 // the row's four threads' copies are visible
+      }
+      if (i >= NA) ok = mbar_wait(&a_empty[as], ((i / NA) - 1) & 1, p.err);
       if (!ok) break;
-      if (tid == 96 && i == 0) QG_STAMP(2);
+      if (tid == 64 && i == 0) QG_STAMP(2);
       uint8_t* ah = sA + (size_t)as * nsplit * QG_ATILE;
-      float w[16];
-      if (dvalid) {
+      uint32_t h[8], l[8];
+      if (dvalid && p.dbgmode != 2) {
         const uintptr_t a = rowsrc + (uintptr_t)(sb0 + j) * QgBlk<TYPE>::BB;
-        const uint8_t* rp = sRaw + ((size_t)rs * QG_M + dr) * p.slot + (a & 15);
-        qg_dequant16<TYPE>(rp, ks, dseg, w);
+        const uint8_t* rp = myraw + (size_t)rs * QG_M * p.slot + (a & 15);
+        qg_dq16_split<TYPE>(rp, ks, dseg, wscale, h, l);
       } else {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) w[e] = 0.f;
+        for (int e = 0; e < 8; ++e) h[e] = l[e] = 0u;
       }
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
-        uint32_t h[4], l[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float x0 = w[8 * cc + 2 * e] * wscale, x1 = w[8 * cc + 2 * e + 1] * wscale;
-          const __half2 hh = __floats2half2_rn(x0, x1);
-          const float2 hf = __half22float2(hh);
-          h[e] = *(const uint32_t*)&hh;
-          l[e] = pack_h2(x0 - hf.x, x1 - hf.y);
-        }
         const int c = 2 * dseg + cc;
-        *(uint4*)(ah + sw128_off(dr, c)) = make_uint4(h[0], h[1], h[2], h[3]);
-        if (split) *(uint4*)(ah + QG_ATILE + sw128_off(dr, c)) = make_uint4(l[0], l[1], l[2], l[3]);
+        *(uint4*)(ah + sw128_off(dr, c)) = make_uint4(h[4 * cc], h[4 * cc + 1], h[4 * cc + 2], h[4 * cc + 3]);
+        if (split)
+          *(uint4*)(ah + QG_ATILE + sw128_off(dr, c)) = make_uint4(l[4 * cc], l[4 * cc + 1], l[4 * cc + 2], l[4 * cc + 3]);
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&a_full[as]);
-        if (ks == 3) mbar_arrive(&raw_empty[rs]);
-      }
+      if (lane == 0) mbar_arrive(&a_full[as]);
     }
-    if (tid == 96) QG_STAMP(4);
-    if (warp < 7) {
-      // ---- epilogue: warps 3..6, TMEM lane quarter warp & 3, thread = tile row ----
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (tid == 64) QG_STAMP(4);
+    if (warp < 6) {
+      // ---- epilogue: warps 2..5, TMEM lane quarter warp & 3, thread = tile row ----
       pdl_wait();      // residual rows (QG_ADD) and the token exponents
       const int q = warp & 3;
       const int r = 32 * q + lane;
@@ -465,7 +526,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       const bool valid = row < p.seg[s].rows;
       if (ok) ok = mbar_wait(acc_full, 0, p.err);
       tc_fence_after();
-      if (tid == 96) QG_STAMP(6);
+      if (tid == 64) QG_STAMP(6);
       const uint32_t taddr = tbase + ((uint32_t)(32 * q) << 16);
       // split K: every slice parks its raw accumulator tile in the workspace;
       // the slice that arrives last sums them in slice order (deterministic)
@@ -483,7 +544,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         }
         __threadfence();
         named_bar_sync(1, 128);
-        if (tid == 96) {
+        if (tid == 64) {
           const int prev = atomicAdd(&p.tickets[tile], 1);
           *s_last = prev == nz - 1;
           if (prev == nz - 1) p.tickets[tile] = 0;      // ready for the next launch
@@ -491,7 +552,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         named_bar_sync(1, 128);
         last = *s_last != 0;
         if (last) __threadfence();
-        if (tid == 96) QG_STAMP(9);
+        if (tid == 64) QG_STAMP(9);
       }
       if (last) {
         float* xch = (float*)sA;                 // SwiGLU: up rows [64][BN] (A ring is free now)
@@ -541,7 +602,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       }
     }
   }
-  if (tid == 96) QG_STAMP(7);
+  if (tid == 64) QG_STAMP(7);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -837,6 +898,8 @@ int launch_qgemm(const QgemmCall& c, cudaStream_t st, bool pdl) {
   p.tickets = c.tickets;
   static const bool trace = getenv("INFERNO_QG_TRACE") != nullptr;
   p.trace = trace ? 1 : 0;
+  static const int dbgmode = getenv("INFERNO_QG_DBGMODE") ? atoi(getenv("INFERNO_QG_DBGMODE")) : 0;
+  p.dbgmode = dbgmode;
   QgMaps maps;
   memset(&maps, 0, sizeof maps);
   int rc;
