@@ -70,7 +70,8 @@ struct QgParams {
   int nbs, nas, nrs;     // ring stages: activation tiles, dequantized A tiles, raw super-blocks
   int split;
   int trace;             // debug: %globaltimer stamps of CTA (0,0,0) into qg_trace
-  int dbgmode;           // debug timing only (wrong results): 1 = no MMAs, 2 = no dequantization
+  int dbgmode;           // debug timing only (wrong results): 1 = no MMAs, 2 = no dequantization,
+                         // 3 = no proxy fence, 4 = no weight staging after the first stages
   float* ws;             // split K: [tile][slice][BN][128] fp32 partial tiles
   int* tickets;          // split K: arrivals per output tile (zero between launches)
   const float* xexp;     // [T] power-of-two exponent applied to each token's fp16 activations
@@ -249,14 +250,27 @@ __device__ __forceinline__ void qg_split2(f2_t w2, uint32_t& h, uint32_t& l) {
   l = *(const uint32_t*)&ll;
 }
 
-// 4 aligned words covering the 16 bytes at a 2-byte aligned shared address
-__device__ __forceinline__ void lds_16_any(const uint8_t* p, uint32_t (&o)[4]) {
-  const uintptr_t a = (uintptr_t)p;
-  const uint32_t* q = (const uint32_t*)(a & ~(uintptr_t)3);
-  const uint32_t sh = (uint32_t)(a & 3) * 8u;
+// explicit shared-memory accesses (32-bit shared-window addresses)
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ void sts128(uint32_t a, uint32_t x, uint32_t y, uint32_t z, uint32_t w) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(x), "r"(y), "r"(z), "r"(w) : "memory");
+}
+
+// the 16 bytes at a 2-byte aligned shared address, as 4 words
+__device__ __forceinline__ void lds_16_any(uint32_t a, uint32_t (&o)[4]) {
+  const uint32_t q = a & ~3u, sh = (a & 3u) * 8u;
   uint32_t w[5];
 #pragma unroll
-  for (int i = 0; i < 5; ++i) w[i] = q[i];
+  for (int i = 0; i < 5; ++i) w[i] = lds32(q + 4 * i);
 #pragma unroll
   for (int i = 0; i < 4; ++i) o[i] = __funnelshift_r(w[i], w[i + 1], sh);
 }
@@ -268,12 +282,12 @@ __device__ __forceinline__ void lds_16_any(const uint8_t* p, uint32_t (&o)[4]) {
 // codes become floats through the 2^23 magic-number trick and the
 // arithmetic runs on fp32 pairs.
 template <int TYPE>
-__device__ __forceinline__ void qg_dq16_split(const uint8_t* rp, int ks, int seg, float wscale, uint32_t (&h)[8],
-                                              uint32_t (&l)[8]) {
+__device__ __forceinline__ void qg_dq16_split(const uint8_t* rp, uint32_t ra, int ks, int seg, float wscale,
+                                              uint32_t (&h)[8], uint32_t (&l)[8]) {
   const int off = 16 * (seg & 1), half = seg >> 1;
   if constexpr (TYPE == T_Q4_K) {
     // rows of Q4_K super-blocks (144 bytes) start on 16 bytes
-    const uint4 hd = *(const uint4*)rp;
+    const uint4 hd = lds128(ra);
     const float d = h2f_bits((uint16_t)(hd.x & 0xffff)), dmin = h2f_bits((uint16_t)(hd.x >> 16));
     const int j = 2 * ks + half;
     uint32_t sj, mj;
@@ -288,7 +302,7 @@ __device__ __forceinline__ void qg_dq16_split(const uint8_t* rp, int ks, int seg
     }
     const float D = d * (float)sj * wscale, M = dmin * (float)mj * wscale;
     const f2_t D2 = pk2f(D, D), nM2 = pk2f(-M, -M), mg = pk2f(MAGIC, MAGIC);
-    const uint4 q4 = *(const uint4*)(rp + 16 + 32 * ks + off);
+    const uint4 q4 = lds128(ra + 16 + 32 * ks + off);
     const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -298,13 +312,15 @@ __device__ __forceinline__ void qg_dq16_split(const uint8_t* rp, int ks, int seg
     }
   } else if constexpr (TYPE == T_Q6_K) {
     const int ns = ks >> 1, hi = ks & 1;
-    const int8_t sci = (int8_t)rp[192 + 8 * ns + 4 * hi + 2 * half + (seg & 1)];
-    const float d = h2f_bits(lds_u16_any(rp + 208));
+    const uint32_t sa = ra + 192 + 8 * ns + 4 * hi + 2 * half + (seg & 1);
+    const int8_t sci = (int8_t)((lds32(sa & ~3u) >> (8 * (sa & 3u))) & 0xff);
+    const uint32_t da = ra + 208;      // 2-byte aligned
+    const float d = h2f_bits((uint16_t)((lds32(da & ~3u) >> (8 * (da & 3u))) & 0xffff));
     const float sd = d * (float)sci * wscale;
     const f2_t S2 = pk2f(sd, sd), mg = pk2f(MAGIC + 32.0f, MAGIC + 32.0f);
     uint32_t la[4], hh[4];
-    lds_16_any(rp + 64 * ns + 32 * half + off, la);
-    lds_16_any(rp + 128 + 32 * ns + off, hh);
+    lds_16_any(ra + 64 * ns + 32 * half + off, la);
+    lds_16_any(ra + 128 + 32 * ns + off, hh);
     const int qsh = 4 * hi, hsh = 2 * half + 4 * hi;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -374,6 +390,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   const int rows_per_tile = swiglu ? QG_M / 2 : QG_M;
   const int r0 = (mt - p.seg[sg].mtile0) * rows_per_tile;
   if (tid == 0) QG_STAMP(0);
+  if (p.trace && tid == 0) atomicMax(&qg_trace[12], gtimer());       // latest CTA start
   const int sb0 = (int)((long long)kz * p.nsb / nz), sb1 = (int)((long long)(kz + 1) * p.nsb / nz);
   const int nsbz = sb1 - sb0, nk = 4 * nsbz;
 
@@ -480,7 +497,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     bool ok = true;
     for (int i = 0; i < nk && ok; ++i) {
       const int j = i >> 2, ks = i & 3, rs = j % NR, as = i % NA;
-      if (ks == 0) {
+      if (ks == 0 && p.dbgmode != 4) {
         __syncwarp();                 // the row's threads are done with stage (j - 1) % NR
         stage_raw(j + NR - 1);
         if (NR == 3) asm volatile("cp.async.wait_group 2;" ::: "memory");
@@ -495,7 +512,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       if (dvalid && p.dbgmode != 2) {
         const uintptr_t a = rowsrc + (uintptr_t)(sb0 + j) * QgBlk<TYPE>::BB;
         const uint8_t* rp = myraw + (size_t)rs * QG_M * p.slot + (a & 15);
-        qg_dq16_split<TYPE>(rp, ks, dseg, wscale, h, l);
+        qg_dq16_split<TYPE>(rp, smem_u32(rp), ks, dseg, wscale, h, l);
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) h[e] = l[e] = 0u;
@@ -503,20 +520,23 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         const int c = 2 * dseg + cc;
-        *(uint4*)(ah + sw128_off(dr, c)) = make_uint4(h[4 * cc], h[4 * cc + 1], h[4 * cc + 2], h[4 * cc + 3]);
-        if (split)
-          *(uint4*)(ah + QG_ATILE + sw128_off(dr, c)) = make_uint4(l[4 * cc], l[4 * cc + 1], l[4 * cc + 2], l[4 * cc + 3]);
+        const uint32_t sa = smem_u32(ah) + sw128_off(dr, c);
+        sts128(sa, h[4 * cc], h[4 * cc + 1], h[4 * cc + 2], h[4 * cc + 3]);
+        if (split) sts128(sa + QG_ATILE, l[4 * cc], l[4 * cc + 1], l[4 * cc + 2], l[4 * cc + 3]);
       }
-      fence_proxy_async_smem();
+      if (p.dbgmode != 3) fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[as]);
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     if (tid == 64) QG_STAMP(4);
-    if (warp < 6) {
-      // ---- epilogue: warps 2..5, TMEM lane quarter warp & 3, thread = tile row ----
+    {
+      // ---- epilogue: all 16 dequantizing warps.  Warp w reads TMEM lane
+      // quarter w & 3 (thread = tile row) and column group (w - 2) >> 2 ----
       pdl_wait();      // residual rows (QG_ADD) and the token exponents
-      const int q = warp & 3;
+      const int q = warp & 3, cg = (warp - 2) >> 2;
+      constexpr int CW = BN / 4;                 // columns per warp
+      const int c_lo = cg * CW;
       const int r = 32 * q + lane;
       int s = sg, row = r0 + r;
       if (swiglu) {
@@ -524,10 +544,15 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         row = r0 + (r & 63);
       }
       const bool valid = row < p.seg[s].rows;
+      float* cs = (float*)(s_last + 4);          // [BN] per-column descale
+      if (du < BN) {
+        const int t = t0 + du;
+        cs[du] = t < p.T ? ldexpf(1.0f, -sw - (int)p.xexp[t]) : 0.f;
+      }
       if (ok) ok = mbar_wait(acc_full, 0, p.err);
       tc_fence_after();
       if (tid == 64) QG_STAMP(6);
-      const uint32_t taddr = tbase + ((uint32_t)(32 * q) << 16);
+      const uint32_t taddr = tbase + ((uint32_t)(32 * q) << 16) + (uint32_t)c_lo;
       // split K: every slice parks its raw accumulator tile in the workspace;
       // the slice that arrives last sums them in slice order (deterministic)
       // and applies the epilogue
@@ -535,36 +560,40 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       float* wsl = nz > 1 ? p.ws + (tile * nz) * (long long)(BN * QG_M) : nullptr;
       bool last = true;
       if (nz > 1) {
-        for (int c0 = 0; c0 < BN; c0 += 8) {
+#pragma unroll
+        for (int c0 = 0; c0 < CW; c0 += 8) {
           uint32_t v[8];
           tmem_ld_x8(taddr + (uint32_t)c0, v);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 8; ++j) __stcg(wsl + (long long)kz * BN * QG_M + (c0 + j) * QG_M + r, __uint_as_float(v[j]));
+          for (int j = 0; j < 8; ++j)
+            __stcg(wsl + (long long)kz * BN * QG_M + (c_lo + c0 + j) * QG_M + r, __uint_as_float(v[j]));
         }
         __threadfence();
-        named_bar_sync(1, 128);
+        named_bar_sync(1, 32 * QG_DQ_WARPS);
         if (tid == 64) {
           const int prev = atomicAdd(&p.tickets[tile], 1);
           *s_last = prev == nz - 1;
           if (prev == nz - 1) p.tickets[tile] = 0;      // ready for the next launch
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, 32 * QG_DQ_WARPS);
         last = *s_last != 0;
         if (last) __threadfence();
         if (tid == 64) QG_STAMP(9);
+      } else {
+        named_bar_sync(1, 32 * QG_DQ_WARPS);     // cs[] written
       }
       if (last) {
-        float* xch = (float*)sA;                 // SwiGLU: up rows [64][BN] (A ring is free now)
-        const float wun = ldexpf(1.0f, -sw);
-        for (int c0 = 0; c0 < BN; c0 += 8) {
+        float* xch = (float*)sA;                 // SwiGLU: [128][BN] (the A ring is free now)
+#pragma unroll
+        for (int c0 = 0; c0 < CW; c0 += 8) {
           float v[8];
           if (nz > 1) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) v[j] = 0.f;
             for (int z = 0; z < nz; ++z)
 #pragma unroll
-              for (int j = 0; j < 8; ++j) v[j] += __ldcg(wsl + (long long)z * BN * QG_M + (c0 + j) * QG_M + r);
+              for (int j = 0; j < 8; ++j) v[j] += __ldcg(wsl + (long long)z * BN * QG_M + (c_lo + c0 + j) * QG_M + r);
           } else {
             uint32_t u[8];
             tmem_ld_x8(taddr + (uint32_t)c0, u);
@@ -575,13 +604,11 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
           if (!ok) continue;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const int t = t0 + c0 + j;
-            if (t >= p.T) break;
-            const float val = v[j] * wun * ldexpf(1.0f, -(int)p.xexp[t]);
+            const int c = c_lo + c0 + j, t = t0 + c;
+            const float val = v[j] * cs[c];
             if (swiglu) {
-              if (r >= 64) xch[(r - 64) * BN + c0 + j] = val;
-              else xch[(64 + r) * BN + c0 + j] = val;   // gate values beside the up values
-            } else if (valid) {
+              xch[(r < 64 ? 64 + r : r - 64) * BN + c] = val;   // gate rows beside the up rows
+            } else if (valid && t < p.T) {
               float* y = p.seg[s].y + (long long)t * p.y_stride + row;
               if (p.epi == QG_ADD) *y += val;
               else *y = val;
@@ -589,13 +616,16 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
           }
         }
         if (swiglu) {
-          named_bar_sync(1, 128);
-          if (r < 64 && valid && ok) {
-            for (int c = 0; c < BN; ++c) {
+          named_bar_sync(1, 32 * QG_DQ_WARPS);
+          // thread (gate row rr, column group): 64 rows x 8 groups over 512 threads
+          const int rr = du & 63, g8 = du >> 6;
+          const int grow = r0 + rr;
+          if (grow < p.seg[0].rows && ok) {
+            for (int c = g8; c < BN; c += 8) {
               const int t = t0 + c;
               if (t >= p.T) break;
-              const float g = xch[(64 + r) * BN + c], u = xch[r * BN + c];
-              p.seg[0].y[(long long)t * p.y_stride + row] = g / (1.0f + expf(-g)) * u;   // src/ModelCPU.jl:455-468
+              const float g = xch[(64 + rr) * BN + c], u = xch[rr * BN + c];
+              p.seg[0].y[(long long)t * p.y_stride + grow] = g / (1.0f + expf(-g)) * u;   // src/ModelCPU.jl:455-468
             }
           }
         }
@@ -610,6 +640,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     tmem_dealloc(tbase, BN < 32 ? 32 : BN);
   }
   if (tid == 32) QG_STAMP(10);
+  if (p.trace && tid == 32) atomicMax(&qg_trace[11], gtimer());      // latest CTA end
+  if (p.trace && tid == 64 && p.seg[0].rows > 0) atomicMax(&qg_trace[13], (unsigned long long)(nk));
 }
 
 // ---------------------------------------------------------------------------
@@ -874,19 +906,23 @@ int launch_qgemm(const QgemmCall& c, cudaStream_t st, bool pdl) {
   const int nsplit = p.split ? 2 : 1;
   const size_t astage = (size_t)nsplit * QG_ATILE, rstage = (size_t)QG_M * p.slot;
   const size_t bstage = (size_t)nsplit * BN * 128;
-  const size_t cap = 227 * 1024 - 1024 - 256;
-  // deepest rings that fit: raw super-blocks first (their HBM latency is the
-  // longest), then dequantized tiles, then activation tiles
-  int nas = 3, nrs = 3, nbs = BN <= 64 ? 4 : 3;
+  const size_t cap = 227 * 1024 - 1024 - 1024;
+  // Ring depths.  The activation (B) tiles come from L2 by TMA with a
+  // latency of about a microsecond, and a B stage can only be refilled once
+  // the MMAs of its step completed: steps run at ~latency / NB, so B gets
+  // the depth (up to 8 stages); dequantized A tiles need only two stages (the
+  // dequantizing warps work one step ahead of the MMA), the raw super-block
+  // ring three (two super-blocks of HBM prefetch).
+  int nas = 2, nrs = 3, nbs = 8;
   auto need = [&] { return nas * astage + nrs * rstage + nbs * bstage; };
-  while (need() > cap && nbs > 2) --nbs;
-  while (need() > cap && nas > 2) --nas;
+  while (need() > cap && nbs > 3) --nbs;
   while (need() > cap && nrs > 2) --nrs;
+  while (need() > cap && nbs > 2) --nbs;
   if (need() > cap) return set_error(INFERNO_EINVAL, "qgemm: tiles do not fit shared memory");
   p.nbs = nbs;
   p.nas = nas;
   p.nrs = nrs;
-  const size_t smem = 1024 + need() + 256;
+  const size_t smem = 1024 + need() + 1024;     // alignment slack, barriers, column scales
   // split K while the output tiles leave SMs idle (one CTA per SM)
   const int ntt = (c.T + BN - 1) / BN, tiles = mt * ntt;
   int sms = 148, dev = 0;
@@ -898,6 +934,10 @@ int launch_qgemm(const QgemmCall& c, cudaStream_t st, bool pdl) {
   p.tickets = c.tickets;
   static const bool trace = getenv("INFERNO_QG_TRACE") != nullptr;
   p.trace = trace ? 1 : 0;
+  if (trace) {
+    static const unsigned long long zeros[16] = {};
+    cudaMemcpyToSymbolAsync(qg_trace, zeros, sizeof zeros, 0, cudaMemcpyHostToDevice, st);
+  }
   static const int dbgmode = getenv("INFERNO_QG_DBGMODE") ? atoi(getenv("INFERNO_QG_DBGMODE")) : 0;
   p.dbgmode = dbgmode;
   QgMaps maps;
