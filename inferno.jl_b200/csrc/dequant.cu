@@ -113,16 +113,17 @@ int launch_dequant(int type, const void* src, long long n, float* dst, cudaStrea
   return cudaGetLastError() == cudaSuccess ? 0 : -3;
 }
 
-// Dequantize one row `row` of a (rows x inner) matrix into dst[inner]
-// (token-embedding lookup: src/ModelCPU.jl:973-976).  `row` is read from
-// device memory so the launch can sit inside a captured graph.
+// Dequantize row row_ptr[b] of a (rows x inner) matrix into dst[b][inner],
+// one CTA per b (token-embedding lookup: src/ModelCPU.jl:973-976).  The rows
+// are read from device memory so the launch can sit inside a captured graph.
 template <int TYPE>
 __global__ void embed_row_kernel(const uint8_t* __restrict__ W, long long row_bytes, int inner,
                                  const int* __restrict__ row_ptr, float* __restrict__ dst, int vocab) {
   pdl_wait();
   pdl_trigger();
-  int row = *row_ptr;
+  int row = row_ptr[blockIdx.x];
   if (row < 0 || row >= vocab) row = 0;
+  dst += (long long)blockIdx.x * inner;
   long long runs = inner / 32;
   // one thread per run (inner/32 runs <= 1024 for every model here)
   int r = threadIdx.x;
@@ -173,11 +174,11 @@ __global__ void embed_row_kernel(const uint8_t* __restrict__ W, long long row_by
 }
 
 int launch_embed_row(int type, const void* W, long long row_bytes, int inner, const int* row_ptr, float* dst,
-                     int vocab, cudaStream_t st, bool pdl) {
-  if (inner % 256 || inner / 32 > 1024) return -1;
+                     int vocab, cudaStream_t st, bool pdl, int nrows) {
+  if (inner % 256 || inner / 32 > 1024 || nrows < 1) return -1;
   int threads = ((inner / 32 + 31) / 32) * 32;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1);
+  cfg.gridDim = dim3(nrows);
   cfg.blockDim = dim3(threads);
   cfg.stream = st;
   cudaLaunchAttribute at[1];

@@ -604,8 +604,10 @@ int bgemv(InfernoEngine* e, const DevTensor* W, int inner, std::initializer_list
     // fp16 hi / lo activations with the prologue applied, then the tcgen05 GEMM
     int rc = 0;
     if (!reuse_act) {
+      // programmatic dependent launch: the conversion waits for its inputs,
+      // the GEMM stages its (constant) weights while the conversion runs
       rc = launch_qgemm_act(x, x_stride, inner, T, pro, pro_w, pro_z, group, e->cfg.rms_eps, e->pf_xhi, e->pf_xlo,
-                            e->pf_xexp, e->st, false);
+                            e->pf_xexp, e->st, true);
       if (rc) return rc;
       mark(e, K_GEMV);
     }
@@ -623,7 +625,7 @@ int bgemv(InfernoEngine* e, const DevTensor* W, int inner, std::initializer_list
     q.err = e->err;
     q.ws = e->qg_ws;
     q.tickets = e->qg_tickets;
-    rc = launch_qgemm(q, e->st, false);
+    rc = launch_qgemm(q, e->st, true);
     if (!rc) mark(e, K_GEMV);
     return rc;
   }
@@ -639,10 +641,9 @@ int enqueue_prefill_chunk(InfernoEngine* e, const int* toks, int T, int pos0, bo
   const InfernoConfig& c = e->cfg;
   const int H = c.hidden_size, I = c.intermediate_size, hdq = c.n_heads * c.head_dim;
   int rc;
-  for (int t = 0; t < T; ++t)
-    if ((rc = launch_embed_row(e->embd->type, e->embd->d, (long long)e->embd->bytes / e->embd->rows(), H, toks + t,
-                               e->xb + (size_t)t * H, c.vocab_size, e->st, false)))
-      return set_error(INFERNO_ECUDA, "prefill embedding launch failed (%d)", rc);
+  if ((rc = launch_embed_row(e->embd->type, e->embd->d, (long long)e->embd->bytes / e->embd->rows(), H, toks, e->xb,
+                             c.vocab_size, e->st, false, T)))
+    return set_error(INFERNO_ECUDA, "prefill embedding launch failed (%d)", rc);
   for (int li = 0; li < c.num_layers; ++li) {
     LayerBind& L = e->layers[li];
     const float* an = (const float*)L.attn_norm->d;
@@ -1491,10 +1492,9 @@ int enqueue_batch_step(InfernoEngine* e, int B) {
   const int kvd = c.n_kv_heads * c.head_dim;
   const size_t kvs = (size_t)c.max_ctx * kvd;
   int rc;
-  for (int b = 0; b < B; ++b)
-    if ((rc = launch_embed_row(e->embd->type, e->embd->d, (long long)e->embd->bytes / e->embd->rows(), H,
-                               e->bt_tok + b, e->xb + (size_t)b * H, c.vocab_size, e->st, false)))
-      return set_error(INFERNO_ECUDA, "batch embedding launch failed (%d)", rc);
+  if ((rc = launch_embed_row(e->embd->type, e->embd->d, (long long)e->embd->bytes / e->embd->rows(), H, e->bt_tok,
+                             e->xb, c.vocab_size, e->st, false, B)))
+    return set_error(INFERNO_ECUDA, "batch embedding launch failed (%d)", rc);
   for (int li = 0; li < c.num_layers; ++li) {
     LayerBind& L = e->layers[li];
     const float* an = (const float*)L.attn_norm->d;

@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(FG_THREADS, 1) fused_inproj_gdn_kernel(const _
     const float colscale = gemv_mma_prologue<T_Q4_K, NW, MMA_PLAIN>(p, xf, xq, xsum, red, vmax, tid);
     const bool nonfinite = *(volatile int*)&red[2 * NW] != 0;
     const float fscale =
-        nonfinite ? __int_as_float(0x7fc00000) : colscale * ldexpf(1.0f, -mma_exp2_scale(vmax[0]));
+        nonfinite ? __int_as_float(0x7fc00000) : colscale * mma_pow2(-mma_exp2_scale(vmax[0]));
     const int nkg = NW / 4, rg = warp % 4, wk = warp / 4;     // TR = 64: 4 row groups x 4 K groups
     const int gq = lane >> 2, c = lane & 3;
     const float limbw = c == 0 ? 1.0f : c == 1 ? 256.0f : c == 2 ? 65536.0f : 16777216.0f;

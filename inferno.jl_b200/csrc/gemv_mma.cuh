@@ -100,9 +100,17 @@ __device__ __forceinline__ int mma_xsum_slot(int ks, int p) {
 // vmax[] and the flag must be zero on entry.
 __device__ __forceinline__ int mma_exp2_scale(float vmax) {
   int e = 0;
-  if (vmax > 0.f && vmax <= 3.0e38f) frexpf(vmax, &e);   // vmax < 2^e
+  if (vmax > 0.f && vmax <= 3.0e38f) {
+    // frexp exponent (vmax < 2^e): from the IEEE exponent field for normal
+    // numbers, the library routine for subnormals
+    const int be = (__float_as_int(vmax) >> 23) & 0xff;
+    if (be > 0) e = be - 126;
+    else frexpf(vmax, &e);
+  }
   return max(-120, min(120, 30 - e));
 }
+// 2^k for |k| <= 120 (a normal float), built from its exponent field
+__device__ __forceinline__ float mma_pow2(int k) { return __int_as_float((k + 127) << 23); }
 
 template <int TYPE, int NW, int MODE>
 __device__ float gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, float* xsum, float* red,
@@ -235,7 +243,7 @@ __device__ float gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, 
   // limbs: one thread per quad (ks, cc) = 4 elements of each k-half
   const int nqv = n >> 3;
   const size_t xq_vec = (size_t)(n >> 8) * 8 * MMA_KS_BYTES;
-  const float up0 = ldexpf(1.0f, mma_exp2_scale(vmax[0]));
+  const float up0 = mma_pow2(mma_exp2_scale(vmax[0]));
   if (!(vmax[0] <= 3.0e38f)) bad = true;
   for (int qq = tid; qq < nxv * nqv; qq += NT) {
     const int v = MODE == MMA_MOE ? qq / nqv : 0, q = qq - v * nqv;
@@ -243,7 +251,7 @@ __device__ float gemv_mma_prologue(const GemvParams& p, float* xf, uint8_t* xq, 
     if (MODE == MMA_MOE) {
       const float vm = vmax[v];
       if (!(vm <= 3.0e38f)) bad = true;
-      up = ldexpf(1.0f, mma_exp2_scale(vm));
+      up = mma_pow2(mma_exp2_scale(vm));
     }
     const int ks = q >> 2, cc = q & 3;
     const float* xfv = xf + (size_t)v * n;
@@ -399,7 +407,7 @@ __device__ float gemv_mma_prologue_reg(const GemvParams& p, uint8_t* xq, float* 
   }
   const float vm = vmax[0];
   if (!(vm <= 3.0e38f)) bad = true;
-  const float up = ldexpf(1.0f, mma_exp2_scale(vm));
+  const float up = mma_pow2(mma_exp2_scale(vm));
 #pragma unroll
   for (int j = 0; j < IT; ++j) {
     const int u = tid + j * NT;
@@ -680,7 +688,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
   const bool nonfinite = *(volatile int*)&red[2 * NW] != 0;
   const uint32_t xtag =
       (MODE == MMA_XCH && p.xch_wk >= 0) ? (uint32_t)(*p.xch_seq + (unsigned long long)p.xch_wk + 1ull) : 0u;
-  const float fscale0 = nonfinite ? __int_as_float(0x7fc00000) : colscale * ldexpf(1.0f, -mma_exp2_scale(vmax[0]));
+  const float fscale0 = nonfinite ? __int_as_float(0x7fc00000) : colscale * mma_pow2(-mma_exp2_scale(vmax[0]));
 
   const bool paired = (p.epi == EPI_SWIGLU);
   const int nrg = p.TR >> 4;            // 16-row groups per tile
@@ -693,6 +701,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
 
   for (int it = 0; it < n_items; ++it) {
     const int s = it % p.stages;
+    if (tid == 0 && it == 0) GEMV_DBG(p, 10);
     if (!mbar_wait(&full[s], (it / p.stages) & 1, p.err)) return;
     if (tid == 0 && it == 0) KT_LAST(p.trace, 5);
     if (tid == 0 && it == 0) GEMV_DBG(p, 5);
@@ -719,7 +728,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
     const uint8_t* xq_t = xq + slot * xq_vec;
     const float* xsum_t = xsum + slot * nsb * 16;
     const float fscale = (MODE == MMA_MOE && slot) ? (nonfinite ? __int_as_float(0x7fc00000)
-                                                                : colscale * ldexpf(1.0f, -mma_exp2_scale(vmax[slot])))
+                                                                : colscale * mma_pow2(-mma_exp2_scale(vmax[slot])))
                                                    : fscale0;
     float acc[2] = {0.f, 0.f}, corr[2] = {0.f, 0.f};
     const bool skip_tile = seg_skipped<MODE == MMA_MOE>(p, sg, row0);

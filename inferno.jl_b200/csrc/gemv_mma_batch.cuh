@@ -89,7 +89,7 @@ __device__ void gemv_mma_batch_prologue(const GemvParams& p, uint8_t* xq, float*
   ss = warp_sum(ss);
   amax = warp_max(amax);
   if (!(amax <= 3.0e38f)) bad = true;
-  const float up = ldexpf(1.0f, mma_exp2_scale(amax));
+  const float up = mma_pow2(mma_exp2_scale(amax));
   uint8_t* xqv = xq + (size_t)v * nsb * 8 * MMA_KSC_BYTES;
   float* xs = xsum + (size_t)v * nsb * 16;
   // nf4 is a multiple of 64 (n % 256 == 0): every lane runs every iteration
@@ -311,7 +311,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) gemv_mma_batch_kernel(const 
   float fscale[MMA_NBT];
 #pragma unroll
   for (int v = 0; v < MMA_NBT; ++v)
-    fscale[v] = v < ncol ? (bad[v] ? __int_as_float(0x7fc00000) : cs[v] * ldexpf(1.0f, -mma_exp2_scale(vmax[v])))
+    fscale[v] = v < ncol ? (bad[v] ? __int_as_float(0x7fc00000) : cs[v] * mma_pow2(-mma_exp2_scale(vmax[v])))
                          : 0.f;
 
   const bool paired = (p.epi == EPI_SWIGLU);

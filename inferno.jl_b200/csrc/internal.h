@@ -198,7 +198,7 @@ void build_rope(int ctx, int rd, float theta, std::vector<float>& cs, std::vecto
 // multiple of 32 giving at most 128 splits)
 int attn_split_len(int max_ctx);
 int launch_embed_row(int type, const void* W, long long row_bytes, int inner, const int* row_ptr, float* dst,
-                     int vocab, cudaStream_t st, bool pdl);
+                     int vocab, cudaStream_t st, bool pdl, int nrows = 1);
 
 // device error word of the library (per device)
 int* device_error_word(int device);

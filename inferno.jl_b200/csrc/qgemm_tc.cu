@@ -70,8 +70,10 @@ struct QgParams {
   int nbs, nas, nrs;     // ring stages: activation tiles, dequantized A tiles, raw super-blocks
   int split;
   int trace;             // debug: %globaltimer stamps of CTA (0,0,0) into qg_trace
-  int dbgmode;           // debug timing only (wrong results): 1 = no MMAs, 2 = no dequantization,
-                         // 3 = no proxy fence, 4 = no weight staging after the first stages
+  int dbgmode;           // debug timing only (wrong results), bits: 1 no MMAs, 2 no dequantization,
+                         // 4 no proxy fence, 8 no weight staging after the first stages,
+                         // 16 no activation loads, 32 one MMA per K slice instead of three, 64 polling waits,
+                         // 128 plain arrivals instead of MMA commits
   float* ws;             // split K: [tile][slice][BN][128] fp32 partial tiles
   int* tickets;          // split K: arrivals per output tile (zero between launches)
   const float* xexp;     // [T] power-of-two exponent applied to each token's fp16 activations
@@ -352,6 +354,22 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   return *(const uint32_t*)&h;
 }
 
+// bounded wait that polls with mbarrier.test_wait (no suspend hint)
+__device__ __forceinline__ bool qg_wait(uint64_t* bar, uint32_t parity, int* err, bool spin) {
+  if (!spin) return mbar_wait(bar, parity, err);
+  for (uint32_t i = 0; i < (1u << 28); ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  if (err) atomicExch(err, DERR_MBAR_TIMEOUT);
+  return false;
+}
+
 // debug timeline of one CTA (QgParams::trace): 16 %globaltimer stamps
 __device__ unsigned long long qg_trace[16];
 #define QG_STAMP(i)                                                                          \
@@ -367,6 +385,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   const int split = p.split;
   const int nsplit = split ? 2 : 1;
   const int NA = p.nas, NR = p.nrs, NB = p.nbs;
+  const bool spin = (p.dbgmode & 64) != 0;
   // ---- shared memory carve-up (1024-byte aligned operand tiles) ----
   uint8_t* base = (uint8_t*)(((uintptr_t)qg_smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = base;                                        // [NA][nsplit][16 KB]
@@ -424,7 +443,11 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       const uint32_t bx = (uint32_t)btile;
       for (int i = 0; i < nk; ++i) {
         const int bs = i % NB;
-        if (i >= NB && !mbar_wait(&b_empty[bs], ((i / NB) - 1) & 1, p.err)) break;
+        if (i >= NB && !qg_wait(&b_empty[bs], ((i / NB) - 1) & 1, p.err, spin)) break;
+        if (p.dbgmode & 16) {          // debug timing: no activation loads
+          mbar_arrive(&b_full[bs]);
+          continue;
+        }
         mbar_arrive_expect_tx(&b_full[bs], bx * nsplit);
         uint8_t* bd = sB + (size_t)bs * nsplit * btile;
         const int kx = (4 * sb0 + i) * QG_BK;
@@ -440,7 +463,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       bool ok = true;
       for (int i = 0; i < nk && ok; ++i) {
         const int as = i % NA, bs = i % NB;
-        ok = mbar_wait(&a_full[as], (i / NA) & 1, p.err) && mbar_wait(&b_full[bs], (i / NB) & 1, p.err);
+        ok = qg_wait(&a_full[as], (i / NA) & 1, p.err, spin) && qg_wait(&b_full[bs], (i / NB) & 1, p.err, spin);
         if (!ok) break;
         tc_fence_after();
         if (i == 0) QG_STAMP(3);
@@ -450,13 +473,18 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         const uint64_t dal = umma_desc_sw128(a_hi + QG_ATILE), dbl = umma_desc_sw128(b_hi + btile);
 #pragma unroll
         for (int kk = 0; kk < QG_BK / 16; ++kk) {
-          if (p.dbgmode == 1) break;
+          if (p.dbgmode & 1) break;
           const uint64_t o = (uint64_t)(2 * kk);     // +32 bytes along K
           umma_f16(tbase, dah + o, dbh + o, idesc, (i | kk) != 0);
-          if (split) {
+          if (split && !(p.dbgmode & 32)) {
             umma_f16(tbase, dah + o, dbl + o, idesc, 1);
             umma_f16(tbase, dal + o, dbh + o, idesc, 1);
           }
+        }
+        if (p.dbgmode & 128) {        // debug timing: plain arrivals instead of MMA commits
+          mbar_arrive(&a_empty[as]);
+          mbar_arrive(&b_empty[bs]);
+          continue;
         }
         umma_commit(&a_empty[as]);
         umma_commit(&b_empty[bs]);
@@ -497,19 +525,19 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     bool ok = true;
     for (int i = 0; i < nk && ok; ++i) {
       const int j = i >> 2, ks = i & 3, rs = j % NR, as = i % NA;
-      if (ks == 0 && p.dbgmode != 4) {
+      if (ks == 0 && !(p.dbgmode & 8)) {
         __syncwarp();                 // the row's threads are done with stage (j - 1) % NR
         stage_raw(j + NR - 1);
         if (NR == 3) asm volatile("cp.async.wait_group 2;" ::: "memory");
         else asm volatile("cp.async.wait_group 1;" ::: "memory");
         __syncwarp();                 // the row's four threads' copies are visible
       }
-      if (i >= NA) ok = mbar_wait(&a_empty[as], ((i / NA) - 1) & 1, p.err);
+      if (i >= NA) ok = qg_wait(&a_empty[as], ((i / NA) - 1) & 1, p.err, spin);
       if (!ok) break;
       if (tid == 64 && i == 0) QG_STAMP(2);
       uint8_t* ah = sA + (size_t)as * nsplit * QG_ATILE;
       uint32_t h[8], l[8];
-      if (dvalid && p.dbgmode != 2) {
+      if (dvalid && !(p.dbgmode & 2)) {
         const uintptr_t a = rowsrc + (uintptr_t)(sb0 + j) * QgBlk<TYPE>::BB;
         const uint8_t* rp = myraw + (size_t)rs * QG_M * p.slot + (a & 15);
         qg_dq16_split<TYPE>(rp, smem_u32(rp), ks, dseg, wscale, h, l);
@@ -524,7 +552,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         sts128(sa, h[4 * cc], h[4 * cc + 1], h[4 * cc + 2], h[4 * cc + 3]);
         if (split) sts128(sa + QG_ATILE, l[4 * cc], l[4 * cc + 1], l[4 * cc + 2], l[4 * cc + 3]);
       }
-      if (p.dbgmode != 3) fence_proxy_async_smem();
+      if (!(p.dbgmode & 4)) fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[as]);
     }
@@ -913,7 +941,8 @@ int launch_qgemm(const QgemmCall& c, cudaStream_t st, bool pdl) {
   // the depth (up to 8 stages); dequantized A tiles need only two stages (the
   // dequantizing warps work one step ahead of the MMA), the raw super-block
   // ring three (two super-blocks of HBM prefetch).
-  int nas = 2, nrs = 3, nbs = 8;
+  static const int env_nas = getenv("INFERNO_QG_NAS") ? atoi(getenv("INFERNO_QG_NAS")) : 2;
+  int nas = env_nas, nrs = 3, nbs = 8;
   auto need = [&] { return nas * astage + nrs * rstage + nbs * bstage; };
   while (need() > cap && nbs > 3) --nbs;
   while (need() > cap && nrs > 2) --nrs;
