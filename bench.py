@@ -556,6 +556,7 @@ def measure_big(workload, steps, warmup, ws, rank, local):
     peak = float(peaks.get("hbm_gbs", 6650.0))
     # weights are read once per batched step: bytes per step, not per token
     per_gpu_gbs = tok_bytes / (ws if tp else 1) / (ms_step / ND / 1000.0) / 1e9
+    comm = m.comm_mode()
     line = {"metric": W["metric"], "value": value, "unit": UNIT, "n_gpus": ws, "steps": steps,
             "warmup": warmup, "ms_per_step": ms_step, "higher_is_better": True,
             "scaling": "strong" if tp else "weak", "vs_baseline": None,
@@ -571,9 +572,10 @@ def measure_big(workload, steps, warmup, ws, rank, local):
                                "frac": per_gpu_gbs / peak, "peak": peak},
             "ms_per_token": ms_step / ND, "prefill_s": prefill_s,
             "prefill_tokens_per_s": P / prefill_s,
-            "comm": ("NCCL all-reduce of the residual after each expert FFN" if spec.n_experts else
-                     ("fused peer-memory residual exchange in the GEMV epilogue / prologue" if not
-                      os.environ.get("INFERNO_TP_NCCL") else "NCCL all-reduce of the residual")) if tp else None}
+            "comm": {"peer-exchange": "fused peer-memory residual exchange in the GEMV epilogue / prologue"
+                              + (" (expert FFN partials)" if spec.n_experts else ""),
+                     "nccl": "NCCL all-reduce of the residual",
+                     "none": None}[comm] if tp else None}
     m.close()
     return line
 

@@ -310,6 +310,12 @@ int inferno_state_restore_device(InfernoEngine* eng);
 /* Kernels launched per decode token by this engine (for launch accounting). */
 int inferno_kernels_per_token(InfernoEngine* eng);
 
+/* How a sharded engine (tp_size > 1) sums residuals across ranks: 0 = not
+ * sharded, 1 = the fused peer-memory exchange in the GEMV epilogue/prologue,
+ * 2 = NCCL all-reduce.  No counterpart in the reference (which runs on one
+ * device); reporting only. */
+int inferno_comm_mode(InfernoEngine* eng);
+
 /* Profiling pass: runs n_tokens greedy steps eagerly (no graph, no PDL) with
  * CUDA events between kernels and accumulates device time per kernel class:
  * [0] embedding, [1] layer GEMVs, [2] GDN step, [3] attention, [4] lm_head

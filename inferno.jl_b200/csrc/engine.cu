@@ -2152,6 +2152,13 @@ int inferno_state_restore_device(InfernoEngine* e) {
   return 0;
 }
 
+int inferno_comm_mode(InfernoEngine* e) {
+  int rc;
+  if ((rc = ready(e))) return rc;
+  if (e->cfg.tp_size <= 1) return 0;
+  return e->xch ? 1 : 2;
+}
+
 int inferno_kernels_per_token(InfernoEngine* e) {
   int rc;
   if ((rc = ready(e))) return rc;

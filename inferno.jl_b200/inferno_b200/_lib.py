@@ -48,7 +48,7 @@ EXPORTS = [
     "inferno_layer_forward", "inferno_forward_tokens", "inferno_decode_greedy",
     "inferno_reset_states", "inferno_dump_hidden", "inferno_state_size", "inferno_state_export",
     "inferno_state_import", "inferno_last_decode_ms", "inferno_engine_destroy",
-    "inferno_state_save_device", "inferno_state_restore_device", "inferno_kernels_per_token",
+    "inferno_state_save_device", "inferno_state_restore_device", "inferno_kernels_per_token", "inferno_comm_mode",
     "inferno_profile_tokens", "inferno_gemv_host_noalloc", "inferno_debug_trace", "inferno_tp_unique_id",
     "inferno_gdn_recurrence", "inferno_gdn_chunked", "inferno_attention_step", "inferno_select_sequence", "inferno_decode_batch", "inferno_forward_tokens_all", "inferno_debug_xch_timeout", "inferno_sample_logits", "inferno_decode_sample",
     "inferno_gguf_open", "inferno_gguf_close", "inferno_gguf_version", "inferno_gguf_n_tensors", "inferno_gguf_n_kv",
@@ -111,6 +111,7 @@ def _sig(L0):
     L.inferno_state_save_device.argtypes = [p]
     L.inferno_state_restore_device.argtypes = [p]
     L.inferno_kernels_per_token.argtypes = [p]
+    L.inferno_comm_mode.argtypes = [p]
     L.inferno_profile_tokens.argtypes = [p, C.c_int32, i, i, p, p]
     L.inferno_decode_sample.argtypes = [p, C.c_int32, i, i, p, p, i, p]
     L.inferno_gguf_open.argtypes = [C.c_char_p, p]

@@ -320,6 +320,11 @@ class Model:
     def restore_device(self):
         call("inferno_state_restore_device", self.h)
 
+    def comm_mode(self) -> str:
+        """How the ranks of a sharded engine sum residuals."""
+        m = check(lib().inferno_comm_mode(self.h), "inferno_comm_mode")
+        return {0: "none", 1: "peer-exchange", 2: "nccl"}[m]
+
     def kernels_per_token(self) -> int:
         return check(lib().inferno_kernels_per_token(self.h), "inferno_kernels_per_token")
 
