@@ -136,14 +136,17 @@ __global__ void __launch_bounds__(WY_THREADS) gdn_wy_prep_kernel(int T, int H, i
 }
 
 // Grid (H, dv / 16), 256 threads.  Rows r0..r0+15 of S_h live in shared
-// memory across the chunks.
+// memory across the chunks, transposed (St[d][i]) so that a thread reads four
+// rows' values of one column as one 16-byte load.  Register tiles: in the D
+// and Y products a thread owns token t and rows i0..i0+3; in the S update
+// column d and eight rows.
 __global__ void __launch_bounds__(WY_THREADS) gdn_wy_state_kernel(int T, int H, int dv, const float* __restrict__ q,
                                                                   const float* __restrict__ k, float* S, float* y,
                                                                   WyScratch o) {
-  extern __shared__ float wsm[];
+  extern __shared__ __align__(16) float wsm[];
   constexpr int KP = WY_DK + 1;
-  float* Ss = wsm;                          // [16][KP]
-  float* Ws = Ss + WY_ROWS * KP;            // [C][KP]
+  float* St = wsm;                          // [dk][16]
+  float* Ws = St + WY_DK * WY_ROWS;         // [C][KP]
   float* Ks = Ws + WY_C * KP;               // [C][KP]
   float* Qs = Ks + WY_C * KP;               // [C][KP]
   float* Ds = Qs + WY_C * KP;               // [C][16]  D rows of this CTA
@@ -154,8 +157,11 @@ __global__ void __launch_bounds__(WY_THREADS) gdn_wy_state_kernel(int T, int H, 
   const int h = blockIdx.x, r0 = blockIdx.y * WY_ROWS, tid = threadIdx.x;
   for (int i = tid; i < WY_ROWS * WY_DK; i += WY_THREADS) {
     const int r = i / WY_DK, d = i % WY_DK;
-    Ss[r * KP + d] = S[((size_t)h * dv + r0 + r) * WY_DK + d];
+    St[d * WY_ROWS + r] = S[((size_t)h * dv + r0 + r) * WY_DK + d];
   }
+  // D / Y tile: token tt, rows i0..i0+3; S tile: column sd, rows si0..si0+7
+  const int tt = tid >> 2, i0 = (tid & 3) * 4;
+  const int sd = tid & (WY_DK - 1), si0 = (tid >> 7) * 8;
   const int nch = (T + WY_C - 1) / WY_C;
   for (int c = 0; c < nch; ++c) {
     const int t0 = c * WY_C, n = min(WY_C, T - t0);
@@ -178,39 +184,81 @@ __global__ void __launch_bounds__(WY_THREADS) gdn_wy_state_kernel(int T, int H, 
       DEs[tid] = tid < n ? expf(glast - gt) : 0.f;
     }
     __syncthreads();
-    // D[t][i] = U[t][i] - W[t] . S[i]   (1024 entries, 4 per thread)
-    const float* Ug = o.U + ((size_t)c * H + h) * WY_C * dv;
-    for (int e = tid; e < WY_C * WY_ROWS; e += WY_THREADS) {
-      const int t = e / WY_ROWS, i = e % WY_ROWS;
-      float acc = Ug[t * dv + r0 + i];
-      for (int d = 0; d < WY_DK; ++d) acc = fmaf(-Ws[t * KP + d], Ss[i * KP + d], acc);
-      Ds[t * WY_ROWS + i] = acc;
+    // D[t][i] = U[t][i] - W[t] . S[i]
+    {
+      const float* Ug = o.U + ((size_t)c * H + h) * WY_C * dv + (size_t)tt * dv + r0 + i0;
+      float a0 = Ug[0], a1 = Ug[1], a2 = Ug[2], a3 = Ug[3];
+      const float* wr = Ws + tt * KP;
+#pragma unroll 8
+      for (int d = 0; d < WY_DK; ++d) {
+        const float w = wr[d];
+        const float4 s4 = *(const float4*)&St[d * WY_ROWS + i0];
+        a0 = fmaf(-w, s4.x, a0);
+        a1 = fmaf(-w, s4.y, a1);
+        a2 = fmaf(-w, s4.z, a2);
+        a3 = fmaf(-w, s4.w, a3);
+      }
+      *(float4*)&Ds[tt * WY_ROWS + i0] = make_float4(a0, a1, a2, a3);
     }
     __syncthreads();
     // Y[t][i] = e^{G_t} Q[t] . S[i] + sum_{j<=t} P[t][j] D[j][i]
-    for (int e = tid; e < WY_C * WY_ROWS; e += WY_THREADS) {
-      const int t = e / WY_ROWS, i = e % WY_ROWS;
-      if (t >= n) continue;
-      float qs = 0.f;
-      for (int d = 0; d < WY_DK; ++d) qs = fmaf(Qs[t * KP + d], Ss[i * KP + d], qs);
-      float acc = EGs[t] * qs;
-      for (int j = 0; j <= t; ++j) acc = fmaf(Ps[t * WY_C + j], Ds[j * WY_ROWS + i], acc);
-      y[((size_t)(t0 + t) * H + h) * dv + r0 + i] = acc;
+    if (tt < n) {
+      float q0 = 0.f, q1 = 0.f, q2 = 0.f, q3 = 0.f;
+      const float* qr = Qs + tt * KP;
+#pragma unroll 8
+      for (int d = 0; d < WY_DK; ++d) {
+        const float qv = qr[d];
+        const float4 s4 = *(const float4*)&St[d * WY_ROWS + i0];
+        q0 = fmaf(qv, s4.x, q0);
+        q1 = fmaf(qv, s4.y, q1);
+        q2 = fmaf(qv, s4.z, q2);
+        q3 = fmaf(qv, s4.w, q3);
+      }
+      const float eg = EGs[tt];
+      float a0 = eg * q0, a1 = eg * q1, a2 = eg * q2, a3 = eg * q3;
+      const float* pr = Ps + tt * WY_C;
+      for (int j = 0; j <= tt; ++j) {
+        const float pv = pr[j];
+        const float4 d4 = *(const float4*)&Ds[j * WY_ROWS + i0];
+        a0 = fmaf(pv, d4.x, a0);
+        a1 = fmaf(pv, d4.y, a1);
+        a2 = fmaf(pv, d4.z, a2);
+        a3 = fmaf(pv, d4.w, a3);
+      }
+      float* yo = y + ((size_t)(t0 + tt) * H + h) * dv + r0 + i0;
+      yo[0] = a0;
+      yo[1] = a1;
+      yo[2] = a2;
+      yo[3] = a3;
     }
     __syncthreads();
     // S[i][d] = e^{G_last} S[i][d] + sum_j e^{G_last - G_j} D[j][i] K[j][d]
-    const float egl = EGs[n - 1];
-    for (int e = tid; e < WY_ROWS * WY_DK; e += WY_THREADS) {
-      const int i = e / WY_DK, d = e % WY_DK;
-      float acc = egl * Ss[i * KP + d];
-      for (int j = 0; j < n; ++j) acc = fmaf(DEs[j] * Ds[j * WY_ROWS + i], Ks[j * KP + d], acc);
-      Ss[i * KP + d] = acc;
+    {
+      const float egl = EGs[n - 1];
+      float acc[8];
+      const float4 sa = *(const float4*)&St[sd * WY_ROWS + si0], sb = *(const float4*)&St[sd * WY_ROWS + si0 + 4];
+      acc[0] = egl * sa.x; acc[1] = egl * sa.y; acc[2] = egl * sa.z; acc[3] = egl * sa.w;
+      acc[4] = egl * sb.x; acc[5] = egl * sb.y; acc[6] = egl * sb.z; acc[7] = egl * sb.w;
+      for (int j = 0; j < n; ++j) {
+        const float kk = Ks[j * KP + sd], de = DEs[j];
+        const float4 da = *(const float4*)&Ds[j * WY_ROWS + si0], db = *(const float4*)&Ds[j * WY_ROWS + si0 + 4];
+        acc[0] = fmaf(de * da.x, kk, acc[0]);
+        acc[1] = fmaf(de * da.y, kk, acc[1]);
+        acc[2] = fmaf(de * da.z, kk, acc[2]);
+        acc[3] = fmaf(de * da.w, kk, acc[3]);
+        acc[4] = fmaf(de * db.x, kk, acc[4]);
+        acc[5] = fmaf(de * db.y, kk, acc[5]);
+        acc[6] = fmaf(de * db.z, kk, acc[6]);
+        acc[7] = fmaf(de * db.w, kk, acc[7]);
+      }
+      *(float4*)&St[sd * WY_ROWS + si0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *(float4*)&St[sd * WY_ROWS + si0 + 4] = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
   }
   __syncthreads();
   for (int i = tid; i < WY_ROWS * WY_DK; i += WY_THREADS) {
     const int r = i / WY_DK, d = i % WY_DK;
-    S[((size_t)h * dv + r0 + r) * WY_DK + d] = Ss[r * KP + d];
+    S[((size_t)h * dv + r0 + r) * WY_DK + d] = St[d * WY_ROWS + r];
   }
 }
 
@@ -231,7 +279,7 @@ int launch_gdn_wy(int T, int H, int dv, const float* q, const float* k, const fl
   o.P = o.U + nch * H * WY_C * dv;
   o.G = o.P + nch * H * WY_C * WY_C;
   const size_t smem1 = ((size_t)2 * WY_C * (WY_DK + 1) + (size_t)WY_C * dv + (size_t)WY_C * (WY_C + 1) + 3 * WY_C) * 4;
-  const size_t smem2 = ((size_t)WY_ROWS * (WY_DK + 1) + 3 * (size_t)WY_C * (WY_DK + 1) + (size_t)WY_C * WY_ROWS +
+  const size_t smem2 = ((size_t)WY_ROWS * WY_DK + 3 * (size_t)WY_C * (WY_DK + 1) + (size_t)WY_C * WY_ROWS +
                         (size_t)WY_C * WY_C + 3 * WY_C) * 4;
   static DeviceOnce once;
   cudaError_t ea = once.run([] {

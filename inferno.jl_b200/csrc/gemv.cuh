@@ -95,7 +95,7 @@ struct GemvParams {
   unsigned long long* xch_parts[8];  // each rank's [2][n][H] words
   float* x_next;
   unsigned long long* trace;      // debug: 8 timeline slots of this launch (KT_*; null = off)
-  int dbg;                        // debug: stamps of CTA 0 / the last CTA into gemv_dbg (INFERNO_GEMV_DBG)
+  int dbg;                        // debug (-DINFERNO_KTRACE=1 builds): stamps into gemv_dbg (INFERNO_GEMV_DBG)
 };
 
 // debug timeline of the tensor-core GEMV (GemvParams::dbg): slots 0-15 CTA 0,
@@ -104,7 +104,7 @@ struct GemvParams {
 static __device__ unsigned long long gemv_dbg[32];
 #define GEMV_DBG(p, i)                                                             \
   do {                                                                             \
-    if ((p).dbg) {                                                                 \
+    if (INFERNO_KTRACE && (p).dbg) {                                               \
       if (blockIdx.x == 0) gemv_dbg[i] = gtimer();                                 \
       else if (blockIdx.x == gridDim.x - 1) gemv_dbg[16 + (i)] = gtimer();         \
     }                                                                              \

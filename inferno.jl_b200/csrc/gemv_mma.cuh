@@ -677,7 +677,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
   if (tid == 0) {
     KT_FIRST(p.trace, 2);
     KT_LAST(p.trace, 3);
-    if (p.dbg && blockIdx.x == 0) gemv_dbg[30] = gemv_dbg[16 + 7];
+    if (INFERNO_KTRACE && p.dbg && blockIdx.x == 0) gemv_dbg[30] = gemv_dbg[16 + 7];
     GEMV_DBG(p, 2);
   }
   const float colscale = reg_pro ? gemv_mma_prologue_reg<TYPE == T_Q6_KR ? T_Q6_K : TYPE, NW, MODE>(p, xq, xsum, red,
@@ -799,7 +799,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
   }
   if (tid == 0) KT_LAST(p.trace, 6);
   if (tid == 0) GEMV_DBG(p, 6);
-  if (p.dbg == 2 && reg_pro) {
+  if (INFERNO_KTRACE && p.dbg == 2 && reg_pro) {
     // debug: the register prologue once more, with its code now in the
     // instruction cache (slots 8 / 9 around it)
     named_bar_sync(1, NW * 32);

@@ -69,8 +69,8 @@ struct QgParams {
   int epi;               // QG_STORE / QG_ADD / QG_SWIGLU
   int nbs, nas, nrs;     // ring stages: activation tiles, dequantized A tiles, raw super-blocks
   int split;
-  int trace;             // debug: %globaltimer stamps of CTA (0,0,0) into qg_trace
-  int dbgmode;           // debug timing only (wrong results), bits: 1 no MMAs, 2 no dequantization,
+  int trace;             // debug (-DINFERNO_KTRACE=1 builds): %globaltimer stamps into qg_trace
+  int dbgmode;           // debug timing only (-DINFERNO_KTRACE=1 builds; wrong results), bits: 1 no MMAs, 2 no dequantization,
                          // 4 no proxy fence, 8 no weight staging after the first stages,
                          // 16 no activation loads, 32 one MMA per K slice instead of three, 64 polling waits,
                          // 128 plain arrivals instead of MMA commits
@@ -374,7 +374,7 @@ __device__ __forceinline__ bool qg_wait(uint64_t* bar, uint32_t parity, int* err
 __device__ unsigned long long qg_trace[16];
 #define QG_STAMP(i)                                                                          \
   do {                                                                                       \
-    if (p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) qg_trace[i] = gtimer(); \
+    if (INFERNO_KTRACE && p.trace && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) qg_trace[i] = gtimer(); \
   } while (0)
 
 template <int TYPE, int BN>
@@ -385,7 +385,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   const int split = p.split;
   const int nsplit = split ? 2 : 1;
   const int NA = p.nas, NR = p.nrs, NB = p.nbs;
-  const bool spin = (p.dbgmode & 64) != 0;
+  const bool spin = INFERNO_KTRACE && (p.dbgmode & 64);
   // ---- shared memory carve-up (1024-byte aligned operand tiles) ----
   uint8_t* base = (uint8_t*)(((uintptr_t)qg_smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* sA = base;                                        // [NA][nsplit][16 KB]
@@ -409,7 +409,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   const int rows_per_tile = swiglu ? QG_M / 2 : QG_M;
   const int r0 = (mt - p.seg[sg].mtile0) * rows_per_tile;
   if (tid == 0) QG_STAMP(0);
-  if (p.trace && tid == 0) atomicMax(&qg_trace[12], gtimer());       // latest CTA start
+  if (INFERNO_KTRACE && p.trace && tid == 0) atomicMax(&qg_trace[12], gtimer());       // latest CTA start
   const int sb0 = (int)((long long)kz * p.nsb / nz), sb1 = (int)((long long)(kz + 1) * p.nsb / nz);
   const int nsbz = sb1 - sb0, nk = 4 * nsbz;
 
@@ -444,7 +444,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       for (int i = 0; i < nk; ++i) {
         const int bs = i % NB;
         if (i >= NB && !qg_wait(&b_empty[bs], ((i / NB) - 1) & 1, p.err, spin)) break;
-        if (p.dbgmode & 16) {          // debug timing: no activation loads
+        if (INFERNO_KTRACE && (p.dbgmode & 16)) {          // debug timing: no activation loads
           mbar_arrive(&b_full[bs]);
           continue;
         }
@@ -473,15 +473,15 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         const uint64_t dal = umma_desc_sw128(a_hi + QG_ATILE), dbl = umma_desc_sw128(b_hi + btile);
 #pragma unroll
         for (int kk = 0; kk < QG_BK / 16; ++kk) {
-          if (p.dbgmode & 1) break;
+          if (INFERNO_KTRACE && (p.dbgmode & 1)) break;
           const uint64_t o = (uint64_t)(2 * kk);     // +32 bytes along K
           umma_f16(tbase, dah + o, dbh + o, idesc, (i | kk) != 0);
-          if (split && !(p.dbgmode & 32)) {
+          if (split && !(INFERNO_KTRACE && (p.dbgmode & 32))) {
             umma_f16(tbase, dah + o, dbl + o, idesc, 1);
             umma_f16(tbase, dal + o, dbh + o, idesc, 1);
           }
         }
-        if (p.dbgmode & 128) {        // debug timing: plain arrivals instead of MMA commits
+        if (INFERNO_KTRACE && (p.dbgmode & 128)) {        // debug timing: plain arrivals instead of MMA commits
           mbar_arrive(&a_empty[as]);
           mbar_arrive(&b_empty[bs]);
           continue;
@@ -525,7 +525,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     bool ok = true;
     for (int i = 0; i < nk && ok; ++i) {
       const int j = i >> 2, ks = i & 3, rs = j % NR, as = i % NA;
-      if (ks == 0 && !(p.dbgmode & 8)) {
+      if (ks == 0 && !(INFERNO_KTRACE && (p.dbgmode & 8))) {
         __syncwarp();                 // the row's threads are done with stage (j - 1) % NR
         stage_raw(j + NR - 1);
         if (NR == 3) asm volatile("cp.async.wait_group 2;" ::: "memory");
@@ -537,7 +537,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       if (tid == 64 && i == 0) QG_STAMP(2);
       uint8_t* ah = sA + (size_t)as * nsplit * QG_ATILE;
       uint32_t h[8], l[8];
-      if (dvalid && !(p.dbgmode & 2)) {
+      if (dvalid && !(INFERNO_KTRACE && (p.dbgmode & 2))) {
         const uintptr_t a = rowsrc + (uintptr_t)(sb0 + j) * QgBlk<TYPE>::BB;
         const uint8_t* rp = myraw + (size_t)rs * QG_M * p.slot + (a & 15);
         qg_dq16_split<TYPE>(rp, smem_u32(rp), ks, dseg, wscale, h, l);
@@ -552,7 +552,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         sts128(sa, h[4 * cc], h[4 * cc + 1], h[4 * cc + 2], h[4 * cc + 3]);
         if (split) sts128(sa + QG_ATILE, l[4 * cc], l[4 * cc + 1], l[4 * cc + 2], l[4 * cc + 3]);
       }
-      if (!(p.dbgmode & 4)) fence_proxy_async_smem();
+      if (!(INFERNO_KTRACE && (p.dbgmode & 4))) fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&a_full[as]);
     }
@@ -668,8 +668,8 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     tmem_dealloc(tbase, BN < 32 ? 32 : BN);
   }
   if (tid == 32) QG_STAMP(10);
-  if (p.trace && tid == 32) atomicMax(&qg_trace[11], gtimer());      // latest CTA end
-  if (p.trace && tid == 64 && p.seg[0].rows > 0) atomicMax(&qg_trace[13], (unsigned long long)(nk));
+  if (INFERNO_KTRACE && p.trace && tid == 32) atomicMax(&qg_trace[11], gtimer());      // latest CTA end
+  if (INFERNO_KTRACE && p.trace && tid == 64 && p.seg[0].rows > 0) atomicMax(&qg_trace[13], (unsigned long long)(nk));
 }
 
 // ---------------------------------------------------------------------------
