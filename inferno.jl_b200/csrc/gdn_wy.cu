@@ -35,6 +35,17 @@ struct WyScratch {
   float* G;   // [nch][H][C]
 };
 
+// 4-byte asynchronous copy global -> shared (zero fill when !valid): a CTA
+// issues a whole chunk's operands at once and waits once, instead of one
+// dependent load round trip per loop iteration
+__device__ __forceinline__ void wy_cp4(float* dst, const float* src, bool valid) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 4 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void wy_cp_wait() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_all;" ::: "memory");
+}
+
 // smem: K, Q [C][dk+1] (padded rows), V [C][dv], A/T [C][C+1], G, beta
 __global__ void __launch_bounds__(WY_THREADS) gdn_wy_prep_kernel(int T, int H, int dv, const float* __restrict__ q,
                                                                  const float* __restrict__ k,
@@ -55,18 +66,22 @@ __global__ void __launch_bounds__(WY_THREADS) gdn_wy_prep_kernel(int T, int H, i
   for (int i = tid; i < WY_C * WY_DK; i += WY_THREADS) {
     const int t = i / WY_DK, d = i % WY_DK;
     const bool ok = t < n;
-    Ks[t * KP + d] = ok ? k[((size_t)(t0 + t) * H + h) * WY_DK + d] : 0.f;
-    Qs[t * KP + d] = ok ? q[((size_t)(t0 + t) * H + h) * WY_DK + d] : 0.f;
+    const size_t src = ok ? ((size_t)(t0 + t) * H + h) * WY_DK + d : 0;
+    wy_cp4(&Ks[t * KP + d], k + src, ok);
+    wy_cp4(&Qs[t * KP + d], q + src, ok);
   }
   for (int i = tid; i < WY_C * dv; i += WY_THREADS) {
     const int t = i / dv, e = i % dv;
-    Vs[i] = t < n ? v[((size_t)(t0 + t) * H + h) * dv + e] : 0.f;
+    const bool ok = t < n;
+    wy_cp4(&Vs[i], v + (ok ? ((size_t)(t0 + t) * H + h) * dv + e : 0), ok);
   }
   if (tid < WY_C) {
     const bool ok = tid < n;
-    Gs[tid] = ok ? g[(size_t)(t0 + tid) * H + h] : 0.f;
-    Bs[tid] = ok ? beta[(size_t)(t0 + tid) * H + h] : 0.f;
+    const size_t src = ok ? (size_t)(t0 + tid) * H + h : 0;
+    wy_cp4(&Gs[tid], g + src, ok);
+    wy_cp4(&Bs[tid], beta + src, ok);
   }
+  wy_cp_wait();
   __syncthreads();
   // inclusive prefix sum of g (one warp, two tokens per lane)
   if (tid < 32) {
@@ -170,12 +185,14 @@ __global__ void __launch_bounds__(WY_THREADS) gdn_wy_state_kernel(int T, int H, 
     for (int i = tid; i < WY_C * WY_DK; i += WY_THREADS) {
       const int t = i / WY_DK, d = i % WY_DK;
       const bool ok = t < n;
-      Ws[t * KP + d] = Wg[i];
-      Ks[t * KP + d] = ok ? k[((size_t)(t0 + t) * H + h) * WY_DK + d] : 0.f;
-      Qs[t * KP + d] = ok ? q[((size_t)(t0 + t) * H + h) * WY_DK + d] : 0.f;
+      const size_t src = ok ? ((size_t)(t0 + t) * H + h) * WY_DK + d : 0;
+      wy_cp4(&Ws[t * KP + d], Wg + i, true);
+      wy_cp4(&Ks[t * KP + d], k + src, ok);
+      wy_cp4(&Qs[t * KP + d], q + src, ok);
     }
     const float* Pg = o.P + ((size_t)c * H + h) * WY_C * WY_C;
-    for (int i = tid; i < WY_C * WY_C; i += WY_THREADS) Ps[i] = Pg[i];
+    for (int i = tid; i < WY_C * WY_C; i += WY_THREADS) wy_cp4(&Ps[i], Pg + i, true);
+    wy_cp_wait();
     if (tid < WY_C) {
       const float gt = o.G[((size_t)c * H + h) * WY_C + tid];
       const float glast = o.G[((size_t)c * H + h) * WY_C + (n - 1)];

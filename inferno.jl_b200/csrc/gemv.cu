@@ -90,6 +90,8 @@ cudaError_t launch_mma_nw(const GemvParams& p, int grid, size_t smem, cudaStream
   bool moe = p.nxv > 1;
   for (int i = 0; i < p.nseg; ++i) moe |= p.seg[i].indirect != 0;
   if (moe) return launch_mma_mode<TYPE, MMA_MOE, NW>(p, grid, smem, st, pdl);
+  if (p.pro != PRO_RMSNORM && p.pro != PRO_NONE) return launch_mma_mode<TYPE, MMA_GATE, NW>(p, grid, smem, st, pdl);
+  if (p.epi == EPI_SWIGLU) return launch_mma_mode<TYPE, MMA_SWIGLU, NW>(p, grid, smem, st, pdl);
   return launch_mma_mode<TYPE, MMA_PLAIN, NW>(p, grid, smem, st, pdl);
 }
 

@@ -39,7 +39,11 @@ constexpr int MMA_KS_BYTES = 256;     // B bytes per k step (8 columns x 32 k)
 // of the MoE (expert-indirect rows, several input vectors) or tensor-parallel
 // exchange paths -- every launch fetches its instructions cold, and unused
 // branches inlined into the hot path cost measurable time per launch.
-enum MmaMode : int { MMA_PLAIN = 0, MMA_MOE = 1, MMA_XCH = 2 };
+// The plain per-token GEMVs are split further by what they run: MMA_PLAIN
+// (register prologue, one row per tile row: store / add / argmax),
+// MMA_SWIGLU (register prologue, gate and up rows paired), MMA_GATE (the
+// general prologue, e.g. head-norm x SiLU(z) of the ssm_out input).
+enum MmaMode : int { MMA_PLAIN = 0, MMA_MOE = 1, MMA_XCH = 2, MMA_GATE = 3, MMA_SWIGLU = 4 };
 // The super-block bodies' outer loops are not unrolled: the per-layer GEMVs
 // are latency-bound and every launch fetches its code cold, so code size
 // matters more than loop overhead.
@@ -670,7 +674,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
     return;
   }
 
-  const bool reg_pro = MODE != MMA_MOE && (p.pro == PRO_RMSNORM || p.pro == PRO_NONE);
+  const bool reg_pro = (MODE == MMA_PLAIN || MODE == MMA_SWIGLU) ||
+                       (MODE == MMA_XCH && (p.pro == PRO_RMSNORM || p.pro == PRO_NONE));
   float4 wpre[mma_pro_items<NW>()];
   if (reg_pro) gemv_mma_prologue_weights<NW>(p, tid, wpre);
   pdl_wait();
@@ -690,7 +695,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
       (MODE == MMA_XCH && p.xch_wk >= 0) ? (uint32_t)(*p.xch_seq + (unsigned long long)p.xch_wk + 1ull) : 0u;
   const float fscale0 = nonfinite ? __int_as_float(0x7fc00000) : colscale * mma_pow2(-mma_exp2_scale(vmax[0]));
 
-  const bool paired = (p.epi == EPI_SWIGLU);
+  const bool paired = MODE == MMA_SWIGLU || ((MODE == MMA_MOE || MODE == MMA_XCH) && p.epi == EPI_SWIGLU);
   const int nrg = p.TR >> 4;            // 16-row groups per tile
   const int nkg = NW / nrg;
   const int rg = warp % nrg, wk = warp / nrg;
@@ -780,7 +785,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
         const int row = row0 + rg * 16 + g + 8 * h;
         const float t = h ? tb : ta;
         if (row < p.seg[sg].rows) {
-          if (p.epi == EPI_ARGMAX) {
+          if ((MODE == MMA_PLAIN || MODE == MMA_XCH) && p.epi == EPI_ARGMAX) {
             if (t > best_v || (t == best_v && row < best_i)) { best_v = t; best_i = row; }
             if (p.seg[sg].y) p.seg[sg].y[row] = t;
           } else if (MODE == MMA_XCH && p.xch_wk >= 0) {
@@ -809,7 +814,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
     (void)gemv_mma_prologue_reg<TYPE == T_Q6_KR ? T_Q6_K : TYPE, NW, MODE>(q, xq, xsum, red, vmax, tid, wpre);
     if (tid == 0) GEMV_DBG(p, 9);
   }
-  if (p.epi == EPI_ARGMAX && wk == 0) {
+  if ((MODE == MMA_PLAIN || MODE == MMA_XCH) && p.epi == EPI_ARGMAX && wk == 0) {
     float v = best_v;
     int i = best_i;
 #pragma unroll
