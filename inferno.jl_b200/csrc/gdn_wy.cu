@@ -35,15 +35,27 @@ struct WyScratch {
   float* G;   // [nch][H][C]
 };
 
-// 4-byte asynchronous copy global -> shared (zero fill when !valid): a CTA
-// issues a whole chunk's operands at once and waits once, instead of one
-// dependent load round trip per loop iteration
-__device__ __forceinline__ void wy_cp4(float* dst, const float* src, bool valid) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 4 : 0)
-               : "memory");
-}
-__device__ __forceinline__ void wy_cp_wait() {
-  asm volatile("cp.async.commit_group;\ncp.async.wait_all;" ::: "memory");
+// [C][dk] rows of a token-major tensor (row t at ((t0+t)*H + h)*dk, zero past
+// n) into padded shared rows [C][KP]: every thread issues its eight 16-byte
+// loads before the first store, so a chunk costs one load round trip
+template <int KP>
+__device__ __forceinline__ void wy_load_rows(float* dst, const float* src, int t0, int n, int H, int h, int tid) {
+  constexpr int NV = WY_C * WY_DK / 4 / WY_THREADS;
+  float4 r[NV];
+#pragma unroll
+  for (int u = 0; u < NV; ++u) {
+    const int e = 4 * (tid + u * WY_THREADS), t = e / WY_DK, d = e % WY_DK;
+    r[u] = t < n ? *(const float4*)&src[((size_t)(t0 + t) * H + h) * WY_DK + d] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int u = 0; u < NV; ++u) {
+    const int e = 4 * (tid + u * WY_THREADS), t = e / WY_DK, d = e % WY_DK;
+    float* o = dst + t * KP + d;
+    o[0] = r[u].x;
+    o[1] = r[u].y;
+    o[2] = r[u].z;
+    o[3] = r[u].w;
+  }
 }
 
 // smem: K, Q [C][dk+1] (padded rows), V [C][dv], A/T [C][C+1], G, beta
@@ -63,25 +75,17 @@ __global__ void __launch_bounds__(WY_THREADS) gdn_wy_prep_kernel(int T, int H, i
   float* Es = Bs + WY_C;                 // [C] e^{G_t}
   const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
   const int t0 = c * WY_C, n = min(WY_C, T - t0);
-  for (int i = tid; i < WY_C * WY_DK; i += WY_THREADS) {
-    const int t = i / WY_DK, d = i % WY_DK;
-    const bool ok = t < n;
-    const size_t src = ok ? ((size_t)(t0 + t) * H + h) * WY_DK + d : 0;
-    wy_cp4(&Ks[t * KP + d], k + src, ok);
-    wy_cp4(&Qs[t * KP + d], q + src, ok);
-  }
+  wy_load_rows<KP>(Ks, k, t0, n, H, h, tid);
+  wy_load_rows<KP>(Qs, q, t0, n, H, h, tid);
   for (int i = tid; i < WY_C * dv; i += WY_THREADS) {
     const int t = i / dv, e = i % dv;
-    const bool ok = t < n;
-    wy_cp4(&Vs[i], v + (ok ? ((size_t)(t0 + t) * H + h) * dv + e : 0), ok);
+    Vs[i] = t < n ? v[((size_t)(t0 + t) * H + h) * dv + e] : 0.f;
   }
   if (tid < WY_C) {
     const bool ok = tid < n;
-    const size_t src = ok ? (size_t)(t0 + tid) * H + h : 0;
-    wy_cp4(&Gs[tid], g + src, ok);
-    wy_cp4(&Bs[tid], beta + src, ok);
+    Gs[tid] = ok ? g[(size_t)(t0 + tid) * H + h] : 0.f;
+    Bs[tid] = ok ? beta[(size_t)(t0 + tid) * H + h] : 0.f;
   }
-  wy_cp_wait();
   __syncthreads();
   // inclusive prefix sum of g (one warp, two tokens per lane)
   if (tid < 32) {
@@ -182,17 +186,17 @@ __global__ void __launch_bounds__(WY_THREADS) gdn_wy_state_kernel(int T, int H, 
     const int t0 = c * WY_C, n = min(WY_C, T - t0);
     __syncthreads();
     const float* Wg = o.W + ((size_t)c * H + h) * WY_C * WY_DK;
-    for (int i = tid; i < WY_C * WY_DK; i += WY_THREADS) {
-      const int t = i / WY_DK, d = i % WY_DK;
-      const bool ok = t < n;
-      const size_t src = ok ? ((size_t)(t0 + t) * H + h) * WY_DK + d : 0;
-      wy_cp4(&Ws[t * KP + d], Wg + i, true);
-      wy_cp4(&Ks[t * KP + d], k + src, ok);
-      wy_cp4(&Qs[t * KP + d], q + src, ok);
-    }
+    wy_load_rows<KP>(Ws, Wg, 0, WY_C, 1, 0, tid);     // W is chunk-major [C][dk]
+    wy_load_rows<KP>(Ks, k, t0, n, H, h, tid);
+    wy_load_rows<KP>(Qs, q, t0, n, H, h, tid);
     const float* Pg = o.P + ((size_t)c * H + h) * WY_C * WY_C;
-    for (int i = tid; i < WY_C * WY_C; i += WY_THREADS) wy_cp4(&Ps[i], Pg + i, true);
-    wy_cp_wait();
+    {
+      float4 pr[WY_C * WY_C / 4 / WY_THREADS];
+#pragma unroll
+      for (int u = 0; u < WY_C * WY_C / 4 / WY_THREADS; ++u) pr[u] = ((const float4*)Pg)[tid + u * WY_THREADS];
+#pragma unroll
+      for (int u = 0; u < WY_C * WY_C / 4 / WY_THREADS; ++u) ((float4*)Ps)[tid + u * WY_THREADS] = pr[u];
+    }
     if (tid < WY_C) {
       const float gt = o.G[((size_t)c * H + h) * WY_C + tid];
       const float glast = o.G[((size_t)c * H + h) * WY_C + (n - 1)];
