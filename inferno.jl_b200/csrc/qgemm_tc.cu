@@ -68,6 +68,7 @@ struct QgParams {
   long long y_stride;    // floats between token rows of y
   int epi;               // QG_STORE / QG_ADD / QG_SWIGLU
   int nbs, nas, nrs;     // ring stages: activation tiles, dequantized A tiles, raw super-blocks
+  int kps;               // K steps per dequantized A stage (1 or 2): one hand-off per stage
   int split;
   int trace;             // debug (-DINFERNO_KTRACE=1 builds): %globaltimer stamps into qg_trace
   int dbgmode;           // debug timing only (-DINFERNO_KTRACE=1 builds; wrong results), bits: 1 no MMAs, 2 no dequantization,
@@ -384,12 +385,12 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = p.split;
   const int nsplit = split ? 2 : 1;
-  const int NA = p.nas, NR = p.nrs, NB = p.nbs;
+  const int NA = p.nas, NR = p.nrs, NB = p.nbs, KPS = p.kps;
   const bool spin = INFERNO_KTRACE && (p.dbgmode & 64);
   // ---- shared memory carve-up (1024-byte aligned operand tiles) ----
   uint8_t* base = (uint8_t*)(((uintptr_t)qg_smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* sA = base;                                        // [NA][nsplit][16 KB]
-  uint8_t* sB = sA + (size_t)NA * nsplit * QG_ATILE;         // [NB][nsplit][BN * 128]
+  uint8_t* sA = base;                                        // [NA][KPS][nsplit][16 KB]
+  uint8_t* sB = sA + (size_t)NA * KPS * nsplit * QG_ATILE;   // [NB][nsplit][BN * 128]
   const int btile = BN * 128;
   uint8_t* sRaw = sB + (size_t)NB * nsplit * btile;          // [NR][128][slot]
   uint64_t* bars = (uint64_t*)(sRaw + (size_t)NR * QG_M * p.slot);
@@ -462,12 +463,13 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
       const uint32_t idesc = umma_idesc_f16(QG_M, BN);
       bool ok = true;
       for (int i = 0; i < nk && ok; ++i) {
-        const int as = i % NA, bs = i % NB;
-        ok = qg_wait(&a_full[as], (i / NA) & 1, p.err, spin) && qg_wait(&b_full[bs], (i / NB) & 1, p.err, spin);
+        const int m = i / KPS, s2 = i - m * KPS, as = m % NA, bs = i % NB;
+        if (s2 == 0) ok = qg_wait(&a_full[as], (m / NA) & 1, p.err, spin);
+        ok = ok && qg_wait(&b_full[bs], (i / NB) & 1, p.err, spin);
         if (!ok) break;
         tc_fence_after();
         if (i == 0) QG_STAMP(3);
-        const uint32_t a_hi = smem_u32(sA + (size_t)as * nsplit * QG_ATILE);
+        const uint32_t a_hi = smem_u32(sA + (size_t)(as * KPS + s2) * nsplit * QG_ATILE);
         const uint32_t b_hi = smem_u32(sB + (size_t)bs * nsplit * btile);
         const uint64_t dah = umma_desc_sw128(a_hi), dbh = umma_desc_sw128(b_hi);
         const uint64_t dal = umma_desc_sw128(a_hi + QG_ATILE), dbl = umma_desc_sw128(b_hi + btile);
@@ -482,11 +484,11 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
           }
         }
         if (INFERNO_KTRACE && (p.dbgmode & 128)) {        // debug timing: plain arrivals instead of MMA commits
-          mbar_arrive(&a_empty[as]);
+          if (s2 == KPS - 1) mbar_arrive(&a_empty[as]);
           mbar_arrive(&b_empty[bs]);
           continue;
         }
-        umma_commit(&a_empty[as]);
+        if (s2 == KPS - 1) umma_commit(&a_empty[as]);
         umma_commit(&b_empty[bs]);
       }
       umma_commit(acc_full);
@@ -524,7 +526,7 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
     const float wscale = ldexpf(1.0f, sw);
     bool ok = true;
     for (int i = 0; i < nk && ok; ++i) {
-      const int j = i >> 2, ks = i & 3, rs = j % NR, as = i % NA;
+      const int j = i >> 2, ks = i & 3, rs = j % NR, m = i / KPS, s2 = i - m * KPS, as = m % NA;
       if (ks == 0 && !(INFERNO_KTRACE && (p.dbgmode & 8))) {
         __syncwarp();                 // the row's threads are done with stage (j - 1) % NR
         stage_raw(j + NR - 1);
@@ -532,10 +534,10 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         else asm volatile("cp.async.wait_group 1;" ::: "memory");
         __syncwarp();                 // the row's four threads' copies are visible
       }
-      if (i >= NA) ok = qg_wait(&a_empty[as], ((i / NA) - 1) & 1, p.err, spin);
+      if (s2 == 0 && m >= NA) ok = qg_wait(&a_empty[as], ((m / NA) - 1) & 1, p.err, spin);
       if (!ok) break;
       if (tid == 64 && i == 0) QG_STAMP(2);
-      uint8_t* ah = sA + (size_t)as * nsplit * QG_ATILE;
+      uint8_t* ah = sA + (size_t)(as * KPS + s2) * nsplit * QG_ATILE;
       uint32_t h[8], l[8];
       if (dvalid && !(INFERNO_KTRACE && (p.dbgmode & 2))) {
         const uintptr_t a = rowsrc + (uintptr_t)(sb0 + j) * QgBlk<TYPE>::BB;
@@ -552,9 +554,11 @@ __global__ void __launch_bounds__(QG_THREADS, 1)
         sts128(sa, h[4 * cc], h[4 * cc + 1], h[4 * cc + 2], h[4 * cc + 3]);
         if (split) sts128(sa + QG_ATILE, l[4 * cc], l[4 * cc + 1], l[4 * cc + 2], l[4 * cc + 3]);
       }
-      if (!(INFERNO_KTRACE && (p.dbgmode & 4))) fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&a_full[as]);
+      if (s2 == KPS - 1) {
+        if (!(INFERNO_KTRACE && (p.dbgmode & 4))) fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&a_full[as]);
+      }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     if (tid == 64) QG_STAMP(4);
@@ -932,7 +936,7 @@ int launch_qgemm(const QgemmCall& c, cudaStream_t st, bool pdl) {
   p.wbound = c.wbound;
   p.err = c.err;
   const int nsplit = p.split ? 2 : 1;
-  const size_t astage = (size_t)nsplit * QG_ATILE, rstage = (size_t)QG_M * p.slot;
+  const size_t rstage = (size_t)QG_M * p.slot;
   const size_t bstage = (size_t)nsplit * BN * 128;
   const size_t cap = 227 * 1024 - 1024 - 1024;
   // Ring depths.  The activation (B) tiles come from L2 by TMA with a
@@ -941,16 +945,29 @@ int launch_qgemm(const QgemmCall& c, cudaStream_t st, bool pdl) {
   // the depth (up to 8 stages); dequantized A tiles need only two stages (the
   // dequantizing warps work one step ahead of the MMA), the raw super-block
   // ring three (two super-blocks of HBM prefetch).
-  static const int env_nas = getenv("INFERNO_QG_NAS") ? atoi(getenv("INFERNO_QG_NAS")) : 2;
-  int nas = env_nas, nrs = 3, nbs = 8;
-  auto need = [&] { return nas * astage + nrs * rstage + nbs * bstage; };
-  while (need() > cap && nbs > 3) --nbs;
-  while (need() > cap && nrs > 2) --nrs;
+  // K steps per A stage: INFERNO_QG_KPS=2 hands two K steps from the
+  // dequantizing warps to the MMA issuer at once (measured: no faster than
+  // one -- the step time is set by the dequantization chain itself).
+  static const int env_kps = getenv("INFERNO_QG_KPS") ? atoi(getenv("INFERNO_QG_KPS")) : 1;
+  int kps = env_kps == 1 ? 1 : 2, nas = 2, nrs = 3, nbs = 8;
+  auto need = [&] { return (size_t)nas * kps * nsplit * QG_ATILE + nrs * rstage + nbs * bstage; };
+  auto shrink = [&] {
+    while (need() > cap && nbs > 3) --nbs;
+    while (need() > cap && nrs > 2) --nrs;
+  };
+  shrink();
+  if (need() > cap && kps == 2) {
+    kps = 1;
+    nrs = 3;
+    nbs = 8;
+    shrink();
+  }
   while (need() > cap && nbs > 2) --nbs;
   if (need() > cap) return set_error(INFERNO_EINVAL, "qgemm: tiles do not fit shared memory");
   p.nbs = nbs;
   p.nas = nas;
   p.nrs = nrs;
+  p.kps = kps;
   const size_t smem = 1024 + need() + 1024;     // alignment slack, barriers, column scales
   // split K while the output tiles leave SMs idle (one CTA per SM)
   const int ntt = (c.T + BN - 1) / BN, tiles = mt * ntt;
