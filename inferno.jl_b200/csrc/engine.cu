@@ -637,6 +637,18 @@ int bgemv(InfernoEngine* e, const DevTensor* W, int inner, std::initializer_list
 // One prefill chunk: T <= PF_MAX_T prompt tokens (device ids) at positions
 // pos0.. through every layer with batched GEMVs and the chunk kernels of
 // prefill.cu; the last chunk also runs the lm_head on its last token.
+// Tensor-parallel prefill: the row-parallel products (ssm_out, attn_output,
+// ffn_down) leave each rank a partial of the residual update; rank 0 adds its
+// partial to the residual rows, the others store theirs over them, and one
+// NCCL all-reduce of the [T][H] rows makes every rank's residual
+// x + sum_r partial_r.
+int pf_residual_epi(InfernoEngine* e) { return (!e->tp || e->cfg.tp_rank == 0) ? EPI_ADD : EPI_STORE; }
+int pf_tp_sum(InfernoEngine* e, int T) {
+  if (!e->tp) return 0;
+  ncclResult_t r = ncclAllReduce(e->xb, e->xb, (size_t)T * e->cfg.hidden_size, ncclFloat, ncclSum, e->comm, e->st);
+  return r == ncclSuccess ? 0 : set_error(INFERNO_ENCCL, "prefill residual all-reduce: %s", ncclGetErrorString(r));
+}
+
 int enqueue_prefill_chunk(InfernoEngine* e, const int* toks, int T, int pos0, bool last, bool logits) {
   const InfernoConfig& c = e->cfg;
   const int H = c.hidden_size, I = c.intermediate_size, hdq = c.n_heads * c.head_dim;
@@ -681,7 +693,8 @@ int enqueue_prefill_chunk(InfernoEngine* e, const int* toks, int T, int pos0, bo
       }
       mark(e, K_GDN);
       if ((rc = bgemv(e, L.ssm_out, e->di, {M(L.ssm_out, e->xb)}, e->yb, T, e->di, H, PRO_HEADNORM_GATE,
-                      (const float*)L.ssm_norm->d, e->zb, c.ssm_dv, EPI_ADD)))
+                      (const float*)L.ssm_norm->d, e->zb, c.ssm_dv, pf_residual_epi(e))) ||
+          (rc = pf_tp_sum(e, T)))
         return rc;
     } else {
       const int kvd = c.n_kv_heads * c.head_dim;
@@ -719,13 +732,17 @@ int enqueue_prefill_chunk(InfernoEngine* e, const int* toks, int T, int pos0, bo
       a.err = e->err;
       if ((rc = launch_attn_chunk(a, pos0, T, e->st))) return rc;
       mark(e, K_ATTN);
-      if ((rc = bgemv(e, L.wo, hdq, {M(L.wo, e->xb)}, e->ob, T, hdq, H, PRO_NONE, nullptr, nullptr, 0, EPI_ADD)))
+      if ((rc = bgemv(e, L.wo, hdq, {M(L.wo, e->xb)}, e->ob, T, hdq, H, PRO_NONE, nullptr, nullptr, 0,
+                      pf_residual_epi(e))) ||
+          (rc = pf_tp_sum(e, T)))
         return rc;
     }
     DevTensor* down = L.ffn_down->type == T_Q6_KR ? &L.ffn_down_raw : L.ffn_down;
     if ((rc = bgemv(e, L.ffn_gate, H, {M(L.ffn_gate, e->hb), M(L.ffn_up, nullptr)}, e->xb, T, H, I, PRO_RMSNORM,
                     (const float*)L.post_norm->d, nullptr, 0, EPI_SWIGLU)) ||
-        (rc = bgemv(e, down, I, {M(down, e->xb)}, e->hb, T, I, H, PRO_NONE, nullptr, nullptr, 0, EPI_ADD)))
+        (rc = bgemv(e, down, I, {M(down, e->xb)}, e->hb, T, I, H, PRO_NONE, nullptr, nullptr, 0,
+                    pf_residual_epi(e))) ||
+        (rc = pf_tp_sum(e, T)))
       return rc;
   }
   if (!last) return 0;
@@ -1366,7 +1383,7 @@ int inferno_engine_finalize(InfernoEngine* e) {
   if ((e->tp || e->ep) && (rc = setup_xch(e))) return rc;
   {
     const char* np = getenv("INFERNO_B200_NO_PREFILL");
-    e->prefill = !(np && atoi(np) != 0) && c.tp_size == 1 && !c.n_experts && !e->dump;
+    e->prefill = !(np && atoi(np) != 0) && !c.n_experts && !e->dump;
     if (e->prefill || e->nseq > 1) {
       const size_t T = PF_MAX_T;
       if ((rc = dalloc(e, &e->xb, T * H)) || (rc = dalloc(e, &e->qkvb, T * e->C)) ||
@@ -1931,7 +1948,17 @@ int inferno_forward_tokens(InfernoEngine* e, const int32_t* tok, int n, int pos0
     if (tok[i] < 0 || tok[i] >= e->cfg.vocab_size) return set_error(INFERNO_EINVAL, "forward_tokens: token %d out of range", tok[i]);
   INF_CUDA_TRY(cudaMemcpyAsync(e->prompt, tok, (size_t)n * 4, cudaMemcpyHostToDevice, e->st));
   if ((rc = set_ctl(e, tok[0], pos0, n))) return rc;
-  if (e->prefill && !e->persistent && n > 1) {
+  if (e->prefill && !e->persistent && n > 1 && e->tp) {
+    // tensor parallel: the first n - 1 tokens as chunks (residual sums by
+    // all-reduce), the last one through the token path, whose vocab-split
+    // lm_head and first-max reduction across ranks it already has
+    for (int off = 0; off < n - 1; off += PF_MAX_T) {
+      const int T = std::min(PF_MAX_T, n - 1 - off);
+      if ((rc = enqueue_prefill_chunk(e, e->prompt + off, T, pos0 + off, false, false))) return rc;
+    }
+    if ((rc = set_ctl(e, tok[n - 1], pos0 + n - 1, 1))) return rc;
+    if ((rc = run_steps(e, 1, logits_out != nullptr))) return rc;
+  } else if (e->prefill && !e->persistent && n > 1) {
     // chunked prefill; afterwards the control block reads as if n decode
     // steps had run (position, step, last token = first-max of the last logits)
     auto enqueue_all = [&]() -> int {

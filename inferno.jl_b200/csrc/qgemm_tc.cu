@@ -696,42 +696,46 @@ __global__ void __launch_bounds__(256) qg_act_kernel(const float* x, long long x
   }
   const float* xr = x + (long long)t * x_stride;
   const float* zr = pro_z ? pro_z + (long long)t * x_stride : nullptr;
+  // shared: the row [K], then the norm weights (K for RMSNorm, `group` for
+  // the head norm) -- constants, staged before griddepcontrol.wait
+  extern __shared__ float qa_v[];
+  float* wsm = qa_v + K;
+  const int nw = pro == PRO_RMSNORM ? K : pro == PRO_HEADNORM_GATE ? group : 0;
+  for (int i = tid; i < nw; i += 256) wsm[i] = pro_w[i];
   pdl_wait();
   pdl_trigger();
-  // pass 1: RMSNorm statistics and max|v|
+  // one global pass over the row (and z), with the RMSNorm statistics
   float ss = 0.f;
-  if (pro == PRO_RMSNORM)
-    for (int i = tid; i < K; i += 256) ss = fmaf(xr[i], xr[i], ss);
+  for (int i = tid; i < K; i += 256) {
+    const float v = xr[i];
+    qa_v[i] = v;
+    ss = fmaf(v, v, ss);
+  }
   ss = warp_sum(ss);
   if (lane == 0) red[0][w] = ss;
   __syncthreads();
   float tot = 0.f;
   for (int i = 0; i < 8; ++i) tot += red[0][i];
   const float inv = pro == PRO_RMSNORM ? 1.0f / sqrtf(tot / (float)K + eps) : 1.0f;
-  auto value = [&](int i) -> float {
-    if (pro == PRO_RMSNORM) return xr[i] * inv * pro_w[i];
-    return xr[i];
-  };
-  // head-norm x SiLU(z) (the ssm_out input): one warp per head group
-  extern __shared__ float qa_v[];
   float amax = 0.f;
   if (pro == PRO_HEADNORM_GATE) {
+    // head-norm x SiLU(z) (the ssm_out input): one warp per head group
     for (int h = w; h < K / group; h += 8) {
       float hs = 0.f;
-      for (int e = lane; e < group; e += 32) hs = fmaf(xr[h * group + e], xr[h * group + e], hs);
+      for (int e = lane; e < group; e += 32) hs = fmaf(qa_v[h * group + e], qa_v[h * group + e], hs);
       hs = warp_sum(hs);
       const float sc = 1.0f / sqrtf(hs / (float)group + eps);
       for (int e = lane; e < group; e += 32) {
         const int i = h * group + e;
         const float z = zr[i];
-        const float v = xr[i] * sc * pro_w[e] * (z / (1.0f + expf(-z)));
+        const float v = qa_v[i] * sc * wsm[e] * (z / (1.0f + expf(-z)));
         qa_v[i] = v;
         amax = fmaxf(amax, fabsf(v));
       }
     }
   } else {
     for (int i = tid; i < K; i += 256) {
-      const float v = value(i);
+      const float v = pro == PRO_RMSNORM ? qa_v[i] * inv * wsm[i] : qa_v[i];
       qa_v[i] = v;
       amax = fmaxf(amax, fabsf(v));
     }
@@ -874,12 +878,12 @@ int launch_qgemm_act(const float* x, long long x_stride, int K, int T, int pro, 
   if (K % 2 || K > 16384) return set_error(INFERNO_EINVAL, "qgemm activations: K %d", K);
   static DeviceOnce once;
   cudaError_t ea = once.run(
-      [] { return cudaFuncSetAttribute(qg_act_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024); });
+      [] { return cudaFuncSetAttribute(qg_act_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 1024); });
   if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "qgemm activations attribute: %s", cudaGetErrorString(ea));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(qgemm_rows_padded(T));
   cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = (size_t)K * 4;
+  cfg.dynamicSmemBytes = (size_t)K * 8;
   cfg.stream = st;
   cudaLaunchAttribute at[1];
   at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
