@@ -541,10 +541,10 @@ __device__ __forceinline__ void gemv_producer(const GemvParams& p, uint64_t* ful
     pdl_trigger();
     waited = true;
   }
-  for (int it = 0; it < n_items; ++it) {
-    const int s = it % p.stages;
+  int s = 0, sph = 1;                   // ring stage; parity of its previous use
+  for (int it = 0; it < n_items; ++it, s = (s + 1 == p.stages) ? 0 : s + 1, sph ^= (s == 0)) {
     if (it >= p.stages) {
-      if (!mbar_wait(&empty[s], ((it / p.stages) - 1) & 1, p.err)) break;
+      if (!mbar_wait(&empty[s], sph, p.err)) break;
     }
     int sg, row0;
     tile_locate(p, blockIdx.x + it * G, sg, row0);

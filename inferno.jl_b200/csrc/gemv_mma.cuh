@@ -696,18 +696,19 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
   const float fscale0 = nonfinite ? __int_as_float(0x7fc00000) : colscale * mma_pow2(-mma_exp2_scale(vmax[0]));
 
   const bool paired = MODE == MMA_SWIGLU || ((MODE == MMA_MOE || MODE == MMA_XCH) && p.epi == EPI_SWIGLU);
-  const int nrg = p.TR >> 4;            // 16-row groups per tile
-  const int nkg = NW / nrg;
-  const int rg = warp % nrg, wk = warp / nrg;
+  const int nrg = p.TR >> 4;            // 16-row groups per tile (1, 2, 4 or 8)
+  const int lg_nrg = __ffs(nrg) - 1;
+  const int nkg = NW >> lg_nrg;
+  const int rg = warp & (nrg - 1), wk = warp >> lg_nrg;
   const int g = lane >> 2, c = lane & 3;
   const float limbw = c == 0 ? 1.0f : c == 1 ? 256.0f : c == 2 ? 65536.0f : 16777216.0f;
   float best_v = -INFINITY;
   int best_i = 0x7fffffff;
 
-  for (int it = 0; it < n_items; ++it) {
-    const int s = it % p.stages;
+  int s = 0, sph = 0;                   // ring stage and its phase parity
+  for (int it = 0; it < n_items; ++it, s = (s + 1 == p.stages) ? 0 : s + 1, sph ^= (s == 0)) {
     if (tid == 0 && it == 0) GEMV_DBG(p, 10);
-    if (!mbar_wait(&full[s], (it / p.stages) & 1, p.err)) return;
+    if (!mbar_wait(&full[s], sph, p.err)) return;
     if (tid == 0 && it == 0) KT_LAST(p.trace, 5);
     if (tid == 0 && it == 0) GEMV_DBG(p, 5);
     int sg, row0;
