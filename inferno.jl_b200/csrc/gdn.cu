@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(const __grid_cons
   extern __shared__ __align__(16) float gsm[];     // [3][H]: w_alpha row, w_beta row, in_norm
   __shared__ __align__(16) float qn[GDN_DK], kn[GDN_DK];
   __shared__ float vrow[GDN_ROWS];
-  __shared__ float red[3][4];
+  __shared__ float red[5][4];
   __shared__ float gate_s[2];
   const int h = blockIdx.x, r0 = blockIdx.y * GDN_ROWS, tid = threadIdx.x;
   const int warp = tid >> 5, lane = tid & 31;
@@ -170,12 +170,14 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(const __grid_cons
   }
   if (tid < GDN_ROWS) p.ring[(long long)cur * C + cv] = nv_;
 
-  block_sum_n<3>(acc3, red);
+  // one block reduction for the RMSNorm statistics, alpha / beta and the
+  // q / k L2 norms
+  float acc5[5] = {acc3[0], acc3[1], acc3[2], qv * qv, kv * kv};
+  block_sum_n<5>(acc5, red);
   if (tid == 0) KT_LAST(p.trace, 4);
-  const float scale = 1.0f / sqrtf(acc3[0] / (float)H + p.eps);
-  const float alpha = acc3[1] * scale, beta_raw = acc3[2] * scale;
-  // gates in Float64 (src/ModelCPU.jl:618-636), one thread, overlapped with
-  // the L2-norm reduction below
+  const float scale = 1.0f / sqrtf(acc5[0] / (float)H + p.eps);
+  const float alpha = acc5[1] * scale, beta_raw = acc5[2] * scale;
+  // gates in Float64 (src/ModelCPU.jl:618-636), one thread
   if (tid == 0) {
     double a = (double)alpha + (double)dt_h;
     a = fmin(20.0, fmax(-20.0, a));
@@ -186,9 +188,7 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(const __grid_cons
     gate_s[1] = (float)(1.0 / (1.0 + exp(-bv)));
   }
   // ---------------- L2 norms (src/ModelCPU.jl:597-616) ----------------
-  float qk2[2] = {qv * qv, kv * kv};
-  __syncthreads();   // red[] reuse
-  block_sum_n<2>(qk2, red);
+  const float qk2[2] = {acc5[3], acc5[4]};
   const float qscale = 1.0f / sqrtf((float)GDN_DK);
   const float qnv = 1.0f / (sqrtf(qk2[0]) + 1.0e-6f) * qscale;
   const float knv = 1.0f / (sqrtf(qk2[1]) + 1.0e-6f);

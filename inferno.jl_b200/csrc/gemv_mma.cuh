@@ -769,7 +769,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
           ta += kpart[(k * nrg + rg) * 16 + g];
           tb += kpart[(k * nrg + rg) * 16 + g + 8];
         }
-      named_bar_sync(2, NW * 32);
+      if (it + 1 < n_items) named_bar_sync(2, NW * 32);   // kpart is reused by the next tile
     }
     if (wk != 0 || c != 0) continue;
     ta *= fscale;
