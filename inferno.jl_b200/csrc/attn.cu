@@ -54,6 +54,7 @@ __device__ __forceinline__ void load_chunk(const AttnParams& p, const float* KC,
 
 __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_constant__ AttnParams p) {
   __shared__ __align__(16) float qs[ATT_HD], knew[ATT_HD], vnew[ATT_HD];
+  __shared__ float qraw[ATT_HD], kraw[ATT_HD];
   __shared__ float sc[ATT_CHUNK];
   __shared__ float red[2][ATT_THREADS / 32];
   __shared__ int ticket;
@@ -88,6 +89,16 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
   float4 kreg[8];
   float vreg[ATT_CHUNK];
   if (s < nact) load_chunk(p, KC, VC, kvh, j0, min(j0 + ATT_CHUNK, j1), pos, kreg, vreg);
+  // constants of the norm + RoPE of this thread's dim d and its rotation
+  // partner (d +- rd/2), loaded before the wait
+  const int half = p.rd / 2;
+  const bool rot = d < 2 * half;
+  const int pd = d < half ? d + half : d - half;
+  const float wq_d = p.q_norm[d], wk_d = p.k_norm[d];
+  const float wq_p = rot ? p.q_norm[pd] : 0.f, wk_p = rot ? p.k_norm[pd] : 0.f;
+  const int ri = d < half ? d : pd;
+  const float rc = rot ? p.rope_cos[(long long)pos * half + ri] : 1.f;
+  const float rs = rot ? p.rope_sin[(long long)pos * half + ri] : 0.f;
   pdl_wait();
   pdl_trigger();
   if (d == 0) {
@@ -101,6 +112,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
   const float qv = QG[(long long)h * 2 * ATT_HD + d];
   const float kv = has_new ? KN[kvh * ATT_HD + d] : 0.f;
   if (has_new) vnew[d] = VN[kvh * ATT_HD + d];
+  qraw[d] = qv;
+  kraw[d] = kv;
   float a = warp_sum(qv * qv), b = warp_sum(kv * kv);
   if (lane == 0) { red[0][warp] = a; red[1][warp] = b; }
   __syncthreads();
@@ -110,21 +123,23 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
   for (int i = 0; i < ATT_THREADS / 32; ++i) { a += red[0][i]; b += red[1][i]; }
   const float iq = 1.0f / sqrtf(a / (float)ATT_HD + p.eps);
   const float ik = 1.0f / sqrtf(b / (float)ATT_HD + p.eps);
-  qs[d] = qv * iq * p.q_norm[d];
-  if (has_new) knew[d] = kv * ik * p.k_norm[d];
-  __syncthreads();
-  const int half = p.rd / 2;
-  if (d < half) {
-    const float c = p.rope_cos[(long long)pos * half + d], sn = p.rope_sin[(long long)pos * half + d];
-    float x1 = qs[d], x2 = qs[d + half];
-    qs[d] = x1 * c - x2 * sn;
-    qs[d + half] = x1 * sn + x2 * c;
-    if (has_new) {
-      x1 = knew[d];
-      x2 = knew[d + half];
-      knew[d] = x1 * c - x2 * sn;
-      knew[d + half] = x1 * sn + x2 * c;
+  // normalised values of d and of its partner, rotated (x1 = first half,
+  // x2 = second half: x1' = x1 c - x2 s, x2' = x1 s + x2 c)
+  {
+    const float nq = qv * iq * wq_d, nk = kv * ik * wk_d;
+    float qo = nq, ko = nk;
+    if (rot) {
+      const float pq = qraw[pd] * iq * wq_p, pk = kraw[pd] * ik * wk_p;
+      if (d < half) {
+        qo = nq * rc - pq * rs;
+        ko = nk * rc - pk * rs;
+      } else {
+        qo = pq * rs + nq * rc;
+        ko = pk * rs + nk * rc;
+      }
     }
+    qs[d] = qo;
+    if (has_new) knew[d] = ko;
   }
   __syncthreads();
   if (has_new && (h % (p.nh / p.nkv)) == 0) {

@@ -177,13 +177,15 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(const __grid_cons
   if (tid == 0) KT_LAST(p.trace, 4);
   const float scale = 1.0f / sqrtf(acc5[0] / (float)H + p.eps);
   const float alpha = acc5[1] * scale, beta_raw = acc5[2] * scale;
-  // gates in Float64 (src/ModelCPU.jl:618-636), one thread
+  // gates in Float64 (src/ModelCPU.jl:618-636): decay and beta on threads of
+  // two different warps, so their double-precision chains run side by side
   if (tid == 0) {
     double a = (double)alpha + (double)dt_h;
     a = fmin(20.0, fmax(-20.0, a));
     const double sp = log(1.0 + exp(a));
     const float decay = (float)((double)a_h * sp);
     gate_s[0] = expf(decay);
+  } else if (tid == 32) {
     const double bv = fmin(20.0, fmax(-20.0, (double)beta_raw));
     gate_s[1] = (float)(1.0 / (1.0 + exp(-bv)));
   }
