@@ -324,7 +324,11 @@ __device__ __forceinline__ void gemv_mma_prologue_weights(const GemvParams& p, i
 #pragma unroll
   for (int j = 0; j < IT; ++j) {
     const int u = tid + j * NT;
-    w4[j] = (p.pro == PRO_RMSNORM && u < nf4) ? ((const float4*)p.pro_w)[u] : make_float4(0.f, 0.f, 0.f, 0.f);
+    // RMSNorm: weight of each element; head norm (groups of 128): the
+    // group's weights, element 4u lying at 4 (u % 32) of its group
+    w4[j] = (p.pro == PRO_RMSNORM && u < nf4)          ? ((const float4*)p.pro_w)[u]
+            : (p.pro == PRO_HEADNORM_GATE && u < nf4) ? ((const float4*)p.pro_w)[u & 31]
+                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
   }
 }
 
@@ -337,8 +341,12 @@ __device__ float gemv_mma_prologue_reg(const GemvParams& p, uint8_t* xq, float* 
   const int lane = tid & 31, w = tid >> 5;
   const bool rms = p.pro == PRO_RMSNORM;
   const bool xch = MODE == MMA_XCH && p.xch_rk >= 0;
+  // head norm x SiLU(z) of the ssm_out input, heads of 128 elements: a warp's
+  // 32 float4 items are one head (MMA_GATE kernels only)
+  constexpr bool HNG = MODE == MMA_GATE;
   bool bad = false;
   float4 v[IT];
+  float4 z4[HNG ? IT : 1];
   float ss = 0.f, amax = 0.f;
   uint32_t tag = 0;
   const unsigned long long* parts = nullptr;
@@ -351,6 +359,7 @@ __device__ float gemv_mma_prologue_reg(const GemvParams& p, uint8_t* xq, float* 
     const int u = tid + j * NT;
     v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (u < nf4) v[j] = xch ? __ldcg((const float4*)p.x + u) : ((const float4*)p.x)[u];
+    if constexpr (HNG) z4[j] = u < nf4 ? ((const float4*)p.pro_z)[u] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   if (xch) {
     // residual = x + the ranks' tagged partials of sync xch_rk (rank order)
@@ -386,7 +395,16 @@ __device__ float gemv_mma_prologue_reg(const GemvParams& p, uint8_t* xq, float* 
     const int u = tid + j * NT;
     if (u >= nf4) continue;
     if (xch && blockIdx.x == 0) ((float4*)p.x_next)[u] = v[j];
-    if (rms) {
+    if constexpr (HNG) {
+      float hs = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, v[j].w * v[j].w)));
+      hs = warp_sum(hs);                 // whole warps take this branch together
+      const float sc = 1.0f / sqrtf(hs / (float)p.pro_group + p.eps);
+      const float4 w4 = wpre[j], zz = z4[j];
+      v[j].x = v[j].x * sc * w4.x * zz.x * (1.0f / (1.0f + expf(-zz.x)));
+      v[j].y = v[j].y * sc * w4.y * zz.y * (1.0f / (1.0f + expf(-zz.y)));
+      v[j].z = v[j].z * sc * w4.z * zz.z * (1.0f / (1.0f + expf(-zz.z)));
+      v[j].w = v[j].w * sc * w4.w * zz.w * (1.0f / (1.0f + expf(-zz.w)));
+    } else if (rms) {
       ss = fmaf(v[j].x, v[j].x, fmaf(v[j].y, v[j].y, fmaf(v[j].z, v[j].z, fmaf(v[j].w, v[j].w, ss))));
       const float4 w4 = wpre[j];
       v[j].x *= w4.x; v[j].y *= w4.y; v[j].z *= w4.z; v[j].w *= w4.w;
@@ -399,7 +417,7 @@ __device__ float gemv_mma_prologue_reg(const GemvParams& p, uint8_t* xq, float* 
   amax = warp_max(amax);
   if (lane == 0) {
     red[w] = ss;
-    atomicMax((int*)&vmax[0], __float_as_int(amax));
+    red[NW + w] = amax;              // per-warp maxima (no shared atomics)
   }
   named_bar_sync(1, NT);
   float colscale = 1.0f;
@@ -409,7 +427,10 @@ __device__ float gemv_mma_prologue_reg(const GemvParams& p, uint8_t* xq, float* 
     for (int i = 0; i < NW; ++i) tss += red[i];
     colscale = 1.0f / sqrtf(tss / (float)n + p.eps);
   }
-  const float vm = vmax[0];
+  float vm = 0.f;
+#pragma unroll
+  for (int i = 0; i < NW; ++i) vm = fmaxf(vm, red[NW + i]);
+  if (tid == 0) vmax[0] = vm;      // read by the tiles after the next barrier
   if (!(vm <= 3.0e38f)) bad = true;
   const float up = mma_pow2(mma_exp2_scale(vm));
 #pragma unroll
@@ -675,7 +696,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
   }
 
   const bool reg_pro = (MODE == MMA_PLAIN || MODE == MMA_SWIGLU) ||
-                       (MODE == MMA_XCH && (p.pro == PRO_RMSNORM || p.pro == PRO_NONE));
+                       (MODE == MMA_XCH && (p.pro == PRO_RMSNORM || p.pro == PRO_NONE)) ||
+                       (MODE == MMA_GATE && p.pro == PRO_HEADNORM_GATE && p.pro_group == 128 && p.inner % 128 == 0);
   float4 wpre[mma_pro_items<NW>()];
   if (reg_pro) gemv_mma_prologue_weights<NW>(p, tid, wpre);
   pdl_wait();
