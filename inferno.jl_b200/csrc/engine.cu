@@ -1399,6 +1399,10 @@ int inferno_engine_finalize(InfernoEngine* e) {
   e->max_out = c.max_ctx + 8;
   // attention splits: multiples of 32 positions, at most 128 splits
   e->split_len = attn_split_len(c.max_ctx);
+  if (const char* sl = getenv("INFERNO_ATT_SPLIT")) {      // measurement knob: positions per split
+    const int v = atoi(sl);
+    if (v >= 32 && v % 32 == 0 && (c.max_ctx + v - 1) / v <= 1024) e->split_len = v;
+  }
   e->nsplit = (c.max_ctx + e->split_len - 1) / e->split_len;
   e->rd = (int)std::lround(c.head_dim * (double)c.partial_rotary_factor);   // src/LoaderCPU.jl:375
   if (any_attn) {
