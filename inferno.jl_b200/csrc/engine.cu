@@ -600,7 +600,11 @@ int bgemv(InfernoEngine* e, const DevTensor* W, int inner, std::initializer_list
   c.eps = e->cfg.rms_eps;
   c.epi = epi;
   c.err = e->err;
-  if (T >= PF_TC_MIN_T && e->pf_xhi && W->wb && qgemm_supported(W->type) && epi != EPI_ARGMAX && inner % 256 == 0) {
+  // the tcgen05 GEMM from 4 token columns on (measured: batched decode of 8
+  // sequences 2561 -> 2700 tokens/s at config 1, 399 -> 458 at config 4
+  // against the integer mma.sync batch GEMV)
+  static const int tc_min = getenv("INFERNO_TC_MIN_T") ? std::max(1, atoi(getenv("INFERNO_TC_MIN_T"))) : GEMM_TC_MIN_T;
+  if (T >= tc_min && e->pf_xhi && W->wb && qgemm_supported(W->type) && epi != EPI_ARGMAX && inner % 256 == 0) {
     // fp16 hi / lo activations with the prologue applied, then the tcgen05 GEMM
     int rc = 0;
     if (!reuse_act) {

@@ -139,9 +139,11 @@ int plan_launch_mma(const GemvCall& c, int dev, int sms, cudaStream_t st, bool p
   // tuning knobs (measurement only): a fixed tile height, a cap on the grid
   static const int env_tr = getenv("INFERNO_MMA_TR") ? atoi(getenv("INFERNO_MMA_TR")) : 0;
   static const int env_cap = getenv("INFERNO_MMA_GRID_CAP") ? atoi(getenv("INFERNO_MMA_GRID_CAP")) : 0;
+  static const int env_tr_big = getenv("INFERNO_MMA_TR_BIG") ? atoi(getenv("INFERNO_MMA_TR_BIG")) : 0;
   if (env_cap > 0 && wbytes <= (64ll << 20)) sms = std::min(sms, env_cap);
   for (int TR : {16, 32, 64, 128}) {
     if (env_tr && TR != env_tr && wbytes <= (64ll << 20)) continue;
+    if (env_tr_big && TR != env_tr_big && wbytes > (64ll << 20)) continue;
     const int nrg = TR / 16, nkg = NW / nrg;
     // a ring of one stage (no weight prefetch past the current tile) only
     // when two do not fit next to the staged activations of a long row

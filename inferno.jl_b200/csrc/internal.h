@@ -154,6 +154,7 @@ constexpr int PF_MAX_T = 128;
 // GEMM (qgemm_tc.cu) and the GDN as token-parallel prep + recurrence;
 // shorter chunks use the batched GEMV and the chunk-sequential GDN kernel
 constexpr int PF_TC_MIN_T = 16;
+constexpr int GEMM_TC_MIN_T = 4;     // batched products on the tcgen05 GEMM from this many columns
 struct GdnParams;
 struct AttnParams;
 int launch_gdn_chunk(const GdnParams& p, int T, cudaStream_t st);
