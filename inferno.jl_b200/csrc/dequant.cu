@@ -1,3 +1,4 @@
+#include <algorithm>
 // Bit-exact dequantization of GGUF super-blocks to fp32.
 //
 // Follows Inferno.jl src/Dequant.jl:12-54 (IQ2_XXS), :304-321 (Q8_0),
@@ -124,59 +125,59 @@ __global__ void embed_row_kernel(const uint8_t* __restrict__ W, long long row_by
   int row = row_ptr[blockIdx.x];
   if (row < 0 || row >= vocab) row = 0;
   dst += (long long)blockIdx.x * inner;
-  long long runs = inner / 32;
-  // one thread per run (inner/32 runs <= 1024 for every model here)
-  int r = threadIdx.x;
-  if (r < runs) {
-    const uint8_t* src = W + (long long)row * row_bytes;
-    // dispatch to the same arithmetic as dequant_kernel
-    if (TYPE == T_Q6_K) {
-      long long blk = r >> 3;
-      int q = r & 7, n = q >> 2, k = q & 3;
-      const uint8_t* b = src + blk * 210;
-      const uint8_t* ql = b + n * 64;
-      const uint8_t* qh = b + 128 + n * 32;
-      const int8_t* sc = (const int8_t*)(b + 192 + n * 8);
-      float d = h2f_bits(ld16(b + 208));
-      float* o = dst + blk * 256 + n * 128 + k * 32;
-      for (int l = 0; l < 32; ++l) {
-        uint32_t lo = (k & 1) ? ql[l + 32] : ql[l];
-        uint32_t nib = (k >= 2) ? (lo >> 4) : (lo & 0x0fu);
-        int qv = (int)(nib | (((qh[l] >> (2 * k)) & 3u) << 4)) - 32;
-        o[l] = __fmul_rn(__fmul_rn(d, (float)sc[l / 16 + 2 * k]), (float)qv);
-      }
-    } else if (TYPE == T_Q4_K || TYPE == T_Q5_K || TYPE == T_Q8_0) {
-      long long blk = r >> 3;
-      int q = r & 7, j = q >> 1, hi = q & 1;
-      if (TYPE == T_Q8_0) {
-        const uint8_t* b = src + (long long)r * 34;
-        float d = h2f_bits(ld16(b));
-        for (int jj = 0; jj < 32; ++jj) dst[r * 32 + jj] = __fmul_rn(d, (float)(int8_t)b[2 + jj]);
-      } else {
-        const uint8_t* b = src + blk * (TYPE == T_Q4_K ? 144 : 176);
-        float d = h2f_bits(ld16(b)), dmin = h2f_bits(ld16(b + 2));
-        uint32_t s, m;
-        kscale_b(b + 4, 2 * j + hi, s, m);
-        float d1 = __fmul_rn(d, (float)s), mn = __fmul_rn(dmin, (float)m);
-        float* o = dst + blk * 256 + j * 64 + hi * 32;
-        const uint8_t* qs = b + (TYPE == T_Q4_K ? 16 : 48) + j * 32;
-        for (int l = 0; l < 32; ++l) {
-          uint32_t v = hi ? (qs[l] >> 4) : (qs[l] & 0x0fu);
-          if (TYPE == T_Q5_K) v += (b[16 + l] & (1u << (2 * j + hi))) ? 16u : 0u;
-          o[l] = __fsub_rn(__fmul_rn(d1, (float)v), mn);
-        }
-      }
-    } else if (TYPE == T_F32) {
-      const float* s = (const float*)src;
-      for (int jj = 0; jj < 32; ++jj) dst[r * 32 + jj] = s[r * 32 + jj];
+  // eight threads per 32-value run, four values each (the same arithmetic
+  // per value as dequant_kernel)
+  const int runs = inner / 32;
+  const uint8_t* src = W + (long long)row * row_bytes;
+  for (int item = threadIdx.x; item < runs * 8; item += blockDim.x) {
+  const int r = item >> 3, l0 = (item & 7) * 4;
+  if (TYPE == T_Q6_K) {
+    const int blk = r >> 3, q = r & 7, n = q >> 2, k = q & 3;
+    const uint8_t* b = src + (long long)blk * 210;
+    const uint8_t* ql = b + n * 64;
+    const uint8_t* qh = b + 128 + n * 32;
+    const int8_t* sc = (const int8_t*)(b + 192 + n * 8);
+    const float d = h2f_bits(ld16(b + 208));
+    float* o = dst + (long long)blk * 256 + n * 128 + k * 32;
+#pragma unroll
+    for (int l = l0; l < l0 + 4; ++l) {
+      const uint32_t lo = (k & 1) ? ql[l + 32] : ql[l];
+      const uint32_t nib = (k >= 2) ? (lo >> 4) : (lo & 0x0fu);
+      const int qv = (int)(nib | (((qh[l] >> (2 * k)) & 3u) << 4)) - 32;
+      o[l] = __fmul_rn(__fmul_rn(d, (float)sc[l / 16 + 2 * k]), (float)qv);
     }
+  } else if (TYPE == T_Q8_0) {
+    const uint8_t* b = src + (long long)r * 34;
+    const float d = h2f_bits(ld16(b));
+#pragma unroll
+    for (int jj = l0; jj < l0 + 4; ++jj) dst[r * 32 + jj] = __fmul_rn(d, (float)(int8_t)b[2 + jj]);
+  } else if (TYPE == T_Q4_K || TYPE == T_Q5_K) {
+    const int blk = r >> 3, q = r & 7, j = q >> 1, hi = q & 1;
+    const uint8_t* b = src + (long long)blk * (TYPE == T_Q4_K ? 144 : 176);
+    const float d = h2f_bits(ld16(b)), dmin = h2f_bits(ld16(b + 2));
+    uint32_t sv, m;
+    kscale_b(b + 4, 2 * j + hi, sv, m);
+    const float d1 = __fmul_rn(d, (float)sv), mn = __fmul_rn(dmin, (float)m);
+    float* o = dst + (long long)blk * 256 + j * 64 + hi * 32;
+    const uint8_t* qs = b + (TYPE == T_Q4_K ? 16 : 48) + j * 32;
+#pragma unroll
+    for (int l = l0; l < l0 + 4; ++l) {
+      uint32_t v = hi ? (qs[l] >> 4) : (qs[l] & 0x0fu);
+      if (TYPE == T_Q5_K) v += (b[16 + l] & (1u << (2 * j + hi))) ? 16u : 0u;
+      o[l] = __fsub_rn(__fmul_rn(d1, (float)v), mn);
+    }
+  } else if (TYPE == T_F32) {
+    const float* sp = (const float*)src;
+#pragma unroll
+    for (int jj = l0; jj < l0 + 4; ++jj) dst[r * 32 + jj] = sp[r * 32 + jj];
+  }
   }
 }
 
 int launch_embed_row(int type, const void* W, long long row_bytes, int inner, const int* row_ptr, float* dst,
                      int vocab, cudaStream_t st, bool pdl, int nrows) {
-  if (inner % 256 || inner / 32 > 1024 || nrows < 1) return -1;
-  int threads = ((inner / 32 + 31) / 32) * 32;
+  if (inner % 256 || nrows < 1) return -1;
+  const int threads = std::min(1024, inner / 32 * 8);     // 8 threads per 32-value run
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nrows);
   cfg.blockDim = dim3(threads);
