@@ -707,6 +707,23 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
     if (INFERNO_KTRACE && p.dbg && blockIdx.x == 0) gemv_dbg[30] = gemv_dbg[16 + 7];
     GEMV_DBG(p, 2);
   }
+  // residual add (EPI_ADD): the old values of the first tile's rows are
+  // loaded now, so their L2 round trip overlaps the prologue instead of
+  // sitting between the MMAs and the store
+  constexpr bool PRE_ADD_MODE = MODE == MMA_PLAIN || MODE == MMA_GATE;
+  float yold[2] = {0.f, 0.f};
+  if (PRE_ADD_MODE && p.epi == EPI_ADD && n_items > 0) {
+    const int nrg0 = p.TR >> 4, lg0 = __ffs(nrg0) - 1;
+    if ((warp >> lg0) == 0 && (lane & 3) == 0) {
+      int sg0, r00;
+      tile_locate(p, blockIdx.x, sg0, r00);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = r00 + (warp & (nrg0 - 1)) * 16 + (lane >> 2) + 8 * h;
+        if (row < p.seg[sg0].rows) yold[h] = p.seg[sg0].y[row];
+      }
+    }
+  }
   const float colscale = reg_pro ? gemv_mma_prologue_reg<TYPE == T_Q6_KR ? T_Q6_K : TYPE, NW, MODE>(p, xq, xsum, red,
                                                                                                      vmax, tid, wpre)
                                  : gemv_mma_prologue<TYPE, NW, MODE>(p, xf, xq, xsum, red, vmax, tid);
@@ -818,7 +835,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) gemv_mma_kerne
             for (int q = 0; q < p.xch_n; ++q) st_relaxed_sys_u64(p.xch_parts[q] + off, wv);
           } else {
             float* y = p.seg[sg].y + row;
-            if (p.epi == EPI_ADD) *y += t;
+            if (p.epi == EPI_ADD) *y = (PRE_ADD_MODE && it == 0 ? yold[h] : *y) + t;
             else *y = t;
           }
         }
