@@ -156,9 +156,18 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
 #pragma unroll
   for (int i = 0; i < 8; ++i) q8[i] = *(const float4*)&qs[part * 32 + 4 * i];
   float m = -INFINITY, l = 0.f, o = 0.f;
+  float4 kreg2[8];
+  float vreg2[ATT_CHUNK];
   for (int c0 = j0; c0 < j1; c0 += ATT_CHUNK) {
     const int cend = min(c0 + ATT_CHUNK, j1);
-    if (c0 != j0) load_chunk(p, KC, VC, kvh, c0, cend, pos, kreg, vreg);
+    if (c0 != j0) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) kreg[i] = kreg2[i];
+#pragma unroll
+      for (int q = 0; q < ATT_CHUNK; ++q) vreg[q] = vreg2[q];
+    }
+    // the next chunk's K/V rows are in flight while this chunk is computed
+    if (c0 + ATT_CHUNK < j1) load_chunk(p, KC, VC, kvh, c0 + ATT_CHUNK, min(c0 + 2 * ATT_CHUNK, j1), pos, kreg2, vreg2);
     // the new row at pos comes from shared memory
     if (c0 + kk == pos) {
 #pragma unroll
@@ -347,9 +356,18 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_group_kernel(const __
     l[gi] = 0.f;
     o[gi] = 0.f;
   }
+  float4 kreg2[8];
+  float vreg2[ATT_CHUNK];
   for (int c0 = j0; c0 < j1; c0 += ATT_CHUNK) {
     const int cend = min(c0 + ATT_CHUNK, j1);
-    if (c0 != j0) load_chunk(p, KC, VC, kvh, c0, cend, pos, kreg, vreg);
+    if (c0 != j0) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) kreg[i] = kreg2[i];
+#pragma unroll
+      for (int q = 0; q < ATT_CHUNK; ++q) vreg[q] = vreg2[q];
+    }
+    // the next chunk's K/V rows are in flight while this chunk is computed
+    if (c0 + ATT_CHUNK < j1) load_chunk(p, KC, VC, kvh, c0 + ATT_CHUNK, min(c0 + 2 * ATT_CHUNK, j1), pos, kreg2, vreg2);
     if (c0 + kk == pos) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) kreg[i] = *(const float4*)&knew[part * 32 + 4 * i];
@@ -459,14 +477,17 @@ int launch_attn_decode(const AttnParams& p, cudaStream_t st, bool pdl, int nseq)
                                 cudaSharedmemCarveoutMaxShared);
   });
   if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "attention attribute: %s", cudaGetErrorString(ea));
-  // GQA groups of 2, 4 or 8 query heads share one CTA per KV head for
-  // long-context caches (max_ctx >= 8192), where a layer's KV outgrows L2 and
-  // re-reading it per query head costs DRAM bytes; short caches keep one CTA
-  // per query head, whose 4x more CTAs finish sooner (measured at config 1:
-  // 1676 vs 1511 tokens/s).  INFERNO_ATT_GROUPED=0/1 forces either.
+  // GQA groups of 2, 4 or 8 query heads share one CTA per KV head when a
+  // layer's KV cache is more than twice the 126 MB L2 (re-reading it per
+  // query head would then cost DRAM bytes); smaller caches keep one CTA per
+  // query head, whose more numerous CTAs finish sooner while the rows come
+  // from L2 (measured at config 1: 1676 vs 1511 tokens/s at a 512-position
+  // cache, 1.94 vs 2.00 ms/token at position 30000 of a 32896-position one).
+  // INFERNO_ATT_GROUPED=0/1 forces either.
   static const int env_grouped = getenv("INFERNO_ATT_GROUPED") ? atoi(getenv("INFERNO_ATT_GROUPED")) : -1;
   const int G = p.nh / p.nkv;
-  const bool grouped = env_grouped >= 0 ? env_grouped != 0 : p.ctx >= 8192;
+  const bool grouped =
+      env_grouped >= 0 ? env_grouped != 0 : (long long)p.ctx * p.nkv * ATT_HD * 8 > (256ll << 20);
   if (grouped && (G == 2 || G == 4 || G == 8)) {
     const cudaError_t e = G == 2 ? launch_attn_group<2>(p, st, pdl, nseq)
                           : G == 4 ? launch_attn_group<4>(p, st, pdl, nseq)
