@@ -217,8 +217,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_kernel(const __grid_c
   if (d == 0) CNT[h] = 0;
   const float* mlp = PML + (long long)h * p.nsplit * 2;
   float M = -INFINITY;
+#pragma unroll 8
   for (int t = 0; t < nact; ++t) M = fmaxf(M, __ldcg(mlp + 2 * t));
   float num = 0.f, den = 0.f;
+#pragma unroll 8
   for (int t = 0; t < nact; ++t) {
     const float w = expf(__ldcg(mlp + 2 * t) - M);
     num = fmaf(w, __ldcg(PO + ((long long)h * p.nsplit + t) * ATT_HD + d), num);
@@ -434,8 +436,11 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_decode_group_kernel(const __
     const int h = h0 + gi;
     const float* mlp = PML + (long long)h * p.nsplit * 2;
     float M = -INFINITY;
-    for (int t = 0; t < nact; ++t) M = fmaxf(M, __ldcg(mlp + 2 * t));
+#pragma unroll 8
+  #pragma unroll 8
+  for (int t = 0; t < nact; ++t) M = fmaxf(M, __ldcg(mlp + 2 * t));
     float num = 0.f, den = 0.f;
+#pragma unroll 8
     for (int t = 0; t < nact; ++t) {
       const float w = expf(__ldcg(mlp + 2 * t) - M);
       num = fmaf(w, __ldcg(PO + ((long long)h * p.nsplit + t) * ATT_HD + d), num);
