@@ -482,17 +482,18 @@ int launch_attn_decode(const AttnParams& p, cudaStream_t st, bool pdl, int nseq)
                                 cudaSharedmemCarveoutMaxShared);
   });
   if (ea != cudaSuccess) return set_error(INFERNO_ECUDA, "attention attribute: %s", cudaGetErrorString(ea));
-  // GQA groups of 2, 4 or 8 query heads share one CTA per KV head when a
-  // layer's KV cache is more than twice the 126 MB L2 (re-reading it per
-  // query head would then cost DRAM bytes); smaller caches keep one CTA per
-  // query head, whose more numerous CTAs finish sooner while the rows come
-  // from L2 (measured at config 1: 1676 vs 1511 tokens/s at a 512-position
-  // cache, 1.94 vs 2.00 ms/token at position 30000 of a 32896-position one).
-  // INFERNO_ATT_GROUPED=0/1 forces either.
-  static const int env_grouped = getenv("INFERNO_ATT_GROUPED") ? atoi(getenv("INFERNO_ATT_GROUPED")) : -1;
+  // GQA groups of 2, 4 or 8 query heads sharing one CTA per KV head
+  // (INFERNO_ATT_GROUPED=1).  The choice is made when the graph is captured,
+  // the position only on the device: grouping wins once a layer's KV has
+  // outgrown L2 (config 4 at position 30000 of a 32K cache: 5.17 vs 5.59
+  // ms/token) but loses while the rows still come from L2 (config 4 at
+  // position ~2300 of the same cache: 297 vs 342 tokens/s; config 1 at a
+  // 512-position cache: 1511 vs 1676), so one CTA per query head is the
+  // default.
+  const char* eg = getenv("INFERNO_ATT_GROUPED");      // read per launch (tests switch it)
+  const int env_grouped = eg ? atoi(eg) : 0;
   const int G = p.nh / p.nkv;
-  const bool grouped =
-      env_grouped >= 0 ? env_grouped != 0 : (long long)p.ctx * p.nkv * ATT_HD * 8 > (256ll << 20);
+  const bool grouped = env_grouped != 0;
   if (grouped && (G == 2 || G == 4 || G == 8)) {
     const cudaError_t e = G == 2 ? launch_attn_group<2>(p, st, pdl, nseq)
                           : G == 4 ? launch_attn_group<4>(p, st, pdl, nseq)

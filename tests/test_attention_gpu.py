@@ -91,6 +91,21 @@ def test_attention_split_lengths_agree(split_len):
     assert _rel(got, ref) < ATT_RTOL, _rel(got, ref)
 
 
+@pytest.mark.parametrize("nh,nkv,ctx,pos", [(4, 2, 2048, 1023), (16, 4, 32896, 300), (16, 4, 32896, 32000),
+                                            (16, 2, 4096, 1500)])
+def test_attention_gqa_grouped_variant(monkeypatch, nh, nkv, ctx, pos):
+    """The GQA-grouped kernel (one CTA per KV head for its 2 / 4 / 8 query
+    heads, INFERNO_ATT_GROUPED=1) gives the oracle's result and the same bits
+    as the one-CTA-per-query-head kernel."""
+    monkeypatch.setenv("INFERNO_ATT_GROUPED", "1")
+    got, ref, gk, *_ = _run(nh=nh, nkv=nkv, ctx=ctx, pos=pos, seed=5)
+    monkeypatch.setenv("INFERNO_ATT_GROUPED", "0")
+    got0, _, gk0, *_ = _run(nh=nh, nkv=nkv, ctx=ctx, pos=pos, seed=5)
+    assert _rel(got, ref) < ATT_RTOL, _rel(got, ref)
+    assert np.array_equal(got, got0)
+    assert np.array_equal(gk, gk0)
+
+
 def test_attention_position_zero_and_bad_args():
     got, ref, *_ = _run(nh=8, nkv=2, ctx=64, pos=0, seed=3)
     assert _rel(got, ref) < ATT_RTOL
